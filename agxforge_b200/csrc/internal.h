@@ -1,0 +1,127 @@
+// internal.h — the library's internal types: context, device pack, GEMV and attention launch descriptions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/agxc.h"
+
+struct agxc_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  unsigned* err_dev = nullptr;   // the device error word
+  int num_sms = 148;
+  int max_smem_optin = 0;
+};
+
+// A pack in the B200 tile layout: tiles[rt][g] of 16 rows x 64 k (512 B at 4 bits, 1,024 B at 8 bits; lane l of a
+// warp owns 16 B at 16 l, two 512-B halves at 8 bits) and, per tile, 64 B of scale/bias: entry r (8 B) =
+// {s[r], s[r+8], b[r], b[r+8]} as 16-bit patterns.
+struct agxc_pack {
+  agxc_ctx* ctx = nullptr;
+  int n = 0, k = 0, bits = 4, group = 64, sdt = 0;
+  int gateup = 0;                 // rows interleaved gate/up per 16-row tile (fused SwiGLU)
+  uint8_t* tiles = nullptr;
+  uint8_t* sb = nullptr;
+  bool owns = true;
+  int64_t bytes() const { return int64_t(n) * k * bits / 8 + int64_t(n) * (k / group) * 4; }
+};
+
+namespace agxc {
+
+constexpr int kTileRows = 16;
+constexpr int kGroup = 64;
+constexpr int kSbBytes = 64;
+inline int tile_bytes(int bits) { return bits == 4 ? 512 : 1024; }
+
+enum Epi : int { EPI_F32 = 0, EPI_RES1 = 1, EPI_RES2 = 2, EPI_SWIGLU = 3, EPI_QKV = 4, EPI_ARGMAX = 5 };
+
+// Everything one GEMV launch reads and writes (the kernel takes what its epilogue needs).
+struct QmvParams {
+  const uint8_t* w = nullptr;
+  const uint8_t* sb = nullptr;
+  int N = 0, K = 0, G = 0;        // rows, columns, groups (K/64)
+  int SC = 1, GC = 0;             // K chunks, groups per chunk
+  int bits = 4, sdt = 0, nb = 1;
+  int stages = 2;
+  // x
+  const void* x = nullptr;
+  int x_f32 = 0, x_ld = 0;
+  const __half* norm_gain = nullptr;
+  float eps = 1e-6f;
+  // outputs
+  float* out_f32 = nullptr;
+  int out_ld = 0;
+  __half* out_f16 = nullptr;
+  const __half* res16 = nullptr;
+  const float* res32 = nullptr;
+  int res_ld = 0;
+  // qkv epilogue: bias, RoPE, q scale, KV append
+  const __half* bias = nullptr;
+  int H = 0, KVH = 0, hd = 0, cap = 0;
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+  const uint32_t* q0 = nullptr;
+  float qscale = 0.f;
+  __half* q16 = nullptr;
+  __half* kcache = nullptr;      // this layer: [nb][KVH][cap][hd]
+  __half* vcache = nullptr;
+  // argmax + generation step
+  int V = 0;
+  const __half* embed = nullptr; // [V][d]
+  __half* x_next = nullptr;      // [nb][d]
+  int d = 0;
+  uint32_t* q0_rw = nullptr;
+  uint32_t* log = nullptr;       // [nb][cap]
+  int32_t* tok_out = nullptr;    // [nb]
+  uint32_t* force_next = nullptr; // [nb] pending forced tokens (consumed and cleared by the step)
+  // scratch
+  float* part = nullptr;         // [SC][N][nb] partial rows
+  float* pairs = nullptr;        // [grid][nb][2] argmax pairs (value, index as float bits)
+  unsigned* counters = nullptr;
+  unsigned* err = nullptr;
+  int pdl = 0;
+};
+
+struct QmvPlan {
+  int SC = 1, GC = 0, RW = 1, EB = 1, stages = 2, grid = 0;
+  size_t smem = 0;
+};
+
+QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits);
+// Scratch sizes a plan needs.
+size_t qmv_part_floats(const QmvPlan& p, int N, int nb, int epi);
+int launch_qmv_epi(const agxc_ctx* ctx, QmvParams p, const QmvPlan& plan, int epi, cudaStream_t s);
+int qmv_configure(const agxc_ctx* ctx);
+
+struct AttnParams {
+  int nb = 1, H = 0, KVH = 0, hd = 128, cap = 0, S = 1;
+  const uint32_t* q0 = nullptr;
+  const __half* q16 = nullptr;
+  const __half* kc = nullptr;
+  const __half* vc = nullptr;
+  __half* out = nullptr;
+  float* part = nullptr;          // [nb][H][S][hd + 2]
+  unsigned* counters = nullptr;   // [nb][KVH]
+  unsigned* err = nullptr;
+  int pdl = 0;
+};
+int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
+size_t attn_part_floats(int nb, int H, int S, int hd);
+int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
+
+int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);
+
+// pack kernels
+int launch_quantize(const float* w, int N, int K, int bits, int sdt, uint32_t* packed, uint16_t* s16, uint16_t* b16,
+                    cudaStream_t s);
+// Re-lay out rows [0, n_src) of a reference-format pack into tile rows; source row tile t lands at destination
+// row tile t * rt_stride + rt_offset.
+int launch_relayout(const uint32_t* packed, const uint16_t* s16, const uint16_t* b16, int n_src, int K, int bits,
+                    uint8_t* tiles, uint8_t* sb, int rt_stride, int rt_offset, cudaStream_t s);
+int launch_unpack(const agxc_pack* p, uint8_t* fields, cudaStream_t s);
+int launch_dequant(const agxc_pack* p, float* w, cudaStream_t s);
+
+}  // namespace agxc

@@ -1,0 +1,676 @@
+// model.cu — the decoder model on one B200: weights, KV cache, activations, the generation state and the decode
+// step as one captured CUDA graph (the reference's layer builder and executor: agxforge/inference/assemble.py
+// layer_ops 429-461 / all_ops 464-520 / build 596-828, and tools/g17decodegen.m encodeToken 167-199).
+//
+// One step (one token per sequence), five kernels a layer plus the head:
+//   D1 qkv     RMSNorm(x16, g1) -> W_qkv -> (+bias) -> RoPE at q0 -> q16 (scaled), K/V cache row q0
+//   D2 attn    split-KV attention over keys 0..q0 with the LSE merge -> attn16
+//   D3 wo      W_o attn16 + x16 -> h (fp32)
+//   D4 ffn     RMSNorm(h, g2) -> W_gate|W_up -> fp16(silu(g) u) -> act16
+//   D5 down    W_down act16 + h -> x16
+//   head       RMSNorm(x16, g_final) -> W_head -> first argmax -> generation step (token log, next x16, q0 + 1)
+// (the final norm, a dispatch of its own in the reference, is fused as the head's prologue.)
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <random>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+struct agxc_model {
+  agxc_ctx* ctx = nullptr;
+  agxc_model_desc d{};
+  int qkv_rows = 0, attn_dim = 0;
+  // weights
+  uint8_t* wmem = nullptr;
+  std::vector<agxc_pack> qkv, wo, gu, down;
+  agxc_pack head;
+  __half* gains = nullptr;      // [L][2][d]
+  __half* bias = nullptr;       // [L][qkv_rows]
+  __half* final_gain = nullptr; // [d]
+  __half* embed = nullptr;      // [V][d]
+  // cache and activations
+  __half* kcache = nullptr;     // [L][B][KVH][cap][hd]
+  __half* vcache = nullptr;
+  __half* x16 = nullptr;        // [B][d]
+  float* h = nullptr;           // [B][d]
+  __half* q16 = nullptr;        // [B][H][hd]
+  __half* attn = nullptr;       // [B][H*hd]
+  __half* act = nullptr;        // [B][F]
+  float* logits = nullptr;      // [B][V] (keep_logits)
+  uint32_t* q0 = nullptr;       // [B]
+  uint32_t* log = nullptr;      // [B][cap]
+  int32_t* tok = nullptr;       // [B]
+  uint32_t* force_next = nullptr; // [B] a token the next step must take (a per-step host input), UNSET = none
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  // scratch
+  float* part = nullptr;
+  float* apart = nullptr;
+  float* pairs = nullptr;
+  unsigned* counters = nullptr;
+  size_t counters_n = 0;
+  // plans
+  agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
+  int attn_S = 1;
+  int pdl = 1;
+  // graph
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int launches = 0;
+  // pinned staging
+  int32_t* h_tok = nullptr;
+  size_t h_tok_n = 0;
+  uint32_t* h_force = nullptr;  // pinned [steps][B]
+  size_t h_force_n = 0;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  std::vector<void*> allocs;
+};
+
+namespace agxc {
+
+namespace {
+
+int dalloc(agxc_model* m, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) return fail(AGXC_ENOMEM, std::string("cudaMalloc(") + std::to_string(bytes) +
+                                                     "): " + cudaGetErrorString(e));
+  m->allocs.push_back(*p);
+  return 0;
+}
+
+template <typename T>
+int dalloc_t(agxc_model* m, T** p, size_t count) {
+  void* v = nullptr;
+  int rc = dalloc(m, &v, std::max<size_t>(count * sizeof(T), 256));
+  *p = static_cast<T*>(v);
+  return rc;
+}
+
+void pack_init(agxc_pack& p, agxc_model* m, int n, int k) {
+  p.ctx = m->ctx;
+  p.n = n;
+  p.k = k;
+  p.bits = m->d.bits;
+  p.group = 64;
+  p.sdt = m->d.scale_dtype;
+  p.owns = false;
+}
+
+size_t pack_tile_bytes(int n, int k, int bits) { return static_cast<size_t>(n) * k * bits / 8; }
+size_t pack_sb_bytes(int n, int k) { return static_cast<size_t>(n / 16) * (k / 64) * 64; }
+
+// When `ev` is given, an event is recorded before and after every launch (kind order: qkv, attn, wo, ffn, down per
+// layer, then head): ev holds 2 * launches events.
+int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+  const agxc_model_desc& D = m->d;
+  const int B = D.batch, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim, d = D.d_model, F = D.ffn;
+  const size_t layer_kv = static_cast<size_t>(B) * KVH * D.cap * hd;
+  int rc;
+  m->launches = 0;
+  for (int l = 0; l < D.n_layers; ++l) {
+    // D1: norm + qkv + bias + RoPE + append
+    QmvParams p;
+    p.w = m->qkv[l].tiles; p.sb = m->qkv[l].sb; p.N = m->qkv_rows; p.K = d; p.bits = D.bits; p.sdt = D.scale_dtype;
+    p.nb = B; p.x = m->x16; p.x_f32 = 0; p.x_ld = d; p.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d;
+    p.eps = D.eps; p.bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
+    p.H = H; p.KVH = KVH; p.hd = hd; p.cap = D.cap; p.cos_t = m->cos_t; p.sin_t = m->sin_t; p.q0 = m->q0;
+    p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+    p.q16 = m->q16; p.kcache = m->kcache + l * layer_kv; p.vcache = m->vcache + l * layer_kv;
+    p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev; p.pdl = m->pdl;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+    if ((rc = launch_qmv_epi(m->ctx, p, m->p_qkv, EPI_QKV, s))) return rc;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+    ++m->launches;
+    // D2: attention
+    AttnParams a;
+    a.nb = B; a.H = H; a.KVH = KVH; a.hd = hd; a.cap = D.cap; a.S = m->attn_S; a.q0 = m->q0; a.q16 = m->q16;
+    a.kc = m->kcache + l * layer_kv; a.vc = m->vcache + l * layer_kv; a.out = m->attn; a.part = m->apart;
+    a.counters = m->counters + 4096; a.err = m->ctx->err_dev; a.pdl = m->pdl;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+    if ((rc = launch_attention(m->ctx, a, s))) return rc;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+    ++m->launches;
+    // D3: o_proj + residual -> h
+    QmvParams q;
+    q.w = m->wo[l].tiles; q.sb = m->wo[l].sb; q.N = d; q.K = m->attn_dim; q.bits = D.bits; q.sdt = D.scale_dtype;
+    q.nb = B; q.x = m->attn; q.x_ld = m->attn_dim; q.out_f32 = m->h; q.out_ld = d; q.res16 = m->x16; q.res_ld = d;
+    q.part = m->part; q.counters = m->counters + 8192; q.err = m->ctx->err_dev; q.pdl = m->pdl;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+    if ((rc = launch_qmv_epi(m->ctx, q, m->p_wo, EPI_RES1, s))) return rc;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+    ++m->launches;
+    // D4: norm + gate/up + SiLU*mul -> act
+    QmvParams g;
+    g.w = m->gu[l].tiles; g.sb = m->gu[l].sb; g.N = 2 * F; g.K = d; g.bits = D.bits; g.sdt = D.scale_dtype;
+    g.nb = B; g.x = m->h; g.x_f32 = 1; g.x_ld = d; g.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d + d;
+    g.eps = D.eps; g.out_f16 = m->act; g.out_ld = F; g.part = m->part; g.counters = m->counters + 12288;
+    g.err = m->ctx->err_dev; g.pdl = m->pdl;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+    if ((rc = launch_qmv_epi(m->ctx, g, m->p_gu, EPI_SWIGLU, s))) return rc;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+    ++m->launches;
+    // D5: down + residual -> x16
+    QmvParams w;
+    w.w = m->down[l].tiles; w.sb = m->down[l].sb; w.N = d; w.K = F; w.bits = D.bits; w.sdt = D.scale_dtype;
+    w.nb = B; w.x = m->act; w.x_ld = F; w.out_f16 = m->x16; w.out_ld = d; w.res32 = m->h; w.res_ld = d;
+    w.part = m->part; w.counters = m->counters + 16384; w.err = m->ctx->err_dev; w.pdl = m->pdl;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+    if ((rc = launch_qmv_epi(m->ctx, w, m->p_down, EPI_RES2, s))) return rc;
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+    ++m->launches;
+  }
+  // head: final norm + lm_head + argmax + generation step
+  QmvParams hp;
+  hp.w = m->head.tiles; hp.sb = m->head.sb; hp.N = D.vocab; hp.K = d; hp.bits = D.bits; hp.sdt = D.scale_dtype;
+  hp.nb = B; hp.x = m->x16; hp.x_ld = d; hp.norm_gain = m->final_gain; hp.eps = D.eps;
+  hp.out_f32 = D.keep_logits ? m->logits : nullptr; hp.V = D.vocab; hp.embed = m->embed; hp.x_next = m->x16;
+  hp.d = d; hp.q0_rw = m->q0; hp.log = m->log; hp.tok_out = m->tok; hp.force_next = m->force_next;
+  hp.cap = D.cap; hp.pairs = m->pairs;
+  hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev; hp.pdl = m->pdl;
+  if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+  if ((rc = launch_qmv_epi(m->ctx, hp, m->p_head, EPI_ARGMAX, s))) return rc;
+  if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+  ++m->launches;
+  return 0;
+}
+
+int ensure_graph(agxc_model* m) {
+  if (m->exec) return 0;
+  cudaStream_t s = m->ctx->stream;
+  AGXC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(m, s);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  m->graph = g;
+  AGXC_CUDA(cudaGraphInstantiate(&m->exec, g, 0));
+  return 0;
+}
+
+}  // namespace
+
+int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
+  const agxc_model_desc& D = *desc;
+  if (D.bits != 4 && D.bits != 8) return fail(AGXC_EINVAL, "model: bits must be 4 or 8");
+  if (D.group != 64) return fail(AGXC_EINVAL, "model: group 64 only");
+  if (D.scale_dtype != 0 && D.scale_dtype != 1) return fail(AGXC_EINVAL, "model: scale_dtype fp16 (0) or bf16 (1)");
+  if (D.head_dim != 64 && D.head_dim != 128) return fail(AGXC_EINVAL, "model: head_dim 64 or 128");
+  if (D.n_kv_heads < 1 || D.n_heads % D.n_kv_heads) return fail(AGXC_EINVAL, "model: heads multiple of kv_heads");
+  if (D.n_heads / D.n_kv_heads > 8) return fail(AGXC_EINVAL, "model: at most 8 query heads per KV head");
+  if (D.d_model % 64 || D.ffn % 64 || (D.n_heads * D.head_dim) % 64)
+    return fail(AGXC_EINVAL, "model: d_model, ffn and heads*head_dim must be multiples of 64");
+  if (D.ffn % 16 || D.vocab % 16 || D.vocab < 16) return fail(AGXC_EINVAL, "model: vocab must be a multiple of 16");
+  if (D.batch < 1 || D.batch > 8) return fail(AGXC_EINVAL, "model: batch 1..8");
+  if (D.cap < 2) return fail(AGXC_EINVAL, "model: cap >= 2");
+  if (D.n_layers < 1) return fail(AGXC_EINVAL, "model: at least one layer");
+  if (D.d_model % 8) return fail(AGXC_EINVAL, "model: d_model multiple of 8");
+
+  agxc_model* m = new agxc_model();
+  m->ctx = ctx;
+  m->d = D;
+  const int L = D.n_layers, d = D.d_model, F = D.ffn, V = D.vocab, B = D.batch, hd = D.head_dim;
+  m->qkv_rows = (D.n_heads + 2 * D.n_kv_heads) * hd;
+  m->attn_dim = D.n_heads * hd;
+  int rc = 0;
+  auto bail = [&](int code) {
+    agxc_model_free(m);
+    return code;
+  };
+
+  // one allocation for every pack (tiles then scale/bias per matrix, 256-byte aligned)
+  struct Mat { agxc_pack* p; int n, k; };
+  m->qkv.resize(L); m->wo.resize(L); m->gu.resize(L); m->down.resize(L);
+  std::vector<Mat> mats;
+  for (int l = 0; l < L; ++l) {
+    mats.push_back({&m->qkv[l], m->qkv_rows, d});
+    mats.push_back({&m->wo[l], d, m->attn_dim});
+    mats.push_back({&m->gu[l], 2 * F, d});
+    mats.push_back({&m->down[l], d, F});
+  }
+  mats.push_back({&m->head, V, d});
+  size_t total = 0;
+  for (auto& x : mats) {
+    total += align_up(pack_tile_bytes(x.n, x.k, D.bits), 256);
+    total += align_up(pack_sb_bytes(x.n, x.k), 256);
+  }
+  void* wm = nullptr;
+  if ((rc = dalloc(m, &wm, total))) return bail(rc);
+  m->wmem = static_cast<uint8_t*>(wm);
+  size_t off = 0;
+  for (auto& x : mats) {
+    pack_init(*x.p, m, x.n, x.k);
+    x.p->tiles = m->wmem + off;
+    off += align_up(pack_tile_bytes(x.n, x.k, D.bits), 256);
+    x.p->sb = m->wmem + off;
+    off += align_up(pack_sb_bytes(x.n, x.k), 256);
+  }
+  for (int l = 0; l < L; ++l) m->gu[l].gateup = 1;
+
+  if ((rc = dalloc_t(m, &m->gains, static_cast<size_t>(L) * 2 * d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->bias, static_cast<size_t>(L) * m->qkv_rows))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->final_gain, d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->embed, static_cast<size_t>(V) * d))) return bail(rc);
+  const size_t kv = static_cast<size_t>(L) * B * D.n_kv_heads * D.cap * hd;
+  if ((rc = dalloc_t(m, &m->kcache, kv))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->vcache, kv))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->x16, static_cast<size_t>(B) * d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->h, static_cast<size_t>(B) * d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->q16, static_cast<size_t>(B) * m->attn_dim))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->attn, static_cast<size_t>(B) * m->attn_dim))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->act, static_cast<size_t>(B) * F))) return bail(rc);
+  if (D.keep_logits && (rc = dalloc_t(m, &m->logits, static_cast<size_t>(B) * V))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->q0, B))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->log, static_cast<size_t>(B) * D.cap))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->tok, B))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->force_next, B))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->cos_t, static_cast<size_t>(D.cap) * hd / 2))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->sin_t, static_cast<size_t>(D.cap) * hd / 2))) return bail(rc);
+
+  // plans and scratch
+  m->p_qkv = plan_qmv(ctx, m->qkv_rows, d, D.bits, B, EPI_QKV, hd, 0);
+  m->p_wo = plan_qmv(ctx, d, m->attn_dim, D.bits, B, EPI_RES1, hd, 0);
+  m->p_gu = plan_qmv(ctx, 2 * F, d, D.bits, B, EPI_SWIGLU, hd, 0);
+  m->p_down = plan_qmv(ctx, d, F, D.bits, B, EPI_RES2, hd, 0);
+  m->p_head = plan_qmv(ctx, V, d, D.bits, B, EPI_ARGMAX, hd, 0);
+  m->attn_S = attn_splits(ctx, B, D.n_kv_heads, D.cap);
+  size_t part = 0;
+  part = std::max(part, qmv_part_floats(m->p_qkv, m->qkv_rows, B, EPI_QKV));
+  part = std::max(part, qmv_part_floats(m->p_wo, d, B, EPI_RES1));
+  part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, B, EPI_SWIGLU));
+  part = std::max(part, qmv_part_floats(m->p_down, d, B, EPI_RES2));
+  if ((rc = dalloc_t(m, &m->part, std::max<size_t>(part, 64)))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->apart, attn_part_floats(B, D.n_heads, m->attn_S, hd)))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(m->p_head.grid) * 16))) return bail(rc);
+  m->counters_n = 24576;
+  if (static_cast<size_t>(m->qkv_rows / hd) > 4096 || static_cast<size_t>(B * D.n_kv_heads) > 4096 ||
+      static_cast<size_t>(2 * F / 32) > 4096 || static_cast<size_t>(d / 16) > 4096)
+    return bail(fail(AGXC_EINVAL, "model: too many epilogue blocks for the counter regions"));
+  if ((rc = dalloc_t(m, &m->counters, m->counters_n))) return bail(rc);
+  cudaStream_t s = ctx->stream;
+  if (cudaMemsetAsync(m->counters, 0, m->counters_n * sizeof(unsigned), s) != cudaSuccess ||
+      cudaMemsetAsync(m->kcache, 0, kv * 2, s) != cudaSuccess || cudaMemsetAsync(m->vcache, 0, kv * 2, s) != cudaSuccess ||
+      cudaMemsetAsync(m->q0, 0, B * 4, s) != cudaSuccess ||
+      cudaMemsetAsync(m->force_next, 0xFF, B * 4, s) != cudaSuccess ||
+      cudaMemsetAsync(m->log, 0xFF, static_cast<size_t>(B) * D.cap * 4, s) != cudaSuccess ||
+      cudaMemsetAsync(m->x16, 0, static_cast<size_t>(B) * d * 2, s) != cudaSuccess ||
+      cudaMemsetAsync(m->bias, 0, static_cast<size_t>(L) * m->qkv_rows * 2, s) != cudaSuccess)
+    return bail(fail(AGXC_ECUDA, "model: initial memset failed"));
+  // gains default to 1.0 (fp16 0x3C00)
+  {
+    std::vector<uint16_t> ones(std::max<size_t>(static_cast<size_t>(L) * 2 * d, d), 0x3C00);
+    if (cudaMemcpy(m->gains, ones.data(), static_cast<size_t>(L) * 2 * d * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->final_gain, ones.data(), static_cast<size_t>(d) * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(AGXC_ECUDA, "model: gain upload failed"));
+  }
+  // RoPE tables: angle p * theta^(-2i/hd) in double, cos/sin rounded once to fp32 (assemble.py:665-668)
+  {
+    const int half = hd / 2;
+    std::vector<float> c(static_cast<size_t>(D.cap) * half), sn(static_cast<size_t>(D.cap) * half);
+    for (int p = 0; p < D.cap; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double inv = std::pow(static_cast<double>(D.rope_theta), -(2.0 * i) / hd);
+        const double ang = static_cast<double>(p) * inv;
+        c[static_cast<size_t>(p) * half + i] = static_cast<float>(std::cos(ang));
+        sn[static_cast<size_t>(p) * half + i] = static_cast<float>(std::sin(ang));
+      }
+    if (cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(AGXC_ECUDA, "model: rope table upload failed"));
+  }
+  if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess)
+    return bail(fail(AGXC_ECUDA, "model: event create failed"));
+  if (cudaStreamSynchronize(s) != cudaSuccess) return bail(fail(AGXC_ECUDA, "model: setup sync failed"));
+  *out = m;
+  return 0;
+}
+
+int model_set_pack(agxc_model* m, int layer, int role, const void* packed, const void* scales, const void* biases,
+                   int on_device) {
+  const agxc_model_desc& D = m->d;
+  if (role != AGXC_ROLE_HEAD && (layer < 0 || layer >= D.n_layers)) return fail(AGXC_EINVAL, "set_pack: bad layer");
+  agxc_pack* dst = nullptr;
+  int n = 0, k = 0, stride = 1, offset = 0;
+  switch (role) {
+    case AGXC_ROLE_QKV: dst = &m->qkv[layer]; n = m->qkv_rows; k = D.d_model; break;
+    case AGXC_ROLE_WO: dst = &m->wo[layer]; n = D.d_model; k = m->attn_dim; break;
+    case AGXC_ROLE_GATE: dst = &m->gu[layer]; n = D.ffn; k = D.d_model; stride = 2; offset = 0; break;
+    case AGXC_ROLE_UP: dst = &m->gu[layer]; n = D.ffn; k = D.d_model; stride = 2; offset = 1; break;
+    case AGXC_ROLE_DOWN: dst = &m->down[layer]; n = D.d_model; k = D.ffn; break;
+    case AGXC_ROLE_HEAD: dst = &m->head; n = D.vocab; k = D.d_model; break;
+    default: return fail(AGXC_EINVAL, "set_pack: unknown role");
+  }
+  cudaStream_t s = m->ctx->stream;
+  const size_t pb = static_cast<size_t>(n) * k * D.bits / 8, sbb = static_cast<size_t>(n) * (k / 64) * 2;
+  const void* dp = packed;
+  const void* ds = scales;
+  const void* db = biases;
+  void* tmp = nullptr;
+  if (!on_device) {
+    AGXC_CUDA(cudaMalloc(&tmp, pb + 2 * sbb));
+    uint8_t* t = static_cast<uint8_t*>(tmp);
+    AGXC_CUDA(cudaMemcpy(t, packed, pb, cudaMemcpyHostToDevice));
+    AGXC_CUDA(cudaMemcpy(t + pb, scales, sbb, cudaMemcpyHostToDevice));
+    AGXC_CUDA(cudaMemcpy(t + pb + sbb, biases, sbb, cudaMemcpyHostToDevice));
+    dp = t; ds = t + pb; db = t + pb + sbb;
+  }
+  int rc = launch_relayout(static_cast<const uint32_t*>(dp), static_cast<const uint16_t*>(ds),
+                           static_cast<const uint16_t*>(db), n, k, D.bits, dst->tiles, dst->sb, stride, offset, s);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (tmp) cudaFree(tmp);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "set_pack sync");
+  return 0;
+}
+
+int model_set_vector(agxc_model* m, int layer, int which, const void* data, size_t bytes, int on_device) {
+  const agxc_model_desc& D = m->d;
+  void* dst = nullptr;
+  size_t want = 0;
+  switch (which) {
+    case AGXC_VEC_ATTN_GAIN: dst = m->gains + static_cast<size_t>(layer) * 2 * D.d_model; want = D.d_model * 2; break;
+    case AGXC_VEC_FFN_GAIN:
+      dst = m->gains + static_cast<size_t>(layer) * 2 * D.d_model + D.d_model; want = D.d_model * 2; break;
+    case AGXC_VEC_QKV_BIAS: dst = m->bias + static_cast<size_t>(layer) * m->qkv_rows; want = m->qkv_rows * 2; break;
+    case AGXC_VEC_FINAL_GAIN: dst = m->final_gain; want = D.d_model * 2; break;
+    case AGXC_VEC_EMBED: dst = m->embed; want = static_cast<size_t>(D.vocab) * D.d_model * 2; break;
+    default: return fail(AGXC_EINVAL, "set_vector: unknown vector");
+  }
+  if (which <= AGXC_VEC_QKV_BIAS && (layer < 0 || layer >= D.n_layers)) return fail(AGXC_EINVAL, "set_vector: layer");
+  if (bytes != want) return fail(AGXC_EINVAL, "set_vector: expected " + std::to_string(want) + " bytes");
+  AGXC_CUDA(cudaMemcpy(dst, data, bytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+  return 0;
+}
+
+__global__ void embed_rows_kernel(const __half* emb, int d, const uint32_t* toks, int n, __half* out) {
+  const int b = blockIdx.x;
+  if (b >= n) return;
+  const uint32_t t = toks[b];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) out[static_cast<size_t>(b) * d + i] = emb[static_cast<size_t>(t) * d + i];
+}
+
+int model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
+  const agxc_model_desc& D = m->d;
+  if (b < 0 || b >= D.batch) return fail(AGXC_EINVAL, "start: sequence index");
+  if (n < 1 || n > D.cap) return fail(AGXC_EINVAL, "start: prompt length must be 1..cap");
+  for (int i = 0; i < n; ++i)
+    if (prompt[i] < 0 || prompt[i] >= D.vocab) return fail(AGXC_EINVAL, "start: token id out of range");
+  cudaStream_t s = m->ctx->stream;
+  const size_t seq_kv = static_cast<size_t>(D.n_kv_heads) * D.cap * D.head_dim;
+  for (int l = 0; l < D.n_layers; ++l) {
+    const size_t off = (static_cast<size_t>(l) * D.batch + b) * seq_kv;
+    AGXC_CUDA(cudaMemsetAsync(m->kcache + off, 0, seq_kv * 2, s));
+    AGXC_CUDA(cudaMemsetAsync(m->vcache + off, 0, seq_kv * 2, s));
+  }
+  std::vector<uint32_t> log(D.cap, kTokenUnset);
+  for (int i = 0; i < n; ++i) log[i] = static_cast<uint32_t>(prompt[i]);
+  AGXC_CUDA(cudaMemcpyAsync(m->log + static_cast<size_t>(b) * D.cap, log.data(), D.cap * 4, cudaMemcpyHostToDevice, s));
+  const uint32_t zero = 0;
+  AGXC_CUDA(cudaMemcpyAsync(m->q0 + b, &zero, 4, cudaMemcpyHostToDevice, s));
+  AGXC_CUDA(cudaMemcpyAsync(m->x16 + static_cast<size_t>(b) * D.d_model,
+                            m->embed + static_cast<size_t>(prompt[0]) * D.d_model, D.d_model * 2,
+                            cudaMemcpyDeviceToDevice, s));
+  AGXC_CUDA(cudaStreamSynchronize(s));
+  return 0;
+}
+
+int model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {
+  const agxc_model_desc& D = m->d;
+  if (b < 0 || b >= D.batch || pos < 0 || n < 0 || pos + n > D.cap) return fail(AGXC_EINVAL, "force: range");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= D.vocab) return fail(AGXC_EINVAL, "force: token id out of range");
+  AGXC_CUDA(cudaMemcpy(m->log + static_cast<size_t>(b) * D.cap + pos, tokens, static_cast<size_t>(n) * 4,
+                       cudaMemcpyHostToDevice));
+  return 0;
+}
+
+__global__ void fill_normal_kernel(__half* dst, size_t n, uint64_t seed) {
+  // Box-Muller over a counter-based hash (splitmix64); a stand-in history, not a parity input
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i >= n) return;
+  uint64_t z = seed + 0x9E3779B97F4A7C15ull * (i + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  const float u1 = (static_cast<float>(z >> 40) + 1.0f) * (1.0f / 16777217.0f);
+  const float u2 = static_cast<float>((z >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+  dst[i] = __float2half_rn(sqrtf(-2.0f * logf(u1)) * cosf(6.2831853f * u2));
+}
+
+int model_fill_history(agxc_model* m, int b, int n, uint64_t seed) {
+  const agxc_model_desc& D = m->d;
+  if (b < 0 || b >= D.batch || n < 0 || n >= D.cap) return fail(AGXC_EINVAL, "fill_history: range");
+  cudaStream_t s = m->ctx->stream;
+  const size_t row = static_cast<size_t>(n) * D.head_dim;
+  for (int l = 0; l < D.n_layers; ++l)
+    for (int kv = 0; kv < D.n_kv_heads; ++kv) {
+      const size_t off = ((static_cast<size_t>(l) * D.batch + b) * D.n_kv_heads + kv) * D.cap * D.head_dim;
+      if (row) {
+        fill_normal_kernel<<<static_cast<unsigned>((row + 255) / 256), 256, 0, s>>>(m->kcache + off, row,
+                                                                                   seed * 131 + l * 17 + kv * 2);
+        fill_normal_kernel<<<static_cast<unsigned>((row + 255) / 256), 256, 0, s>>>(m->vcache + off, row,
+                                                                                   seed * 131 + l * 17 + kv * 2 + 1);
+      }
+    }
+  AGXC_CUDA(cudaGetLastError());
+  std::mt19937_64 rng(seed);
+  std::vector<uint32_t> log(D.cap, kTokenUnset);
+  for (int i = 0; i <= n; ++i) log[i] = static_cast<uint32_t>(rng() % static_cast<uint64_t>(D.vocab));
+  AGXC_CUDA(cudaMemcpyAsync(m->log + static_cast<size_t>(b) * D.cap, log.data(), D.cap * 4, cudaMemcpyHostToDevice, s));
+  const uint32_t q0 = static_cast<uint32_t>(n);
+  AGXC_CUDA(cudaMemcpyAsync(m->q0 + b, &q0, 4, cudaMemcpyHostToDevice, s));
+  AGXC_CUDA(cudaMemcpyAsync(m->x16 + static_cast<size_t>(b) * D.d_model,
+                            m->embed + static_cast<size_t>(log[n]) * D.d_model, D.d_model * 2, cudaMemcpyDeviceToDevice,
+                            s));
+  AGXC_CUDA(cudaStreamSynchronize(s));
+  return 0;
+}
+
+int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* tokens_out, float* logits_out,
+                 int sync_each, agxc_timing* t) {
+  const agxc_model_desc& D = m->d;
+  if (steps < 0) return fail(AGXC_EINVAL, "decode: steps");
+  if (forced_in) {
+    for (size_t i = 0; i < static_cast<size_t>(steps) * D.batch; ++i) {
+      const uint32_t f = static_cast<uint32_t>(forced_in[i]);
+      if (f != kTokenUnset && f >= static_cast<uint32_t>(D.vocab)) return fail(AGXC_EINVAL, "decode: forced token out of range");
+    }
+    const size_t nf = static_cast<size_t>(std::max(steps, 1)) * D.batch;
+    if (m->h_force_n < nf) {
+      if (m->h_force) cudaFreeHost(m->h_force);
+      m->h_force = nullptr;
+      AGXC_CUDA(cudaMallocHost(&m->h_force, nf * 4));
+      m->h_force_n = nf;
+    }
+    std::memcpy(m->h_force, forced_in, static_cast<size_t>(steps) * D.batch * 4);
+  }
+  if (logits_out && !D.keep_logits) return fail(AGXC_EINVAL, "decode: logits_out needs keep_logits");
+  int rc = ensure_graph(m);
+  if (rc) return rc;
+  cudaStream_t s = m->ctx->stream;
+  const size_t need = static_cast<size_t>(std::max(steps, 1)) * D.batch;
+  if (tokens_out && m->h_tok_n < need) {
+    if (m->h_tok) cudaFreeHost(m->h_tok);
+    m->h_tok = nullptr;
+    AGXC_CUDA(cudaMallocHost(&m->h_tok, need * 4));
+    m->h_tok_n = need;
+  }
+  const auto h0 = std::chrono::steady_clock::now();
+  AGXC_CUDA(cudaEventRecord(m->ev0, s));
+  for (int i = 0; i < steps; ++i) {
+    if (forced_in)  // this step's input: one token per sequence (UNSET = choose), pinned host -> device
+      AGXC_CUDA(cudaMemcpyAsync(m->force_next, m->h_force + static_cast<size_t>(i) * D.batch, D.batch * 4,
+                                cudaMemcpyHostToDevice, s));
+    AGXC_CUDA(cudaGraphLaunch(m->exec, s));
+    if (tokens_out)
+      AGXC_CUDA(cudaMemcpyAsync(m->h_tok + static_cast<size_t>(i) * D.batch, m->tok, D.batch * 4,
+                                cudaMemcpyDeviceToHost, s));
+    if (logits_out)
+      AGXC_CUDA(cudaMemcpyAsync(logits_out + static_cast<size_t>(i) * D.batch * D.vocab, m->logits,
+                                static_cast<size_t>(D.batch) * D.vocab * 4, cudaMemcpyDeviceToHost, s));
+    if (sync_each) AGXC_CUDA(cudaStreamSynchronize(s));
+  }
+  AGXC_CUDA(cudaEventRecord(m->ev1, s));
+  AGXC_CUDA(cudaEventSynchronize(m->ev1));
+  const auto h1 = std::chrono::steady_clock::now();
+  if (tokens_out) std::memcpy(tokens_out, m->h_tok, static_cast<size_t>(steps) * D.batch * 4);
+  uint32_t err = 0;
+  AGXC_CUDA(cudaMemcpy(&err, m->ctx->err_dev, 4, cudaMemcpyDeviceToHost));
+  if (t) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, m->ev0, m->ev1);
+    t->gpu_ms = ms;
+    t->host_ms = std::chrono::duration<float, std::milli>(h1 - h0).count();
+    t->launches_per_step = m->launches;
+  }
+  if (err) {
+    const uint32_t zero = 0;
+    cudaMemcpy(m->ctx->err_dev, &zero, 4, cudaMemcpyHostToDevice);
+    if (err & kErrMbarTimeout) return fail(AGXC_ETIMEOUT, "decode: a bounded device wait gave up");
+    return fail(AGXC_ECORRUPT, "decode: device error word " + std::to_string(err));
+  }
+  return 0;
+}
+
+int model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_launches) {
+  const int per_step = 5 * m->d.n_layers + 1;
+  std::vector<cudaEvent_t> ev(2 * per_step, nullptr);
+  for (auto& e : ev)
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      for (auto& x : ev)
+        if (x) cudaEventDestroy(x);
+      return fail(AGXC_ECUDA, "profile: event create failed");
+    }
+  for (int k = 0; k < 6; ++k) { kind_ms[k] = 0.f; kind_launches[k] = 0; }
+  cudaStream_t s = m->ctx->stream;
+  const int saved_pdl = m->pdl;
+  m->pdl = 0;  // events between launches: every kernel timed on its own
+  int rc = 0;
+  for (int i = 0; i < steps && !rc; ++i) {
+    rc = enqueue_step(m, s, ev.data());
+    if (rc) break;
+    if (cudaStreamSynchronize(s) != cudaSuccess) { rc = fail(AGXC_ECUDA, "profile: sync failed"); break; }
+    for (int j = 0; j < per_step; ++j) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, ev[2 * j], ev[2 * j + 1]);
+      const int kind = j == per_step - 1 ? 5 : j % 5;
+      kind_ms[kind] += ms;
+      kind_launches[kind] += 1;
+    }
+  }
+  m->pdl = saved_pdl;
+  for (auto& e : ev) cudaEventDestroy(e);
+  return rc;
+}
+
+void model_free(agxc_model* m) {
+  if (!m) return;
+  if (m->exec) cudaGraphExecDestroy(m->exec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  if (m->ev0) cudaEventDestroy(m->ev0);
+  if (m->ev1) cudaEventDestroy(m->ev1);
+  if (m->h_tok) cudaFreeHost(m->h_tok);
+  if (m->h_force) cudaFreeHost(m->h_force);
+  for (void* p : m->allocs) cudaFree(p);
+  delete m;
+}
+
+}  // namespace agxc
+
+// ---------------------------------------------------------------------------------------------- C ABI (model)
+extern "C" {
+
+int agxc_model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
+  if (!ctx || !desc || !out) return agxc::fail(AGXC_EINVAL, "model_create: null argument");
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return agxc::fail(AGXC_ECUDA, "model_create: cudaSetDevice");
+  return agxc::model_create(ctx, desc, out);
+}
+
+void agxc_model_free(agxc_model* m) { agxc::model_free(m); }
+
+int agxc_model_set_pack(agxc_model* m, int layer, int role, const void* packed, const void* scales,
+                        const void* biases, int on_device) {
+  if (!m || !packed || !scales || !biases) return agxc::fail(AGXC_EINVAL, "set_pack: null argument");
+  return agxc::model_set_pack(m, layer, role, packed, scales, biases, on_device);
+}
+
+int agxc_model_set_vector(agxc_model* m, int layer, int which, const void* data, size_t bytes, int on_device) {
+  if (!m || !data) return agxc::fail(AGXC_EINVAL, "set_vector: null argument");
+  return agxc::model_set_vector(m, layer, which, data, bytes, on_device);
+}
+
+int64_t agxc_model_weight_bytes(const agxc_model* m) {
+  if (!m) return 0;
+  int64_t t = m->head.bytes();
+  for (int l = 0; l < m->d.n_layers; ++l) t += m->qkv[l].bytes() + m->wo[l].bytes() + m->gu[l].bytes() + m->down[l].bytes();
+  return t;
+}
+
+int agxc_model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
+  if (!m || !prompt) return agxc::fail(AGXC_EINVAL, "start: null argument");
+  return agxc::model_start(m, b, prompt, n);
+}
+
+int agxc_model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {
+  if (!m || (!tokens && n)) return agxc::fail(AGXC_EINVAL, "force: null argument");
+  return agxc::model_force(m, b, pos, tokens, n);
+}
+
+int agxc_model_fill_history(agxc_model* m, int b, int n, uint64_t seed) {
+  if (!m) return agxc::fail(AGXC_EINVAL, "fill_history: null model");
+  return agxc::model_fill_history(m, b, n, seed);
+}
+
+int agxc_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* tokens_out, float* logits_out,
+                int sync_each, agxc_timing* t) {
+  if (!m) return agxc::fail(AGXC_EINVAL, "decode: null model");
+  return agxc::model_decode(m, steps, forced_in, tokens_out, logits_out, sync_each, t);
+}
+
+int agxc_model_state(agxc_model* m, int b, uint32_t* q0, uint32_t* log) {
+  if (!m || b < 0 || b >= m->d.batch) return agxc::fail(AGXC_EINVAL, "state: bad argument");
+  if (q0) AGXC_CUDA(cudaMemcpy(q0, m->q0 + b, 4, cudaMemcpyDeviceToHost));
+  if (log) AGXC_CUDA(cudaMemcpy(log, m->log + static_cast<size_t>(b) * m->d.cap, m->d.cap * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int agxc_model_read_kv(agxc_model* m, int layer, int b, int n, uint16_t* k_out, uint16_t* v_out) {
+  if (!m) return agxc::fail(AGXC_EINVAL, "read_kv: null model");
+  const agxc_model_desc& D = m->d;
+  if (layer < 0 || layer >= D.n_layers || b < 0 || b >= D.batch || n < 0 || n > D.cap)
+    return agxc::fail(AGXC_EINVAL, "read_kv: range");
+  for (int kv = 0; kv < D.n_kv_heads; ++kv) {
+    const size_t off = ((static_cast<size_t>(layer) * D.batch + b) * D.n_kv_heads + kv) * D.cap * D.head_dim;
+    const size_t bytes = static_cast<size_t>(n) * D.head_dim * 2;
+    if (k_out) AGXC_CUDA(cudaMemcpy(k_out + static_cast<size_t>(kv) * n * D.head_dim, m->kcache + off, bytes, cudaMemcpyDeviceToHost));
+    if (v_out) AGXC_CUDA(cudaMemcpy(v_out + static_cast<size_t>(kv) * n * D.head_dim, m->vcache + off, bytes, cudaMemcpyDeviceToHost));
+  }
+  return 0;
+}
+
+int agxc_model_logits_dev(agxc_model* m, const float** out) {
+  if (!m || !out) return agxc::fail(AGXC_EINVAL, "logits_dev: null argument");
+  if (!m->d.keep_logits) return agxc::fail(AGXC_EINVAL, "logits_dev: model made without keep_logits");
+  *out = m->logits;
+  return 0;
+}
+
+int agxc_model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_launches) {
+  if (!m || !kind_ms || !kind_launches || steps < 1) return agxc::fail(AGXC_EINVAL, "profile: bad argument");
+  return agxc::model_profile(m, steps, kind_ms, kind_launches);
+}
+
+int agxc_model_kernel_count(agxc_model* m, int32_t* n) {
+  if (!m || !n) return agxc::fail(AGXC_EINVAL, "kernel_count: null argument");
+  *n = 5 * m->d.n_layers + 1;
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,267 @@
+"""The layer builder: a decoder's weights, KV cache and decode graph on the B200 (the reference's
+agxforge/inference/assemble.py: configure 71-92, build 596-828; its region R and token log 650-669).
+
+    configure(config)           a config dict (or JSON path): {"model": name | shape overrides, "bits", "scale_dtype",
+                                "cap", "batch", "seed", "keep_logits"}; returns the normalised config
+    build(config, ...)          a DecodeModel: the library's model object with every pack, gain, bias and the
+                                embedding set. Synthetic weights are generated on the device from the config's seed
+                                (N(0, 0.02) fp32, then the device quantiser), or taken from given reference-format
+                                packs (`weights=`)
+    DecodeModel.start(b, prompt)  the sequence's prompt in its token log, x = embedding(prompt[0]), q0 = 0
+    DecodeModel.decode(steps)     run steps (execute.decode wraps it in the reference's report)
+
+The layer is five kernels (RMSNorm+qkv+bias+RoPE+append, split-KV attention + merge, o_proj + residual,
+RMSNorm+gate/up+SiLU*mul, down + residual) and the head one (final norm + vocabulary GEMV + argmax + generation
+step); a whole step is one CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+
+import numpy as np
+
+from agxforge_b200 import _native as N
+from agxforge_b200.inference import models
+from agxforge_b200.kernels import qmv as Q
+
+ROLE = {"qkv": N.ROLE_QKV, "wo": N.ROLE_WO, "gate": N.ROLE_GATE, "up": N.ROLE_UP, "down": N.ROLE_DOWN,
+        "head": N.ROLE_HEAD}
+ROLE_INDEX = {"qkv": 0, "wo": 1, "gate": 2, "up": 3, "down": 4, "head": 5}
+
+DEFAULTS = dict(model="internlm2.5-1.8b", bits=4, scale_dtype="fp16", cap=2048, batch=1, seed=2, keep_logits=False,
+                init_std=0.02, embed_std=0.02, bias_std=0.02)
+
+
+def configure(config):
+    """Normalise a config (dict or path of a JSON file)."""
+    if isinstance(config, (str, os.PathLike)):
+        with open(config) as f:
+            config = json.load(f)
+    cfg = dict(DEFAULTS)
+    cfg.update(config or {})
+    shape = cfg["model"]
+    if isinstance(shape, str):
+        shape = models.get(shape)
+    elif isinstance(shape, dict):
+        base = models.get(shape.pop("base")) if "base" in shape else None
+        shape = base.replace(**shape) if base else models.Model(**shape)
+    cfg["shape"] = shape
+    if cfg["bits"] not in (4, 8):
+        raise ValueError("configure: bits 4 or 8")
+    if cfg["scale_dtype"] not in Q.SCALE_DTYPES:
+        raise ValueError("configure: scale_dtype fp16 or bf16")
+    if not 1 <= int(cfg["batch"]) <= 8:
+        raise ValueError("configure: batch 1..8")
+    return cfg
+
+
+def _gen(torch, seed, *key):
+    g = torch.Generator(device="cuda")
+    g.manual_seed((int(seed) * 1000003 + hash_key(*key)) % (2 ** 63))
+    return g
+
+
+def hash_key(*key):
+    """A stable integer for a (layer, role) key (seed derivation; Python's hash() is salted per process)."""
+    h = 1469598103934665603
+    for part in key:
+        for ch in str(part).encode():
+            h = ((h ^ ch) * 1099511628211) % (2 ** 64)
+        h = ((h ^ 0xFF) * 1099511628211) % (2 ** 64)
+    return h
+
+
+class DecodeModel:
+    """The device model (owns the library's model object)."""
+
+    def __init__(self, cfg, device=0):
+        import torch
+        if not torch.cuda.is_available():
+            raise RuntimeError("agxforge_b200 needs a CUDA device (B200); none is visible")
+        self.cfg = cfg
+        self.shape = S = cfg["shape"]
+        self.device = device
+        self.bits = int(cfg["bits"])
+        self.batch = int(cfg["batch"])
+        self.cap = int(cfg["cap"])
+        d = N.ModelDesc(S.D_MODEL, S.LAYERS, S.HEADS, S.KV_HEADS, S.HEAD_DIM, S.FFN, S.VOCAB, self.bits, 64,
+                        Q.SCALE_DTYPES[cfg["scale_dtype"]], self.cap, self.batch, int(S.QKV_BIAS), float(S.EPS),
+                        float(S.ROPE_THETA), int(bool(cfg["keep_logits"])))
+        h = C.c_void_p()
+        torch.cuda.set_device(device)
+        N.check(N.lib().agxc_model_create(N.context(device), C.byref(d), C.byref(h)), "model_create")
+        self._h = h
+        self.packs = None   # reference-format packs kept on the host when build(keep_packs=True)
+
+    @property
+    def handle(self):
+        return self._h
+
+    # ---------------------------------------------------------------- weights
+    def set_pack(self, layer, role, packed, scales, biases):
+        """A reference-format pack (torch device tensors or numpy host arrays)."""
+        on_dev = not isinstance(packed, np.ndarray)
+        if on_dev:
+            import torch
+            torch.cuda.synchronize()
+            args = [C.c_void_p(t.data_ptr()) for t in (packed, scales, biases)]
+        else:
+            arrs = [np.ascontiguousarray(a) for a in (packed, scales, biases)]
+            args = [a.ctypes.data_as(C.c_void_p) for a in arrs]
+        N.check(N.lib().agxc_model_set_pack(self._h, layer, ROLE[role], *args, int(on_dev)), "set_pack %s" % role)
+
+    def set_vector(self, layer, which, data):
+        """fp16 vector: which in {"attn_gain", "ffn_gain", "qkv_bias", "final_gain", "embed"}."""
+        idx = {"attn_gain": N.VEC_ATTN_GAIN, "ffn_gain": N.VEC_FFN_GAIN, "qkv_bias": N.VEC_QKV_BIAS,
+               "final_gain": N.VEC_FINAL_GAIN, "embed": N.VEC_EMBED}[which]
+        if isinstance(data, np.ndarray):
+            a = np.ascontiguousarray(data.astype(np.float16, copy=False))
+            N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, a.ctypes.data_as(C.c_void_p), a.nbytes, 0),
+                    "set_vector %s" % which)
+        else:
+            import torch
+            t = data.to(torch.float16).contiguous()
+            torch.cuda.synchronize()
+            N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, C.c_void_p(t.data_ptr()),
+                                                  t.numel() * 2, 1), "set_vector %s" % which)
+
+    @property
+    def weight_bytes(self):
+        return int(N.lib().agxc_model_weight_bytes(self._h))
+
+    @property
+    def kernels_per_step(self):
+        n = C.c_int32()
+        N.check(N.lib().agxc_model_kernel_count(self._h, C.byref(n)))
+        return n.value
+
+    # ---------------------------------------------------------------- sequences
+    def start(self, b, prompt):
+        p = np.ascontiguousarray(np.asarray(prompt, np.int32))
+        N.check(N.lib().agxc_model_start(self._h, b, p.ctypes.data_as(C.c_void_p), p.size), "start")
+
+    def force(self, b, pos, tokens):
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        N.check(N.lib().agxc_model_force(self._h, b, pos, t.ctypes.data_as(C.c_void_p), t.size), "force")
+
+    def fill_history(self, b, n, seed=0):
+        N.check(N.lib().agxc_model_fill_history(self._h, b, n, seed), "fill_history")
+
+    def state(self, b):
+        q0 = np.zeros(1, np.uint32)
+        log = np.zeros(self.cap, np.uint32)
+        N.check(N.lib().agxc_model_state(self._h, b, q0.ctypes.data_as(C.c_void_p), log.ctypes.data_as(C.c_void_p)))
+        return int(q0[0]), log
+
+    def read_kv(self, layer, b, n):
+        S = self.shape
+        k = np.zeros((S.KV_HEADS, n, S.HEAD_DIM), np.uint16)
+        v = np.zeros_like(k)
+        N.check(N.lib().agxc_model_read_kv(self._h, layer, b, n, k.ctypes.data_as(C.c_void_p),
+                                           v.ctypes.data_as(C.c_void_p)), "read_kv")
+        return k.view(np.float16), v.view(np.float16)
+
+    def decode(self, steps, forced=None, want_tokens=True, want_logits=False, sync_each=False):
+        """Run `steps` steps. Returns (tokens [steps, batch] or None, logits [steps, batch, V] or None, timing dict)."""
+        B, V = self.batch, self.shape.VOCAB
+        toks = np.zeros((steps, B), np.int32) if want_tokens else None
+        lg = np.zeros((steps, B, V), np.float32) if want_logits else None
+        fin = None
+        if forced is not None:
+            fin = np.ascontiguousarray(np.asarray(forced, np.int64).astype(np.uint32).view(np.int32).reshape(steps, B))
+        t = N.Timing()
+        N.check(N.lib().agxc_decode(self._h, steps, None if fin is None else fin.ctypes.data_as(C.c_void_p),
+                                    None if toks is None else toks.ctypes.data_as(C.c_void_p),
+                                    None if lg is None else lg.ctypes.data_as(C.c_void_p), int(bool(sync_each)),
+                                    C.byref(t)), "decode")
+        return toks, lg, dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches_per_step=t.launches_per_step)
+
+    def close(self):
+        if getattr(self, "_h", None) and N._lib is not None:
+            N._lib.agxc_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+def synthetic_pack(torch, N_, K, bits, scale_dtype, gen, std, device):
+    """N(0, std) fp32 weights generated on the device, quantised on the device: reference-format (packed, s, b)."""
+    W = torch.randn((N_, K), generator=gen, device="cuda:%d" % device, dtype=torch.float32) * std
+    out = Q.quantize(W, bits=bits, scale_dtype=scale_dtype, device=device)
+    del W
+    return out
+
+
+def build(config, device=0, weights=None, keep_packs=False):
+    """Create the device model. `weights` (optional) = dict with reference-format packs {(layer, role): (packed,
+    scales, biases)} (roles qkv, wo, gate, up, down; (None, "head")) and fp16 vectors {"embed", "final_gain",
+    (layer, "attn_gain"), (layer, "ffn_gain"), (layer, "qkv_bias")}; missing entries are generated synthetically.
+    keep_packs=True keeps a host copy of every pack and vector in model.packs (for the CPU oracle); an integer n keeps
+    the packs of the first n layers only (and the head)."""
+    import torch
+    cfg = configure(config)
+    S = cfg["shape"]
+    m = DecodeModel(cfg, device)
+    bits, sdt, seed = m.bits, cfg["scale_dtype"], cfg["seed"]
+    weights = weights or {}
+    kept = {} if keep_packs else None
+
+    def host(t):
+        return t.cpu().numpy() if hasattr(t, "cpu") else t
+
+    keep_layers = S.LAYERS if keep_packs is True else int(keep_packs or 0)
+
+    def keep_pack(key, p):
+        if kept is not None and (key[0] is None or key[0] < keep_layers):
+            a, s, b = (host(x) for x in p)
+            kept[key] = (a.view(np.uint32), s.view(np.uint16), b.view(np.uint16))
+
+    # embedding first: a tied head is its quantisation
+    emb = weights.get("embed")
+    if emb is None:
+        emb = (torch.randn((S.VOCAB, S.D_MODEL), generator=_gen(torch, seed, "embed"), device="cuda:%d" % device)
+               * cfg["embed_std"]).to(torch.float16)
+    m.set_vector(0, "embed", emb)
+    if kept is not None:
+        kept["embed"] = host(emb).astype(np.float16)
+    for l in range(S.LAYERS):
+        for role, n, k in S.matrices():
+            p = weights.get((l, role))
+            if p is None:
+                p = synthetic_pack(torch, n, k, bits, sdt, _gen(torch, seed, l, role), cfg["init_std"], device)
+            m.set_pack(l, role, *p)
+            keep_pack((l, role), p)
+        for vec in ("attn_gain", "ffn_gain"):
+            v = weights.get((l, vec))
+            if v is not None:
+                m.set_vector(l, vec, v)
+            if kept is not None:
+                kept[(l, vec)] = np.asarray(host(v), np.float16) if v is not None else np.ones(S.D_MODEL, np.float16)
+        if S.QKV_BIAS:
+            v = weights.get((l, "qkv_bias"))
+            if v is None:
+                v = (torch.randn((S.QKV,), generator=_gen(torch, seed, l, "bias"), device="cuda:%d" % device)
+                     * cfg["bias_std"]).to(torch.float16)
+            m.set_vector(l, "qkv_bias", v)
+            if kept is not None:
+                kept[(l, "qkv_bias")] = host(v).astype(np.float16)
+    p = weights.get((None, "head"))
+    if p is None:
+        if S.TIED:
+            e32 = emb.to(torch.float32) if hasattr(emb, "to") else torch.from_numpy(np.asarray(emb, np.float32)).cuda()
+            p = Q.quantize(e32, bits=bits, scale_dtype=sdt, device=device)
+        else:
+            p = synthetic_pack(torch, S.VOCAB, S.D_MODEL, bits, sdt, _gen(torch, seed, "head"), cfg["init_std"], device)
+    m.set_pack(0, "head", *p)
+    keep_pack((None, "head"), p)
+    fg = weights.get("final_gain")
+    if fg is not None:
+        m.set_vector(0, "final_gain", fg)
+    if kept is not None:
+        kept["final_gain"] = np.asarray(host(fg), np.float16) if fg is not None else np.ones(S.D_MODEL, np.float16)
+    torch.cuda.synchronize()
+    m.packs = kept
+    return m

@@ -1,0 +1,25 @@
+"""RMSNorm for decode (the reference's agxforge/kernels/norm.py:42-155 build_rmsnorm_wide): one row per CTA,
+y = fp16(x * rsqrt(mean(x^2) + eps) * g). Inside the decode step the norm is fused into the GEMV that consumes it
+(qmv.qmv(..., norm_gain=g)); this standalone form is the final norm's reference shape and a test surface."""
+from __future__ import annotations
+
+import ctypes as C
+
+from agxforge_b200 import _native as N
+
+
+def rmsnorm(x, g, eps=1e-6, device=0):
+    import torch
+    if x.dim() == 1:
+        x = x[None]
+    nb, d = x.shape
+    if g.shape[-1] != d or g.dtype != torch.float16:
+        raise ValueError("rmsnorm: gain fp16 [d]")
+    if x.dtype not in (torch.float16, torch.float32):
+        raise ValueError("rmsnorm: x fp16 or fp32")
+    x, g = x.contiguous(), g.contiguous()
+    out = torch.empty((nb, d), dtype=torch.float16, device=x.device)
+    N.check(N.lib().agxc_rmsnorm_dev(N.context(device), N.ptr(x), int(x.dtype == torch.float32), nb, d, N.ptr(g),
+                                     float(eps), N.ptr(out), C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+            "rmsnorm")
+    return out

@@ -1,0 +1,322 @@
+"""Benchmark of the quantized decode path on B200: decode tok/s and % of the HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config internlm-q4-1792]
+
+Default workload (BASELINE config 3 at its headline point): InternLM2.5-1.8B-shaped decoder, random-init (seed 2,
+N(0, 0.02) weights, 4-bit affine group 64 with fp16 scale/bias), batch 1, a history of 1,792 uniform-random token
+ids, then K greedy decode steps at positions 1,792 .. 1,792+K-1 (W warm-up steps just before them). A step is one
+token: one CUDA-graph replay of the 121 kernels. Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB of KV
+per token against a 126 MB L2), so no flush is needed between steps.
+
+One JSON line on rank 0:
+  value          tokens/s over the K timed steps (device time, CUDA events, inputs resident in HBM), summed over ranks
+  e2e            the same steps through the public C-ABI decode call with a host->device copy of each step's input
+                 token (pinned) and a device->host read of its chosen token, host-synchronised every step
+  roofline       the dominant kernel (largest share of step time, from a CUDA-event profile of every launch):
+                 algorithmic bytes per launch / its mean launch time, against the measured HBM copy bandwidth
+  step_roofline  the whole step: (pack bytes + KV bytes read) per token x tokens/s, against the same peak
+  cpu_baseline   the reference's CPU decode step (its QSim chain) as the numpy FP32 port in oracle/cpu_decode.py,
+                 timed on this host's cores on a bounded sample (a few layers + the head of one token, scaled)
+Multi-GPU (torchrun, --gpus N): configs 1-4 do not shard (replicas only): every rank decodes its own sequence on its
+own GPU, timing is the max over ranks, `value` sums the tokens of all ranks ("scaling": "weak").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (model, bits, batch, history)
+    "internlm-q4-1792": ("internlm2.5-1.8b", 4, 1, 1792),
+    "internlm-q4-196": ("internlm2.5-1.8b", 4, 1, 196),
+    "internlm-q8-1792": ("internlm2.5-1.8b", 8, 1, 1792),
+    "internlm-q8-1792-b8": ("internlm2.5-1.8b", 8, 8, 1792),
+    "qwen-q4-196": ("qwen2.5-0.5b", 4, 1, 196),
+}
+METRIC = "decode tok/s and % HBM roofline (batch 1, ctx 1792, 4-bit) vs CPU ref"
+KIND_NAMES = ["qkv", "attn", "wo", "ffn", "down", "head"]
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, max clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(gpus):
+    if gpus <= 1 or "RANK" not in os.environ:
+        return 0, 1, 0, None
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world, local, dist
+
+
+def cpu_baseline_sample(m, sample_layers, pos):
+    """Time the numpy FP32 port of the reference's CPU decode step on `sample_layers` layers + the head."""
+    from oracle.cpu_decode import CpuDecoder
+    cpu = CpuDecoder(m.shape, m.packs, m.bits, m.cfg["scale_dtype"], pos + 2)
+    t_layer, t_head = cpu.timed_sample(sample_layers, pos)
+    per_token = t_layer * m.shape.LAYERS + t_head
+    return per_token, t_layer, t_head, cpu.threads
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference's CPU implementation of the path (the port; the reference's Python package
+    cannot travel with this repository) on this host's cores, same config/metric."""
+    import torch
+    from agxforge_b200.inference import assemble
+    model, bits, batch, hist = CONFIGS[args.config]
+    cfg = dict(model=model, bits=bits, batch=1, cap=hist + 8, seed=2)
+    # the packs come from the same device quantiser as our arm (same seeded weights), copied to the host
+    m = assemble.build(cfg, keep_packs=args.ref_layers)
+    torch.cuda.synchronize()
+    samples = []
+    for i in range(max(1, args.ref_steps)):
+        per_token, t_layer, t_head, cores = cpu_baseline_sample(m, args.ref_layers, hist)
+        samples.append(per_token)
+    per_token = statistics.median(samples)
+    v = batch / per_token if batch == 1 else 1.0 / per_token
+    line = dict(metric=METRIC, impl="reference", value=round(1.0 / per_token, 5), unit="tok/s", n_gpus=args.gpus,
+                steps=args.steps, warmup=args.warmup, ms_per_step=round(per_token * 1e3, 1), higher_is_better=True,
+                scaling="weak", vs_baseline=None, dtype="f32", data="synthetic",
+                config=dict(workload=args.config, model=model, bits=bits, batch=1, history=hist),
+                cpu_baseline=dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores, kind="port",
+                                  sample="%d of %d layers + head of one token at position %d, median of %d, scaled "
+                                         "to the full depth" % (args.ref_layers, m.shape.LAYERS, hist,
+                                                                 len(samples))),
+                e2e=dict(value=round(1.0 / per_token, 5), unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="internlm-q4-1792", choices=sorted(CONFIGS))
+    ap.add_argument("--ref-layers", type=int, default=2)
+    ap.add_argument("--ref-steps", type=int, default=1)
+    ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+
+    rank, world, local, dist = dist_setup(args.gpus)
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, rank)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    import torch
+    from agxforge_b200.inference import assemble
+
+    model, bits, batch, hist = CONFIGS[args.config]
+    K, W = args.steps, args.warmup
+    cap = hist + K + 8
+    keep = args.ref_layers if (rank == 0 and not args.no_cpu) else False
+    m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=2 + rank), device=local,
+                       keep_packs=keep)
+    S = m.shape
+    rng = np.random.default_rng(1792 + rank)
+    # the history: prompt of hist - W + 1 random ids, consumed by the decode loop; then W warm-up steps at positions
+    # hist - W .. hist - 1; the timed steps are at positions hist .. hist + K - 1
+    P = hist - W + 1
+    for b in range(batch):
+        m.start(b, rng.integers(0, S.VOCAB, P).tolist())
+    m.decode(P - 1 + W, want_tokens=False)
+    torch.cuda.synchronize()
+
+    # ---- timed: K graph replays back to back, CUDA events on the library's stream
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        _, _, t = m.decode(K, want_tokens=False)
+    torch.cuda.synchronize()
+    gpu_ms = t["gpu_ms"]
+    launches = t["launches_per_step"]
+    if dist is not None:
+        tt = torch.tensor([gpu_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        gpu_ms = float(tt.item())
+        dist.barrier()
+    tok_s = world * batch * K / (gpu_ms / 1e3)
+
+    # ---- e2e: the same number of steps through the C-ABI decode call, host input and output every step
+    if dist is not None:
+        dist.barrier()
+    forced = np.full((K, batch), 0xFFFFFFFF, np.uint64)     # the step's input: "no forced token" (4 B per seq)
+    t0 = time.perf_counter()
+    _, _, te = m.decode(K, forced=forced, want_tokens=True, sync_each=True)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e_tok_s = world * batch * K / e2e_s
+
+    # ---- per-kernel profile (CUDA events around every launch, no overlap) -> the dominant kernel's roofline
+    import ctypes as C
+    from agxforge_b200 import _native as N
+    kind_ms = (C.c_float * 6)()
+    kind_n = (C.c_int32 * 6)()
+    N.check(N.lib().agxc_model_profile(m.handle, args.profile_steps, kind_ms, kind_n), "profile")
+    pos_mid = hist + K + W // 2
+    kvrow = 2 * S.KV_HEADS * S.HEAD_DIM * 2                      # K+V bytes per position per layer
+    from agxforge_b200.inference.models import Model  # noqa: F401
+    mats = {r: (n, k) for r, n, k in S.matrices()}
+
+    def pack_bytes(n, k):
+        return n * k * bits // 8 + (n * k // 64) * 4
+    kind_bytes = {
+        "qkv": pack_bytes(*mats["qkv"]) * batch ** 0,
+        "attn": batch * kvrow * (pos_mid + 1),
+        "wo": pack_bytes(*mats["wo"]),
+        "ffn": pack_bytes(*mats["gate"]) + pack_bytes(*mats["up"]),
+        "down": pack_bytes(*mats["down"]),
+        "head": pack_bytes(S.VOCAB, S.D_MODEL),
+    }
+    total_ms = sum(kind_ms[i] for i in range(6))
+    dom = max(range(6), key=lambda i: kind_ms[i])
+    dname = KIND_NAMES[dom]
+    per_launch_ms = kind_ms[dom] / max(1, kind_n[dom])
+    peak, peak_kind = peaks()
+    achieved = kind_bytes[dname] / (per_launch_ms / 1e3) / 1e9
+    kinds = {KIND_NAMES[i]: dict(launches=int(kind_n[i]), ms=round(kind_ms[i], 4),
+                                 share=round(kind_ms[i] / total_ms, 4) if total_ms else None,
+                                 us_per_launch=round(1e3 * kind_ms[i] / max(1, kind_n[i]), 3),
+                                 gbs=round(kind_bytes[KIND_NAMES[i]] / (kind_ms[i] / max(1, kind_n[i]) / 1e3) / 1e9, 1)
+                                 if kind_ms[i] > 0 else None) for i in range(6)}
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.md")
+    if os.path.exists(tpath):
+        for ln in open(tpath):
+            if ln.startswith("traffic %s %s " % (args.config, dname)):
+                try:
+                    traffic = int(ln.split()[3])
+                except (IndexError, ValueError):
+                    traffic = None
+
+    # whole-step algorithmic bytes: every pack once + every sequence's KV over the timed positions (mean)
+    w_bytes = m.weight_bytes
+    kv_bytes = batch * S.LAYERS * kvrow * (hist + (K - 1) / 2.0 + 1)
+    step_bytes = w_bytes + kv_bytes
+    step_s = gpu_ms / 1e3 / K
+    step_gbs = step_bytes / step_s / 1e9
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        per_token, t_layer, t_head, cores = cpu_baseline_sample(m, args.ref_layers, hist)
+        cpu = dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores, kind="port",
+                   sample="%d of %d layers + head of one token at position %d (%.2f s/layer, %.2f s head), scaled "
+                          "to the full depth" % (args.ref_layers, S.LAYERS, hist, t_layer, t_head))
+
+    if rank == 0:
+        line = dict(
+            metric=METRIC, value=round(tok_s, 2), unit="tok/s", n_gpus=world, steps=K, warmup=W,
+            ms_per_step=round(gpu_ms / K, 4), higher_is_better=True, scaling="weak", vs_baseline=None, dtype="u4" if
+            bits == 4 else "u8", data="synthetic (seeded random-init weights and uniform-random token ids)",
+            config=dict(workload=args.config, model=model, bits=bits, group=64, scale_dtype="fp16", batch=batch,
+                        history=hist, positions=[hist, hist + K - 1], parallelism="replicas" if world > 1 else "1gpu",
+                        l2="inputs larger than L2 (%.2f GB per step vs 126 MB L2)" % (step_bytes / 1e9)),
+            e2e=dict(value=round(e2e_tok_s, 2), unit="tok/s", h2d_bytes_per_step=4 * batch,
+                     d2h_bytes_per_step=4 * batch),
+            roofline=dict(bound="hbm", kernel=dname, achieved=round(achieved, 1), peak=peak, unit="GB/s",
+                          frac=round(achieved / peak, 4), traffic=traffic, peak_source=peak_kind,
+                          bytes_per_launch=kind_bytes[dname], us_per_launch=round(per_launch_ms * 1e3, 3)),
+            step_roofline=dict(bound="hbm", achieved=round(step_gbs, 1), peak=peak, unit="GB/s",
+                               frac=round(step_gbs / peak, 4), bytes_per_token=int(step_bytes / batch),
+                               weight_bytes=w_bytes, peak_source=peak_kind),
+            kernels=kinds,
+            cpu_baseline=cpu,
+            clocks=clk.summary(),
+            gpu_launches=int(launches * K),
+        )
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+/* agxc.h — C ABI of libagxcuda.so, the B200 (sm_100a) quantized-decode library.
+ *
+ * This ABI replaces the process boundary of the reference's decode path: agxforge/inference/execute.py:37-49 runs
+ * the Metal executor tools/g17decodegen.m as a subprocess (graph.json in, a JSON report out). Here the host calls
+ * these entry points in-process; the Python package agxforge_b200 binds them with ctypes.
+ *
+ * Conventions
+ *   - Every entry point returns 0 (AGXC_OK) or a negative AGXC_E* code; agxc_last_error() gives the message for the
+ *     calling thread's last failure.
+ *   - Pointers named *_dev are device pointers (e.g. from torch tensors; the caller keeps ownership). Host arrays
+ *     are read or written synchronously and never retained.
+ *   - A context owns one device and one CUDA stream; calls on one context are not concurrent. A model owns every
+ *     device buffer it allocates (weights, KV cache, activations, scratch) and frees them in agxc_model_free.
+ *   - `stream` arguments are cudaStream_t values passed as void* (NULL = the context's stream).
+ */
+#ifndef AGXC_H
+#define AGXC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AGXC_API __attribute__((visibility("default")))
+#else
+#define AGXC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AGXC_OK 0
+#define AGXC_EINVAL (-1)      /* bad argument or shape (the reference raises ValueError, qmv.py:74-80) */
+#define AGXC_ECUDA (-2)       /* a CUDA runtime call failed */
+#define AGXC_ENCCL (-3)       /* a collective failed */
+#define AGXC_ETIMEOUT (-4)    /* a bounded device wait gave up (the kernel set the error word) */
+#define AGXC_ECORRUPT (-5)    /* a guard or sentinel check failed */
+#define AGXC_ENOMEM (-6)      /* device allocation failed */
+#define AGXC_EUNSUPPORTED (-7)
+
+#define AGXC_SCALE_FP16 0
+#define AGXC_SCALE_BF16 1
+
+#define AGXC_TOKEN_UNSET 0xFFFFFFFFu  /* a free log entry: the model chooses (agxforge/kernels/argmax.py:133-145) */
+
+typedef struct agxc_ctx agxc_ctx;
+typedef struct agxc_pack agxc_pack;
+typedef struct agxc_model agxc_model;
+
+/* ---- context -------------------------------------------------------------------------------------------- */
+AGXC_API const char* agxc_last_error(void);
+AGXC_API int agxc_version(void);
+/* Opens `device` and creates the context's stream. */
+AGXC_API int agxc_init(int device, agxc_ctx** out);
+AGXC_API void agxc_ctx_free(agxc_ctx* ctx);
+AGXC_API int agxc_ctx_sync(agxc_ctx* ctx);
+/* The context's device error word (bounded waits that gave up set bits in it); 0 = clean. Reading clears it. */
+AGXC_API int agxc_ctx_error_word(agxc_ctx* ctx, uint32_t* word);
+
+/* ---- weight packs (agxforge/kernels/qmv.py:17-18, 1854-1880) ------------------------------------------------
+ * Reference format: packed uint32 [n][k*bits/32], element k of row n in bits [bits*(k % (32/bits)), ...) of word
+ * k/(32/bits) (low field first); scales and biases 16-bit [n][k/group] (fp16 or bf16 patterns). */
+typedef struct {
+  int32_t n, k, bits, group, scale_dtype;
+} agxc_pack_desc;
+
+/* Quantise fp32 weights [n][k] on the device into the reference format (replaces qmv.quantize, qmv.py:1854). */
+AGXC_API int agxc_quantize_dev(agxc_ctx* ctx, const agxc_pack_desc* desc, const float* w_dev, uint32_t* packed_dev,
+                      uint16_t* scales_dev, uint16_t* biases_dev, void* stream);
+
+/* Upload a reference-format pack and re-lay it out for the B200 GEMV (16x64 tiles, 128-bit loads per lane).
+ * `on_device` = 1 when the three arrays are device pointers, 0 when they are host arrays. */
+AGXC_API int agxc_pack_create(agxc_ctx* ctx, const agxc_pack_desc* desc, const void* packed, const void* scales,
+                     const void* biases, int on_device, agxc_pack** out);
+AGXC_API void agxc_pack_free(agxc_pack* pack);
+/* Bytes of the device copy (fields + scale/bias), for roofline accounting. */
+AGXC_API int64_t agxc_pack_bytes(const agxc_pack* pack);
+/* The pack's fields unpacked to uint8 [n][k] (replaces assemble._unpack, assemble.py:834-840) and its fp32 weights
+ * w = fma(q, s, b) rounded once (the dequant contract of qmv_dq_reference, qmv.py:1699-1750). Device outputs. */
+AGXC_API int agxc_pack_unpack_dev(const agxc_pack* pack, uint8_t* fields_dev, void* stream);
+AGXC_API int agxc_pack_dequant_dev(const agxc_pack* pack, float* w_dev, void* stream);
+
+/* ---- the GEMV family (agxforge/kernels/qmv.py build_qmv2 341-881 and its epilogues) ---------------------------
+ * y[b][n] = sum_k x[b][k] * (s[n,g] q[n,k] + b[n,g]) for nb <= 8 activation rows b, with an optional RMSNorm of x
+ * fused in front (qmv.with_norm, qmv.py:176-183) and one epilogue: */
+#define AGXC_EPI_F32 0        /* y fp32 [nb][n]                                                  (qmv2 plain)    */
+#define AGXC_EPI_RES1 1       /* h fp32 = y + x16 residual                              (with_residual add16)    */
+#define AGXC_EPI_RES2 2       /* x16 fp16 = fp16(y + h)                            (with_residual add32_to16)    */
+#define AGXC_EPI_SWIGLU 3     /* act fp16 [nb][n/2] = fp16(silu(gate) * up); pack made with agxc_pack_create_gateup */
+
+typedef struct {
+  const agxc_pack* pack;
+  int32_t nb;                 /* activation rows, 1..8 */
+  const void* x_dev;          /* [nb][x_ld], fp16 (x_f32 = 0) or fp32 (x_f32 = 1) */
+  int32_t x_f32, x_ld;
+  const uint16_t* norm_gain_dev; /* fp16 [k]; non-NULL = RMSNorm x first: fp16(x * rsqrt(mean(x^2) + eps) * g) */
+  float eps;
+  int32_t epi;
+  void* out_dev;              /* fp32 [nb][out_ld] (F32, RES1) or fp16 [nb][out_ld] (RES2, SWIGLU) */
+  int32_t out_ld;
+  const void* res_dev;        /* RES1: fp16 [nb][res_ld]; RES2: fp32 [nb][res_ld] */
+  int32_t res_ld;
+  int32_t splits;             /* K chunks; 0 = planner's choice */
+} agxc_qmv_args;
+
+/* Gate and up projections [f][k] each, re-laid out as ONE interleaved pack of 2f rows for the fused SwiGLU
+ * (replaces qmv_swiglu_layout, qmv.py:214-219). Arrays as in agxc_pack_create. */
+AGXC_API int agxc_pack_create_gateup(agxc_ctx* ctx, const agxc_pack_desc* desc_each, const void* g_packed,
+                            const void* g_scales, const void* g_biases, const void* u_packed, const void* u_scales,
+                            const void* u_biases, int on_device, agxc_pack** out);
+
+AGXC_API int agxc_qmv(agxc_ctx* ctx, const agxc_qmv_args* args, void* stream);
+
+/* Standalone RMSNorm rows (norm.build_rmsnorm_wide, agxforge/kernels/norm.py:42-155): out fp16 [nb][d]. */
+AGXC_API int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int nb, int d, const uint16_t* gain_dev,
+                     float eps, uint16_t* out_dev, void* stream);
+
+/* ---- decode attention (agxforge/kernels/attention.py: split 86-165, merge 1326-1371; attn_reference 1458) -----
+ * One query row per head at position q0[b] (keys 0..q0, q0 clamped to cap-1); q16 fp16 [nb][heads][head_dim]
+ * already scaled by log2(e)/sqrt(head_dim) (the softmax is base 2); caches fp16 [nb][kv_heads][cap][head_dim];
+ * out fp16 [nb][heads*head_dim]. Split-KV over `splits` chunks (0 = planner) with a log-sum-exp merge. */
+AGXC_API int agxc_attention_dev(agxc_ctx* ctx, int nb, int heads, int kv_heads, int head_dim, int cap, const uint32_t* q0_dev,
+                       const uint16_t* q16_dev, const uint16_t* k_dev, const uint16_t* v_dev, uint16_t* out_dev,
+                       int splits, void* stream);
+
+/* ---- the model (agxforge/inference/assemble.py configure 71-92, build 596-828; models.py 26-54) -------------- */
+typedef struct {
+  int32_t d_model, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab;
+  int32_t bits, group, scale_dtype;
+  int32_t cap;                /* KV capacity and token-log length per sequence */
+  int32_t batch;              /* independent sequences decoded together, 1..8 */
+  int32_t qkv_bias;           /* 1 = the qkv projection has a bias (Qwen2) */
+  float eps, rope_theta;
+  int32_t keep_logits;        /* 1 = keep the head's fp32 logits [batch][vocab] readable after each step */
+} agxc_model_desc;
+
+#define AGXC_ROLE_QKV 0
+#define AGXC_ROLE_WO 1
+#define AGXC_ROLE_GATE 2
+#define AGXC_ROLE_UP 3
+#define AGXC_ROLE_DOWN 4
+#define AGXC_ROLE_HEAD 5      /* layer ignored */
+#define AGXC_VEC_ATTN_GAIN 0  /* fp16 [d] */
+#define AGXC_VEC_FFN_GAIN 1   /* fp16 [d] */
+#define AGXC_VEC_QKV_BIAS 2   /* fp16 [qkv rows] */
+#define AGXC_VEC_FINAL_GAIN 3 /* fp16 [d], layer ignored */
+#define AGXC_VEC_EMBED 4      /* fp16 [vocab][d], layer ignored */
+
+AGXC_API int agxc_model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out);
+AGXC_API void agxc_model_free(agxc_model* m);
+/* Set one projection from a reference-format pack (host or device arrays); gate and up are interleaved internally. */
+AGXC_API int agxc_model_set_pack(agxc_model* m, int layer, int role, const void* packed, const void* scales,
+                        const void* biases, int on_device);
+/* Set one fp16 vector (gains, bias, embedding table). */
+AGXC_API int agxc_model_set_vector(agxc_model* m, int layer, int which, const void* data, size_t bytes, int on_device);
+/* Algorithmic bytes of the model's packs (fields + 16-bit scale and bias), for roofline accounting. */
+AGXC_API int64_t agxc_model_weight_bytes(const agxc_model* m);
+
+/* Start sequence b: clears its KV cache and log, writes its prompt (n tokens, n >= 1) into the token log, puts the
+ * embedding of prompt[0] in x and sets q0 = 0 (assemble.py:650-669's R_init). Later decode steps take the logged
+ * tokens (teacher forcing, tools/g17forcehistory.py) until the log runs out, then choose by argmax. */
+AGXC_API int agxc_model_start(agxc_model* m, int b, const int32_t* prompt, int n);
+/* Overwrite log entries [pos, pos+n) of sequence b from the host (forcing), without touching q0. */
+AGXC_API int agxc_model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n);
+/* Fill positions [0, n) of every layer's KV cache of sequence b with seeded N(0,1) fp16 values and set q0 = n
+ * (a stand-in history for throughput runs whose histories are too long to decode through). */
+AGXC_API int agxc_model_fill_history(agxc_model* m, int b, int n, uint64_t seed);
+
+/* Run `steps` decode steps (one token per sequence per step, the whole step one CUDA graph replay; the reference's
+ * pipelined executor loop, tools/g17decodegen.m:264-290). Each step's token per sequence is: the step's entry of
+ * `forced_in` (host, [steps][batch], AGXC_TOKEN_UNSET = none; copied host -> device before the step) if given and
+ * set, else the token log's entry at q0 + 1 (the prompt), else the first argmax of the logits. After each step the
+ * chosen tokens are device-resident; when `tokens_out` (host, [steps][batch]) is non-NULL each step's tokens are
+ * copied back, and when `logits_out` (host, [steps][batch][vocab], needs keep_logits) is non-NULL, the logits too.
+ * `sync_each` = 1 waits for every step (the host sees each token before the next launch). */
+typedef struct {
+  float gpu_ms;               /* device time of the steps (CUDA events) */
+  float host_ms;              /* host wall time of the call */
+  int32_t launches_per_step;  /* kernels in one step's graph */
+} agxc_timing;
+AGXC_API int agxc_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* tokens_out, float* logits_out,
+                int sync_each, agxc_timing* t);
+
+/* Copy the state of sequence b to the host: q0 and the token log (cap entries). */
+AGXC_API int agxc_model_state(agxc_model* m, int b, uint32_t* q0, uint32_t* log);
+/* Read back layer `layer`'s K and V cache rows [0, n) of sequence b (fp16 patterns, [kv_heads][n][head_dim] each). */
+AGXC_API int agxc_model_read_kv(agxc_model* m, int layer, int b, int n, uint16_t* k_out, uint16_t* v_out);
+/* Device pointer of the last step's logits [batch][vocab] fp32 (keep_logits) for in-place checks. */
+AGXC_API int agxc_model_logits_dev(agxc_model* m, const float** out);
+
+/* Run `steps` decode steps with every kernel launched on its own between two CUDA events (no graph, no overlap)
+ * and return, per kernel kind, the summed device time (ms) and the number of launches. Kinds: */
+#define AGXC_KIND_QKV 0
+#define AGXC_KIND_ATTN 1
+#define AGXC_KIND_WO 2
+#define AGXC_KIND_FFN 3
+#define AGXC_KIND_DOWN 4
+#define AGXC_KIND_HEAD 5
+AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/, int32_t* kind_launches /*[6]*/);
+
+/* Kernels per decode step and their names (for launch accounting). */
+AGXC_API int agxc_model_kernel_count(agxc_model* m, int32_t* n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AGXC_H */

@@ -1,0 +1,132 @@
+"""Model-level parity on the B200: the whole decode step (5 kernels a layer + the head) under teacher forcing,
+every step's logits against the FP64 oracle (bound 0.05 + 0.003*|ref|) and the argmax against the half-transport
+oracle; the device token log, q0 and KV cache rows against the oracle's.
+
+Small shapes run all layers; the BASELINE shapes run at full width and full vocabulary with fewer layers (the
+kernels are the same per layer; depth only repeats them), so the FP64 oracle finishes in seconds."""
+import numpy as np
+import pytest
+
+from oracle import decoder as D
+
+from tests import modelcheck as MC
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    if not t.cuda.is_available():
+        pytest.skip("no GPU")
+    return t
+
+
+def _build(shape, bits=4, batch=1, cap=256, seed=0, sdt="fp16"):
+    from agxforge_b200.inference import assemble
+    return assemble.build(dict(model=shape, bits=bits, batch=batch, cap=cap, seed=seed, keep_logits=True,
+                               scale_dtype=sdt), keep_packs=True)
+
+
+SMALL = dict(NAME="small", D_MODEL=256, LAYERS=2, HEADS=4, KV_HEADS=2, HEAD_DIM=64, FFN=512, VOCAB=1024,
+             ROPE_THETA=1e6, EPS=1e-6)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_small_model_forced_decode(torch, bits):
+    m = _build(dict(SMALL), bits=bits)
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, 1024, 20).tolist()
+    seqs, lg, toks = MC.run_forced(m, [prompt], 8, seed=2)
+    rep = MC.compare(m, seqs, lg, 8)
+    assert rep[0]["argmax_agree"] >= 7
+
+
+def test_small_model_state_and_cache(torch):
+    m = _build(dict(SMALL, QKV_BIAS=True), bits=4)
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, 1024, 12).tolist()
+    seqs, lg, toks = MC.run_forced(m, [prompt], 4, seed=4)
+    q0, log = m.state(0)
+    T = len(seqs[0])
+    assert q0 == T - 1
+    assert list(log[:T]) == seqs[0]
+    assert np.all(log[T:] == 0xFFFFFFFF)
+    # the KV cache rows the device appended equal the half-transport oracle's rotated k and v (fp16), within 1 ulp
+    om = MC.oracle_model(m)
+    _, kept = om.forward(seqs[0][:T - 1], "half", keep=True)
+    for l in range(m.shape.LAYERS):
+        k, v = m.read_kv(l, 0, T - 1)
+        kr, vr = kept[l]
+        kr = kr.transpose(1, 0, 2)
+        vr = vr.transpose(1, 0, 2)
+        ulp_k = np.spacing(np.abs(kr).astype(np.float16)).astype(np.float64)
+        ulp_v = np.spacing(np.abs(vr).astype(np.float16)).astype(np.float64)
+        # later layers see inputs that already differ by rounding: allow a few ulps plus a relative slack
+        assert np.all(np.abs(k.astype(np.float64) - kr) <= 8 * ulp_k + 1e-2 * np.abs(kr).max())
+        assert np.all(np.abs(v.astype(np.float64) - vr) <= 8 * ulp_v + 1e-2 * np.abs(vr).max())
+
+
+def test_free_generation_argmax_is_device_argmax(torch):
+    """Free generation (no forcing): every token the device chose is the first argmax of the logits it produced
+    (bit-exact: the same fp32 values), and the log records it."""
+    m = _build(dict(SMALL), bits=4)
+    m.start(0, [5, 17, 33])
+    m.decode(2, want_tokens=False)
+    toks, lg, _ = m.decode(6, want_tokens=True, want_logits=True)
+    for i in range(6):
+        assert int(toks[i, 0]) == int(np.argmax(lg[i, 0]))
+    q0, log = m.state(0)
+    assert q0 == 8
+    assert list(log[3:9]) == [int(t) for t in toks[:, 0]]
+
+
+def test_batched_sequences_independent(torch):
+    m = _build(dict(SMALL), bits=4, batch=3)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 1024, n).tolist() for n in (7, 15, 11)]
+    seqs, lg, toks = MC.run_forced(m, prompts, 5, seed=6)
+    rep = MC.compare(m, seqs, lg, 5)
+    assert all(r["argmax_agree"] >= 4 for r in rep)
+
+
+def test_qwen25_shape_two_layers(torch):
+    from agxforge_b200.inference import models
+    shape = models.QWEN25_05B.replace(LAYERS=2)
+    m = _build(shape, bits=4, cap=256, seed=0)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, shape.VOCAB, 40).tolist()
+    seqs, lg, toks = MC.run_forced(m, [prompt], 4, seed=1)
+    MC.compare(m, seqs, lg, 4)
+
+
+def test_internlm_shape_two_layers_long_context(torch):
+    from agxforge_b200.inference import models
+    shape = models.INTERNLM25_18B.replace(LAYERS=2)
+    m = _build(shape, bits=4, cap=2048, seed=2)
+    rng = np.random.default_rng(2)
+    prompt = rng.integers(0, shape.VOCAB, 300).tolist()
+    seqs, lg, toks = MC.run_forced(m, [prompt], 3, seed=3)
+    MC.compare(m, seqs, lg, 3)
+
+
+def test_internlm_q8_two_layers(torch):
+    from agxforge_b200.inference import models
+    shape = models.INTERNLM25_18B.replace(LAYERS=2)
+    m = _build(shape, bits=8, cap=512, seed=3)
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, shape.VOCAB, 64).tolist()
+    seqs, lg, toks = MC.run_forced(m, [prompt], 3, seed=5)
+    MC.compare(m, seqs, lg, 3)
+
+
+def test_execute_report_keys(torch):
+    from agxforge_b200.inference import execute
+    m = _build(dict(SMALL), bits=4)
+    m.start(0, [1, 2, 3])
+    rep = execute.decode(m, 5)
+    for key in ("out_ids", "tokens_per_s", "per_token_ms", "gpu_ms_per_token", "host_ms_per_token",
+                "dispatches_per_token", "batch"):
+        assert key in rep
+    assert len(rep["out_ids"]) == 5
+    assert rep["dispatches_per_token"] == 5 * 2 + 1
