@@ -1,12 +1,13 @@
 // attention.cu — split-KV decode attention with a log-sum-exp merge (agxforge/kernels/attention.py: the split
 // 86-165 and merge 1326-1371, attn_reference 1458-1580), and the standalone RMSNorm (norm.py:42-155).
 //
-// One CTA per (sequence, KV head, key chunk): the chunk boundaries follow the live length q0 + 1 read on the device,
-// so a captured graph serves every position. The CTA's 4 warps stream the chunk's K and V rows (each lane 4 or 2 of
-// the head dims, 8-byte loads), score every query head of the GQA group against each key (the group shares the
-// K/V stream), and keep an online base-2 softmax per head (q is pre-scaled by log2(e)/sqrt(hd)). Partials
-// (m, l, o[hd]) go to scratch; the last CTA of the (sequence, KV head) merges the chunks in order:
-// M = max m_s, w_s = 2^(m_s - M), L = sum l_s w_s, O = sum o_s w_s, out = fp16(O / L).
+// One CTA per (key chunk, KV head, sequence): the chunk boundaries follow the live length q0 + 1 read on the device,
+// so a captured graph serves every position. The chunk's K and V rows move into shared memory by bulk TMA copies
+// (sub-chunks of 64 keys, two stages; the history rows are requested before the upstream kernel finishes, the new row
+// q0 after). 8 warps take blocks of 4 keys (each lane 4 or 2 of the head dims), score every query head of the GQA
+// group against each key (the group shares the K/V stream) and keep an online base-2 softmax per head (q is
+// pre-scaled by log2(e)/sqrt(hd)). Partials (m, l, o[hd]) go to scratch; the last CTA of the (sequence, KV head)
+// merges the chunks: M = max m_s, w_s = 2^(m_s - M), L = sum l_s w_s, O = sum o_s w_s, out = fp16(O / L).
 #include <algorithm>
 
 #include "common.cuh"
@@ -16,9 +17,11 @@ namespace agxc {
 
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = 8;
 constexpr int kKeyBlock = 4;
+constexpr int kSub = 64;        // keys per shared-memory sub-chunk (K and V rows of one KV head)
+constexpr int kMinChunk = 32;   // the fewest keys a chunk takes before more chunks are used
 
 template <int HD>
 struct Lanes;
@@ -27,8 +30,10 @@ struct Lanes<128> {
   static constexpr int D = 4;
   __device__ static void load(const __half* p, float* f) {
     const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    __half2 h0, h1;
+    memcpy(&h0, &u.x, 4);
+    memcpy(&h1, &u.y, 4);
+    const float2 a = __half22float2(h0), b = __half22float2(h1);
     f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
   }
 };
@@ -41,26 +46,60 @@ struct Lanes<64> {
   }
 };
 
+__host__ __device__ inline int attn_smem_bytes(int hd) { return 128 + 2 * 2 * kSub * hd * 2; }
+
+// One CTA per (chunk, KV head, sequence). Chunk s covers keys [s L, min(nk, (s+1) L)), L = max(32, ceil(nk / S)):
+// short contexts use fewer chunks, the rest return after reporting an empty partial.
 template <int HD, int GM>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   constexpr int D = Lanes<HD>::D;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  __half* kv = reinterpret_cast<__half*>(smem + 128);  // stage st: K rows at st*2*kSub*HD, V rows after kSub*HD
   const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = p.H / p.KVH;
   __shared__ float sm_m[kAttnWarps][GM], sm_l[kAttnWarps][GM];
   __shared__ float sm_o[kAttnWarps][GM][HD];
+  __shared__ float sw[GM][64];
+  __shared__ float sL[GM];
   __shared__ int s_last;
 
+  // the history rows (keys before q0) were written by earlier steps: they stream in before the upstream kernel
+  // (which appends row q0) has finished
+  int pos = static_cast<int>(p.q0[b]);
+  if (pos > p.cap - 1) pos = p.cap - 1;
+  const int nk = pos + 1;
+  const int L = max(kMinChunk, (nk + p.S - 1) / p.S);
+  const int j0 = s * L;
+  const int j1 = min(nk, j0 + L);
+  const int nsub = j1 > j0 ? (j1 - j0 + kSub - 1) / kSub : 0;
+  const size_t kvbase = (static_cast<size_t>(b) * p.KVH + kvh) * p.cap * HD;
+
+  auto issue = [&](int i) {  // sub-chunk i -> stage i % 2: the rows below pos (row pos comes after the wait)
+    const int a = j0 + i * kSub;
+    const int n = max(0, min(min(a + kSub, j1), pos) - a);
+    uint64_t* bar = &bars[i & 1];
+    __half* dst = kv + (i & 1) * 2 * kSub * HD;
+    mbar_arrive_expect_tx(bar, static_cast<unsigned>(2 * n * HD * 2));
+    if (n) {
+      bulk_g2s(dst, p.kc + kvbase + static_cast<size_t>(a) * HD, n * HD * 2, bar);
+      bulk_g2s(dst + kSub * HD, p.vc + kvbase + static_cast<size_t>(a) * HD, n * HD * 2, bar);
+    }
+  };
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int i = 0; i < 2 && i < nsub; ++i) issue(i);
+  }
   if (p.pdl) {
     pdl_wait();
     pdl_launch_dependents();
   }
-  int pos = static_cast<int>(p.q0[b]);
-  if (pos > p.cap - 1) pos = p.cap - 1;
-  const int nk = pos + 1;
-  const int L = (nk + p.S - 1) / p.S;
-  const int j0 = s * L;
-  const int j1 = min(nk, j0 + L);
 
   float q[GM][D], o[GM][D], m[GM], l[GM];
 #pragma unroll
@@ -71,68 +110,86 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     for (int d = 0; d < D; ++d) { o[g][d] = 0.f; q[g][d] = 0.f; }
     if (g < G) Lanes<HD>::load(p.q16 + (static_cast<size_t>(b) * p.H + kvh * G + g) * HD + lane * D, q[g]);
   }
-  const size_t kvbase = (static_cast<size_t>(b) * p.KVH + kvh) * p.cap * HD;
-  const __half* kc = p.kc + kvbase + lane * D;
-  const __half* vc = p.vc + kvbase + lane * D;
 
-  // warp w takes key blocks j0 + 4 (w + 4 t) ... ; keys past j1 are skipped, never read
-  for (int jb = j0 + warp * kKeyBlock; jb < j1; jb += kAttnWarps * kKeyBlock) {
-    float kf[kKeyBlock][D], vf[kKeyBlock][D];
-#pragma unroll
-    for (int t = 0; t < kKeyBlock; ++t) {
-      const int j = jb + t;
-      if (j < j1) {
-        Lanes<HD>::load(kc + static_cast<size_t>(j) * HD, kf[t]);
-        Lanes<HD>::load(vc + static_cast<size_t>(j) * HD, vf[t]);
-      } else {
-#pragma unroll
-        for (int d = 0; d < D; ++d) { kf[t][d] = 0.f; vf[t][d] = 0.f; }
+  bool ok = true;
+  for (int i = 0; i < nsub; ++i) {
+    const int a = j0 + i * kSub;
+    const int n = min(kSub, j1 - a);
+    __half* st = kv + (i & 1) * 2 * kSub * HD;
+    if (!mbar_wait_bounded(&bars[i & 1], (i >> 1) & 1, p.err)) ok = false;
+    if (pos >= a && pos < a + n) {  // the new row, appended by the upstream kernel
+      for (int t = tid; t < HD / 8; t += kAttnThreads) {
+        reinterpret_cast<uint4*>(st + (pos - a) * HD)[t] =
+            reinterpret_cast<const uint4*>(p.kc + kvbase + static_cast<size_t>(pos) * HD)[t];
+        reinterpret_cast<uint4*>(st + kSub * HD + (pos - a) * HD)[t] =
+            reinterpret_cast<const uint4*>(p.vc + kvbase + static_cast<size_t>(pos) * HD)[t];
       }
     }
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g >= G) break;
-      float sc[kKeyBlock];
-#pragma unroll
-      for (int t = 0; t < kKeyBlock; ++t) {
-        float part = 0.f;
-#pragma unroll
-        for (int d = 0; d < D; ++d) part = fmaf(q[g][d], kf[t][d], part);
-        sc[t] = warp_sum(part);
-      }
-      float mn = m[g];
-#pragma unroll
-      for (int t = 0; t < kKeyBlock; ++t)
-        if (jb + t < j1) mn = fmaxf(mn, sc[t]);
-      const float a = exp2f(m[g] - mn);
-      float lsum = l[g] * a;
-#pragma unroll
-      for (int d = 0; d < D; ++d) o[g][d] *= a;
+    __syncthreads();
+    for (int kb = warp * kKeyBlock; kb < n; kb += kAttnWarps * kKeyBlock) {
+      float kf[kKeyBlock][D], vf[kKeyBlock][D];
 #pragma unroll
       for (int t = 0; t < kKeyBlock; ++t) {
-        const float pr = jb + t < j1 ? exp2f(sc[t] - mn) : 0.f;
-        lsum += pr;
-#pragma unroll
-        for (int d = 0; d < D; ++d) o[g][d] = fmaf(pr, vf[t][d], o[g][d]);
+        const int j = min(kb + t, n - 1);
+        Lanes<HD>::load(st + j * HD + lane * D, kf[t]);
+        Lanes<HD>::load(st + kSub * HD + j * HD + lane * D, vf[t]);
       }
-      l[g] = lsum;
-      m[g] = mn;
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g < G) {
+          float sc[kKeyBlock];
+#pragma unroll
+          for (int t = 0; t < kKeyBlock; ++t) {
+            float part = 0.f;
+#pragma unroll
+            for (int d = 0; d < D; ++d) part = fmaf(q[g][d], kf[t][d], part);
+            sc[t] = warp_sum(part);
+          }
+          float mn = m[g];
+#pragma unroll
+          for (int t = 0; t < kKeyBlock; ++t)
+            if (kb + t < n) mn = fmaxf(mn, sc[t]);
+          const float al = exp2f(m[g] - mn);
+          float lsum = l[g] * al;
+#pragma unroll
+          for (int d = 0; d < D; ++d) o[g][d] *= al;
+#pragma unroll
+          for (int t = 0; t < kKeyBlock; ++t) {
+            const float pr = kb + t < n ? exp2f(sc[t] - mn) : 0.f;
+            lsum += pr;
+#pragma unroll
+            for (int d = 0; d < D; ++d) o[g][d] = fmaf(pr, vf[t][d], o[g][d]);
+          }
+          l[g] = lsum;
+          m[g] = mn;
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with this stage
+    if (tid == 0 && i + 2 < nsub) {
+      fence_proxy_async();  // the stage's generic writes (row q0) before the next bulk copy into it
+      issue(i + 2);
     }
   }
 
-  // combine the 4 warps
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+  // combine the warps
 #pragma unroll
-    for (int d = 0; d < D; ++d) sm_o[warp][g][lane * D + d] = o[g][d];
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+      if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+#pragma unroll
+      for (int d = 0; d < D; ++d) sm_o[warp][g][lane * D + d] = o[g][d];
+    }
   }
   __syncthreads();
   const int PW = HD + 2;
   for (int t = tid; t < G * HD; t += kAttnThreads) {
     const int g = t / HD, d = t % HD;
     float M = -INFINITY;
+#pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][g]);
     float Ls = 0.f, Os = 0.f;
+#pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) {
       const float f = sm_m[w][g] == -INFINITY ? 0.f : exp2f(sm_m[w][g] - M);
       Ls = fmaf(sm_l[w][g], f, Ls);
@@ -143,7 +200,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     dst[2 + d] = Os;
   }
   __threadfence();
-  __syncthreads();
+  if (__syncthreads_or(!ok)) return;  // a chunk never landed: the error word is set
   if (tid == 0) {
     unsigned* c = p.counters + static_cast<size_t>(b) * p.KVH + kvh;
     const unsigned prev = atomicAdd(c, 1u);
@@ -153,19 +210,33 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // the merge of the S chunk partials: per head, lanes take chunks (M, weights, L by warp reductions), then every
+  // (head, dim) sums its chunks' o with the weights (chunk loads independent, so they overlap)
+  for (int g = warp; g < G; g += kAttnWarps) {
+    const float* src = p.part + ((static_cast<size_t>(b) * p.H + kvh * G + g) * p.S) * PW;
+    const float m0 = lane < p.S ? ld_cg(src + lane * PW) : -INFINITY;
+    const float m1 = lane + 32 < p.S ? ld_cg(src + (lane + 32) * PW) : -INFINITY;
+    const float M = warp_max(fmaxf(m0, m1));
+    const float w0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M);
+    const float w1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M);
+    const float l0 = w0 != 0.f ? ld_cg(src + lane * PW + 1) : 0.f;
+    const float l1 = w1 != 0.f ? ld_cg(src + (lane + 32) * PW + 1) : 0.f;
+    const float Ls = warp_sum(l0 * w0 + l1 * w1);
+    sw[g][lane] = w0;
+    sw[g][lane + 32] = w1;
+    if (lane == 0) sL[g] = Ls;
+  }
+  __syncthreads();
   for (int t = tid; t < G * HD; t += kAttnThreads) {
     const int g = t / HD, d = t % HD;
-    const float* src = p.part + ((static_cast<size_t>(b) * p.H + kvh * G + g) * p.S) * PW;
-    float M = -INFINITY;
-    for (int c = 0; c < p.S; ++c) M = fmaxf(M, ld_cg(src + c * PW));
-    float Ls = 0.f, Os = 0.f;
+    const float* src = p.part + ((static_cast<size_t>(b) * p.H + kvh * G + g) * p.S) * PW + 2 + d;
+    float Os = 0.f;
+#pragma unroll 8
     for (int c = 0; c < p.S; ++c) {
-      const float mc = ld_cg(src + c * PW);
-      const float w = mc == -INFINITY ? 0.f : exp2f(mc - M);
-      Ls = fmaf(ld_cg(src + c * PW + 1), w, Ls);
-      Os = fmaf(ld_cg(src + c * PW + 2 + d), w, Os);
+      const float w = sw[g][c];
+      if (w != 0.f) Os = fmaf(ld_cg(src + c * PW), w, Os);
     }
-    p.out[(static_cast<size_t>(b) * p.H + kvh * G + g) * HD + d] = __float2half_rn(Os / Ls);
+    p.out[(static_cast<size_t>(b) * p.H + kvh * G + g) * HD + d] = __float2half_rn(Os / sL[g]);
   }
 }
 
@@ -174,7 +245,7 @@ int launch_attn_t(const AttnParams& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.S, p.KVH, p.nb);
   cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = attn_smem_bytes(HD);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   int na = 0;
@@ -186,6 +257,15 @@ int launch_attn_t(const AttnParams& p, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = na;
   AGXC_CUDA(cudaLaunchKernelEx(&cfg, attn_kernel<HD, GM>, p));
+  return 0;
+}
+
+template <typename K>
+int attn_allow(K kern, int optin) {
+  cudaFuncAttributes fa;
+  AGXC_CUDA(cudaFuncGetAttributes(&fa, kern));
+  AGXC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 optin - static_cast<int>(fa.sharedSizeBytes)));
   return 0;
 }
 
@@ -220,8 +300,19 @@ __global__ void rmsnorm_kernel(const void* x, int x_f32, int d, const __half* g,
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap) {
   const int sms = ctx ? ctx->num_sms : kNumSMs;
   int S = std::max(1, 2 * sms / std::max(1, nb * KVH));
-  S = std::min(S, std::max(1, cap / 16));
+  S = std::min(S, std::max(1, (cap + kMinChunk - 1) / kMinChunk));
   return std::min(S, 64);
+}
+
+int attn_configure(const agxc_ctx* ctx) {
+  const int o = ctx->max_smem_optin;
+  int rc;
+  if ((rc = attn_allow(attn_kernel<128, 1>, o)) || (rc = attn_allow(attn_kernel<128, 2>, o)) ||
+      (rc = attn_allow(attn_kernel<128, 4>, o)) || (rc = attn_allow(attn_kernel<128, 8>, o)) ||
+      (rc = attn_allow(attn_kernel<64, 1>, o)) || (rc = attn_allow(attn_kernel<64, 2>, o)) ||
+      (rc = attn_allow(attn_kernel<64, 4>, o)) || (rc = attn_allow(attn_kernel<64, 8>, o)))
+    return rc;
+  return 0;
 }
 
 size_t attn_part_floats(int nb, int H, int S, int hd) { return static_cast<size_t>(nb) * H * S * (hd + 2); }
@@ -231,12 +322,14 @@ int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s) {
   const int G = p.H / p.KVH;
   if (p.hd != 64 && p.hd != 128) return fail(AGXC_EINVAL, "attention: head_dim 64 or 128");
   if (G > 8) return fail(AGXC_EINVAL, "attention: at most 8 query heads per KV head");
-  if (p.S < 1 || p.nb < 1) return fail(AGXC_EINVAL, "attention: splits and batch must be positive");
+  if (p.S < 1 || p.S > 64 || p.nb < 1) return fail(AGXC_EINVAL, "attention: 1..64 splits and a positive batch");
   if (p.hd == 128) {
+    if (G == 1) return launch_attn_t<128, 1>(p, s);
     if (G <= 2) return launch_attn_t<128, 2>(p, s);
     if (G <= 4) return launch_attn_t<128, 4>(p, s);
     return launch_attn_t<128, 8>(p, s);
   }
+  if (G == 1) return launch_attn_t<64, 1>(p, s);
   if (G <= 2) return launch_attn_t<64, 2>(p, s);
   if (G <= 4) return launch_attn_t<64, 4>(p, s);
   return launch_attn_t<64, 8>(p, s);

@@ -4,18 +4,31 @@
 // y[b][n] = sum_g ( s[n,g] * sum_{k in g} q[n,k] x[b][k]  +  b[n,g] * sum_{k in g} x[b][k] )
 //
 // The reference factorises each trip the same way (qmv.py:1577-1649: t = sum q x, acc += s t + b sx). Here:
-//   * the weight stream moves by bulk TMA copies (cp.async.bulk + mbarrier) of whole work units — RW row tiles x GC
-//     groups, contiguous in the tile layout — into a ring of shared-memory stages, issued ahead by one thread;
-//   * each warp dequantises its lane's fields with one AND (4-bit; one PRMT for 8-bit) per two weights into fp16
-//     SUBNORMALS q * 2^-24 (exact), so no subtract or convert is needed, and forms sum q x on the tensor cores with
-//     mma.sync m16n8k16 (weight rows = M, activation rows = N <= 8, fp32 accumulate); the 2^24 (2^20 for the
-//     upper nibble pair) is folded into the scale on the CUDA cores;
-//   * the activation rows are staged in shared memory (fp16 values: every GEMV input of the decode graph is an fp16
-//     tensor — the normed rows, the attention output, the SwiGLU product), with their per-group sums;
-//   * the RMSNorm of the input is fused in front (with_norm, qmv.py:176-183), recomputed per CTA from the row;
-//   * split-K partials (and epilogue blocks wider than a unit: a RoPE head) meet through a scratch buffer and a
-//     last-arriver counter (no spin-waits).
+//   * WORK: a unit is RW (1, 2 or 4) row tiles of 16 rows over the CTA's K range (all of K unless split, SC > 1). A
+//     CTA runs its units in order; a unit streams through shared memory in chunks of CG groups: one 3-D TMA box
+//     (RW row tiles x CG tiles x tile bytes) of the tile array [row tile][group][tile], and one of its scale/bias.
+//   * PRODUCER: one warp issues the TMA copies (cp.async.bulk.tensor.3d, completing on a "full" mbarrier) of the
+//     chunks into a ring of stages, as far ahead as free stages allow — across unit boundaries, and (with
+//     programmatic dependent launch) before the upstream kernel has finished, since weights do not depend on it. A
+//     stage is refilled when all consumer warps have released it ("empty" mbarrier).
+//   * CONSUMERS: 16 warps, RW row tiles x (16 / RW) K lanes. Each dequantises its lane's fields with one AND (4-bit; one PRMT for 8-bit) per two weights
+//     into fp16 SUBNORMALS q * 2^-24 (exact), and forms sum q x on the tensor cores with mma.sync m16n8k16 (weight
+//     rows = M, activation rows = N <= 8, fp32 accumulate); scale and bias are applied per group on the CUDA cores
+//     and the 2^24 once per row at the end. Warps accumulate over their groups across
+//     all chunks of a unit and meet once per unit in shared memory.
+//   * the activation rows of the CTA's K range are staged once in shared memory as fp16 (every GEMV input of the
+//     decode graph holds fp16 values), with their per-group sums; the RMSNorm of the input is fused in front
+//     (with_norm, qmv.py:176-183), recomputed per CTA from the row.
+//   * EPILOGUES on the unit's rows: fp32 out; + fp16 residual -> fp32 (add16); + fp32 residual -> fp16 (add32_to16);
+//     SiLU(gate) * up -> fp16 (gate and up row tiles interleaved, RW = 2); bias + RoPE + q scale + KV append (the qkv
+//     pack's rows are placed so tile rows r and r + 8 are a RoPE pair i, i + hd/2); per-CTA first maximum + the
+//     generation step (head). When K is split (SC > 1) partial rows meet through scratch and a last-arriver counter.
+//   Every wait is bounded; no thread spins on another CTA.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "internal.h"
@@ -24,114 +37,210 @@ namespace agxc {
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = 8;
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + the producer warp
+constexpr int kMaxStages = 8;
 constexpr float k2p24 = 16777216.0f;
 constexpr float k2p20 = 1048576.0f;
 
 struct Smem {
-  // offsets in bytes from the dynamic shared memory base
-  int bars, ring, stage_bytes, wbytes, xs, xstride, xsum, red, uv, ev, misc;
+  int full, empty, dead, ring, stage_bytes, wbytes, xs, xstride, xsum, red, uv, ev, misc, total;
 };
 
-__host__ __device__ inline Smem smem_layout(int bits, int nbt, int RW, int GC, int stages, int EB) {
+__host__ __device__ inline Smem smem_layout(int bits, int nbt, int RW, int CG, int GC, int stages) {
   Smem L;
   const int TB = bits == 4 ? 512 : 1024;
-  L.bars = 0;
-  L.ring = 128;
-  L.wbytes = RW * GC * TB;
-  L.stage_bytes = (L.wbytes + RW * GC * 64 + 127) / 128 * 128;
+  L.full = 0;
+  L.empty = 8 * kMaxStages;
+  L.dead = 16 * kMaxStages;
+  L.ring = 256;
+  L.wbytes = RW * CG * TB;
+  L.stage_bytes = (L.wbytes + RW * CG * 64 + 127) / 128 * 128;
   L.xs = L.ring + stages * L.stage_bytes;
   L.xstride = GC * 64 + 8;  // halves; the 16-byte pad keeps 8 rows' fragment loads bank-conflict free
   L.xsum = L.xs + ((nbt * L.xstride * 2 + 127) / 128) * 128;
   L.red = L.xsum + GC * 8 * 4;
-  L.uv = L.red + kWarps * 16 * 8 * 4;
+  L.uv = L.red + kConsumerWarps * 16 * 8 * 4;
   L.ev = L.uv + RW * 16 * 8 * 4;
-  L.misc = L.ev + EB * 16 * 8 * 4;
+  L.misc = L.ev + RW * 16 * 8 * 4;
+  L.total = L.misc + 1024;
   return L;
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+
+__device__ __forceinline__ bool consumer_sync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(kConsumers)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
+// One group (16 rows x 64 k, one tile) of one warp: dequant + 4 MMAs. Accumulates per C element
+//   ys += s * T  (T = the group's sum q x scaled by 2^-24)   and   yb += b * sum x,
+// so the row's value is ys * 2^24 + yb (applied once, after the last group).
+template <int BITS, int NBT>
+__device__ __forceinline__ void group_step(const uint8_t* tile, const uint8_t* sbt, const __half* xg, const float* xs,
+                                          int lane, int sdt, float* ys, float* yb) {
+  const int r8 = lane >> 2, c4 = lane & 3;
+  const uint2 sv = *reinterpret_cast<const uint2*>(sbt + r8 * 8);
+  const uint4 xa = *reinterpret_cast<const uint4*>(xg + c4 * 16);
+  const uint4 xb = *reinterpret_cast<const uint4*>(xg + c4 * 16 + 8);
+  float2 xsv;
+  if (NBT > 1) xsv = *reinterpret_cast<const float2*>(xs + 2 * c4);
+  else xsv.x = xsv.y = xs[2 * c4];
+  float2 s2, b2;  // (row r8, row r8 + 8)
+  if (sdt) {
+    s2 = make_float2(__uint_as_float(sv.x << 16), __uint_as_float(sv.x & 0xffff0000u));
+    b2 = make_float2(__uint_as_float(sv.y << 16), __uint_as_float(sv.y & 0xffff0000u));
+  } else {
+    __half2 hs, hb;
+    memcpy(&hs, &sv.x, 4);
+    memcpy(&hb, &sv.y, 4);
+    s2 = __half22float2(hs);
+    b2 = __half22float2(hb);
+  }
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2c = 0.f, b3 = 0.f;
+  float T0, T1, T2, T3;
+  if (BITS == 4) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(tile + lane * 16);
+    constexpr uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u;
+    mma_16816(a0, a1, a2, a3, wv.x & M0, wv.y & M0, wv.z & M0, wv.w & M0, xa.x, xa.y);
+    mma_16816(b0, b1, b2c, b3, wv.x & M1, wv.y & M1, wv.z & M1, wv.w & M1, xa.z, xa.w);
+    const uint32_t sx = wv.x >> 8, sy = wv.y >> 8, sz = wv.z >> 8, sw = wv.w >> 8;
+    mma_16816(a0, a1, a2, a3, sx & M0, sy & M0, sz & M0, sw & M0, xb.x, xb.y);
+    mma_16816(b0, b1, b2c, b3, sx & M1, sy & M1, sz & M1, sw & M1, xb.z, xb.w);
+    // the upper nibble of each byte carried 2^4: its chain is 16x the lower one's scale
+    T0 = fmaf(b0, 0.0625f, a0); T2 = fmaf(b2c, 0.0625f, a2);
+    T1 = fmaf(b1, 0.0625f, a1); T3 = fmaf(b3, 0.0625f, a3);
+  } else {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(tile + lane * 16);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(tile + 512 + lane * 16);
+    constexpr uint32_t PL = 0x4140u, PH = 0x4342u;
+    mma_16816(a0, a1, a2, a3, prmt(w0.x, 0, PL), prmt(w0.x, 0, PH), prmt(w0.y, 0, PL), prmt(w0.y, 0, PH), xa.x, xa.y);
+    mma_16816(b0, b1, b2c, b3, prmt(w0.z, 0, PL), prmt(w0.z, 0, PH), prmt(w0.w, 0, PL), prmt(w0.w, 0, PH), xa.z, xa.w);
+    mma_16816(a0, a1, a2, a3, prmt(w1.x, 0, PL), prmt(w1.x, 0, PH), prmt(w1.y, 0, PL), prmt(w1.y, 0, PH), xb.x, xb.y);
+    mma_16816(b0, b1, b2c, b3, prmt(w1.z, 0, PL), prmt(w1.z, 0, PH), prmt(w1.w, 0, PL), prmt(w1.w, 0, PH), xb.z, xb.w);
+    T0 = a0 + b0; T2 = a2 + b2c; T1 = a1 + b1; T3 = a3 + b3;
+  }
+  ys[0] = fmaf(s2.x, T0, ys[0]);
+  ys[2] = fmaf(s2.y, T2, ys[2]);
+  yb[0] = fmaf(b2.x, xsv.x, yb[0]);
+  yb[2] = fmaf(b2.y, xsv.x, yb[2]);
+  if (NBT > 1) {
+    ys[1] = fmaf(s2.x, T1, ys[1]);
+    ys[3] = fmaf(s2.y, T3, ys[3]);
+    yb[1] = fmaf(b2.x, xsv.y, yb[1]);
+    yb[3] = fmaf(b2.y, xsv.y, yb[3]);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ epilogues
-// vals: [rows][8] fp32 (row-major, column = activation row b) for the block starting at physical row `row0`.
+// vals: [rows][8] fp32 (column = activation row b) for the block of `rows` physical rows starting at `row0`.
 template <int EPI>
 __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc) {
   const int tid = threadIdx.x;
   const int nb = p.nb;
   if (EPI == EPI_F32) {
-    for (int t = tid; t < rows * nb; t += kThreads) {
+    for (int t = tid; t < rows * nb; t += kConsumers) {
       const int r = t / nb, b = t % nb;
       p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * 8 + b];
     }
   } else if (EPI == EPI_RES1) {
-    for (int t = tid; t < rows * nb; t += kThreads) {
+    for (int t = tid; t < rows * nb; t += kConsumers) {
       const int r = t / nb, b = t % nb;
       const float x = __half2float(p.res16[static_cast<size_t>(b) * p.res_ld + row0 + r]);
       p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * 8 + b] + x;
     }
   } else if (EPI == EPI_RES2) {
-    for (int t = tid; t < rows * nb; t += kThreads) {
+    for (int t = tid; t < rows * nb; t += kConsumers) {
       const int r = t / nb, b = t % nb;
       const float h = p.res32[static_cast<size_t>(b) * p.res_ld + row0 + r];
       p.out_f16[static_cast<size_t>(b) * p.out_ld + row0 + r] = __float2half_rn(vals[r * 8 + b] + h);
     }
   } else if (EPI == EPI_SWIGLU) {
-    // the block is a gate tile (rows 0..15) and its up tile (rows 16..31); output index (row0 / 32) * 16 + r
-    const int o0 = row0 / 32 * 16;
-    for (int t = tid; t < 16 * nb; t += kThreads) {
+    // pairs of row tiles: a gate tile (rows 0..15 of the pair) and its up tile (rows 16..31); output (row0/32)*16 + r
+    for (int t = tid; t < rows / 2 * nb; t += kConsumers) {
       const int r = t / nb, b = t % nb;
-      const float g = vals[r * 8 + b], u = vals[(16 + r) * 8 + b];
-      p.out_f16[static_cast<size_t>(b) * p.out_ld + o0 + r] = __float2half_rn(silu_f(g) * u);
+      const int pr = r / 16, rr = r % 16;
+      const float g = vals[(pr * 32 + rr) * 8 + b], u = vals[(pr * 32 + 16 + rr) * 8 + b];
+      p.out_f16[static_cast<size_t>(b) * p.out_ld + (row0 / 32 + pr) * 16 + rr] = __float2half_rn(silu_f(g) * u);
     }
   } else if (EPI == EPI_QKV) {
-    // one head: bias, rotate-half RoPE at the sequence's position (q and k), q scaled for the base-2 softmax,
-    // fp16 q to the attention's input; fp16 k and v appended to the cache at the position.
+    // each 16-row tile of a head holds logical rows (8t + r, hd/2 + 8t + r) at tile rows (r, r + 8): a RoPE pair.
+    // bias, rotate-half RoPE at the sequence's position (q and k heads), q scaled for the base-2 softmax and stored
+    // fp16; k and v stored fp16 into the cache row at the position.
     const int hd = p.hd, half = hd / 2;
-    const int head = row0 / hd;
-    for (int t = tid; t < hd * nb; t += kThreads) {
-      const int i = t / nb, b = t % nb;
-      float y = vals[i * 8 + b];
-      if (p.bias) y += __half2float(p.bias[row0 + i]);
+    for (int t = tid; t < rows / 2 * nb; t += kConsumers) {
+      const int pr = t / nb, b = t % nb;
+      const int tile = pr / 8, r = pr % 8;
+      const int prow0 = row0 + tile * 16;          // physical row of the tile's first row
+      const int head = prow0 / hd;
+      const int tt = (prow0 % hd) / 16;            // tile index within the head
+      const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
+      float y1 = vals[(tile * 16 + r) * 8 + b], y2 = vals[(tile * 16 + r + 8) * 8 + b];
+      if (p.bias) {
+        y1 += __half2float(p.bias[head * hd + i1]);
+        y2 += __half2float(p.bias[head * hd + i2]);
+      }
       int pos = static_cast<int>(p.q0[b]);
       if (pos > p.cap - 1) pos = p.cap - 1;
       if (head < p.H + p.KVH) {
-        const int j = i < half ? i + half : i - half;
-        float yp = vals[j * 8 + b];
-        if (p.bias) yp += __half2float(p.bias[row0 + j]);
-        const int ci = i < half ? i : i - half;
-        const float c = p.cos_t[static_cast<size_t>(pos) * half + ci];
-        const float s = p.sin_t[static_cast<size_t>(pos) * half + ci];
-        const float o = i < half ? y * c - yp * s : y * c + yp * s;
+        const float c = p.cos_t[static_cast<size_t>(pos) * half + i1];
+        const float s = p.sin_t[static_cast<size_t>(pos) * half + i1];
+        const float o1 = y1 * c - y2 * s, o2 = y2 * c + y1 * s;
         if (head < p.H) {
-          p.q16[(static_cast<size_t>(b) * p.H + head) * hd + i] = __float2half_rn(o * p.qscale);
+          __half* q = p.q16 + (static_cast<size_t>(b) * p.H + head) * hd;
+          q[i1] = __float2half_rn(o1 * p.qscale);
+          q[i2] = __float2half_rn(o2 * p.qscale);
         } else {
-          const int kv = head - p.H;
-          p.kcache[((static_cast<size_t>(b) * p.KVH + kv) * p.cap + pos) * hd + i] = __float2half_rn(o);
+          __half* k = p.kcache + ((static_cast<size_t>(b) * p.KVH + (head - p.H)) * p.cap + pos) * hd;
+          k[i1] = __float2half_rn(o1);
+          k[i2] = __float2half_rn(o2);
         }
       } else {
-        const int kv = head - p.H - p.KVH;
-        p.vcache[((static_cast<size_t>(b) * p.KVH + kv) * p.cap + pos) * hd + i] = __float2half_rn(y);
+        __half* v = p.vcache + ((static_cast<size_t>(b) * p.KVH + (head - p.H - p.KVH)) * p.cap + pos) * hd;
+        v[i1] = __float2half_rn(y1);
+        v[i2] = __float2half_rn(y2);
       }
     }
   } else if (EPI == EPI_ARGMAX) {
     if (p.out_f32) {
-      for (int t = tid; t < rows * nb; t += kThreads) {
+      for (int t = tid; t < rows * nb; t += kConsumers) {
         const int r = t / nb, b = t % nb;
         p.out_f32[static_cast<size_t>(b) * p.V + row0 + r] = vals[r * 8 + b];
       }
     }
-    if (tid < nb) {
-      // running first-maximum of this CTA: misc[2b] value, misc[2b+1] index (as int bits)
-      float bv = misc[2 * tid];
-      int bi = __float_as_int(misc[2 * tid + 1]);
-      for (int r = 0; r < rows; ++r) {
-        const float v = vals[r * 8 + tid];
-        const int idx = row0 + r;
-        if (v > bv || (v == bv && idx < bi)) { bv = v; bi = idx; }
+    // warp b keeps the running first-maximum of column b: misc[2b] value, misc[2b+1] index (int bits)
+    const int w = tid >> 5, lane = tid & 31;
+    if (w < nb) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int r = lane; r < rows; r += 32) {
+        const float v = vals[r * 8 + w];
+        if (v > bv) { bv = v; bi = row0 + r; }  // rows ascend per lane: the first of equal values stays
       }
-      misc[2 * tid] = bv;
-      misc[2 * tid + 1] = __int_as_float(bi);
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) {
+        const float cv = misc[2 * w];
+        const int ci = __float_as_int(misc[2 * w + 1]);
+        if (bv > cv || (bv == cv && bi < ci)) { misc[2 * w] = bv; misc[2 * w + 1] = __int_as_float(bi); }
+      }
     }
   }
 }
@@ -142,11 +251,11 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
 __device__ void argmax_finish(const QmvParams& p, float* misc) {
   const int tid = threadIdx.x;
   const int nb = p.nb;
-  __shared__ int s_tok[8];
+  int* s_tok = reinterpret_cast<int*>(misc + 48);
   for (int b = 0; b < nb; ++b) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int c = tid; c < static_cast<int>(gridDim.x); c += kThreads) {
+    for (int c = tid; c < static_cast<int>(gridDim.x); c += kConsumers) {
       const float v = ld_cg(p.pairs + (static_cast<size_t>(c) * 8 + b) * 2);
       const int i = __float_as_int(ld_cg(p.pairs + (static_cast<size_t>(c) * 8 + b) * 2 + 1));
       if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
@@ -158,14 +267,14 @@ __device__ void argmax_finish(const QmvParams& p, float* misc) {
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
     if ((tid & 31) == 0) { misc[16 + 2 * (tid >> 5)] = bv; misc[17 + 2 * (tid >> 5)] = __int_as_float(bi); }
-    __syncthreads();
+    consumer_sync();
     if (tid == 0) {
-      for (int w = 1; w < kWarps; ++w) {
+      for (int w = 1; w < kConsumerWarps; ++w) {
         const float ov = misc[16 + 2 * w];
         const int oi = __float_as_int(misc[17 + 2 * w]);
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
       }
-      uint32_t pos = p.q0_rw[b];
+      const uint32_t pos = p.q0_rw[b];
       const uint32_t p1 = pos + 1;
       uint32_t f = p.force_next ? p.force_next[b] : kTokenUnset;
       if (p.force_next) p.force_next[b] = kTokenUnset;
@@ -180,243 +289,274 @@ __device__ void argmax_finish(const QmvParams& p, float* misc) {
       if (p.tok_out) p.tok_out[b] = static_cast<int32_t>(tok);
       s_tok[b] = static_cast<int>(tok);
     }
-    __syncthreads();
+    consumer_sync();
   }
   // the chosen tokens' embedding rows become the next step's x
   const int dv = p.d / 8;
-  for (int t = tid; t < nb * dv; t += kThreads) {
+  for (int t = tid; t < nb * dv; t += kConsumers) {
     const int b = t / dv, i = t % dv;
     const uint4* src = reinterpret_cast<const uint4*>(p.embed + static_cast<size_t>(s_tok[b]) * p.d);
     reinterpret_cast<uint4*>(p.x_next + static_cast<size_t>(b) * p.d)[i] = src[i];
   }
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 template <int BITS, int NBT, int RW, int EPI>
-__global__ void __launch_bounds__(kThreads) qmv_kernel(QmvParams p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    qmv_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ CUtensorMap tmw,
+               const __grid_constant__ CUtensorMap tmsb) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int TB = BITS == 4 ? 512 : 1024;
-  constexpr int EB_MAX = EPI == EPI_QKV ? 8 : (EPI == EPI_SWIGLU ? 2 : 1);
-  const int GC = p.GC, SC = p.SC, stages = p.stages;
-  const int EB = EPI == EPI_QKV ? p.hd / 16 : (EPI == EPI_SWIGLU ? 2 : 1);
-  const Smem L = smem_layout(BITS, NBT, RW, GC, stages, EB_MAX);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  const int CG = p.CG, GC = p.GC, SC = p.SC, stages = p.stages;
+  const int nchunks = GC / CG;
+  const Smem L = smem_layout(BITS, NBT, RW, CG, GC, stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.empty);
+  volatile int* dead = reinterpret_cast<volatile int*>(smem + L.dead);
   __half* xs16 = reinterpret_cast<__half*>(smem + L.xs);
   float* xsum = reinterpret_cast<float*>(smem + L.xsum);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* uv = reinterpret_cast<float*>(smem + L.uv);
   float* ev = reinterpret_cast<float*>(smem + L.ev);
   float* misc = reinterpret_cast<float*>(smem + L.misc);
-  __shared__ int s_flag;
+  volatile int* flag = reinterpret_cast<volatile int*>(misc + 60);
 
   const int rows_units = p.N / 16 / RW;
   const int units = rows_units * SC;
   const int sc = blockIdx.x % SC;         // constant per CTA: gridDim.x is a multiple of SC
   const int k0 = sc * GC * 64;
   const int my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-
-  auto issue = [&](int i) {  // unit i of this CTA into stage i % stages
-    const int u = blockIdx.x + i * gridDim.x;
-    const int rb = u / SC;
-    const int st = i % stages;
-    uint8_t* dst = smem + L.ring + st * L.stage_bytes;
-    mbar_arrive_expect_tx(&bars[st], RW * GC * (TB + 64));
-    for (int r = 0; r < RW; ++r) {
-      const size_t tile0 = static_cast<size_t>(rb * RW + r) * p.G + static_cast<size_t>(sc) * GC;
-      bulk_g2s(dst + r * GC * TB, p.w + tile0 * TB, GC * TB, &bars[st]);
-      bulk_g2s(dst + L.wbytes + r * GC * 64, p.sb + tile0 * 64, GC * 64, &bars[st]);
-    }
-  };
+  const int total_chunks = my_units * nchunks;
 
   if (tid == 0) {
-    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    *dead = 0;
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    for (int i = 0; i < stages && i < my_units; ++i) issue(i);
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer: stream every chunk of this CTA's units through the ring (weights only, so it
+    // runs ahead of the upstream kernel under programmatic dependent launch)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmw)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmsb)) : "memory");
+      for (int k = 0; k < total_chunks; ++k) {
+        const int slot = k % stages;
+        if (k >= stages && !*dead) {
+          if (!mbar_wait_bounded(&empty[slot], ((k / stages) - 1) & 1, p.err)) *dead = 1;
+        }
+        if (*dead) break;
+        const int i = k / nchunks, c = k % nchunks;
+        const int u = blockIdx.x + i * gridDim.x;
+        const int rb = u / SC;
+        uint8_t* dst = smem + L.ring + slot * L.stage_bytes;
+        mbar_arrive_expect_tx(&full[slot], RW * CG * (TB + 64));
+        tma_load_3d(dst, &tmw, 0, sc * GC + c * CG, rb * RW, &full[slot]);
+        tma_load_3d(dst + L.wbytes, &tmsb, 0, sc * GC + c * CG, rb * RW, &full[slot]);
+      }
+    }
+    return;
   }
-  // everything above reads only weights: with programmatic dependent launch it overlaps the upstream kernel
+
+  // ---------------- consumers
   if (p.pdl) {
     pdl_wait();
     pdl_launch_dependents();
   }
-
-  // ---- stage the activation rows of this CTA's K chunk (RMSNorm fused when a gain is given)
   const int nb = p.nb;
+  // stage the activation rows of this CTA's K range (RMSNorm fused when a gain is given)
   for (int b = 0; b < nb; ++b) {
     float r = 1.0f;
     if (p.norm_gain) {
       float ss = 0.f;
       if (p.x_f32) {
-        const float* xr = static_cast<const float*>(p.x) + static_cast<size_t>(b) * p.x_ld;
-        for (int k = tid; k < p.K; k += kThreads) { const float v = xr[k]; ss = fmaf(v, v, ss); }
+        const float4* xr =
+            reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + static_cast<size_t>(b) * p.x_ld);
+        for (int k = tid; k < p.K / 4; k += kConsumers) {
+          const float4 v = xr[k];
+          ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
       } else {
-        const __half* xr = static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld;
-        for (int k = tid; k < p.K; k += kThreads) { const float v = __half2float(xr[k]); ss = fmaf(v, v, ss); }
+        const uint4* xr =
+            reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld);
+        for (int k = tid; k < p.K / 8; k += kConsumers) {
+          const uint4 u = xr[k];
+          __half2 h[4];
+          memcpy(h, &u, 16);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+          }
+        }
       }
       ss = warp_sum(ss);
       if (lane == 0) red[warp] = ss;
-      __syncthreads();
+      consumer_sync();
       if (tid == 0) {
         float tot = 0.f;
-        for (int w = 0; w < kWarps; ++w) tot += red[w];
+        for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
         red[64] = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
       }
-      __syncthreads();
+      consumer_sync();
       r = red[64];
-      __syncthreads();
+      consumer_sync();
     }
     __half* dst = xs16 + b * L.xstride;
-    for (int k = tid; k < GC * 64; k += kThreads) {
-      float v;
-      if (p.x_f32) v = static_cast<const float*>(p.x)[static_cast<size_t>(b) * p.x_ld + k0 + k];
-      else v = __half2float(static_cast<const __half*>(p.x)[static_cast<size_t>(b) * p.x_ld + k0 + k]);
-      if (p.norm_gain) v = (v * r) * __half2float(p.norm_gain[k0 + k]);
-      dst[k] = __float2half_rn(v);
+    const int n8 = GC * 8;  // 8 elements per step
+    for (int k = tid; k < n8; k += kConsumers) {
+      float v[8];
+      if (p.x_f32) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                                                            static_cast<size_t>(b) * p.x_ld + k0) + 2 * k;
+        const float4 a = src[0], c = src[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+      } else {
+        const uint4 u = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) +
+                                                       static_cast<size_t>(b) * p.x_ld + k0)[k];
+        __half2 h[4];
+        memcpy(h, &u, 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h[j]);
+          v[2 * j] = f.x; v[2 * j + 1] = f.y;
+        }
+      }
+      if (p.norm_gain) {
+        const uint4 gu = reinterpret_cast<const uint4*>(p.norm_gain + k0)[k];
+        __half2 gh[4];
+        memcpy(gh, &gu, 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 g = __half22float2(gh[j]);
+          v[2 * j] = (v[2 * j] * r) * g.x;
+          v[2 * j + 1] = (v[2 * j + 1] * r) * g.y;
+        }
+      }
+      __half2 oh[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) oh[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      uint4 o;
+      memcpy(&o, oh, 16);
+      reinterpret_cast<uint4*>(dst)[k] = o;
     }
   }
-  __syncthreads();
-  for (int t = tid; t < GC * 8; t += kThreads) {
-    const int g = t / 8, b = t % 8;
+  consumer_sync();
+  // per-group sums of the staged rows: 8 threads per (group, row), 8 elements each, combined by shuffles
+  for (int t = tid; t < GC * 64; t += kConsumers) {
+    const int g = t / 64, b = (t / 8) % 8, part = t % 8;
     float s = 0.f;
     if (b < nb) {
-      const __half* src = xs16 + b * L.xstride + g * 64;
-      for (int k = 0; k < 64; ++k) s += __half2float(src[k]);
+      const uint4 u = reinterpret_cast<const uint4*>(xs16 + b * L.xstride + g * 64)[part];
+      __half2 h[4];
+      memcpy(h, &u, 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        s += f.x + f.y;
+      }
     }
-    xsum[t] = s;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    if (part == 0) xsum[g * 8 + b] = s;
   }
   if (EPI == EPI_ARGMAX && tid < 8) {
     misc[2 * tid] = -INFINITY;
     misc[2 * tid + 1] = __int_as_float(0x7fffffff);
   }
-  __syncthreads();
+  consumer_sync();
 
   const int rr = warp % RW, kw = warp / RW;
-  constexpr int KW = kWarps / RW;
+  constexpr int KW = kConsumerWarps / RW;
   const int r8 = lane >> 2, c4 = lane & 3;
   const int col = r8 < nb ? r8 : nb - 1;
   const __half* xrow = xs16 + col * L.xstride;
-  bool ok = true;
-  int fail_unit = 0;
+  bool waited_ok = true;
+  int k = 0;  // chunk counter
 
   for (int i = 0; i < my_units; ++i) {
     const int u = blockIdx.x + i * gridDim.x;
     const int rb = u / SC;
-    const int st = i % stages;
-    // every thread waits (bounded); a stage that never lands makes the whole CTA leave at the barrier below
-    const bool landed = mbar_wait_bounded(&bars[st], (i / stages) & 1, p.err);
-    const uint8_t* wst = smem + L.ring + st * L.stage_bytes + rr * GC * TB;
-    const uint8_t* sbst = smem + L.ring + st * L.stage_bytes + L.wbytes + rr * GC * 64;
-    float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
-    for (int gi = kw; gi < GC; gi += KW) {
-      const uint2 sv = *reinterpret_cast<const uint2*>(sbst + gi * 64 + r8 * 8);
-      const uint4 xa = *reinterpret_cast<const uint4*>(xrow + gi * 64 + c4 * 16);
-      const uint4 xb = *reinterpret_cast<const uint4*>(xrow + gi * 64 + c4 * 16 + 8);
-      const float2 xsv = *reinterpret_cast<const float2*>(xsum + gi * 8 + 2 * c4);
-      const float s_r = scale_to_f32(static_cast<uint16_t>(sv.x & 0xffffu), p.sdt);
-      const float s_r8 = scale_to_f32(static_cast<uint16_t>(sv.x >> 16), p.sdt);
-      const float b_r = scale_to_f32(static_cast<uint16_t>(sv.y & 0xffffu), p.sdt);
-      const float b_r8 = scale_to_f32(static_cast<uint16_t>(sv.y >> 16), p.sdt);
-      if (BITS == 4) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wst + gi * TB + lane * 16);
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-        constexpr uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u;
-        mma_16816(a0, a1, a2, a3, wv.x & M0, wv.y & M0, wv.z & M0, wv.w & M0, xa.x, xa.y);
-        mma_16816(b0, b1, b2, b3, wv.x & M1, wv.y & M1, wv.z & M1, wv.w & M1, xa.z, xa.w);
-        const uint32_t sx = wv.x >> 8, sy = wv.y >> 8, sz = wv.z >> 8, sw = wv.w >> 8;
-        mma_16816(a0, a1, a2, a3, sx & M0, sy & M0, sz & M0, sw & M0, xb.x, xb.y);
-        mma_16816(b0, b1, b2, b3, sx & M1, sy & M1, sz & M1, sw & M1, xb.z, xb.w);
-        const float sr24 = s_r * k2p24, sr20 = s_r * k2p20, s824 = s_r8 * k2p24, s820 = s_r8 * k2p20;
-        y0 = fmaf(sr24, a0, y0); y0 = fmaf(sr20, b0, y0); y0 = fmaf(b_r, xsv.x, y0);
-        y2 = fmaf(s824, a2, y2); y2 = fmaf(s820, b2, y2); y2 = fmaf(b_r8, xsv.x, y2);
-        if (NBT > 1) {
-          y1 = fmaf(sr24, a1, y1); y1 = fmaf(sr20, b1, y1); y1 = fmaf(b_r, xsv.y, y1);
-          y3 = fmaf(s824, a3, y3); y3 = fmaf(s820, b3, y3); y3 = fmaf(b_r8, xsv.y, y3);
-        }
-      } else {
-        const uint4 w0 = *reinterpret_cast<const uint4*>(wst + gi * TB + lane * 16);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(wst + gi * TB + 512 + lane * 16);
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        constexpr uint32_t PL = 0x4140u, PH = 0x4342u;
-        mma_16816(a0, a1, a2, a3, prmt(w0.x, 0, PL), prmt(w0.x, 0, PH), prmt(w0.y, 0, PL), prmt(w0.y, 0, PH), xa.x,
-                  xa.y);
-        mma_16816(a0, a1, a2, a3, prmt(w0.z, 0, PL), prmt(w0.z, 0, PH), prmt(w0.w, 0, PL), prmt(w0.w, 0, PH), xa.z,
-                  xa.w);
-        mma_16816(a0, a1, a2, a3, prmt(w1.x, 0, PL), prmt(w1.x, 0, PH), prmt(w1.y, 0, PL), prmt(w1.y, 0, PH), xb.x,
-                  xb.y);
-        mma_16816(a0, a1, a2, a3, prmt(w1.z, 0, PL), prmt(w1.z, 0, PH), prmt(w1.w, 0, PL), prmt(w1.w, 0, PH), xb.z,
-                  xb.w);
-        const float sr24 = s_r * k2p24, s824 = s_r8 * k2p24;
-        y0 = fmaf(sr24, a0, y0); y0 = fmaf(b_r, xsv.x, y0);
-        y2 = fmaf(s824, a2, y2); y2 = fmaf(b_r8, xsv.x, y2);
-        if (NBT > 1) {
-          y1 = fmaf(sr24, a1, y1); y1 = fmaf(b_r, xsv.y, y1);
-          y3 = fmaf(s824, a3, y3); y3 = fmaf(b_r8, xsv.y, y3);
-        }
+    float ys[4] = {0.f, 0.f, 0.f, 0.f}, yb[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < nchunks; ++c, ++k) {
+      const int slot = k % stages;
+      if (!*dead && !mbar_wait_bounded(&full[slot], (k / stages) & 1, p.err)) {
+        *dead = 1;
+        waited_ok = false;
       }
+      const uint8_t* st = smem + L.ring + slot * L.stage_bytes;
+      const uint8_t* wst = st + rr * CG * TB;
+      const uint8_t* sbst = st + L.wbytes + rr * CG * 64;
+#pragma unroll 4
+      for (int gi = kw; gi < CG; gi += KW) {
+        const int gg = c * CG + gi;  // group index within the CTA's K range
+        group_step<BITS, NBT>(wst + gi * TB, sbst + gi * 64, xrow + gg * 64, xsum + gg * 8, lane, p.sdt, ys, yb);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
     float* rw = red + warp * 128;
-    rw[r8 * 8 + 2 * c4] = y0;
-    rw[r8 * 8 + 2 * c4 + 1] = y1;
-    rw[(r8 + 8) * 8 + 2 * c4] = y2;
-    rw[(r8 + 8) * 8 + 2 * c4 + 1] = y3;
-    if (__syncthreads_or(!landed)) {
-      ok = false;
-      fail_unit = i;
-      break;
-    }
-    if (tid == 0 && i + stages < my_units) issue(i + stages);  // every warp is done with stage st
-    for (int t = tid; t < RW * 16 * 8; t += kThreads) {
+    rw[r8 * 8 + 2 * c4] = fmaf(ys[0], k2p24, yb[0]);
+    rw[r8 * 8 + 2 * c4 + 1] = fmaf(ys[1], k2p24, yb[1]);
+    rw[(r8 + 8) * 8 + 2 * c4] = fmaf(ys[2], k2p24, yb[2]);
+    rw[(r8 + 8) * 8 + 2 * c4 + 1] = fmaf(ys[3], k2p24, yb[3]);
+    consumer_sync();
+    for (int t = tid; t < RW * 16 * 8; t += kConsumers) {
       const int row = t / 8, b = t % 8;
       const int rt = row / 16, rw16 = row % 16;
       float s = 0.f;
-      for (int k = 0; k < KW; ++k) s += red[(rt + k * RW) * 128 + rw16 * 8 + b];
+#pragma unroll
+      for (int q = 0; q < KW; ++q) s += red[(rt + q * RW) * 128 + rw16 * 8 + b];
       uv[t] = s;
     }
-    __syncthreads();
+    consumer_sync();
     const int row0 = rb * RW * 16;
-    if (SC == 1 && EB <= RW) {
+    if (SC == 1) {
       epilogue<EPI>(p, row0, RW * 16, uv, misc);
     } else {
-      // scratch path: this unit's partial rows, then the block's last arriver sums the chunks and runs the epilogue
-      for (int t = tid; t < RW * 16 * nb; t += kThreads) {
+      // split K: this unit's partial rows to scratch; the last of the SC units of these rows sums them in order
+      for (int t = tid; t < RW * 16 * nb; t += kConsumers) {
         const int row = t / nb, b = t % nb;
         p.part[(static_cast<size_t>(sc) * p.N + row0 + row) * nb + b] = uv[row * 8 + b];
       }
       __threadfence();
-      __syncthreads();
-      const int blk = row0 / (EB * 16);
-      const unsigned expect = static_cast<unsigned>((EB / RW) * SC);
+      consumer_sync();
       if (tid == 0) {
-        const unsigned prev = atomicAdd(&p.counters[blk], 1u);
-        s_flag = prev == expect - 1;
-        if (s_flag) atomicExch(&p.counters[blk], 0u);
+        const unsigned prev = atomicAdd(&p.counters[rb], 1u);
+        *flag = prev == static_cast<unsigned>(SC) - 1;
+        if (*flag) atomicExch(&p.counters[rb], 0u);
       }
-      __syncthreads();
-      if (s_flag) {
+      consumer_sync();
+      if (*flag) {
         __threadfence();
-        const int brow0 = blk * EB * 16;
-        for (int t = tid; t < EB * 16 * 8; t += kThreads) {
+        for (int t = tid; t < RW * 16 * 8; t += kConsumers) {
           const int row = t / 8, b = t % 8;
           float s = 0.f;
           if (b < nb)
-            for (int c = 0; c < SC; ++c) s += ld_cg(p.part + (static_cast<size_t>(c) * p.N + brow0 + row) * nb + b);
+            for (int q = 0; q < SC; ++q) s += ld_cg(p.part + (static_cast<size_t>(q) * p.N + row0 + row) * nb + b);
           ev[t] = s;
         }
-        __syncthreads();
-        epilogue<EPI>(p, brow0, EB * 16, ev, misc);
+        consumer_sync();
+        epilogue<EPI>(p, row0, RW * 16, ev, misc);
       }
+      consumer_sync();
     }
-    __syncthreads();
   }
 
-  if (!ok) {
-    // a stage never arrived: drain what this CTA issued (bounded) and leave; the host reads the error word
-    for (int j = fail_unit; j < fail_unit + stages && j < my_units; ++j)
-      mbar_wait_bounded(&bars[j % stages], (j / stages) & 1, nullptr, 100000000ull);
-    return;
-  }
+  if (consumer_sync_or(!waited_ok)) return;  // a stage never landed: the error word is set; leave uniformly
 
   if (EPI == EPI_ARGMAX) {
     if (tid < 8) {
@@ -424,24 +564,54 @@ __global__ void __launch_bounds__(kThreads) qmv_kernel(QmvParams p) {
       p.pairs[(static_cast<size_t>(blockIdx.x) * 8 + tid) * 2 + 1] = misc[2 * tid + 1];
     }
     __threadfence();
-    __syncthreads();
+    consumer_sync();
     if (tid == 0) {
       const unsigned prev = atomicAdd(&p.counters[0], 1u);
-      s_flag = prev == gridDim.x - 1;
-      if (s_flag) atomicExch(&p.counters[0], 0u);
+      *flag = prev == gridDim.x - 1;
+      if (*flag) atomicExch(&p.counters[0], 0u);
     }
-    __syncthreads();
-    if (s_flag) {
+    consumer_sync();
+    if (*flag) {
       __threadfence();
       argmax_finish(p, misc);
     }
   }
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int encode_fn() {
+  if (g_encode) return 0;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  AGXC_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+  if (q != cudaDriverEntryPointSuccess || !fn) return fail(AGXC_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return 0;
+}
+
+// A 3-D map over an array [rows][groups][inner 32-bit words] with a box of (inner, CG groups, RW row tiles).
+int make_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW) {
+  if (int rc = encode_fn()) return rc;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner_words), static_cast<cuuint64_t>(G),
+                        static_cast<cuuint64_t>(RT)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner_words) * 4,
+                           static_cast<cuuint64_t>(inner_words) * 4 * G};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(inner_words), static_cast<cuuint32_t>(CG),
+                       static_cast<cuuint32_t>(RW)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AGXC_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return 0;
+}
+
 template <int BITS, int NBT, int RW, int EPI>
-int launch_one(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, cudaStream_t s) {
+int launch_one(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, const CUtensorMap& tw,
+               const CUtensorMap& ts, cudaStream_t s) {
   auto kern = qmv_kernel<BITS, NBT, RW, EPI>;
-  if (ctx && static_cast<int>(plan.smem) > ctx->max_smem_optin)
+  if (ctx && static_cast<int>(plan.smem) + 1024 > ctx->max_smem_optin)
     return fail(AGXC_EINVAL, "qmv: plan needs more shared memory than the device offers");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid);
@@ -457,41 +627,73 @@ int launch_one(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, cud
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  AGXC_CUDA(cudaLaunchKernelEx(&cfg, kern, p));
+  AGXC_CUDA(cudaLaunchKernelEx(&cfg, kern, p, tw, ts));
   return 0;
 }
 
+template <int BITS, int NBT, int EPI>
+int dispatch_rw(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, const CUtensorMap& tw,
+                const CUtensorMap& ts, cudaStream_t s) {
+  if (plan.RW == 1) return launch_one<BITS, NBT, 1, EPI>(ctx, p, plan, tw, ts, s);
+  if (plan.RW == 2) return launch_one<BITS, NBT, 2, EPI>(ctx, p, plan, tw, ts, s);
+  return launch_one<BITS, NBT, 4, EPI>(ctx, p, plan, tw, ts, s);
+}
+
 template <int BITS, int NBT>
-int dispatch_epi(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, int epi, cudaStream_t s) {
+int dispatch_epi(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, int epi, const CUtensorMap& tw,
+                 const CUtensorMap& ts, cudaStream_t s) {
   switch (epi) {
-    case EPI_F32: return launch_one<BITS, NBT, 1, EPI_F32>(ctx, p, plan, s);
-    case EPI_RES1: return launch_one<BITS, NBT, 1, EPI_RES1>(ctx, p, plan, s);
-    case EPI_RES2: return launch_one<BITS, NBT, 1, EPI_RES2>(ctx, p, plan, s);
-    case EPI_SWIGLU: return launch_one<BITS, NBT, 2, EPI_SWIGLU>(ctx, p, plan, s);
-    case EPI_QKV: return launch_one<BITS, NBT, 1, EPI_QKV>(ctx, p, plan, s);
-    case EPI_ARGMAX: return launch_one<BITS, NBT, 1, EPI_ARGMAX>(ctx, p, plan, s);
+    case EPI_F32: return dispatch_rw<BITS, NBT, EPI_F32>(ctx, p, plan, tw, ts, s);
+    case EPI_RES1: return dispatch_rw<BITS, NBT, EPI_RES1>(ctx, p, plan, tw, ts, s);
+    case EPI_RES2: return dispatch_rw<BITS, NBT, EPI_RES2>(ctx, p, plan, tw, ts, s);
+    case EPI_SWIGLU:
+      if (plan.RW == 2) return launch_one<BITS, NBT, 2, EPI_SWIGLU>(ctx, p, plan, tw, ts, s);
+      return launch_one<BITS, NBT, 4, EPI_SWIGLU>(ctx, p, plan, tw, ts, s);
+    case EPI_QKV: return dispatch_rw<BITS, NBT, EPI_QKV>(ctx, p, plan, tw, ts, s);
+    case EPI_ARGMAX: return dispatch_rw<BITS, NBT, EPI_ARGMAX>(ctx, p, plan, tw, ts, s);
   }
   return fail(AGXC_EINVAL, "qmv: unknown epilogue");
 }
 
 template <int BITS>
-int dispatch_nb(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, int epi, cudaStream_t s) {
-  if (p.nb == 1) return dispatch_epi<BITS, 1>(ctx, p, plan, epi, s);
-  if (p.nb == 2) return dispatch_epi<BITS, 2>(ctx, p, plan, epi, s);
-  if (p.nb <= 4) return dispatch_epi<BITS, 4>(ctx, p, plan, epi, s);
-  return dispatch_epi<BITS, 8>(ctx, p, plan, epi, s);
+int dispatch_nb(const agxc_ctx* ctx, const QmvParams& p, const QmvPlan& plan, int epi, const CUtensorMap& tw,
+                const CUtensorMap& ts, cudaStream_t s) {
+  if (p.nb == 1) return dispatch_epi<BITS, 1>(ctx, p, plan, epi, tw, ts, s);
+  if (p.nb == 2) return dispatch_epi<BITS, 2>(ctx, p, plan, epi, tw, ts, s);
+  if (p.nb <= 4) return dispatch_epi<BITS, 4>(ctx, p, plan, epi, tw, ts, s);
+  return dispatch_epi<BITS, 8>(ctx, p, plan, epi, tw, ts, s);
 }
 
 int nb_tmpl(int nb) { return nb == 1 ? 1 : nb == 2 ? 2 : nb <= 4 ? 4 : 8; }
 
+// The opt-in limit covers static + dynamic shared memory: each kernel may take the limit less its static part.
+template <typename K>
+int allow_smem(K kern, int optin) {
+  cudaFuncAttributes fa;
+  AGXC_CUDA(cudaFuncGetAttributes(&fa, kern));
+  AGXC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 optin - static_cast<int>(fa.sharedSizeBytes)));
+  return 0;
+}
+
+template <int BITS, int NBT, int EPI>
+int configure_rw(int smem) {
+  int rc;
+  if ((rc = allow_smem(qmv_kernel<BITS, NBT, 1, EPI>, smem)) || (rc = allow_smem(qmv_kernel<BITS, NBT, 2, EPI>, smem)) ||
+      (rc = allow_smem(qmv_kernel<BITS, NBT, 4, EPI>, smem)))
+    return rc;
+  return 0;
+}
+
 template <int BITS, int NBT>
 int configure_nb(int smem) {
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 1, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 1, EPI_RES1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 1, EPI_RES2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 2, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 1, EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  AGXC_CUDA(cudaFuncSetAttribute(qmv_kernel<BITS, NBT, 1, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int rc;
+  if ((rc = configure_rw<BITS, NBT, EPI_F32>(smem)) || (rc = configure_rw<BITS, NBT, EPI_RES1>(smem)) ||
+      (rc = configure_rw<BITS, NBT, EPI_RES2>(smem)) || (rc = configure_rw<BITS, NBT, EPI_QKV>(smem)) ||
+      (rc = configure_rw<BITS, NBT, EPI_ARGMAX>(smem)) ||
+      (rc = allow_smem(qmv_kernel<BITS, NBT, 2, EPI_SWIGLU>, smem)) ||
+      (rc = allow_smem(qmv_kernel<BITS, NBT, 4, EPI_SWIGLU>, smem)))
+    return rc;
   return 0;
 }
 
@@ -506,63 +708,86 @@ int qmv_configure(const agxc_ctx* ctx) {
       (rc = configure_nb<4, 8>(smem)) || (rc = configure_nb<8, 1>(smem)) || (rc = configure_nb<8, 2>(smem)) ||
       (rc = configure_nb<8, 4>(smem)) || (rc = configure_nb<8, 8>(smem)))
     return rc;
-  return 0;
+  return encode_fn();
 }
 
+// The launch plan. One CTA per SM, persistent over units. RW (row tiles per unit) minimises the row tiles the busiest
+// CTA carries (ties go to the larger RW: fewer per-unit reductions). K is split only when the CTA's activation rows
+// would not fit in ~40 KB (or when asked). Chunks of CG groups of at most 36 KB; as many stages as ~100 KB allows.
 QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits) {
   QmvPlan P;
-  P.RW = epi == EPI_SWIGLU ? 2 : 1;
-  P.EB = epi == EPI_QKV ? hd / 16 : (epi == EPI_SWIGLU ? 2 : 1);
   const int G = K / 64;
   const int TB = tile_bytes(bits);
-  const int rows_units = N / 16 / P.RW;
+  const int RT = N / 16;
   const int sms = ctx ? ctx->num_sms : kNumSMs;
-  const int target = 2 * sms;
-  const int max_stage = 40 * 1024;
-  int SC = 0;
+  const int nbt = nb_tmpl(nb);
+  int SC = 1;
   if (splits > 0 && G % splits == 0) {
     SC = splits;
   } else {
-    int fallback = 0;
-    for (int c = 1; c <= G; ++c) {
-      if (G % c) continue;
-      const int GC = G / c;
-      if (P.RW * GC * (TB + 64) > max_stage) continue;
-      if (!fallback) fallback = c;
-      SC = c;
-      if (rows_units * c >= target) break;
-      if (GC <= kWarps / P.RW) break;  // one group per warp: do not split further
-    }
-    if (!SC) SC = fallback ? fallback : G;
+    while (G % (SC * 2) == 0 && static_cast<long>(nbt) * (G / SC) * 64 * 2 > 40 * 1024) SC *= 2;
   }
   if (epi == EPI_ARGMAX) SC = 1;  // the argmax needs whole rows per unit
+  int best_rw = 1;
+  long best_cost = -1;
+  for (int rw : {4, 2, 1}) {
+    if (RT % rw) continue;
+    if (epi == EPI_SWIGLU && rw == 1) continue;  // a gate tile and its up tile share a unit
+    const long units = static_cast<long>(RT / rw) * SC;
+    const long cost = (units + sms - 1) / sms * rw;
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best_rw = rw; }
+  }
+  P.RW = best_rw;
+  P.EB = 1;
   P.SC = SC;
   P.GC = G / SC;
-  const int stage_bytes = (P.RW * P.GC * (TB + 64) + 127) / 128 * 128;
-  P.stages = std::max(2, std::min(4, (96 * 1024) / stage_bytes));
-  const int units = rows_units * SC;
-  int grid = std::min(units, target);
+  int CG = 1;
+  for (int c = 1; c <= P.GC; ++c)
+    if (P.GC % c == 0 && P.RW * c * (TB + 64) <= 36 * 1024 && c <= 256) CG = c;
+  P.CG = CG;
+  const int stage_bytes = (P.RW * CG * (TB + 64) + 127) / 128 * 128;
+  const int units = RT / P.RW * SC;
+  const int chunks_per_cta = (units + sms - 1) / sms * (P.GC / CG);
+  P.stages = std::max(2, std::min({kMaxStages, (100 * 1024) / stage_bytes, std::max(2, chunks_per_cta)}));
+  int grid = std::min(units, sms);
   grid = std::max(SC, grid / SC * SC);
   P.grid = grid;
-  const Smem L = smem_layout(bits, nb_tmpl(nb), P.RW, P.GC, P.stages, epi == EPI_QKV ? 8 : (epi == EPI_SWIGLU ? 2 : 1));
-  P.smem = L.misc + 256;
+  P.smem = smem_layout(bits, nbt, P.RW, CG, P.GC, P.stages).total;
   return P;
 }
 
 size_t qmv_part_floats(const QmvPlan& p, int N, int nb, int epi) {
-  if (p.SC == 1 && p.EB <= p.RW) return 0;
+  if (p.SC == 1) return 0;
   return static_cast<size_t>(p.SC) * N * nb;
 }
 
-int launch_qmv_epi(const agxc_ctx* ctx, QmvParams p, const QmvPlan& plan, int epi, cudaStream_t s) {
+int qmv_maps(const QmvPlan& plan, const uint8_t* w, const uint8_t* sb, int N, int K, int bits, CUtensorMap* tw,
+             CUtensorMap* ts) {
+  const int G = K / 64, RT = N / 16;
+  int rc = make_map(tw, w, tile_bytes(bits) / 4, G, RT, plan.CG, plan.RW);
+  if (!rc) rc = make_map(ts, sb, 16, G, RT, plan.CG, plan.RW);
+  return rc;
+}
+
+int launch_qmv_epi(const agxc_ctx* ctx, QmvParams p, const QmvPlan& plan, int epi, cudaStream_t s,
+                   const CUtensorMap* tw, const CUtensorMap* ts) {
   if (p.N % 16 || p.K % 64) return fail(AGXC_EINVAL, "qmv: N must be a multiple of 16 and K of 64");
   if (p.nb < 1 || p.nb > 8) return fail(AGXC_EINVAL, "qmv: 1 to 8 activation rows");
+  if (plan.SC > 1 && (!p.part || !p.counters)) return fail(AGXC_EINVAL, "qmv: split K needs scratch");
+  if ((p.N / 16) % plan.RW) return fail(AGXC_EINVAL, "qmv: plan's RW does not divide the row tiles");
   p.G = p.K / 64;
   p.SC = plan.SC;
   p.GC = plan.GC;
+  p.CG = plan.CG;
   p.stages = plan.stages;
-  if (p.bits == 4) return dispatch_nb<4>(ctx, p, plan, epi, s);
-  if (p.bits == 8) return dispatch_nb<8>(ctx, p, plan, epi, s);
+  CUtensorMap mw, ms;
+  if (!tw || !ts) {
+    if (int rc = qmv_maps(plan, p.w, p.sb, p.N, p.K, p.bits, &mw, &ms)) return rc;
+    tw = &mw;
+    ts = &ms;
+  }
+  if (p.bits == 4) return dispatch_nb<4>(ctx, p, plan, epi, *tw, *ts, s);
+  if (p.bits == 8) return dispatch_nb<8>(ctx, p, plan, epi, *tw, *ts, s);
   return fail(AGXC_EINVAL, "qmv: 4- or 8-bit weights");
 }
 

@@ -1,6 +1,7 @@
 // internal.h — the library's internal types: context, device pack, GEMV and attention launch descriptions.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -43,7 +44,7 @@ struct QmvParams {
   const uint8_t* w = nullptr;
   const uint8_t* sb = nullptr;
   int N = 0, K = 0, G = 0;        // rows, columns, groups (K/64)
-  int SC = 1, GC = 0;             // K chunks, groups per chunk
+  int SC = 1, GC = 0, CG = 0;     // K splits, groups per unit (K range of a CTA), groups per streamed chunk
   int bits = 4, sdt = 0, nb = 1;
   int stages = 2;
   // x
@@ -86,14 +87,18 @@ struct QmvParams {
 };
 
 struct QmvPlan {
-  int SC = 1, GC = 0, RW = 1, EB = 1, stages = 2, grid = 0;
+  int SC = 1, GC = 0, CG = 0, RW = 1, EB = 1, stages = 2, grid = 0;
   size_t smem = 0;
 };
 
 QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits);
 // Scratch sizes a plan needs.
 size_t qmv_part_floats(const QmvPlan& p, int N, int nb, int epi);
-int launch_qmv_epi(const agxc_ctx* ctx, QmvParams p, const QmvPlan& plan, int epi, cudaStream_t s);
+// tw/ts: the plan's tensor maps of the pack (weights, scale/bias); NULL = encode them for this launch.
+int launch_qmv_epi(const agxc_ctx* ctx, QmvParams p, const QmvPlan& plan, int epi, cudaStream_t s,
+                   const CUtensorMap* tw = nullptr, const CUtensorMap* ts = nullptr);
+int qmv_maps(const QmvPlan& plan, const uint8_t* w, const uint8_t* sb, int N, int K, int bits, CUtensorMap* tw,
+             CUtensorMap* ts);
 int qmv_configure(const agxc_ctx* ctx);
 
 struct AttnParams {
@@ -111,6 +116,7 @@ struct AttnParams {
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
+int attn_configure(const agxc_ctx* ctx);
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);
 
@@ -118,9 +124,10 @@ int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, flo
 int launch_quantize(const float* w, int N, int K, int bits, int sdt, uint32_t* packed, uint16_t* s16, uint16_t* b16,
                     cudaStream_t s);
 // Re-lay out rows [0, n_src) of a reference-format pack into tile rows; source row tile t lands at destination
-// row tile t * rt_stride + rt_offset.
+// row tile t * rt_stride + rt_offset. rope_hd > 0 places the rows of each head of rope_hd rows so that tile t of the
+// head holds logical rows 8t..8t+7 (tile rows 0-7) and rope_hd/2 + 8t.. (tile rows 8-15): RoPE pairs share a tile.
 int launch_relayout(const uint32_t* packed, const uint16_t* s16, const uint16_t* b16, int n_src, int K, int bits,
-                    uint8_t* tiles, uint8_t* sb, int rt_stride, int rt_offset, cudaStream_t s);
+                    uint8_t* tiles, uint8_t* sb, int rt_stride, int rt_offset, cudaStream_t s, int rope_hd = 0);
 int launch_unpack(const agxc_pack* p, uint8_t* fields, cudaStream_t s);
 int launch_dequant(const agxc_pack* p, float* w, cudaStream_t s);
 

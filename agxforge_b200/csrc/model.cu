@@ -337,9 +337,9 @@ int model_set_pack(agxc_model* m, int layer, int role, const void* packed, const
   const agxc_model_desc& D = m->d;
   if (role != AGXC_ROLE_HEAD && (layer < 0 || layer >= D.n_layers)) return fail(AGXC_EINVAL, "set_pack: bad layer");
   agxc_pack* dst = nullptr;
-  int n = 0, k = 0, stride = 1, offset = 0;
+  int n = 0, k = 0, stride = 1, offset = 0, rope_hd = 0;
   switch (role) {
-    case AGXC_ROLE_QKV: dst = &m->qkv[layer]; n = m->qkv_rows; k = D.d_model; break;
+    case AGXC_ROLE_QKV: dst = &m->qkv[layer]; n = m->qkv_rows; k = D.d_model; rope_hd = D.head_dim; break;
     case AGXC_ROLE_WO: dst = &m->wo[layer]; n = D.d_model; k = m->attn_dim; break;
     case AGXC_ROLE_GATE: dst = &m->gu[layer]; n = D.ffn; k = D.d_model; stride = 2; offset = 0; break;
     case AGXC_ROLE_UP: dst = &m->gu[layer]; n = D.ffn; k = D.d_model; stride = 2; offset = 1; break;
@@ -362,7 +362,8 @@ int model_set_pack(agxc_model* m, int layer, int role, const void* packed, const
     dp = t; ds = t + pb; db = t + pb + sbb;
   }
   int rc = launch_relayout(static_cast<const uint32_t*>(dp), static_cast<const uint16_t*>(ds),
-                           static_cast<const uint16_t*>(db), n, k, D.bits, dst->tiles, dst->sb, stride, offset, s);
+                           static_cast<const uint16_t*>(db), n, k, D.bits, dst->tiles, dst->sb, stride, offset, s,
+                           rope_hd);
   cudaError_t e = cudaStreamSynchronize(s);
   if (tmp) cudaFree(tmp);
   if (rc) return rc;

@@ -73,9 +73,17 @@ __device__ __forceinline__ uint32_t field_of(const uint32_t* __restrict__ packed
   return (word >> (bits * (k % per))) & ((1u << bits) - 1u);
 }
 
+// The source row of physical row `prow` (identity, or the RoPE-pair placement within heads of rope_hd rows).
+__device__ __forceinline__ int src_row(int prow, int rope_hd) {
+  if (!rope_hd) return prow;
+  const int head = prow / rope_hd, within = prow % rope_hd;
+  const int t = within / 16, r16 = within % 16;
+  return head * rope_hd + (r16 < 8 ? 8 * t + r16 : rope_hd / 2 + 8 * t + (r16 - 8));
+}
+
 // One thread per 32-bit word of the destination tiles.
 __global__ void relayout_kernel(const uint32_t* __restrict__ packed, int n_src, int K, int bits,
-                                uint8_t* __restrict__ tiles, int rt_stride, int rt_offset) {
+                                uint8_t* __restrict__ tiles, int rt_stride, int rt_offset, int rope_hd) {
   const int G = K / 64;
   const int words_per_tile = bits == 4 ? 128 : 256;
   const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
@@ -90,7 +98,7 @@ __global__ void relayout_kernel(const uint32_t* __restrict__ packed, int n_src, 
   if (bits == 4) {
     const int lane = widx >> 2, i = widx & 3;
     const int r = lane >> 2, c = lane & 3;
-    const int row = rt * 16 + r + ((i & 1) ? 8 : 0);
+    const int row = src_row(rt * 16 + r + ((i & 1) ? 8 : 0), rope_hd);
     const int hi = i >> 1;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -103,7 +111,7 @@ __global__ void relayout_kernel(const uint32_t* __restrict__ packed, int n_src, 
     const int wi = 4 * h + m, j = wi >> 1, hi = wi & 1;
     const int r = lane >> 2, c = lane & 3;
     const int k0 = 64 * g + 16 * c + 4 * j + 2 * hi;
-    const int row0 = rt * 16 + r, row1 = row0 + 8;
+    const int row0 = src_row(rt * 16 + r, rope_hd), row1 = src_row(rt * 16 + r + 8, rope_hd);
     word = field_of(packed, K, 8, row0, k0) | (field_of(packed, K, 8, row0, k0 + 1) << 8) |
            (field_of(packed, K, 8, row1, k0) << 16) | (field_of(packed, K, 8, row1, k0 + 1) << 24);
   }
@@ -114,7 +122,7 @@ __global__ void relayout_kernel(const uint32_t* __restrict__ packed, int n_src, 
 
 // One thread per (tile, r): the 8-byte scale/bias entry {s[r], s[r+8], b[r], b[r+8]}.
 __global__ void relayout_sb_kernel(const uint16_t* __restrict__ s16, const uint16_t* __restrict__ b16, int n_src,
-                                   int K, uint8_t* __restrict__ sb, int rt_stride, int rt_offset) {
+                                   int K, uint8_t* __restrict__ sb, int rt_stride, int rt_offset, int rope_hd) {
   const int G = K / 64;
   const long long gid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const long long total = static_cast<long long>(n_src / 16) * G * 8;
@@ -124,7 +132,7 @@ __global__ void relayout_sb_kernel(const uint16_t* __restrict__ s16, const uint1
   const int g = static_cast<int>(tile % G);
   const int rt = static_cast<int>(tile / G);
   const int rt_dst = rt * rt_stride + rt_offset;
-  const size_t r0 = static_cast<size_t>(rt) * 16 + r, r1 = r0 + 8;
+  const size_t r0 = src_row(rt * 16 + r, rope_hd), r1 = src_row(rt * 16 + r + 8, rope_hd);
   ushort4 e;
   e.x = s16[r0 * G + g];
   e.y = s16[r1 * G + g];
@@ -134,16 +142,17 @@ __global__ void relayout_sb_kernel(const uint16_t* __restrict__ s16, const uint1
 }
 
 int launch_relayout(const uint32_t* packed, const uint16_t* s16, const uint16_t* b16, int n_src, int K, int bits,
-                    uint8_t* tiles, uint8_t* sb, int rt_stride, int rt_offset, cudaStream_t s) {
+                    uint8_t* tiles, uint8_t* sb, int rt_stride, int rt_offset, cudaStream_t s, int rope_hd) {
+  if (rope_hd && (rope_hd % 16 || n_src % rope_hd)) return fail(AGXC_EINVAL, "relayout: rows must be whole heads");
   const int G = K / 64;
   const long long words = static_cast<long long>(n_src / 16) * G * (bits == 4 ? 128 : 256);
   const int threads = 256;
   relayout_kernel<<<static_cast<unsigned>((words + threads - 1) / threads), threads, 0, s>>>(
-      packed, n_src, K, bits, tiles, rt_stride, rt_offset);
+      packed, n_src, K, bits, tiles, rt_stride, rt_offset, rope_hd);
   AGXC_CUDA(cudaGetLastError());
   const long long ents = static_cast<long long>(n_src / 16) * G * 8;
   relayout_sb_kernel<<<static_cast<unsigned>((ents + threads - 1) / threads), threads, 0, s>>>(
-      s16, b16, n_src, K, sb, rt_stride, rt_offset);
+      s16, b16, n_src, K, sb, rt_stride, rt_offset, rope_hd);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

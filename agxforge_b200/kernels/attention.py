@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes as C
 
 from agxforge_b200 import _native as N
+from agxforge_b200.kernels import qmv as _qmv
 
 
 def attention(q16, K, V, q0, splits=0, device=0):
@@ -36,5 +37,5 @@ def attention(q16, K, V, q0, splits=0, device=0):
     q16, K, V = q16.contiguous(), K.contiguous(), V.contiguous()
     N.check(N.lib().agxc_attention_dev(N.context(device), nb, H, KVH, hd, cap, N.ptr(q0t), N.ptr(q16), N.ptr(K),
                                        N.ptr(V), N.ptr(out), int(splits),
-                                       C.c_void_p(torch.cuda.current_stream().cuda_stream)), "attention")
+                                       _qmv._stream(torch)), "attention")
     return out

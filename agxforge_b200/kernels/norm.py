@@ -6,6 +6,7 @@ from __future__ import annotations
 import ctypes as C
 
 from agxforge_b200 import _native as N
+from agxforge_b200.kernels import qmv as _qmv
 
 
 def rmsnorm(x, g, eps=1e-6, device=0):
@@ -20,6 +21,6 @@ def rmsnorm(x, g, eps=1e-6, device=0):
     x, g = x.contiguous(), g.contiguous()
     out = torch.empty((nb, d), dtype=torch.float16, device=x.device)
     N.check(N.lib().agxc_rmsnorm_dev(N.context(device), N.ptr(x), int(x.dtype == torch.float32), nb, d, N.ptr(g),
-                                     float(eps), N.ptr(out), C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                                     float(eps), N.ptr(out), _qmv._stream(torch)),
             "rmsnorm")
     return out

@@ -32,7 +32,10 @@ def _torch():
 
 
 def _stream(torch):
-    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    """torch's current stream as a cudaStream_t. torch's default stream has handle 0, which the C ABI reads as "the
+    context's own stream"; it is passed as cudaStreamLegacy (1) so our kernels stay ordered with torch's work."""
+    h = torch.cuda.current_stream().cuda_stream
+    return C.c_void_p(h if h else 1)
 
 
 def check_shape(N_, K, bits, group=64):
