@@ -19,6 +19,7 @@ TOKEN_UNSET = 0xFFFFFFFF
 EPI_F32, EPI_RES1, EPI_RES2, EPI_SWIGLU = 0, 1, 2, 3
 ROLE_QKV, ROLE_WO, ROLE_GATE, ROLE_UP, ROLE_DOWN, ROLE_HEAD = range(6)
 VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
+OPT_PDL = 0
 
 
 class PackDesc(C.Structure):
@@ -30,7 +31,8 @@ class QmvArgs(C.Structure):
     _fields_ = [("pack", C.c_void_p), ("nb", C.c_int32), ("x_dev", C.c_void_p), ("x_f32", C.c_int32),
                 ("x_ld", C.c_int32), ("norm_gain_dev", C.c_void_p), ("eps", C.c_float), ("epi", C.c_int32),
                 ("out_dev", C.c_void_p), ("out_ld", C.c_int32), ("res_dev", C.c_void_p), ("res_ld", C.c_int32),
-                ("splits", C.c_int32)]
+                ("splits", C.c_int32), ("row_tiles", C.c_int32), ("chunk_groups", C.c_int32),
+                ("stages", C.c_int32)]
 
 
 class ModelDesc(C.Structure):
@@ -77,6 +79,8 @@ SIGNATURES = {
     "agxc_model_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
     "agxc_model_logits_dev": (_I, [_P, C.POINTER(_P)]),
     "agxc_model_profile": (_I, [_P, _I, _P, _P]),
+    "agxc_model_set_option": (_I, [_P, _I, _I]),
+    "agxc_model_plan_info": (_I, [_P, C.c_char_p, C.c_size_t]),
     "agxc_model_kernel_count": (_I, [_P, C.POINTER(C.c_int32)]),
 }
 

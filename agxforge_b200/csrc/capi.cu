@@ -237,8 +237,12 @@ int agxc_qmv(agxc_ctx* ctx, const agxc_qmv_args* a, void* stream) {
     return fail(AGXC_EINVAL, "qmv: res_ld < N");
   const int G = pk->k / 64;
   if (a->splits < 0 || (a->splits > 0 && G % a->splits)) return fail(AGXC_EINVAL, "qmv: splits must divide K/64");
+  if (a->row_tiles && a->row_tiles != 1 && a->row_tiles != 2 && a->row_tiles != 4 && a->row_tiles != 8)
+    return fail(AGXC_EINVAL, "qmv: row_tiles 1, 2, 4 or 8");
+  if (a->stages && (a->stages < 2 || a->stages > 8)) return fail(AGXC_EINVAL, "qmv: stages 2..8");
   const int epi = a->epi;
-  QmvPlan plan = plan_qmv(ctx, pk->n, pk->k, pk->bits, a->nb, epi, 0, a->splits);
+  QmvPlan plan = plan_qmv(ctx, pk->n, pk->k, pk->bits, a->nb, epi, 0, a->splits, a->row_tiles, a->chunk_groups,
+                          a->stages);
   QmvParams p;
   p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.bits = pk->bits; p.sdt = pk->sdt; p.nb = a->nb;
   p.x = a->x_dev; p.x_f32 = a->x_f32; p.x_ld = a->x_ld;
@@ -289,18 +293,7 @@ int agxc_attention_dev(agxc_ctx* ctx, int nb, int heads, int kv_heads, int head_
   p.vc = reinterpret_cast<const __half*>(v_dev);
   p.out = reinterpret_cast<__half*>(out_dev);
   p.err = ctx->err_dev;
-  cudaStream_t s = stream_of(ctx, stream);
-  float* part = nullptr;
-  unsigned* cnt = nullptr;
-  AGXC_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&part), attn_part_floats(nb, heads, p.S, head_dim) * 4, s));
-  AGXC_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&cnt), static_cast<size_t>(nb) * kv_heads * 4, s));
-  AGXC_CUDA(cudaMemsetAsync(cnt, 0, static_cast<size_t>(nb) * kv_heads * 4, s));
-  p.part = part;
-  p.counters = cnt;
-  int rc = launch_attention(ctx, p, s);
-  cudaFreeAsync(part, s);
-  cudaFreeAsync(cnt, s);
-  return rc;
+  return launch_attention(ctx, p, stream_of(ctx, stream));
 }
 
 }  // extern "C"

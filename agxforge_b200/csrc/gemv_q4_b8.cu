@@ -1,0 +1,4 @@
+// Instantiates the 4-bit GEMV kernels for 8 activation rows (see gemv_impl.cuh).
+#include "gemv_impl.cuh"
+
+AGXC_GEMV_INSTANTIATE(4, 8)

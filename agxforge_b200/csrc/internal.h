@@ -15,6 +15,7 @@ struct agxc_ctx {
   unsigned* err_dev = nullptr;   // the device error word
   int num_sms = 148;
   int max_smem_optin = 0;
+  int max_cluster = 8;           // the largest attention cluster the device places
 };
 
 // A pack in the B200 tile layout: tiles[rt][g] of 16 rows x 64 k (512 B at 4 bits, 1,024 B at 8 bits; lane l of a
@@ -91,7 +92,9 @@ struct QmvPlan {
   size_t smem = 0;
 };
 
-QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits);
+// force_*: 0 = the planner's choice (tuning and tests override them)
+QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits, int force_rw = 0,
+                 int force_cg = 0, int force_stages = 0);
 // Scratch sizes a plan needs.
 size_t qmv_part_floats(const QmvPlan& p, int N, int nb, int epi);
 // tw/ts: the plan's tensor maps of the pack (weights, scale/bias); NULL = encode them for this launch.
@@ -108,15 +111,15 @@ struct AttnParams {
   const __half* kc = nullptr;
   const __half* vc = nullptr;
   __half* out = nullptr;
-  float* part = nullptr;          // [nb][H][S][hd + 2]
-  unsigned* counters = nullptr;   // [nb][KVH]
+  float* part = nullptr;          // unused (the chunks merge in distributed shared memory)
+  unsigned* counters = nullptr;   // unused
   unsigned* err = nullptr;
   int pdl = 0;
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
-int attn_configure(const agxc_ctx* ctx);
+int attn_configure(agxc_ctx* ctx);
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);
 

@@ -13,7 +13,9 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <string>
 #include <random>
 #include <vector>
 
@@ -287,7 +289,6 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, B, EPI_SWIGLU));
   part = std::max(part, qmv_part_floats(m->p_down, d, B, EPI_RES2));
   if ((rc = dalloc_t(m, &m->part, std::max<size_t>(part, 64)))) return bail(rc);
-  if ((rc = dalloc_t(m, &m->apart, attn_part_floats(B, D.n_heads, m->attn_S, hd)))) return bail(rc);
   if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(m->p_head.grid) * 16))) return bail(rc);
   m->counters_n = 24576;
   if (static_cast<size_t>(m->qkv_rows / hd) > 4096 || static_cast<size_t>(B * D.n_kv_heads) > 4096 ||
@@ -666,6 +667,37 @@ int agxc_model_logits_dev(agxc_model* m, const float** out) {
 int agxc_model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_launches) {
   if (!m || !kind_ms || !kind_launches || steps < 1) return agxc::fail(AGXC_EINVAL, "profile: bad argument");
   return agxc::model_profile(m, steps, kind_ms, kind_launches);
+}
+
+int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
+  if (!m || !buf || !len) return agxc::fail(AGXC_EINVAL, "plan_info: bad argument");
+  auto one = [](const char* name, const agxc::QmvPlan& p) {
+    return std::string("\"") + name + "\": {\"row_tiles\": " + std::to_string(p.RW) + ", \"splits\": " +
+           std::to_string(p.SC) + ", \"groups\": " + std::to_string(p.GC) + ", \"chunk_groups\": " +
+           std::to_string(p.CG) + ", \"stages\": " + std::to_string(p.stages) + ", \"grid\": " +
+           std::to_string(p.grid) + ", \"smem\": " + std::to_string(p.smem) + "}";
+  };
+  std::string j = "{" + one("qkv", m->p_qkv) + ", " + one("wo", m->p_wo) + ", " + one("ffn", m->p_gu) + ", " +
+                  one("down", m->p_down) + ", " + one("head", m->p_head) + ", \"attn\": {\"chunks\": " +
+                  std::to_string(m->attn_S) + ", \"max_cluster\": " + std::to_string(m->ctx->max_cluster) +
+                  "}, \"pdl\": " + std::to_string(m->pdl) + "}";
+  std::snprintf(buf, len, "%s", j.c_str());
+  return 0;
+}
+
+int agxc_model_set_option(agxc_model* m, int option, int value) {
+  if (!m) return agxc::fail(AGXC_EINVAL, "set_option: null model");
+  if (option != AGXC_OPT_PDL) return agxc::fail(AGXC_EINVAL, "set_option: unknown option");
+  m->pdl = value ? 1 : 0;
+  if (m->exec) {
+    cudaGraphExecDestroy(m->exec);
+    m->exec = nullptr;
+  }
+  if (m->graph) {
+    cudaGraphDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  return 0;
 }
 
 int agxc_model_kernel_count(agxc_model* m, int32_t* n) {

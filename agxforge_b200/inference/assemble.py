@@ -127,6 +127,19 @@ class DecodeModel:
             N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, C.c_void_p(t.data_ptr()),
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
+    def set_option(self, option, value):
+        """Model options: "pdl" (programmatic dependent launch between the step's kernels, default on)."""
+        opts = {"pdl": N.OPT_PDL}
+        if option not in opts:
+            raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
+        N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")
+
+    def plan_info(self):
+        """The launch plan of every kernel of the step (dict)."""
+        buf = C.create_string_buffer(4096)
+        N.check(N.lib().agxc_model_plan_info(self._h, buf, 4096), "plan_info")
+        return json.loads(buf.value.decode())
+
     @property
     def weight_bytes(self):
         return int(N.lib().agxc_model_weight_bytes(self._h))
@@ -179,9 +192,11 @@ class DecodeModel:
         return toks, lg, dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches_per_step=t.launches_per_step)
 
     def close(self):
-        if getattr(self, "_h", None) and N._lib is not None:
-            N._lib.agxc_model_free(self._h)
-            self._h = None
+        h = getattr(self, "_h", None)
+        lib = getattr(N, "_lib", None) if N is not None else None
+        if h and lib is not None:
+            lib.agxc_model_free(h)
+        self._h = None
 
     def __del__(self):
         self.close()

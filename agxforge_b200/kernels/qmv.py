@@ -137,15 +137,19 @@ class Pack:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h and N._lib is not None:
-            N._lib.agxc_pack_free(h)
-            self._h = None
+        lib = getattr(N, "_lib", None) if N is not None else None
+        if h and lib is not None:
+            lib.agxc_pack_free(h)
+        self._h = None
 
 
-def qmv(pack, x, norm_gain=None, eps=1e-6, epi="f32", res=None, out=None, splits=0):
+def qmv(pack, x, norm_gain=None, eps=1e-6, epi="f32", res=None, out=None, splits=0, row_tiles=0, chunk_groups=0,
+        stages=0):
     """y = W x on the device for x [nb, K] (nb 1..8; fp16 or fp32 torch tensor). Optional RMSNorm of x first
     (norm_gain fp16 [K]). epi: "f32" -> fp32 [nb, N]; "add16" -> fp32 h = y + res (fp16); "add32_to16" -> fp16
-    fp16(y + res) (res fp32); "swiglu" -> fp16 [nb, N/2] fp16(silu(gate) up). Returns the output tensor."""
+    fp16(y + res) (res fp32); "swiglu" -> fp16 [nb, N/2] fp16(silu(gate) up). Returns the output tensor.
+    splits / row_tiles / chunk_groups / stages override the launch planner (0 = its choice).
+    x is staged as fp16: every GEMV input of the decode graph holds fp16 values."""
     torch = _torch()
     if epi not in EPILOGUES:
         raise ValueError("qmv: epilogue one of %s" % sorted(EPILOGUES))
@@ -170,6 +174,7 @@ def qmv(pack, x, norm_gain=None, eps=1e-6, epi="f32", res=None, out=None, splits
     if norm_gain is not None:
         norm_gain = norm_gain.contiguous()
     a = N.QmvArgs(pack.handle, nb, N.ptr(x), int(x.dtype == torch.float32), K, N.ptr(norm_gain), float(eps),
-                  EPILOGUES[epi], N.ptr(out), nout, N.ptr(res), pack.N if res is not None else 0, int(splits))
+                  EPILOGUES[epi], N.ptr(out), nout, N.ptr(res), pack.N if res is not None else 0, int(splits),
+                  int(row_tiles), int(chunk_groups), int(stages))
     N.check(N.lib().agxc_qmv(N.context(pack.device), C.byref(a), _stream(torch)), "qmv")
     return out

@@ -307,6 +307,7 @@ def main():
                                frac=round(step_gbs / peak, 4), bytes_per_token=int(step_bytes / batch),
                                weight_bytes=w_bytes, peak_source=peak_kind),
             kernels=kinds,
+            plans=m.plan_info(),
             cpu_baseline=cpu,
             clocks=clk.summary(),
             gpu_launches=int(launches * K),

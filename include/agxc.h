@@ -100,7 +100,10 @@ typedef struct {
   int32_t out_ld;
   const void* res_dev;        /* RES1: fp16 [nb][res_ld]; RES2: fp32 [nb][res_ld] */
   int32_t res_ld;
-  int32_t splits;             /* K chunks; 0 = planner's choice */
+  int32_t splits;             /* K splits across CTAs; 0 = planner's choice */
+  int32_t row_tiles;          /* 16-row tiles per work unit (1, 2, 4, 8); 0 = planner's choice */
+  int32_t chunk_groups;       /* 64-k groups per streamed chunk; 0 = planner's choice */
+  int32_t stages;             /* shared-memory ring stages (2..8); 0 = planner's choice */
 } agxc_qmv_args;
 
 /* Gate and up projections [f][k] each, re-laid out as ONE interleaved pack of 2f rows for the fused SwiGLU
@@ -118,7 +121,8 @@ AGXC_API int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int n
 /* ---- decode attention (agxforge/kernels/attention.py: split 86-165, merge 1326-1371; attn_reference 1458) -----
  * One query row per head at position q0[b] (keys 0..q0, q0 clamped to cap-1); q16 fp16 [nb][heads][head_dim]
  * already scaled by log2(e)/sqrt(head_dim) (the softmax is base 2); caches fp16 [nb][kv_heads][cap][head_dim];
- * out fp16 [nb][heads*head_dim]. Split-KV over `splits` chunks (0 = planner) with a log-sum-exp merge. */
+ * out fp16 [nb][heads*head_dim]. Split-KV over `splits` key chunks (a power of two up to 16, one thread-block
+ * cluster per KV head; 0 = planner) with a log-sum-exp merge in distributed shared memory. */
 AGXC_API int agxc_attention_dev(agxc_ctx* ctx, int nb, int heads, int kv_heads, int head_dim, int cap, const uint32_t* q0_dev,
                        const uint16_t* q16_dev, const uint16_t* k_dev, const uint16_t* v_dev, uint16_t* out_dev,
                        int splits, void* stream);
@@ -197,6 +201,15 @@ AGXC_API int agxc_model_logits_dev(agxc_model* m, const float** out);
 #define AGXC_KIND_DOWN 4
 #define AGXC_KIND_HEAD 5
 AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/, int32_t* kind_launches /*[6]*/);
+
+/* Model options (each re-captures the step's graph on the next decode). */
+#define AGXC_OPT_PDL 0        /* 1 (default): launch each kernel with programmatic dependent launch, so it streams its
+                                 weights while its predecessor finishes; 0: plain stream order */
+AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
+
+/* The model's launch plans as a JSON object (per kernel: row tiles per unit, K splits, groups per unit and chunk,
+ * stages, grid, shared memory; attention: key chunks per KV head). Writes at most `len` bytes including the NUL. */
+AGXC_API int agxc_model_plan_info(agxc_model* m, char* buf, size_t len);
 
 /* Kernels per decode step and their names (for launch accounting). */
 AGXC_API int agxc_model_kernel_count(agxc_model* m, int32_t* n);

@@ -237,7 +237,7 @@ def test_attention_splits_agree(torch):
     K = rng.standard_normal((1, KVH, cap, hd)).astype(np.float16)
     V = rng.standard_normal((1, KVH, cap, hd)).astype(np.float16)
     ref = D.attention_step(q16[0].astype(np.float64), K[0], V[0], q0 + 1, KVH)
-    for S in (1, 3, 16, 64):
+    for S in (1, 2, 4, 8, 16):
         out = A.attention(torch.from_numpy(q16).cuda(), torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(),
                           [q0], splits=S).cpu().numpy().astype(np.float64).reshape(H, hd)
         assert np.all(np.abs(out - ref) <= 2 * ulp16(ref) + 2e-3 * np.abs(ref).max())
@@ -253,3 +253,32 @@ def test_bad_shapes_raise(torch):
         Q.qmv(pk, torch.zeros((1, 128), dtype=torch.float16, device="cuda"))
     with pytest.raises(ValueError):
         Q.qmv(pk, torch.zeros((9, 256), dtype=torch.float16, device="cuda"))
+
+
+@pytest.mark.parametrize("rw,cg,st", [(1, 32, 2), (2, 16, 3), (4, 8, 4), (8, 4, 8), (8, 16, 2), (1, 2, 5)])
+@pytest.mark.parametrize("nb", [1, 3])
+def test_gemv_plan_overrides_agree(torch, rw, cg, st, nb):
+    """Every unit shape (row tiles x K lanes), chunk size and ring depth computes the same GEMV."""
+    from agxforge_b200.kernels import qmv as Q
+    pk, x16, W64 = _gemv_case(torch, 4, 512, 2048, nb, seed=21)
+    y = Q.qmv(pk, torch.from_numpy(x16).cuda(), row_tiles=rw, chunk_groups=cg, stages=st).cpu().numpy()
+    ref = x16.astype(np.float64) @ W64.T
+    bound = 32 * EPS32 * (np.abs(x16.astype(np.float64)) @ np.abs(W64).T) + 1e-7
+    assert np.all(np.abs(y.astype(np.float64) - ref) <= bound)
+
+
+@pytest.mark.parametrize("rw", [2, 4, 8])
+def test_swiglu_unit_shapes(torch, rw):
+    from agxforge_b200.kernels import qmv as Q
+    rng = np.random.default_rng(31)
+    F, K = 256, 1024
+    g = P.quantize(_w(rng, F, K), 4, scale_dtype="fp16")
+    u = P.quantize(_w(rng, F, K), 4, scale_dtype="fp16")
+    pk = Q.Pack.gateup(g[:3], u[:3], F, K, bits=4)
+    x16 = rng.standard_normal((1, K)).astype(np.float16)
+    act = Q.qmv(pk, torch.from_numpy(x16).cuda(), epi="swiglu", row_tiles=rw).cpu().numpy().astype(np.float64)
+    x = x16.astype(np.float64)
+    gv = x @ P.dequant64(g[3], g[1], g[2], "fp16").T
+    uv = x @ P.dequant64(u[3], u[1], u[2], "fp16").T
+    want = D.silu(gv) * uv
+    assert np.all(np.abs(act - want) <= 2 * ulp16(want) + 1e-4 * np.abs(want).max())
