@@ -114,6 +114,15 @@ AGXC_API int agxc_pack_create_gateup(agxc_ctx* ctx, const agxc_pack_desc* desc_e
 
 AGXC_API int agxc_qmv(agxc_ctx* ctx, const agxc_qmv_args* args, void* stream);
 
+/* agxc_qmv for callers that may not allocate device memory (no counterpart in the reference, whose GEMV kernels
+ * take no scratch). Same arguments, kernels, launch plan and results as agxc_qmv; the split-K scratch comes from a
+ * static device block (1,048,576 fp32 partials, 8,192 row-block counters) instead of the stream-ordered allocator.
+ * Rejects with AGXC_EINVAL, before launching, a plan whose splits x N x nb partials or N / 16 + 1 counters exceed
+ * that block. Clears the counters it uses on `stream` before the launch (cudaMemsetAsync). The block is shared by
+ * every call on a device: calls that may overlap there (other streams, threads, a graph replay) race and must be
+ * ordered on one stream. The first call on a device looks up the block's address; make it outside stream capture. */
+AGXC_API int agxc_qmv_noalloc(agxc_ctx* ctx, const agxc_qmv_args* args, void* stream);
+
 /* Standalone RMSNorm rows (norm.build_rmsnorm_wide, agxforge/kernels/norm.py:42-155): out fp16 [nb][d]. */
 AGXC_API int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int nb, int d, const uint16_t* gain_dev,
                      float eps, uint16_t* out_dev, void* stream);
