@@ -2,14 +2,18 @@
 // 86-165 and merge 1326-1371, attn_reference 1458-1580), and the standalone RMSNorm (norm.py:42-155).
 //
 // One thread-block CLUSTER per (KV head, sequence); its CTAs take consecutive key chunks of the live length q0 + 1
-// (read on the device, so a captured graph serves every position). A chunk's K and V rows move into shared memory by
-// bulk TMA copies (sub-chunks of 64 keys, two stages; the history rows are requested before the upstream kernel
-// finishes, the new row q0 is read after it, into registers). 8 warps take blocks of 4 keys (each lane 4 or 2 of the
-// head dims), score every query head of the GQA group against each key (the group shares the K/V stream) and keep an
-// online base-2 softmax per head (q is pre-scaled by log2(e)/sqrt(hd)). Each CTA's partial (m, l, o[hd]) stays in its
-// shared memory; after a cluster barrier every CTA merges a slice of the outputs by reading the others' partials
-// through distributed shared memory: M = max m_s, w_s = 2^(m_s - M), L = sum l_s w_s, O = sum o_s w_s,
-// out = fp16(O / L). No global scratch, fences or atomics.
+// (read on the device, so a captured graph serves every position). The scores and the weighted values run on the
+// tensor cores (mma.sync m16n8k16, fp16 in, fp32 accumulate) with the KEYS as the M dimension and the GQA group's
+// query heads (up to 8) as N, so one MMA covers every head of the group:
+//     S^T[16 keys][8 heads]  = K[16 keys][hd] . Q^T[hd][8 heads]        (K fragments by ldmatrix)
+//     O^T[hd][8 heads]      += V^T[hd][16 keys] . P^T[16 keys][8 heads]  (V by ldmatrix.trans, P^T by movmatrix.trans)
+// q is pre-scaled by log2(e)/sqrt(hd), so the softmax is base 2; P is rounded to fp16 for the second product, the
+// running sums stay fp32. K and V move into shared memory by TMA tensor copies (boxes of 64 dims x 128 keys, 128-byte
+// swizzle, so ldmatrix reads without bank conflicts) in 128-key sub-chunks, two stages; each warp takes a 16-key tile
+// of every sub-chunk. The history rows are requested before the upstream kernel finishes; the new row q0 is read after
+// it and replaces its stale copy in shared memory. Each CTA's partial (m, l, o[hd]) stays in its shared memory;
+// after a cluster barrier every CTA merges a slice of the outputs by reading the others' partials through
+// distributed shared memory: M = max m_s, w_s = 2^(m_s - M), L = sum l_s w_s, O = sum o_s w_s, out = fp16(O / L).
 #include <algorithm>
 
 #include "common.cuh"
@@ -21,35 +25,26 @@ namespace {
 
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = 8;
-constexpr int kKeyBlock = 4;
-constexpr int kSub = 64;        // keys per shared-memory sub-chunk (K and V rows of one KV head)
-constexpr int kMinChunk = 32;   // the fewest keys a chunk takes before more chunks are used
+constexpr int kSub = kAttnKeys;  // keys per shared-memory sub-chunk: one 16-key tile per warp
+constexpr int kMinChunk = 32;    // the fewest keys a chunk takes before more chunks are used
+constexpr int kHeadsN = 8;       // the MMA's N: query heads of one KV head
 
-template <int HD>
-struct Lanes;
-template <>
-struct Lanes<128> {
-  static constexpr int D = 4;
-  __device__ static void load(const __half* p, float* f) {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    __half2 h0, h1;
-    memcpy(&h0, &u.x, 4);
-    memcpy(&h1, &u.y, 4);
-    const float2 a = __half22float2(h0), b = __half22float2(h1);
-    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
-  }
-};
-template <>
-struct Lanes<64> {
-  static constexpr int D = 2;
-  __device__ static void load(const __half* p, float* f) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p));
-    f[0] = a.x; f[1] = a.y;
-  }
-};
+// A stage holds K then V of one sub-chunk, each as HD / 64 boxes of [kSub rows][128 B] in the TMA's 128-byte swizzle
+// (the 16-byte chunk c of row r sits at chunk c ^ (r % 8)), so ldmatrix reads 8 rows of one chunk without conflicts.
+__host__ __device__ constexpr int box_bytes() { return kSub * 128; }
+__host__ __device__ constexpr int stage_bytes(int hd) { return 2 * (hd / 64) * box_bytes(); }
+__host__ __device__ inline int attn_smem_bytes(int hd) { return 1024 + 2 * stage_bytes(hd); }
 
-__host__ __device__ inline int attn_smem_bytes(int hd) { return 128 + 2 * 2 * kSub * hd * 2; }
-
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset of (row, 16-byte chunk) in a box
+  return static_cast<uint32_t>(row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -63,27 +58,46 @@ __device__ __forceinline__ float ld_dsmem(uint32_t a) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
   return v;
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
 
 // One CLUSTER per (KV head, sequence): its gridDim.x CTAs take consecutive key chunks [s L, min(nk, (s+1) L)),
 // L = ceil(nk / gridDim.x), and meet in distributed shared memory for the merge. Every CTA passes both cluster
 // barriers on every path (an empty chunk contributes m = -inf), so no CTA waits on one that left.
-template <int HD, int GM>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
-  constexpr int D = Lanes<HD>::D;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  __half* kv = reinterpret_cast<__half*>(smem + 128);  // stage st: K rows at st*2*kSub*HD, V rows after kSub*HD
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const __grid_constant__ CUtensorMap tk,
+                                                            const __grid_constant__ CUtensorMap tv) {
+  constexpr int KS = HD / 16;  // k-steps of the score product, dim tiles of the value product
+  constexpr int NB = HD / 64;  // boxes per K (or V) sub-chunk
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // the swizzle wants 1,024 B
   const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int CL = gridDim.x;  // the cluster spans gridDim.x: the CTA's rank is blockIdx.x
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, t4 = lane & 3;  // MMA fragment coordinates
   const int G = p.H / p.KVH;
-  __shared__ float sm_m[kAttnWarps][GM], sm_l[kAttnWarps][GM];
-  __shared__ float sm_o[kAttnWarps][GM][HD];
-  __shared__ float part_m[GM], part_l[GM];
-  __shared__ float part_o[GM][HD];
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ float sm_m[kAttnWarps][kHeadsN], sm_l[kAttnWarps][kHeadsN];
+  __shared__ float part_m[kHeadsN], part_l[kHeadsN];
+  __shared__ float part_o[kHeadsN][HD];
 
-  // the history rows (keys before q0) were written by earlier steps: they stream in before the upstream kernel
-  // (which appends row q0) has finished
   int pos = static_cast<int>(p.q0[b]);
   if (pos > p.cap - 1) pos = p.cap - 1;
   const int nk = pos + 1;
@@ -92,22 +106,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   const int j1 = min(nk, j0 + L);
   const int nsub = j1 > j0 ? (j1 - j0 + kSub - 1) / kSub : 0;
   const size_t kvbase = (static_cast<size_t>(b) * p.KVH + kvh) * p.cap * HD;
+  const int zrow = p.z0 + b * p.KVH + kvh;
 
-  auto issue = [&](int i) {  // sub-chunk i -> stage i % 2: the rows below pos (row pos is read after the wait)
-    const int a = j0 + i * kSub;
-    const int n = max(0, min(min(a + kSub, j1), pos) - a);
+  // sub-chunk i -> stage i % 2: whole boxes of kSub rows from key j0 + i kSub (rows past the cache end read as zero;
+  // rows from pos on are replaced or masked: row pos is written by the upstream kernel, read after the wait)
+  auto issue = [&](int i) {
     uint64_t* bar = &bars[i & 1];
-    __half* dst = kv + (i & 1) * 2 * kSub * HD;
-    mbar_arrive_expect_tx(bar, static_cast<unsigned>(2 * n * HD * 2));
-    if (n) {
-      bulk_g2s(dst, p.kc + kvbase + static_cast<size_t>(a) * HD, n * HD * 2, bar);
-      bulk_g2s(dst + kSub * HD, p.vc + kvbase + static_cast<size_t>(a) * HD, n * HD * 2, bar);
+    uint8_t* st = smem + (i & 1) * stage_bytes(HD);
+    mbar_arrive_expect_tx(bar, static_cast<unsigned>(stage_bytes(HD)));
+#pragma unroll
+    for (int h = 0; h < NB; ++h) {
+      tma_load_3d(st + h * box_bytes(), &tk, h * 64, j0 + i * kSub, zrow, bar);
+      tma_load_3d(st + (NB + h) * box_bytes(), &tv, h * 64, j0 + i * kSub, zrow, bar);
     }
   };
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
   }
   __syncthreads();
   if (tid == 0) {
@@ -118,98 +136,135 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     pdl_launch_dependents();
   }
 
-  float q[GM][D], o[GM][D], m[GM], l[GM];
+  // Q^T fragments (B operand, N = heads): lane (g8, t4) holds Q[head g8][16 ks + 2 t4 + {0, 1, 8, 9}]
+  uint32_t qb[KS][2];
+  {
+    const bool live = g8 < G;
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        p.q16 + (static_cast<size_t>(b) * p.H + kvh * G + (live ? g8 : 0)) * HD);
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int d = 0; d < D; ++d) { o[g][d] = 0.f; q[g][d] = 0.f; }
-    if (g < G) Lanes<HD>::load(p.q16 + (static_cast<size_t>(b) * p.H + kvh * G + g) * HD + lane * D, q[g]);
+    for (int ks = 0; ks < KS; ++ks) {
+      qb[ks][0] = live ? qrow[ks * 8 + t4] : 0u;
+      qb[ks][1] = live ? qrow[ks * 8 + 4 + t4] : 0u;
+    }
   }
-  // the new row, appended by the upstream kernel: this lane's dims, in registers
-  float knew[D], vnew[D];
-  const bool has_new = pos >= j0 && pos < j1;
-  if (has_new) {
-    Lanes<HD>::load(p.kc + kvbase + static_cast<size_t>(pos) * HD + lane * D, knew);
-    Lanes<HD>::load(p.vc + kvbase + static_cast<size_t>(pos) * HD + lane * D, vnew);
-  } else {
+  // running state for heads 2 t4 and 2 t4 + 1; O^T accumulators: dims 16 dt + g8 (+8) x heads 2 t4 (+1)
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float oacc[KS][4];
 #pragma unroll
-    for (int d = 0; d < D; ++d) knew[d] = vnew[d] = 0.f;
-  }
+  for (int dt = 0; dt < KS; ++dt) oacc[dt][0] = oacc[dt][1] = oacc[dt][2] = oacc[dt][3] = 0.f;
 
+  const int kt = warp * 16;               // this warp's 16-key tile of every sub-chunk
+  const int krow = kt + (lane & 7) + ((lane >> 3) & 1) * 8;   // ldmatrix row addresses: K (A = K)
+  const int vrow = kt + (lane & 7) + (lane >> 4) * 8;         // and V (A = V^T, transposed load)
   bool ok = true;
-  for (int i = 0; i < nsub; ++i) {
+  int i = 0;
+  for (; i < nsub; ++i) {
     const int a = j0 + i * kSub;
     const int n = min(kSub, j1 - a);
-    const __half* st = kv + (i & 1) * 2 * kSub * HD;
-    if (ok && !mbar_wait_bounded(&bars[i & 1], (i >> 1) & 1, p.err)) ok = false;
-    for (int kb = warp * kKeyBlock; kb < n; kb += kAttnWarps * kKeyBlock) {
-      float kf[kKeyBlock][D], vf[kKeyBlock][D];
-#pragma unroll
-      for (int t = 0; t < kKeyBlock; ++t) {
-        const int j = min(kb + t, n - 1);
-        if (a + j == pos) {
-#pragma unroll
-          for (int d = 0; d < D; ++d) { kf[t][d] = knew[d]; vf[t][d] = vnew[d]; }
-        } else {
-          Lanes<HD>::load(st + j * HD + lane * D, kf[t]);
-          Lanes<HD>::load(st + kSub * HD + j * HD + lane * D, vf[t]);
-        }
+    uint8_t* Ks = smem + (i & 1) * stage_bytes(HD);
+    uint8_t* Vs = Ks + NB * box_bytes();
+    const bool landed = mbar_wait_bounded(&bars[i & 1], (i >> 1) & 1, p.err);
+    if (__syncthreads_or(!landed)) {  // leave together: the error word is set
+      ok = false;
+      break;
+    }
+    const int n16 = (n + 15) & ~15;
+    if ((pos >= a && pos < a + n) || n16 != n) {  // CTA-uniform
+      // the new row from global (after the dependency wait); V rows up to the next tile zeroed (P = 0 there, and
+      // 0 x NaN would not vanish in the product)
+      if (pos >= a && pos < a + n && tid < 2 * HD / 8) {
+        const int kv = tid / (HD / 8), c = tid % (HD / 8);
+        const uint4 v = reinterpret_cast<const uint4*>((kv ? p.vc : p.kc) + kvbase + static_cast<size_t>(pos) * HD)[c];
+        *reinterpret_cast<uint4*>((kv ? Vs : Ks) + (c >> 3) * box_bytes() + swz(pos - a, c)) = v;
       }
+      for (int t = tid; t < (n16 - n) * (HD / 8); t += kAttnThreads) {
+        const int r = n + t / (HD / 8), c = t % (HD / 8);
+        *reinterpret_cast<uint4*>(Vs + (c >> 3) * box_bytes() + swz(r, c)) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async();  // generic writes into a buffer that later bulk copies overwrite
+      __syncthreads();
+    }
+
+    if (kt < n) {
+      // S^T tile: keys kt + g8 (c0, c1) and kt + g8 + 8 (c2, c3), heads 2 t4 and 2 t4 + 1
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        if (g < G) {
-          float sc[kKeyBlock];
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        const int c = ks * 2 + (lane >> 4);
+        ldsm_x4(smem_u32(Ks + (c >> 3) * box_bytes() + swz(krow, c)), a0, a1, a2, a3);
+        mma_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+      }
+      const bool va = kt + g8 < n, vb = kt + g8 + 8 < n;
+      const float s0 = va ? c0 : -INFINITY, s1 = va ? c1 : -INFINITY;
+      const float s2 = vb ? c2 : -INFINITY, s3 = vb ? c3 : -INFINITY;
+      float x0 = fmaxf(s0, s2), x1 = fmaxf(s1, s3);
 #pragma unroll
-          for (int t = 0; t < kKeyBlock; ++t) {
-            float part = 0.f;
+      for (int off = 4; off <= 16; off <<= 1) {
+        x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+        x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
+      }
+      const float mn0 = fmaxf(m0, x0), mn1 = fmaxf(m1, x1);  // finite: key kt is live
+      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+      const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1), p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
+      l0 = fmaf(l0, al0, p0 + p2);
+      l1 = fmaf(l1, al1, p1 + p3);
+      m0 = mn0;
+      m1 = mn1;
+      // P^T as the B operand: lane (g8, t4) needs P[head g8][keys 2 t4 (+1)] and [keys 2 t4 + 8 (+9)]
+      const uint32_t pb0 = movm_t(pack_h2(p0, p1)), pb1 = movm_t(pack_h2(p2, p3));
 #pragma unroll
-            for (int d = 0; d < D; ++d) part = fmaf(q[g][d], kf[t][d], part);
-            sc[t] = warp_sum(part);
-          }
-          float mn = m[g];
-#pragma unroll
-          for (int t = 0; t < kKeyBlock; ++t)
-            if (kb + t < n) mn = fmaxf(mn, sc[t]);
-          const float al = exp2f(m[g] - mn);
-          float lsum = l[g] * al;
-#pragma unroll
-          for (int d = 0; d < D; ++d) o[g][d] *= al;
-#pragma unroll
-          for (int t = 0; t < kKeyBlock; ++t) {
-            const float pr = kb + t < n ? exp2f(sc[t] - mn) : 0.f;
-            lsum += pr;
-#pragma unroll
-            for (int d = 0; d < D; ++d) o[g][d] = fmaf(pr, vf[t][d], o[g][d]);
-          }
-          l[g] = lsum;
-          m[g] = mn;
-        }
+      for (int dt = 0; dt < KS; ++dt) {
+        oacc[dt][0] *= al0;
+        oacc[dt][1] *= al1;
+        oacc[dt][2] *= al0;
+        oacc[dt][3] *= al1;
+        uint32_t a0, a1, a2, a3;
+        const int c = dt * 2 + ((lane >> 3) & 1);
+        ldsm_x4_t(smem_u32(Vs + (c >> 3) * box_bytes() + swz(vrow, c)), a0, a1, a2, a3);
+        mma_16816(oacc[dt][0], oacc[dt][1], oacc[dt][2], oacc[dt][3], a0, a1, a2, a3, pb0, pb1);
       }
     }
     __syncthreads();  // every warp is done with this stage
     if (tid == 0 && i + 2 < nsub) issue(i + 2);
   }
   if (!ok) {
-    // a sub-chunk never landed (the error word is set): wait out what is still in flight (bounded), then take part
-    // in the cluster barriers with an empty partial
-    if (tid == 0)
-      for (int i = 0; i < nsub && i < 2; ++i) mbar_wait_bounded(&bars[i & 1], 0, nullptr, 100000000ull);
+    // a sub-chunk never landed: wait out the copies still in flight (bounded), contribute nothing
+    if (tid == 0) {
+      mbar_wait_bounded(&bars[i & 1], (i >> 1) & 1, nullptr, 100000000ull);
+      if (i + 1 < nsub) mbar_wait_bounded(&bars[(i + 1) & 1], ((i + 1) >> 1) & 1, nullptr, 100000000ull);
+    }
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
 #pragma unroll
-    for (int g = 0; g < GM; ++g) m[g] = -INFINITY;
+    for (int dt = 0; dt < KS; ++dt) oacc[dt][0] = oacc[dt][1] = oacc[dt][2] = oacc[dt][3] = 0.f;
+    __syncthreads();
   }
 
-  // combine the warps into this CTA's chunk partial
+  // l over the warp's 16 key rows (lanes with the same t4); then the warp's partial to shared memory (the stage
+  // buffers are free now)
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+  for (int off = 4; off <= 16; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  float (*sm_o)[kHeadsN][HD] = reinterpret_cast<float (*)[kHeadsN][HD]>(smem);
+  if (g8 == 0) {
+    sm_m[warp][2 * t4] = m0;
+    sm_m[warp][2 * t4 + 1] = m1;
+    sm_l[warp][2 * t4] = l0;
+    sm_l[warp][2 * t4 + 1] = l1;
+  }
 #pragma unroll
-      for (int d = 0; d < D; ++d) sm_o[warp][g][lane * D + d] = o[g][d];
-    }
+  for (int dt = 0; dt < KS; ++dt) {
+    sm_o[warp][2 * t4][16 * dt + g8] = oacc[dt][0];
+    sm_o[warp][2 * t4 + 1][16 * dt + g8] = oacc[dt][1];
+    sm_o[warp][2 * t4][16 * dt + g8 + 8] = oacc[dt][2];
+    sm_o[warp][2 * t4 + 1][16 * dt + g8 + 8] = oacc[dt][3];
   }
   __syncthreads();
+  // combine the warps into this CTA's chunk partial
   for (int t = tid; t < G * HD; t += kAttnThreads) {
     const int g = t / HD, d = t % HD;
     float M = -INFINITY;
@@ -225,37 +280,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     if (d == 0) { part_m[g] = M; part_l[g] = Ls; }
     part_o[g][d] = Os;
   }
-  // the chunks meet in distributed shared memory: CTA s merges outputs [s per, (s+1) per) of the G x HD
+  // the chunks meet in distributed shared memory: CTA s merges outputs [s per, (s+1) per) of the G x HD; CL adjacent
+  // lanes take one output, lane r reading chunk r's partial, so every remote load of a pass is in flight at once
   cluster_sync_all();
   const int total = G * HD, per = (total + CL - 1) / CL;
-  for (int t = s * per + tid; t < min(total, (s + 1) * per); t += kAttnThreads) {
-    const int g = t / HD, d = t % HD;
-    float M = -INFINITY;
-    for (int r = 0; r < CL; ++r) M = fmaxf(M, ld_dsmem(dsmem_addr(&part_m[g], r)));
-    float Ls = 0.f, Os = 0.f;
-    for (int r = 0; r < CL; ++r) {
-      const float mr = ld_dsmem(dsmem_addr(&part_m[g], r));
-      if (mr == -INFINITY) continue;
-      const float w = exp2f(mr - M);
-      Ls = fmaf(ld_dsmem(dsmem_addr(&part_l[g], r)), w, Ls);
-      Os = fmaf(ld_dsmem(dsmem_addr(&part_o[g][d], r)), w, Os);
+  const int ro = kAttnThreads / CL;
+  const int r = tid % CL;
+  for (int base = 0; base < per; base += ro) {  // the same trip count in every thread
+    const int oi = base + tid / CL, t = s * per + oi;
+    const bool valid = oi < per && t < total;
+    const int tt = valid ? t : 0;
+    const int g = tt / HD, d = tt % HD;
+    const float mr = ld_dsmem(dsmem_addr(&part_m[g], r));
+    const float lr = ld_dsmem(dsmem_addr(&part_l[g], r));
+    const float orr = ld_dsmem(dsmem_addr(&part_o[g][d], r));
+    float M = mr;
+    for (int off = 1; off < CL; off <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w = mr == -INFINITY ? 0.f : exp2f(mr - M);
+    float Ls = lr * w, Os = orr * w;
+    for (int off = 1; off < CL; off <<= 1) {
+      Ls += __shfl_xor_sync(0xffffffffu, Ls, off);
+      Os += __shfl_xor_sync(0xffffffffu, Os, off);
     }
-    p.out[(static_cast<size_t>(b) * p.H + kvh * G + g) * HD + d] = __float2half_rn(Os / Ls);
+    if (valid && r == 0) p.out[(static_cast<size_t>(b) * p.H + kvh * G + g) * HD + d] = __float2half_rn(Os / Ls);
   }
   cluster_sync_all();  // no CTA leaves while another still reads its partial
 }
 
-template <int HD, int GM>
-int launch_attn_t(const AttnParams& p, cudaStream_t s) {
+template <int HD>
+cudaLaunchConfig_t attn_config(const AttnParams& p, cudaStream_t s, cudaLaunchAttribute* attr, int cluster) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.S, p.KVH, p.nb);
+  cfg.gridDim = dim3(cluster, p.KVH, p.nb);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = attn_smem_bytes(HD);
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeClusterDimension;
-  attr[na].val.clusterDim.x = p.S;
+  attr[na].val.clusterDim.x = cluster;
   attr[na].val.clusterDim.y = 1;
   attr[na].val.clusterDim.z = 1;
   ++na;
@@ -266,7 +327,14 @@ int launch_attn_t(const AttnParams& p, cudaStream_t s) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  AGXC_CUDA(cudaLaunchKernelEx(&cfg, attn_kernel<HD, GM>, p));
+  return cfg;
+}
+
+template <int HD>
+int launch_attn_t(const AttnParams& p, cudaStream_t s, const CUtensorMap& tk, const CUtensorMap& tv) {
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = attn_config<HD>(p, s, attr, p.S);
+  AGXC_CUDA(cudaLaunchKernelEx(&cfg, attn_kernel<HD>, p, tk, tv));
   return 0;
 }
 
@@ -280,26 +348,22 @@ int attn_allow(K kern, int optin) {
   return 0;
 }
 
-// The largest power-of-two cluster (<= 16) the device can place for this kernel.
-template <int HD, int GM>
-int max_cluster() {
-  for (int c = 16; c >= 1; c /= 2) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(c, 1, 1);
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(HD);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = c;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+// How many clusters of each power-of-two size (1 .. 16) the device keeps resident at once.
+template <int HD>
+void cluster_residency(int* active) {
+  AttnParams p;
+  p.KVH = 1;
+  for (int i = 0; i < 5; ++i) {
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = attn_config<HD>(p, nullptr, attr, 1 << i);
+    cfg.gridDim = dim3(1 << i, 1, 1);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_kernel<HD, GM>, &cfg) == cudaSuccess && n > 0) return c;
-    cudaGetLastError();
+    if (cudaOccupancyMaxActiveClusters(&n, attn_kernel<HD>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    active[i] = n;
   }
-  return 1;
 }
 
 __global__ void rmsnorm_kernel(const void* x, int x_f32, int d, const __half* g, float eps, __half* out) {
@@ -330,48 +394,53 @@ __global__ void rmsnorm_kernel(const void* x, int x_f32, int d, const __half* g,
 
 }  // namespace
 
-// The cluster size (key chunks per KV head): a power of two filling the SMs once with the (KV head, sequence)
-// clusters, no more chunks than cap / 32 keys, and no larger than the device places.
+// The cluster size (key chunks per KV head): the largest power of two whose nb x KVH clusters are all resident at
+// once (one wave), without more CTAs than SMs, and with at least 32 keys of cap per chunk.
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap) {
   const int sms = ctx ? ctx->num_sms : kNumSMs;
-  const int want = std::max(1, sms / std::max(1, nb * KVH));
+  const int clusters = std::max(1, nb * KVH);
   int S = 1;
-  while (S * 2 <= want && S * 2 <= std::max(1, cap / kMinChunk) && S * 2 <= (ctx ? ctx->max_cluster : 8)) S *= 2;
+  for (int i = 1; i < 5; ++i) {
+    const int c = 1 << i;
+    if (c * clusters > sms || c > std::max(1, cap / kMinChunk)) break;
+    if (ctx && (c > ctx->max_cluster || ctx->cluster_active[i] < clusters)) break;
+    S = c;
+  }
   return S;
 }
 
 int attn_configure(agxc_ctx* ctx) {
   const int o = ctx->max_smem_optin;
   int rc;
-  if ((rc = attn_allow(attn_kernel<128, 1>, o)) || (rc = attn_allow(attn_kernel<128, 2>, o)) ||
-      (rc = attn_allow(attn_kernel<128, 4>, o)) || (rc = attn_allow(attn_kernel<128, 8>, o)) ||
-      (rc = attn_allow(attn_kernel<64, 1>, o)) || (rc = attn_allow(attn_kernel<64, 2>, o)) ||
-      (rc = attn_allow(attn_kernel<64, 4>, o)) || (rc = attn_allow(attn_kernel<64, 8>, o)))
-    return rc;
-  ctx->max_cluster = max_cluster<128, 8>();  // the largest variant bounds every other
+  if ((rc = attn_allow(attn_kernel<128>, o)) || (rc = attn_allow(attn_kernel<64>, o))) return rc;
+  cluster_residency<128>(ctx->cluster_active);  // the larger variant bounds the smaller
+  ctx->max_cluster = 1;
+  for (int i = 0; i < 5; ++i)
+    if (ctx->cluster_active[i] > 0) ctx->max_cluster = 1 << i;
   return 0;
 }
 
 size_t attn_part_floats(int nb, int H, int S, int hd) { return static_cast<size_t>(nb) * H * S * (hd + 2); }
 
-int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s) {
+int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk,
+                     const CUtensorMap* tv) {
   if (p.H % p.KVH) return fail(AGXC_EINVAL, "attention: heads must be a multiple of kv_heads");
   const int G = p.H / p.KVH;
   if (p.hd != 64 && p.hd != 128) return fail(AGXC_EINVAL, "attention: head_dim 64 or 128");
-  if (G > 8) return fail(AGXC_EINVAL, "attention: at most 8 query heads per KV head");
+  if (G > kHeadsN) return fail(AGXC_EINVAL, "attention: at most 8 query heads per KV head");
   if (p.S < 1 || p.S > 16 || (p.S & (p.S - 1)) || p.nb < 1)
     return fail(AGXC_EINVAL, "attention: splits a power of two up to 16, and a positive batch");
   if (ctx && p.S > ctx->max_cluster) return fail(AGXC_EINVAL, "attention: splits exceed the device's cluster size");
-  if (p.hd == 128) {
-    if (G == 1) return launch_attn_t<128, 1>(p, s);
-    if (G <= 2) return launch_attn_t<128, 2>(p, s);
-    if (G <= 4) return launch_attn_t<128, 4>(p, s);
-    return launch_attn_t<128, 8>(p, s);
+  CUtensorMap mk, mv;
+  if (!tk || !tv) {
+    const int64_t Z = static_cast<int64_t>(p.nb) * p.KVH;
+    if (int rc = encode_kv_map(&mk, p.kc, p.hd, p.cap, Z)) return rc;
+    if (int rc = encode_kv_map(&mv, p.vc, p.hd, p.cap, Z)) return rc;
+    tk = &mk;
+    tv = &mv;
   }
-  if (G == 1) return launch_attn_t<64, 1>(p, s);
-  if (G <= 2) return launch_attn_t<64, 2>(p, s);
-  if (G <= 4) return launch_attn_t<64, 4>(p, s);
-  return launch_attn_t<64, 8>(p, s);
+  if (p.hd == 128) return launch_attn_t<128>(p, s, *tk, *tv);
+  return launch_attn_t<64>(p, s, *tk, *tv);
 }
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out,

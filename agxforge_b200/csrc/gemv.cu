@@ -74,6 +74,19 @@ int make_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, i
 
 }  // namespace
 
+int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z) {
+  if (int rc = encode_fn()) return rc;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(Z)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(hd) * 2 * cap};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kAttnKeys), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AGXC_ECUDA, "cuTensorMapEncodeTiled (KV) failed (" + std::to_string(r) + ")");
+  return 0;
+}
+
 // Every GEMV instantiation may use up to the device's opt-in shared memory (set once per device, outside any
 // stream capture).
 int qmv_configure(const agxc_ctx* ctx) {

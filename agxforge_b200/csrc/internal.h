@@ -16,6 +16,7 @@ struct agxc_ctx {
   int num_sms = 148;
   int max_smem_optin = 0;
   int max_cluster = 8;           // the largest attention cluster the device places
+  int cluster_active[5] = {0, 0, 0, 0, 0};  // attention clusters of 1, 2, 4, 8, 16 CTAs resident at once
 };
 
 // A pack in the B200 tile layout: tiles[rt][g] of 16 rows x 64 k (512 B at 4 bits, 1,024 B at 8 bits; lane l of a
@@ -115,10 +116,16 @@ struct AttnParams {
   unsigned* counters = nullptr;   // unused
   unsigned* err = nullptr;
   int pdl = 0;
+  int z0 = 0;                     // the first (sequence, KV head) row of kc/vc in the tensor maps' third dimension
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
+// A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
+constexpr int kAttnKeys = 128;
+int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);
 size_t attn_part_floats(int nb, int H, int S, int hd);
-int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
+// tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
+int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,
+                     const CUtensorMap* tv = nullptr);
 int attn_configure(agxc_ctx* ctx);
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);
