@@ -20,6 +20,7 @@ EPI_F32, EPI_RES1, EPI_RES2, EPI_SWIGLU = 0, 1, 2, 3
 ROLE_QKV, ROLE_WO, ROLE_GATE, ROLE_UP, ROLE_DOWN, ROLE_HEAD = range(6)
 VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
 OPT_PDL = 0
+OPT_TRACE = 1
 
 
 class PackDesc(C.Structure):
@@ -82,6 +83,7 @@ SIGNATURES = {
     "agxc_model_profile": (_I, [_P, _I, _P, _P]),
     "agxc_model_set_option": (_I, [_P, _I, _I]),
     "agxc_model_plan_info": (_I, [_P, C.c_char_p, C.c_size_t]),
+    "agxc_model_trace_read": (_I, [_P, C.POINTER(C.c_uint64), _I, C.POINTER(C.c_int32)]),
     "agxc_model_kernel_count": (_I, [_P, C.POINTER(C.c_int32)]),
 }
 

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
     }
   };
   if (tid == 0) {
+    trace_mark(p.trace, 0);
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
@@ -133,8 +134,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   }
   if (p.pdl) {
     pdl_wait();
-    pdl_launch_dependents();
+    if (p.pdl == 1) pdl_launch_dependents();
   }
+  if (tid == 0) trace_mark(p.trace, 1);
 
   // Q^T fragments (B operand, N = heads): lane (g8, t4) holds Q[head g8][16 ks + 2 t4 + {0, 1, 8, 9}]
   uint32_t qb[KS][2];
@@ -242,6 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
     __syncthreads();
   }
 
+  if (p.pdl == 2) pdl_launch_dependents();
   // l over the warp's 16 key rows (lanes with the same t4); then the warp's partial to shared memory (the stage
   // buffers are free now)
 #pragma unroll
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
     if (valid && r == 0) p.out[(static_cast<size_t>(b) * p.H + kvh * G + g) * HD + d] = __float2half_rn(Os / Ls);
   }
   cluster_sync_all();  // no CTA leaves while another still reads its partial
+  if (tid == 0) trace_mark(p.trace, 2);
 }
 
 template <int HD>

@@ -68,6 +68,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// The launch trace (optional): per launch kTraceSlots {min, max} pairs over its CTAs of %globaltimer at CTA entry
+// (slot 0), after the dependency wait (slot 1), at CTA exit (slot 2), and for the GEMV after its activation rows are
+// staged (slot 3), after its last unit's epilogue (slot 4) and when its first weight chunk has landed (slot 5).
+// `t` NULL = not traced.
+constexpr int kTraceSlots = 6;
+__device__ __forceinline__ void trace_mark(unsigned long long* t, int slot) {
+  if (!t) return;
+  const unsigned long long v = globaltimer_ns();
+  atomicMin(t + 2 * slot, v);
+  atomicMax(t + 2 * slot + 1, v);
+}
+
 // A bounded wait on an mbarrier phase: gives up after `limit_ns` of the global timer, sets kErrMbarTimeout in the
 // error word and returns false. Every wait in this library is bounded; none spins forever.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, unsigned* err,

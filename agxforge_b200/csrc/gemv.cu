@@ -39,7 +39,7 @@ size_t smem_total(int bits, int nbt, int RW, int CG, int GC, int stages) {
   off += (static_cast<size_t>(nbt) * (GC * 64 + 8) * 2 + 127) / 128 * 128;
   off += static_cast<size_t>(GC) * 8 * 4;
   off += static_cast<size_t>(kConsumerWarps) * 16 * nbt * 4;
-  off += 2 * static_cast<size_t>(RW) * 16 * nbt * 4;
+  off += 3 * static_cast<size_t>(RW) * 16 * nbt * 4;
   return off + 1024;
 }
 

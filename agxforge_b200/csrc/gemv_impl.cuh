@@ -43,7 +43,7 @@ constexpr int kMaxStages = 8;
 constexpr float k2p24 = 16777216.0f;
 
 struct Smem {
-  int full, empty, dead, ring, stage_bytes, wbytes, xs, xstride, xsum, red, uv, ev, misc, total;
+  int full, empty, dead, ring, stage_bytes, wbytes, xs, xstride, xsum, red, uv, ev, resv, misc, total;
 };
 
 __host__ __device__ inline Smem smem_layout(int bits, int nbt, int RW, int CG, int GC, int stages) {
@@ -61,7 +61,8 @@ __host__ __device__ inline Smem smem_layout(int bits, int nbt, int RW, int CG, i
   L.red = L.xsum + GC * 8 * 4;
   L.uv = L.red + kConsumerWarps * 16 * nbt * 4;
   L.ev = L.uv + RW * 16 * nbt * 4;
-  L.misc = L.ev + RW * 16 * nbt * 4;
+  L.resv = L.ev + RW * 16 * nbt * 4;  // the first unit's residual rows, prefetched before the dependency wait
+  L.misc = L.resv + RW * 16 * nbt * 4;
   L.total = L.misc + 1024;
   return L;
 }
@@ -167,7 +168,9 @@ __device__ __forceinline__ void group_step(uint32_t aw, uint32_t asb, uint32_t a
 // ------------------------------------------------------------------------------------------------ epilogues
 // vals: [rows][NBT] fp32 (column = activation row b) for the block of `rows` physical rows starting at `row0`.
 template <int EPI, int NBT>
-__device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc) {
+// resv: the residual of these rows prefetched ([rows][NBT] fp32), or NULL to read it here
+__device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc,
+                         const float* resv = nullptr) {
   const int tid = threadIdx.x;
   const int nb = p.nb;
   if (EPI == EPI_F32) {
@@ -180,14 +183,14 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
     for (int t = tid; t < rows * NBT; t += kConsumers) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
-      const float x = __half2float(p.res16[static_cast<size_t>(b) * p.res_ld + row0 + r]);
+      const float x = resv ? resv[r * NBT + b] : __half2float(p.res16[static_cast<size_t>(b) * p.res_ld + row0 + r]);
       p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * NBT + b] + x;
     }
   } else if (EPI == EPI_RES2) {
     for (int t = tid; t < rows * NBT; t += kConsumers) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
-      const float h = p.res32[static_cast<size_t>(b) * p.res_ld + row0 + r];
+      const float h = resv ? resv[r * NBT + b] : p.res32[static_cast<size_t>(b) * p.res_ld + row0 + r];
       p.out_f16[static_cast<size_t>(b) * p.out_ld + row0 + r] = __float2half_rn(vals[r * NBT + b] + h);
     }
   } else if (EPI == EPI_SWIGLU) {
@@ -333,6 +336,26 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 8 consecutive elements of activation row b from column `col` (fp16 or fp32 rows of p.x), as fp32
+__device__ __forceinline__ void load8(const QmvParams& p, int b, int col, float* v) {
+  if (p.x_f32) {
+    const float4* src =
+        reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + static_cast<size_t>(b) * p.x_ld + col);
+    const float4 a = src[0], c = src[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld + col);
+    __half2 h[4];
+    memcpy(h, &u, 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+
 template <int BITS, int NBT, int RW, int EPI>
 __global__ void __launch_bounds__(kThreads, 2)
     qmv_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ CUtensorMap tmw,
@@ -362,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int rb0 = blockIdx.x / SC, rb_step = gridDim.x / SC;  // unit i covers row block rb0 + i rb_step
 
   if (tid == 0) {
+    trace_mark(p.trace, 0);
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
@@ -398,113 +422,118 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---------------- consumers
+  const int nb = p.nb;
+  const int n8 = GC * 8;  // 8-element vectors of this CTA's K range, per activation row
+  // The staging below gives vector k of every row to thread k % 512, so when 512 is a multiple of n8 each thread
+  // owns one vector index: its norm gain (a weight) is loaded before the dependency wait.
+  const bool fixed_k = kConsumers % n8 == 0;
+  uint4 gpre = make_uint4(0u, 0u, 0u, 0u);
+  if (p.norm_gain && fixed_k && tid < n8) gpre = reinterpret_cast<const uint4*>(p.norm_gain + k0)[tid];
+  // The residual rows of the first unit: written by a kernel at least two launches back (the upstream kernel only
+  // passed its own dependency wait on it), so they are read now, from L2, before this kernel's wait.
+  float* resv = reinterpret_cast<float*>(smem + L.resv);
+  constexpr bool kRes = EPI == EPI_RES1 || EPI == EPI_RES2;
+  if (kRes && my_units > 0) {
+    const int row0 = rb0 * RW * 16;
+    for (int t = tid; t < RW * 16 * NBT; t += kConsumers) {
+      const int r = t / NBT, b = t % NBT;
+      float v = 0.f;
+      if (b < nb) {
+        const size_t at = static_cast<size_t>(b) * p.res_ld + row0 + r;
+        v = EPI == EPI_RES1 ? __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p.res16) + at)))
+                            : __ldcg(p.res32 + at);
+      }
+      resv[t] = v;
+    }
+  }
   if (p.pdl) {
     pdl_wait();
-    pdl_launch_dependents();
+    if (p.pdl == 1) pdl_launch_dependents();
   }
-  const int nb = p.nb;
-  // stage the activation rows of this CTA's K range (RMSNorm fused when a gain is given)
-  for (int b = 0; b < nb; ++b) {
-    float r = 1.0f;
-    if (p.norm_gain) {
-      float ss = 0.f;
-      if (p.x_f32) {
-        const float4* xr =
-            reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + static_cast<size_t>(b) * p.x_ld);
-        for (int k = tid; k < p.K / 4; k += kConsumers) {
-          const float4 v = xr[k];
-          ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-        }
-      } else {
-        const uint4* xr =
-            reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld);
+  if (tid == 0) trace_mark(p.trace, 1);
+  // RMSNorm: each row's sum of squares over the whole row (all p.K columns), every row's loads independent
+  if (p.norm_gain) {
+    float ssb[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      ssb[b] = 0.f;
+      if (b < nb) {
         for (int k = tid; k < p.K / 8; k += kConsumers) {
-          const uint4 u = xr[k];
-          __half2 h[4];
-          memcpy(h, &u, 16);
+          float v[8];
+          load8(p, b, k * 8, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ssb[b] = fmaf(v[j], v[j], ssb[b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const float t = warp_sum(ssb[b]);
+      if (lane == 0 && b < nb) red[warp * 8 + b] = t;
+    }
+    consumer_sync();
+  }
+  // stage the rows as fp16 (normalised and scaled by the gain when given) and the per-group sums of the staged
+  // values; the 8 vectors of a 64-group sit in 8 adjacent lanes. Every thread runs the same number of steps.
+  const int steps = (n8 + kConsumers - 1) / kConsumers;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    if (b < nb) {
+      float r = 1.0f;
+      if (p.norm_gain) {
+        float tot = 0.f;
+        for (int w = 0; w < kConsumerWarps; ++w) tot += red[w * 8 + b];
+        r = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
+      }
+      __half* dst = xs16 + b * L.xstride;
+      for (int st = 0; st < steps; ++st) {
+        const int k = tid + st * kConsumers;
+        const bool live = k < n8;
+        float v[8];
+        if (live) {
+          load8(p, b, k0 + k * 8, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = 0.f;
+        }
+        if (p.norm_gain && live) {
+          const uint4 gu = fixed_k ? gpre : reinterpret_cast<const uint4*>(p.norm_gain + k0)[k];
+          __half2 gh[4];
+          memcpy(gh, &gu, 16);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+            const float2 g = __half22float2(gh[j]);
+            v[2 * j] = (v[2 * j] * r) * g.x;
+            v[2 * j + 1] = (v[2 * j + 1] * r) * g.y;
           }
         }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      consumer_sync();
-      if (tid == 0) {
-        float tot = 0.f;
-        for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
-        red[64] = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
-      }
-      consumer_sync();
-      r = red[64];
-      consumer_sync();
-    }
-    __half* dst = xs16 + b * L.xstride;
-    const int n8 = GC * 8;  // 8 elements per step
-    for (int k = tid; k < n8; k += kConsumers) {
-      float v[8];
-      if (p.x_f32) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
-                                                            static_cast<size_t>(b) * p.x_ld + k0) + 2 * k;
-        const float4 a = src[0], c = src[1];
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
-      } else {
-        const uint4 u = reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) +
-                                                       static_cast<size_t>(b) * p.x_ld + k0)[k];
-        __half2 h[4];
-        memcpy(h, &u, 16);
+        __half2 oh[4];
+        float sum = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(h[j]);
-          v[2 * j] = f.x; v[2 * j + 1] = f.y;
+          oh[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+          const float2 f = __half22float2(oh[j]);
+          sum += f.x + f.y;
         }
-      }
-      if (p.norm_gain) {
-        const uint4 gu = reinterpret_cast<const uint4*>(p.norm_gain + k0)[k];
-        __half2 gh[4];
-        memcpy(gh, &gu, 16);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 g = __half22float2(gh[j]);
-          v[2 * j] = (v[2 * j] * r) * g.x;
-          v[2 * j + 1] = (v[2 * j + 1] * r) * g.y;
+        if (live) {
+          uint4 o;
+          memcpy(&o, oh, 16);
+          reinterpret_cast<uint4*>(dst)[k] = o;
         }
-      }
-      __half2 oh[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) oh[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-      uint4 o;
-      memcpy(&o, oh, 16);
-      reinterpret_cast<uint4*>(dst)[k] = o;
-    }
-  }
-  consumer_sync();
-  // per-group sums of the staged rows: 8 threads per (group, row), 8 elements each, combined by shuffles
-  for (int t = tid; t < GC * 64; t += kConsumers) {
-    const int g = t / 64, b = (t / 8) % 8, part = t % 8;
-    float s = 0.f;
-    if (b < nb) {
-      const uint4 u = reinterpret_cast<const uint4*>(xs16 + b * L.xstride + g * 64)[part];
-      __half2 h[4];
-      memcpy(h, &u, 16);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(h[j]);
-        s += f.x + f.y;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if (live && (k & 7) == 0) xsum[(k >> 3) * 8 + b] = sum;
       }
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    if (part == 0) xsum[g * 8 + b] = s;
   }
   if (EPI == EPI_ARGMAX && tid < 8) {
     misc[2 * tid] = -INFINITY;
     misc[2 * tid + 1] = __int_as_float(0x7fffffff);
   }
   consumer_sync();
+  if (p.pdl == 2) pdl_launch_dependents();  // the dependent kernel's weight prefetch starts once x is staged
+  if (tid == 0) trace_mark(p.trace, 3);
 
   const int rr = warp % RW, kw = warp / RW;
   constexpr int KW = kConsumerWarps / RW;
@@ -528,6 +557,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         *dead = 1;
         waited_ok = false;
       }
+      if (i == 0 && c == 0 && tid == 0) trace_mark(p.trace, 5);
       const uint32_t st = ring0 + slot * L.stage_bytes;
       uint32_t aw = st + lane_w + kw * TB;
       uint32_t asb = st + lane_sb + kw * 64;
@@ -567,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     consumer_sync();
     const int row0 = rb * RW * 16;
     if (SC == 1) {
-      epilogue<EPI, NBT>(p, row0, RW * 16, uv, misc);
+      epilogue<EPI, NBT>(p, row0, RW * 16, uv, misc, kRes && i == 0 ? resv : nullptr);
     } else {
       // split K: this unit's partial rows to scratch; the last of the SC units of these rows sums them in order
       for (int t = tid; t < RW * 16 * NBT; t += kConsumers) {
@@ -592,13 +622,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           ev[t] = s;
         }
         consumer_sync();
-        epilogue<EPI, NBT>(p, row0, RW * 16, ev, misc);
+        epilogue<EPI, NBT>(p, row0, RW * 16, ev, misc, kRes && i == 0 ? resv : nullptr);
       }
       consumer_sync();
     }
   }
 
   if (consumer_sync_or(!waited_ok)) return;  // a stage never landed: the error word is set; leave uniformly
+  if (tid == 0) trace_mark(p.trace, 4);
 
   if (EPI == EPI_ARGMAX) {
     if (tid < 8) {
@@ -618,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       argmax_finish(p, misc);
     }
   }
+  if (tid == 0) trace_mark(p.trace, 2);
 }
 
 template <int BITS, int NBT, int RW, int EPI>

@@ -86,6 +86,7 @@ struct QmvParams {
   unsigned* counters = nullptr;
   unsigned* err = nullptr;
   int pdl = 0;
+  unsigned long long* trace = nullptr;  // this launch's six trace words, or NULL
 };
 
 struct QmvPlan {
@@ -117,6 +118,7 @@ struct AttnParams {
   unsigned* err = nullptr;
   int pdl = 0;
   int z0 = 0;                     // the first (sequence, KV head) row of kc/vc in the tensor maps' third dimension
+  unsigned long long* trace = nullptr;  // this launch's six trace words, or NULL
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.

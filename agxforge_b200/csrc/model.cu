@@ -58,7 +58,9 @@ struct agxc_model {
   // plans
   agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
   int attn_S = 1;
-  int pdl = 1;
+  int pdl = 2;
+  unsigned long long* trace = nullptr;  // [launches][12] when tracing (AGXC_OPT_TRACE)
+  int trace_n = 0;
   // graph
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -105,6 +107,16 @@ void pack_init(agxc_pack& p, agxc_model* m, int n, int k) {
 size_t pack_tile_bytes(int n, int k, int bits) { return static_cast<size_t>(n) * k * bits / 8; }
 size_t pack_sb_bytes(int n, int k) { return static_cast<size_t>(n / 16) * (k / 64) * 64; }
 
+// This launch's trace words (the launch index is m->launches), or NULL when not tracing.
+unsigned long long* trace_slot(agxc_model* m) {
+  return m->trace && m->launches < m->trace_n ? m->trace + 2 * kTraceSlots * m->launches : nullptr;
+}
+
+__global__ void trace_reset_kernel(unsigned long long* t, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) t[i] = (i & 1) ? 0ull : ~0ull;
+}
+
 // When `ev` is given, an event is recorded before and after every launch (kind order: qkv, attn, wo, ffn, down per
 // layer, then head): ev holds 2 * launches events.
 int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
@@ -122,7 +134,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     p.H = H; p.KVH = KVH; p.hd = hd; p.cap = D.cap; p.cos_t = m->cos_t; p.sin_t = m->sin_t; p.q0 = m->q0;
     p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
     p.q16 = m->q16; p.kcache = m->kcache + l * layer_kv; p.vcache = m->vcache + l * layer_kv;
-    p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev; p.pdl = m->pdl;
+    p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev; p.pdl = m->pdl; p.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_qmv_epi(m->ctx, p, m->p_qkv, EPI_QKV, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -131,7 +143,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     AttnParams a;
     a.nb = B; a.H = H; a.KVH = KVH; a.hd = hd; a.cap = D.cap; a.S = m->attn_S; a.q0 = m->q0; a.q16 = m->q16;
     a.kc = m->kcache + l * layer_kv; a.vc = m->vcache + l * layer_kv; a.out = m->attn; a.part = m->apart;
-    a.counters = m->counters + 4096; a.err = m->ctx->err_dev; a.pdl = m->pdl;
+    a.counters = m->counters + 4096; a.err = m->ctx->err_dev; a.pdl = m->pdl; a.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_attention(m->ctx, a, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -140,7 +152,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     QmvParams q;
     q.w = m->wo[l].tiles; q.sb = m->wo[l].sb; q.N = d; q.K = m->attn_dim; q.bits = D.bits; q.sdt = D.scale_dtype;
     q.nb = B; q.x = m->attn; q.x_ld = m->attn_dim; q.out_f32 = m->h; q.out_ld = d; q.res16 = m->x16; q.res_ld = d;
-    q.part = m->part; q.counters = m->counters + 8192; q.err = m->ctx->err_dev; q.pdl = m->pdl;
+    q.part = m->part; q.counters = m->counters + 8192; q.err = m->ctx->err_dev; q.pdl = m->pdl; q.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_qmv_epi(m->ctx, q, m->p_wo, EPI_RES1, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -150,7 +162,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     g.w = m->gu[l].tiles; g.sb = m->gu[l].sb; g.N = 2 * F; g.K = d; g.bits = D.bits; g.sdt = D.scale_dtype;
     g.nb = B; g.x = m->h; g.x_f32 = 1; g.x_ld = d; g.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d + d;
     g.eps = D.eps; g.out_f16 = m->act; g.out_ld = F; g.part = m->part; g.counters = m->counters + 12288;
-    g.err = m->ctx->err_dev; g.pdl = m->pdl;
+    g.err = m->ctx->err_dev; g.pdl = m->pdl; g.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_qmv_epi(m->ctx, g, m->p_gu, EPI_SWIGLU, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -159,7 +171,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     QmvParams w;
     w.w = m->down[l].tiles; w.sb = m->down[l].sb; w.N = d; w.K = F; w.bits = D.bits; w.sdt = D.scale_dtype;
     w.nb = B; w.x = m->act; w.x_ld = F; w.out_f16 = m->x16; w.out_ld = d; w.res32 = m->h; w.res_ld = d;
-    w.part = m->part; w.counters = m->counters + 16384; w.err = m->ctx->err_dev; w.pdl = m->pdl;
+    w.part = m->part; w.counters = m->counters + 16384; w.err = m->ctx->err_dev; w.pdl = m->pdl; w.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_qmv_epi(m->ctx, w, m->p_down, EPI_RES2, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -172,7 +184,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
   hp.out_f32 = D.keep_logits ? m->logits : nullptr; hp.V = D.vocab; hp.embed = m->embed; hp.x_next = m->x16;
   hp.d = d; hp.q0_rw = m->q0; hp.log = m->log; hp.tok_out = m->tok; hp.force_next = m->force_next;
   hp.cap = D.cap; hp.pairs = m->pairs;
-  hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev; hp.pdl = m->pdl;
+  hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev; hp.pdl = m->pdl; hp.trace = trace_slot(m);
   if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
   if ((rc = launch_qmv_epi(m->ctx, hp, m->p_head, EPI_ARGMAX, s))) return rc;
   if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
@@ -580,6 +592,7 @@ void model_free(agxc_model* m) {
   if (m->ev1) cudaEventDestroy(m->ev1);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_force) cudaFreeHost(m->h_force);
+  if (m->trace) cudaFree(m->trace);
   for (void* p : m->allocs) cudaFree(p);
   delete m;
 }
@@ -685,10 +698,45 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
   return 0;
 }
 
+int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n) {
+  if (!m || !out || !n) return agxc::fail(AGXC_EINVAL, "trace_read: null argument");
+  if (!m->trace) return agxc::fail(AGXC_EINVAL, "trace_read: tracing is off (AGXC_OPT_TRACE)");
+  const int k = std::min(capacity, m->trace_n);
+  AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  const int w = 2 * agxc::kTraceSlots;
+  AGXC_CUDA(cudaMemcpy(out, m->trace, static_cast<size_t>(k) * w * 8, cudaMemcpyDeviceToHost));
+  agxc::trace_reset_kernel<<<(w * m->trace_n + 255) / 256, 256, 0, m->ctx->stream>>>(m->trace, w * m->trace_n);
+  AGXC_CUDA(cudaGetLastError());
+  *n = k;
+  return 0;
+}
+
 int agxc_model_set_option(agxc_model* m, int option, int value) {
   if (!m) return agxc::fail(AGXC_EINVAL, "set_option: null model");
-  if (option != AGXC_OPT_PDL) return agxc::fail(AGXC_EINVAL, "set_option: unknown option");
-  m->pdl = value ? 1 : 0;
+  if (option == AGXC_OPT_PDL) {
+    if (value < 0 || value > 2) return agxc::fail(AGXC_EINVAL, "set_option: pdl 0, 1 or 2");
+    m->pdl = value;
+  } else if (option == AGXC_OPT_TRACE) {
+    if (value && !m->trace) {
+      const int n = 2 * agxc::kTraceSlots * (5 * m->d.n_layers + 1);
+      void* t = nullptr;
+      if (cudaMalloc(&t, static_cast<size_t>(n) * 8) != cudaSuccess) {
+        cudaGetLastError();
+        return agxc::fail(AGXC_ENOMEM, "set_option: trace buffer");
+      }
+      m->trace = static_cast<unsigned long long*>(t);
+      m->trace_n = n / (2 * agxc::kTraceSlots);
+      agxc::trace_reset_kernel<<<(n + 255) / 256, 256, 0, m->ctx->stream>>>(m->trace, n);
+      AGXC_CUDA(cudaGetLastError());
+    } else if (!value && m->trace) {
+      AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+      cudaFree(m->trace);
+      m->trace = nullptr;
+      m->trace_n = 0;
+    }
+  } else {
+    return agxc::fail(AGXC_EINVAL, "set_option: unknown option");
+  }
   if (m->exec) {
     cudaGraphExecDestroy(m->exec);
     m->exec = nullptr;

@@ -128,11 +128,36 @@ class DecodeModel:
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
     def set_option(self, option, value):
-        """Model options: "pdl" (programmatic dependent launch between the step's kernels, default on)."""
-        opts = {"pdl": N.OPT_PDL}
+        """Model options: "pdl" (programmatic dependent launch between the step's kernels: 0 off, 1 successor let in
+        after the dependency wait, 2 (default) after the inputs are staged); "trace"
+        (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace())."""
+        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")
+
+    def trace(self):
+        """The launch trace since tracing started or the last call, then reset: one dict per launch of the step (in
+        step order) with its kind and the first / last CTA entry, dependency-wait and exit times in ns, relative to
+        the step's first entry."""
+        cap = 5 * self.shape.LAYERS + 1
+        W = 12
+        buf = (C.c_uint64 * (W * cap))()
+        n = C.c_int32()
+        N.check(N.lib().agxc_model_trace_read(self._h, buf, cap, C.byref(n)), "trace_read")
+        kinds = ["qkv", "attn", "wo", "ffn", "down"] * self.shape.LAYERS + ["head"]
+        t0 = min(buf[W * i] for i in range(n.value))
+        out = []
+        for i in range(n.value):
+            w = [buf[W * i + j] for j in range(W)]
+            rec = dict(kind=kinds[i], entry=(w[0] - t0, w[1] - t0), wait=(w[2] - t0, w[3] - t0),
+                       exit=(w[4] - t0, w[5] - t0))
+            if w[7]:  # GEMV phases
+                rec["staged"] = (w[6] - t0, w[7] - t0)
+                rec["looped"] = (w[8] - t0, w[9] - t0)
+                rec["landed"] = (w[10] - t0, w[11] - t0)
+            out.append(rec)
+        return out
 
     def plan_info(self):
         """The launch plan of every kernel of the step (dict)."""

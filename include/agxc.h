@@ -212,9 +212,21 @@ AGXC_API int agxc_model_logits_dev(agxc_model* m, const float** out);
 AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/, int32_t* kind_launches /*[6]*/);
 
 /* Model options (each re-captures the step's graph on the next decode). */
-#define AGXC_OPT_PDL 0        /* 1 (default): launch each kernel with programmatic dependent launch, so it streams its
-                                 weights while its predecessor finishes; 0: plain stream order */
+#define AGXC_OPT_PDL 0        /* programmatic dependent launch between the step's kernels, so each streams its weights
+                                 while its predecessor finishes: 1 a kernel lets its successor start right after its
+                                 own dependency wait; 2 (default) only after it staged its inputs (GEMV) or read its
+                                 keys (attention); 0 plain stream order */
+#define AGXC_OPT_TRACE 1      /* 1: every launch of the step records, over its CTAs, the first and last %globaltimer
+                                 (ns) at CTA entry, after the dependency wait, and at CTA exit (read with
+                                 agxc_model_trace_read); 0 (default): off */
 AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
+
+/* The launch trace accumulated since tracing started or the last read (min and max over all steps in between), then
+ * reset: out[launch][12] = {first, last} CTA times in ns of the device's global timer at entry, after the dependency
+ * wait, at exit, and (GEMV launches; all-ones and 0 elsewhere) after staging the activation rows, after the last
+ * unit's epilogue, and when the first weight chunk had landed. Launches in step order (per layer qkv, attn, wo, ffn,
+ * down; then head); *n = launches. */
+AGXC_API int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n);
 
 /* The model's launch plans as a JSON object (per kernel: row tiles per unit, K splits, groups per unit and chunk,
  * stages, grid, shared memory; attention: key chunks per KV head). Writes at most `len` bytes including the NUL. */

@@ -130,3 +130,46 @@ def test_execute_report_keys(torch):
         assert key in rep
     assert len(rep["out_ids"]) == 5
     assert rep["dispatches_per_token"] == 5 * 2 + 1
+
+
+def test_launch_trace(torch):
+    """AGXC_OPT_TRACE: one step's launches in step order, each CTA entry <= its wait <= its exit, the step's kernels
+    ordered by their dependency waits (no CTA passes its wait before every CTA of the predecessor reached its exit),
+    and the
+    traced step's tokens equal to an untraced twin's."""
+    m = _build(dict(SMALL), bits=4)
+    twin = _build(dict(SMALL), bits=4)
+    for x in (m, twin):
+        x.start(0, [5, 6, 7])
+    m.set_option("trace", 1)
+    a = m.decode(3)[0]
+    tr = m.trace()
+    b = twin.decode(3)[0]
+    assert np.array_equal(a, b)
+    assert [t["kind"] for t in tr] == ["qkv", "attn", "wo", "ffn", "down"] * 2 + ["head"]
+    for t in tr:
+        assert t["entry"][0] <= t["entry"][1] and t["wait"][0] <= t["wait"][1] and t["exit"][0] <= t["exit"][1]
+        assert t["entry"][0] <= t["wait"][0] <= t["exit"][1]
+    m.decode(1)
+    one = m.trace()
+    for prev, cur in zip(one, one[1:]):
+        assert cur["wait"][0] >= prev["exit"][1]
+    m.set_option("trace", 0)
+    with pytest.raises(ValueError):
+        m.trace()
+
+
+def test_pdl_modes_agree(torch):
+    """Programmatic dependent launch only moves when a kernel may start: plain stream order (0), the successor let in
+    right after the dependency wait (1), or after the inputs are staged (2) give bit-identical tokens and logits."""
+    out = []
+    for mode in (0, 1, 2):
+        m = _build(dict(SMALL), bits=4, seed=4)
+        m.set_option("pdl", mode)
+        m.start(0, [9, 8, 7, 6])
+        toks, lg, _ = m.decode(6, want_logits=True)
+        out.append((toks, lg))
+        m.close()
+    for toks, lg in out[1:]:
+        assert np.array_equal(toks, out[0][0])
+        assert np.array_equal(lg, out[0][1])
