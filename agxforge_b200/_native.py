@@ -21,6 +21,7 @@ ROLE_QKV, ROLE_WO, ROLE_GATE, ROLE_UP, ROLE_DOWN, ROLE_HEAD = range(6)
 VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
 OPT_PDL = 0
 OPT_TRACE = 1
+OPT_PERSISTENT = 2
 
 
 class PackDesc(C.Structure):
@@ -84,6 +85,8 @@ SIGNATURES = {
     "agxc_model_set_option": (_I, [_P, _I, _I]),
     "agxc_model_plan_info": (_I, [_P, C.c_char_p, C.c_size_t]),
     "agxc_model_trace_read": (_I, [_P, C.POINTER(C.c_uint64), _I, C.POINTER(C.c_int32)]),
+    "agxc_model_trace_cta_read": (_I, [_P, C.POINTER(C.c_uint64), C.c_size_t, C.POINTER(C.c_int32),
+                                       C.POINTER(C.c_int32)]),
     "agxc_model_kernel_count": (_I, [_P, C.POINTER(C.c_int32)]),
 }
 

@@ -18,6 +18,8 @@ constexpr unsigned kTokenUnset = 0xFFFFFFFFu;
 constexpr unsigned kErrMbarTimeout = 1u << 0;
 constexpr unsigned kErrBadToken = 1u << 1;
 constexpr unsigned kErrBadPos = 1u << 2;
+constexpr unsigned kErrGridTimeout = 1u << 3;  // a grid barrier of the persistent step gave up
+constexpr unsigned kErrAbort = 1u << 4;        // a wait gave up: every other wait of the launch leaves too
 
 // ----------------------------------------------------------------------------------------------- host errors
 void set_error(const std::string& msg);

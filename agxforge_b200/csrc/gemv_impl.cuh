@@ -169,33 +169,37 @@ __device__ __forceinline__ void group_step(uint32_t aw, uint32_t asb, uint32_t a
 // vals: [rows][NBT] fp32 (column = activation row b) for the block of `rows` physical rows starting at `row0`.
 template <int EPI, int NBT>
 // resv: the residual of these rows prefetched ([rows][NBT] fp32), or NULL to read it here
+// t0 / tstride: the calling threads' index and count (default: all consumer threads); the argmax keeps its running
+// maximum in misc[0], misc[1] of the calling group (one warp, t0 = lane, when a warp finalises a unit alone).
 __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc,
-                         const float* resv = nullptr) {
-  const int tid = threadIdx.x;
+                         const float* resv = nullptr, int t0 = -1, int tstride = kConsumers) {
+  const int tid = t0 >= 0 ? t0 : static_cast<int>(threadIdx.x);
   const int nb = p.nb;
   if (EPI == EPI_F32) {
-    for (int t = tid; t < rows * NBT; t += kConsumers) {
+    for (int t = tid; t < rows * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
       p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * NBT + b];
     }
   } else if (EPI == EPI_RES1) {
-    for (int t = tid; t < rows * NBT; t += kConsumers) {
+    for (int t = tid; t < rows * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
-      const float x = resv ? resv[r * NBT + b] : __half2float(p.res16[static_cast<size_t>(b) * p.res_ld + row0 + r]);
+      const float x = resv ? resv[r * NBT + b]
+                           : __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p.res16) +
+                                                                  static_cast<size_t>(b) * p.res_ld + row0 + r)));
       p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * NBT + b] + x;
     }
   } else if (EPI == EPI_RES2) {
-    for (int t = tid; t < rows * NBT; t += kConsumers) {
+    for (int t = tid; t < rows * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
-      const float h = resv ? resv[r * NBT + b] : p.res32[static_cast<size_t>(b) * p.res_ld + row0 + r];
+      const float h = resv ? resv[r * NBT + b] : __ldcg(p.res32 + static_cast<size_t>(b) * p.res_ld + row0 + r);
       p.out_f16[static_cast<size_t>(b) * p.out_ld + row0 + r] = __float2half_rn(vals[r * NBT + b] + h);
     }
   } else if (EPI == EPI_SWIGLU) {
     // pairs of row tiles: a gate tile (rows 0..15 of the pair) and its up tile (rows 16..31); output (row0/32)*16 + r
-    for (int t = tid; t < rows / 2 * NBT; t += kConsumers) {
+    for (int t = tid; t < rows / 2 * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
       const int pr = r / 16, rr = r % 16;
@@ -207,7 +211,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
     // bias, rotate-half RoPE at the sequence's position (q and k heads), q scaled for the base-2 softmax and stored
     // fp16; k and v stored fp16 into the cache row at the position.
     const int hd = p.hd, half = hd / 2;
-    for (int t = tid; t < rows / 2 * NBT; t += kConsumers) {
+    for (int t = tid; t < rows / 2 * NBT; t += tstride) {
       const int pr = t / NBT, b = t % NBT;
       if (b >= nb) continue;
       const int tile = pr / 8, r = pr % 8;
@@ -243,7 +247,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
     }
   } else if (EPI == EPI_ARGMAX) {
     if (p.out_f32) {
-      for (int t = tid; t < rows * NBT; t += kConsumers) {
+      for (int t = tid; t < rows * NBT; t += tstride) {
         const int r = t / NBT, b = t % NBT;
         if (b >= nb) continue;
         p.out_f32[static_cast<size_t>(b) * p.V + row0 + r] = vals[r * NBT + b];
@@ -336,15 +340,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// 8 consecutive elements of activation row b from column `col` (fp16 or fp32 rows of p.x), as fp32
+// 8 consecutive elements of activation row b from column `col` (fp16 or fp32 rows of p.x), as fp32. Activations are
+// written by other CTAs (or kernels) of the step, so they are read from L2, never from a possibly stale L1 line.
 __device__ __forceinline__ void load8(const QmvParams& p, int b, int col, float* v) {
   if (p.x_f32) {
     const float4* src =
         reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + static_cast<size_t>(b) * p.x_ld + col);
-    const float4 a = src[0], c = src[1];
+    const float4 a = __ldcg(src), c = __ldcg(src + 1);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
   } else {
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld + col);
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(static_cast<const __half*>(p.x) + static_cast<size_t>(b) * p.x_ld + col));
     __half2 h[4];
     memcpy(h, &u, 16);
 #pragma unroll

@@ -121,6 +121,34 @@ struct AttnParams {
   unsigned long long* trace = nullptr;  // this launch's six trace words, or NULL
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
+
+// ---- the persistent step kernel (step.cu): a batch-1 decode step as one cooperative launch running a program of
+// phases (GEMV with an epilogue, or attention) separated by grid barriers
+enum { kPhaseGemv = 0, kPhaseAttn = 1 };
+struct alignas(16) StepPhase {
+  int kind = kPhaseGemv;
+  int q_epi = 0;                  // GEMV epilogue
+  int RW = 1, CG = 0, nchunks = 0, units = 0;  // GEMV plan: row tiles a unit, groups a chunk, chunks a unit, units
+  int S = 1;                      // attention: key chunks per KV head (one CTA each)
+  QmvParams q;
+  AttnParams a;
+  unsigned long long* cta_trace = nullptr;  // tracing: [CTA][6] stamps (barrier arrival, start, end, 3 inner points)
+};
+struct StepParams {
+  const StepPhase* phases = nullptr;
+  int nphases = 0;
+  unsigned* bar = nullptr;        // [0] barrier arrivals, [1] CTAs that left (zero between launches)
+  unsigned* err = nullptr;
+  const uint32_t* q0 = nullptr;   // the step's position (batch 1)
+  int cap = 0;
+  int kmax = 0;                   // the widest GEMV input (sizes the activation staging)
+  int ring = 2;                   // shared-memory ring stages
+};
+int step_plan_gemv(StepPhase* P, int N, int K, int bits, int epi, int grid);
+// *ok = 1 when one CTA of the step kernel fits every SM (called once per model, outside stream capture)
+int step_configure(const agxc_ctx* ctx, int bits, int hd, int kmax, int* ok, int* stages);
+int step_launch(const StepParams& sp, int bits, int hd, int grid, cudaStream_t s);
+size_t step_smem(int kmax, int stages);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
 constexpr int kAttnKeys = 128;
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);

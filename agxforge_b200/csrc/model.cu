@@ -59,7 +59,16 @@ struct agxc_model {
   agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
   int attn_S = 1;
   int pdl = 2;
+  // the persistent step kernel (batch 1): its program, grid barrier words, and whether the device runs it
+  int persistent = 0;
+  int step_ok = 0;
+  int step_kmax = 0;
+  int step_ring = 0;
+  agxc::StepPhase* step_phases = nullptr;
+  int step_nphases = 0;
+  unsigned* step_bar = nullptr;
   unsigned long long* trace = nullptr;  // [launches][12] when tracing (AGXC_OPT_TRACE)
+  unsigned long long* cta_trace = nullptr;  // persistent step, tracing: [phase][CTA][6]
   int trace_n = 0;
   // graph
   cudaGraph_t graph = nullptr;
@@ -117,84 +126,148 @@ __global__ void trace_reset_kernel(unsigned long long* t, int n) {
   if (i < n) t[i] = (i & 1) ? 0ull : ~0ull;
 }
 
-// When `ev` is given, an event is recorded before and after every launch (kind order: qkv, attn, wo, ffn, down per
-// layer, then head): ev holds 2 * launches events.
-int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+// The parameters of layer l's five launches (qkv, attention, o_proj, gate/up, down) and of the head: one place for
+// the per-kernel graph and the persistent step kernel.
+void layer_params(agxc_model* m, int l, QmvParams& p, AttnParams& a, QmvParams& q, QmvParams& g, QmvParams& w) {
   const agxc_model_desc& D = m->d;
   const int B = D.batch, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim, d = D.d_model, F = D.ffn;
   const size_t layer_kv = static_cast<size_t>(B) * KVH * D.cap * hd;
+  // D1: norm + qkv + bias + RoPE + append
+  p.w = m->qkv[l].tiles; p.sb = m->qkv[l].sb; p.N = m->qkv_rows; p.K = d; p.bits = D.bits; p.sdt = D.scale_dtype;
+  p.nb = B; p.x = m->x16; p.x_f32 = 0; p.x_ld = d; p.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d;
+  p.eps = D.eps; p.bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
+  p.H = H; p.KVH = KVH; p.hd = hd; p.cap = D.cap; p.cos_t = m->cos_t; p.sin_t = m->sin_t; p.q0 = m->q0;
+  p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  p.q16 = m->q16; p.kcache = m->kcache + l * layer_kv; p.vcache = m->vcache + l * layer_kv;
+  p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev;
+  // D2: attention
+  a.nb = B; a.H = H; a.KVH = KVH; a.hd = hd; a.cap = D.cap; a.S = m->attn_S; a.q0 = m->q0; a.q16 = m->q16;
+  a.kc = m->kcache + l * layer_kv; a.vc = m->vcache + l * layer_kv; a.out = m->attn; a.part = m->apart;
+  a.counters = m->counters + 4096; a.err = m->ctx->err_dev;
+  // D3: o_proj + residual -> h
+  q.w = m->wo[l].tiles; q.sb = m->wo[l].sb; q.N = d; q.K = m->attn_dim; q.bits = D.bits; q.sdt = D.scale_dtype;
+  q.nb = B; q.x = m->attn; q.x_ld = m->attn_dim; q.out_f32 = m->h; q.out_ld = d; q.res16 = m->x16; q.res_ld = d;
+  q.part = m->part; q.counters = m->counters + 8192; q.err = m->ctx->err_dev;
+  // D4: norm + gate/up + SiLU*mul -> act
+  g.w = m->gu[l].tiles; g.sb = m->gu[l].sb; g.N = 2 * F; g.K = d; g.bits = D.bits; g.sdt = D.scale_dtype;
+  g.nb = B; g.x = m->h; g.x_f32 = 1; g.x_ld = d; g.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d + d;
+  g.eps = D.eps; g.out_f16 = m->act; g.out_ld = F; g.part = m->part; g.counters = m->counters + 12288;
+  g.err = m->ctx->err_dev;
+  // D5: down + residual -> x16
+  w.w = m->down[l].tiles; w.sb = m->down[l].sb; w.N = d; w.K = F; w.bits = D.bits; w.sdt = D.scale_dtype;
+  w.nb = B; w.x = m->act; w.x_ld = F; w.out_f16 = m->x16; w.out_ld = d; w.res32 = m->h; w.res_ld = d;
+  w.part = m->part; w.counters = m->counters + 16384; w.err = m->ctx->err_dev;
+}
+
+void head_params(agxc_model* m, QmvParams& hp) {
+  const agxc_model_desc& D = m->d;
+  const int d = D.d_model;
+  hp.w = m->head.tiles; hp.sb = m->head.sb; hp.N = D.vocab; hp.K = d; hp.bits = D.bits; hp.sdt = D.scale_dtype;
+  hp.nb = D.batch; hp.x = m->x16; hp.x_ld = d; hp.norm_gain = m->final_gain; hp.eps = D.eps;
+  hp.out_f32 = D.keep_logits ? m->logits : nullptr; hp.V = D.vocab; hp.embed = m->embed; hp.x_next = m->x16;
+  hp.d = d; hp.q0_rw = m->q0; hp.log = m->log; hp.tok_out = m->tok; hp.force_next = m->force_next;
+  hp.cap = D.cap; hp.pairs = m->pairs;
+  hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev;
+}
+
+// The persistent step's program (batch 1): 5 phases a layer + the head, uploaded to the device once.
+int build_step_program(agxc_model* m) {
+  const agxc_model_desc& D = m->d;
+  std::vector<StepPhase> ph;
+  const int grid = m->ctx->num_sms;
+  const int S = std::max(1, grid / D.n_kv_heads);
+  for (int l = 0; l < D.n_layers; ++l) {
+    StepPhase P1, P2, P3, P4, P5;
+    layer_params(m, l, P1.q, P2.a, P3.q, P4.q, P5.q);
+    int rc;
+    if ((rc = step_plan_gemv(&P1, m->qkv_rows, D.d_model, D.bits, EPI_QKV, grid)) ||
+        (rc = step_plan_gemv(&P3, D.d_model, m->attn_dim, D.bits, EPI_RES1, grid)) ||
+        (rc = step_plan_gemv(&P4, 2 * D.ffn, D.d_model, D.bits, EPI_SWIGLU, grid)) ||
+        (rc = step_plan_gemv(&P5, D.d_model, D.ffn, D.bits, EPI_RES2, grid)))
+      return rc;
+    P2.kind = kPhaseAttn;
+    P2.S = S;
+    if (m->cta_trace) {  // per phase, per CTA stamps, in step order
+      const size_t base = ph.size(), w = static_cast<size_t>(grid) * kTraceSlots;
+      P1.cta_trace = m->cta_trace + w * base;
+      P2.cta_trace = m->cta_trace + w * (base + 1);
+      P3.cta_trace = m->cta_trace + w * (base + 2);
+      P4.cta_trace = m->cta_trace + w * (base + 3);
+      P5.cta_trace = m->cta_trace + w * (base + 4);
+    }
+    ph.push_back(P1);
+    ph.push_back(P2);
+    ph.push_back(P3);
+    ph.push_back(P4);
+    ph.push_back(P5);
+  }
+  StepPhase Ph;
+  head_params(m, Ph.q);
+  if (int rc = step_plan_gemv(&Ph, D.vocab, D.d_model, D.bits, EPI_ARGMAX, grid)) return rc;
+  if (m->cta_trace) Ph.cta_trace = m->cta_trace + static_cast<size_t>(grid) * kTraceSlots * ph.size();
+  ph.push_back(Ph);
+  AGXC_CUDA(cudaMemcpy(m->step_phases, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
+  m->step_nphases = static_cast<int>(ph.size());
+  return 0;
+}
+
+int enqueue_step_persistent(agxc_model* m, cudaStream_t s) {
+  StepParams sp;
+  sp.phases = m->step_phases;
+  sp.nphases = m->step_nphases;
+  sp.bar = m->step_bar;
+  sp.err = m->ctx->err_dev;
+  sp.q0 = m->q0;
+  sp.cap = m->d.cap;
+  sp.kmax = m->step_kmax;
+  sp.ring = m->step_ring;
+  m->launches = 1;
+  return step_launch(sp, m->d.bits, m->d.head_dim, m->ctx->num_sms, s);
+}
+
+// When `ev` is given, an event is recorded before and after every launch (kind order: qkv, attn, wo, ffn, down per
+// layer, then head): ev holds 2 * launches events.
+int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+  if (!ev && m->persistent && m->step_ok) return enqueue_step_persistent(m, s);
+  const agxc_model_desc& D = m->d;
   int rc;
   m->launches = 0;
-  for (int l = 0; l < D.n_layers; ++l) {
-    // D1: norm + qkv + bias + RoPE + append
-    QmvParams p;
-    p.w = m->qkv[l].tiles; p.sb = m->qkv[l].sb; p.N = m->qkv_rows; p.K = d; p.bits = D.bits; p.sdt = D.scale_dtype;
-    p.nb = B; p.x = m->x16; p.x_f32 = 0; p.x_ld = d; p.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d;
-    p.eps = D.eps; p.bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
-    p.H = H; p.KVH = KVH; p.hd = hd; p.cap = D.cap; p.cos_t = m->cos_t; p.sin_t = m->sin_t; p.q0 = m->q0;
-    p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
-    p.q16 = m->q16; p.kcache = m->kcache + l * layer_kv; p.vcache = m->vcache + l * layer_kv;
-    p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev; p.pdl = m->pdl; p.trace = trace_slot(m);
+  auto launch_gemv = [&](QmvParams& x, const QmvPlan& plan, int epi) -> int {
+    x.pdl = m->pdl;
+    x.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
-    if ((rc = launch_qmv_epi(m->ctx, p, m->p_qkv, EPI_QKV, s))) return rc;
+    if (int r = launch_qmv_epi(m->ctx, x, plan, epi, s)) return r;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
     ++m->launches;
-    // D2: attention
+    return 0;
+  };
+  for (int l = 0; l < D.n_layers; ++l) {
+    QmvParams p, q, g, w;
     AttnParams a;
-    a.nb = B; a.H = H; a.KVH = KVH; a.hd = hd; a.cap = D.cap; a.S = m->attn_S; a.q0 = m->q0; a.q16 = m->q16;
-    a.kc = m->kcache + l * layer_kv; a.vc = m->vcache + l * layer_kv; a.out = m->attn; a.part = m->apart;
-    a.counters = m->counters + 4096; a.err = m->ctx->err_dev; a.pdl = m->pdl; a.trace = trace_slot(m);
+    layer_params(m, l, p, a, q, g, w);
+    if ((rc = launch_gemv(p, m->p_qkv, EPI_QKV))) return rc;
+    a.pdl = m->pdl;
+    a.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if ((rc = launch_attention(m->ctx, a, s))) return rc;
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
     ++m->launches;
-    // D3: o_proj + residual -> h
-    QmvParams q;
-    q.w = m->wo[l].tiles; q.sb = m->wo[l].sb; q.N = d; q.K = m->attn_dim; q.bits = D.bits; q.sdt = D.scale_dtype;
-    q.nb = B; q.x = m->attn; q.x_ld = m->attn_dim; q.out_f32 = m->h; q.out_ld = d; q.res16 = m->x16; q.res_ld = d;
-    q.part = m->part; q.counters = m->counters + 8192; q.err = m->ctx->err_dev; q.pdl = m->pdl; q.trace = trace_slot(m);
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
-    if ((rc = launch_qmv_epi(m->ctx, q, m->p_wo, EPI_RES1, s))) return rc;
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
-    ++m->launches;
-    // D4: norm + gate/up + SiLU*mul -> act
-    QmvParams g;
-    g.w = m->gu[l].tiles; g.sb = m->gu[l].sb; g.N = 2 * F; g.K = d; g.bits = D.bits; g.sdt = D.scale_dtype;
-    g.nb = B; g.x = m->h; g.x_f32 = 1; g.x_ld = d; g.norm_gain = m->gains + static_cast<size_t>(l) * 2 * d + d;
-    g.eps = D.eps; g.out_f16 = m->act; g.out_ld = F; g.part = m->part; g.counters = m->counters + 12288;
-    g.err = m->ctx->err_dev; g.pdl = m->pdl; g.trace = trace_slot(m);
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
-    if ((rc = launch_qmv_epi(m->ctx, g, m->p_gu, EPI_SWIGLU, s))) return rc;
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
-    ++m->launches;
-    // D5: down + residual -> x16
-    QmvParams w;
-    w.w = m->down[l].tiles; w.sb = m->down[l].sb; w.N = d; w.K = F; w.bits = D.bits; w.sdt = D.scale_dtype;
-    w.nb = B; w.x = m->act; w.x_ld = F; w.out_f16 = m->x16; w.out_ld = d; w.res32 = m->h; w.res_ld = d;
-    w.part = m->part; w.counters = m->counters + 16384; w.err = m->ctx->err_dev; w.pdl = m->pdl; w.trace = trace_slot(m);
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
-    if ((rc = launch_qmv_epi(m->ctx, w, m->p_down, EPI_RES2, s))) return rc;
-    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
-    ++m->launches;
+    if ((rc = launch_gemv(q, m->p_wo, EPI_RES1)) || (rc = launch_gemv(g, m->p_gu, EPI_SWIGLU)) ||
+        (rc = launch_gemv(w, m->p_down, EPI_RES2)))
+      return rc;
   }
-  // head: final norm + lm_head + argmax + generation step
   QmvParams hp;
-  hp.w = m->head.tiles; hp.sb = m->head.sb; hp.N = D.vocab; hp.K = d; hp.bits = D.bits; hp.sdt = D.scale_dtype;
-  hp.nb = B; hp.x = m->x16; hp.x_ld = d; hp.norm_gain = m->final_gain; hp.eps = D.eps;
-  hp.out_f32 = D.keep_logits ? m->logits : nullptr; hp.V = D.vocab; hp.embed = m->embed; hp.x_next = m->x16;
-  hp.d = d; hp.q0_rw = m->q0; hp.log = m->log; hp.tok_out = m->tok; hp.force_next = m->force_next;
-  hp.cap = D.cap; hp.pairs = m->pairs;
-  hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev; hp.pdl = m->pdl; hp.trace = trace_slot(m);
-  if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
-  if ((rc = launch_qmv_epi(m->ctx, hp, m->p_head, EPI_ARGMAX, s))) return rc;
-  if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
-  ++m->launches;
-  return 0;
+  head_params(m, hp);
+  return launch_gemv(hp, m->p_head, EPI_ARGMAX);
 }
 
 int ensure_graph(agxc_model* m) {
   if (m->exec) return 0;
   cudaStream_t s = m->ctx->stream;
+  if (m->persistent && m->step_ok && !m->step_nphases) {
+    AGXC_CUDA(cudaStreamSynchronize(s));
+    if (int rc = build_step_program(m)) return rc;
+  }
   AGXC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = enqueue_step(m, s);
   cudaGraph_t g = nullptr;
@@ -301,14 +374,31 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, B, EPI_SWIGLU));
   part = std::max(part, qmv_part_floats(m->p_down, d, B, EPI_RES2));
   if ((rc = dalloc_t(m, &m->part, std::max<size_t>(part, 64)))) return bail(rc);
-  if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(m->p_head.grid) * 16))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(std::max(m->p_head.grid, ctx->num_sms)) * 16)))
+    return bail(rc);
+  // the persistent step kernel: batch 1, when its shared memory fits one CTA per SM
+  m->step_kmax = std::max({d, m->attn_dim, F});
+  if (B == 1) {
+    if ((rc = step_configure(ctx, D.bits, hd, m->step_kmax, &m->step_ok, &m->step_ring))) return bail(rc);
+    if (D.n_heads / D.n_kv_heads > 8) m->step_ok = 0;
+  }
+  if (m->step_ok) {
+    if ((rc = dalloc_t(m, &m->apart, static_cast<size_t>(ctx->num_sms) * 8 * (hd + 2)))) return bail(rc);
+    if ((rc = dalloc_t(m, &m->step_bar, 64))) return bail(rc);
+    void* ph = nullptr;
+    if (cudaMalloc(&ph, static_cast<size_t>(5 * L + 1) * sizeof(StepPhase)) != cudaSuccess)
+      return bail(fail(AGXC_ENOMEM, "model: step program"));
+    m->allocs.push_back(ph);
+    m->step_phases = static_cast<StepPhase*>(ph);
+  }
   m->counters_n = 24576;
   if (static_cast<size_t>(m->qkv_rows / hd) > 4096 || static_cast<size_t>(B * D.n_kv_heads) > 4096 ||
       static_cast<size_t>(2 * F / 32) > 4096 || static_cast<size_t>(d / 16) > 4096)
     return bail(fail(AGXC_EINVAL, "model: too many epilogue blocks for the counter regions"));
   if ((rc = dalloc_t(m, &m->counters, m->counters_n))) return bail(rc);
   cudaStream_t s = ctx->stream;
-  if (cudaMemsetAsync(m->counters, 0, m->counters_n * sizeof(unsigned), s) != cudaSuccess ||
+  if ((m->step_bar && cudaMemsetAsync(m->step_bar, 0, 64 * sizeof(unsigned), s) != cudaSuccess) ||
+      cudaMemsetAsync(m->counters, 0, m->counters_n * sizeof(unsigned), s) != cudaSuccess ||
       cudaMemsetAsync(m->kcache, 0, kv * 2, s) != cudaSuccess || cudaMemsetAsync(m->vcache, 0, kv * 2, s) != cudaSuccess ||
       cudaMemsetAsync(m->q0, 0, B * 4, s) != cudaSuccess ||
       cudaMemsetAsync(m->force_next, 0xFF, B * 4, s) != cudaSuccess ||
@@ -593,6 +683,7 @@ void model_free(agxc_model* m) {
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_force) cudaFreeHost(m->h_force);
   if (m->trace) cudaFree(m->trace);
+  if (m->cta_trace) cudaFree(m->cta_trace);
   for (void* p : m->allocs) cudaFree(p);
   delete m;
 }
@@ -693,7 +784,10 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
   std::string j = "{" + one("qkv", m->p_qkv) + ", " + one("wo", m->p_wo) + ", " + one("ffn", m->p_gu) + ", " +
                   one("down", m->p_down) + ", " + one("head", m->p_head) + ", \"attn\": {\"chunks\": " +
                   std::to_string(m->attn_S) + ", \"max_cluster\": " + std::to_string(m->ctx->max_cluster) +
-                  "}, \"pdl\": " + std::to_string(m->pdl) + "}";
+                  "}, \"pdl\": " + std::to_string(m->pdl) + ", \"persistent\": {\"on\": " +
+                  std::to_string(m->persistent && m->step_ok) + ", \"fits\": " + std::to_string(m->step_ok) +
+                  ", \"ring_stages\": " + std::to_string(m->step_ring) + ", \"grid\": " +
+                  std::to_string(m->ctx->num_sms) + "}}";
   std::snprintf(buf, len, "%s", j.c_str());
   return 0;
 }
@@ -711,11 +805,24 @@ int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n
   return 0;
 }
 
+int agxc_model_trace_cta_read(agxc_model* m, uint64_t* out, size_t capacity, int32_t* phases, int32_t* ctas) {
+  if (!m || !out || !phases || !ctas) return agxc::fail(AGXC_EINVAL, "trace_cta_read: null argument");
+  if (!m->cta_trace) return agxc::fail(AGXC_EINVAL, "trace_cta_read: no persistent-step trace (AGXC_OPT_TRACE)");
+  const size_t w = static_cast<size_t>(m->trace_n) * m->ctx->num_sms * agxc::kTraceSlots;
+  AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  AGXC_CUDA(cudaMemcpy(out, m->cta_trace, std::min(capacity, w) * 8, cudaMemcpyDeviceToHost));
+  *phases = m->trace_n;
+  *ctas = m->ctx->num_sms;
+  return 0;
+}
+
 int agxc_model_set_option(agxc_model* m, int option, int value) {
   if (!m) return agxc::fail(AGXC_EINVAL, "set_option: null model");
   if (option == AGXC_OPT_PDL) {
     if (value < 0 || value > 2) return agxc::fail(AGXC_EINVAL, "set_option: pdl 0, 1 or 2");
     m->pdl = value;
+  } else if (option == AGXC_OPT_PERSISTENT) {
+    m->persistent = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {
     if (value && !m->trace) {
       const int n = 2 * agxc::kTraceSlots * (5 * m->d.n_layers + 1);
@@ -726,6 +833,15 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
       }
       m->trace = static_cast<unsigned long long*>(t);
       m->trace_n = n / (2 * agxc::kTraceSlots);
+      if (m->step_ok) {
+        const size_t cw = static_cast<size_t>(m->trace_n) * m->ctx->num_sms * agxc::kTraceSlots;
+        if (cudaMalloc(&t, cw * 8) != cudaSuccess) {
+          cudaGetLastError();
+          return agxc::fail(AGXC_ENOMEM, "set_option: trace buffer");
+        }
+        m->cta_trace = static_cast<unsigned long long*>(t);
+        AGXC_CUDA(cudaMemset(m->cta_trace, 0, cw * 8));
+      }
       agxc::trace_reset_kernel<<<(n + 255) / 256, 256, 0, m->ctx->stream>>>(m->trace, n);
       AGXC_CUDA(cudaGetLastError());
     } else if (!value && m->trace) {
@@ -733,6 +849,8 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
       cudaFree(m->trace);
       m->trace = nullptr;
       m->trace_n = 0;
+      if (m->cta_trace) cudaFree(m->cta_trace);
+      m->cta_trace = nullptr;
     }
   } else {
     return agxc::fail(AGXC_EINVAL, "set_option: unknown option");
@@ -745,6 +863,7 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
     cudaGraphDestroy(m->graph);
     m->graph = nullptr;
   }
+  m->step_nphases = 0;  // the step program is rebuilt with the new options
   return 0;
 }
 

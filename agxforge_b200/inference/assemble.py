@@ -130,8 +130,9 @@ class DecodeModel:
     def set_option(self, option, value):
         """Model options: "pdl" (programmatic dependent launch between the step's kernels: 0 off, 1 successor let in
         after the dependency wait, 2 (default) after the inputs are staged); "trace"
-        (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace())."""
-        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE}
+        (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace());
+        "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off)."""
+        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")

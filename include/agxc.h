@@ -219,6 +219,11 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_TRACE 1      /* 1: every launch of the step records, over its CTAs, the first and last %globaltimer
                                  (ns) at CTA entry, after the dependency wait, and at CTA exit (read with
                                  agxc_model_trace_read); 0 (default): off */
+#define AGXC_OPT_PERSISTENT 2 /* 1: a batch-1 model runs each step as ONE persistent cooperative kernel (one CTA per
+                                 SM streams every weight of the step through its shared-memory ring while the phases
+                                 run between grid barriers) when the device fits it; 0 (default): one kernel per
+                                 projection and attention, chained by programmatic dependent launch (always the case
+                                 for batch > 1) */
 AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
 
 /* The launch trace accumulated since tracing started or the last read (min and max over all steps in between), then
@@ -227,6 +232,11 @@ AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
  * unit's epilogue, and when the first weight chunk had landed. Launches in step order (per layer qkv, attn, wo, ffn,
  * down; then head); *n = launches. */
 AGXC_API int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n);
+/* The persistent step's per-CTA trace of the last traced step: out[phase][CTA][6] global-timer stamps (ns) at the
+ * phase's barrier arrival, after the barrier, at the phase's end, and three inner points (GEMV: inputs staged, units
+ * done, first chunk landed; attention: queries loaded, units done, keys done), 0 = not reached. *phases, *ctas = the
+ * dimensions; at most `capacity` words are written. */
+AGXC_API int agxc_model_trace_cta_read(agxc_model* m, uint64_t* out, size_t capacity, int32_t* phases, int32_t* ctas);
 
 /* The model's launch plans as a JSON object (per kernel: row tiles per unit, K splits, groups per unit and chunk,
  * stages, grid, shared memory; attention: key chunks per KV head). Writes at most `len` bytes including the NUL. */

@@ -120,16 +120,18 @@ def test_internlm_q8_two_layers(torch):
     MC.compare(m, seqs, lg, 3)
 
 
-def test_execute_report_keys(torch):
+@pytest.mark.parametrize("persistent", [0, 1])
+def test_execute_report_keys(torch, persistent):
     from agxforge_b200.inference import execute
     m = _build(dict(SMALL), bits=4)
+    m.set_option("persistent", persistent)
     m.start(0, [1, 2, 3])
     rep = execute.decode(m, 5)
     for key in ("out_ids", "tokens_per_s", "per_token_ms", "gpu_ms_per_token", "host_ms_per_token",
                 "dispatches_per_token", "batch"):
         assert key in rep
     assert len(rep["out_ids"]) == 5
-    assert rep["dispatches_per_token"] == 5 * 2 + 1
+    assert rep["dispatches_per_token"] == (1 if persistent else 5 * 2 + 1)
 
 
 def test_launch_trace(torch):
@@ -140,6 +142,7 @@ def test_launch_trace(torch):
     m = _build(dict(SMALL), bits=4)
     twin = _build(dict(SMALL), bits=4)
     for x in (m, twin):
+        x.set_option("persistent", 0)
         x.start(0, [5, 6, 7])
     m.set_option("trace", 1)
     a = m.decode(3)[0]
@@ -173,3 +176,26 @@ def test_pdl_modes_agree(torch):
     for toks, lg in out[1:]:
         assert np.array_equal(toks, out[0][0])
         assert np.array_equal(lg, out[0][1])
+
+
+@pytest.mark.parametrize("shape,bits,layers,prompt_len", [("small", 4, 2, 20), ("small", 8, 2, 20),
+                                                          ("internlm2.5-1.8b", 4, 2, 300), ("qwen2.5-0.5b", 4, 2, 40)])
+def test_persistent_step_against_oracle_and_kernel_path(torch, shape, bits, layers, prompt_len):
+    """The batch-1 step as one persistent kernel and as one kernel per projection: both within the FP64 bound of the
+    oracle step by step, with the same argmax tokens."""
+    from agxforge_b200.inference import models
+    sh = dict(SMALL) if shape == "small" else models.get(shape).replace(LAYERS=layers)
+    vocab = sh["VOCAB"] if shape == "small" else sh.VOCAB
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, vocab, prompt_len).tolist()
+    toks = {}
+    for persistent in (1, 0):
+        m = _build(dict(sh) if shape == "small" else sh, bits=bits, cap=prompt_len + 16, seed=3)
+        m.set_option("persistent", persistent)
+        assert m.plan_info()["persistent"]["on"] == persistent
+        seqs, lg, tk = MC.run_forced(m, [prompt], 6, seed=5)
+        rep = MC.compare(m, seqs, lg, 6)
+        assert rep[0]["argmax_agree"] >= 5
+        toks[persistent] = tk
+        m.close()
+    assert np.array_equal(toks[0], toks[1])
