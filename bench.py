@@ -3,10 +3,14 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config internlm-q4-1792]
 
 Default workload (BASELINE config 3 at its headline point): InternLM2.5-1.8B-shaped decoder, random-init (seed 2,
-N(0, 0.02) weights, 4-bit affine group 64 with fp16 scale/bias), batch 1, a history of 1,792 uniform-random token
-ids, then K greedy decode steps at positions 1,792 .. 1,792+K-1 (W warm-up steps just before them). A step is one
-token: one CUDA-graph replay of the 121 kernels. Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB of KV
-per token against a 126 MB L2), so no flush is needed between steps.
+N(0, 0.02) weights, 4-bit affine group 64 with fp16 scale/bias), batch 1, a history of 1,792 - W positions (the KV
+cache rows filled on the device with seeded N(0, 1) fp16 values: throughput does not depend on their content), W
+warm-up steps, then K greedy decode steps at positions 1,792 .. 1,792+K-1. A step is one token: one CUDA-graph replay
+of the 121 kernels. Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB of KV per token against a 126 MB L2),
+so no flush is needed between steps.
+
+    python bench.py --kernel-case ffn|qkv|wo|down|head|attn   one launch of that kernel of the workload (after 3
+                                                               warm-ups) through the C-ABI: the ncu capture case
 
 One JSON line on rank 0:
   value          tokens/s over the K timed steps (device time, CUDA events, inputs resident in HBM), summed over ranks
@@ -58,33 +62,46 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region (SM clock, max clock, throttle reasons)."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi samples (every 20 ms) kept when their timestamp falls inside the timed region: SM clock, max clock,
+    throttle reasons."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.lines = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t_end = time.time() + 3.0
+            while not self.lines and time.time() < t_end:  # the sampler is up before the timed region starts
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def __exit__(self, *a):
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
         if self.proc:
+            time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -93,21 +110,21 @@ class Clocks:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        inside = [ln for t, ln in self.lines if self.t0 is not None and self.t0 <= t <= self.t1 + 0.02]
+        for ln in inside:
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                sm.append(float(parts[2]))
+                mx.append(float(parts[3]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.NAMES, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
                 "samples": len(sm)}
 
@@ -163,10 +180,50 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def kernel_case(args, rank):
+    """One launch of one kernel of the workload, after 3 warm-up launches of it (the ncu capture case: `-k` on the
+    kernel's name, `-s 3 -c 1`). GEMV kernels run through agxc_qmv on packs of the workload's shape (same planner and
+    kernels as the model); attention through agxc_attention_dev on a cache of the workload's shape at position 1,792."""
+    import torch
+    from agxforge_b200.kernels import attention as A
+    from agxforge_b200.kernels import qmv as Q
+    from agxforge_b200.inference import models
+    model, bits, batch, hist = CONFIGS[args.config]
+    S = models.get(model)
+    torch.manual_seed(5)
+    if args.kernel_case == "attn":
+        cap = hist + 8
+        K = torch.randn(batch, S.KV_HEADS, cap, S.HEAD_DIM, device="cuda").half()
+        V = torch.randn(batch, S.KV_HEADS, cap, S.HEAD_DIM, device="cuda").half()
+        q = (torch.randn(batch, S.HEADS, S.HEAD_DIM, device="cuda") * 0.1).half()
+        for _ in range(4):
+            A.attention(q, K, V, [hist] * batch)
+    else:
+        shapes = {r: (n, k) for r, n, k in S.matrices()}
+        n, k = {"qkv": shapes["qkv"], "wo": shapes["wo"], "ffn": shapes["gate"], "down": shapes["down"],
+                "head": (S.VOCAB, S.D_MODEL)}[args.kernel_case]
+        W = torch.randn(n, k, device="cuda") * 0.02
+        if args.kernel_case == "ffn":
+            g = Q.quantize(W, bits=bits)
+            u = Q.quantize(torch.randn(n, k, device="cuda") * 0.02, bits=bits)
+            pk = Q.Pack.gateup(g, u, n, k, bits=bits)
+            epi = "swiglu"
+        else:
+            pk = Q.Pack(*Q.quantize(W, bits=bits), n, k, bits=bits)
+            epi = "f32"
+        del W
+        x = torch.randn(batch, k, device="cuda").half()
+        for _ in range(4):
+            Q.qmv(pk, x, epi=epi)
+    torch.cuda.synchronize()
+    if rank == 0:
+        print(json.dumps(dict(kernel_case=args.kernel_case, config=args.config, launches=4)), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="internlm-q4-1792", choices=sorted(CONFIGS))
@@ -174,6 +231,7 @@ def main():
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-case", choices=KIND_NAMES, default=None)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -188,6 +246,11 @@ def main():
 
     import torch
     from agxforge_b200.inference import assemble
+    if args.kernel_case:
+        kernel_case(args, rank)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     model, bits, batch, hist = CONFIGS[args.config]
     K, W = args.steps, args.warmup
@@ -197,21 +260,24 @@ def main():
                        keep_packs=keep)
     S = m.shape
     rng = np.random.default_rng(1792 + rank)
-    # the history: prompt of hist - W + 1 random ids, consumed by the decode loop; then W warm-up steps at positions
-    # hist - W .. hist - 1; the timed steps are at positions hist .. hist + K - 1
-    P = hist - W + 1
+    # the history: positions 0 .. hist - W - 1 filled on the device (seeded), a random current token; then W warm-up
+    # steps at positions hist - W .. hist - 1; the timed steps are at positions hist .. hist + K - 1
     for b in range(batch):
-        m.start(b, rng.integers(0, S.VOCAB, P).tolist())
-    m.decode(P - 1 + W, want_tokens=False)
+        m.start(b, [int(rng.integers(0, S.VOCAB))])
+        m.fill_history(b, hist - W, seed=1792 + 7 * rank + b)
+    m.decode(W, want_tokens=False)
     torch.cuda.synchronize()
 
     # ---- timed: K graph replays back to back, CUDA events on the library's stream
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local) as clk:
-        _, _, t = m.decode(K, want_tokens=False)
+    clk = Clocks(local).start()
+    clk.mark_start()
+    _, _, t = m.decode(K, want_tokens=False)
     torch.cuda.synchronize()
+    clk.mark_end()
+    clk.stop()
     gpu_ms = t["gpu_ms"]
     launches = t["launches_per_step"]
     if dist is not None:
@@ -240,7 +306,7 @@ def main():
     kind_ms = (C.c_float * 6)()
     kind_n = (C.c_int32 * 6)()
     N.check(N.lib().agxc_model_profile(m.handle, args.profile_steps, kind_ms, kind_n), "profile")
-    pos_mid = hist + K + W // 2
+    pos_mid = hist + K + K + args.profile_steps // 2  # the profiled steps follow the timed and the e2e steps
     kvrow = 2 * S.KV_HEADS * S.HEAD_DIM * 2                      # K+V bytes per position per layer
     from agxforge_b200.inference.models import Model  # noqa: F401
     mats = {r: (n, k) for r, n, k in S.matrices()}
