@@ -104,7 +104,7 @@ int qmv_configure(const agxc_ctx* ctx) {
 // larger RW (fewer per-unit reductions). K is split only when the CTA's activation rows would not fit in ~40 KB (or
 // when asked). A chunk holds CG groups of every row tile of the unit (at most 36 KB, CG a multiple of the 16 / RW
 // K lanes that divides the CTA's groups); as many stages as ~80 KB allows (two CTAs, this kernel and its
-// programmatic-dependent successor, share an SM).
+// programmatic-dependent successor, share an SM; 160 KB for the head, which has no successor in the step).
 QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits, int force_rw,
                  int force_cg, int force_stages) {
   (void)hd;
@@ -157,7 +157,10 @@ QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, i
   const int stage_bytes = (P.RW * P.CG * (TB + 64) + 127) / 128 * 128;
   const int units = RT / P.RW * SC;
   const int chunks_per_cta = (units + sms - 1) / sms * (P.GC / P.CG);
-  P.stages = std::max(2, std::min({kMaxStages, (80 * 1024) / stage_bytes, std::max(2, chunks_per_cta)}));
+  // the vocab head is the graph's last kernel: no programmatic-dependent successor shares its SM, so its ring may take
+  // most of the shared memory
+  const int ring_cap = epi == EPI_ARGMAX ? 160 * 1024 : 80 * 1024;
+  P.stages = std::max(2, std::min({kMaxStages, ring_cap / stage_bytes, std::max(2, chunks_per_cta)}));
   if (force_stages >= 2 && force_stages <= kMaxStages) P.stages = force_stages;
   int grid = std::min(units, sms);
   grid = std::max(SC, grid / SC * SC);

@@ -168,7 +168,8 @@ __device__ __forceinline__ void group_step(uint32_t aw, uint32_t asb, uint32_t a
 // ------------------------------------------------------------------------------------------------ epilogues
 // vals: [rows][NBT] fp32 (column = activation row b) for the block of `rows` physical rows starting at `row0`.
 template <int EPI, int NBT>
-// resv: the residual of these rows prefetched ([rows][NBT] fp32), or NULL to read it here
+// resv: prefetched operands of these rows, or NULL to read them here: the residual ([rows][NBT] fp32) of RES1/RES2,
+// the RoPE (cos, sin) per pair ([rows/2][NBT][2]) of QKV
 // t0 / tstride: the calling threads' index and count (default: all consumer threads); the argmax keeps its running
 // maximum in misc[0], misc[1] of the calling group (one warp, t0 = lane, when a warp finalises a unit alone).
 __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc,
@@ -227,8 +228,8 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       int pos = static_cast<int>(p.q0[b]);
       if (pos > p.cap - 1) pos = p.cap - 1;
       if (head < p.H + p.KVH) {
-        const float c = p.cos_t[static_cast<size_t>(pos) * half + i1];
-        const float s = p.sin_t[static_cast<size_t>(pos) * half + i1];
+        const float c = resv ? resv[2 * t] : p.cos_t[static_cast<size_t>(pos) * half + i1];
+        const float s = resv ? resv[2 * t + 1] : p.sin_t[static_cast<size_t>(pos) * half + i1];
         const float o1 = y1 * c - y2 * s, o2 = y2 * c + y1 * s;
         if (head < p.H) {
           __half* q = p.q16 + (static_cast<size_t>(b) * p.H + head) * hd;
@@ -361,6 +362,94 @@ __device__ __forceinline__ void load8(const QmvParams& p, int b, int col, float*
   }
 }
 
+// Stage ONE activation row of the whole K range (fp16, RMSNorm fused when a gain is given) and its per-group sums
+// (xsum[g * 8]). A thread's vectors (k = tid, tid + 512) and their gains are loaded together and stay in registers
+// across the norm's reduction: one L2 round trip and one barrier (rows up to 8,192; wider rows reload the rest).
+__device__ __forceinline__ void stage_row1(const QmvParams& p, __half* xs16, float* xsum, float* red) {
+  constexpr int kCache = 2;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n8 = p.K / 8;
+  const int steps = (n8 + kConsumers - 1) / kConsumers;
+  float v[kCache][8];
+  uint4 gv[kCache];
+#pragma unroll
+  for (int st = 0; st < kCache; ++st) {
+    const int k = tid + st * kConsumers;
+    gv[st] = make_uint4(0u, 0u, 0u, 0u);
+    if (st < steps && k < n8) {
+      load8(p, 0, k * 8, v[st]);
+      if (p.norm_gain) gv[st] = reinterpret_cast<const uint4*>(p.norm_gain)[k];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[st][j] = 0.f;
+    }
+  }
+  float r = 1.0f;
+  if (p.norm_gain) {
+    float ss = 0.f;
+#pragma unroll
+    for (int st = 0; st < kCache; ++st)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[st][j], v[st][j], ss);
+    for (int k = tid + kCache * kConsumers; k < n8; k += kConsumers) {  // rows wider than the cache
+      float w[8];
+      load8(p, 0, k * 8, w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(w[j], w[j], ss);
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    consumer_sync();
+    float tot = 0.f;
+    for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
+    r = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
+  }
+  for (int st = 0; st < steps; ++st) {
+    const int k = tid + st * kConsumers;
+    const bool live = k < n8;
+    float x[8];
+    uint4 gu = make_uint4(0u, 0u, 0u, 0u);
+    if (st < kCache) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = st == 0 ? v[0][j] : v[1][j];
+      gu = st == 0 ? gv[0] : gv[1];
+    } else if (live) {
+      load8(p, 0, k * 8, x);
+      if (p.norm_gain) gu = reinterpret_cast<const uint4*>(p.norm_gain)[k];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = 0.f;
+    }
+    if (p.norm_gain && live) {
+      __half2 gh[4];
+      memcpy(gh, &gu, 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 g = __half22float2(gh[j]);
+        x[2 * j] = (x[2 * j] * r) * g.x;
+        x[2 * j + 1] = (x[2 * j + 1] * r) * g.y;
+      }
+    }
+    __half2 oh[4];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      oh[j] = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
+      const float2 f = __half22float2(oh[j]);
+      sum += f.x + f.y;
+    }
+    if (live) {
+      uint4 o;
+      memcpy(&o, oh, 16);
+      reinterpret_cast<uint4*>(xs16)[k] = o;
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (live && (k & 7) == 0) xsum[(k >> 3) * 8] = sum;
+  }
+}
+
 template <int BITS, int NBT, int RW, int EPI>
 __global__ void __launch_bounds__(kThreads, 2)
     qmv_kernel(const __grid_constant__ QmvParams p, const __grid_constant__ CUtensorMap tmw,
@@ -451,11 +540,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       resv[t] = v;
     }
   }
+  // The RoPE (cos, sin) of the first unit's pairs at the sequence's position, when the position was written by an
+  // earlier kernel than the upstream one (pos_ready: every qkv launch after the step's first).
+  constexpr bool kRope = EPI == EPI_QKV;
+  if (kRope && p.pos_ready && my_units > 0) {
+    const int row0 = rb0 * RW * 16, half = p.hd / 2;
+    for (int t = tid; t < RW * 8 * NBT; t += kConsumers) {
+      const int pr = t / NBT, b = t % NBT;
+      float c = 0.f, sn = 0.f;
+      if (b < nb) {
+        const int tile = pr / 8, r = pr % 8;
+        const int tt = ((row0 + tile * 16) % p.hd) / 16;
+        int pos = static_cast<int>(__ldcg(p.q0 + b));
+        if (pos > p.cap - 1) pos = p.cap - 1;
+        c = p.cos_t[static_cast<size_t>(pos) * half + 8 * tt + r];
+        sn = p.sin_t[static_cast<size_t>(pos) * half + 8 * tt + r];
+      }
+      resv[2 * t] = c;
+      resv[2 * t + 1] = sn;
+    }
+  }
   if (p.pdl) {
     pdl_wait();
     if (p.pdl == 1) pdl_launch_dependents();
   }
   if (tid == 0) trace_mark(p.trace, 1);
+  if (nb == 1 && SC == 1) {
+    stage_row1(p, xs16, xsum, red);  // batch 1: one L2 round trip, x and gains held in registers
+  } else {
   // RMSNorm: each row's sum of squares over the whole row (all p.K columns), every row's loads independent
   if (p.norm_gain) {
     float ssb[8];
@@ -532,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   }
+  }
   if (EPI == EPI_ARGMAX && tid < 8) {
     misc[2 * tid] = -INFINITY;
     misc[2 * tid + 1] = __int_as_float(0x7fffffff);
@@ -602,7 +715,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     consumer_sync();
     const int row0 = rb * RW * 16;
     if (SC == 1) {
-      epilogue<EPI, NBT>(p, row0, RW * 16, uv, misc, kRes && i == 0 ? resv : nullptr);
+      epilogue<EPI, NBT>(p, row0, RW * 16, uv, misc, (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
     } else {
       // split K: this unit's partial rows to scratch; the last of the SC units of these rows sums them in order
       for (int t = tid; t < RW * 16 * NBT; t += kConsumers) {
@@ -627,7 +740,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           ev[t] = s;
         }
         consumer_sync();
-        epilogue<EPI, NBT>(p, row0, RW * 16, ev, misc, kRes && i == 0 ? resv : nullptr);
+        epilogue<EPI, NBT>(p, row0, RW * 16, ev, misc,
+                           (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
       }
       consumer_sync();
     }

@@ -140,6 +140,7 @@ void layer_params(agxc_model* m, int l, QmvParams& p, AttnParams& a, QmvParams& 
   p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
   p.q16 = m->q16; p.kcache = m->kcache + l * layer_kv; p.vcache = m->vcache + l * layer_kv;
   p.part = m->part; p.counters = m->counters; p.err = m->ctx->err_dev;
+  p.pos_ready = l > 0;  // q0 is advanced by the head, the kernel just before layer 0's qkv
   // D2: attention
   a.nb = B; a.H = H; a.KVH = KVH; a.hd = hd; a.cap = D.cap; a.S = m->attn_S; a.q0 = m->q0; a.q16 = m->q16;
   a.kc = m->kcache + l * layer_kv; a.vc = m->vcache + l * layer_kv; a.out = m->attn; a.part = m->apart;

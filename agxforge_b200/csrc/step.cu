@@ -205,88 +205,6 @@ struct Ring {
   }
 };
 
-// Stage the activation row (fp16, RMSNorm fused when a gain is given) and its per-group sums; one row (batch 1).
-// A thread's vectors (k = tid, tid + 512, ...) stay in registers between the norm's two passes (K <= 8,192 fits).
-__device__ void stage_row(const QmvParams& p, __half* xs16, float* xsum, float* red) {
-  constexpr int kCache = 2;  // vectors of 8 per thread kept in registers
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n8 = p.K / 8;
-  const int steps = (n8 + kConsumers - 1) / kConsumers;
-  float v[kCache][8];
-#pragma unroll
-  for (int st = 0; st < kCache; ++st) {
-    const int k = tid + st * kConsumers;
-    if (st < steps && k < n8) {
-      gemv::load8(p, 0, k * 8, v[st]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[st][j] = 0.f;
-    }
-  }
-  float r = 1.0f;
-  if (p.norm_gain) {
-    float ss = 0.f;
-#pragma unroll
-    for (int st = 0; st < kCache; ++st)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(v[st][j], v[st][j], ss);
-    for (int k = tid + kCache * kConsumers; k < n8; k += kConsumers) {  // rows wider than the cache
-      float w[8];
-      gemv::load8(p, 0, k * 8, w);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(w[j], w[j], ss);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    consumer_sync();
-    float tot = 0.f;
-    for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
-    r = rsqrtf(tot / static_cast<float>(p.K) + p.eps);
-  }
-  for (int st = 0; st < steps; ++st) {
-    const int k = tid + st * kConsumers;
-    const bool live = k < n8;
-    float x[8];
-    if (st < kCache) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = st == 0 ? v[0][j] : v[1][j];
-    } else if (live) {
-      gemv::load8(p, 0, k * 8, x);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) x[j] = 0.f;
-    }
-    if (p.norm_gain && live) {
-      const uint4 gu = reinterpret_cast<const uint4*>(p.norm_gain)[k];
-      __half2 gh[4];
-      memcpy(gh, &gu, 16);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 g = __half22float2(gh[j]);
-        x[2 * j] = (x[2 * j] * r) * g.x;
-        x[2 * j + 1] = (x[2 * j + 1] * r) * g.y;
-      }
-    }
-    __half2 oh[4];
-    float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      oh[j] = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
-      const float2 f = __half22float2(oh[j]);
-      sum += f.x + f.y;
-    }
-    if (live) {
-      uint4 o;
-      memcpy(&o, oh, 16);
-      reinterpret_cast<uint4*>(xs16)[k] = o;
-    }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-    if (live && (k & 7) == 0) xsum[(k >> 3) * 8] = sum;
-  }
-}
-
 // The CTA's units (u = blockIdx.x, + gridDim.x, ...) stream through the ring; all 16 warps work on every chunk (RW
 // row tiles x 16 / RW K lanes) but never wait for one another inside a unit: each warp parks its partial rows in
 // shared memory and moves on. Every kUnitBatch units one barrier, then warp j sums unit j's partials and runs its
@@ -309,7 +227,7 @@ __device__ bool gemv_phase(const StepPhase& P, uint8_t* smem, const Smem& L, Rin
   volatile int* flag = reinterpret_cast<volatile int*>(misc + 60);
 
   if (tid == 0) mark(P, 1);
-  stage_row(p, xs16, xsum, red);
+  gemv::stage_row1(p, xs16, xsum, red);
   if (EPI == EPI_ARGMAX && lane == 0) {
     wmisc[0] = -INFINITY;
     wmisc[1] = __int_as_float(0x7fffffff);
