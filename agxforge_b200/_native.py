@@ -22,6 +22,7 @@ VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
 OPT_PDL = 0
 OPT_TRACE = 1
 OPT_PERSISTENT = 2
+OPT_BULK = 3
 
 
 class PackDesc(C.Structure):

@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
     __syncthreads();
   }
 
-  if (p.pdl == 2) pdl_launch_dependents();
+  if (p.pdl >= 2) pdl_launch_dependents();
   // l over the warp's 16 key rows (lanes with the same t4); then the warp's partial to shared memory (the stage
   // buffers are free now)
 #pragma unroll

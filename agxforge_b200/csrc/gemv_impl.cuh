@@ -505,8 +505,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (*dead) break;
           uint8_t* dst = smem + L.ring + slot * L.stage_bytes;
           mbar_arrive_expect_tx(&full[slot], RW * CG * (TB + 64));
-          tma_load_3d(dst, &tmw, 0, sc * GC + c * CG, rb * RW, &full[slot]);
-          tma_load_3d(dst + L.wbytes, &tmsb, 0, sc * GC + c * CG, rb * RW, &full[slot]);
+          if (p.bulk) {
+            // plain bulk copies: a row tile's CG groups are contiguous in the row-tile-major pack
+            for (int r2 = 0; r2 < RW; ++r2) {
+              const size_t t = static_cast<size_t>(rb * RW + r2) * p.G + sc * GC + c * CG;
+              bulk_g2s(dst + r2 * CG * TB, p.w + t * TB, CG * TB, &full[slot]);
+              bulk_g2s(dst + L.wbytes + r2 * CG * 64, p.sb + t * 64, CG * 64, &full[slot]);
+            }
+          } else {
+            tma_load_3d(dst, &tmw, 0, sc * GC + c * CG, rb * RW, &full[slot]);
+            tma_load_3d(dst + L.wbytes, &tmsb, 0, sc * GC + c * CG, rb * RW, &full[slot]);
+          }
           if (++slot == stages) { slot = 0; phase ^= 1; }
         }
         if (*dead) break;
@@ -747,6 +756,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
+  if (p.pdl == 3) pdl_launch_dependents();  // mode 3: the successor starts once every chunk is consumed
   if (consumer_sync_or(!waited_ok)) return;  // a stage never landed: the error word is set; leave uniformly
   if (tid == 0) trace_mark(p.trace, 4);
 

@@ -81,6 +81,7 @@ struct QmvParams {
   int32_t* tok_out = nullptr;    // [nb]
   uint32_t* force_next = nullptr; // [nb] pending forced tokens (consumed and cleared by the step)
   int pos_ready = 0;              // qkv: q0 was final before the upstream kernel started (RoPE read before the wait)
+  int bulk = 0;                   // weights by plain bulk copies (1) or 3-D TMA tensor boxes (0)
   // scratch
   float* part = nullptr;         // [SC][N][nb] partial rows
   float* pairs = nullptr;        // [grid][nb][2] argmax pairs (value, index as float bits)

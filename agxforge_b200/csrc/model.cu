@@ -58,9 +58,10 @@ struct agxc_model {
   // plans
   agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
   int attn_S = 1;
-  int pdl = 2;
+  int pdl = 1;
   // the persistent step kernel (batch 1): its program, grid barrier words, and whether the device runs it
   int persistent = 0;
+  int bulk = 0;                 // GEMV weights by plain bulk copies (AGXC_OPT_BULK)
   int step_ok = 0;
   int step_kmax = 0;
   int step_ring = 0;
@@ -235,6 +236,7 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
   m->launches = 0;
   auto launch_gemv = [&](QmvParams& x, const QmvPlan& plan, int epi) -> int {
     x.pdl = m->pdl;
+    x.bulk = m->bulk;
     x.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
     if (int r = launch_qmv_epi(m->ctx, x, plan, epi, s)) return r;
@@ -820,8 +822,10 @@ int agxc_model_trace_cta_read(agxc_model* m, uint64_t* out, size_t capacity, int
 int agxc_model_set_option(agxc_model* m, int option, int value) {
   if (!m) return agxc::fail(AGXC_EINVAL, "set_option: null model");
   if (option == AGXC_OPT_PDL) {
-    if (value < 0 || value > 2) return agxc::fail(AGXC_EINVAL, "set_option: pdl 0, 1 or 2");
+    if (value < 0 || value > 3) return agxc::fail(AGXC_EINVAL, "set_option: pdl 0, 1, 2 or 3");
     m->pdl = value;
+  } else if (option == AGXC_OPT_BULK) {
+    m->bulk = value ? 1 : 0;
   } else if (option == AGXC_OPT_PERSISTENT) {
     m->persistent = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {

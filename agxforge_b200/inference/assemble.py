@@ -128,11 +128,13 @@ class DecodeModel:
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
     def set_option(self, option, value):
-        """Model options: "pdl" (programmatic dependent launch between the step's kernels: 0 off, 1 successor let in
-        after the dependency wait, 2 (default) after the inputs are staged); "trace"
+        """Model options: "pdl" (programmatic dependent launch between the step's kernels: 0 off, 1 (default)
+        successor let in after the dependency wait, 2 after the inputs are staged, 3 after the last weight chunk);
+        "trace"
         (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace());
-        "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off)."""
-        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT}
+        "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off); "bulk" (GEMV weights
+        by plain bulk copies instead of TMA tensor boxes)."""
+        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT, "bulk": N.OPT_BULK}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")

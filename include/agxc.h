@@ -213,9 +213,10 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 
 /* Model options (each re-captures the step's graph on the next decode). */
 #define AGXC_OPT_PDL 0        /* programmatic dependent launch between the step's kernels, so each streams its weights
-                                 while its predecessor finishes: 1 a kernel lets its successor start right after its
-                                 own dependency wait; 2 (default) only after it staged its inputs (GEMV) or read its
-                                 keys (attention); 0 plain stream order */
+                                 while its predecessor finishes: 1 (default) a kernel lets its successor start right
+                                 after its own dependency wait; 2 only after it staged its inputs (GEMV) or read its
+                                 keys (attention); 3 only after its last weight chunk (GEMV) or its keys (attention);
+                                 0 plain stream order */
 #define AGXC_OPT_TRACE 1      /* 1: every launch of the step records, over its CTAs, the first and last %globaltimer
                                  (ns) at CTA entry, after the dependency wait, and at CTA exit (read with
                                  agxc_model_trace_read); 0 (default): off */
@@ -224,6 +225,8 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
                                  run between grid barriers) when the device fits it; 0 (default): one kernel per
                                  projection and attention, chained by programmatic dependent launch (always the case
                                  for batch > 1) */
+#define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
+                                 a chunk); 0 (default): by 3-D TMA tensor boxes */
 AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
 
 /* The launch trace accumulated since tracing started or the last read (min and max over all steps in between), then

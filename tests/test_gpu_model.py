@@ -164,9 +164,10 @@ def test_launch_trace(torch):
 
 def test_pdl_modes_agree(torch):
     """Programmatic dependent launch only moves when a kernel may start: plain stream order (0), the successor let in
-    right after the dependency wait (1), or after the inputs are staged (2) give bit-identical tokens and logits."""
+    right after the dependency wait (1), after the inputs are staged (2) or after the last weight chunk (3) give
+    bit-identical tokens and logits."""
     out = []
-    for mode in (0, 1, 2):
+    for mode in (0, 1, 2, 3):
         m = _build(dict(SMALL), bits=4, seed=4)
         m.set_option("pdl", mode)
         m.start(0, [9, 8, 7, 6])
