@@ -68,6 +68,7 @@ SIGNATURES = {
     "agxc_pack_dequant_dev": (_I, [_P, _P, _P]),
     "agxc_qmv": (_I, [_P, C.POINTER(QmvArgs), _P]),
     "agxc_qmv_noalloc": (_I, [_P, C.POINTER(QmvArgs), _P]),
+    "agxc_qmm": (_I, [_P, _P, _P, _I, _P, _I, _I, _P]),
     "agxc_rmsnorm_dev": (_I, [_P, _P, _I, _I, _I, _P, C.c_float, _P, _P]),
     "agxc_attention_dev": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),

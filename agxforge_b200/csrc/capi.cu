@@ -120,6 +120,10 @@ int agxc_init(int device, agxc_ctx** out) {
     agxc_ctx_free(c);
     return rc;
   }
+  if (int rc = qmm_configure(c)) {
+    agxc_ctx_free(c);
+    return rc;
+  }
   *out = c;
   return 0;
 }
@@ -269,6 +273,21 @@ int agxc_qmv(agxc_ctx* ctx, const agxc_qmv_args* a, void* stream) {
   if (part) cudaFreeAsync(part, s);
   if (cnt) cudaFreeAsync(cnt, s);
   return rc;
+}
+
+int agxc_qmm(agxc_ctx* ctx, const agxc_pack* pack, const void* x_dev, int batch, float* y_dev, int ldy, int ksplit,
+             void* stream) {
+  if (!ctx || !pack || !x_dev || !y_dev) return fail(AGXC_EINVAL, "qmm: null argument");
+  if (pack->gateup) return fail(AGXC_EINVAL, "qmm: a plain pack (not gate/up interleaved)");
+  cudaStream_t s = stream_of(ctx, stream);
+  const int G = pack->k / 64, tiles = pack->n / 128;
+  if (ksplit == 0) {  // split K until the tiles fill the SMs (a divisor of the groups)
+    ksplit = 1;
+    while (tiles * ksplit * 2 <= ctx->num_sms && G % (ksplit * 2) == 0) ksplit *= 2;
+  }
+  if (ksplit > 1)
+    for (int b = 0; b < batch; ++b) AGXC_CUDA(cudaMemsetAsync(y_dev + static_cast<size_t>(b) * ldy, 0, pack->n * 4, s));
+  return launch_qmm(ctx, pack, x_dev, batch, y_dev, ldy, ksplit, s);
 }
 
 int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int nb, int d, const uint16_t* gain_dev, float eps,

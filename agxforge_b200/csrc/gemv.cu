@@ -74,6 +74,20 @@ int make_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, i
 
 }  // namespace
 
+int encode_act_map(CUtensorMap* m, const void* x, int B, int K) {
+  if (int rc = encode_fn()) return rc;
+  if (K % 64 || (reinterpret_cast<uintptr_t>(x) & 15)) return fail(AGXC_EINVAL, "qmm: X rows of K % 64 == 0, 16-B aligned");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(B)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AGXC_ECUDA, "cuTensorMapEncodeTiled (X) failed (" + std::to_string(r) + ")");
+  return 0;
+}
+
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z) {
   if (int rc = encode_fn()) return rc;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(Z)};

@@ -154,6 +154,13 @@ size_t step_smem(int kmax, int stages);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
 constexpr int kAttnKeys = 128;
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);
+// A TMA map over fp16 activation rows X [B][K]: boxes of 64 columns x B rows, 128-byte swizzle.
+int encode_act_map(CUtensorMap* m, const void* x, int B, int K);
+
+// ---- the batched GEMM (qmm.cu): Y [B][ldy] fp32 = X [B][K] fp16 W^T, B = 32..256 (multiple of 16), tcgen05 + TMEM
+int qmm_configure(const agxc_ctx* ctx);
+int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
+               cudaStream_t s);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 // tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,

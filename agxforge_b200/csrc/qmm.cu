@@ -1,0 +1,376 @@
+// qmm.cu — the batched quantized GEMM of the decode step for B >= 32 activation rows (the reference's tensor-unit
+// path, tools/g17qsm.py:1-21 and assemble.layer_ops_qsm agxforge/inference/assemble.py:368-426:
+// Y^T = W^T X^T with W dequantised once to fp16), on Blackwell's 5th-generation tensor cores.
+//
+// One CTA per 128 weight rows (x a K range when K is split): the MMA's M is the weight rows, its N the activation
+// rows (B = 32 .. 256), K advances by one 64-group per chunk. Per chunk:
+//   * the PRODUCER warp brings the chunk's 8 packed row tiles and their scale/bias (two 3-D TMA boxes of the pack)
+//     and the activations' 64 columns (a 2-D TMA box of X [B][K] fp16, 128-byte swizzle) into a ring stage;
+//   * four DEQUANT warps turn the tiles into fp16 weights in the MMA's canonical K-major 128-byte-swizzled layout
+//     (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes 1024 away
+//     exactly, HFMA2 applies the row's scale and bias with one rounding);
+//   * the MMA warp issues four tcgen05.mma.kind::f16 (M 128, N B, K 16) accumulating in TMEM, and commits: the
+//     commit releases the stage and the dequant buffer when the tensor core has read them.
+// After the last chunk the dequant warps read the 128 x B fp32 accumulator back with tcgen05.ld (warp w reads TMEM
+// lanes 32 (w % 4) ..) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace agxc {
+
+namespace {
+
+constexpr int kM = 128;          // weight rows per CTA (the MMA's M)
+constexpr int kThreads = 192;    // warp 0 producer, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
+constexpr int kDeqWarps = 4;
+
+struct QmmParams {
+  const uint8_t* w = nullptr;
+  const uint8_t* sb = nullptr;
+  int N = 0, K = 0, G = 0, bits = 4, sdt = 0;
+  int B = 0;                      // activation rows (MMA N), a multiple of 16 in [32, 256]
+  int ksplit = 1;                 // K ranges (CTAs) per 128-row tile
+  int stages = 4;
+  float* y = nullptr;             // fp32 [B][ldy]
+  int ldy = 0;
+  unsigned* err = nullptr;
+};
+
+struct QmmSmem {
+  int bars, tmem_slot, deq, stage0, stage_bytes, x_off, w_off, sb_off, total;
+};
+
+__host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages) {
+  QmmSmem L;
+  const int TB = bits == 4 ? 512 : 1024;
+  L.bars = 0;                                   // raw_full[S], raw_empty[S], deq_full[2], deq_empty[2], acc_full
+  L.tmem_slot = 512;
+  L.deq = 1024;                                 // two fp16 weight tiles of 128 x 64 (16 KB each)
+  L.stage0 = L.deq + 2 * kM * 128;
+  L.x_off = 0;                                  // X tile: B rows x 128 B (1,024-aligned for the swizzle)
+  L.w_off = (B * 128 + 1023) / 1024 * 1024;
+  L.sb_off = L.w_off + 8 * TB;
+  L.stage_bytes = (L.sb_off + 8 * 64 + 1023) / 1024 * 1024;
+  L.total = L.stage0 + stages * L.stage_bytes;
+  return L;
+}
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  // UMMA shared-memory descriptor, K-major, 128-byte swizzle: start >> 4 (bits 0-13), leading byte offset 16 B
+  // (bits 16-29), stride byte offset 1,024 B between 8-row atoms (bits 32-45), version 1 (bits 46-47), layout
+  // SWIZZLE_128B = 2 (bits 61-63)
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  // instruction descriptor: fp32 accumulator (bits 4-5 = 1), fp16 A and B (formats 0), both K-major, N >> 3 at bits
+  // 17-22, M >> 4 at bits 24-28
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t hsub_1024(uint32_t v) {  // fp16 pair minus 1024 (exact for 1024 + q, q < 1024)
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(0x64006400u));
+  return r;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint16_t to_f16_bits(uint16_t v, int sdt) {
+  if (!sdt) return v;
+  return __half_as_ushort(__float2half_rn(__uint_as_float(static_cast<uint32_t>(v) << 16)));
+}
+
+// One lane-task of the dequantisation: lane (r, c) of row tile t of the chunk -> rows 16t + r and 16t + r + 8,
+// k = 16c .. 16c + 15 (16-byte chunks 2c and 2c + 1 of each 128-byte row), fp16, swizzled.
+template <int BITS>
+__device__ __forceinline__ void dequant_task(const uint8_t* wraw, const uint8_t* sbraw, uint8_t* deq, int t, int l,
+                                             int sdt) {
+  const int r = l >> 2, c = l & 3;
+  const uint2 e = *reinterpret_cast<const uint2*>(sbraw + t * 64 + r * 8);  // {s[r], s[r+8], b[r], b[r+8]}
+  const uint32_t s0 = to_f16_bits(static_cast<uint16_t>(e.x & 0xFFFFu), sdt);
+  const uint32_t s1 = to_f16_bits(static_cast<uint16_t>(e.x >> 16), sdt);
+  const uint32_t b0 = to_f16_bits(static_cast<uint16_t>(e.y & 0xFFFFu), sdt);
+  const uint32_t b1 = to_f16_bits(static_cast<uint16_t>(e.y >> 16), sdt);
+  const uint32_t s2[2] = {s0 | (s0 << 16), s1 | (s1 << 16)};
+  const uint32_t b2[2] = {b0 | (b0 << 16), b1 | (b1 << 16)};
+  uint32_t o[2][2][4];  // [row half][chunk][word]
+  if (BITS == 4) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(wraw + t * 512 + l * 16);
+    const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};  // i: row r + 8 (i & 1), hi = i >> 1
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {      // row r (h 0) or r + 8 (h 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {    // pair (k0, k0 + 1), k0 = 16c + 4j + 2hi
+#pragma unroll
+        for (int hi = 0; hi < 2; ++hi) {
+          const uint32_t q = ((w[h + 2 * hi] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+          o[h][j >> 1][2 * (j & 1) + hi] = hfma2(hsub_1024(q), s2[h], b2[h]);
+        }
+      }
+    }
+  } else {
+    const uint4 lo = *reinterpret_cast<const uint4*>(wraw + t * 1024 + l * 16);
+    const uint4 hi4 = *reinterpret_cast<const uint4*>(wraw + t * 1024 + 512 + l * 16);
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi4.x, hi4.y, hi4.z, hi4.w};  // wi: k0 = 16c + 4 (wi >> 1) + 2 (wi & 1)
+#pragma unroll
+    for (int wi = 0; wi < 8; ++wi) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t q = prmt(w[wi], 0x64646464u, h ? 0x4342u : 0x4140u);  // (1024 + q[k0], 1024 + q[k0 + 1])
+        o[h][wi >> 2][wi & 3] = hfma2(hsub_1024(q), s2[h], b2[h]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = 16 * t + r + 8 * h;
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+      const int chunk = 2 * c + ch;
+      *reinterpret_cast<uint4*>(deq + row * 128 + (((chunk ^ (row & 7)) & 7) << 4)) =
+          make_uint4(o[h][ch][0], o[h][ch][1], o[h][ch][2], o[h][ch][3]);
+    }
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, const __grid_constant__ CUtensorMap tw,
+                                                          const __grid_constant__ CUtensorMap ts,
+                                                          const __grid_constant__ CUtensorMap tx) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr int TB = BITS == 4 ? 512 : 1024;
+  const QmmSmem L = qmm_layout(BITS, p.B, p.stages);
+  const int S = p.stages;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* raw_empty = raw_full + S;
+  uint64_t* deq_full = raw_empty + S;
+  uint64_t* deq_empty = deq_full + 2;
+  uint64_t* acc_full = deq_empty + 2;
+  volatile int* dead = reinterpret_cast<volatile int*>(acc_full + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tile = blockIdx.x / p.ksplit, ks = blockIdx.x % p.ksplit;
+  const int gper = p.G / p.ksplit;              // groups (chunks) of this CTA's K range
+  const int g0 = ks * gper;
+  const int ncols = p.B <= 32 ? 32 : p.B <= 64 ? 64 : p.B <= 128 ? 128 : 256;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 1);
+    }
+    for (int d = 0; d < 2; ++d) {
+      mbar_init(&deq_full[d], kDeqWarps);
+      mbar_init(&deq_empty[d], 1);
+    }
+    mbar_init(acc_full, 1);
+    *dead = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {  // TMEM: ncols fp32 columns x 128 lanes for the accumulator
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ts)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
+      const unsigned bytes = static_cast<unsigned>(p.B * 128 + 8 * TB + 8 * 64);
+      int issued = 0;
+      for (int i = 0; i < gper && !*dead; ++i, ++issued) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&raw_empty[s], ((i / S) - 1) & 1, p.err)) {
+          *dead = 1;
+          break;
+        }
+        uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+        mbar_arrive_expect_tx(&raw_full[s], bytes);
+        tma_3d(st + L.w_off, &tw, 0, g0 + i, tile * 8, &raw_full[s]);
+        tma_3d(st + L.sb_off, &ts, 0, g0 + i, tile * 8, &raw_full[s]);
+        tma_2d(st + L.x_off, &tx, (g0 + i) * 64, 0, &raw_full[s]);
+      }
+      if (*dead) {  // a wait gave up: no copy of this CTA may land after it leaves (bounded)
+        for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+          mbar_wait_bounded(&raw_full[i % S], (i / S) & 1, nullptr, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(p.B);
+      for (int i = 0; i < gper; ++i) {
+        const int s = i % S, d = i & 1;
+        if (*dead || !mbar_wait_bounded(&deq_full[d], (i >> 1) & 1, p.err)) {
+          *dead = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + L.deq + d * kM * 128);
+        const uint32_t b0 = smem_u32(smem + L.stage0 + s * L.stage_bytes + L.x_off);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // four K = 16 steps: +32 bytes within the swizzled 128-byte rows
+          const uint64_t ad = desc_sw128(a0 + 32 * k), bd = desc_sw128(b0 + 32 * k);
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          asm volatile(
+              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+              "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+              : "memory");
+        }
+        tc_commit(&raw_empty[s]);  // the stage (weights read, X read) is free once these MMAs are done
+        tc_commit(&deq_empty[d]);
+      }
+      tc_commit(acc_full);  // every MMA of the CTA done: the accumulator is final
+    }
+  } else {
+    // ---- dequant warps, then the epilogue
+    const int dw = warp - 2;  // 0..3
+    for (int i = 0; i < gper; ++i) {
+      const int s = i % S, d = i & 1;
+      const bool ok1 = !*dead && mbar_wait_bounded(&raw_full[s], (i / S) & 1, p.err);
+      const bool ok2 = ok1 && (i < 2 || mbar_wait_bounded(&deq_empty[d], ((i >> 1) - 1) & 1, p.err));
+      if (!__all_sync(0xffffffffu, ok2)) {  // the warp leaves together
+        *dead = 1;
+        break;
+      }
+      const uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+      uint8_t* deq = smem + L.deq + d * kM * 128;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {  // 8 row tiles x 32 lanes = 256 tasks over 128 threads
+        const int task = dw * 64 + q * 32 + lane;  // tile = task / 32
+        dequant_task<BITS>(st + L.w_off, st + L.sb_off, deq, task >> 5, task & 31, p.sdt);
+      }
+      fence_proxy_async();  // the tensor core reads what these generic stores wrote
+      __syncwarp();
+      if (lane == 0) mbar_arrive1(&deq_full[d]);
+    }
+    // epilogue: TMEM lanes 32 (warp % 4) .. + 31 = weight rows; columns = activation rows
+    const bool ok = __all_sync(0xffffffffu, !*dead && mbar_wait_bounded(acc_full, 0, p.err));  // warp-uniform:
+    tc_fence_after();                                                                        // tcgen05.ld is aligned
+    if (ok) {
+      const int q4 = warp & 3;
+      const int row = tile * kM + 32 * q4 + lane;
+      const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+      for (int c0 = 0; c0 < p.B; c0 += 16) {
+        uint32_t v[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(base + static_cast<uint32_t>(c0)));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < p.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float* dst = p.y + static_cast<size_t>(c0 + j) * p.ldy + row;
+            if (p.ksplit > 1) atomicAdd(dst, __uint_as_float(v[j]));
+            else *dst = __uint_as_float(v[j]);
+          }
+        }
+      }
+    }
+  }
+  // every role is done (the tensor core too: acc_full waited, or the error path below): free TMEM
+  if (*dead && tid == 64) mbar_wait_bounded(acc_full, 0, nullptr, 100000000ull);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+template <int BITS>
+int qmm_allow(int optin) {
+  cudaFuncAttributes fa;
+  AGXC_CUDA(cudaFuncGetAttributes(&fa, qmm_kernel<BITS>));
+  AGXC_CUDA(cudaFuncSetAttribute(qmm_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 optin - static_cast<int>(fa.sharedSizeBytes)));
+  return 0;
+}
+
+}  // namespace
+
+int qmm_configure(const agxc_ctx* ctx) {
+  int rc;
+  if ((rc = qmm_allow<4>(ctx->max_smem_optin)) || (rc = qmm_allow<8>(ctx->max_smem_optin))) return rc;
+  return 0;
+}
+
+// Y [B][ldy] fp32 = X [B][K] fp16 x W^T for a pack W [N][K]: 128-row tiles, the K range split over ksplit CTAs when
+// the tiles alone would leave SMs idle (then Y must hold zeros: the CTAs add into it).
+int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
+               cudaStream_t s) {
+  if (B < 32 || B > 256 || B % 16) return fail(AGXC_EINVAL, "qmm: 32 to 256 activation rows, a multiple of 16");
+  if (pk->n % kM) return fail(AGXC_EINVAL, "qmm: N must be a multiple of 128");
+  if (ldy < pk->n) return fail(AGXC_EINVAL, "qmm: ldy < N");
+  const int G = pk->k / 64;
+  if (ksplit < 1 || G % ksplit) return fail(AGXC_EINVAL, "qmm: ksplit must divide K/64");
+  QmmParams p;
+  p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.G = G; p.bits = pk->bits; p.sdt = pk->sdt;
+  p.B = B; p.ksplit = ksplit; p.y = y; p.ldy = ldy; p.err = ctx->err_dev;
+  // as many stages as fit beside the two dequant tiles (at most 8)
+  p.stages = 8;
+  while (p.stages > 2 && qmm_layout(pk->bits, B, p.stages).total + 1024 > ctx->max_smem_optin - 2048) --p.stages;
+  const int smem = qmm_layout(pk->bits, B, p.stages).total + 1024;
+  // maps: the pack's tiles and scale/bias as boxes of 1 group x 8 row tiles; X [B][K] fp16 as 64 x B boxes
+  QmvPlan plan;
+  plan.CG = 1;
+  plan.RW = 8;
+  CUtensorMap tw, ts, tx;
+  if (int rc = qmv_maps(plan, pk->tiles, pk->sb, pk->n, pk->k, pk->bits, &tw, &ts)) return rc;
+  if (int rc = encode_act_map(&tx, x, B, pk->k)) return rc;
+  const int grid = (pk->n / kM) * ksplit;
+  if (pk->bits == 4) qmm_kernel<4><<<grid, kThreads, smem, s>>>(p, tw, ts, tx);
+  else qmm_kernel<8><<<grid, kThreads, smem, s>>>(p, tw, ts, tx);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace agxc

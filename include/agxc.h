@@ -123,6 +123,14 @@ AGXC_API int agxc_qmv(agxc_ctx* ctx, const agxc_qmv_args* args, void* stream);
  * ordered on one stream. The first call on a device looks up the block's address; make it outside stream capture. */
 AGXC_API int agxc_qmv_noalloc(agxc_ctx* ctx, const agxc_qmv_args* args, void* stream);
 
+/* The batched GEMM for 32..256 activation rows (a multiple of 16) on the tensor cores (the reference's tensor-unit
+ * path, tools/g17qsm.py:1-21, assemble.layer_ops_qsm agxforge/inference/assemble.py:368-426; the weights are
+ * dequantised once to fp16 as there): y fp32 [batch][ldy] = x fp16 [batch][k] W^T for a plain pack (n a multiple of
+ * 128). `ksplit` splits K over CTAs (0 = until the 128-row tiles fill the SMs; with a split the call zeroes y first
+ * and the CTAs add into it). */
+AGXC_API int agxc_qmm(agxc_ctx* ctx, const agxc_pack* pack, const void* x_dev, int batch, float* y_dev, int ldy,
+                      int ksplit, void* stream);
+
 /* Standalone RMSNorm rows (norm.build_rmsnorm_wide, agxforge/kernels/norm.py:42-155): out fp16 [nb][d]. */
 AGXC_API int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int nb, int d, const uint16_t* gain_dev,
                      float eps, uint16_t* out_dev, void* stream);
