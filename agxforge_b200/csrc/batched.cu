@@ -1,0 +1,175 @@
+// batched.cu — the per-row steps of the batched decode step (B >= 32 sequences), between the tensor-core GEMMs of
+// qmm.cu: the projections produce fp32 rows y [B][n] in the packs' physical row order, and these kernels finish
+// them exactly as the single-sequence GEMV epilogues do (gemv_impl.cuh), so both paths share every rounding point:
+//   rope_append   bias, rotate-half RoPE at each sequence's position, q scale (fp16 q), K and V rows into the cache
+//                 (the qkv pack's tile rows r and r + 8 are a RoPE pair; attention.py:1309-1323)
+//   residual_add16     h = y + x16 (fp32)                      (with_residual add16, qmv.py:112-120)
+//   residual_add32_16  x16 = fp16(y + h)                       (with_residual add32_to16, qmv.py:825-833)
+//   swiglu        act = fp16(silu(gate) * up) over the interleaved gate/up row tiles (qmv.py:214-226)
+//   argmax_gen    per sequence: the first maximum of the logits, then the generation step (argmax.py:141-215,
+//                 assemble.py:918-930): forced token, else the logged one, else the argmax; log, q0 + 1, x16 = emb[tok]
+#include <cmath>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace agxc {
+
+namespace {
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+__global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows, const __half* __restrict__ bias,
+                                   const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                   const uint32_t* __restrict__ q0, int H, int KVH, int hd, int cap, float qscale,
+                                   __half* __restrict__ q16, __half* __restrict__ kc, __half* __restrict__ vc, int B) {
+  const int pairs = rows / 2;
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (t >= static_cast<long long>(B) * pairs) return;
+  const int b = static_cast<int>(t / pairs), pr = static_cast<int>(t % pairs);
+  const int half = hd / 2;
+  const int tile = pr / 8, r = pr % 8;
+  const int prow0 = tile * 16;
+  const int head = prow0 / hd, tt = (prow0 % hd) / 16;
+  const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
+  const float* yb = y + static_cast<size_t>(b) * ld;
+  float y1 = yb[prow0 + r], y2 = yb[prow0 + r + 8];
+  if (bias) {
+    y1 += __half2float(bias[head * hd + i1]);
+    y2 += __half2float(bias[head * hd + i2]);
+  }
+  int pos = static_cast<int>(q0[b]);
+  if (pos > cap - 1) pos = cap - 1;
+  if (head < H + KVH) {
+    const float c = cos_t[static_cast<size_t>(pos) * half + i1];
+    const float s = sin_t[static_cast<size_t>(pos) * half + i1];
+    const float o1 = y1 * c - y2 * s, o2 = y2 * c + y1 * s;
+    if (head < H) {
+      __half* q = q16 + (static_cast<size_t>(b) * H + head) * hd;
+      q[i1] = __float2half_rn(o1 * qscale);
+      q[i2] = __float2half_rn(o2 * qscale);
+    } else {
+      __half* k = kc + ((static_cast<size_t>(b) * KVH + (head - H)) * cap + pos) * hd;
+      k[i1] = __float2half_rn(o1);
+      k[i2] = __float2half_rn(o2);
+    }
+  } else {
+    __half* v = vc + ((static_cast<size_t>(b) * KVH + (head - H - KVH)) * cap + pos) * hd;
+    v[i1] = __float2half_rn(y1);
+    v[i2] = __float2half_rn(y2);
+  }
+}
+
+__global__ void residual16_kernel(const float* __restrict__ y, int ld, const __half* __restrict__ x16, float* h, int d,
+                                  int B) {
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (t >= static_cast<long long>(B) * d) return;
+  const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
+  h[t] = y[static_cast<size_t>(b) * ld + i] + __half2float(x16[t]);
+}
+
+__global__ void residual32_kernel(const float* __restrict__ y, int ld, const float* __restrict__ h, __half* x16, int d,
+                                  int B) {
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (t >= static_cast<long long>(B) * d) return;
+  const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
+  x16[t] = __float2half_rn(y[static_cast<size_t>(b) * ld + i] + h[t]);
+}
+
+__global__ void swiglu_kernel(const float* __restrict__ y, int ld, __half* __restrict__ act, int F, int B) {
+  const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (t >= static_cast<long long>(B) * F) return;
+  const int b = static_cast<int>(t / F), j = static_cast<int>(t % F);
+  const int p = j / 16, r = j % 16;  // gate row tile 2p, up row tile 2p + 1 of the interleaved pack
+  const float* yb = y + static_cast<size_t>(b) * ld;
+  const float g = yb[32 * p + r], u = yb[32 * p + 16 + r];
+  act[t] = __float2half_rn(silu(g) * u);
+}
+
+constexpr int kArgThreads = 512;
+
+__global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
+    const float* __restrict__ logits, int V, const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log,
+    int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int si[kArgThreads / 32];
+  __shared__ int s_tok;
+  const float* lb = logits + static_cast<size_t>(b) * V;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < V; i += kArgThreads) {
+    const float v = lb[i];
+    if (v > bv) { bv = v; bi = i; }  // ascending per thread: the first of equal values stays
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kArgThreads / 32; ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+    const uint32_t pos = q0[b];
+    const uint32_t p1 = pos + 1;
+    uint32_t f = force_next[b];
+    force_next[b] = kTokenUnset;
+    if (f == kTokenUnset && p1 < static_cast<uint32_t>(cap)) f = log[static_cast<size_t>(b) * cap + p1];
+    uint32_t tk = f != kTokenUnset ? f : static_cast<uint32_t>(bi);
+    if (tk >= static_cast<uint32_t>(V)) {
+      atomicOr(err, kErrBadToken);
+      tk = 0;
+    }
+    if (p1 < static_cast<uint32_t>(cap)) log[static_cast<size_t>(b) * cap + p1] = tk;
+    q0[b] = p1 < static_cast<uint32_t>(cap) ? p1 : static_cast<uint32_t>(cap - 1);
+    tok_out[b] = static_cast<int32_t>(tk);
+    s_tok = static_cast<int>(tk);
+  }
+  __syncthreads();
+  const uint4* src = reinterpret_cast<const uint4*>(embed + static_cast<size_t>(s_tok) * d);
+  uint4* dst = reinterpret_cast<uint4*>(x16 + static_cast<size_t>(b) * d);
+  for (int i = tid; i < d / 8; i += kArgThreads) dst[i] = src[i];
+}
+
+inline unsigned blocks_for(long long n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+}  // namespace
+
+int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
+                       const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
+                       __half* vc, int B, cudaStream_t s) {
+  rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
+      y, ld, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_residual16(const float* y, int ld, const __half* x16, float* h, int d, int B, cudaStream_t s) {
+  residual16_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, ld, x16, h, d, B);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_residual32(const float* y, int ld, const float* h, __half* x16, int d, int B, cudaStream_t s) {
+  residual32_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, ld, h, x16, d, B);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_t s) {
+  swiglu_kernel<<<blocks_for(static_cast<long long>(B) * F, 256), 256, 0, s>>>(y, ld, act, F, B);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
+                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s) {
+  argmax_gen_kernel<<<B, kArgThreads, 0, s>>>(logits, V, embed, d, q0, log, cap, tok, force_next, x16, err);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace agxc

@@ -285,8 +285,8 @@ int agxc_qmm(agxc_ctx* ctx, const agxc_pack* pack, const void* x_dev, int batch,
     ksplit = 1;
     while (tiles * ksplit * 2 <= ctx->num_sms && G % (ksplit * 2) == 0) ksplit *= 2;
   }
-  if (ksplit > 1)
-    for (int b = 0; b < batch; ++b) AGXC_CUDA(cudaMemsetAsync(y_dev + static_cast<size_t>(b) * ldy, 0, pack->n * 4, s));
+  if (ksplit > 1)  // the CTAs add their K ranges into y: one 2-D clear of the [batch][n] rows
+    AGXC_CUDA(cudaMemset2DAsync(y_dev, static_cast<size_t>(ldy) * 4, 0, static_cast<size_t>(pack->n) * 4, batch, s));
   return launch_qmm(ctx, pack, x_dev, batch, y_dev, ldy, ksplit, s);
 }
 

@@ -157,6 +157,16 @@ int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);
 // A TMA map over fp16 activation rows X [B][K]: boxes of 64 columns x B rows, 128-byte swizzle.
 int encode_act_map(CUtensorMap* m, const void* x, int B, int K);
 
+// ---- the per-row steps of the batched decode step (batched.cu)
+int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
+                       const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
+                       __half* vc, int B, cudaStream_t s);
+int launch_residual16(const float* y, int ld, const __half* x16, float* h, int d, int B, cudaStream_t s);
+int launch_residual32(const float* y, int ld, const float* h, __half* x16, int d, int B, cudaStream_t s);
+int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_t s);
+int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
+                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s);
+
 // ---- the batched GEMM (qmm.cu): Y [B][ldy] fp32 = X [B][K] fp16 W^T, B = 32..256 (multiple of 16), tcgen05 + TMEM
 int qmm_configure(const agxc_ctx* ctx);
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,

@@ -42,7 +42,9 @@ struct agxc_model {
   __half* q16 = nullptr;        // [B][H][hd]
   __half* attn = nullptr;       // [B][H*hd]
   __half* act = nullptr;        // [B][F]
-  float* logits = nullptr;      // [B][V] (keep_logits)
+  float* logits = nullptr;      // [B][V] (keep_logits; always for batch >= 32)
+  __half* xn16 = nullptr;       // batch >= 32: normed GEMM input [B][d]
+  float* ybuf = nullptr;        // batch >= 32: GEMM output rows [B][max(qkv rows, 2F, d)]
   uint32_t* q0 = nullptr;       // [B]
   uint32_t* log = nullptr;      // [B][cap]
   int32_t* tok = nullptr;       // [B]
@@ -227,9 +229,69 @@ int enqueue_step_persistent(agxc_model* m, cudaStream_t s) {
   return step_launch(sp, m->d.bits, m->d.head_dim, m->ctx->num_sms, s);
 }
 
+// The batched step (batch >= 32): RMSNorm -> tensor-core GEMM -> per-row kernel for each projection, attention
+// between. With `ev`, events bracket the six kinds (qkv = norm + GEMM + RoPE/append; attn; wo = GEMM + residual; ffn =
+// norm + GEMM + SwiGLU; down = GEMM + residual; head = norm + GEMM + argmax/generation).
+int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
+  const agxc_model_desc& D = m->d;
+  const int B = D.batch, d = D.d_model, F = D.ffn, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim;
+  int rc;
+  int kind = 0;
+  auto open = [&]() -> int {
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * kind], s));
+    return 0;
+  };
+  auto close = [&]() -> int {
+    if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * kind + 1], s));
+    ++kind;
+    return 0;
+  };
+  auto gemm = [&](const agxc_pack& pk, const __half* x, float* y, int ld) -> int {
+    const int tiles = pk.n / 128, G = pk.k / 64;
+    int ks = 1;
+    while (tiles * ks * 2 <= m->ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
+    if (ks > 1) AGXC_CUDA(cudaMemset2DAsync(y, static_cast<size_t>(ld) * 4, 0, static_cast<size_t>(pk.n) * 4, B, s));
+    return launch_qmm(m->ctx, &pk, x, B, y, ld, ks, s);
+  };
+  const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  m->launches = 0;
+  for (int l = 0; l < D.n_layers; ++l) {
+    QmvParams p, q, g, w;
+    AttnParams a;
+    layer_params(m, l, p, a, q, g, w);
+    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, p.norm_gain, D.eps, m->xn16, s)) ||
+        (rc = gemm(m->qkv[l], m->xn16, m->ybuf, m->qkv_rows)) ||
+        (rc = launch_rope_append(m->ybuf, m->qkv_rows, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, H, KVH, hd,
+                                 D.cap, qscale, m->q16, p.kcache, p.vcache, B, s)) ||
+        (rc = close()))
+      return rc;
+    a.pdl = 0;
+    if ((rc = open()) || (rc = launch_attention(m->ctx, a, s)) || (rc = close())) return rc;
+    if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d)) ||
+        (rc = launch_residual16(m->ybuf, d, m->x16, m->h, d, B, s)) || (rc = close()))
+      return rc;
+    if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s)) ||
+        (rc = gemm(m->gu[l], m->xn16, m->ybuf, 2 * F)) || (rc = launch_swiglu(m->ybuf, 2 * F, m->act, F, B, s)) ||
+        (rc = close()))
+      return rc;
+    if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d)) ||
+        (rc = launch_residual32(m->ybuf, d, m->h, m->x16, d, B, s)) || (rc = close()))
+      return rc;
+  }
+  if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
+      (rc = gemm(m->head, m->xn16, m->logits, D.vocab)) ||
+      (rc = launch_argmax_gen(m->logits, D.vocab, m->embed, d, m->q0, m->log, D.cap, m->tok, m->force_next, m->x16,
+                              m->ctx->err_dev, B, s)) ||
+      (rc = close()))
+    return rc;
+  m->launches = 11 * D.n_layers + 3;  // kernels (the split-K zero fills are memset nodes)
+  return 0;
+}
+
 // When `ev` is given, an event is recorded before and after every launch (kind order: qkv, attn, wo, ffn, down per
 // layer, then head): ev holds 2 * launches events.
 int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
+  if (m->d.batch >= 32) return enqueue_step_batched(m, s, ev);
   if (!ev && m->persistent && m->step_ok) return enqueue_step_persistent(m, s);
   const agxc_model_desc& D = m->d;
   int rc;
@@ -298,7 +360,12 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if (D.d_model % 64 || D.ffn % 64 || (D.n_heads * D.head_dim) % 64)
     return fail(AGXC_EINVAL, "model: d_model, ffn and heads*head_dim must be multiples of 64");
   if (D.ffn % 16 || D.vocab % 16 || D.vocab < 16) return fail(AGXC_EINVAL, "model: vocab must be a multiple of 16");
-  if (D.batch < 1 || D.batch > 8) return fail(AGXC_EINVAL, "model: batch 1..8");
+  const bool batched = D.batch >= 32;
+  if (D.batch < 1 || (D.batch > 8 && !batched) || D.batch > 256 || (batched && D.batch % 16))
+    return fail(AGXC_EINVAL, "model: batch 1..8 (GEMV), or 32..256 in steps of 16 (tensor-core GEMM)");
+  if (batched && (D.d_model % 128 || D.ffn % 64 || ((D.n_heads + 2 * D.n_kv_heads) * D.head_dim) % 128 ||
+                  D.vocab % 128))
+    return fail(AGXC_EINVAL, "model: batch >= 32 needs d_model, qkv rows and vocab multiples of 128");
   if (D.cap < 2) return fail(AGXC_EINVAL, "model: cap >= 2");
   if (D.n_layers < 1) return fail(AGXC_EINVAL, "model: at least one layer");
   if (D.d_model % 8) return fail(AGXC_EINVAL, "model: d_model multiple of 8");
@@ -356,7 +423,13 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if ((rc = dalloc_t(m, &m->q16, static_cast<size_t>(B) * m->attn_dim))) return bail(rc);
   if ((rc = dalloc_t(m, &m->attn, static_cast<size_t>(B) * m->attn_dim))) return bail(rc);
   if ((rc = dalloc_t(m, &m->act, static_cast<size_t>(B) * F))) return bail(rc);
-  if (D.keep_logits && (rc = dalloc_t(m, &m->logits, static_cast<size_t>(B) * V))) return bail(rc);
+  if ((D.keep_logits || batched) && (rc = dalloc_t(m, &m->logits, static_cast<size_t>(B) * V))) return bail(rc);
+  if (batched) {  // the tensor-core GEMMs' normed fp16 inputs and fp32 output rows
+    const size_t yn = std::max({static_cast<size_t>(m->qkv_rows), static_cast<size_t>(2) * F,
+                                static_cast<size_t>(d)});
+    if ((rc = dalloc_t(m, &m->xn16, static_cast<size_t>(B) * d))) return bail(rc);
+    if ((rc = dalloc_t(m, &m->ybuf, static_cast<size_t>(B) * yn))) return bail(rc);
+  }
   if ((rc = dalloc_t(m, &m->q0, B))) return bail(rc);
   if ((rc = dalloc_t(m, &m->log, static_cast<size_t>(B) * D.cap))) return bail(rc);
   if ((rc = dalloc_t(m, &m->tok, B))) return bail(rc);
@@ -365,17 +438,18 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if ((rc = dalloc_t(m, &m->sin_t, static_cast<size_t>(D.cap) * hd / 2))) return bail(rc);
 
   // plans and scratch
-  m->p_qkv = plan_qmv(ctx, m->qkv_rows, d, D.bits, B, EPI_QKV, hd, 0);
-  m->p_wo = plan_qmv(ctx, d, m->attn_dim, D.bits, B, EPI_RES1, hd, 0);
-  m->p_gu = plan_qmv(ctx, 2 * F, d, D.bits, B, EPI_SWIGLU, hd, 0);
-  m->p_down = plan_qmv(ctx, d, F, D.bits, B, EPI_RES2, hd, 0);
-  m->p_head = plan_qmv(ctx, V, d, D.bits, B, EPI_ARGMAX, hd, 0);
+  const int nbg = std::min(B, 8);  // the GEMV plans (batch >= 32 runs the tensor-core GEMM instead)
+  m->p_qkv = plan_qmv(ctx, m->qkv_rows, d, D.bits, nbg, EPI_QKV, hd, 0);
+  m->p_wo = plan_qmv(ctx, d, m->attn_dim, D.bits, nbg, EPI_RES1, hd, 0);
+  m->p_gu = plan_qmv(ctx, 2 * F, d, D.bits, nbg, EPI_SWIGLU, hd, 0);
+  m->p_down = plan_qmv(ctx, d, F, D.bits, nbg, EPI_RES2, hd, 0);
+  m->p_head = plan_qmv(ctx, V, d, D.bits, nbg, EPI_ARGMAX, hd, 0);
   m->attn_S = attn_splits(ctx, B, D.n_kv_heads, D.cap);
   size_t part = 0;
-  part = std::max(part, qmv_part_floats(m->p_qkv, m->qkv_rows, B, EPI_QKV));
-  part = std::max(part, qmv_part_floats(m->p_wo, d, B, EPI_RES1));
-  part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, B, EPI_SWIGLU));
-  part = std::max(part, qmv_part_floats(m->p_down, d, B, EPI_RES2));
+  part = std::max(part, qmv_part_floats(m->p_qkv, m->qkv_rows, nbg, EPI_QKV));
+  part = std::max(part, qmv_part_floats(m->p_wo, d, nbg, EPI_RES1));
+  part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, nbg, EPI_SWIGLU));
+  part = std::max(part, qmv_part_floats(m->p_down, d, nbg, EPI_RES2));
   if ((rc = dalloc_t(m, &m->part, std::max<size_t>(part, 64)))) return bail(rc);
   if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(std::max(m->p_head.grid, ctx->num_sms)) * 16)))
     return bail(rc);

@@ -6,13 +6,13 @@
 // rows (B = 32 .. 256), K advances by one 64-group per chunk. Per chunk:
 //   * the PRODUCER warp brings the chunk's 8 packed row tiles and their scale/bias (two 3-D TMA boxes of the pack)
 //     and the activations' 64 columns (a 2-D TMA box of X [B][K] fp16, 128-byte swizzle) into a ring stage;
-//   * four DEQUANT warps turn the tiles into fp16 weights in the MMA's canonical K-major 128-byte-swizzled layout
+//   * eight DEQUANT warps turn the tiles into fp16 weights in the MMA's canonical K-major 128-byte-swizzled layout
 //     (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes 1024 away
 //     exactly, HFMA2 applies the row's scale and bias with one rounding);
 //   * the MMA warp issues four tcgen05.mma.kind::f16 (M 128, N B, K 16) accumulating in TMEM, and commits: the
 //     commit releases the stage and the dequant buffer when the tensor core has read them.
 // After the last chunk the dequant warps read the 128 x B fp32 accumulator back with tcgen05.ld (warp w reads TMEM
-// lanes 32 (w % 4) ..) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
+// lanes 32 (w % 4) ..; the two warps of a lane quarter split the columns) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -27,8 +27,9 @@ namespace agxc {
 namespace {
 
 constexpr int kM = 128;          // weight rows per CTA (the MMA's M)
-constexpr int kThreads = 192;    // warp 0 producer, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
-constexpr int kDeqWarps = 4;
+constexpr int kThreads = 320;    // warp 0 producer, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
+constexpr int kDeqWarps = 8;
+constexpr int kDeqBufs = 8;      // fp16 weight tiles in flight between the dequant warps and the tensor core
 
 struct QmmParams {
   const uint8_t* w = nullptr;
@@ -49,10 +50,10 @@ struct QmmSmem {
 __host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages) {
   QmmSmem L;
   const int TB = bits == 4 ? 512 : 1024;
-  L.bars = 0;                                   // raw_full[S], raw_empty[S], deq_full[2], deq_empty[2], acc_full
-  L.tmem_slot = 512;
-  L.deq = 1024;                                 // two fp16 weight tiles of 128 x 64 (16 KB each)
-  L.stage0 = L.deq + 2 * kM * 128;
+  L.bars = 0;                                   // raw_full[S], raw_empty[S], deq_full[D], deq_empty[D], acc_full
+  L.tmem_slot = 512;                            // (S <= 16: the barriers fit below)
+  L.deq = 1024;                                 // kDeqBufs fp16 weight tiles of 128 x 64 (16 KB each)
+  L.stage0 = L.deq + kDeqBufs * kM * 128;
   L.x_off = 0;                                  // X tile: B rows x 128 B (1,024-aligned for the swizzle)
   L.w_off = (B * 128 + 1023) / 1024 * 1024;
   L.sb_off = L.w_off + 8 * TB;
@@ -180,8 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* raw_empty = raw_full + S;
   uint64_t* deq_full = raw_empty + S;
-  uint64_t* deq_empty = deq_full + 2;
-  uint64_t* acc_full = deq_empty + 2;
+  uint64_t* deq_empty = deq_full + kDeqBufs;
+  uint64_t* acc_full = deq_empty + kDeqBufs;
   volatile int* dead = reinterpret_cast<volatile int*>(acc_full + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], 1);
     }
-    for (int d = 0; d < 2; ++d) {
+    for (int d = 0; d < kDeqBufs; ++d) {
       mbar_init(&deq_full[d], kDeqWarps);
       mbar_init(&deq_empty[d], 1);
     }
@@ -244,8 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(p.B);
       for (int i = 0; i < gper; ++i) {
-        const int s = i % S, d = i & 1;
-        if (*dead || !mbar_wait_bounded(&deq_full[d], (i >> 1) & 1, p.err)) {
+        const int s = i % S, d = i % kDeqBufs;
+        if (*dead || !mbar_wait_bounded(&deq_full[d], (i / kDeqBufs) & 1, p.err)) {
           *dead = 1;
           break;
         }
@@ -269,22 +270,19 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
     }
   } else {
     // ---- dequant warps, then the epilogue
-    const int dw = warp - 2;  // 0..3
+    const int dw = warp - 2;  // 0..7
     for (int i = 0; i < gper; ++i) {
-      const int s = i % S, d = i & 1;
+      const int s = i % S, d = i % kDeqBufs;
       const bool ok1 = !*dead && mbar_wait_bounded(&raw_full[s], (i / S) & 1, p.err);
-      const bool ok2 = ok1 && (i < 2 || mbar_wait_bounded(&deq_empty[d], ((i >> 1) - 1) & 1, p.err));
+      const bool ok2 =
+          ok1 && (i < kDeqBufs || mbar_wait_bounded(&deq_empty[d], ((i / kDeqBufs) - 1) & 1, p.err));
       if (!__all_sync(0xffffffffu, ok2)) {  // the warp leaves together
         *dead = 1;
         break;
       }
       const uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
       uint8_t* deq = smem + L.deq + d * kM * 128;
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {  // 8 row tiles x 32 lanes = 256 tasks over 128 threads
-        const int task = dw * 64 + q * 32 + lane;  // tile = task / 32
-        dequant_task<BITS>(st + L.w_off, st + L.sb_off, deq, task >> 5, task & 31, p.sdt);
-      }
+      dequant_task<BITS>(st + L.w_off, st + L.sb_off, deq, dw, lane, p.sdt);  // warp dw: row tile dw
       fence_proxy_async();  // the tensor core reads what these generic stores wrote
       __syncwarp();
       if (lane == 0) mbar_arrive1(&deq_full[d]);
@@ -296,7 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       const int q4 = warp & 3;
       const int row = tile * kM + 32 * q4 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
-      for (int c0 = 0; c0 < p.B; c0 += 16) {
+      const int half = (p.B / 16 + 1) / 2 * 16;  // columns of the first warp of the quarter
+      const int cb = dw < 4 ? 0 : half, ce = dw < 4 ? half : p.B;
+      for (int c0 = cb; c0 < ce; c0 += 16) {
         uint32_t v[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -355,8 +355,9 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
   QmmParams p;
   p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.G = G; p.bits = pk->bits; p.sdt = pk->sdt;
   p.B = B; p.ksplit = ksplit; p.y = y; p.ldy = ldy; p.err = ctx->err_dev;
-  // as many stages as fit beside the two dequant tiles (at most 8)
-  p.stages = 8;
+  // as many stages as fit beside the dequant tiles (at most 16: a stage cycles through the copy, the dequant and the
+  // MMA's completion before it is refilled, so small stages want many)
+  p.stages = 16;
   while (p.stages > 2 && qmm_layout(pk->bits, B, p.stages).total + 1024 > ctx->max_smem_optin - 2048) --p.stages;
   const int smem = qmm_layout(pk->bits, B, p.stages).total + 1024;
   // maps: the pack's tiles and scale/bias as boxes of 1 group x 8 row tiles; X [B][K] fp16 as 64 x B boxes

@@ -52,8 +52,9 @@ def configure(config):
         raise ValueError("configure: bits 4 or 8")
     if cfg["scale_dtype"] not in Q.SCALE_DTYPES:
         raise ValueError("configure: scale_dtype fp16 or bf16")
-    if not 1 <= int(cfg["batch"]) <= 8:
-        raise ValueError("configure: batch 1..8")
+    B = int(cfg["batch"])
+    if not (1 <= B <= 8 or (32 <= B <= 256 and B % 16 == 0)):
+        raise ValueError("configure: batch 1..8 (GEMV step), or 32..256 in steps of 16 (tensor-core GEMM step)")
     return cfg
 
 

@@ -9,8 +9,9 @@ warm-up steps, then K greedy decode steps at positions 1,792 .. 1,792+K-1. A ste
 of the 121 kernels. Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB of KV per token against a 126 MB L2),
 so no flush is needed between steps.
 
-    python bench.py --kernel-case ffn|qkv|wo|down|head|attn   one launch of that kernel of the workload (after 3
-                                                               warm-ups) through the C-ABI: the ncu capture case
+    python bench.py --kernel-case ffn|qkv|wo|down|head|attn [--case-batch B]
+        one launch of that kernel of the workload (after 3 warm-ups) through the C-ABI: the ncu capture case
+        (B >= 32: the batched tensor-core GEMM agxc_qmm on the kernel's shape)
 
 One JSON line on rank 0:
   value          tokens/s over the K timed steps (device time, CUDA events, inputs resident in HBM), summed over ranks
@@ -46,6 +47,8 @@ CONFIGS = {
     "internlm-q4-196": ("internlm2.5-1.8b", 4, 1, 196),
     "internlm-q8-1792": ("internlm2.5-1.8b", 8, 1, 1792),
     "internlm-q8-1792-b8": ("internlm2.5-1.8b", 8, 8, 1792),
+    "internlm-q4-1792-b32": ("internlm2.5-1.8b", 4, 32, 1792),     # tensor-core GEMM step (batch >= 32)
+    "internlm-q4-1792-b128": ("internlm2.5-1.8b", 4, 128, 1792),
     "qwen-q4-196": ("qwen2.5-0.5b", 4, 1, 196),
 }
 METRIC = "decode tok/s and % HBM roofline (batch 1, ctx 1792, 4-bit) vs CPU ref"
@@ -198,6 +201,19 @@ def kernel_case(args, rank):
         q = (torch.randn(batch, S.HEADS, S.HEAD_DIM, device="cuda") * 0.1).half()
         for _ in range(4):
             A.attention(q, K, V, [hist] * batch)
+    elif (args.case_batch or batch) >= 32:
+        # the batched tensor-core GEMM (agxc_qmm) on the kernel's shape (gate/up as one plain 2F-row pack)
+        from agxforge_b200.kernels.qmm import qmm
+        B = args.case_batch or batch
+        shapes = {r: (n, k) for r, n, k in S.matrices()}
+        n, k = {"qkv": shapes["qkv"], "wo": shapes["wo"], "ffn": (2 * shapes["gate"][0], shapes["gate"][1]),
+                "down": shapes["down"], "head": (S.VOCAB, S.D_MODEL)}[args.kernel_case]
+        W = torch.randn(n, k, device="cuda") * 0.02
+        pk = Q.Pack(*Q.quantize(W, bits=bits), n, k, bits=bits)
+        del W
+        x = torch.randn(B, k, device="cuda").half()
+        for _ in range(4):
+            qmm(pk, x)
     else:
         shapes = {r: (n, k) for r, n, k in S.matrices()}
         n, k = {"qkv": shapes["qkv"], "wo": shapes["wo"], "ffn": shapes["gate"], "down": shapes["down"],
@@ -212,12 +228,13 @@ def kernel_case(args, rank):
             pk = Q.Pack(*Q.quantize(W, bits=bits), n, k, bits=bits)
             epi = "f32"
         del W
-        x = torch.randn(batch, k, device="cuda").half()
+        x = torch.randn(args.case_batch or batch, k, device="cuda").half()
         for _ in range(4):
             Q.qmv(pk, x, epi=epi)
     torch.cuda.synchronize()
     if rank == 0:
-        print(json.dumps(dict(kernel_case=args.kernel_case, config=args.config, launches=4)), flush=True)
+        print(json.dumps(dict(kernel_case=args.kernel_case, config=args.config, batch=args.case_batch or batch,
+                              launches=4)), flush=True)
 
 
 def main():
@@ -232,6 +249,8 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-case", choices=KIND_NAMES, default=None)
+    ap.add_argument("--case-batch", type=int, default=0,
+                    help="activation rows of --kernel-case (default: the config's batch; >= 32 = tensor-core qmm)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

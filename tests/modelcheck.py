@@ -61,13 +61,12 @@ def run_forced(m, prompts, steps, seed=0):
     return seqs, lg, toks
 
 
-def compare(m, seqs, lg, steps, check_argmax=True, min_margin_factor=4.0):
-    """Per sequence: the oracle's logits at the last `steps` positions; returns a report dict and asserts the bound
-    and (where the oracle's top-2 margin clears the observed error) the argmax."""
+def compare(m, seqs, lg, steps, check_argmax=True, min_margin_factor=4.0, which=None):
+    """Per sequence (all, or the indices in `which`): the oracle's logits at the last `steps` positions; returns a
+    report dict and asserts the bound and (where the oracle's top-2 margin clears the observed error) the argmax."""
     om = oracle_model(m)
-    B = m.batch
     report = []
-    for b in range(B):
+    for b in (range(m.batch) if which is None else which):
         toks = seqs[b][: len(seqs[b]) - 1]            # the tokens fed at each position
         T = len(toks)
         pos = list(range(T - steps, T))
