@@ -23,6 +23,7 @@ OPT_PDL = 0
 OPT_TRACE = 1
 OPT_PERSISTENT = 2
 OPT_BULK = 3
+OPT_WAIT_MS = 4
 
 
 class PackDesc(C.Structure):
@@ -43,7 +44,8 @@ class ModelDesc(C.Structure):
                 ("head_dim", C.c_int32), ("ffn", C.c_int32), ("vocab", C.c_int32), ("bits", C.c_int32),
                 ("group", C.c_int32), ("scale_dtype", C.c_int32), ("cap", C.c_int32), ("batch", C.c_int32),
                 ("qkv_bias", C.c_int32), ("eps", C.c_float), ("rope_theta", C.c_float),
-                ("keep_logits", C.c_int32)]
+                ("keep_logits", C.c_int32), ("tp_world", C.c_int32), ("tp_rank", C.c_int32),
+                ("tp_id", C.c_uint8 * 128)]
 
 
 class Timing(C.Structure):
@@ -72,6 +74,8 @@ SIGNATURES = {
     "agxc_rmsnorm_dev": (_I, [_P, _P, _I, _I, _I, _P, C.c_float, _P, _P]),
     "agxc_attention_dev": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
+    "agxc_tp_unique_id": (_I, [_P]),
+    "agxc_model_vocab_slice": (_I, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "agxc_model_free": (None, [_P]),
     "agxc_model_set_pack": (_I, [_P, _I, _I, _P, _P, _P, _I]),
     "agxc_model_set_vector": (_I, [_P, _I, _I, _P, C.c_size_t, _I]),

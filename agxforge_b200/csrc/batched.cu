@@ -8,6 +8,7 @@
 //   swiglu        act = fp16(silu(gate) * up) over the interleaved gate/up row tiles (qmv.py:214-226)
 //   argmax_gen    per sequence: the first maximum of the logits, then the generation step (argmax.py:141-215,
 //                 assemble.py:918-930): forced token, else the logged one, else the argmax; log, q0 + 1, x16 = emb[tok]
+//   argmax_part / gen_from_pairs   the same split around an all-gather when the vocabulary is sliced over ranks
 #include <cmath>
 
 #include "common.cuh"
@@ -88,16 +89,12 @@ __global__ void swiglu_kernel(const float* __restrict__ y, int ld, __half* __res
 
 constexpr int kArgThreads = 512;
 
-__global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
-    const float* __restrict__ logits, int V, const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log,
-    int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
-  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float sv[kArgThreads / 32];
-  __shared__ int si[kArgThreads / 32];
-  __shared__ int s_tok;
-  const float* lb = logits + static_cast<size_t>(b) * V;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
+// The first maximum of one sequence's logits over the block: (value, index + v0) in every thread's registers.
+__device__ __forceinline__ void block_first_max(const float* __restrict__ lb, int V, int v0, float* sv, int* si,
+                                                float& bv, int& bi) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  bv = -INFINITY;
+  bi = 0x7fffffff;
   for (int i = tid; i < V; i += kArgThreads) {
     const float v = lb[i];
     if (v > bv) { bv = v; bi = i; }  // ascending per thread: the first of equal values stays
@@ -110,15 +107,24 @@ __global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
   }
   if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
   __syncthreads();
+  bv = sv[0];
+  bi = si[0];
+  for (int w = 1; w < kArgThreads / 32; ++w)
+    if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+  if (bi != 0x7fffffff) bi += v0;
+}
+
+// The generation step of sequence b given its argmax `best` (thread 0), then x16[b] = embed[token] (all threads).
+__device__ void gen_step(int b, int best, int V, const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log,
+                         int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err, int* s_tok) {
+  const int tid = threadIdx.x;
   if (tid == 0) {
-    for (int w = 1; w < kArgThreads / 32; ++w)
-      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
     const uint32_t pos = q0[b];
     const uint32_t p1 = pos + 1;
     uint32_t f = force_next[b];
     force_next[b] = kTokenUnset;
     if (f == kTokenUnset && p1 < static_cast<uint32_t>(cap)) f = log[static_cast<size_t>(b) * cap + p1];
-    uint32_t tk = f != kTokenUnset ? f : static_cast<uint32_t>(bi);
+    uint32_t tk = f != kTokenUnset ? f : static_cast<uint32_t>(best);
     if (tk >= static_cast<uint32_t>(V)) {
       atomicOr(err, kErrBadToken);
       tk = 0;
@@ -126,12 +132,59 @@ __global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
     if (p1 < static_cast<uint32_t>(cap)) log[static_cast<size_t>(b) * cap + p1] = tk;
     q0[b] = p1 < static_cast<uint32_t>(cap) ? p1 : static_cast<uint32_t>(cap - 1);
     tok_out[b] = static_cast<int32_t>(tk);
-    s_tok = static_cast<int>(tk);
+    *s_tok = static_cast<int>(tk);
   }
   __syncthreads();
-  const uint4* src = reinterpret_cast<const uint4*>(embed + static_cast<size_t>(s_tok) * d);
+  const uint4* src = reinterpret_cast<const uint4*>(embed + static_cast<size_t>(*s_tok) * d);
   uint4* dst = reinterpret_cast<uint4*>(x16 + static_cast<size_t>(b) * d);
-  for (int i = tid; i < d / 8; i += kArgThreads) dst[i] = src[i];
+  for (int i = tid; i < d / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+__global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
+    const float* __restrict__ logits, int V, const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log,
+    int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int si[kArgThreads / 32];
+  __shared__ int s_tok;
+  const int b = blockIdx.x;
+  float bv;
+  int bi;
+  block_first_max(logits + static_cast<size_t>(b) * V, V, 0, sv, si, bv, bi);
+  gen_step(b, bi, V, embed, d, q0, log, cap, tok_out, force_next, x16, err, &s_tok);
+}
+
+// Tensor parallel head, step 1: the first maximum of this rank's vocabulary slice [v0, v0 + V) of sequence b as a
+// (value bits, global index) pair.
+__global__ void __launch_bounds__(kArgThreads) argmax_part_kernel(const float* __restrict__ logits, int V, int v0,
+                                                                 uint32_t* pairs) {
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int si[kArgThreads / 32];
+  const int b = blockIdx.x;
+  float bv;
+  int bi;
+  block_first_max(logits + static_cast<size_t>(b) * V, V, v0, sv, si, bv, bi);
+  if (threadIdx.x == 0) {
+    pairs[2 * b] = __float_as_uint(bv);
+    pairs[2 * b + 1] = static_cast<uint32_t>(bi);
+  }
+}
+
+// Step 2, after the all-gather of every rank's pairs ([ranks][B][2], slices in ascending vocabulary order): the
+// largest value, the lowest index among equal values (= the first maximum over the whole vocabulary), then the
+// generation step, identically on every rank.
+__global__ void gen_from_pairs_kernel(const uint32_t* __restrict__ pairs, int ranks, int B, int V,
+                                      const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log, int cap,
+                                      int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
+  __shared__ int s_tok;
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int r = 0; r < ranks; ++r) {
+    const float v = __uint_as_float(pairs[(static_cast<size_t>(r) * B + b) * 2]);
+    const int i = static_cast<int>(pairs[(static_cast<size_t>(r) * B + b) * 2 + 1]);
+    if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+  }
+  gen_step(b, bi, V, embed, d, q0, log, cap, tok_out, force_next, x16, err, &s_tok);
 }
 
 inline unsigned blocks_for(long long n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
@@ -168,6 +221,20 @@ int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_
 int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
                       int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s) {
   argmax_gen_kernel<<<B, kArgThreads, 0, s>>>(logits, V, embed, d, q0, log, cap, tok, force_next, x16, err);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int B, cudaStream_t s) {
+  argmax_part_kernel<<<B, kArgThreads, 0, s>>>(logits, V, v0, pairs);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
+                          uint32_t* log, int cap, int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B,
+                          cudaStream_t s) {
+  gen_from_pairs_kernel<<<B, 256, 0, s>>>(pairs, ranks, B, V, embed, d, q0, log, cap, tok, force_next, x16, err);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

@@ -167,6 +167,21 @@ int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_
 int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
                       int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s);
 
+int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int B, cudaStream_t s);
+int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
+                          uint32_t* log, int cap, int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B,
+                          cudaStream_t s);
+
+// ---- tensor parallelism (tp.cu): NCCL loaded at run time
+struct TpComm;
+int tp_unique_id(void* out128);
+int tp_comm_create(int world, int rank, const void* id128, TpComm** out);
+void tp_comm_free(TpComm* c);
+int tp_allreduce_f32(TpComm* c, float* buf, size_t n, cudaStream_t s);
+int tp_allgather_u32(TpComm* c, const uint32_t* send, uint32_t* recv, size_t n, cudaStream_t s);
+// Wait for `done` at most timeout_ms; past it abort the communicator and return AGXC_ETIMEOUT.
+int tp_wait(TpComm* c, cudaEvent_t done, int timeout_ms);
+
 // ---- the batched GEMM (qmm.cu): Y [B][ldy] fp32 = X [B][K] fp16 W^T, B = 32..256 (multiple of 16), tcgen05 + TMEM
 int qmm_configure(const agxc_ctx* ctx);
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,

@@ -84,6 +84,14 @@ struct agxc_model {
   size_t h_force_n = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   std::vector<void*> allocs;
+  // tensor parallelism: m->d holds this rank's LOCAL shape (heads, KV heads, ffn, vocabulary slice)
+  int tp = 1, tp_rank = 0;
+  int vt = 0;                   // the global vocabulary (token ids, the embedding table)
+  int v0 = 0;                   // the first global token id of this rank's vocabulary slice
+  agxc::TpComm* comm = nullptr;
+  uint32_t* amax = nullptr;     // [B][2] this rank's (value bits, global index) per sequence
+  uint32_t* amax_all = nullptr; // [tp][B][2] every rank's, after the all-gather
+  int wait_ms = 60000;
 };
 
 namespace agxc {
@@ -268,6 +276,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     a.pdl = 0;
     if ((rc = open()) || (rc = launch_attention(m->ctx, a, s)) || (rc = close())) return rc;
     if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d)) ||
+        (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
         (rc = launch_residual16(m->ybuf, d, m->x16, m->h, d, B, s)) || (rc = close()))
       return rc;
     if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s)) ||
@@ -275,8 +284,21 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
         (rc = close()))
       return rc;
     if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d)) ||
+        (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
         (rc = launch_residual32(m->ybuf, d, m->h, m->x16, d, B, s)) || (rc = close()))
       return rc;
+  }
+  if (m->comm) {  // vocabulary sliced over ranks: local first maxima, all-gathered, then the same choice everywhere
+    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
+        (rc = gemm(m->head, m->xn16, m->logits, D.vocab)) ||
+        (rc = launch_argmax_part(m->logits, D.vocab, m->v0, m->amax, B, s)) ||
+        (rc = tp_allgather_u32(m->comm, m->amax, m->amax_all, static_cast<size_t>(2) * B, s)) ||
+        (rc = launch_gen_from_pairs(m->amax_all, m->tp, m->vt, m->embed, d, m->q0, m->log, D.cap, m->tok,
+                                    m->force_next, m->x16, m->ctx->err_dev, B, s)) ||
+        (rc = close()))
+      return rc;
+    m->launches = 11 * D.n_layers + 4;  // this library's kernels (the collectives are the communicator's)
+    return 0;
   }
   if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
       (rc = gemm(m->head, m->xn16, m->logits, D.vocab)) ||
@@ -326,6 +348,13 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
   return launch_gemv(hp, m->p_head, EPI_ARGMAX);
 }
 
+// Wait for an event recorded after a step (or a call's steps): bounded and aborting under tensor parallelism.
+int wait_done(agxc_model* m, cudaEvent_t e) {
+  if (m->comm) return tp_wait(m->comm, e, m->wait_ms);
+  AGXC_CUDA(cudaEventSynchronize(e));
+  return 0;
+}
+
 int ensure_graph(agxc_model* m) {
   if (m->exec) return 0;
   cudaStream_t s = m->ctx->stream;
@@ -349,6 +378,8 @@ int ensure_graph(agxc_model* m) {
 
 }  // namespace
 
+int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_model** out);
+
 int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   const agxc_model_desc& D = *desc;
   if (D.bits != 4 && D.bits != 8) return fail(AGXC_EINVAL, "model: bits must be 4 or 8");
@@ -369,10 +400,47 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if (D.cap < 2) return fail(AGXC_EINVAL, "model: cap >= 2");
   if (D.n_layers < 1) return fail(AGXC_EINVAL, "model: at least one layer");
   if (D.d_model % 8) return fail(AGXC_EINVAL, "model: d_model multiple of 8");
+  const int T = D.tp_world > 1 ? D.tp_world : 1;
+  if (D.tp_world < 0 || T > 8 || D.tp_rank < 0 || D.tp_rank >= T)
+    return fail(AGXC_EINVAL, "model: tp_world 0..8 and 0 <= tp_rank < tp_world");
+  if (T > 1) {
+    if (!batched) return fail(AGXC_EINVAL, "model: tensor parallelism needs batch >= 32 (the tensor-core GEMM step)");
+    if (D.n_heads % T || D.n_kv_heads % T || D.ffn % (64 * T))
+      return fail(AGXC_EINVAL, "model: tensor parallelism needs heads and KV heads divisible by tp_world, ffn by 64 "
+                               "x tp_world");
+  }
+  return model_create_local(ctx, D, T, out);
+}
+
+// The rank's vocabulary slice of the head, in 128-row tiles: [first, first + count).
+void vocab_slice(int vocab, int world, int rank, int* first, int* count) {
+  const int tiles = vocab / 128;
+  const int t0 = static_cast<int>(static_cast<int64_t>(tiles) * rank / world);
+  const int t1 = static_cast<int>(static_cast<int64_t>(tiles) * (rank + 1) / world);
+  *first = world > 1 ? 128 * t0 : 0;
+  *count = world > 1 ? 128 * (t1 - t0) : vocab;
+}
+
+int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_model** out) {
+  agxc_model_desc D = G;  // this rank's local shape
+  int v0 = 0, vn = G.vocab;
+  vocab_slice(G.vocab, T, T > 1 ? G.tp_rank : 0, &v0, &vn);
+  D.n_heads = G.n_heads / T;
+  D.n_kv_heads = G.n_kv_heads / T;
+  D.ffn = G.ffn / T;
+  D.vocab = vn;
+  const bool batched = D.batch >= 32;
+  if (vn < 128 && T > 1) return fail(AGXC_EINVAL, "model: fewer 128-row vocabulary tiles than ranks");
+  if (batched && ((D.n_heads + 2 * D.n_kv_heads) * D.head_dim) % 128)
+    return fail(AGXC_EINVAL, "model: batch >= 32 needs each rank's qkv rows a multiple of 128");
 
   agxc_model* m = new agxc_model();
   m->ctx = ctx;
   m->d = D;
+  m->tp = T;
+  m->tp_rank = T > 1 ? G.tp_rank : 0;
+  m->vt = G.vocab;
+  m->v0 = v0;
   const int L = D.n_layers, d = D.d_model, F = D.ffn, V = D.vocab, B = D.batch, hd = D.head_dim;
   m->qkv_rows = (D.n_heads + 2 * D.n_kv_heads) * hd;
   m->attn_dim = D.n_heads * hd;
@@ -414,7 +482,7 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if ((rc = dalloc_t(m, &m->gains, static_cast<size_t>(L) * 2 * d))) return bail(rc);
   if ((rc = dalloc_t(m, &m->bias, static_cast<size_t>(L) * m->qkv_rows))) return bail(rc);
   if ((rc = dalloc_t(m, &m->final_gain, d))) return bail(rc);
-  if ((rc = dalloc_t(m, &m->embed, static_cast<size_t>(V) * d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->embed, static_cast<size_t>(m->vt) * d))) return bail(rc);
   const size_t kv = static_cast<size_t>(L) * B * D.n_kv_heads * D.cap * hd;
   if ((rc = dalloc_t(m, &m->kcache, kv))) return bail(rc);
   if ((rc = dalloc_t(m, &m->vcache, kv))) return bail(rc);
@@ -508,6 +576,19 @@ int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess)
     return bail(fail(AGXC_ECUDA, "model: event create failed"));
   if (cudaStreamSynchronize(s) != cudaSuccess) return bail(fail(AGXC_ECUDA, "model: setup sync failed"));
+  if (T > 1) {  // collective: every rank gets here; one warm-up of each collective before any graph capture
+    if ((rc = dalloc_t(m, &m->amax, static_cast<size_t>(2) * B))) return bail(rc);
+    if ((rc = dalloc_t(m, &m->amax_all, static_cast<size_t>(2) * B * T))) return bail(rc);
+    if ((rc = tp_comm_create(T, m->tp_rank, G.tp_id, &m->comm))) return bail(rc);
+    if (cudaMemsetAsync(m->ybuf, 0, static_cast<size_t>(B) * d * 4, s) != cudaSuccess ||
+        cudaMemsetAsync(m->amax, 0, static_cast<size_t>(2) * B * 4, s) != cudaSuccess)
+      return bail(fail(AGXC_ECUDA, "model: memset"));
+    if ((rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s)) ||
+        (rc = tp_allgather_u32(m->comm, m->amax, m->amax_all, static_cast<size_t>(2) * B, s)))
+      return bail(rc);
+    if (cudaEventRecord(m->ev1, s) != cudaSuccess) return bail(fail(AGXC_ECUDA, "model: event record"));
+    if ((rc = wait_done(m, m->ev1))) return bail(rc);
+  }
   *out = m;
   return 0;
 }
@@ -561,7 +642,7 @@ int model_set_vector(agxc_model* m, int layer, int which, const void* data, size
       dst = m->gains + static_cast<size_t>(layer) * 2 * D.d_model + D.d_model; want = D.d_model * 2; break;
     case AGXC_VEC_QKV_BIAS: dst = m->bias + static_cast<size_t>(layer) * m->qkv_rows; want = m->qkv_rows * 2; break;
     case AGXC_VEC_FINAL_GAIN: dst = m->final_gain; want = D.d_model * 2; break;
-    case AGXC_VEC_EMBED: dst = m->embed; want = static_cast<size_t>(D.vocab) * D.d_model * 2; break;
+    case AGXC_VEC_EMBED: dst = m->embed; want = static_cast<size_t>(m->vt) * D.d_model * 2; break;
     default: return fail(AGXC_EINVAL, "set_vector: unknown vector");
   }
   if (which <= AGXC_VEC_QKV_BIAS && (layer < 0 || layer >= D.n_layers)) return fail(AGXC_EINVAL, "set_vector: layer");
@@ -582,7 +663,7 @@ int model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
   if (b < 0 || b >= D.batch) return fail(AGXC_EINVAL, "start: sequence index");
   if (n < 1 || n > D.cap) return fail(AGXC_EINVAL, "start: prompt length must be 1..cap");
   for (int i = 0; i < n; ++i)
-    if (prompt[i] < 0 || prompt[i] >= D.vocab) return fail(AGXC_EINVAL, "start: token id out of range");
+    if (prompt[i] < 0 || prompt[i] >= m->vt) return fail(AGXC_EINVAL, "start: token id out of range");
   cudaStream_t s = m->ctx->stream;
   const size_t seq_kv = static_cast<size_t>(D.n_kv_heads) * D.cap * D.head_dim;
   for (int l = 0; l < D.n_layers; ++l) {
@@ -606,7 +687,7 @@ int model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {
   const agxc_model_desc& D = m->d;
   if (b < 0 || b >= D.batch || pos < 0 || n < 0 || pos + n > D.cap) return fail(AGXC_EINVAL, "force: range");
   for (int i = 0; i < n; ++i)
-    if (tokens[i] < 0 || tokens[i] >= D.vocab) return fail(AGXC_EINVAL, "force: token id out of range");
+    if (tokens[i] < 0 || tokens[i] >= m->vt) return fail(AGXC_EINVAL, "force: token id out of range");
   AGXC_CUDA(cudaMemcpy(m->log + static_cast<size_t>(b) * D.cap + pos, tokens, static_cast<size_t>(n) * 4,
                        cudaMemcpyHostToDevice));
   return 0;
@@ -633,17 +714,18 @@ int model_fill_history(agxc_model* m, int b, int n, uint64_t seed) {
   for (int l = 0; l < D.n_layers; ++l)
     for (int kv = 0; kv < D.n_kv_heads; ++kv) {
       const size_t off = ((static_cast<size_t>(l) * D.batch + b) * D.n_kv_heads + kv) * D.cap * D.head_dim;
+      const uint64_t g = static_cast<uint64_t>(m->tp_rank) * D.n_kv_heads + kv;  // the global KV head
       if (row) {
         fill_normal_kernel<<<static_cast<unsigned>((row + 255) / 256), 256, 0, s>>>(m->kcache + off, row,
-                                                                                   seed * 131 + l * 17 + kv * 2);
+                                                                                   seed * 131 + l * 17 + g * 2);
         fill_normal_kernel<<<static_cast<unsigned>((row + 255) / 256), 256, 0, s>>>(m->vcache + off, row,
-                                                                                   seed * 131 + l * 17 + kv * 2 + 1);
+                                                                                   seed * 131 + l * 17 + g * 2 + 1);
       }
     }
   AGXC_CUDA(cudaGetLastError());
   std::mt19937_64 rng(seed);
   std::vector<uint32_t> log(D.cap, kTokenUnset);
-  for (int i = 0; i <= n; ++i) log[i] = static_cast<uint32_t>(rng() % static_cast<uint64_t>(D.vocab));
+  for (int i = 0; i <= n; ++i) log[i] = static_cast<uint32_t>(rng() % static_cast<uint64_t>(m->vt));
   AGXC_CUDA(cudaMemcpyAsync(m->log + static_cast<size_t>(b) * D.cap, log.data(), D.cap * 4, cudaMemcpyHostToDevice, s));
   const uint32_t q0 = static_cast<uint32_t>(n);
   AGXC_CUDA(cudaMemcpyAsync(m->q0 + b, &q0, 4, cudaMemcpyHostToDevice, s));
@@ -661,7 +743,8 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
   if (forced_in) {
     for (size_t i = 0; i < static_cast<size_t>(steps) * D.batch; ++i) {
       const uint32_t f = static_cast<uint32_t>(forced_in[i]);
-      if (f != kTokenUnset && f >= static_cast<uint32_t>(D.vocab)) return fail(AGXC_EINVAL, "decode: forced token out of range");
+      if (f != kTokenUnset && f >= static_cast<uint32_t>(m->vt))
+        return fail(AGXC_EINVAL, "decode: forced token out of range");
     }
     const size_t nf = static_cast<size_t>(std::max(steps, 1)) * D.batch;
     if (m->h_force_n < nf) {
@@ -696,10 +779,13 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
     if (logits_out)
       AGXC_CUDA(cudaMemcpyAsync(logits_out + static_cast<size_t>(i) * D.batch * D.vocab, m->logits,
                                 static_cast<size_t>(D.batch) * D.vocab * 4, cudaMemcpyDeviceToHost, s));
-    if (sync_each) AGXC_CUDA(cudaStreamSynchronize(s));
+    if (sync_each) {
+      AGXC_CUDA(cudaEventRecord(m->ev1, s));
+      if ((rc = wait_done(m, m->ev1))) return rc;
+    }
   }
   AGXC_CUDA(cudaEventRecord(m->ev1, s));
-  AGXC_CUDA(cudaEventSynchronize(m->ev1));
+  if ((rc = wait_done(m, m->ev1))) return rc;
   const auto h1 = std::chrono::steady_clock::now();
   if (tokens_out) std::memcpy(tokens_out, m->h_tok, static_cast<size_t>(steps) * D.batch * 4);
   uint32_t err = 0;
@@ -737,7 +823,10 @@ int model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_launch
   for (int i = 0; i < steps && !rc; ++i) {
     rc = enqueue_step(m, s, ev.data());
     if (rc) break;
-    if (cudaStreamSynchronize(s) != cudaSuccess) { rc = fail(AGXC_ECUDA, "profile: sync failed"); break; }
+    if (cudaEventRecord(m->ev1, s) != cudaSuccess || (rc = wait_done(m, m->ev1))) {
+      if (!rc) rc = fail(AGXC_ECUDA, "profile: sync failed");
+      break;
+    }
     for (int j = 0; j < per_step; ++j) {
       float ms = 0.f;
       cudaEventElapsedTime(&ms, ev[2 * j], ev[2 * j + 1]);
@@ -761,6 +850,7 @@ void model_free(agxc_model* m) {
   if (m->h_force) cudaFreeHost(m->h_force);
   if (m->trace) cudaFree(m->trace);
   if (m->cta_trace) cudaFree(m->cta_trace);
+  tp_comm_free(m->comm);  // after the graphs that hold its collectives
   for (void* p : m->allocs) cudaFree(p);
   delete m;
 }
@@ -850,6 +940,13 @@ int agxc_model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_l
   return agxc::model_profile(m, steps, kind_ms, kind_launches);
 }
 
+int agxc_model_vocab_slice(const agxc_model* m, int32_t* offset, int32_t* count) {
+  if (!m || !offset || !count) return agxc::fail(AGXC_EINVAL, "vocab_slice: null argument");
+  *offset = m->v0;
+  *count = m->d.vocab;
+  return 0;
+}
+
 int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
   if (!m || !buf || !len) return agxc::fail(AGXC_EINVAL, "plan_info: bad argument");
   auto one = [](const char* name, const agxc::QmvPlan& p) {
@@ -864,7 +961,11 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
                   "}, \"pdl\": " + std::to_string(m->pdl) + ", \"persistent\": {\"on\": " +
                   std::to_string(m->persistent && m->step_ok) + ", \"fits\": " + std::to_string(m->step_ok) +
                   ", \"ring_stages\": " + std::to_string(m->step_ring) + ", \"grid\": " +
-                  std::to_string(m->ctx->num_sms) + "}}";
+                  std::to_string(m->ctx->num_sms) + "}, \"tp\": {\"world\": " + std::to_string(m->tp) +
+                  ", \"rank\": " + std::to_string(m->tp_rank) + ", \"heads\": " + std::to_string(m->d.n_heads) +
+                  ", \"kv_heads\": " + std::to_string(m->d.n_kv_heads) + ", \"ffn\": " +
+                  std::to_string(m->d.ffn) + ", \"vocab_offset\": " + std::to_string(m->v0) +
+                  ", \"vocab_count\": " + std::to_string(m->d.vocab) + "}}";
   std::snprintf(buf, len, "%s", j.c_str());
   return 0;
 }
@@ -900,6 +1001,10 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
     m->pdl = value;
   } else if (option == AGXC_OPT_BULK) {
     m->bulk = value ? 1 : 0;
+  } else if (option == AGXC_OPT_WAIT_MS) {
+    if (value < 1) return agxc::fail(AGXC_EINVAL, "set_option: wait_ms must be positive");
+    m->wait_ms = value;
+    return 0;  // no graph change
   } else if (option == AGXC_OPT_PERSISTENT) {
     m->persistent = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {

@@ -2,7 +2,9 @@
 agxforge/inference/assemble.py: configure 71-92, build 596-828; its region R and token log 650-669).
 
     configure(config)           a config dict (or JSON path): {"model": name | shape overrides, "bits", "scale_dtype",
-                                "cap", "batch", "seed", "keep_logits"}; returns the normalised config
+                                "cap", "batch", "seed", "keep_logits", "tp", "tp_rank"}; returns the normalised config
+                                (tp > 1: tensor parallel over tp ranks, one process per GPU, torch.distributed
+                                initialised; each rank builds its shard of the same seeded weights, see tp.py)
     build(config, ...)          a DecodeModel: the library's model object with every pack, gain, bias and the
                                 embedding set. Synthetic weights are generated on the device from the config's seed
                                 (N(0, 0.02) fp32, then the device quantiser), or taken from given reference-format
@@ -24,6 +26,7 @@ import numpy as np
 
 from agxforge_b200 import _native as N
 from agxforge_b200.inference import models
+from agxforge_b200.inference import tp as TP
 from agxforge_b200.kernels import qmv as Q
 
 ROLE = {"qkv": N.ROLE_QKV, "wo": N.ROLE_WO, "gate": N.ROLE_GATE, "up": N.ROLE_UP, "down": N.ROLE_DOWN,
@@ -55,6 +58,11 @@ def configure(config):
     B = int(cfg["batch"])
     if not (1 <= B <= 8 or (32 <= B <= 256 and B % 16 == 0)):
         raise ValueError("configure: batch 1..8 (GEMV step), or 32..256 in steps of 16 (tensor-core GEMM step)")
+    cfg["tp"] = int(cfg.get("tp") or 1)
+    cfg["tp_rank"] = int(cfg.get("tp_rank") or 0)
+    TP.check(shape, cfg["tp"], B)
+    if not 0 <= cfg["tp_rank"] < cfg["tp"]:
+        raise ValueError("configure: 0 <= tp_rank < tp")
     return cfg
 
 
@@ -77,7 +85,7 @@ def hash_key(*key):
 class DecodeModel:
     """The device model (owns the library's model object)."""
 
-    def __init__(self, cfg, device=0):
+    def __init__(self, cfg, device=0, tp_id=None):
         import torch
         if not torch.cuda.is_available():
             raise RuntimeError("agxforge_b200 needs a CUDA device (B200); none is visible")
@@ -90,10 +98,19 @@ class DecodeModel:
         d = N.ModelDesc(S.D_MODEL, S.LAYERS, S.HEADS, S.KV_HEADS, S.HEAD_DIM, S.FFN, S.VOCAB, self.bits, 64,
                         Q.SCALE_DTYPES[cfg["scale_dtype"]], self.cap, self.batch, int(S.QKV_BIAS), float(S.EPS),
                         float(S.ROPE_THETA), int(bool(cfg["keep_logits"])))
+        self.tp, self.tp_rank = int(cfg.get("tp", 1)), int(cfg.get("tp_rank", 0))
+        if self.tp > 1:
+            if tp_id is None or len(tp_id) != 128:
+                raise ValueError("DecodeModel: tensor parallelism needs the 128-byte communicator id (tp.exchange_id)")
+            d.tp_world, d.tp_rank = self.tp, self.tp_rank
+            C.memmove(d.tp_id, bytes(tp_id), 128)
         h = C.c_void_p()
         torch.cuda.set_device(device)
         N.check(N.lib().agxc_model_create(N.context(device), C.byref(d), C.byref(h)), "model_create")
         self._h = h
+        off, cnt = C.c_int32(), C.c_int32()
+        N.check(N.lib().agxc_model_vocab_slice(h, C.byref(off), C.byref(cnt)), "vocab_slice")
+        self.vocab_offset, self.vocab_count = off.value, cnt.value
         self.packs = None   # reference-format packs kept on the host when build(keep_packs=True)
 
     @property
@@ -134,8 +151,10 @@ class DecodeModel:
         "trace"
         (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace());
         "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off); "bulk" (GEMV weights
-        by plain bulk copies instead of TMA tensor boxes)."""
-        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT, "bulk": N.OPT_BULK}
+        by plain bulk copies instead of TMA tensor boxes); "wait_ms" (tensor parallel: the host's bound on a decode
+        call, past which the communicator is aborted and TimeoutError raised; default 60000)."""
+        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT, "bulk": N.OPT_BULK,
+                "wait_ms": N.OPT_WAIT_MS}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")
@@ -207,7 +226,7 @@ class DecodeModel:
 
     def decode(self, steps, forced=None, want_tokens=True, want_logits=False, sync_each=False):
         """Run `steps` steps. Returns (tokens [steps, batch] or None, logits [steps, batch, V] or None, timing dict)."""
-        B, V = self.batch, self.shape.VOCAB
+        B, V = self.batch, self.vocab_count   # the rank's vocabulary slice under tensor parallelism
         toks = np.zeros((steps, B), np.int32) if want_tokens else None
         lg = np.zeros((steps, B, V), np.float32) if want_logits else None
         fin = None
@@ -248,7 +267,9 @@ def build(config, device=0, weights=None, keep_packs=False):
     import torch
     cfg = configure(config)
     S = cfg["shape"]
-    m = DecodeModel(cfg, device)
+    world, rank = cfg["tp"], cfg["tp_rank"]
+    tp_id = TP.exchange_id(world, rank) if world > 1 else None
+    m = DecodeModel(cfg, device, tp_id=tp_id)
     bits, sdt, seed = m.bits, cfg["scale_dtype"], cfg["seed"]
     weights = weights or {}
     kept = {} if keep_packs else None
@@ -276,7 +297,7 @@ def build(config, device=0, weights=None, keep_packs=False):
             p = weights.get((l, role))
             if p is None:
                 p = synthetic_pack(torch, n, k, bits, sdt, _gen(torch, seed, l, role), cfg["init_std"], device)
-            m.set_pack(l, role, *p)
+            m.set_pack(l, role, *TP.shard_pack(role, p, S, bits, world, rank))
             keep_pack((l, role), p)
         for vec in ("attn_gain", "ffn_gain"):
             v = weights.get((l, vec))
@@ -289,7 +310,7 @@ def build(config, device=0, weights=None, keep_packs=False):
             if v is None:
                 v = (torch.randn((S.QKV,), generator=_gen(torch, seed, l, "bias"), device="cuda:%d" % device)
                      * cfg["bias_std"]).to(torch.float16)
-            m.set_vector(l, "qkv_bias", v)
+            m.set_vector(l, "qkv_bias", TP.shard_bias(v, S, world, rank))
             if kept is not None:
                 kept[(l, "qkv_bias")] = host(v).astype(np.float16)
     p = weights.get((None, "head"))
@@ -299,7 +320,7 @@ def build(config, device=0, weights=None, keep_packs=False):
             p = Q.quantize(e32, bits=bits, scale_dtype=sdt, device=device)
         else:
             p = synthetic_pack(torch, S.VOCAB, S.D_MODEL, bits, sdt, _gen(torch, seed, "head"), cfg["init_std"], device)
-    m.set_pack(0, "head", *p)
+    m.set_pack(0, "head", *TP.shard_pack("head", p, S, bits, world, rank))
     keep_pack((None, "head"), p)
     fg = weights.get("final_gain")
     if fg is not None:

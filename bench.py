@@ -49,9 +49,14 @@ CONFIGS = {
     "internlm-q8-1792-b8": ("internlm2.5-1.8b", 8, 8, 1792),
     "internlm-q4-1792-b32": ("internlm2.5-1.8b", 4, 32, 1792),     # tensor-core GEMM step (batch >= 32)
     "internlm-q4-1792-b128": ("internlm2.5-1.8b", 4, 128, 1792),
+    "internlm-q8-1792-b32": ("internlm2.5-1.8b", 8, 32, 1792),
+    "internlm-q8-1792-b128": ("internlm2.5-1.8b", 8, 128, 1792),
+    # tensor parallel over all ranks (--gpus N = TP N; strong scaling: the same 64 sequences at every N)
+    "internlm7b-q4-8192-b64-tp": ("internlm2.5-7b", 4, 64, 8192),
     "qwen-q4-196": ("qwen2.5-0.5b", 4, 1, 196),
 }
 METRIC = "decode tok/s and % HBM roofline (batch 1, ctx 1792, 4-bit) vs CPU ref"
+TP_CONFIGS = {"internlm7b-q4-8192-b64-tp"}
 KIND_NAMES = ["qkv", "attn", "wo", "ffn", "down", "head"]
 
 
@@ -274,16 +279,18 @@ def main():
     model, bits, batch, hist = CONFIGS[args.config]
     K, W = args.steps, args.warmup
     cap = hist + K + 8
+    tp = world if args.config in TP_CONFIGS else 1
+    rseed = 0 if tp > 1 else rank        # tensor parallel ranks hold shards of ONE model and the same sequences
     keep = args.ref_layers if (rank == 0 and not args.no_cpu) else False
-    m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=2 + rank), device=local,
-                       keep_packs=keep)
+    m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=2 + rseed, tp=tp,
+                            tp_rank=rank if tp > 1 else 0), device=local, keep_packs=keep)
     S = m.shape
-    rng = np.random.default_rng(1792 + rank)
+    rng = np.random.default_rng(1792 + rseed)
     # the history: positions 0 .. hist - W - 1 filled on the device (seeded), a random current token; then W warm-up
     # steps at positions hist - W .. hist - 1; the timed steps are at positions hist .. hist + K - 1
     for b in range(batch):
         m.start(b, [int(rng.integers(0, S.VOCAB))])
-        m.fill_history(b, hist - W, seed=1792 + 7 * rank + b)
+        m.fill_history(b, hist - W, seed=1792 + 7 * rseed + b)
     m.decode(W, want_tokens=False)
     torch.cuda.synchronize()
 
@@ -304,7 +311,8 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         gpu_ms = float(tt.item())
         dist.barrier()
-    tok_s = world * batch * K / (gpu_ms / 1e3)
+    replicas = world if tp == 1 else 1
+    tok_s = replicas * batch * K / (gpu_ms / 1e3)
 
     # ---- e2e: the same number of steps through the C-ABI decode call, host input and output every step
     if dist is not None:
@@ -317,7 +325,7 @@ def main():
         tt = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_s = float(tt.item())
-    e2e_tok_s = world * batch * K / e2e_s
+    e2e_tok_s = replicas * batch * K / e2e_s
 
     # ---- per-kernel profile (CUDA events around every launch, no overlap) -> the dominant kernel's roofline
     import ctypes as C
@@ -326,19 +334,19 @@ def main():
     kind_n = (C.c_int32 * 6)()
     N.check(N.lib().agxc_model_profile(m.handle, args.profile_steps, kind_ms, kind_n), "profile")
     pos_mid = hist + K + K + args.profile_steps // 2  # the profiled steps follow the timed and the e2e steps
-    kvrow = 2 * S.KV_HEADS * S.HEAD_DIM * 2                      # K+V bytes per position per layer
-    from agxforge_b200.inference.models import Model  # noqa: F401
-    mats = {r: (n, k) for r, n, k in S.matrices()}
+    # this rank's shapes (the whole model at tp 1)
+    hl, kvl, fl, hd, d = S.HEADS // tp, S.KV_HEADS // tp, S.FFN // tp, S.HEAD_DIM, S.D_MODEL
+    kvrow = 2 * kvl * hd * 2                                       # K+V bytes per position per layer
 
     def pack_bytes(n, k):
         return n * k * bits // 8 + (n * k // 64) * 4
     kind_bytes = {
-        "qkv": pack_bytes(*mats["qkv"]) * batch ** 0,
+        "qkv": pack_bytes((hl + 2 * kvl) * hd, d),
         "attn": batch * kvrow * (pos_mid + 1),
-        "wo": pack_bytes(*mats["wo"]),
-        "ffn": pack_bytes(*mats["gate"]) + pack_bytes(*mats["up"]),
-        "down": pack_bytes(*mats["down"]),
-        "head": pack_bytes(S.VOCAB, S.D_MODEL),
+        "wo": pack_bytes(d, hl * hd),
+        "ffn": 2 * pack_bytes(fl, d),
+        "down": pack_bytes(d, fl),
+        "head": pack_bytes(m.vocab_count, d),
     }
     total_ms = sum(kind_ms[i] for i in range(6))
     dom = max(range(6), key=lambda i: kind_ms[i])
@@ -378,10 +386,12 @@ def main():
     if rank == 0:
         line = dict(
             metric=METRIC, value=round(tok_s, 2), unit="tok/s", n_gpus=world, steps=K, warmup=W,
-            ms_per_step=round(gpu_ms / K, 4), higher_is_better=True, scaling="weak", vs_baseline=None, dtype="u4" if
+            ms_per_step=round(gpu_ms / K, 4), higher_is_better=True, scaling="strong" if tp > 1 else "weak",
+            vs_baseline=None, dtype="u4" if
             bits == 4 else "u8", data="synthetic (seeded random-init weights and uniform-random token ids)",
             config=dict(workload=args.config, model=model, bits=bits, group=64, scale_dtype="fp16", batch=batch,
-                        history=hist, positions=[hist, hist + K - 1], parallelism="replicas" if world > 1 else "1gpu",
+                        history=hist, positions=[hist, hist + K - 1],
+                        parallelism=("tp%d" % tp) if tp > 1 else ("replicas" if world > 1 else "1gpu"),
                         l2="inputs larger than L2 (%.2f GB per step vs 126 MB L2)" % (step_bytes / 1e9)),
             e2e=dict(value=round(e2e_tok_s, 2), unit="tok/s", h2d_bytes_per_step=4 * batch,
                      d2h_bytes_per_step=4 * batch),

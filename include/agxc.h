@@ -149,11 +149,29 @@ typedef struct {
   int32_t d_model, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab;
   int32_t bits, group, scale_dtype;
   int32_t cap;                /* KV capacity and token-log length per sequence */
-  int32_t batch;              /* independent sequences decoded together, 1..8 */
+  int32_t batch;              /* independent sequences decoded together: 1..8 (GEMV step) or 32..256 in steps of 16
+                                 (tensor-core GEMM step; d_model, qkv rows and vocab multiples of 128) */
   int32_t qkv_bias;           /* 1 = the qkv projection has a bias (Qwen2) */
   float eps, rope_theta;
   int32_t keep_logits;        /* 1 = keep the head's fp32 logits [batch][vocab] readable after each step */
+  /* Tensor parallelism (no counterpart in the reference, which runs one device): tp_world ranks, one process per
+   * GPU, each holding n_heads/tp_world query heads and n_kv_heads/tp_world KV heads (qkv rows of those heads, their
+   * KV cache), ffn/tp_world gate/up rows and down columns, the o_proj columns of its heads, and a vocabulary slice of
+   * the head in 128-row tiles (agxc_model_vocab_slice). The shapes above stay GLOBAL; set_pack takes the rank's
+   * slice of each reference-format pack. The o_proj and down partial sums are all-reduced (fp32 sum) before their
+   * residual, and the head's per-rank first maxima are all-gathered before the token choice, so every rank holds the
+   * same residual stream, token log and q0. Needs batch >= 32, heads, KV heads divisible by tp_world and ffn by
+   * 64 * tp_world. tp_world 0 or 1 = one device. tp_id = the communicator id from agxc_tp_unique_id on rank 0, the
+   * same bytes on every rank. Creation is collective: every rank calls agxc_model_create. */
+  int32_t tp_world, tp_rank;
+  uint8_t tp_id[128];
 } agxc_model_desc;
+
+/* A fresh communicator id (128 bytes) for a tensor-parallel model (rank 0 makes it, the caller sends it to the other
+ * ranks). The collective library (NCCL, libnccl.so.2) is loaded on first use; AGXC_EUNSUPPORTED without it. */
+AGXC_API int agxc_tp_unique_id(void* id128);
+/* The rank's vocabulary slice of the head: global token ids [offset, offset + count). */
+AGXC_API int agxc_model_vocab_slice(const agxc_model* m, int32_t* offset, int32_t* count);
 
 #define AGXC_ROLE_QKV 0
 #define AGXC_ROLE_WO 1
@@ -192,7 +210,8 @@ AGXC_API int agxc_model_fill_history(agxc_model* m, int b, int n, uint64_t seed)
  * `forced_in` (host, [steps][batch], AGXC_TOKEN_UNSET = none; copied host -> device before the step) if given and
  * set, else the token log's entry at q0 + 1 (the prompt), else the first argmax of the logits. After each step the
  * chosen tokens are device-resident; when `tokens_out` (host, [steps][batch]) is non-NULL each step's tokens are
- * copied back, and when `logits_out` (host, [steps][batch][vocab], needs keep_logits) is non-NULL, the logits too.
+ * copied back, and when `logits_out` (host, [steps][batch][vocab], needs keep_logits) is non-NULL, the logits too
+ * (under tensor parallelism [steps][batch][count]: the rank's vocabulary slice).
  * `sync_each` = 1 waits for every step (the host sees each token before the next launch). */
 typedef struct {
   float gpu_ms;               /* device time of the steps (CUDA events) */
@@ -235,6 +254,9 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
                                  for batch > 1) */
 #define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
                                  a chunk); 0 (default): by 3-D TMA tensor boxes */
+#define AGXC_OPT_WAIT_MS 4     /* tensor parallel: host bound (ms, default 60000) on a decode call's completion; past it
+                                 the communicator is aborted (its kernels end) and the call returns AGXC_ETIMEOUT, so a
+                                 rank that died between steps cannot hold the others' GPUs */
 AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
 
 /* The launch trace accumulated since tracing started or the last read (min and max over all steps in between), then
