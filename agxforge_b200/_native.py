@@ -48,6 +48,12 @@ class ModelDesc(C.Structure):
                 ("tp_id", C.c_uint8 * 128)]
 
 
+class EncoderDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("layers", C.c_int32), ("heads", C.c_int32), ("ffn", C.c_int32),
+                ("vocab", C.c_int32), ("max_position", C.c_int32), ("type_vocab", C.c_int32), ("eps", C.c_float),
+                ("max_batch", C.c_int32), ("max_seq", C.c_int32)]
+
+
 class Timing(C.Structure):
     _fields_ = [("gpu_ms", C.c_float), ("host_ms", C.c_float), ("launches_per_step", C.c_int32)]
 
@@ -75,6 +81,12 @@ SIGNATURES = {
     "agxc_attention_dev": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "agxc_tp_unique_id": (_I, [_P]),
+    "agxc_hgemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P, _P, _P, _P]),
+    "agxc_encoder_create": (_I, [_P, C.POINTER(EncoderDesc), C.POINTER(_P)]),
+    "agxc_encoder_free": (None, [_P]),
+    "agxc_encoder_set_param": (_I, [_P, _I, _I, _P, C.c_size_t, _I]),
+    "agxc_encoder_forward": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, C.POINTER(Timing)]),
+    "agxc_encoder_profile": (_I, [_P, _I, _I, _I, _P, _P]),
     "agxc_model_vocab_slice": (_I, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "agxc_model_free": (None, [_P]),
     "agxc_model_set_pack": (_I, [_P, _I, _I, _P, _P, _P, _I]),

@@ -124,6 +124,10 @@ int agxc_init(int device, agxc_ctx** out) {
     agxc_ctx_free(c);
     return rc;
   }
+  if (int rc = encoder_configure(c)) {
+    agxc_ctx_free(c);
+    return rc;
+  }
   *out = c;
   return 0;
 }

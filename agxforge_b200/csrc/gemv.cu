@@ -74,12 +74,15 @@ int make_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, i
 
 }  // namespace
 
-int encode_act_map(CUtensorMap* m, const void* x, int B, int K) {
+int encode_act_map(CUtensorMap* m, const void* x, int B, int K) { return encode_rows_map(m, x, B, K, B); }
+
+int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows) {
   if (int rc = encode_fn()) return rc;
-  if (K % 64 || (reinterpret_cast<uintptr_t>(x) & 15)) return fail(AGXC_EINVAL, "qmm: X rows of K % 64 == 0, 16-B aligned");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(B)};
+  if (K % 64 || (reinterpret_cast<uintptr_t>(x) & 15) || box_rows < 1 || box_rows > 256)
+    return fail(AGXC_EINVAL, "tensor map: rows of K % 64 == 0 fp16, 16-B aligned, boxes of 1..256 rows");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(B)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -154,6 +154,8 @@ size_t step_smem(int kmax, int stages);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
 constexpr int kAttnKeys = 128;
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);
+// fp16 rows [rows][K] (K % 64 == 0) as boxes of 64 columns x box_rows rows, 128-byte swizzle (the UMMA K-major tile)
+int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows);
 // A TMA map over fp16 activation rows X [B][K]: boxes of 64 columns x B rows, 128-byte swizzle.
 int encode_act_map(CUtensorMap* m, const void* x, int B, int K);
 
@@ -171,6 +173,12 @@ int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int 
 int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
                           uint32_t* log, int cap, int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B,
                           cudaStream_t s);
+
+// ---- the encoder's tensor-core GEMM (encoder.cu): C [M][N] = A [M][K] W [N][K]^T (+ bias; epi 0 fp32, 1 fp16
+// GELU, 2 fp32 + residual)
+int launch_hgemm(const agxc_ctx* ctx, const __half* A, const __half* W, int M, int N, int K, const __half* bias,
+                 int epi, float* out32, __half* out16, const float* res32, cudaStream_t s);
+int encoder_configure(const agxc_ctx* ctx);
 
 // ---- tensor parallelism (tp.cu): NCCL loaded at run time
 struct TpComm;

@@ -278,6 +278,65 @@ AGXC_API int agxc_model_plan_info(agxc_model* m, char* buf, size_t len);
 /* Kernels per decode step and their names (for launch accounting). */
 AGXC_API int agxc_model_kernel_count(agxc_model* m, int32_t* n);
 
+/* ---- the BERT sentence encoder (MiniLM; tools/g17inferencereference.py:18-99 graph_reference over the graph of
+ * agxforge/g17/inferencegraph.py:208-289 import_graph with sentence pooling; lowered stages
+ * tools/g17inferencelower.py:56-139) ---------------------------------------------------------------------------
+ * Embedding gather + LayerNorm, per layer q/k/v/o and FFN linears with bias on the tensor cores (fp16 operands,
+ * fp32 accumulation), GELU (erf), padding-masked softmax attention, post-attention and post-FFN LayerNorms, then the
+ * masked mean over each sequence's valid rows and L2 normalisation. Batches of sequences [batch][seq] with 0/1
+ * masks (the reference takes one sequence of exactly 32 tokens). Parameters are fp16, in the checkpoint's layout
+ * (linear weights [out][in]). */
+typedef struct agxc_encoder agxc_encoder;
+typedef struct {
+  int32_t hidden, layers, heads, ffn, vocab, max_position, type_vocab;
+  float eps;                  /* LayerNorm epsilon (MiniLM: 1e-12) */
+  int32_t max_batch, max_seq; /* activation buffers are sized for max_batch x max_seq tokens */
+} agxc_encoder_desc;
+
+#define AGXC_ENC_WORD 0       /* [vocab][hidden] */
+#define AGXC_ENC_POSITION 1   /* [max_position][hidden] */
+#define AGXC_ENC_TOKEN_TYPE 2 /* [type_vocab][hidden] */
+#define AGXC_ENC_EMB_LN_W 3   /* [hidden] embeddings.LayerNorm */
+#define AGXC_ENC_EMB_LN_B 4
+#define AGXC_ENC_Q_W 5        /* per layer: attention.self.query.weight [hidden][hidden] */
+#define AGXC_ENC_Q_B 6
+#define AGXC_ENC_K_W 7
+#define AGXC_ENC_K_B 8
+#define AGXC_ENC_V_W 9
+#define AGXC_ENC_V_B 10
+#define AGXC_ENC_O_W 11       /* attention.output.dense */
+#define AGXC_ENC_O_B 12
+#define AGXC_ENC_LN1_W 13     /* attention.output.LayerNorm */
+#define AGXC_ENC_LN1_B 14
+#define AGXC_ENC_FFN1_W 15    /* intermediate.dense [ffn][hidden] */
+#define AGXC_ENC_FFN1_B 16
+#define AGXC_ENC_FFN2_W 17    /* output.dense [hidden][ffn] */
+#define AGXC_ENC_FFN2_B 18
+#define AGXC_ENC_LN2_W 19     /* output.LayerNorm */
+#define AGXC_ENC_LN2_B 20
+
+/* The encoder's tensor-core GEMM alone (tests): C [M][N] = A [M][K] fp16 x W [N][K]^T fp16 + bias (fp16 [N],
+ * nullable), epi 0: out32 fp32; 1: out16 = fp16(gelu_erf(.)); 2: out32 = . + res32. M % 128, N % 64, K % 64 == 0. */
+AGXC_API int agxc_hgemm_dev(agxc_ctx* ctx, const uint16_t* A, const uint16_t* W, int M, int N, int K,
+                            const uint16_t* bias, int epi, float* out32, uint16_t* out16, const float* res32,
+                            void* stream);
+AGXC_API int agxc_encoder_create(agxc_ctx* ctx, const agxc_encoder_desc* desc, agxc_encoder** out);
+AGXC_API void agxc_encoder_free(agxc_encoder* e);
+/* One fp16 parameter (layer ignored for the embedding entries); `bytes` must be its exact size. */
+AGXC_API int agxc_encoder_set_param(agxc_encoder* e, int layer, int which, const void* data, size_t bytes,
+                                    int on_device);
+/* Sentence embeddings out [batch][hidden] fp32 of token_ids [batch][seq] (int32), attention_mask [batch][seq] (0/1,
+ * at least one 1 per sequence), token_type_ids (NULL = all 0); positions 0..seq-1. on_device = 1: every pointer is
+ * device memory and the call only enqueues on the context's stream; 0: host arrays, copied in and out (the call
+ * returns when `out` holds the result). Rejects (AGXC_EINVAL) ids, types or masks outside their domain, as the
+ * reference refuses them. `t` (nullable) gets the device time of the encoder's kernels. */
+AGXC_API int agxc_encoder_forward(agxc_encoder* e, const int32_t* token_ids, const int32_t* attention_mask,
+                                  const int32_t* token_type_ids, int batch, int seq, float* out, int on_device,
+                                  agxc_timing* t);
+/* Per-stage device time of `reps` forwards (each stage timed on its own): ms[8] = embedding, qkv, attention, o_proj
+ * + residual, LayerNorms, FFN up + GELU, FFN down + residual, pooling; launches[8] their launch counts. */
+AGXC_API int agxc_encoder_profile(agxc_encoder* e, int batch, int seq, int reps, float* ms, int32_t* launches);
+
 #ifdef __cplusplus
 }
 #endif
