@@ -87,6 +87,7 @@ SIGNATURES = {
     "agxc_encoder_set_param": (_I, [_P, _I, _I, _P, C.c_size_t, _I]),
     "agxc_encoder_forward": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, C.POINTER(Timing)]),
     "agxc_encoder_profile": (_I, [_P, _I, _I, _I, _P, _P]),
+    "agxc_encoder_replay": (_I, [_P, _I, _I, C.POINTER(Timing)]),
     "agxc_model_vocab_slice": (_I, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "agxc_model_free": (None, [_P]),
     "agxc_model_set_pack": (_I, [_P, _I, _I, _P, _P, _P, _I]),

@@ -431,6 +431,7 @@ struct agxc_encoder {
   int g_batch = 0, g_seq = 0, g_types = -1;
   int launches = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  void* flush = nullptr;              // 256 MB written between timed forwards (agxc_encoder_replay)
   int32_t* h_in = nullptr;            // pinned staging: ids, mask, types
   float* h_out = nullptr;
   std::vector<void*> allocs;
@@ -769,6 +770,43 @@ int agxc_encoder_forward(agxc_encoder* e, const int32_t* token_ids, const int32_
     t->host_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - h0).count();
     t->launches_per_step = e->launches;
   }
+  return 0;
+}
+
+int agxc_encoder_replay(agxc_encoder* e, int reps, int flush_l2, agxc_timing* t) {
+  using namespace agxc;
+  if (!e || !t || reps < 1) return fail(AGXC_EINVAL, "encoder_replay: bad argument");
+  if (!e->exec) return fail(AGXC_EINVAL, "encoder_replay: no forward has run yet");
+  cudaStream_t s = e->ctx->stream;
+  constexpr size_t kFlush = size_t(256) << 20;
+  if (flush_l2 && !e->flush) {
+    void* f = nullptr;
+    if (int rc = ealloc(e, &f, kFlush)) return rc;
+    e->flush = f;
+  }
+  const auto h0 = std::chrono::steady_clock::now();
+  float total = 0.f;
+  if (!flush_l2) {
+    AGXC_CUDA(cudaEventRecord(e->ev0, s));
+    for (int i = 0; i < reps; ++i) AGXC_CUDA(cudaGraphLaunch(e->exec, s));
+    AGXC_CUDA(cudaEventRecord(e->ev1, s));
+    AGXC_CUDA(cudaEventSynchronize(e->ev1));
+    cudaEventElapsedTime(&total, e->ev0, e->ev1);
+  } else {
+    for (int i = 0; i < reps; ++i) {
+      AGXC_CUDA(cudaMemsetAsync(e->flush, i & 0xFF, kFlush, s));
+      AGXC_CUDA(cudaEventRecord(e->ev0, s));
+      AGXC_CUDA(cudaGraphLaunch(e->exec, s));
+      AGXC_CUDA(cudaEventRecord(e->ev1, s));
+      AGXC_CUDA(cudaEventSynchronize(e->ev1));
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+      total += ms;
+    }
+  }
+  t->gpu_ms = total;
+  t->host_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - h0).count();
+  t->launches_per_step = e->launches;
   return 0;
 }
 

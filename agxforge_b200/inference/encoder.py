@@ -40,6 +40,12 @@ EMBED_PARAMS = {
 }
 
 
+# BASELINE config 2's shape (sentence-transformers MiniLM-L6: the checkpoint's config.json fields)
+MINILM_L6 = dict(model_type="bert", architectures=["BertModel"], hidden_size=384, num_attention_heads=12,
+                 intermediate_size=1536, num_hidden_layers=6, vocab_size=30522, max_position_embeddings=512,
+                 type_vocab_size=2, layer_norm_eps=1e-12, hidden_act="gelu")
+
+
 def check_config(config):
     """The reference's admission of a BERT config (agxforge/g17/inferencegraph.py:116-157), plus this encoder's
     shape limits. Returns (hidden, layers, heads, ffn, vocab, max_position, type_vocab, eps)."""
@@ -221,6 +227,13 @@ class Encoder:
                                              None if types is None else C.c_void_p(types.data_ptr()), B, S,
                                              C.c_void_p(out.data_ptr()), 1, None), "encoder_forward")
         return out
+
+    def replay(self, reps, flush_l2=True):
+        """`reps` forwards on the last forward's inputs (resident on the device), L2 flushed before each when
+        flush_l2: device ms of the forwards, launches per forward."""
+        t = N.Timing()
+        N.check(N.lib().agxc_encoder_replay(self._h, int(reps), int(bool(flush_l2)), C.byref(t)), "encoder_replay")
+        return dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches=t.launches_per_step)
 
     def profile(self, batch, seq, reps=3):
         """Per-stage device time (ms summed over `reps` forwards, each launch timed on its own) and launch counts."""

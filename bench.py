@@ -57,6 +57,9 @@ CONFIGS = {
 }
 METRIC = "decode tok/s and % HBM roofline (batch 1, ctx 1792, 4-bit) vs CPU ref"
 TP_CONFIGS = {"internlm7b-q4-8192-b64-tp"}
+# the MiniLM-L6 sentence encoder, 32 sequences x 128 tokens, valid lengths uniform in 16..128
+ENCODER_CONFIGS = {"minilm-b32-s128": (32, 128)}
+ENCODER_METRIC = "encoder sentences/s (MiniLM-L6, batch 32 x seq 128, fp16 tensor cores) vs CPU ref"
 KIND_NAMES = ["qkv", "attn", "wo", "ffn", "down", "head"]
 
 
@@ -188,6 +191,113 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def encoder_inputs(B, S, seed, vocab=30522):
+    """Config 2's inputs: uniform-random ids, per-row valid lengths uniform in 16..S, 0/1 masks."""
+    rng = np.random.default_rng(seed)
+    ids = rng.integers(0, vocab, (B, S)).astype(np.int32)
+    lens = rng.integers(16, S + 1, B)
+    return ids, (np.arange(S)[None, :] < lens[:, None]).astype(np.int32)
+
+
+def encoder_cpu_sample(B, S, sample):
+    """The reference's CPU encoder (graph_reference's FP64 policy, restated in oracle/encoder.py) on `sample` of the
+    B sequences, all host threads: seconds per sentence."""
+    from oracle import encoder as E
+    params = E.make_params(1)
+    ids, mask = encoder_inputs(B, S, 1)
+    t0 = time.perf_counter()
+    E.forward(params, ids[:sample], mask[:sample], policy="fp64")
+    return (time.perf_counter() - t0) / sample, os.cpu_count()
+
+
+def run_encoder_reference(args):
+    B, S = ENCODER_CONFIGS[args.config]
+    per = [encoder_cpu_sample(B, S, 4)[0] for _ in range(max(1, args.ref_steps))]
+    v = 1.0 / statistics.median(per)
+    cores = os.cpu_count()
+    line = dict(metric=ENCODER_METRIC, impl="reference", value=round(v, 3), unit="sentences/s", n_gpus=args.gpus,
+                steps=args.steps, warmup=args.warmup, ms_per_step=round(B * 1e3 / v, 1), higher_is_better=True,
+                scaling="weak", vs_baseline=None, dtype="f64", data="synthetic",
+                config=dict(workload=args.config, model="minilm-l6", batch=B, seq=S),
+                cpu_baseline=dict(value=round(v, 3), unit="sentences/s", cores=cores, kind="port",
+                                  sample="4 of the %d sequences of one batch, FP64 graph reference, median of %d"
+                                         % (B, len(per))),
+                e2e=dict(value=round(v, 3), unit="sentences/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def run_encoder(args, rank, world, local, dist):
+    """Config 2 on each GPU (replicas only: the encoder's batches are independent)."""
+    import torch
+    from agxforge_b200.inference.encoder import MINILM_L6, Encoder
+    B, S = ENCODER_CONFIGS[args.config]
+    K, W = args.steps, args.warmup
+    enc = Encoder.synthetic(MINILM_L6, seed=1 + rank, max_batch=B, max_seq=S, device=local)
+    ids, mask = encoder_inputs(B, S, 1 + rank)
+    inputs = dict(token_ids=ids, attention_mask=mask)
+    for _ in range(W):
+        enc.forward(inputs)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clk = Clocks(local).start()
+    clk.mark_start()
+    t = enc.replay(K, flush_l2=True)       # K forwards, inputs resident, L2 flushed before each, device time
+    clk.mark_end()
+    clk.stop()
+    gpu_ms = t["gpu_ms"]
+    # e2e: the public forward call, host ids/mask in and embeddings out every batch
+    t0 = time.perf_counter()
+    for _ in range(K):
+        enc.forward(inputs)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([gpu_ms, e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        gpu_ms, e2e_s = float(tt[0].item()), float(tt[1].item())
+    value = world * B * K / (gpu_ms / 1e3)
+    e2e_v = world * B * K / e2e_s
+    prof = enc.profile(B, S, reps=3)
+    W_, F_, M = 384, 1536, B * S
+    flops = {"qkv": 2 * M * 3 * W_ * W_, "o_proj": 2 * M * W_ * W_, "ffn_up": 2 * M * F_ * W_,
+             "ffn_down": 2 * M * W_ * F_}
+    dom = max(flops, key=lambda k: prof[k]["ms"])
+    per_launch_ms = prof[dom]["ms"] / max(1, prof[dom]["launches"])
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (bf16 burst)"
+    except Exception:
+        peak, src = 1590.0, "fallback"
+    achieved = flops[dom] / (per_launch_ms / 1e3) / 1e12
+    total_flops = 6 * sum(flops.values()) + 6 * 4 * B * 12 * S * S * 32
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        per, cores = encoder_cpu_sample(B, S, 4)
+        cpu = dict(value=round(1.0 / per, 3), unit="sentences/s", cores=cores, kind="port",
+                   sample="4 of the %d sequences of one batch, FP64 graph reference (oracle/encoder.py)" % B)
+    if rank == 0:
+        line = dict(
+            metric=ENCODER_METRIC, value=round(value, 1), unit="sentences/s", n_gpus=world, steps=K, warmup=W,
+            ms_per_step=round(gpu_ms / K, 4), higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f16",
+            data="synthetic (seeded random-init parameters, uniform-random ids, valid lengths 16..128)",
+            config=dict(workload=args.config, model="minilm-l6", batch=B, seq=S,
+                        parallelism="replicas" if world > 1 else "1gpu",
+                        l2="L2 flushed (256 MB written) before every timed forward; the working set (21 MB of "
+                           "weights + activations) would otherwise stay in the 126 MB L2"),
+            e2e=dict(value=round(e2e_v, 1), unit="sentences/s", h2d_bytes_per_step=2 * B * S * 4,
+                     d2h_bytes_per_step=B * W_ * 4),
+            roofline=dict(bound="tensor", kernel=dom, achieved=round(achieved, 1), peak=peak, unit="TFLOP/s",
+                          frac=round(achieved / peak, 4), traffic=None, peak_source=src,
+                          flops_per_launch=flops[dom], us_per_launch=round(per_launch_ms * 1e3, 2)),
+            step_roofline=dict(bound="tensor", achieved=round(total_flops / (gpu_ms / K / 1e3) / 1e12, 1), peak=peak,
+                               unit="TFLOP/s", frac=round(total_flops / (gpu_ms / K / 1e3) / 1e12 / peak, 4),
+                               flops_per_step=total_flops),
+            kernels={k: dict(ms=round(v["ms"] / 3, 4), launches=v["launches"] // 3) for k, v in prof.items()},
+            cpu_baseline=cpu, clocks=clk.summary(), gpu_launches=int(t["launches"] * K))
+        print(json.dumps(line), flush=True)
+    enc.close()
+
+
 def kernel_case(args, rank):
     """One launch of one kernel of the workload, after 3 warm-up launches of it (the ncu capture case: `-k` on the
     kernel's name, `-s 3 -c 1`). GEMV kernels run through agxc_qmv on packs of the workload's shape (same planner and
@@ -248,7 +358,7 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="internlm-q4-1792", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="internlm-q4-1792", choices=sorted(CONFIGS) + sorted(ENCODER_CONFIGS))
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--profile-steps", type=int, default=4)
@@ -261,6 +371,15 @@ def main():
         ap.error("--warmup must be at least 3")
 
     rank, world, local, dist = dist_setup(args.gpus)
+    if args.config in ENCODER_CONFIGS:
+        if args.impl == "reference":
+            if rank == 0:
+                run_encoder_reference(args)
+        else:
+            run_encoder(args, rank, world, local, dist)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, rank)

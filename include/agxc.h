@@ -333,6 +333,10 @@ AGXC_API int agxc_encoder_set_param(agxc_encoder* e, int layer, int which, const
 AGXC_API int agxc_encoder_forward(agxc_encoder* e, const int32_t* token_ids, const int32_t* attention_mask,
                                   const int32_t* token_type_ids, int batch, int seq, float* out, int on_device,
                                   agxc_timing* t);
+/* `reps` forwards on the inputs of the last agxc_encoder_forward call (already on the device), one CUDA graph replay
+ * each; t->gpu_ms = their device time (CUDA events on the context's stream). flush_l2 = 1: a 256 MB buffer (twice
+ * the L2) is written between forwards and only the forwards are timed, so none starts with the weights in L2. */
+AGXC_API int agxc_encoder_replay(agxc_encoder* e, int reps, int flush_l2, agxc_timing* t);
 /* Per-stage device time of `reps` forwards (each stage timed on its own): ms[8] = embedding, qkv, attention, o_proj
  * + residual, LayerNorms, FFN up + GELU, FFN down + residual, pooling; launches[8] their launch counts. */
 AGXC_API int agxc_encoder_profile(agxc_encoder* e, int batch, int seq, int reps, float* ms, int32_t* launches);
