@@ -24,6 +24,7 @@ OPT_TRACE = 1
 OPT_PERSISTENT = 2
 OPT_BULK = 3
 OPT_WAIT_MS = 4
+OPT_TP_FUSED = 5
 
 
 class PackDesc(C.Structure):

@@ -174,7 +174,9 @@ __global__ void __launch_bounds__(kArgThreads) argmax_part_kernel(const float* _
 // generation step, identically on every rank.
 __global__ void gen_from_pairs_kernel(const uint32_t* __restrict__ pairs, int ranks, int B, int V,
                                       const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log, int cap,
-                                      int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
+                                      int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err,
+                                      unsigned* epoch) {
+  if (epoch && blockIdx.x == 0 && threadIdx.x == 0) *epoch += 1;  // the step's last kernel: the next step begins
   __shared__ int s_tok;
   const int b = blockIdx.x;
   float bv = -INFINITY;
@@ -185,6 +187,54 @@ __global__ void gen_from_pairs_kernel(const uint32_t* __restrict__ pairs, int ra
     if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
   }
   gen_step(b, bi, V, embed, d, q0, log, cap, tok_out, force_next, x16, err, &s_tok);
+}
+
+// Tensor parallel, after the GEMM's peer pushes: wait (bounded, 2 s of the global timer) until every rank's tiles
+// have arrived, then out = sum over ranks in rank order + residual, the same on every rank (the sums are
+// bit-identical everywhere because every rank adds the same slots in the same order).
+__global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, const unsigned* flag,
+                                 const unsigned* epoch, int uses_per_step, int use_in_step, int tiles,
+                                 const __half* __restrict__ res16, const float* __restrict__ res32,
+                                 float* __restrict__ out32, __half* __restrict__ out16, int d, int B, unsigned* err) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const unsigned use = *epoch * static_cast<unsigned>(uses_per_step) + static_cast<unsigned>(use_in_step);
+    const unsigned target = (use + 1u) * static_cast<unsigned>(ranks * tiles);
+    unsigned v;
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (unsigned it = 0;; ++it) {
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+      if (static_cast<int>(v - target) >= 0) break;
+      if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+        atomicOr(err, kErrMbarTimeout);
+        ok = 0;
+        break;
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  const size_t n = static_cast<size_t>(B) * d;
+  const size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4;
+  if (i >= n) return;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (s_ok) {
+    for (int r = 0; r < ranks; ++r) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(recv + r * n + i));
+      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+    }
+  }
+  if (res16) {  // h = sum + x16 (o_proj, add16)
+    const __half2 x01 = *reinterpret_cast<const __half2*>(res16 + i);
+    const __half2 x23 = *reinterpret_cast<const __half2*>(res16 + i + 2);
+    *reinterpret_cast<float4*>(out32 + i) = make_float4(a.x + __low2float(x01), a.y + __high2float(x01),
+                                                        a.z + __low2float(x23), a.w + __high2float(x23));
+  } else {      // x16 = fp16(sum + h) (down, add32_to16)
+    const float4 h = *reinterpret_cast<const float4*>(res32 + i);
+    *reinterpret_cast<__half2*>(out16 + i) = __floats2half2_rn(a.x + h.x, a.y + h.y);
+    *reinterpret_cast<__half2*>(out16 + i + 2) = __floats2half2_rn(a.z + h.z, a.w + h.w);
+  }
 }
 
 inline unsigned blocks_for(long long n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
@@ -225,6 +275,16 @@ int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, ui
   return 0;
 }
 
+int launch_tp_reduce(const float* recv, int ranks, const unsigned* flag, const unsigned* epoch, int uses_per_step,
+                     int use_in_step, int tiles, const __half* res16, const float* res32, float* out32,
+                     __half* out16, int d, int B, unsigned* err, cudaStream_t s) {
+  if (d % 4) return fail(AGXC_EINVAL, "tp_reduce: d multiple of 4");
+  tp_reduce_kernel<<<blocks_for(static_cast<long long>(B) * d / 4, 256), 256, 0, s>>>(
+      recv, ranks, flag, epoch, uses_per_step, use_in_step, tiles, res16, res32, out32, out16, d, B, err);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
+
 int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int B, cudaStream_t s) {
   argmax_part_kernel<<<B, kArgThreads, 0, s>>>(logits, V, v0, pairs);
   AGXC_CUDA(cudaGetLastError());
@@ -233,8 +293,9 @@ int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int 
 
 int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
                           uint32_t* log, int cap, int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B,
-                          cudaStream_t s) {
-  gen_from_pairs_kernel<<<B, 256, 0, s>>>(pairs, ranks, B, V, embed, d, q0, log, cap, tok, force_next, x16, err);
+                          cudaStream_t s, unsigned* epoch) {
+  gen_from_pairs_kernel<<<B, 256, 0, s>>>(pairs, ranks, B, V, embed, d, q0, log, cap, tok, force_next, x16, err,
+                                          epoch);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

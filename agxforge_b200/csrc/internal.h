@@ -172,7 +172,7 @@ int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, ui
 int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int B, cudaStream_t s);
 int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
                           uint32_t* log, int cap, int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B,
-                          cudaStream_t s);
+                          cudaStream_t s, unsigned* epoch = nullptr);
 
 // ---- the encoder's tensor-core GEMM (encoder.cu): C [M][N] = A [M][K] W [N][K]^T (+ bias; epi 0 fp32, 1 fp16
 // GELU, 2 fp32 + residual)
@@ -192,8 +192,23 @@ int tp_wait(TpComm* c, cudaEvent_t done, int timeout_ms);
 
 // ---- the batched GEMM (qmm.cu): Y [B][ldy] fp32 = X [B][K] fp16 W^T, B = 32..256 (multiple of 16), tcgen05 + TMEM
 int qmm_configure(const agxc_ctx* ctx);
+// The tensor-parallel push of finished output tiles (the GEMM + all-reduce fusion): the last of a tile's K-split
+// CTAs stores the tile's B x 128 block of Y into every rank's receive slot for this rank (peer memory over NVLink,
+// plain stores), then adds 1 to every rank's arrival counter (system scope, release).
+struct QmmPush {
+  float* slot[8] = {};      // rank r's receive slot for this rank's partial sums, [B][N]
+  unsigned* flag[8] = {};   // rank r's arrival counter of that slot buffer
+  unsigned* tile_ctr = nullptr;  // [N / 128] arrival counts of the K-split CTAs (local; reset by the last)
+  int ranks = 0;
+};
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s);
+               cudaStream_t s, const QmmPush* push = nullptr);
+// After the pushes of every rank: out = sum over ranks r (in order) of recv[r] [B][d] + residual, waiting (bounded)
+// until *flag >= (use + 1) x ranks x tiles with use = *epoch x uses_per_step + use_in_step. res16 -> h fp32 (o_proj),
+// or res32 -> x16 fp16 (down).
+int launch_tp_reduce(const float* recv, int ranks, const unsigned* flag, const unsigned* epoch, int uses_per_step,
+                     int use_in_step, int tiles, const __half* res16, const float* res32, float* out32,
+                     __half* out16, int d, int B, unsigned* err, cudaStream_t s);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 // tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,

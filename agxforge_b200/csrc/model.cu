@@ -92,6 +92,16 @@ struct agxc_model {
   uint32_t* amax = nullptr;     // [B][2] this rank's (value bits, global index) per sequence
   uint32_t* amax_all = nullptr; // [tp][B][2] every rank's, after the all-gather
   int wait_ms = 60000;
+  // the fused GEMM + all-reduce (peer memory): recv = [2 buffers (o_proj, down)][tp ranks][B][d] fp32 then 2 arrival
+  // counters, one allocation exported to the other ranks by CUDA IPC; peer[r] = rank r's allocation, mapped here
+  int tp_fused = 0;             // 1: o_proj and down push their tiles to every rank and reduce locally (no NCCL)
+  int tp_fused_ok = 0;          // the peer mappings exist on every rank
+  float* recv = nullptr;
+  unsigned* recv_flags = nullptr;
+  void* peer[8] = {};
+  unsigned* tile_ctr = nullptr; // [d / 128]
+  unsigned* epoch = nullptr;    // steps run in the fused mode
+  std::string tp_fused_why;
 };
 
 namespace agxc {
@@ -254,12 +264,26 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     ++kind;
     return 0;
   };
-  auto gemm = [&](const agxc_pack& pk, const __half* x, float* y, int ld) -> int {
+  auto gemm = [&](const agxc_pack& pk, const __half* x, float* y, int ld, const QmmPush* push = nullptr) -> int {
     const int tiles = pk.n / 128, G = pk.k / 64;
     int ks = 1;
     while (tiles * ks * 2 <= m->ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
     if (ks > 1) AGXC_CUDA(cudaMemset2DAsync(y, static_cast<size_t>(ld) * 4, 0, static_cast<size_t>(pk.n) * 4, B, s));
-    return launch_qmm(m->ctx, &pk, x, B, y, ld, ks, s);
+    return launch_qmm(m->ctx, &pk, x, B, y, ld, ks, s, push);
+  };
+  const bool fused = m->comm && m->tp_fused && m->tp_fused_ok;
+  auto push_of = [&](int buf) {  // this rank's slot of buffer `buf` on every rank, and their counters
+    QmmPush ps;
+    ps.ranks = m->tp;
+    ps.tile_ctr = m->tile_ctr;
+    const size_t slot = (static_cast<size_t>(buf) * m->tp + m->tp_rank) * B * d;
+    const size_t flags = static_cast<size_t>(2) * m->tp * B * d;
+    for (int r = 0; r < m->tp; ++r) {
+      float* base = static_cast<float*>(m->peer[r]);
+      ps.slot[r] = base + slot;
+      ps.flag[r] = reinterpret_cast<unsigned*>(base + flags) + buf;
+    }
+    return ps;
   };
   const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
   m->launches = 0;
@@ -275,18 +299,34 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
       return rc;
     a.pdl = 0;
     if ((rc = open()) || (rc = launch_attention(m->ctx, a, s)) || (rc = close())) return rc;
-    if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d)) ||
-        (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
-        (rc = launch_residual16(m->ybuf, d, m->x16, m->h, d, B, s)) || (rc = close()))
+    if (fused) {  // o_proj tiles pushed to every rank by the GEMM; the sum over ranks fused with the residual
+      QmmPush ps = push_of(0);
+      if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, &ps)) ||
+          (rc = launch_tp_reduce(m->recv, m->tp, m->recv_flags, m->epoch, D.n_layers, l, d / 128, m->x16, nullptr,
+                                 m->h, nullptr, d, B, m->ctx->err_dev, s)) ||
+          (rc = close()))
+        return rc;
+    } else if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, nullptr)) ||
+               (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
+               (rc = launch_residual16(m->ybuf, d, m->x16, m->h, d, B, s)) || (rc = close())) {
       return rc;
+    }
     if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s)) ||
         (rc = gemm(m->gu[l], m->xn16, m->ybuf, 2 * F)) || (rc = launch_swiglu(m->ybuf, 2 * F, m->act, F, B, s)) ||
         (rc = close()))
       return rc;
-    if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d)) ||
-        (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
-        (rc = launch_residual32(m->ybuf, d, m->h, m->x16, d, B, s)) || (rc = close()))
+    if (fused) {
+      QmmPush ps = push_of(1);
+      if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, &ps)) ||
+          (rc = launch_tp_reduce(m->recv + static_cast<size_t>(m->tp) * B * d, m->tp, m->recv_flags + 1, m->epoch,
+                                 D.n_layers, l, d / 128, nullptr, m->h, nullptr, m->x16, d, B, m->ctx->err_dev, s)) ||
+          (rc = close()))
+        return rc;
+    } else if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, nullptr)) ||
+               (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
+               (rc = launch_residual32(m->ybuf, d, m->h, m->x16, d, B, s)) || (rc = close())) {
       return rc;
+    }
   }
   if (m->comm) {  // vocabulary sliced over ranks: local first maxima, all-gathered, then the same choice everywhere
     if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
@@ -294,7 +334,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
         (rc = launch_argmax_part(m->logits, D.vocab, m->v0, m->amax, B, s)) ||
         (rc = tp_allgather_u32(m->comm, m->amax, m->amax_all, static_cast<size_t>(2) * B, s)) ||
         (rc = launch_gen_from_pairs(m->amax_all, m->tp, m->vt, m->embed, d, m->q0, m->log, D.cap, m->tok,
-                                    m->force_next, m->x16, m->ctx->err_dev, B, s)) ||
+                                    m->force_next, m->x16, m->ctx->err_dev, B, s, fused ? m->epoch : nullptr)) ||
         (rc = close()))
       return rc;
     m->launches = 11 * D.n_layers + 4;  // this library's kernels (the collectives are the communicator's)
@@ -379,6 +419,83 @@ int ensure_graph(agxc_model* m) {
 }  // namespace
 
 int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_model** out);
+
+// A bounded barrier over the ranks: a one-float all-reduce, waited for on the host.
+int tp_barrier(agxc_model* m) {
+  cudaStream_t s = m->ctx->stream;
+  if (int rc = tp_allreduce_f32(m->comm, m->ybuf, 1, s)) return rc;
+  AGXC_CUDA(cudaEventRecord(m->ev1, s));
+  return wait_done(m, m->ev1);
+}
+
+// The fused GEMM + all-reduce: the receive buffers (one allocation per rank, exported by CUDA IPC), every other
+// rank's mapped here; the handles travel by an all-gather on the communicator. Every rank ends with the same
+// tp_fused_ok (an all-reduce of the per-rank outcomes), so all ranks take the same path.
+int tp_peer_setup(agxc_model* m) {
+  const int T = m->tp, B = m->d.batch, d = m->d.d_model;
+  cudaStream_t s = m->ctx->stream;
+  const size_t bytes = static_cast<size_t>(2) * T * B * d * 4 + 256;
+  void* base = nullptr;
+  AGXC_CUDA(cudaMalloc(&base, bytes));
+  m->allocs.push_back(base);
+  AGXC_CUDA(cudaMemset(base, 0, bytes));
+  m->recv = static_cast<float*>(base);
+  m->recv_flags = reinterpret_cast<unsigned*>(m->recv + static_cast<size_t>(2) * T * B * d);
+  if (int rc = dalloc_t(m, &m->tile_ctr, static_cast<size_t>(d / 128))) return rc;
+  if (int rc = dalloc_t(m, &m->epoch, 1)) return rc;
+  AGXC_CUDA(cudaMemset(m->tile_ctr, 0, static_cast<size_t>(d / 128) * 4));
+  AGXC_CUDA(cudaMemset(m->epoch, 0, 4));
+  m->peer[m->tp_rank] = base;
+  int ok = 1;
+  cudaIpcMemHandle_t mine;
+  std::memset(&mine, 0, sizeof(mine));
+  if (cudaIpcGetMemHandle(&mine, base) != cudaSuccess) {
+    cudaGetLastError();
+    ok = 0;
+    m->tp_fused_why = "cudaIpcGetMemHandle failed";
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle of 64 bytes");
+  uint32_t* hd = nullptr;
+  if (int rc = dalloc_t(m, &hd, static_cast<size_t>(16) * (T + 1))) return rc;
+  AGXC_CUDA(cudaMemcpy(hd, &mine, 64, cudaMemcpyHostToDevice));
+  if (int rc = tp_allgather_u32(m->comm, hd, hd + 16, 16, s)) return rc;
+  AGXC_CUDA(cudaEventRecord(m->ev1, s));
+  if (int rc = wait_done(m, m->ev1)) return rc;
+  std::vector<cudaIpcMemHandle_t> all(T);
+  AGXC_CUDA(cudaMemcpy(all.data(), hd + 16, static_cast<size_t>(64) * T, cudaMemcpyDeviceToHost));
+  for (int r = 0; r < T && ok; ++r) {
+    if (r == m->tp_rank) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      m->tp_fused_why = "cudaIpcOpenMemHandle of rank " + std::to_string(r) + " failed";
+      break;
+    }
+    m->peer[r] = p;
+  }
+  // agree: the sum of the per-rank outcomes must be T
+  const float one = ok ? 1.f : 0.f;
+  AGXC_CUDA(cudaMemcpy(m->ybuf, &one, 4, cudaMemcpyHostToDevice));
+  if (int rc = tp_allreduce_f32(m->comm, m->ybuf, 1, s)) return rc;
+  AGXC_CUDA(cudaEventRecord(m->ev1, s));
+  if (int rc = wait_done(m, m->ev1)) return rc;
+  float sum = 0.f;
+  AGXC_CUDA(cudaMemcpy(&sum, m->ybuf, 4, cudaMemcpyDeviceToHost));
+  m->tp_fused_ok = sum == static_cast<float>(T);
+  if (!m->tp_fused_ok && m->tp_fused_why.empty()) m->tp_fused_why = "a peer rank could not map the buffers";
+  m->tp_fused = m->tp_fused_ok;
+  return 0;
+}
+
+// Before the buffers go: every rank stops using the others' (barrier), unmaps them, and waits until all have.
+void tp_peer_teardown(agxc_model* m) {
+  if (!m->comm || !m->recv || !m->ev1) return;
+  const bool synced = tp_barrier(m) == 0;
+  for (int r = 0; r < m->tp; ++r)
+    if (r != m->tp_rank && m->peer[r]) cudaIpcCloseMemHandle(m->peer[r]);
+  if (synced) tp_barrier(m);
+}
 
 int model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out) {
   const agxc_model_desc& D = *desc;
@@ -588,6 +705,7 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
       return bail(rc);
     if (cudaEventRecord(m->ev1, s) != cudaSuccess) return bail(fail(AGXC_ECUDA, "model: event record"));
     if ((rc = wait_done(m, m->ev1))) return bail(rc);
+    if ((rc = tp_peer_setup(m))) return bail(rc);
   }
   *out = m;
   return 0;
@@ -844,13 +962,14 @@ void model_free(agxc_model* m) {
   if (!m) return;
   if (m->exec) cudaGraphExecDestroy(m->exec);
   if (m->graph) cudaGraphDestroy(m->graph);
+  tp_peer_teardown(m);    // after the graphs, before the buffers the other ranks write (uses ev1)
+  tp_comm_free(m->comm);  // after the graphs that hold its collectives
   if (m->ev0) cudaEventDestroy(m->ev0);
   if (m->ev1) cudaEventDestroy(m->ev1);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_force) cudaFreeHost(m->h_force);
   if (m->trace) cudaFree(m->trace);
   if (m->cta_trace) cudaFree(m->cta_trace);
-  tp_comm_free(m->comm);  // after the graphs that hold its collectives
   for (void* p : m->allocs) cudaFree(p);
   delete m;
 }
@@ -965,7 +1084,9 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
                   ", \"rank\": " + std::to_string(m->tp_rank) + ", \"heads\": " + std::to_string(m->d.n_heads) +
                   ", \"kv_heads\": " + std::to_string(m->d.n_kv_heads) + ", \"ffn\": " +
                   std::to_string(m->d.ffn) + ", \"vocab_offset\": " + std::to_string(m->v0) +
-                  ", \"vocab_count\": " + std::to_string(m->d.vocab) + "}}";
+                  ", \"vocab_count\": " + std::to_string(m->d.vocab) + ", \"fused\": " +
+                  std::to_string(m->comm && m->tp_fused && m->tp_fused_ok) + ", \"fused_available\": " +
+                  std::to_string(m->tp_fused_ok) + "}}";
   std::snprintf(buf, len, "%s", j.c_str());
   return 0;
 }
@@ -1001,6 +1122,11 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
     m->pdl = value;
   } else if (option == AGXC_OPT_BULK) {
     m->bulk = value ? 1 : 0;
+  } else if (option == AGXC_OPT_TP_FUSED) {
+    if (value && !m->tp_fused_ok)
+      return agxc::fail(AGXC_EUNSUPPORTED, "set_option: no fused tensor-parallel path (" +
+                                               (m->comm ? m->tp_fused_why : std::string("single device")) + ")");
+    m->tp_fused = value ? 1 : 0;
   } else if (option == AGXC_OPT_WAIT_MS) {
     if (value < 1) return agxc::fail(AGXC_EINVAL, "set_option: wait_ms must be positive");
     m->wait_ms = value;

@@ -41,6 +41,7 @@ struct QmmParams {
   float* y = nullptr;             // fp32 [B][ldy]
   int ldy = 0;
   unsigned* err = nullptr;
+  QmmPush push;                   // ranks > 0: push finished tiles to every rank (tensor parallel)
 };
 
 struct QmmSmem {
@@ -100,6 +101,18 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// AND of a predicate over the 256 epilogue threads (named barrier 1): their decisions stay uniform.
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t hsub_1024(uint32_t v) {  // fp16 pair minus 1024 (exact for 1024 + q, q < 1024)
   uint32_t r;
@@ -315,6 +328,33 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
         }
       }
     }
+    if (p.push.ranks > 0) {
+      // tensor parallel: the tile's last K-split CTA sends the finished B x 128 block of Y to every rank
+      __threadfence();                               // this CTA's partial sums are visible at L2
+      const bool all_ok = epi_all(ok);
+      volatile int* s_last = dead + 1;
+      if (all_ok && dw == 0 && lane == 0) {
+        const unsigned prev = atomicAdd(p.push.tile_ctr + tile, 1u);
+        *s_last = prev == static_cast<unsigned>(p.ksplit - 1);
+        if (*s_last) p.push.tile_ctr[tile] = 0;      // every K-split CTA of the tile has arrived
+      }
+      epi_sync();
+      if (all_ok && *s_last) {
+        __threadfence();                             // the other CTAs' sums, read below from L2
+        const int et = dw * 32 + lane;               // 0 .. 255
+        for (int i = et; i < p.B * (kM / 4); i += 256) {
+          const int b = i / (kM / 4), n = tile * kM + (i % (kM / 4)) * 4;
+          const float4 v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
+          for (int r = 0; r < p.push.ranks; ++r)
+            *reinterpret_cast<float4*>(p.push.slot[r] + static_cast<size_t>(b) * p.N + n) = v4;
+        }
+        __threadfence_system();                      // the stores reach every rank before its counter moves
+        epi_sync();
+        if (et == 0)
+          for (int r = 0; r < p.push.ranks; ++r)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
+      }
+    }
   }
   // every role is done (the tensor core too: acc_full waited, or the error path below): free TMEM
   if (*dead && tid == 64) mbar_wait_bounded(acc_full, 0, nullptr, 100000000ull);
@@ -346,7 +386,7 @@ int qmm_configure(const agxc_ctx* ctx) {
 // Y [B][ldy] fp32 = X [B][K] fp16 x W^T for a pack W [N][K]: 128-row tiles, the K range split over ksplit CTAs when
 // the tiles alone would leave SMs idle (then Y must hold zeros: the CTAs add into it).
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s) {
+               cudaStream_t s, const QmmPush* push) {
   if (B < 32 || B > 256 || B % 16) return fail(AGXC_EINVAL, "qmm: 32 to 256 activation rows, a multiple of 16");
   if (pk->n % kM) return fail(AGXC_EINVAL, "qmm: N must be a multiple of 128");
   if (ldy < pk->n) return fail(AGXC_EINVAL, "qmm: ldy < N");
@@ -355,6 +395,10 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
   QmmParams p;
   p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.G = G; p.bits = pk->bits; p.sdt = pk->sdt;
   p.B = B; p.ksplit = ksplit; p.y = y; p.ldy = ldy; p.err = ctx->err_dev;
+  if (push) {
+    if (push->ranks < 1 || push->ranks > 8 || !push->tile_ctr) return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks");
+    p.push = *push;
+  }
   // as many stages as fit beside the dequant tiles (at most 16: a stage cycles through the copy, the dequant and the
   // MMA's completion before it is refilled, so small stages want many)
   p.stages = 16;

@@ -152,9 +152,11 @@ class DecodeModel:
         (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace());
         "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off); "bulk" (GEMV weights
         by plain bulk copies instead of TMA tensor boxes); "wait_ms" (tensor parallel: the host's bound on a decode
-        call, past which the communicator is aborted and TimeoutError raised; default 60000)."""
+        call, past which the communicator is aborted and TimeoutError raised; default 60000); "tp_fused" (tensor
+        parallel: 1 = the o_proj/down GEMMs push their tiles to every rank over NVLink and the sum is fused with the
+        residual, the default where available; 0 = NCCL all-reduce; every rank must set the same value)."""
         opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT, "bulk": N.OPT_BULK,
-                "wait_ms": N.OPT_WAIT_MS}
+                "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")

@@ -363,6 +363,8 @@ def main():
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--tp-allreduce", default="fused", choices=["fused", "nccl"],
+                    help="tensor-parallel configs: GEMM + peer-memory all-reduce (fused) or NCCL all-reduce")
     ap.add_argument("--kernel-case", choices=KIND_NAMES, default=None)
     ap.add_argument("--case-batch", type=int, default=0,
                     help="activation rows of --kernel-case (default: the config's batch; >= 32 = tensor-core qmm)")
@@ -404,6 +406,8 @@ def main():
     m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=2 + rseed, tp=tp,
                             tp_rank=rank if tp > 1 else 0), device=local, keep_packs=keep)
     S = m.shape
+    if tp > 1 and args.tp_allreduce == "nccl":
+        m.set_option("tp_fused", 0)
     rng = np.random.default_rng(1792 + rseed)
     # the history: positions 0 .. hist - W - 1 filled on the device (seeded), a random current token; then W warm-up
     # steps at positions hist - W .. hist - 1; the timed steps are at positions hist .. hist + K - 1

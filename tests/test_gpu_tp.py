@@ -25,23 +25,25 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(case, world):
+def _run(case, world, mode="fused"):
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
-           os.path.join(ROOT, "tests", "tp_worker.py"), "--case", case]
+           os.path.join(ROOT, "tests", "tp_worker.py"), "--case", case, "--mode", mode]
     p = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
     assert p.returncode == 0, "tp worker failed (%d):\n%s\n%s" % (p.returncode, p.stdout[-3000:], p.stderr[-3000:])
     rep = json.loads(lines[-1])
     assert rep["ok"] and rep["tokens_agree"]
+    assert rep["fused"] == (1 if mode == "fused" else 0)
     return rep
 
 
-@pytest.mark.parametrize("case", ["small", "small8"])
-def test_tp2_small_against_oracle_and_one_device(case):
+@pytest.mark.parametrize("case,mode", [("small", "fused"), ("small", "nccl"), ("small8", "fused")])
+def test_tp2_small_against_oracle_and_one_device(case, mode):
+    """The fused GEMM + peer-memory all-reduce and the NCCL all-reduce, each against the oracle and one device."""
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
-    rep = _run(case, 2)
+    rep = _run(case, 2, mode)
     assert rep["max_diff_vs_tp1"] < 0.02
 
 

@@ -24,6 +24,7 @@ SMALL = dict(NAME="small", D_MODEL=256, LAYERS=2, HEADS=4, KV_HEADS=2, HEAD_DIM=
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="small", choices=["small", "small8", "internlm7b"])
+    ap.add_argument("--mode", default="fused", choices=["fused", "nccl"])
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -41,13 +42,19 @@ def main():
     vocab = shape["VOCAB"] if isinstance(shape, dict) else shape.VOCAB
     cfg = dict(model=shape, bits=bits, batch=B, cap=cap, seed=9, keep_logits=True, tp=world, tp_rank=rank)
     m = assemble.build(dict(cfg), device=local, keep_packs=(rank == 0 and check_oracle))
+    info = m.plan_info()["tp"]
+    if args.mode == "nccl":
+        m.set_option("tp_fused", 0)       # every rank sets the same value
+    elif not info["fused_available"]:
+        raise SystemExit("rank %d: the fused path is not available" % rank)
     rng = np.random.default_rng(21)
     prompts = [rng.integers(0, vocab, int(n)).tolist() for n in rng.integers(3, 30, B)]
     seqs, lg, _ = MC.run_forced(m, prompts, steps, seed=22)
     free_t, free_lg, _ = m.decode(3, want_tokens=True, want_logits=True)
     parts = [None] * world
     dist.all_gather_object(parts, (m.vocab_offset, lg, free_t, free_lg))
-    ok, report = True, dict(case=args.case, world=world, rank=rank)
+    ok, report = True, dict(case=args.case, world=world, rank=rank, mode=args.mode,
+                            fused=m.plan_info()["tp"]["fused"])
     if rank == 0:
         parts.sort(key=lambda p: p[0])
         full = np.concatenate([p[1] for p in parts], axis=2)
