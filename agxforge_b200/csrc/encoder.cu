@@ -38,7 +38,7 @@ namespace {
 
 constexpr int kGM = 128;            // token rows per GEMM CTA (the MMA's M)
 constexpr int kGThreads = 192;      // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
-enum { kEpiF32 = 0, kEpiGelu16 = 1, kEpiRes32 = 2 };
+enum { kEpiF32 = 0, kEpiGelu16 = 1, kEpiRes32 = 2, kEpiResLn = 3 };
 
 struct HgemmParams {
   int M = 0, N = 0, K = 0, bn = 128, stages = 3;
@@ -46,25 +46,34 @@ struct HgemmParams {
   const __half* bias = nullptr;     // [N]
   float* out32 = nullptr;           // [M][N] (F32, RES32)
   __half* out16 = nullptr;          // [M][N] (GELU16)
-  const float* res32 = nullptr;     // [M][N] (RES32)
+  const float* res32 = nullptr;     // [M][N] (RES32, RESLN; may alias out32)
+  const __half* ln_g = nullptr;     // [N] LayerNorm gain and bias (RESLN: the tile is the whole row, bn == N)
+  const __half* ln_b = nullptr;
+  float eps = 0.f;
   unsigned* err = nullptr;
 };
 
 struct HgemmSmem {
-  int bars, tmem_slot, bias, stage0, stage_bytes, b_off, total;
+  int bars, tmem_slot, bias, lng, lnb, stage0, stage_bytes, b_off, total;
 };
 
 __host__ __device__ inline HgemmSmem hgemm_layout(int bn, int stages) {
   HgemmSmem L;
   L.bars = 0;              // full[S], empty[S], acc_full, dead flag (S <= 8)
   L.tmem_slot = 256;
-  L.bias = 512;            // bn fp32
-  L.stage0 = 2048;         // 1,024-aligned stages: A 128 x 128 B, then B bn x 128 B
+  L.bias = 512;            // bn fp32 (bn <= 512)
+  L.lng = L.bias + 2048;   // LayerNorm gain, bias: bn fp32 each
+  L.lnb = L.lng + 2048;
+  L.stage0 = (L.lnb + 2048 + 1023) / 1024 * 1024;  // 1,024-aligned stages (the 128-byte swizzle's atom): A 128 x
+                                                  // 128 B, then B bn x 128 B
   L.b_off = kGM * 128;
   L.stage_bytes = L.b_off + bn * 128;
   L.total = L.stage0 + stages * L.stage_bytes;
   return L;
 }
+
+// TMEM columns for a bn-wide fp32 accumulator (a power of two >= 32)
+__host__ __device__ inline int tmem_cols(int bn) { return bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : bn <= 256 ? 256 : 512; }
 
 __device__ __forceinline__ uint64_t desc_k128(uint32_t saddr) {
   // UMMA shared-memory descriptor, K-major, 128-byte swizzle: start >> 4 (bits 0-13), leading byte offset 16 B
@@ -97,6 +106,10 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
   volatile int* dead = reinterpret_cast<volatile int*>(acc_full + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   float* sbias = reinterpret_cast<float*>(smem + L.bias);
+  float* slng = reinterpret_cast<float*>(smem + L.lng);
+  float* slnb = reinterpret_cast<float*>(smem + L.lnb);
+  const int ncols = tmem_cols(p.bn);
+  const int bsub = p.bn > 128 ? 128 : p.bn;  // B rows per TMA box and per MMA (N)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n0 = blockIdx.x * p.bn, m0 = blockIdx.y * kGM;
   const int KT = p.K / 64;
@@ -112,12 +125,18 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(p.bn)
+                 "r"(ncols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   }
-  for (int c = tid; c < p.bn; c += kGThreads) sbias[c] = p.bias ? __half2float(p.bias[n0 + c]) : 0.f;
+  for (int c = tid; c < p.bn; c += kGThreads) {
+    sbias[c] = p.bias ? __half2float(p.bias[n0 + c]) : 0.f;
+    if (p.epi == kEpiResLn) {
+      slng[c] = __half2float(p.ln_g[c]);
+      slnb[c] = __half2float(p.ln_b[c]);
+    }
+  }
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
@@ -137,7 +156,7 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
         uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
         mbar_arrive_expect_tx(&full[s], bytes);
         tma_rows(st, &ta, i * 64, m0, &full[s]);
-        tma_rows(st + L.b_off, &tb, i * 64, n0, &full[s]);
+        for (int j = 0; j < p.bn / bsub; ++j) tma_rows(st + L.b_off + j * bsub * 128, &tb, i * 64, n0 + j * bsub, &full[s]);
       }
       if (*dead) {  // no copy of this CTA may land after it leaves (bounded)
         for (int i = issued > S ? issued - S : 0; i < issued; ++i)
@@ -146,7 +165,7 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
-      const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(p.bn >> 3) << 17) |
+      const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(bsub >> 3) << 17) |
                              (static_cast<uint32_t>(kGM >> 4) << 24);  // fp32 accum, fp16 A/B, K-major, N, M
       for (int i = 0; i < KT; ++i) {
         const int s = i % S;
@@ -157,15 +176,17 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t a0 = smem_u32(smem + L.stage0 + s * L.stage_bytes);
         const uint32_t b0 = a0 + L.b_off;
+        for (int j = 0; j < p.bn / bsub; ++j) {  // N sub-blocks of bsub columns (TMEM columns j * bsub ..)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = desc_k128(a0 + 32 * k), bd = desc_k128(b0 + 32 * k);
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-              "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-              : "memory");
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = desc_k128(a0 + 32 * k), bd = desc_k128(b0 + j * bsub * 128 + 32 * k);
+            const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem + static_cast<uint32_t>(j * bsub)),
+                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+                : "memory");
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                          smem_u32(&empty[s]))
@@ -179,7 +200,79 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
     // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = token rows; columns = output features
     const bool ok = __all_sync(0xffffffffu, !*dead && mbar_wait_bounded(acc_full, 0, p.err));
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
+    if (p.epi == kEpiResLn) {
+      // the tile's residual rows into shared memory, coalesced (the stages are free: every MMA has completed), rows
+      // padded to N + 4 floats so the row-per-thread reads below are conflict-free
+      const int rs = p.N + 4;
+      float* sres = reinterpret_cast<float*>(smem + L.stage0);
+      if (ok) {
+        const int n4 = p.N / 4;
+        for (int i = tid - 64; i < kGM * n4; i += 128) {
+          const int r = i / n4, c = (i % n4) * 4;
+          *reinterpret_cast<float4*>(sres + r * rs + c) =
+              __ldcg(reinterpret_cast<const float4*>(p.res32 + static_cast<size_t>(m0 + r) * p.N + c));
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+      if (ok) {
+      // the whole row is in this thread's TMEM lane: x = acc + bias + residual, LayerNorm in three passes
+      const int q4 = warp & 3;
+      const int row = m0 + 32 * q4 + lane;
+      const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+      const float* res = sres + (32 * q4 + lane) * rs;
+      float mean = 0.f, den = 1.f;
+      for (int pass = 0; pass < 3; ++pass) {
+        float acc_s = 0.f;
+        for (int c0 = 0; c0 < p.bn; c0 += 16) {
+          uint32_t v[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+              "%14, %15}, [%16];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+              : "r"(base + static_cast<uint32_t>(c0)));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          float x[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 rv = *reinterpret_cast<const float4*>(res + c0 + 4 * j);
+            x[4 * j] = __uint_as_float(v[4 * j]) + sbias[c0 + 4 * j] + rv.x;
+            x[4 * j + 1] = __uint_as_float(v[4 * j + 1]) + sbias[c0 + 4 * j + 1] + rv.y;
+            x[4 * j + 2] = __uint_as_float(v[4 * j + 2]) + sbias[c0 + 4 * j + 2] + rv.z;
+            x[4 * j + 3] = __uint_as_float(v[4 * j + 3]) + sbias[c0 + 4 * j + 3] + rv.w;
+          }
+          if (pass == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc_s += x[j];
+          } else if (pass == 1) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float dlt = x[j] - mean;
+              acc_s = fmaf(dlt, dlt, acc_s);
+            }
+          } else {
+            float y[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = (x[j] - mean) / den * slng[c0 + j] + slnb[c0 + j];
+            float4* o32 = reinterpret_cast<float4*>(p.out32 + static_cast<size_t>(row) * p.N + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o32[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+            uint32_t hv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const __half2 t2 = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+              hv[j] = *reinterpret_cast<const uint32_t*>(&t2);
+            }
+            uint4* o16 = reinterpret_cast<uint4*>(p.out16 + static_cast<size_t>(row) * p.N + c0);
+            o16[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            o16[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+          }
+        }
+        if (pass == 0) mean = acc_s / p.N;
+        else if (pass == 1) den = sqrtf(acc_s / p.N + p.eps);
+      }
+      }
+    } else if (ok) {
       const int q4 = warp & 3;
       const int row = m0 + 32 * q4 + lane;
       const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
@@ -227,7 +320,7 @@ __global__ void __launch_bounds__(kGThreads, 1) hgemm_kernel(const HgemmParams p
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.bn) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
   }
 }
 
@@ -348,6 +441,151 @@ __global__ void attn_kernel(const float* __restrict__ qkv, const int32_t* __rest
   }
 }
 
+// fp16 hi/lo split of a pair: hi = fp16(x), lo = fp16(x - hi) (exact residual up to fp16 rounding), so
+// hi_a.hi_b + hi_a.lo_b + lo_a.hi_b on the tensor cores carries ~22 significant bits — fp32-class products.
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Masked softmax attention of one (head, sequence) on the tensor cores, seq <= 16 KT, head width 32: each warp takes
+// 16-query tiles; S = Q K^T and O = P V by m16n8k16 MMAs with both operands split hi/lo (three MMAs per product), the
+// whole score row in registers (no online rescaling), P kept in registers between the two products (the score
+// accumulator of keys 16j..16j+15 is the A fragment of step j). Keys past seq or with mask 0 score -inf.
+template <int KT>
+__global__ void __launch_bounds__(128) attn_tc_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ mask,
+                                                      int seq, int width, float scale, __half* __restrict__ ctx) {
+  constexpr int HW = 32, SP = 16 * KT, LD = HW + 4;
+  extern __shared__ float sm[];
+  float* ks = sm;                 // [SP][LD] fp32, zero past seq
+  float* vs = sm + SP * LD;
+  int* ms = reinterpret_cast<int*>(vs + SP * LD);
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int ld = 3 * width;
+  const size_t r0 = static_cast<size_t>(b) * seq;
+  for (int i = tid; i < SP * (HW / 4); i += 128) {
+    const int s = i / (HW / 4), c = (i % (HW / 4)) * 4;
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+    if (s < seq) {
+      const float* src = qkv + (r0 + s) * ld + h * HW + c;
+      kv = *reinterpret_cast<const float4*>(src + width);
+      vv = *reinterpret_cast<const float4*>(src + 2 * width);
+    }
+    *reinterpret_cast<float4*>(ks + s * LD + c) = kv;
+    *reinterpret_cast<float4*>(vs + s * LD + c) = vv;
+  }
+  for (int s = tid; s < SP; s += 128) ms[s] = s < seq ? mask[r0 + s] != 0 : 0;
+  __syncthreads();
+  for (int mt = warp; mt < KT; mt += 4) {
+    const int qa = mt * 16 + g, qb = qa + 8;  // this thread's two query rows
+    // Q fragments (2 k-steps of 16 dims), split
+    uint32_t qh[2][4], ql[2][4];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int c = 16 * k + 2 * t;
+      float2 x0 = make_float2(0.f, 0.f), x1 = x0, x2 = x0, x3 = x0;
+      if (qa < seq) {
+        const float* q = qkv + (r0 + qa) * ld + h * HW;
+        x0 = *reinterpret_cast<const float2*>(q + c);
+        x2 = *reinterpret_cast<const float2*>(q + c + 8);
+      }
+      if (qb < seq) {
+        const float* q = qkv + (r0 + qb) * ld + h * HW;
+        x1 = *reinterpret_cast<const float2*>(q + c);
+        x3 = *reinterpret_cast<const float2*>(q + c + 8);
+      }
+      split2(x0.x, x0.y, qh[k][0], ql[k][0]);
+      split2(x1.x, x1.y, qh[k][1], ql[k][1]);
+      split2(x2.x, x2.y, qh[k][2], ql[k][2]);
+      split2(x3.x, x3.y, qh[k][3], ql[k][3]);
+    }
+    float sc[2 * KT][4];
+#pragma unroll
+    for (int nt = 0; nt < 2 * KT; ++nt) {
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+      const float* kr = ks + (nt * 8 + g) * LD;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = 16 * k + 2 * t;
+        uint32_t bh0, bl0, bh1, bl1;
+        split2(kr[c], kr[c + 1], bh0, bl0);
+        split2(kr[c + 8], kr[c + 9], bh1, bl1);
+        mma_16816(d0, d1, d2, d3, qh[k][0], qh[k][1], qh[k][2], qh[k][3], bh0, bh1);
+        mma_16816(d0, d1, d2, d3, qh[k][0], qh[k][1], qh[k][2], qh[k][3], bl0, bl1);
+        mma_16816(d0, d1, d2, d3, ql[k][0], ql[k][1], ql[k][2], ql[k][3], bh0, bh1);
+      }
+      const int k0 = nt * 8 + 2 * t;
+      sc[nt][0] = ms[k0] ? d0 * scale : -INFINITY;
+      sc[nt][1] = ms[k0 + 1] ? d1 * scale : -INFINITY;
+      sc[nt][2] = ms[k0] ? d2 * scale : -INFINITY;
+      sc[nt][3] = ms[k0 + 1] ? d3 * scale : -INFINITY;
+    }
+    float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2 * KT; ++nt) {
+      m0 = fmaxf(m0, fmaxf(sc[nt][0], sc[nt][1]));
+      m1 = fmaxf(m1, fmaxf(sc[nt][2], sc[nt][3]));
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    if (m0 == -INFINITY) m0 = 0.f;  // no valid key (refused on the host path): all weights 0
+    if (m1 == -INFINITY) m1 = 0.f;
+    float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2 * KT; ++nt) {
+      sc[nt][0] = expf(sc[nt][0] - m0);
+      sc[nt][1] = expf(sc[nt][1] - m0);
+      sc[nt][2] = expf(sc[nt][2] - m1);
+      sc[nt][3] = expf(sc[nt][3] - m1);
+      l0 += sc[nt][0] + sc[nt][1];
+      l1 += sc[nt][2] + sc[nt][3];
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int dt = 0; dt < 4; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KT; ++kk) {
+      uint32_t ph[4], pl[4];
+      split2(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
+      split2(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
+      split2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
+      split2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+      const float* v0 = vs + (kk * 16 + 2 * t) * LD;
+#pragma unroll
+      for (int dt = 0; dt < 4; ++dt) {
+        const int c = dt * 8 + g;
+        uint32_t bh0, bl0, bh1, bl1;
+        split2(v0[c], v0[LD + c], bh0, bl0);
+        split2(v0[8 * LD + c], v0[9 * LD + c], bh1, bl1);
+        mma_16816(acc[dt][0], acc[dt][1], acc[dt][2], acc[dt][3], ph[0], ph[1], ph[2], ph[3], bh0, bh1);
+        mma_16816(acc[dt][0], acc[dt][1], acc[dt][2], acc[dt][3], ph[0], ph[1], ph[2], ph[3], bl0, bl1);
+        mma_16816(acc[dt][0], acc[dt][1], acc[dt][2], acc[dt][3], pl[0], pl[1], pl[2], pl[3], bh0, bh1);
+      }
+    }
+    const float i0 = l0 > 0.f ? 1.0f / l0 : 0.f, i1 = l1 > 0.f ? 1.0f / l1 : 0.f;
+#pragma unroll
+    for (int dt = 0; dt < 4; ++dt) {
+      const int c = h * HW + dt * 8 + 2 * t;
+      if (qa < seq)
+        *reinterpret_cast<__half2*>(ctx + (r0 + qa) * width + c) = __floats2half2_rn(acc[dt][0] * i0, acc[dt][1] * i0);
+      if (qb < seq)
+        *reinterpret_cast<__half2*>(ctx + (r0 + qb) * width + c) = __floats2half2_rn(acc[dt][2] * i1, acc[dt][3] * i1);
+    }
+  }
+}
+
 // Masked mean over a sequence's valid rows, then L2 normalisation: one CTA per sequence, one thread per feature.
 __global__ void pool_kernel(const float* __restrict__ x, const int32_t* __restrict__ mask, int seq, int width,
                             float* __restrict__ out) {
@@ -384,19 +622,32 @@ int hgemm_allow(int optin) {
 
 // C [M][N] = A [M][K] fp16 x W [N][K]^T fp16 (+ bias, GELU / residual by `epi`): M % 128, N % 64, K % 64 == 0.
 int launch_hgemm(const agxc_ctx* ctx, const __half* A, const __half* W, int M, int N, int K, const __half* bias,
-                 int epi, float* out32, __half* out16, const float* res32, cudaStream_t s) {
+                 int epi, float* out32, __half* out16, const float* res32, cudaStream_t s, const __half* ln_g,
+                 const __half* ln_b, float eps) {
   if (M % kGM || N % 64 || K % 64 || M <= 0 || N <= 0 || K <= 0)
     return fail(AGXC_EINVAL, "hgemm: M multiple of 128, N and K multiples of 64");
+  if (epi == kEpiResLn && (N % 128 || N > 384 || !ln_g || !ln_b))
+    return fail(AGXC_EINVAL, "hgemm: the LayerNorm epilogue needs rows of 128, 256 or 384 features");
   HgemmParams p;
   p.M = M; p.N = N; p.K = K; p.epi = epi; p.bias = bias; p.out32 = out32; p.out16 = out16; p.res32 = res32;
+  p.ln_g = ln_g; p.ln_b = ln_b; p.eps = eps;
   p.err = ctx->err_dev;
-  // 128 output features per CTA when that alone gives a full wave, else 64 (more CTAs for the narrow outputs)
-  p.bn = (N % 128 == 0 && (M / kGM) * (N / 128) >= ctx->num_sms) ? 128 : 64;
-  p.stages = std::min(K / 64, p.bn == 128 ? 3 : 4);  // two CTAs per SM
-  const int smem = hgemm_layout(p.bn, p.stages).total + 1024;
+  if (epi == kEpiResLn) {
+    p.bn = N;  // the whole row in one CTA's TMEM
+    const int room = ctx->max_smem_optin - 1024 - hgemm_layout(p.bn, 0).total;
+    p.stages = std::max(2, std::min({K / 64, 4, room / hgemm_layout(p.bn, 1).stage_bytes}));
+  } else {
+    // 128 output features per CTA when that alone gives a full wave, else 64 (more CTAs for the narrow outputs)
+    p.bn = (N % 128 == 0 && (M / kGM) * (N / 128) >= ctx->num_sms) ? 128 : 64;
+    p.stages = std::min(K / 64, p.bn == 128 ? 3 : 4);  // two CTAs per SM
+  }
+  int smem = hgemm_layout(p.bn, p.stages).total + 1024;
+  if (epi == kEpiResLn)  // the residual tile (128 rows of N + 4 floats) reuses the stages
+    smem = std::max(smem, hgemm_layout(p.bn, 0).total + kGM * (N + 4) * 4 + 1024);
+  if (smem > ctx->max_smem_optin) return fail(AGXC_EINVAL, "hgemm: tile does not fit shared memory");
   CUtensorMap ta, tb;
   if (int rc = encode_rows_map(&ta, A, M, K, kGM)) return rc;
-  if (int rc = encode_rows_map(&tb, W, N, K, p.bn)) return rc;
+  if (int rc = encode_rows_map(&tb, W, N, K, p.bn > 128 ? 128 : p.bn)) return rc;
   hgemm_kernel<<<dim3(N / p.bn, M / kGM), kGThreads, smem, s>>>(p, ta, tb);
   AGXC_CUDA(cudaGetLastError());
   return 0;
@@ -516,7 +767,21 @@ int enqueue_forward(agxc_encoder* e, int B, int Sq, bool with_types, cudaStream_
          })))
       return rc;
     if ((rc = timed(2, [&]() -> int {
-           if (HW == 32)
+           if (HW == 32 && Sq <= 128) {
+             const int KT = (Sq + 15) / 16;
+             const size_t sm = static_cast<size_t>(16 * KT) * 36 * 4 * 2 + static_cast<size_t>(16 * KT) * 4;
+             const dim3 grid(D.heads, B);
+             switch (KT) {
+               case 1: attn_tc_kernel<1><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 2: attn_tc_kernel<2><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 3: attn_tc_kernel<3><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 4: attn_tc_kernel<4><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 5: attn_tc_kernel<5><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 6: attn_tc_kernel<6><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               case 7: attn_tc_kernel<7><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+               default: attn_tc_kernel<8><<<grid, 128, sm, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16); break;
+             }
+           } else if (HW == 32)
              attn_kernel<32><<<dim3(D.heads, B), 128, attn_smem, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16);
            else if (HW == 64)
              attn_kernel<64><<<dim3(D.heads, B), 128, attn_smem, s>>>(e->qkv32, e->mask, Sq, W, scale, e->ctx16);
@@ -526,20 +791,37 @@ int enqueue_forward(agxc_encoder* e, int B, int Sq, bool with_types, cudaStream_
            return 0;
          })))
       return rc;
-    if ((rc = timed(3, [&] {
-           return launch_hgemm(e->ctx, e->ctx16, L.wo, M, W, W, L.bo, kEpiRes32, e->y32, nullptr, e->x32, s);
-         })))
+    // o_proj + bias + residual + LayerNorm in one kernel when the row fits one CTA's TMEM and the 128-row tiles
+    // alone fill the SMs (measured at 32 tiles: 52 us against 19 + 12 us for the GEMM and the LayerNorm kernel apart)
+    const bool ln_fused = W <= 384 && M / kGM >= e->ctx->num_sms;
+    if (ln_fused) {
+      if ((rc = timed(3, [&] {
+             return launch_hgemm(e->ctx, e->ctx16, L.wo, M, W, W, L.bo, kEpiResLn, e->x32, e->x16, e->x32, s, L.ln1w,
+                                 L.ln1b, D.eps);
+           })))
+        return rc;
+    } else if ((rc = timed(3, [&] {
+                  return launch_hgemm(e->ctx, e->ctx16, L.wo, M, W, W, L.bo, kEpiRes32, e->y32, nullptr, e->x32, s);
+                })) ||
+               (rc = timed(4, [&] { return launch_ln(e, e->y32, false, nullptr, L.ln1w, L.ln1b, M, Sq, s); }))) {
       return rc;
-    if ((rc = timed(4, [&] { return launch_ln(e, e->y32, false, nullptr, L.ln1w, L.ln1b, M, Sq, s); }))) return rc;
+    }
     if ((rc = timed(5, [&] {
            return launch_hgemm(e->ctx, e->x16, L.w1, M, F, W, L.b1, kEpiGelu16, nullptr, e->u16, nullptr, s);
          })))
       return rc;
-    if ((rc = timed(6, [&] {
-           return launch_hgemm(e->ctx, e->u16, L.w2, M, W, F, L.b2, kEpiRes32, e->y32, nullptr, e->x32, s);
-         })))
+    if (ln_fused) {  // FFN down + bias + residual + LayerNorm in one kernel
+      if ((rc = timed(6, [&] {
+             return launch_hgemm(e->ctx, e->u16, L.w2, M, W, F, L.b2, kEpiResLn, e->x32, e->x16, e->x32, s, L.ln2w,
+                                 L.ln2b, D.eps);
+           })))
+        return rc;
+    } else if ((rc = timed(6, [&] {
+                  return launch_hgemm(e->ctx, e->u16, L.w2, M, W, F, L.b2, kEpiRes32, e->y32, nullptr, e->x32, s);
+                })) ||
+               (rc = timed(4, [&] { return launch_ln(e, e->y32, false, nullptr, L.ln2w, L.ln2b, M, Sq, s); }))) {
       return rc;
-    if ((rc = timed(4, [&] { return launch_ln(e, e->y32, false, nullptr, L.ln2w, L.ln2b, M, Sq, s); }))) return rc;
+    }
   }
   if ((rc = timed(7, [&]() -> int {
          pool_kernel<<<B, (W + 31) / 32 * 32, 0, s>>>(e->x32, e->mask, Sq, W, e->out);
@@ -589,14 +871,16 @@ int check_shape(const agxc_encoder* e, int B, int Sq) {
 extern "C" {
 
 int agxc_hgemm_dev(agxc_ctx* ctx, const uint16_t* A, const uint16_t* W, int M, int N, int K, const uint16_t* bias,
-                   int epi, float* out32, uint16_t* out16, const float* res32, void* stream) {
+                   int epi, float* out32, uint16_t* out16, const float* res32, const uint16_t* ln_g,
+                   const uint16_t* ln_b, float eps, void* stream) {
   using namespace agxc;
   if (!ctx || !A || !W) return fail(AGXC_EINVAL, "hgemm: null argument");
-  if (epi < 0 || epi > 2 || (epi == 1 ? !out16 : !out32) || (epi == 2 && !res32))
-    return fail(AGXC_EINVAL, "hgemm: epi 0 (out32), 1 (out16), 2 (out32 + res32)");
+  if (epi < 0 || epi > 3 || (epi == 1 ? !out16 : !out32) || (epi >= 2 && !res32) || (epi == 3 && !out16))
+    return fail(AGXC_EINVAL, "hgemm: epi 0 (out32), 1 (out16), 2 (out32 + res32), 3 (LayerNorm: out32, out16)");
   return launch_hgemm(ctx, reinterpret_cast<const __half*>(A), reinterpret_cast<const __half*>(W), M, N, K,
                       reinterpret_cast<const __half*>(bias), epi, out32, reinterpret_cast<__half*>(out16), res32,
-                      stream ? static_cast<cudaStream_t>(stream) : ctx->stream);
+                      stream ? static_cast<cudaStream_t>(stream) : ctx->stream,
+                      reinterpret_cast<const __half*>(ln_g), reinterpret_cast<const __half*>(ln_b), eps);
 }
 
 int agxc_encoder_create(agxc_ctx* ctx, const agxc_encoder_desc* desc, agxc_encoder** out) {

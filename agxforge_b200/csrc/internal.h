@@ -176,8 +176,10 @@ int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half*
 
 // ---- the encoder's tensor-core GEMM (encoder.cu): C [M][N] = A [M][K] W [N][K]^T (+ bias; epi 0 fp32, 1 fp16
 // GELU, 2 fp32 + residual)
+// epi 3: out32 (may alias res32), out16 = LayerNorm(. + bias + res32) over whole rows (N 128..512)
 int launch_hgemm(const agxc_ctx* ctx, const __half* A, const __half* W, int M, int N, int K, const __half* bias,
-                 int epi, float* out32, __half* out16, const float* res32, cudaStream_t s);
+                 int epi, float* out32, __half* out16, const float* res32, cudaStream_t s,
+                 const __half* ln_g = nullptr, const __half* ln_b = nullptr, float eps = 0.f);
 int encoder_configure(const agxc_ctx* ctx);
 
 // ---- tensor parallelism (tp.cu): NCCL loaded at run time

@@ -321,10 +321,12 @@ typedef struct {
 #define AGXC_ENC_LN2_B 20
 
 /* The encoder's tensor-core GEMM alone (tests): C [M][N] = A [M][K] fp16 x W [N][K]^T fp16 + bias (fp16 [N],
- * nullable), epi 0: out32 fp32; 1: out16 = fp16(gelu_erf(.)); 2: out32 = . + res32. M % 128, N % 64, K % 64 == 0. */
+ * nullable), epi 0: out32 fp32; 1: out16 = fp16(gelu_erf(.)); 2: out32 = . + res32; 3: y = LayerNorm(. + res32)
+ * with gain ln_g, bias ln_b (fp16 [N]) and eps over whole rows (N 128, 256 or 384), out32 = y (may alias
+ * res32), out16 = fp16(y). M % 128, N % 64, K % 64 == 0. */
 AGXC_API int agxc_hgemm_dev(agxc_ctx* ctx, const uint16_t* A, const uint16_t* W, int M, int N, int K,
                             const uint16_t* bias, int epi, float* out32, uint16_t* out16, const float* res32,
-                            void* stream);
+                            const uint16_t* ln_g, const uint16_t* ln_b, float eps, void* stream);
 AGXC_API int agxc_encoder_create(agxc_ctx* ctx, const agxc_encoder_desc* desc, agxc_encoder** out);
 AGXC_API void agxc_encoder_free(agxc_encoder* e);
 /* One fp16 parameter (layer ignored for the embedding entries); `bytes` must be its exact size. */

@@ -35,8 +35,10 @@ def enc(torch):
     e.close()
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 64, 64), (256, 1152, 384), (4096, 384, 1536), (384, 1536, 384)])
-@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("M,N,K,epi", [(m, n, k, e) for (m, n, k) in [(128, 64, 64), (256, 1152, 384),
+                                                                      (4096, 384, 1536), (384, 1536, 384)]
+                                         for e in (0, 1, 2)] + [(256, 384, 384, 3), (4096, 384, 1536, 3),
+                                                                (128, 128, 64, 3), (256, 256, 256, 3)])
 def test_hgemm_against_torch(torch, M, N, K, epi):
     import ctypes as C
     from agxforge_b200 import _native as N_
@@ -48,9 +50,16 @@ def test_hgemm_against_torch(torch, M, N, K, epi):
     out32 = torch.full((M, N), float("nan"), device="cuda")
     out16 = torch.full((M, N), float("nan"), device="cuda").half()
     ref = A.float() @ W.float().T + bias.float()
+    g1 = (1 + 0.1 * torch.randn(N, device="cuda", generator=g)).half()
+    b1 = (0.1 * torch.randn(N, device="cuda", generator=g)).half()
+    if epi == 3:
+        out32 = res.clone()  # in place over the residual, as the encoder runs it
     N_.check(N_.lib().agxc_hgemm_dev(N_.context(0), C.c_void_p(A.data_ptr()), C.c_void_p(W.data_ptr()), M, N, K,
                                      C.c_void_p(bias.data_ptr()), epi, C.c_void_p(out32.data_ptr()),
-                                     C.c_void_p(out16.data_ptr()), C.c_void_p(res.data_ptr()), None), "hgemm")
+                                     C.c_void_p(out16.data_ptr()),
+                                     C.c_void_p(out32.data_ptr() if epi == 3 else res.data_ptr()),
+                                     C.c_void_p(g1.data_ptr()), C.c_void_p(b1.data_ptr()), C.c_float(1e-12), None),
+             "hgemm")
     torch.cuda.synchronize()
     # fp32 accumulation of exact fp16 products: only the summation order differs from the reference matmul
     tol = 1e-5 * (A.float().abs() @ W.float().abs().T).max().item() + 1e-6
@@ -60,8 +69,16 @@ def test_hgemm_against_torch(torch, M, N, K, epi):
         want = torch.nn.functional.gelu(ref, approximate="none")
         err = (out16.float() - want).abs()
         assert (err <= tol + 2 ** -10 * want.abs() + 1e-7).all(), err.max().item()
-    else:
+    elif epi == 2:
         assert (out32 - (ref + res)).abs().max().item() <= tol + 1e-6
+    else:
+        x = ref + res
+        c = x - x.mean(-1, keepdim=True)
+        want = c / torch.sqrt((c * c).mean(-1, keepdim=True) + 1e-12) * g1.float() + b1.float()
+        scale = 1.0 / torch.sqrt((c * c).mean(-1, keepdim=True))
+        assert ((out32 - want).abs() <= 4 * (tol + 1e-6) * scale * g1.float().abs() + 1e-5).all()
+        assert ((out16.float() - want).abs() <= 4 * (tol + 1e-6) * scale * g1.float().abs() + 2 ** -10 *
+                want.abs() + 1e-5).all()
 
 
 def test_reference_golden_vectors(enc):
@@ -93,7 +110,7 @@ def test_baseline_workload_against_oracle(enc):
     assert E.within_bound(got, half).all(), np.abs(got - half).max()
     for b in range(32):
         assert E.cosine(got[b], orig[b]) >= 0.999
-    assert t["launches"] == 1 + 7 * 6 + 1
+    assert t["launches"] == 1 + 7 * 6 + 1  # embedding, per layer qkv / attention / o / LN / up / down / LN, pooling
 
 
 def test_token_types_and_shorter_batches(enc):
@@ -126,3 +143,32 @@ def test_refusals(enc):
         enc.forward(dict(token_ids=ids, attention_mask=mask, position_ids=np.arange(32)[::-1]))
     with pytest.raises(ValueError):
         enc.forward(dict(token_ids=np.zeros((33, 8), np.int32), attention_mask=np.ones((33, 8), np.int32)))
+
+
+def test_long_sequences_fp32_attention_path(torch):
+    """Sequences longer than 128 tokens take the fp32 CUDA-core attention (the tensor-core kernel holds a whole
+    score row of at most 128 keys in registers); both paths meet the same bound."""
+    from agxforge_b200.inference.encoder import Encoder
+    cfg = dict(E.MINILM_L6, num_hidden_layers=2)
+    e = Encoder(cfg, max_batch=4, max_seq=200).load(E.make_params(7, cfg))
+    ids, mask = _workload(seed=8, B=4, S=200)
+    for S in (200, 128, 50):
+        got = e.forward(dict(token_ids=ids[:, :S], attention_mask=mask[:, :S]))
+        ref = E.forward(E.make_params(7, cfg), ids[:, :S], mask[:, :S], policy="half", config=cfg)
+        assert E.within_bound(got, ref).all(), (S, np.abs(got - ref).max())
+    e.close()
+
+
+def test_large_batch_fused_layernorm_epilogue(torch):
+    """Enough token rows for one full wave of 128-row tiles: o_proj and FFN down carry the LayerNorm in their
+    epilogue (5 launches a layer instead of 7), within the same bound."""
+    from agxforge_b200.inference.encoder import Encoder
+    cfg = dict(E.MINILM_L6, num_hidden_layers=2)
+    B, S = 152, 128                                   # 19,456 rows = 152 tiles >= 148 SMs
+    e = Encoder(cfg, max_batch=B, max_seq=S).load(E.make_params(9, cfg))
+    ids, mask = _workload(seed=10, B=B, S=S)
+    got, t = e.forward(dict(token_ids=ids, attention_mask=mask), timing=True)
+    assert t["launches"] == 1 + 5 * 2 + 1
+    ref = E.forward(E.make_params(9, cfg), ids, mask, policy="half", config=cfg)
+    assert E.within_bound(got, ref).all(), np.abs(got - ref).max()
+    e.close()
