@@ -1,7 +1,8 @@
 // batched.cu — the per-row steps of the batched decode step (B >= 32 sequences), between the tensor-core GEMMs of
 // qmm.cu: the projections produce fp32 rows y [B][n] in the packs' physical row order, and these kernels finish
 // them exactly as the single-sequence GEMV epilogues do (gemv_impl.cuh), so both paths share every rounding point:
-//   rope_append   bias, rotate-half RoPE at each sequence's position, q scale (fp16 q), K and V rows into the cache
+//   rope_append   bias, rotate-half RoPE at each row's position, q scale (fp16 q), K and V rows into the cache of the
+//                 row's sequence (the row itself, or one sequence for every row of a prefill chunk)
 //                 (the qkv pack's tile rows r and r + 8 are a RoPE pair; attention.py:1309-1323)
 //   residual_add16     h = y + x16 (fp32)                      (with_residual add16, qmv.py:112-120)
 //   residual_add32_16  x16 = fp16(y + h)                       (with_residual add32_to16, qmv.py:825-833)
@@ -23,7 +24,8 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 __global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows, const __half* __restrict__ bias,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                    const uint32_t* __restrict__ q0, int H, int KVH, int hd, int cap, float qscale,
-                                   __half* __restrict__ q16, __half* __restrict__ kc, __half* __restrict__ vc, int B) {
+                                   __half* __restrict__ q16, __half* __restrict__ kc, __half* __restrict__ vc, int B,
+                                   int seq) {
   const int pairs = rows / 2;
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * pairs) return;
@@ -41,6 +43,7 @@ __global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows
   }
   int pos = static_cast<int>(q0[b]);
   if (pos > cap - 1) pos = cap - 1;
+  const int sq = seq >= 0 ? seq : b;  // the cache sequence of this row (prefill: every row of one sequence)
   if (head < H + KVH) {
     const float c = cos_t[static_cast<size_t>(pos) * half + i1];
     const float s = sin_t[static_cast<size_t>(pos) * half + i1];
@@ -50,12 +53,12 @@ __global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows
       q[i1] = __float2half_rn(o1 * qscale);
       q[i2] = __float2half_rn(o2 * qscale);
     } else {
-      __half* k = kc + ((static_cast<size_t>(b) * KVH + (head - H)) * cap + pos) * hd;
+      __half* k = kc + ((static_cast<size_t>(sq) * KVH + (head - H)) * cap + pos) * hd;
       k[i1] = __float2half_rn(o1);
       k[i2] = __float2half_rn(o2);
     }
   } else {
-    __half* v = vc + ((static_cast<size_t>(b) * KVH + (head - H - KVH)) * cap + pos) * hd;
+    __half* v = vc + ((static_cast<size_t>(sq) * KVH + (head - H - KVH)) * cap + pos) * hd;
     v[i1] = __float2half_rn(y1);
     v[i2] = __float2half_rn(y2);
   }
@@ -243,9 +246,9 @@ inline unsigned blocks_for(long long n, int threads) { return static_cast<unsign
 
 int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
-                       __half* vc, int B, cudaStream_t s) {
+                       __half* vc, int B, cudaStream_t s, int seq) {
   rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
-      y, ld, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B);
+      y, ld, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

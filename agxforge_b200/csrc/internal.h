@@ -160,9 +160,14 @@ int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows
 int encode_act_map(CUtensorMap* m, const void* x, int B, int K);
 
 // ---- the per-row steps of the batched decode step (batched.cu)
+// q0: each row's position; seq < 0: row b is sequence b's (batched decode), else every row is sequence seq's (prefill)
 int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
-                       __half* vc, int B, cudaStream_t s);
+                       __half* vc, int B, cudaStream_t s, int seq = -1);
+// causal attention of M prompt rows at positions p0 .. p0 + M - 1 of cache sequence `seq` (prefill.cu)
+int launch_prefill_attention(const __half* q16, const __half* kc, const __half* vc, int M, int p0, int H, int KVH,
+                             int hd, int cap, int seq, __half* out, cudaStream_t s);
+int prefill_configure(const agxc_ctx* ctx);
 int launch_residual16(const float* y, int ld, const __half* x16, float* h, int d, int B, cudaStream_t s);
 int launch_residual32(const float* y, int ld, const float* h, __half* x16, int d, int B, cudaStream_t s);
 int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_t s);

@@ -102,9 +102,22 @@ struct agxc_model {
   unsigned* tile_ctr = nullptr; // [d / 128]
   unsigned* epoch = nullptr;    // steps run in the fused mode
   std::string tp_fused_why;
+  // the prefill section (allocated on first use): chunks of up to kPrefillRows prompt rows of one sequence
+  __half* pf_x16 = nullptr;     // [rows][d]
+  float* pf_h = nullptr;        // [rows][d]
+  __half* pf_xn16 = nullptr;    // [rows][d]
+  float* pf_y = nullptr;        // [rows][max(qkv rows, 2F, d)]
+  __half* pf_q16 = nullptr;     // [rows][H][hd]
+  __half* pf_attn = nullptr;    // [rows][H hd]
+  __half* pf_act = nullptr;     // [rows][F]
+  uint32_t* pf_pos = nullptr;   // [rows]
+  uint32_t* pf_tok = nullptr;   // [cap] the prompt
 };
 
 namespace agxc {
+
+int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
+            const QmmPush* push = nullptr);
 
 namespace {
 
@@ -265,11 +278,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     return 0;
   };
   auto gemm = [&](const agxc_pack& pk, const __half* x, float* y, int ld, const QmmPush* push = nullptr) -> int {
-    const int tiles = pk.n / 128, G = pk.k / 64;
-    int ks = 1;
-    while (tiles * ks * 2 <= m->ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
-    if (ks > 1) AGXC_CUDA(cudaMemset2DAsync(y, static_cast<size_t>(ld) * 4, 0, static_cast<size_t>(pk.n) * 4, B, s));
-    return launch_qmm(m->ctx, &pk, x, B, y, ld, ks, s, push);
+    return run_qmm(m, pk, x, B, y, ld, s, push);
   };
   const bool fused = m->comm && m->tp_fused && m->tp_fused_ok;
   auto push_of = [&](int buf) {  // this rank's slot of buffer `buf` on every rank, and their counters
@@ -801,6 +810,120 @@ int model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
   return 0;
 }
 
+constexpr int kPrefillRows = 256;  // rows per prefill chunk (the tensor-core GEMM's largest row count)
+
+__global__ void positions_kernel(uint32_t* pos, int p0, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) pos[i] = static_cast<uint32_t>(p0 + i);
+}
+
+// Y [rows][ld] = X [rows][K] W^T on the tensor cores, the K range split over CTAs when the 128-row tiles alone leave
+// SMs idle (Y zeroed first: the CTAs add into it).
+int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
+            const QmmPush* push) {
+  const int tiles = pk.n / 128, G = pk.k / 64;
+  int ks = 1;
+  while (tiles * ks * 2 <= m->ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
+  if (ks > 1) AGXC_CUDA(cudaMemset2DAsync(y, static_cast<size_t>(ld) * 4, 0, static_cast<size_t>(pk.n) * 4, rows, s));
+  return launch_qmm(m->ctx, &pk, x, rows, y, ld, ks, s, push);
+}
+
+int prefill_buffers(agxc_model* m) {
+  if (m->pf_x16) return 0;
+  const agxc_model_desc& D = m->d;
+  const size_t R = kPrefillRows, d = D.d_model, F = D.ffn;
+  const size_t yn = std::max({static_cast<size_t>(m->qkv_rows), 2 * F, d});
+  int rc;
+  if ((rc = dalloc_t(m, &m->pf_x16, R * d)) || (rc = dalloc_t(m, &m->pf_h, R * d)) ||
+      (rc = dalloc_t(m, &m->pf_xn16, R * d)) || (rc = dalloc_t(m, &m->pf_y, R * yn)) ||
+      (rc = dalloc_t(m, &m->pf_q16, R * m->attn_dim)) || (rc = dalloc_t(m, &m->pf_attn, R * m->attn_dim)) ||
+      (rc = dalloc_t(m, &m->pf_act, R * F)) || (rc = dalloc_t(m, &m->pf_pos, R)) ||
+      (rc = dalloc_t(m, &m->pf_tok, static_cast<size_t>(D.cap))))
+    return rc;
+  // rows past a chunk's end are GEMM padding: they start at zero and only ever hold finite values
+  AGXC_CUDA(cudaMemset(m->pf_x16, 0, R * d * 2));
+  AGXC_CUDA(cudaMemset(m->pf_attn, 0, R * m->attn_dim * 2));
+  AGXC_CUDA(cudaMemset(m->pf_act, 0, R * F * 2));
+  return 0;
+}
+
+// Start sequence b with its prompt and run positions 0 .. n-2 as the prefill section: chunks of up to 256 rows, each
+// layer as RMSNorm rows -> qkv GEMM -> RoPE + append (the chunk's K/V rows into b's cache) -> causal attention of the
+// chunk -> o_proj GEMM -> add16 -> RMSNorm rows -> gate/up GEMM -> SwiGLU -> down GEMM -> add32_to16 (the reference's
+// prefill steps, agxforge/inference/prefill.py:8-14). Then q0 = n-1 and x = embedding(prompt[n-1]): the next decode
+// step runs position n-1 and chooses the first generated token, as after n-1 teacher-forced decode steps.
+int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timing* t) {
+  const agxc_model_desc& D = m->d;
+  if (m->comm) return fail(AGXC_EUNSUPPORTED, "prefill: tensor-parallel models feed the prompt through decode steps");
+  if (m->qkv_rows % 128 || D.d_model % 128 || (2 * D.ffn) % 128)
+    return fail(AGXC_EUNSUPPORTED, "prefill: needs qkv rows, d_model and 2 x ffn multiples of 128");
+  if (int rc = model_start(m, b, prompt, n)) return rc;
+  if (int rc = prefill_buffers(m)) return rc;
+  cudaStream_t s = m->ctx->stream;
+  const auto h0 = std::chrono::steady_clock::now();
+  AGXC_CUDA(cudaEventRecord(m->ev0, s));
+  const int total = n - 1;
+  const int d = D.d_model, F = D.ffn, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim;
+  const size_t layer_kv = static_cast<size_t>(D.batch) * KVH * D.cap * hd;
+  const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  int rc = 0, launches = 0;
+  if (total > 0) {
+    std::vector<uint32_t> tok(prompt, prompt + n);
+    AGXC_CUDA(cudaMemcpyAsync(m->pf_tok, tok.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, s));
+  }
+  for (int p0 = 0; p0 < total && !rc; p0 += kPrefillRows) {
+    const int Mc = std::min(kPrefillRows, total - p0);
+    const int Mp = std::max(32, (Mc + 15) / 16 * 16);
+    embed_rows_kernel<<<Mc, 256, 0, s>>>(m->embed, d, m->pf_tok + p0, Mc, m->pf_x16);
+    positions_kernel<<<(Mc + 255) / 256, 256, 0, s>>>(m->pf_pos, p0, Mc);
+    AGXC_CUDA(cudaGetLastError());
+    launches += 2;
+    for (int l = 0; l < D.n_layers && !rc; ++l) {
+      const __half* g1 = m->gains + static_cast<size_t>(l) * 2 * d;
+      const __half* bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
+      __half* kc = m->kcache + l * layer_kv;
+      __half* vc = m->vcache + l * layer_kv;
+      if ((rc = launch_rmsnorm(m->pf_x16, 0, Mp, d, g1, D.eps, m->pf_xn16, s)) ||
+          (rc = run_qmm(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, s)) ||
+          (rc = launch_rope_append(m->pf_y, m->qkv_rows, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd,
+                                   D.cap, qscale, m->pf_q16, kc, vc, Mc, s, b)) ||
+          (rc = launch_prefill_attention(m->pf_q16, kc, vc, Mc, p0, H, KVH, hd, D.cap, b, m->pf_attn, s)) ||
+          (rc = run_qmm(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, s)) ||
+          (rc = launch_residual16(m->pf_y, d, m->pf_x16, m->pf_h, d, Mp, s)) ||
+          (rc = launch_rmsnorm(m->pf_h, 1, Mp, d, g1 + d, D.eps, m->pf_xn16, s)) ||
+          (rc = run_qmm(m, m->gu[l], m->pf_xn16, Mp, m->pf_y, 2 * F, s)) ||
+          (rc = launch_swiglu(m->pf_y, 2 * F, m->pf_act, F, Mp, s)) ||
+          (rc = run_qmm(m, m->down[l], m->pf_act, Mp, m->pf_y, d, s)) ||
+          (rc = launch_residual32(m->pf_y, d, m->pf_h, m->pf_x16, d, Mp, s)))
+        break;
+      launches += 11;
+    }
+  }
+  if (rc) return rc;
+  // the last prompt token is the next decode step's input, at position n-1
+  const uint32_t q0 = static_cast<uint32_t>(n - 1);
+  AGXC_CUDA(cudaMemcpyAsync(m->q0 + b, &q0, 4, cudaMemcpyHostToDevice, s));
+  AGXC_CUDA(cudaMemcpyAsync(m->x16 + static_cast<size_t>(b) * d, m->embed + static_cast<size_t>(prompt[n - 1]) * d,
+                            static_cast<size_t>(d) * 2, cudaMemcpyDeviceToDevice, s));
+  AGXC_CUDA(cudaEventRecord(m->ev1, s));
+  AGXC_CUDA(cudaEventSynchronize(m->ev1));
+  if (t) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, m->ev0, m->ev1);
+    t->gpu_ms = ms;
+    t->host_ms = std::chrono::duration<float, std::milli>(std::chrono::steady_clock::now() - h0).count();
+    t->launches_per_step = launches;
+  }
+  uint32_t err = 0;
+  AGXC_CUDA(cudaMemcpy(&err, m->ctx->err_dev, 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    const uint32_t zero = 0;
+    cudaMemcpy(m->ctx->err_dev, &zero, 4, cudaMemcpyHostToDevice);
+    return fail(err & kErrMbarTimeout ? AGXC_ETIMEOUT : AGXC_ECORRUPT, "prefill: device error word " + std::to_string(err));
+  }
+  return 0;
+}
+
 int model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {
   const agxc_model_desc& D = m->d;
   if (b < 0 || b >= D.batch || pos < 0 || n < 0 || pos + n > D.cap) return fail(AGXC_EINVAL, "force: range");
@@ -1008,6 +1131,11 @@ int64_t agxc_model_weight_bytes(const agxc_model* m) {
 int agxc_model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
   if (!m || !prompt) return agxc::fail(AGXC_EINVAL, "start: null argument");
   return agxc::model_start(m, b, prompt, n);
+}
+
+int agxc_model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timing* t) {
+  if (!m || !prompt) return agxc::fail(AGXC_EINVAL, "prefill: null argument");
+  return agxc::model_prefill(m, b, prompt, n, t);
 }
 
 int agxc_model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {

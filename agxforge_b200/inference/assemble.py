@@ -205,6 +205,15 @@ class DecodeModel:
         p = np.ascontiguousarray(np.asarray(prompt, np.int32))
         N.check(N.lib().agxc_model_start(self._h, b, p.ctypes.data_as(C.c_void_p), p.size), "start")
 
+    def prefill(self, b, prompt):
+        """Start sequence b with its prompt and run positions 0 .. len-2 as the prefill section (chunks of up to 256
+        rows on the tensor-core GEMM with causal attention); the next decode step runs the last prompt token. Returns
+        {gpu_ms, host_ms, launches}."""
+        p = np.ascontiguousarray(np.asarray(prompt, np.int32))
+        t = N.Timing()
+        N.check(N.lib().agxc_model_prefill(self._h, b, p.ctypes.data_as(C.c_void_p), p.size, C.byref(t)), "prefill")
+        return dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches=t.launches_per_step)
+
     def force(self, b, pos, tokens):
         t = np.ascontiguousarray(np.asarray(tokens, np.int32))
         N.check(N.lib().agxc_model_force(self._h, b, pos, t.ctypes.data_as(C.c_void_p), t.size), "force")

@@ -499,6 +499,16 @@ def main():
     step_s = gpu_ms / 1e3 / K
     step_gbs = step_bytes / step_s / 1e9
 
+    # the prefill section on the same model: the history as a prompt of `hist` tokens (positions 0 .. hist-2 through
+    # the tensor-core GEMMs and the causal prefill attention), one warm-up then one timed run (device time)
+    prefill = None
+    if tp == 1 and S.QKV % 128 == 0 and S.D_MODEL % 128 == 0:
+        prompt = rng.integers(0, S.VOCAB, hist).tolist()
+        m.prefill(0, prompt)
+        pt = m.prefill(0, prompt)
+        prefill = dict(tokens=hist - 1, gpu_ms=round(pt["gpu_ms"], 3),
+                       tok_s=round((hist - 1) / (pt["gpu_ms"] / 1e3), 1), launches=pt["launches"])
+
     cpu = None
     if rank == 0 and not args.no_cpu:
         per_token, t_layer, t_head, cores = cpu_baseline_sample(m, args.ref_layers, hist)
@@ -525,6 +535,7 @@ def main():
                                frac=round(step_gbs / peak, 4), bytes_per_token=int(step_bytes / batch),
                                weight_bytes=w_bytes, peak_source=peak_kind),
             kernels=kinds,
+            prefill=prefill,
             plans=m.plan_info(),
             cpu_baseline=cpu,
             clocks=clk.summary(),

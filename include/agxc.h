@@ -218,6 +218,13 @@ typedef struct {
   float host_ms;              /* host wall time of the call */
   int32_t launches_per_step;  /* kernels in one step's graph */
 } agxc_timing;
+/* Start sequence b with its prompt (as agxc_model_start) and run positions 0 .. n-2 as the PREFILL section
+ * (agxforge/inference/prefill.py:1-30: the prompt as M-row passes): chunks of up to 256 rows through every layer on the
+ * tensor-core GEMM (agxc_qmm) with a causal attention over the chunk, writing b's KV cache rows 0 .. n-2. Leaves
+ * q0 = n-1 and x = embedding(prompt[n-1]), so the next agxc_decode step runs position n-1 and chooses the first
+ * generated token: the state n-1 teacher-forced decode steps would leave (within rounding). Needs qkv rows, d_model
+ * and 2 x ffn multiples of 128 and one device; `t` (nullable) gets the device time. */
+AGXC_API int agxc_model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timing* t);
 AGXC_API int agxc_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* tokens_out, float* logits_out,
                 int sync_each, agxc_timing* t);
 
