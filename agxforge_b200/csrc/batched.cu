@@ -10,6 +10,7 @@
 //   argmax_gen    per sequence: the first maximum of the logits, then the generation step (argmax.py:141-215,
 //                 assemble.py:918-930): forced token, else the logged one, else the argmax; log, q0 + 1, x16 = emb[tok]
 //   argmax_part / gen_from_pairs   the same split around an all-gather when the vocabulary is sliced over ranks
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -192,52 +193,72 @@ __global__ void gen_from_pairs_kernel(const uint32_t* __restrict__ pairs, int ra
   gen_step(b, bi, V, embed, d, q0, log, cap, tok_out, force_next, x16, err, &s_tok);
 }
 
-// Tensor parallel, after the GEMM's peer pushes: wait (bounded, 2 s of the global timer) until every rank's tiles
-// have arrived, then out = sum over ranks in rank order + residual, the same on every rank (the sums are
-// bit-identical everywhere because every rank adds the same slots in the same order).
-__global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, const unsigned* flag,
-                                 const unsigned* epoch, int uses_per_step, int use_in_step, int tiles,
-                                 const __half* __restrict__ res16, const float* __restrict__ res32,
-                                 float* __restrict__ out32, __half* __restrict__ out16, int d, int B, unsigned* err) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    const unsigned use = *epoch * static_cast<unsigned>(uses_per_step) + static_cast<unsigned>(use_in_step);
-    const unsigned target = (use + 1u) * static_cast<unsigned>(ranks * tiles);
+// A bounded spin until *flag reaches target (the signed difference handles wrap-around); false after 2 s.
+__device__ bool wait_flag_sys(const unsigned* flag, unsigned target, unsigned* err) {
+  const uint64_t t0 = globaltimer_ns();
+  for (unsigned it = 0;; ++it) {
     unsigned v;
-    int ok = 1;
-    const uint64_t t0 = globaltimer_ns();
-    for (unsigned it = 0;; ++it) {
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-      if (static_cast<int>(v - target) >= 0) break;
-      if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
-        atomicOr(err, kErrMbarTimeout);
-        ok = 0;
-        break;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (static_cast<int>(v - target) >= 0) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+      atomicOr(err, kErrMbarTimeout);
+      return false;
+    }
+  }
+}
+
+// Tensor parallel, after the GEMM's pushes. Two-shot (one cooperative grid: its blocks wait on one another's gather
+// signals, so all are resident): this rank's rows [rank d / ranks, ...) = the sum over ranks in rank order plus the
+// residual, stored into every rank's residual stream. One-shot: every row, reduced here and stored here only. Either
+// way the sums are bit-identical on every rank: the same slots added in the same order.
+__global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, int rank, const unsigned* flag,
+                                 const unsigned* epoch, int uses_per_step, int use_in_step, int tiles_per_rank,
+                                 const __half* __restrict__ res16, const float* __restrict__ res32, TpGather gather,
+                                 int d, int B, unsigned* err, int two_shot) {
+  __shared__ int s_ok;
+  const unsigned use = *epoch * static_cast<unsigned>(uses_per_step) + static_cast<unsigned>(use_in_step);
+  const unsigned arrivals = static_cast<unsigned>(ranks * tiles_per_rank * (two_shot ? 1 : ranks));
+  if (threadIdx.x == 0) s_ok = wait_flag_sys(flag, (use + 1u) * arrivals, err);
+  __syncthreads();
+  const int w = two_shot ? d / ranks : d, n0 = two_shot ? rank * w : 0;  // the rows reduced here
+  const int rlo = two_shot ? 0 : rank, rhi = two_shot ? ranks : rank + 1;  // the ranks whose streams are written
+  const size_t slot = static_cast<size_t>(B) * d;
+  const int per_row = w / 4;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * per_row; i += gridDim.x * blockDim.x) {
+    const int b = i / per_row;
+    const size_t at = static_cast<size_t>(b) * d + n0 + (i % per_row) * 4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s_ok) {
+      for (int r = 0; r < ranks; ++r) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(recv + r * slot + at));
+        a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
       }
     }
-    s_ok = ok;
-  }
-  __syncthreads();
-  const size_t n = static_cast<size_t>(B) * d;
-  const size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 4;
-  if (i >= n) return;
-  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (s_ok) {
-    for (int r = 0; r < ranks; ++r) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(recv + r * n + i));
-      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+    if (res16) {  // h = sum + x16 (o_proj, add16)
+      const __half2 x01 = *reinterpret_cast<const __half2*>(res16 + at);
+      const __half2 x23 = *reinterpret_cast<const __half2*>(res16 + at + 2);
+      const float4 o = make_float4(a.x + __low2float(x01), a.y + __high2float(x01), a.z + __low2float(x23),
+                                   a.w + __high2float(x23));
+      for (int r = rlo; r < rhi; ++r) *reinterpret_cast<float4*>(gather.out32[r] + at) = o;
+    } else {      // x16 = fp16(sum + h) (down, add32_to16)
+      const float4 h = *reinterpret_cast<const float4*>(res32 + at);
+      const __half2 o01 = __floats2half2_rn(a.x + h.x, a.y + h.y), o23 = __floats2half2_rn(a.z + h.z, a.w + h.w);
+      for (int r = rlo; r < rhi; ++r) {
+        *reinterpret_cast<__half2*>(gather.out16[r] + at) = o01;
+        *reinterpret_cast<__half2*>(gather.out16[r] + at + 2) = o23;
+      }
     }
   }
-  if (res16) {  // h = sum + x16 (o_proj, add16)
-    const __half2 x01 = *reinterpret_cast<const __half2*>(res16 + i);
-    const __half2 x23 = *reinterpret_cast<const __half2*>(res16 + i + 2);
-    *reinterpret_cast<float4*>(out32 + i) = make_float4(a.x + __low2float(x01), a.y + __high2float(x01),
-                                                        a.z + __low2float(x23), a.w + __high2float(x23));
-  } else {      // x16 = fp16(sum + h) (down, add32_to16)
-    const float4 h = *reinterpret_cast<const float4*>(res32 + i);
-    *reinterpret_cast<__half2*>(out16 + i) = __floats2half2_rn(a.x + h.x, a.y + h.y);
-    *reinterpret_cast<__half2*>(out16 + i + 2) = __floats2half2_rn(a.z + h.z, a.w + h.w);
+  if (!two_shot) return;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < ranks; ++r)
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(gather.gflag[r]) : "memory");
+    // every rank's rows are here once every block of every rank has signalled this use
+    wait_flag_sys(gather.gflag[rank], (use + 1u) * static_cast<unsigned>(ranks) * gridDim.x, err);
   }
+  __syncthreads();
 }
 
 inline unsigned blocks_for(long long n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
@@ -278,13 +299,24 @@ int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, ui
   return 0;
 }
 
-int launch_tp_reduce(const float* recv, int ranks, const unsigned* flag, const unsigned* epoch, int uses_per_step,
-                     int use_in_step, int tiles, const __half* res16, const float* res32, float* out32,
-                     __half* out16, int d, int B, unsigned* err, cudaStream_t s) {
-  if (d % 4) return fail(AGXC_EINVAL, "tp_reduce: d multiple of 4");
-  tp_reduce_kernel<<<blocks_for(static_cast<long long>(B) * d / 4, 256), 256, 0, s>>>(
-      recv, ranks, flag, epoch, uses_per_step, use_in_step, tiles, res16, res32, out32, out16, d, B, err);
-  AGXC_CUDA(cudaGetLastError());
+int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* flag, const unsigned* epoch,
+                     int uses_per_step, int use_in_step, int tiles_per_rank, const __half* res16, const float* res32,
+                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot) {
+  if (d % (4 * ranks)) return fail(AGXC_EINVAL, "tp_reduce: d a multiple of 4 x ranks");
+  const long long elems4 = static_cast<long long>(B) * d / (two_shot ? ranks : 1) / 4;
+  // two-shot: a fixed grid, the same on every rank (the gather target counts every rank's blocks), all resident
+  const int grid = static_cast<int>(two_shot ? std::min<long long>(kNumSMs, (elems4 + 255) / 256) : (elems4 + 255) / 256);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = two_shot ? 1 : 0;
+  AGXC_CUDA(cudaLaunchKernelEx(&cfg, tp_reduce_kernel, recv, ranks, rank, flag, epoch, uses_per_step, use_in_step,
+                               tiles_per_rank, res16, res32, gather, d, B, err, two_shot ? 1 : 0));
   return 0;
 }
 

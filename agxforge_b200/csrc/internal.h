@@ -199,23 +199,34 @@ int tp_wait(TpComm* c, cudaEvent_t done, int timeout_ms);
 
 // ---- the batched GEMM (qmm.cu): Y [B][ldy] fp32 = X [B][K] fp16 W^T, B = 32..256 (multiple of 16), tcgen05 + TMEM
 int qmm_configure(const agxc_ctx* ctx);
-// The tensor-parallel push of finished output tiles (the GEMM + all-reduce fusion): the last of a tile's K-split
-// CTAs stores the tile's B x 128 block of Y into every rank's receive slot for this rank (peer memory over NVLink,
-// plain stores), then adds 1 to every rank's arrival counter (system scope, release).
+// The tensor-parallel push of finished output tiles (the GEMM + all-reduce fusion, reduce-scatter half): rank r owns
+// output rows [r N / ranks, (r + 1) N / ranks); the last of a tile's K-split CTAs stores the tile's B x 128 block of Y
+// into its owner's receive slot for this rank (peer memory over NVLink, plain stores), then adds 1 to the owner's
+// arrival counter (system scope, release).
 struct QmmPush {
   float* slot[8] = {};      // rank r's receive slot for this rank's partial sums, [B][N]
   unsigned* flag[8] = {};   // rank r's arrival counter of that slot buffer
   unsigned* tile_ctr = nullptr;  // [N / 128] arrival counts of the K-split CTAs (local; reset by the last)
   int ranks = 0;
+  int tiles_per_rank = 0;   // 128-row tiles owned by each rank
+  int to_owner = 0;         // 1: each tile to its owner only (two-shot); 0: every tile to every rank (one-shot)
 };
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
                cudaStream_t s, const QmmPush* push = nullptr);
-// After the pushes of every rank: out = sum over ranks r (in order) of recv[r] [B][d] + residual, waiting (bounded)
-// until *flag >= (use + 1) x ranks x tiles with use = *epoch x uses_per_step + use_in_step. res16 -> h fp32 (o_proj),
-// or res32 -> x16 fp16 (down).
-int launch_tp_reduce(const float* recv, int ranks, const unsigned* flag, const unsigned* epoch, int uses_per_step,
-                     int use_in_step, int tiles, const __half* res16, const float* res32, float* out32,
-                     __half* out16, int d, int B, unsigned* err, cudaStream_t s);
+// After the GEMM's pushes (use = *epoch x uses_per_step + use_in_step; every wait bounded). One-shot: wait until every
+// rank's tiles are here (*flag >= (use + 1) x ranks x ranks x tiles_per_rank), reduce every row in rank order plus the
+// residual into this rank's own output. Two-shot (one cooperative grid): wait for this rank's rows only (*flag >=
+// (use + 1) x ranks x tiles_per_rank), reduce them, store the result into every rank's output rows (peer stores),
+// signal every rank's gather counter, then wait until every rank's rows have arrived here. res16 -> out32 (h fp32,
+// o_proj) or res32 -> out16 (x16 fp16, down).
+struct TpGather {
+  float* out32[8] = {};
+  __half* out16[8] = {};
+  unsigned* gflag[8] = {};  // rank r's gather counter of this buffer
+};
+int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* flag, const unsigned* epoch,
+                     int uses_per_step, int use_in_step, int tiles_per_rank, const __half* res16, const float* res32,
+                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 // tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,

@@ -96,10 +96,16 @@ struct agxc_model {
   // counters, one allocation exported to the other ranks by CUDA IPC; peer[r] = rank r's allocation, mapped here
   int tp_fused = 0;             // 1: o_proj and down push their tiles to every rank and reduce locally (no NCCL)
   int tp_fused_ok = 0;          // the peer mappings exist on every rank
+  int tp_fused_ran = 0;         // a fused step has run (the variant is fixed from then on)
+  int tp_two_shot = 0;          // 1 (4 or more ranks): reduce-scatter by the GEMM + all-gather; 0: every rank's tiles
+                                // to every rank (2 ranks: one synchronisation instead of two)
   float* recv = nullptr;
   unsigned* recv_flags = nullptr;
   void* peer[8] = {};
   unsigned* tile_ctr = nullptr; // [d / 128]
+  size_t peer_flags_off = 0;    // byte offsets in every rank's exported allocation: counters (2 arrival, 2 gather),
+  size_t peer_h_off = 0;        // the residual stream h [B][d] fp32 and x16 [B][d] fp16 (the model's own h and x16)
+  size_t peer_x16_off = 0;
   unsigned* epoch = nullptr;    // steps run in the fused mode
   std::string tp_fused_why;
   // the prefill section (allocated on first use): chunks of up to kPrefillRows prompt rows of one sequence
@@ -281,18 +287,29 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     return run_qmm(m, pk, x, B, y, ld, s, push);
   };
   const bool fused = m->comm && m->tp_fused && m->tp_fused_ok;
-  auto push_of = [&](int buf) {  // this rank's slot of buffer `buf` on every rank, and their counters
+  auto push_of = [&](int buf) {  // this rank's slot of buffer `buf` on every rank, and their arrival counters
     QmmPush ps;
     ps.ranks = m->tp;
+    ps.tiles_per_rank = d / 128 / m->tp;
+    ps.to_owner = m->tp_two_shot;
     ps.tile_ctr = m->tile_ctr;
     const size_t slot = (static_cast<size_t>(buf) * m->tp + m->tp_rank) * B * d;
-    const size_t flags = static_cast<size_t>(2) * m->tp * B * d;
     for (int r = 0; r < m->tp; ++r) {
-      float* base = static_cast<float*>(m->peer[r]);
-      ps.slot[r] = base + slot;
-      ps.flag[r] = reinterpret_cast<unsigned*>(base + flags) + buf;
+      uint8_t* base = static_cast<uint8_t*>(m->peer[r]);
+      ps.slot[r] = reinterpret_cast<float*>(base) + slot;
+      ps.flag[r] = reinterpret_cast<unsigned*>(base + m->peer_flags_off) + buf;
     }
     return ps;
+  };
+  auto gather_of = [&](int buf) {  // every rank's residual stream (h for o_proj, x16 for down) and gather counter
+    TpGather g;
+    for (int r = 0; r < m->tp; ++r) {
+      uint8_t* base = static_cast<uint8_t*>(m->peer[r]);
+      g.out32[r] = reinterpret_cast<float*>(base + m->peer_h_off);
+      g.out16[r] = reinterpret_cast<__half*>(base + m->peer_x16_off);
+      g.gflag[r] = reinterpret_cast<unsigned*>(base + m->peer_flags_off) + 2 + buf;
+    }
+    return g;
   };
   const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
   m->launches = 0;
@@ -308,11 +325,12 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
       return rc;
     a.pdl = 0;
     if ((rc = open()) || (rc = launch_attention(m->ctx, a, s)) || (rc = close())) return rc;
-    if (fused) {  // o_proj tiles pushed to every rank by the GEMM; the sum over ranks fused with the residual
+    if (fused) {  // o_proj tiles pushed to their owner ranks by the GEMM; each owner's sum + residual to every rank
       QmmPush ps = push_of(0);
       if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, &ps)) ||
-          (rc = launch_tp_reduce(m->recv, m->tp, m->recv_flags, m->epoch, D.n_layers, l, d / 128, m->x16, nullptr,
-                                 m->h, nullptr, d, B, m->ctx->err_dev, s)) ||
+          (rc = launch_tp_reduce(m->recv, m->tp, m->tp_rank, m->recv_flags, m->epoch, D.n_layers, l,
+                                 ps.tiles_per_rank, m->x16, nullptr, gather_of(0), d, B, m->ctx->err_dev, s,
+                                 m->tp_two_shot)) ||
           (rc = close()))
         return rc;
     } else if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, nullptr)) ||
@@ -327,8 +345,9 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     if (fused) {
       QmmPush ps = push_of(1);
       if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, &ps)) ||
-          (rc = launch_tp_reduce(m->recv + static_cast<size_t>(m->tp) * B * d, m->tp, m->recv_flags + 1, m->epoch,
-                                 D.n_layers, l, d / 128, nullptr, m->h, nullptr, m->x16, d, B, m->ctx->err_dev, s)) ||
+          (rc = launch_tp_reduce(m->recv + static_cast<size_t>(m->tp) * B * d, m->tp, m->tp_rank, m->recv_flags + 1,
+                                 m->epoch, D.n_layers, l, ps.tiles_per_rank, nullptr, m->h, gather_of(1), d, B,
+                                 m->ctx->err_dev, s, m->tp_two_shot)) ||
           (rc = close()))
         return rc;
     } else if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, nullptr)) ||
@@ -443,13 +462,21 @@ int tp_barrier(agxc_model* m) {
 int tp_peer_setup(agxc_model* m) {
   const int T = m->tp, B = m->d.batch, d = m->d.d_model;
   cudaStream_t s = m->ctx->stream;
-  const size_t bytes = static_cast<size_t>(2) * T * B * d * 4 + 256;
+  if ((d / 128) % T) {
+    m->tp_fused_why = "d_model / 128 is not a multiple of the ranks";
+    return 0;
+  }
+  // [2][T][B][d] fp32 receive slots | 4 counters | h [B][d] fp32 | x16 [B][d] fp16, each 256-byte aligned
+  m->peer_flags_off = static_cast<size_t>(2) * T * B * d * 4;
+  m->peer_h_off = m->peer_flags_off + 256;
+  m->peer_x16_off = m->peer_h_off + align_up(static_cast<size_t>(B) * d * 4, 256);
+  const size_t bytes = m->peer_x16_off + align_up(static_cast<size_t>(B) * d * 2, 256);
   void* base = nullptr;
   AGXC_CUDA(cudaMalloc(&base, bytes));
   m->allocs.push_back(base);
   AGXC_CUDA(cudaMemset(base, 0, bytes));
   m->recv = static_cast<float*>(base);
-  m->recv_flags = reinterpret_cast<unsigned*>(m->recv + static_cast<size_t>(2) * T * B * d);
+  m->recv_flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(base) + m->peer_flags_off);
   if (int rc = dalloc_t(m, &m->tile_ctr, static_cast<size_t>(d / 128))) return rc;
   if (int rc = dalloc_t(m, &m->epoch, 1)) return rc;
   AGXC_CUDA(cudaMemset(m->tile_ctr, 0, static_cast<size_t>(d / 128) * 4));
@@ -492,8 +519,17 @@ int tp_peer_setup(agxc_model* m) {
   float sum = 0.f;
   AGXC_CUDA(cudaMemcpy(&sum, m->ybuf, 4, cudaMemcpyDeviceToHost));
   m->tp_fused_ok = sum == static_cast<float>(T);
+  m->tp_two_shot = T >= 4;
   if (!m->tp_fused_ok && m->tp_fused_why.empty()) m->tp_fused_why = "a peer rank could not map the buffers";
   m->tp_fused = m->tp_fused_ok;
+  if (m->tp_fused_ok) {  // the residual stream lives in the exported allocation: owners write every rank's rows
+    AGXC_CUDA(cudaMemcpy(static_cast<uint8_t*>(base) + m->peer_h_off, m->h, static_cast<size_t>(B) * d * 4,
+                         cudaMemcpyDeviceToDevice));
+    AGXC_CUDA(cudaMemcpy(static_cast<uint8_t*>(base) + m->peer_x16_off, m->x16, static_cast<size_t>(B) * d * 2,
+                         cudaMemcpyDeviceToDevice));
+    m->h = reinterpret_cast<float*>(static_cast<uint8_t*>(base) + m->peer_h_off);
+    m->x16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(base) + m->peer_x16_off);
+  }
   return 0;
 }
 
@@ -999,6 +1035,7 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
   if (logits_out && !D.keep_logits) return fail(AGXC_EINVAL, "decode: logits_out needs keep_logits");
   int rc = ensure_graph(m);
   if (rc) return rc;
+  if (m->comm && m->tp_fused && m->tp_fused_ok) m->tp_fused_ran = 1;
   cudaStream_t s = m->ctx->stream;
   const size_t need = static_cast<size_t>(std::max(steps, 1)) * D.batch;
   if (tokens_out && m->h_tok_n < need) {
@@ -1060,6 +1097,7 @@ int model_profile(agxc_model* m, int steps, float* kind_ms, int32_t* kind_launch
   cudaStream_t s = m->ctx->stream;
   const int saved_pdl = m->pdl;
   m->pdl = 0;  // events between launches: every kernel timed on its own
+  if (m->comm && m->tp_fused && m->tp_fused_ok) m->tp_fused_ran = 1;
   int rc = 0;
   for (int i = 0; i < steps && !rc; ++i) {
     rc = enqueue_step(m, s, ev.data());
@@ -1213,7 +1251,8 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
                   ", \"kv_heads\": " + std::to_string(m->d.n_kv_heads) + ", \"ffn\": " +
                   std::to_string(m->d.ffn) + ", \"vocab_offset\": " + std::to_string(m->v0) +
                   ", \"vocab_count\": " + std::to_string(m->d.vocab) + ", \"fused\": " +
-                  std::to_string(m->comm && m->tp_fused && m->tp_fused_ok) + ", \"fused_available\": " +
+                  std::to_string(m->comm && m->tp_fused && m->tp_fused_ok) + ", \"two_shot\": " +
+                  std::to_string(m->tp_two_shot) + ", \"fused_available\": " +
                   std::to_string(m->tp_fused_ok) + "}}";
   std::snprintf(buf, len, "%s", j.c_str());
   return 0;
@@ -1251,9 +1290,14 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
   } else if (option == AGXC_OPT_BULK) {
     m->bulk = value ? 1 : 0;
   } else if (option == AGXC_OPT_TP_FUSED) {
+    if (value < 0 || value > 3) return agxc::fail(AGXC_EINVAL, "set_option: tp_fused 0, 1, 2 or 3");
     if (value && !m->tp_fused_ok)
       return agxc::fail(AGXC_EUNSUPPORTED, "set_option: no fused tensor-parallel path (" +
                                                (m->comm ? m->tp_fused_why : std::string("single device")) + ")");
+    const int two = value == 2 ? 1 : value == 3 ? 0 : (m->tp >= 4);
+    if (value && two != m->tp_two_shot && m->tp_fused_ran)  // the arrival counters already count the other variant
+      return agxc::fail(AGXC_EINVAL, "set_option: the fused variant is fixed once a fused step has run");
+    if (value) m->tp_two_shot = two;
     m->tp_fused = value ? 1 : 0;
   } else if (option == AGXC_OPT_WAIT_MS) {
     if (value < 1) return agxc::fail(AGXC_EINVAL, "set_option: wait_ms must be positive");

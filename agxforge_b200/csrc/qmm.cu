@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       }
     }
     if (p.push.ranks > 0) {
-      // tensor parallel: the tile's last K-split CTA sends the finished B x 128 block of Y to every rank
+      // tensor parallel: the tile's last K-split CTA sends the finished B x 128 block of Y to the ranks
       __threadfence();                               // this CTA's partial sums are visible at L2
       const bool all_ok = epi_all(ok);
       volatile int* s_last = dead + 1;
@@ -341,17 +341,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       epi_sync();
       if (all_ok && *s_last) {
         __threadfence();                             // the other CTAs' sums, read below from L2
+        // to_owner: the tile's rows go to the one rank owning them (reduce-scatter; d / ranks consecutive rows a
+        // rank); else to every rank (each then reduces all rows itself)
+        const int r0 = p.push.to_owner ? tile / p.push.tiles_per_rank : 0;
+        const int r1 = p.push.to_owner ? r0 + 1 : p.push.ranks;
         const int et = dw * 32 + lane;               // 0 .. 255
         for (int i = et; i < p.B * (kM / 4); i += 256) {
           const int b = i / (kM / 4), n = tile * kM + (i % (kM / 4)) * 4;
           const float4 v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
-          for (int r = 0; r < p.push.ranks; ++r)
+          for (int r = r0; r < r1; ++r)
             *reinterpret_cast<float4*>(p.push.slot[r] + static_cast<size_t>(b) * p.N + n) = v4;
         }
-        __threadfence_system();                      // the stores reach every rank before its counter moves
+        __threadfence_system();                      // the stores reach their ranks before the counters move
         epi_sync();
         if (et == 0)
-          for (int r = 0; r < p.push.ranks; ++r)
+          for (int r = r0; r < r1; ++r)
             asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
       }
     }
@@ -396,7 +400,9 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
   p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.G = G; p.bits = pk->bits; p.sdt = pk->sdt;
   p.B = B; p.ksplit = ksplit; p.y = y; p.ldy = ldy; p.err = ctx->err_dev;
   if (push) {
-    if (push->ranks < 1 || push->ranks > 8 || !push->tile_ctr) return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks");
+    if (push->ranks < 1 || push->ranks > 8 || !push->tile_ctr || push->tiles_per_rank < 1 ||
+        push->tiles_per_rank * push->ranks != pk->n / kM)
+      return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks owning equal numbers of 128-row tiles");
     p.push = *push;
   }
   // as many stages as fit beside the dequant tiles (at most 16: a stage cycles through the copy, the dequant and the

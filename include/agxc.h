@@ -262,10 +262,12 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
                                  a chunk); 0 (default): by 3-D TMA tensor boxes */
 #define AGXC_OPT_TP_FUSED 5    /* tensor parallel: 1 (default when every rank could map the others' buffers) = the
-                                 o_proj and down GEMMs push each finished tile into every rank's receive buffer over
-                                 NVLink (peer stores) and a bounded-wait kernel sums the ranks' slots fused with the
-                                 residual; 0 = NCCL all-reduce between the GEMM and the residual kernel. Every rank
-                                 must set the same value. */
+                                 o_proj and down GEMMs carry the all-reduce over NVLink peer memory: with 2 ranks each
+                                 finished tile goes to every rank and a bounded-wait kernel sums the ranks' slots
+                                 fused with the residual (one-shot); with 4 or more, each tile goes to the rank owning
+                                 its rows and a cooperative kernel reduces them and stores them into every rank's
+                                 residual stream (two-shot). 2 / 3 force two-shot / one-shot (before the first fused
+                                 step only); 0 = NCCL all-reduce. Every rank must set the same value. */
 #define AGXC_OPT_WAIT_MS 4     /* tensor parallel: host bound (ms, default 60000) on a decode call's completion; past it
                                  the communicator is aborted (its kernels end) and the call returns AGXC_ETIMEOUT, so a
                                  rank that died between steps cannot hold the others' GPUs */

@@ -34,11 +34,12 @@ def _run(case, world, mode="fused"):
     assert p.returncode == 0, "tp worker failed (%d):\n%s\n%s" % (p.returncode, p.stdout[-3000:], p.stderr[-3000:])
     rep = json.loads(lines[-1])
     assert rep["ok"] and rep["tokens_agree"]
-    assert rep["fused"] == (1 if mode == "fused" else 0)
+    assert rep["fused"] == (0 if mode == "nccl" else 1)
     return rep
 
 
-@pytest.mark.parametrize("case,mode", [("small", "fused"), ("small", "nccl"), ("small8", "fused")])
+@pytest.mark.parametrize("case,mode", [("small", "fused"), ("small", "nccl"), ("small", "two_shot"),
+                                       ("small8", "fused")])
 def test_tp2_small_against_oracle_and_one_device(case, mode):
     """The fused GEMM + peer-memory all-reduce and the NCCL all-reduce, each against the oracle and one device."""
     if _gpus() < 2:

@@ -24,7 +24,7 @@ SMALL = dict(NAME="small", D_MODEL=256, LAYERS=2, HEADS=4, KV_HEADS=2, HEAD_DIM=
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="small", choices=["small", "small8", "internlm7b"])
-    ap.add_argument("--mode", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--mode", default="fused", choices=["fused", "nccl", "two_shot"])
     args = ap.parse_args()
     import torch
     import torch.distributed as dist
@@ -45,6 +45,8 @@ def main():
     info = m.plan_info()["tp"]
     if args.mode == "nccl":
         m.set_option("tp_fused", 0)       # every rank sets the same value
+    elif args.mode == "two_shot":
+        m.set_option("tp_fused", 2)       # reduce-scatter + all-gather even with 2 ranks
     elif not info["fused_available"]:
         raise SystemExit("rank %d: the fused path is not available" % rank)
     rng = np.random.default_rng(21)
