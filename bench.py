@@ -22,8 +22,16 @@ One JSON line on rank 0:
   step_roofline  the whole step: (pack bytes + KV bytes read) per token x tokens/s, against the same peak
   cpu_baseline   the reference's CPU decode step (its QSim chain) as the numpy FP32 port in oracle/cpu_decode.py,
                  timed on this host's cores on a bounded sample (a few layers + the head of one token, scaled)
+  prefill        the same model's prefill section on a prompt of `history` tokens (device time, prompt tok/s)
 Multi-GPU (torchrun, --gpus N): configs 1-4 do not shard (replicas only): every rank decodes its own sequence on its
 own GPU, timing is the max over ranks, `value` sums the tokens of all ranks ("scaling": "weak").
+
+Other workloads (--config):
+  internlm-q{4,8}-1792-b{32,128}   batch 32 / 128 sequences: the tensor-core GEMM decode step
+  internlm7b-q4-8192-b64-tp        BASELINE config 5: the 7B shape, 64 sequences x 8,192-token histories, tensor
+                                   parallel over the N ranks ("scaling": "strong"); --tp-allreduce fused | nccl
+  minilm-b32-s128                  BASELINE config 2: the MiniLM-L6 sentence encoder, 32 x 128 tokens, sentences/s
+                                   against the tensor-core roofline, L2 flushed before every timed forward
 """
 from __future__ import annotations
 
