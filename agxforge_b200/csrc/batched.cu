@@ -22,7 +22,15 @@ namespace {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-__global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows, const __half* __restrict__ bias,
+// row b, column n of a GEMM's output (its K ranges added in order)
+__device__ __forceinline__ float yval(const YRows& y, int b, int n) {
+  const size_t at = static_cast<size_t>(b) * y.ld + n;
+  float v = y.y[at];
+  for (int q = 1; q < y.ks; ++q) v += y.y[q * y.slice + at];
+  return v;
+}
+
+__global__ void rope_append_kernel(const YRows y, int rows, const __half* __restrict__ bias,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                    const uint32_t* __restrict__ q0, int H, int KVH, int hd, int cap, float qscale,
                                    __half* __restrict__ q16, __half* __restrict__ kc, __half* __restrict__ vc, int B,
@@ -36,8 +44,7 @@ __global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows
   const int prow0 = tile * 16;
   const int head = prow0 / hd, tt = (prow0 % hd) / 16;
   const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
-  const float* yb = y + static_cast<size_t>(b) * ld;
-  float y1 = yb[prow0 + r], y2 = yb[prow0 + r + 8];
+  float y1 = yval(y, b, prow0 + r), y2 = yval(y, b, prow0 + r + 8);
   if (bias) {
     y1 += __half2float(bias[head * hd + i1]);
     y2 += __half2float(bias[head * hd + i2]);
@@ -65,29 +72,26 @@ __global__ void rope_append_kernel(const float* __restrict__ y, int ld, int rows
   }
 }
 
-__global__ void residual16_kernel(const float* __restrict__ y, int ld, const __half* __restrict__ x16, float* h, int d,
-                                  int B) {
+__global__ void residual16_kernel(const YRows y, const __half* __restrict__ x16, float* h, int d, int B) {
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
   const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
-  h[t] = y[static_cast<size_t>(b) * ld + i] + __half2float(x16[t]);
+  h[t] = yval(y, b, i) + __half2float(x16[t]);
 }
 
-__global__ void residual32_kernel(const float* __restrict__ y, int ld, const float* __restrict__ h, __half* x16, int d,
-                                  int B) {
+__global__ void residual32_kernel(const YRows y, const float* __restrict__ h, __half* x16, int d, int B) {
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
   const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
-  x16[t] = __float2half_rn(y[static_cast<size_t>(b) * ld + i] + h[t]);
+  x16[t] = __float2half_rn(yval(y, b, i) + h[t]);
 }
 
-__global__ void swiglu_kernel(const float* __restrict__ y, int ld, __half* __restrict__ act, int F, int B) {
+__global__ void swiglu_kernel(const YRows y, __half* __restrict__ act, int F, int B) {
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * F) return;
   const int b = static_cast<int>(t / F), j = static_cast<int>(t % F);
   const int p = j / 16, r = j % 16;  // gate row tile 2p, up row tile 2p + 1 of the interleaved pack
-  const float* yb = y + static_cast<size_t>(b) * ld;
-  const float g = yb[32 * p + r], u = yb[32 * p + 16 + r];
+  const float g = yval(y, b, 32 * p + r), u = yval(y, b, 32 * p + 16 + r);
   act[t] = __float2half_rn(silu(g) * u);
 }
 
@@ -265,29 +269,29 @@ inline unsigned blocks_for(long long n, int threads) { return static_cast<unsign
 
 }  // namespace
 
-int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
+int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
                        __half* vc, int B, cudaStream_t s, int seq) {
   rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
-      y, ld, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
+      y, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }
 
-int launch_residual16(const float* y, int ld, const __half* x16, float* h, int d, int B, cudaStream_t s) {
-  residual16_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, ld, x16, h, d, B);
+int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s) {
+  residual16_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, x16, h, d, B);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }
 
-int launch_residual32(const float* y, int ld, const float* h, __half* x16, int d, int B, cudaStream_t s) {
-  residual32_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, ld, h, x16, d, B);
+int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s) {
+  residual32_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, h, x16, d, B);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }
 
-int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_t s) {
-  swiglu_kernel<<<blocks_for(static_cast<long long>(B) * F, 256), 256, 0, s>>>(y, ld, act, F, B);
+int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s) {
+  swiglu_kernel<<<blocks_for(static_cast<long long>(B) * F, 256), 256, 0, s>>>(y, act, F, B);
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

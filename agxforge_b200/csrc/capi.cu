@@ -293,9 +293,16 @@ int agxc_qmm(agxc_ctx* ctx, const agxc_pack* pack, const void* x_dev, int batch,
     ksplit = 1;
     while (tiles * ksplit * 2 <= ctx->num_sms && G % (ksplit * 2) == 0) ksplit *= 2;
   }
-  if (ksplit > 1)  // the CTAs add their K ranges into y: one 2-D clear of the [batch][n] rows
-    AGXC_CUDA(cudaMemset2DAsync(y_dev, static_cast<size_t>(ldy) * 4, 0, static_cast<size_t>(pack->n) * 4, batch, s));
-  return launch_qmm(ctx, pack, x_dev, batch, y_dev, ldy, ksplit, s);
+  if (ksplit < 2) return launch_qmm(ctx, pack, x_dev, batch, y_dev, ldy, ksplit, s);
+  // split K: stream-ordered scratch for the ranges' partial sums and the tile counters
+  const size_t part_bytes = static_cast<size_t>(ksplit) * batch * pack->n * 4, ctr_bytes = static_cast<size_t>(tiles) * 4;
+  void* scratch = nullptr;
+  AGXC_CUDA(cudaMallocAsync(&scratch, part_bytes + ctr_bytes, s));
+  unsigned* ctr = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(scratch) + part_bytes);
+  int rc = cudaMemsetAsync(ctr, 0, ctr_bytes, s) == cudaSuccess ? 0 : fail(AGXC_ECUDA, "qmm: counter clear");
+  if (!rc) rc = launch_qmm(ctx, pack, x_dev, batch, y_dev, ldy, ksplit, s, nullptr, static_cast<float*>(scratch), ctr);
+  cudaFreeAsync(scratch, s);
+  return rc;
 }
 
 int agxc_rmsnorm_dev(agxc_ctx* ctx, const void* x_dev, int x_f32, int nb, int d, const uint16_t* gain_dev, float eps,

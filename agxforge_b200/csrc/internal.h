@@ -159,18 +159,27 @@ int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows
 // A TMA map over fp16 activation rows X [B][K]: boxes of 64 columns x B rows, 128-byte swizzle.
 int encode_act_map(CUtensorMap* m, const void* x, int B, int K);
 
+// A GEMM's output rows as its consumers read them: value(b, n) = sum over q < ks of y[q slice + b ld + n] (the K
+// ranges' partial sums in a fixed order; ks = 1: the finished rows).
+struct YRows {
+  const float* y = nullptr;
+  int ld = 0;
+  int ks = 1;
+  size_t slice = 0;
+};
+
 // ---- the per-row steps of the batched decode step (batched.cu)
 // q0: each row's position; seq < 0: row b is sequence b's (batched decode), else every row is sequence seq's (prefill)
-int launch_rope_append(const float* y, int ld, int rows, const __half* bias, const float* cos_t, const float* sin_t,
+int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
                        __half* vc, int B, cudaStream_t s, int seq = -1);
 // causal attention of M prompt rows at positions p0 .. p0 + M - 1 of cache sequence `seq` (prefill.cu)
 int launch_prefill_attention(const __half* q16, const __half* kc, const __half* vc, int M, int p0, int H, int KVH,
                              int hd, int cap, int seq, __half* out, cudaStream_t s);
 int prefill_configure(const agxc_ctx* ctx);
-int launch_residual16(const float* y, int ld, const __half* x16, float* h, int d, int B, cudaStream_t s);
-int launch_residual32(const float* y, int ld, const float* h, __half* x16, int d, int B, cudaStream_t s);
-int launch_swiglu(const float* y, int ld, __half* act, int F, int B, cudaStream_t s);
+int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s);
+int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s);
+int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s);
 int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
                       int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s);
 
@@ -206,13 +215,15 @@ int qmm_configure(const agxc_ctx* ctx);
 struct QmmPush {
   float* slot[8] = {};      // rank r's receive slot for this rank's partial sums, [B][N]
   unsigned* flag[8] = {};   // rank r's arrival counter of that slot buffer
-  unsigned* tile_ctr = nullptr;  // [N / 128] arrival counts of the K-split CTAs (local; reset by the last)
   int ranks = 0;
   int tiles_per_rank = 0;   // 128-row tiles owned by each rank
   int to_owner = 0;         // 1: each tile to its owner only (two-shot); 0: every tile to every rank (one-shot)
 };
+// ksplit > 1: `part` [ksplit][B][N] fp32 scratch and `tile_ctr` [N / 128] zeroed counters (also needed by `push`);
+// the last K-range CTA of each tile sums the ranges in order into y (deterministic, y need not be cleared). y NULL
+// (ksplit > 1, no push): only the partial sums are written, for consumers that add them (YRows).
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s, const QmmPush* push = nullptr);
+               cudaStream_t s, const QmmPush* push = nullptr, float* part = nullptr, unsigned* tile_ctr = nullptr);
 // After the GEMM's pushes (use = *epoch x uses_per_step + use_in_step; every wait bounded). One-shot: wait until every
 // rank's tiles are here (*flag >= (use + 1) x ranks x ranks x tiles_per_rank), reduce every row in rank order plus the
 // residual into this rank's own output. Two-shot (one cooperative grid): wait for this rank's rows only (*flag >=

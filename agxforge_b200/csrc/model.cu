@@ -102,7 +102,8 @@ struct agxc_model {
   float* recv = nullptr;
   unsigned* recv_flags = nullptr;
   void* peer[8] = {};
-  unsigned* tile_ctr = nullptr; // [d / 128]
+  unsigned* tile_ctr = nullptr; // [widest pack's tiles] GEMM arrival counters (split K, the peer push)
+  float* qpart = nullptr;       // batch >= 32: the split-K partial sums of the step's GEMMs
   size_t peer_flags_off = 0;    // byte offsets in every rank's exported allocation: counters (2 arrival, 2 gather),
   size_t peer_h_off = 0;        // the residual stream h [B][d] fp32 and x16 [B][d] fp16 (the model's own h and x16)
   size_t peer_x16_off = 0;
@@ -118,12 +119,17 @@ struct agxc_model {
   __half* pf_act = nullptr;     // [rows][F]
   uint32_t* pf_pos = nullptr;   // [rows]
   uint32_t* pf_tok = nullptr;   // [cap] the prompt
+  float* pf_part = nullptr;     // the split-K partial sums of the prefill GEMMs
 };
 
 namespace agxc {
 
 int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
-            const QmmPush* push = nullptr);
+            float* part, const QmmPush* push = nullptr);
+int qmm_ksplit(const agxc_ctx* ctx, const agxc_pack& pk);
+int qmm_scratch(agxc_model* m, int rows, float** part);
+int gemm_rows(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* ybuf, int ld, float* part,
+              cudaStream_t s, YRows* out);
 
 namespace {
 
@@ -283,16 +289,21 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     ++kind;
     return 0;
   };
+  // finished rows in y (the head, the peer push, an NCCL all-reduce) / rows whose consumers add the K ranges
   auto gemm = [&](const agxc_pack& pk, const __half* x, float* y, int ld, const QmmPush* push = nullptr) -> int {
-    return run_qmm(m, pk, x, B, y, ld, s, push);
+    return run_qmm(m, pk, x, B, y, ld, s, m->qpart, push);
   };
+  YRows yr;
+  auto gemm_r = [&](const agxc_pack& pk, const __half* x, int ld) -> int {
+    return gemm_rows(m, pk, x, B, m->ybuf, ld, m->qpart, s, &yr);
+  };
+  const YRows ydone{m->ybuf, d, 1, 0};
   const bool fused = m->comm && m->tp_fused && m->tp_fused_ok;
   auto push_of = [&](int buf) {  // this rank's slot of buffer `buf` on every rank, and their arrival counters
     QmmPush ps;
     ps.ranks = m->tp;
     ps.tiles_per_rank = d / 128 / m->tp;
     ps.to_owner = m->tp_two_shot;
-    ps.tile_ctr = m->tile_ctr;
     const size_t slot = (static_cast<size_t>(buf) * m->tp + m->tp_rank) * B * d;
     for (int r = 0; r < m->tp; ++r) {
       uint8_t* base = static_cast<uint8_t*>(m->peer[r]);
@@ -318,9 +329,9 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     AttnParams a;
     layer_params(m, l, p, a, q, g, w);
     if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, p.norm_gain, D.eps, m->xn16, s)) ||
-        (rc = gemm(m->qkv[l], m->xn16, m->ybuf, m->qkv_rows)) ||
-        (rc = launch_rope_append(m->ybuf, m->qkv_rows, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, H, KVH, hd,
-                                 D.cap, qscale, m->q16, p.kcache, p.vcache, B, s)) ||
+        (rc = gemm_r(m->qkv[l], m->xn16, m->qkv_rows)) ||
+        (rc = launch_rope_append(yr, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, H, KVH, hd, D.cap, qscale, m->q16,
+                                 p.kcache, p.vcache, B, s)) ||
         (rc = close()))
       return rc;
     a.pdl = 0;
@@ -333,13 +344,17 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
                                  m->tp_two_shot)) ||
           (rc = close()))
         return rc;
-    } else if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, nullptr)) ||
-               (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
-               (rc = launch_residual16(m->ybuf, d, m->x16, m->h, d, B, s)) || (rc = close())) {
+    } else if (m->comm) {  // NCCL: the finished rows all-reduced, then the residual
+      if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, nullptr)) ||
+          (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s)) ||
+          (rc = launch_residual16(ydone, m->x16, m->h, d, B, s)) || (rc = close()))
+        return rc;
+    } else if ((rc = open()) || (rc = gemm_r(m->wo[l], m->attn, d)) ||
+               (rc = launch_residual16(yr, m->x16, m->h, d, B, s)) || (rc = close())) {
       return rc;
     }
     if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s)) ||
-        (rc = gemm(m->gu[l], m->xn16, m->ybuf, 2 * F)) || (rc = launch_swiglu(m->ybuf, 2 * F, m->act, F, B, s)) ||
+        (rc = gemm_r(m->gu[l], m->xn16, 2 * F)) || (rc = launch_swiglu(yr, m->act, F, B, s)) ||
         (rc = close()))
       return rc;
     if (fused) {
@@ -350,9 +365,13 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
                                  m->ctx->err_dev, s, m->tp_two_shot)) ||
           (rc = close()))
         return rc;
-    } else if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, nullptr)) ||
-               (m->comm && (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s))) ||
-               (rc = launch_residual32(m->ybuf, d, m->h, m->x16, d, B, s)) || (rc = close())) {
+    } else if (m->comm) {
+      if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, nullptr)) ||
+          (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s)) ||
+          (rc = launch_residual32(ydone, m->h, m->x16, d, B, s)) || (rc = close()))
+        return rc;
+    } else if ((rc = open()) || (rc = gemm_r(m->down[l], m->act, d)) ||
+               (rc = launch_residual32(yr, m->h, m->x16, d, B, s)) || (rc = close())) {
       return rc;
     }
   }
@@ -374,7 +393,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
                               m->ctx->err_dev, B, s)) ||
       (rc = close()))
     return rc;
-  m->launches = 11 * D.n_layers + 3;  // kernels (the split-K zero fills are memset nodes)
+  m->launches = 11 * D.n_layers + 3;
   return 0;
 }
 
@@ -477,9 +496,7 @@ int tp_peer_setup(agxc_model* m) {
   AGXC_CUDA(cudaMemset(base, 0, bytes));
   m->recv = static_cast<float*>(base);
   m->recv_flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(base) + m->peer_flags_off);
-  if (int rc = dalloc_t(m, &m->tile_ctr, static_cast<size_t>(d / 128))) return rc;
   if (int rc = dalloc_t(m, &m->epoch, 1)) return rc;
-  AGXC_CUDA(cudaMemset(m->tile_ctr, 0, static_cast<size_t>(d / 128) * 4));
   AGXC_CUDA(cudaMemset(m->epoch, 0, 4));
   m->peer[m->tp_rank] = base;
   int ok = 1;
@@ -659,6 +676,7 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
                                 static_cast<size_t>(d)});
     if ((rc = dalloc_t(m, &m->xn16, static_cast<size_t>(B) * d))) return bail(rc);
     if ((rc = dalloc_t(m, &m->ybuf, static_cast<size_t>(B) * yn))) return bail(rc);
+    if ((rc = qmm_scratch(m, B, &m->qpart))) return bail(rc);
   }
   if ((rc = dalloc_t(m, &m->q0, B))) return bail(rc);
   if ((rc = dalloc_t(m, &m->log, static_cast<size_t>(B) * D.cap))) return bail(rc);
@@ -853,15 +871,57 @@ __global__ void positions_kernel(uint32_t* pos, int p0, int n) {
   if (i < n) pos[i] = static_cast<uint32_t>(p0 + i);
 }
 
-// Y [rows][ld] = X [rows][K] W^T on the tensor cores, the K range split over CTAs when the 128-row tiles alone leave
-// SMs idle (Y zeroed first: the CTAs add into it).
-int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
-            const QmmPush* push) {
+// K ranges of a pack's GEMM: split until the 128-row tiles fill the SMs (a divisor of the groups)
+int qmm_ksplit(const agxc_ctx* ctx, const agxc_pack& pk) {
   const int tiles = pk.n / 128, G = pk.k / 64;
   int ks = 1;
-  while (tiles * ks * 2 <= m->ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
-  if (ks > 1) AGXC_CUDA(cudaMemset2DAsync(y, static_cast<size_t>(ld) * 4, 0, static_cast<size_t>(pk.n) * 4, rows, s));
-  return launch_qmm(m->ctx, &pk, x, rows, y, ld, ks, s, push);
+  while (tiles * ks * 2 <= ctx->num_sms && G % (ks * 2) == 0) ks *= 2;
+  return ks;
+}
+
+// Y [rows][ld] = X [rows][K] W^T on the tensor cores; with several K ranges their partial sums go to `part`
+// ([ks][rows][N]) and the last range of each tile adds them up in order.
+int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
+            float* part, const QmmPush* push) {
+  return launch_qmm(m->ctx, &pk, x, rows, y, ld, qmm_ksplit(m->ctx, pk), s, push, part, m->tile_ctr);
+}
+
+// The GEMM for consumers that add the K ranges themselves: split K writes the ranges' partial sums to `part` and
+// nothing else (no summing pass); one range writes the finished rows to ybuf.
+int gemm_rows(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* ybuf, int ld, float* part,
+              cudaStream_t s, YRows* out) {
+  const int ks = qmm_ksplit(m->ctx, pk);
+  if (ks > 1) {
+    *out = YRows{part, pk.n, ks, static_cast<size_t>(rows) * pk.n};
+    return launch_qmm(m->ctx, &pk, x, rows, nullptr, pk.n, ks, s, nullptr, part, nullptr);
+  }
+  *out = YRows{ybuf, ld, 1, 0};
+  return launch_qmm(m->ctx, &pk, x, rows, ybuf, ld, 1, s);
+}
+
+// The tile counters (the widest pack's tiles) and a partial-sum scratch for `rows` activation rows of any of the
+// model's split-K GEMMs.
+int qmm_scratch(agxc_model* m, int rows, float** part) {
+  const agxc_model_desc& D = m->d;
+  size_t need = 0;
+  auto take = [&](const agxc_pack& pk) {
+    const int ks = qmm_ksplit(m->ctx, pk);
+    if (ks > 1) need = std::max(need, static_cast<size_t>(ks) * rows * pk.n);
+  };
+  for (int l = 0; l < D.n_layers; ++l) {
+    take(m->qkv[l]);
+    take(m->wo[l]);
+    take(m->gu[l]);
+    take(m->down[l]);
+  }
+  take(m->head);
+  if (!m->tile_ctr) {
+    const size_t tiles = std::max({static_cast<size_t>(m->head.n), static_cast<size_t>(2) * D.ffn,
+                                   static_cast<size_t>(m->qkv_rows), static_cast<size_t>(D.d_model)}) / 128 + 1;
+    if (int rc = dalloc_t(m, &m->tile_ctr, tiles)) return rc;
+    AGXC_CUDA(cudaMemset(m->tile_ctr, 0, tiles * 4));
+  }
+  return dalloc_t(m, part, std::max<size_t>(need, 64));
 }
 
 int prefill_buffers(agxc_model* m) {
@@ -874,7 +934,7 @@ int prefill_buffers(agxc_model* m) {
       (rc = dalloc_t(m, &m->pf_xn16, R * d)) || (rc = dalloc_t(m, &m->pf_y, R * yn)) ||
       (rc = dalloc_t(m, &m->pf_q16, R * m->attn_dim)) || (rc = dalloc_t(m, &m->pf_attn, R * m->attn_dim)) ||
       (rc = dalloc_t(m, &m->pf_act, R * F)) || (rc = dalloc_t(m, &m->pf_pos, R)) ||
-      (rc = dalloc_t(m, &m->pf_tok, static_cast<size_t>(D.cap))))
+      (rc = dalloc_t(m, &m->pf_tok, static_cast<size_t>(D.cap))) || (rc = qmm_scratch(m, kPrefillRows, &m->pf_part)))
     return rc;
   // rows past a chunk's end are GEMM padding: they start at zero and only ever hold finite values
   AGXC_CUDA(cudaMemset(m->pf_x16, 0, R * d * 2));
@@ -903,6 +963,7 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
   const size_t layer_kv = static_cast<size_t>(D.batch) * KVH * D.cap * hd;
   const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
   int rc = 0, launches = 0;
+  YRows yr;
   if (total > 0) {
     std::vector<uint32_t> tok(prompt, prompt + n);
     AGXC_CUDA(cudaMemcpyAsync(m->pf_tok, tok.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, s));
@@ -920,17 +981,17 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
       __half* kc = m->kcache + l * layer_kv;
       __half* vc = m->vcache + l * layer_kv;
       if ((rc = launch_rmsnorm(m->pf_x16, 0, Mp, d, g1, D.eps, m->pf_xn16, s)) ||
-          (rc = run_qmm(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, s)) ||
-          (rc = launch_rope_append(m->pf_y, m->qkv_rows, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd,
-                                   D.cap, qscale, m->pf_q16, kc, vc, Mc, s, b)) ||
+          (rc = gemm_rows(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, m->pf_part, s, &yr)) ||
+          (rc = launch_rope_append(yr, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd, D.cap, qscale,
+                                   m->pf_q16, kc, vc, Mc, s, b)) ||
           (rc = launch_prefill_attention(m->pf_q16, kc, vc, Mc, p0, H, KVH, hd, D.cap, b, m->pf_attn, s)) ||
-          (rc = run_qmm(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, s)) ||
-          (rc = launch_residual16(m->pf_y, d, m->pf_x16, m->pf_h, d, Mp, s)) ||
+          (rc = gemm_rows(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
+          (rc = launch_residual16(yr, m->pf_x16, m->pf_h, d, Mp, s)) ||
           (rc = launch_rmsnorm(m->pf_h, 1, Mp, d, g1 + d, D.eps, m->pf_xn16, s)) ||
-          (rc = run_qmm(m, m->gu[l], m->pf_xn16, Mp, m->pf_y, 2 * F, s)) ||
-          (rc = launch_swiglu(m->pf_y, 2 * F, m->pf_act, F, Mp, s)) ||
-          (rc = run_qmm(m, m->down[l], m->pf_act, Mp, m->pf_y, d, s)) ||
-          (rc = launch_residual32(m->pf_y, d, m->pf_h, m->pf_x16, d, Mp, s)))
+          (rc = gemm_rows(m, m->gu[l], m->pf_xn16, Mp, m->pf_y, 2 * F, m->pf_part, s, &yr)) ||
+          (rc = launch_swiglu(yr, m->pf_act, F, Mp, s)) ||
+          (rc = gemm_rows(m, m->down[l], m->pf_act, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
+          (rc = launch_residual32(yr, m->pf_h, m->pf_x16, d, Mp, s)))
         break;
       launches += 11;
     }

@@ -40,6 +40,8 @@ struct QmmParams {
   int stages = 4;
   float* y = nullptr;             // fp32 [B][ldy]
   int ldy = 0;
+  float* part = nullptr;          // ksplit > 1: [ksplit][B][N] fp32, each K range's partial sums
+  unsigned* tile_ctr = nullptr;   // ksplit > 1 or push: [N / 128] arrival counts (zero; reset by the last arrival)
   unsigned* err = nullptr;
   QmmPush push;                   // ranks > 0: push finished tiles to every rank (tensor parallel)
 };
@@ -319,44 +321,59 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
             : "r"(base + static_cast<uint32_t>(c0)));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (row < p.N) {
+          // one K range: straight into Y; several: this range's partial sums into its own slice
+          float* dst = p.ksplit > 1 ? p.part + static_cast<size_t>(ks) * p.B * p.N : p.y;
+          const int ld = p.ksplit > 1 ? p.N : p.ldy;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float* dst = p.y + static_cast<size_t>(c0 + j) * p.ldy + row;
-            if (p.ksplit > 1) atomicAdd(dst, __uint_as_float(v[j]));
-            else *dst = __uint_as_float(v[j]);
-          }
+          for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(c0 + j) * ld + row] = __uint_as_float(v[j]);
         }
       }
     }
-    if (p.push.ranks > 0) {
-      // tensor parallel: the tile's last K-split CTA sends the finished B x 128 block of Y to the ranks
+    const bool push = p.push.ranks > 0;
+    if ((p.ksplit > 1 && p.y) || push) {  // (y NULL: the consumers add the K ranges themselves)
+      // the tile's last K-range CTA sums the ranges in order (the same result every run: no atomics on the data)
+      // and, under tensor parallelism, sends the finished B x 128 block of Y to the ranks
       __threadfence();                               // this CTA's partial sums are visible at L2
       const bool all_ok = epi_all(ok);
       volatile int* s_last = dead + 1;
       if (all_ok && dw == 0 && lane == 0) {
-        const unsigned prev = atomicAdd(p.push.tile_ctr + tile, 1u);
+        const unsigned prev = atomicAdd(p.tile_ctr + tile, 1u);
         *s_last = prev == static_cast<unsigned>(p.ksplit - 1);
-        if (*s_last) p.push.tile_ctr[tile] = 0;      // every K-split CTA of the tile has arrived
+        if (*s_last) p.tile_ctr[tile] = 0;           // every K-range CTA of the tile has arrived
       }
       epi_sync();
       if (all_ok && *s_last) {
-        __threadfence();                             // the other CTAs' sums, read below from L2
+        __threadfence();                             // the other CTAs' partials, read below from L2
         // to_owner: the tile's rows go to the one rank owning them (reduce-scatter; d / ranks consecutive rows a
         // rank); else to every rank (each then reduces all rows itself)
-        const int r0 = p.push.to_owner ? tile / p.push.tiles_per_rank : 0;
-        const int r1 = p.push.to_owner ? r0 + 1 : p.push.ranks;
+        const int r0 = push && p.push.to_owner ? tile / p.push.tiles_per_rank : 0;
+        const int r1 = !push ? 0 : p.push.to_owner ? r0 + 1 : p.push.ranks;
         const int et = dw * 32 + lane;               // 0 .. 255
+        const size_t slice = static_cast<size_t>(p.B) * p.N;
         for (int i = et; i < p.B * (kM / 4); i += 256) {
           const int b = i / (kM / 4), n = tile * kM + (i % (kM / 4)) * 4;
-          const float4 v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
+          float4 v4;
+          if (p.ksplit > 1) {
+            const float* src = p.part + static_cast<size_t>(b) * p.N + n;
+            v4 = __ldcg(reinterpret_cast<const float4*>(src));
+            for (int q = 1; q < p.ksplit; ++q) {
+              const float4 t4 = __ldcg(reinterpret_cast<const float4*>(src + q * slice));
+              v4.x += t4.x; v4.y += t4.y; v4.z += t4.z; v4.w += t4.w;
+            }
+            *reinterpret_cast<float4*>(p.y + static_cast<size_t>(b) * p.ldy + n) = v4;
+          } else {
+            v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
+          }
           for (int r = r0; r < r1; ++r)
             *reinterpret_cast<float4*>(p.push.slot[r] + static_cast<size_t>(b) * p.N + n) = v4;
         }
-        __threadfence_system();                      // the stores reach their ranks before the counters move
-        epi_sync();
-        if (et == 0)
-          for (int r = r0; r < r1; ++r)
-            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
+        if (push) {
+          __threadfence_system();                    // the stores reach their ranks before the counters move
+          epi_sync();
+          if (et == 0)
+            for (int r = r0; r < r1; ++r)
+              asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
+        }
       }
     }
   }
@@ -390,7 +407,7 @@ int qmm_configure(const agxc_ctx* ctx) {
 // Y [B][ldy] fp32 = X [B][K] fp16 x W^T for a pack W [N][K]: 128-row tiles, the K range split over ksplit CTAs when
 // the tiles alone would leave SMs idle (then Y must hold zeros: the CTAs add into it).
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s, const QmmPush* push) {
+               cudaStream_t s, const QmmPush* push, float* part, unsigned* tile_ctr) {
   if (B < 32 || B > 256 || B % 16) return fail(AGXC_EINVAL, "qmm: 32 to 256 activation rows, a multiple of 16");
   if (pk->n % kM) return fail(AGXC_EINVAL, "qmm: N must be a multiple of 128");
   if (ldy < pk->n) return fail(AGXC_EINVAL, "qmm: ldy < N");
@@ -399,8 +416,12 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
   QmmParams p;
   p.w = pk->tiles; p.sb = pk->sb; p.N = pk->n; p.K = pk->k; p.G = G; p.bits = pk->bits; p.sdt = pk->sdt;
   p.B = B; p.ksplit = ksplit; p.y = y; p.ldy = ldy; p.err = ctx->err_dev;
+  p.part = part;
+  p.tile_ctr = tile_ctr;
+  if ((ksplit > 1 && (!part || (y && !tile_ctr))) || (push && (!tile_ctr || !y)) || (!y && ksplit < 2))
+    return fail(AGXC_EINVAL, "qmm: split K and the peer push need the partial-sum scratch, the tile counters and Y");
   if (push) {
-    if (push->ranks < 1 || push->ranks > 8 || !push->tile_ctr || push->tiles_per_rank < 1 ||
+    if (push->ranks < 1 || push->ranks > 8 || push->tiles_per_rank < 1 ||
         push->tiles_per_rank * push->ranks != pk->n / kM)
       return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks owning equal numbers of 128-row tiles");
     p.push = *push;

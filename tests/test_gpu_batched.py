@@ -100,3 +100,20 @@ def test_batched_plan_rejects_unaligned_shapes(torch):
     with pytest.raises(Exception, match="multiples of 128"):  # vocab 1040: 16-row tiles, not 128-row GEMM tiles
         assemble.build(dict(model=dict(SMALL, VOCAB=1040), bits=4, batch=32, cap=64, seed=0))
     assemble.build(dict(model=dict(SMALL, VOCAB=1040), bits=4, batch=8, cap=64, seed=0)).close()
+
+
+def test_batched_step_is_deterministic(torch):
+    """The split-K GEMMs add their K ranges in a fixed order (no atomics on the data): two runs of the same forced
+    decode give bit-identical logits."""
+    outs = []
+    for _ in range(2):
+        m = _build(dict(SMALL), bits=4, batch=32, seed=12)
+        rng = np.random.default_rng(13)
+        for b in range(32):
+            m.start(b, rng.integers(0, 1024, 6).tolist())
+        m.decode(5, want_tokens=False)
+        f = rng.integers(0, 1024, (3, 32))
+        _, lg, _ = m.decode(3, forced=f, want_tokens=True, want_logits=True)
+        outs.append(lg)
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
