@@ -67,6 +67,7 @@ SIGNATURES = {
     "agxc_init": (_I, [_I, C.POINTER(_P)]),
     "agxc_ctx_free": (None, [_P]),
     "agxc_ctx_sync": (_I, [_P]),
+    "agxc_ctx_stream": (_I, [_P, C.POINTER(C.c_void_p)]),
     "agxc_ctx_error_word": (_I, [_P, C.POINTER(C.c_uint32)]),
     "agxc_quantize_dev": (_I, [_P, C.POINTER(PackDesc), _P, _P, _P, _P, _P]),
     "agxc_pack_create": (_I, [_P, C.POINTER(PackDesc), _P, _P, _P, _I, C.POINTER(_P)]),
@@ -160,6 +161,15 @@ def context(device=0):
             _ctx[device] = p
         h = p
     return h
+
+
+def ctx_stream(device=0):
+    """The context's own stream on ``device`` as a torch.cuda.ExternalStream (the stream the model and encoder calls
+    enqueue on)."""
+    import torch
+    h = C.c_void_p()
+    check(lib().agxc_ctx_stream(context(device), C.byref(h)), "ctx_stream")
+    return torch.cuda.ExternalStream(h.value, device=device)
 
 
 def ptr(t):

@@ -150,6 +150,12 @@ int agxc_ctx_sync(agxc_ctx* ctx) {
   return 0;
 }
 
+int agxc_ctx_stream(agxc_ctx* ctx, void** stream) {
+  if (!ctx || !stream) return fail(AGXC_EINVAL, "ctx_stream: null argument");
+  *stream = ctx->stream;
+  return 0;
+}
+
 int agxc_ctx_error_word(agxc_ctx* ctx, uint32_t* word) {
   if (!ctx || !word) return fail(AGXC_EINVAL, "error_word: null argument");
   AGXC_CUDA(cudaMemcpy(word, ctx->err_dev, 4, cudaMemcpyDeviceToHost));

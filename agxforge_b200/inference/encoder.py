@@ -214,8 +214,9 @@ class Encoder:
 
     def forward_device(self, ids, mask, types=None, out=None):
         """Device tensors int32 [batch, seq] -> out float32 [batch, hidden] (allocated when None), enqueued on the
-        library's stream (no host synchronisation; an id or type outside its table is reported by the next
-        synchronising call)."""
+        library's stream, ordered after torch's current stream (which produced the inputs) and before its later work
+        (which reads `out`) with events, no host synchronisation; an id or type outside its table is reported by the
+        next synchronising call."""
         import torch
         B, S = ids.shape
         for t in (ids, mask) + ((types,) if types is not None else ()):
@@ -223,9 +224,14 @@ class Encoder:
                 raise ValueError("refused: int32 contiguous device tensors [batch, seq]")
         if out is None:
             out = torch.empty((B, self.hidden), dtype=torch.float32, device=ids.device)
+        mine, theirs = N.ctx_stream(self.device), torch.cuda.current_stream(ids.device)
+        mine.wait_stream(theirs)
         N.check(N.lib().agxc_encoder_forward(self._h, C.c_void_p(ids.data_ptr()), C.c_void_p(mask.data_ptr()),
                                              None if types is None else C.c_void_p(types.data_ptr()), B, S,
                                              C.c_void_p(out.data_ptr()), 1, None), "encoder_forward")
+        for t in (ids, mask, out) + ((types,) if types is not None else ()):
+            t.record_stream(mine)  # torch's allocator keeps them until the library's stream is past this forward
+        theirs.wait_stream(mine)
         return out
 
     def replay(self, reps, flush_l2=True):

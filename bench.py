@@ -81,36 +81,72 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples (every 20 ms) kept when their timestamp falls inside the timed region: SM clock, max clock,
-    throttle reasons."""
-    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, max SM clock and throttle reasons sampled DURING the timed region, every 5 ms, by a host thread through
+    NVML (read-only queries; the device is found by the CUDA device's UUID, so CUDA_VISIBLE_DEVICES cannot point it
+    at another GPU). Each sample carries its own wall time and is kept when it falls inside the timed region. Without
+    NVML: nvidia-smi, line-buffered, its samples placed by their own timestamps."""
     NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    # NVML clock-event reason bits (nvml.h): HwSlowdown, HwThermalSlowdown, SwThermalSlowdown, SwPowerCap
+    BITS = [0x8, 0x40, 0x20, 0x4]
+    Q = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.samples = []          # (wall time, sm MHz, max sm MHz, [reason names])
         self.t0 = self.t1 = None
+        self.proc = None
+        self.source = None
+        self._stop = threading.Event()
+
+    def _uuid(self):
+        import torch
+        u = str(torch.cuda.get_device_properties(self.index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-            t_end = time.time() + 3.0
-            while not self.lines and time.time() < t_end:  # the sampler is up before the timed region starts
-                time.sleep(0.01)
-        except Exception:
-            self.proc = None
-        return self
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(self._uuid())
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append((time.time(), line.strip()))
+            def run():
+                while not self._stop.is_set():
+                    t = time.time()
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = int(reasons(h))
+                    self.samples.append((t, sm, mx, [n for n, bit in zip(self.NAMES, self.BITS) if r & bit]))
+                    time.sleep(0.005)
+            self.source = "nvml"
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            try:
+                self.proc = subprocess.Popen(["stdbuf", "-oL", "nvidia-smi", "-i", self._uuid(),
+                                              "--query-gpu=" + self.Q, "--format=csv,noheader,nounits", "-lms", "20"],
+                                             stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:  # noqa: BLE001
+                return self
+
+            def run():
+                for line in self.proc.stdout:
+                    parts = [x.strip() for x in line.split(",")]
+                    try:
+                        t = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                        t += float("0." + parts[0].split(".")[1]) if "." in parts[0] else 0.0
+                        self.samples.append((t, float(parts[1]), float(parts[2]),
+                                             [n for n, v in zip(self.NAMES, parts[3:7]) if v.lower() == "active"]))
+                    except (ValueError, IndexError):
+                        continue
+            self.source = "nvidia-smi"
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+        t_end = time.time() + 3.0
+        while not self.samples and time.time() < t_end:  # the sampler is up before the timed region starts
+            time.sleep(0.005)
+        return self
 
     def mark_start(self):
         self.t0 = time.time()
@@ -119,33 +155,25 @@ class Clocks:
         self.t1 = time.time()
 
     def stop(self):
+        self._stop.set()
         if self.proc:
-            time.sleep(0.05)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
-            except Exception:
+            except Exception:  # noqa: BLE001
                 self.proc.kill()
+        if getattr(self, "thread", None) is not None:
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        inside = [ln for t, ln in self.lines if self.t0 is not None and self.t0 <= t <= self.t1 + 0.02]
-        for ln in inside:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 10:
-                continue
-            try:
-                sm.append(float(parts[2]))
-                mx.append(float(parts[3]))
-            except ValueError:
-                continue
-            for n, v in zip(self.NAMES, parts[6:10]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [x for x in list(self.samples) if self.t0 is not None and self.t0 <= x[0] <= self.t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "source": self.source}
+        reasons = sorted({n for x in inside for n in x[3]})
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": max(x[2] for x in inside),
+                "reasons": reasons, "samples": len(inside), "source": self.source}
 
 
 def dist_setup(gpus):

@@ -54,6 +54,9 @@ AGXC_API int agxc_version(void);
 AGXC_API int agxc_init(int device, agxc_ctx** out);
 AGXC_API void agxc_ctx_free(agxc_ctx* ctx);
 AGXC_API int agxc_ctx_sync(agxc_ctx* ctx);
+/* The context's own stream (the one NULL `stream` arguments and the model / encoder calls enqueue on), as a
+ * cudaStream_t in *stream: a caller that produces device inputs on another stream orders the two with events. */
+AGXC_API int agxc_ctx_stream(agxc_ctx* ctx, void** stream);
 /* The context's device error word (bounded waits that gave up set bits in it); 0 = clean. Reading clears it. */
 AGXC_API int agxc_ctx_error_word(agxc_ctx* ctx, uint32_t* word);
 

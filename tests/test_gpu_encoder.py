@@ -42,6 +42,7 @@ def enc(torch):
 def test_hgemm_against_torch(torch, M, N, K, epi):
     import ctypes as C
     from agxforge_b200 import _native as N_
+    from agxforge_b200.kernels import qmv as Q
     g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
     A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
     W = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
@@ -58,7 +59,8 @@ def test_hgemm_against_torch(torch, M, N, K, epi):
                                      C.c_void_p(bias.data_ptr()), epi, C.c_void_p(out32.data_ptr()),
                                      C.c_void_p(out16.data_ptr()),
                                      C.c_void_p(out32.data_ptr() if epi == 3 else res.data_ptr()),
-                                     C.c_void_p(g1.data_ptr()), C.c_void_p(b1.data_ptr()), C.c_float(1e-12), None),
+                                     C.c_void_p(g1.data_ptr()), C.c_void_p(b1.data_ptr()), C.c_float(1e-12),
+                                     Q._stream(torch)),  # torch's stream: ordered after the operands' writes
              "hgemm")
     torch.cuda.synchronize()
     # fp32 accumulation of exact fp16 products: only the summation order differs from the reference matmul
