@@ -83,6 +83,7 @@ struct agxc_model {
   uint32_t* h_force = nullptr;  // pinned [steps][B]
   size_t h_force_n = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  cudaEvent_t ev_pipe[2] = {nullptr, nullptr};  // sync_each 2: the last two steps' ends
   std::vector<void*> allocs;
   // tensor parallelism: m->d holds this rank's LOCAL shape (heads, KV heads, ffn, vocabulary slice)
   int tp = 1, tp_rank = 0;
@@ -753,7 +754,9 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
         cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
       return bail(fail(AGXC_ECUDA, "model: rope table upload failed"));
   }
-  if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess)
+  if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->ev_pipe[0], cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->ev_pipe[1], cudaEventDisableTiming) != cudaSuccess)
     return bail(fail(AGXC_ECUDA, "model: event create failed"));
   if (cudaStreamSynchronize(s) != cudaSuccess) return bail(fail(AGXC_ECUDA, "model: setup sync failed"));
   if (T > 1) {  // collective: every rank gets here; one warm-up of each collective before any graph capture
@@ -1078,6 +1081,7 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
                  int sync_each, agxc_timing* t) {
   const agxc_model_desc& D = m->d;
   if (steps < 0) return fail(AGXC_EINVAL, "decode: steps");
+  if (sync_each < 0 || sync_each > 2) return fail(AGXC_EINVAL, "decode: sync_each 0, 1 or 2");
   if (forced_in) {
     for (size_t i = 0; i < static_cast<size_t>(steps) * D.batch; ++i) {
       const uint32_t f = static_cast<uint32_t>(forced_in[i]);
@@ -1118,7 +1122,10 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
     if (logits_out)
       AGXC_CUDA(cudaMemcpyAsync(logits_out + static_cast<size_t>(i) * D.batch * D.vocab, m->logits,
                                 static_cast<size_t>(D.batch) * D.vocab * 4, cudaMemcpyDeviceToHost, s));
-    if (sync_each) {
+    if (sync_each == 2) {  // this step queued behind the previous one; wait for that one (its token is home)
+      AGXC_CUDA(cudaEventRecord(m->ev_pipe[i & 1], s));
+      if (i > 0 && (rc = wait_done(m, m->ev_pipe[(i - 1) & 1]))) return rc;
+    } else if (sync_each) {
       AGXC_CUDA(cudaEventRecord(m->ev1, s));
       if ((rc = wait_done(m, m->ev1))) return rc;
     }
@@ -1188,6 +1195,8 @@ void model_free(agxc_model* m) {
   tp_comm_free(m->comm);  // after the graphs that hold its collectives
   if (m->ev0) cudaEventDestroy(m->ev0);
   if (m->ev1) cudaEventDestroy(m->ev1);
+  for (cudaEvent_t e : m->ev_pipe)
+    if (e) cudaEventDestroy(e);
   if (m->h_tok) cudaFreeHost(m->h_tok);
   if (m->h_force) cudaFreeHost(m->h_force);
   if (m->trace) cudaFree(m->trace);

@@ -236,7 +236,11 @@ class DecodeModel:
         return k.view(np.float16), v.view(np.float16)
 
     def decode(self, steps, forced=None, want_tokens=True, want_logits=False, sync_each=False):
-        """Run `steps` steps. Returns (tokens [steps, batch] or None, logits [steps, batch, V] or None, timing dict)."""
+        """Run `steps` steps. Returns (tokens [steps, batch] or None, logits [steps, batch, V] or None, timing dict).
+        sync_each: 0 / False waits once at the end; 1 / True waits for every step before queueing the next; 2 keeps
+        one step queued ahead and waits for the step before it (each step's tokens reach the host one step later)."""
+        if int(sync_each) not in (0, 1, 2):
+            raise ValueError("decode: sync_each 0, 1 or 2")
         B, V = self.batch, self.vocab_count   # the rank's vocabulary slice under tensor parallelism
         toks = np.zeros((steps, B), np.int32) if want_tokens else None
         lg = np.zeros((steps, B, V), np.float32) if want_logits else None
@@ -246,7 +250,7 @@ class DecodeModel:
         t = N.Timing()
         N.check(N.lib().agxc_decode(self._h, steps, None if fin is None else fin.ctypes.data_as(C.c_void_p),
                                     None if toks is None else toks.ctypes.data_as(C.c_void_p),
-                                    None if lg is None else lg.ctypes.data_as(C.c_void_p), int(bool(sync_each)),
+                                    None if lg is None else lg.ctypes.data_as(C.c_void_p), int(sync_each),
                                     C.byref(t)), "decode")
         return toks, lg, dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches_per_step=t.launches_per_step)
 

@@ -16,7 +16,9 @@ so no flush is needed between steps.
 One JSON line on rank 0:
   value          tokens/s over the K timed steps (device time, CUDA events, inputs resident in HBM), summed over ranks
   e2e            the same steps through the public C-ABI decode call with a host->device copy of each step's input
-                 token (pinned) and a device->host read of its chosen token, host-synchronised every step
+                 token (pinned) and a device->host read of its chosen token every step, the host waiting for step
+                 i - 1 once step i is queued (sync_each 2, a streaming server's loop); "lockstep" = the same with the
+                 host waiting for every step before queueing the next (sync_each 1)
   roofline       the dominant kernel (largest share of step time, from a CUDA-event profile of every launch):
                  algorithmic bytes per launch / its mean launch time, against the measured HBM copy bandwidth
   step_roofline  the whole step: (pack bytes + KV bytes read) per token x tokens/s, against the same peak
@@ -435,7 +437,7 @@ def main():
 
     model, bits, batch, hist = CONFIGS[args.config]
     K, W = args.steps, args.warmup
-    cap = hist + K + 8
+    cap = hist + 4 * K + args.profile_steps + 8   # timed, e2e (sizing + two runs), profiled steps: no position clamps
     tp = world if args.config in TP_CONFIGS else 1
     rseed = 0 if tp > 1 else rank        # tensor parallel ranks hold shards of ONE model and the same sequences
     keep = args.ref_layers if (rank == 0 and not args.no_cpu) else False
@@ -477,14 +479,23 @@ def main():
     if dist is not None:
         dist.barrier()
     forced = np.full((K, batch), 0xFFFFFFFF, np.uint64)     # the step's input: "no forced token" (4 B per seq)
+    m.decode(K, forced=forced, want_tokens=True, sync_each=2)  # untimed: sizes the call's pinned host buffers
+    if dist is not None:
+        dist.barrier()
     t0 = time.perf_counter()
-    _, _, te = m.decode(K, forced=forced, want_tokens=True, sync_each=True)
+    _, _, te = m.decode(K, forced=forced, want_tokens=True, sync_each=2)
     e2e_s = time.perf_counter() - t0
     if dist is not None:
-        tt = torch.tensor([e2e_s], device="cuda")
+        dist.barrier()
+    t0 = time.perf_counter()
+    m.decode(K, forced=forced, want_tokens=True, sync_each=1)
+    lock_s = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([e2e_s, lock_s], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_s = float(tt.item())
+        e2e_s, lock_s = float(tt[0].item()), float(tt[1].item())
     e2e_tok_s = replicas * batch * K / e2e_s
+    lock_tok_s = replicas * batch * K / lock_s
 
     # ---- per-kernel profile (CUDA events around every launch, no overlap) -> the dominant kernel's roofline
     import ctypes as C
@@ -492,7 +503,7 @@ def main():
     kind_ms = (C.c_float * 6)()
     kind_n = (C.c_int32 * 6)()
     N.check(N.lib().agxc_model_profile(m.handle, args.profile_steps, kind_ms, kind_n), "profile")
-    pos_mid = hist + K + K + args.profile_steps // 2  # the profiled steps follow the timed and the e2e steps
+    pos_mid = hist + 4 * K + args.profile_steps // 2  # the profiled steps follow the timed and the e2e steps
     # this rank's shapes (the whole model at tp 1)
     hl, kvl, fl, hd, d = S.HEADS // tp, S.KV_HEADS // tp, S.FFN // tp, S.HEAD_DIM, S.D_MODEL
     kvrow = 2 * kvl * hd * 2                                       # K+V bytes per position per layer
@@ -563,7 +574,8 @@ def main():
                         parallelism=("tp%d" % tp) if tp > 1 else ("replicas" if world > 1 else "1gpu"),
                         l2="inputs larger than L2 (%.2f GB per step vs 126 MB L2)" % (step_bytes / 1e9)),
             e2e=dict(value=round(e2e_tok_s, 2), unit="tok/s", h2d_bytes_per_step=4 * batch,
-                     d2h_bytes_per_step=4 * batch),
+                     d2h_bytes_per_step=4 * batch, loop="one step queued ahead (sync_each 2)",
+                     lockstep=round(lock_tok_s, 2)),
             roofline=dict(bound="hbm", kernel=dname, achieved=round(achieved, 1), peak=peak, unit="GB/s",
                           frac=round(achieved / peak, 4), traffic=traffic, peak_source=peak_kind,
                           bytes_per_launch=kind_bytes[dname], us_per_launch=round(per_launch_ms * 1e3, 3)),

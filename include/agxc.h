@@ -215,7 +215,9 @@ AGXC_API int agxc_model_fill_history(agxc_model* m, int b, int n, uint64_t seed)
  * chosen tokens are device-resident; when `tokens_out` (host, [steps][batch]) is non-NULL each step's tokens are
  * copied back, and when `logits_out` (host, [steps][batch][vocab], needs keep_logits) is non-NULL, the logits too
  * (under tensor parallelism [steps][batch][count]: the rank's vocabulary slice).
- * `sync_each` = 1 waits for every step (the host sees each token before the next launch). */
+ * `sync_each` = 1 waits for every step (the host sees each token before the next launch); 2 keeps one step queued
+ * ahead: after queueing step i it waits for step i - 1, whose tokens are then on the host (a streaming server's
+ * loop: each token reaches the host one step after it is chosen, and the device never idles between steps). */
 typedef struct {
   float gpu_ms;               /* device time of the steps (CUDA events) */
   float host_ms;              /* host wall time of the call */

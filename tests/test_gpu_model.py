@@ -81,6 +81,29 @@ def test_free_generation_argmax_is_device_argmax(torch):
     assert list(log[3:9]) == [int(t) for t in toks[:, 0]]
 
 
+def test_decode_host_loops_agree(torch):
+    """The three host loops of agxc_decode (wait once at the end, wait for every step, one step queued ahead) run the
+    same graph: the same prompts give the same free-run tokens, with and without forced inputs; other modes are
+    refused."""
+    outs = []
+    for mode in (0, 1, 2):
+        m = _build(dict(SMALL), bits=4, batch=2, seed=3)
+        m.start(0, [5, 17, 33])
+        m.start(1, [9, 2])
+        m.decode(2, want_tokens=False)
+        free, _, _ = m.decode(7, want_tokens=True, sync_each=mode)
+        unset = np.full((4, 2), 0xFFFFFFFF, np.uint64)
+        unset[1, 0] = 77                                   # one forced token in the middle
+        forced, _, _ = m.decode(4, forced=unset, want_tokens=True, sync_each=mode)
+        outs.append((free, forced, m.state(0)[0]))
+        if mode == 2:
+            with pytest.raises(ValueError):
+                m.decode(1, sync_each=3)
+        m.close()
+    for free, forced, q0 in outs[1:]:
+        assert np.array_equal(free, outs[0][0]) and np.array_equal(forced, outs[0][1]) and q0 == outs[0][2]
+
+
 def test_batched_sequences_independent(torch):
     m = _build(dict(SMALL), bits=4, batch=3)
     rng = np.random.default_rng(5)
