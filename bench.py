@@ -13,6 +13,10 @@ so no flush is needed between steps.
         one launch of that kernel of the workload (after 3 warm-ups) through the C-ABI: the ncu capture case
         (B >= 32: the batched tensor-core GEMM agxc_qmm on the kernel's shape)
 
+    python bench.py --trace-step [--config ...]
+        one traced decode step of a batch-1 workload (AGXC_OPT_TRACE: every CTA's entry, dependency-wait, staging,
+        first-chunk, loop-end and exit times on the global timer), printed as per-phase means over the middle layers
+
 One JSON line on rank 0:
   value          tokens/s over the K timed steps (device time, CUDA events, inputs resident in HBM), summed over ranks
   e2e            the same steps through the public C-ABI decode call with a host->device copy of each step's input
@@ -199,6 +203,43 @@ def cpu_baseline_sample(m, sample_layers, pos):
     t_layer, t_head = cpu.timed_sample(sample_layers, pos)
     per_token = t_layer * m.shape.LAYERS + t_head
     return per_token, t_layer, t_head, cpu.threads
+
+
+def trace_step(args):
+    """--trace-step: one traced step of a batch-1 config after the bench's warm-up, reduced to per-phase means (µs)
+    over layers 2 .. L-2. For phase i: handoff = its last CTA past the dependency wait - phase i-1's last exit;
+    stage = activations staged - wait; first = first weight chunk landed - staged; loop = last chunk consumed - first
+    chunk; total = its last exit - phase i-1's last exit (all taken at the slowest CTA)."""
+    import numpy as np
+    from agxforge_b200.inference import assemble
+    model, bits, batch, hist = CONFIGS[args.config]
+    if batch != 1:
+        raise SystemExit("--trace-step: batch-1 configs only")
+    m = assemble.build(dict(model=model, bits=bits, batch=1, cap=hist + 16, seed=2))
+    m.set_option("persistent", 0)
+    m.start(0, [1])
+    m.fill_history(0, hist - args.warmup, seed=1792)
+    m.decode(args.warmup, want_tokens=False)
+    m.set_option("trace", 1)
+    m.decode(1, want_tokens=False)
+    m.trace()                                  # the first traced step primes the trace buffers
+    m.decode(1, want_tokens=False)
+    tr = m.trace()
+    m.close()
+    L = len(tr) // 5
+    per = {}
+    for i in range(10, 5 * (L - 2)):
+        d, p = tr[i], tr[i - 1]
+        rec = dict(handoff=d["wait"][1] - p["exit"][1], total=d["exit"][1] - p["exit"][1],
+                   entry_spread=d["entry"][1] - d["entry"][0], exit_spread=d["exit"][1] - d["exit"][0])
+        if "staged" in d:
+            rec.update(stage=d["staged"][1] - d["wait"][1], first=d["landed"][1] - d["staged"][1],
+                       loop=d["looped"][1] - d["landed"][1])
+        per.setdefault(d["kind"], []).append(rec)
+    phases = {k: {f: round(float(np.mean([r[f] for r in v])) / 1e3, 2) for f in v[0]} for k, v in per.items()}
+    head = tr[-1]
+    print(json.dumps(dict(trace_step=args.config, layers=L, step_us=round((head["exit"][1] - tr[0]["entry"][0]) / 1e3, 1),
+                          head_us=round((head["exit"][1] - tr[-2]["exit"][1]) / 1e3, 2), phases=phases)), flush=True)
 
 
 def run_reference(args, rank):
@@ -404,6 +445,7 @@ def main():
     ap.add_argument("--tp-allreduce", default="fused", choices=["fused", "nccl"],
                     help="tensor-parallel configs: GEMM + peer-memory all-reduce (fused) or NCCL all-reduce")
     ap.add_argument("--kernel-case", choices=KIND_NAMES, default=None)
+    ap.add_argument("--trace-step", action="store_true")
     ap.add_argument("--case-batch", type=int, default=0,
                     help="activation rows of --kernel-case (default: the config's batch; >= 32 = tensor-core qmm)")
     args = ap.parse_args()
@@ -431,6 +473,12 @@ def main():
     from agxforge_b200.inference import assemble
     if args.kernel_case:
         kernel_case(args, rank)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+    if args.trace_step:
+        if rank == 0:
+            trace_step(args)
         if dist is not None:
             dist.destroy_process_group()
         return
