@@ -122,7 +122,8 @@ int qmv_configure(const agxc_ctx* ctx) {
 // when asked). A chunk holds CG groups of every row tile of the unit (at most 36 KB, CG a multiple of the 16 / RW
 // K lanes that divides the CTA's groups); as many stages as ~80 KB allows (two CTAs, this kernel and its
 // programmatic-dependent successor, share an SM; 160 KB for the head, which has no successor in the step). With one
-// activation row, a CTA whose whole weight share fits 160 KB keeps all of it in flight instead (chunks up to 72 KB).
+// activation row, a CTA whose whole weight share fits 160 KB keeps all of it in flight instead (chunks up to 72 KB),
+// and a larger share gets a ring of up to 144 KB.
 QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, int hd, int splits, int force_rw,
                  int force_cg, int force_stages) {
   (void)hd;
@@ -179,26 +180,35 @@ QmvPlan plan_qmv(const agxc_ctx* ctx, int N, int K, int bits, int nb, int epi, i
   // most of the shared memory
   const int ring_cap = epi == EPI_ARGMAX ? 160 * 1024 : 80 * 1024;
   P.stages = std::max(2, std::min({kMaxStages, ring_cap / stage_bytes, std::max(2, chunks_per_cta)}));
-  // One activation row, no forced chunk size or depth: when the CTA's whole weight share fits 160 KB but not the ring
-  // above, it all goes in flight at entry, in chunks of up to 72 KB (fewer chunk hand-offs). The successor then shares
-  // the SM only once this kernel's CTAs leave. Measured on the 1.8B model's gate/up GEMV (147 KB per CTA): 722 us per
-  // decode step against 793 us with two 36 KB stages; four 36 KB stages gave 731 us.
-  if (nb == 1 && epi != EPI_ARGMAX && force_cg <= 0 && force_stages < 2 && chunks_per_cta > P.stages &&
-      static_cast<long>(chunks_per_cta) * stage_bytes <= 160 * 1024) {
-    const int kw = kConsumerWarps / P.RW;
-    for (int c = P.GC; c > P.CG; --c) {
-      if (P.GC % c == 0 && c % kw == 0 && P.RW * c * (TB + 64) <= 72 * 1024) {
-        P.CG = c;
-        break;
+  // One activation row, no forced chunk size or depth: more weight bytes in flight per SM than the 80 KB ring. When the
+  // CTA's whole weight share fits 160 KB it all goes in flight at entry, in chunks of up to 72 KB (fewer chunk
+  // hand-offs); a larger share gets a ring of up to 144 KB in its default chunks. The successor then shares the SM only
+  // once this kernel's CTAs leave. Measured per decode step of the 1.8B model (batch 1, history 1,792): 4-bit gate/up
+  // (147 KB a CTA) whole in two 72 KB chunks 722 us against 793 us with two 36 KB stages (four 36 KB stages: 731 us);
+  // 8-bit down (139 KB a CTA) whole 917 us against 956 us; 8-bit gate/up (278 KB a CTA) four 34 KB stages 835 us
+  // against 917 us with two (three: 910 us; two 69 KB chunks: 848 us).
+  if (nb == 1 && epi != EPI_ARGMAX && force_cg <= 0 && force_stages < 2 && chunks_per_cta > P.stages) {
+    if (static_cast<long>(chunks_per_cta) * stage_bytes <= 160 * 1024) {
+      const int kw = kConsumerWarps / P.RW;
+      for (int c = P.GC; c > P.CG; --c) {
+        if (P.GC % c == 0 && c % kw == 0 && P.RW * c * (TB + 64) <= 72 * 1024) {
+          P.CG = c;
+          break;
+        }
       }
+      P.stages = std::max(2, std::min(kMaxStages, (units + sms - 1) / sms * (P.GC / P.CG)));
+    } else {
+      P.stages = std::max(P.stages, std::min(kMaxStages, 144 * 1024 / stage_bytes));
     }
-    P.stages = std::max(2, std::min(kMaxStages, (units + sms - 1) / sms * (P.GC / P.CG)));
   }
   if (force_stages >= 2 && force_stages <= kMaxStages) P.stages = force_stages;
   int grid = std::min(units, sms);
   grid = std::max(SC, grid / SC * SC);
   P.grid = grid;
   P.smem = smem_total(bits, nbt, P.RW, P.CG, P.GC, P.stages);
+  const size_t optin = ctx ? static_cast<size_t>(ctx->max_smem_optin) : 227 * 1024;
+  while (force_stages < 2 && P.stages > 2 && P.smem > optin)  // an unforced ring gives way to the staged activations
+    P.smem = smem_total(bits, nbt, P.RW, P.CG, P.GC, --P.stages);
   return P;
 }
 
