@@ -4,11 +4,19 @@ agxforge/inference/assemble.py: configure 71-92, build 596-828; its region R and
     configure(config)           a config dict (or JSON path): {"model": name | shape overrides, "bits", "scale_dtype",
                                 "cap", "batch", "seed", "keep_logits", "tp", "tp_rank"}; returns the normalised config
                                 (tp > 1: tensor parallel over tp ranks, one process per GPU, torch.distributed
-                                initialised; each rank builds its shard of the same seeded weights, see tp.py)
+                                initialised; each rank builds its shard of the same seeded weights, see tp.py).
+                                configure(deliver, config), the reference's two-argument form, is accepted: the
+                                deliver index of compiled G17 bundles has no counterpart and is ignored; the config
+                                becomes the module's current one, which build(bits) uses
     build(config, ...)          a DecodeModel: the library's model object with every pack, gain, bias and the
                                 embedding set. Synthetic weights are generated on the device from the config's seed
                                 (N(0, 0.02) fp32, then the device quantiser), or taken from given reference-format
-                                packs (`weights=`)
+                                packs (`weights=`, e.g. checkpoint.load). build(bits) (the reference's form) builds the
+                                current config at that width; the reference returns (graph.json dict, ops), here the
+                                device model is the graph
+    simulate(bits, tokens)      the reference's CPU replay of the built graph (assemble.py:934-955) is not part of this
+                                package (it has no CPU path); the CPU restatement of the decode step that the tests
+                                compare against lives in the repository's oracle package
     DecodeModel.start(b, prompt)  the sequence's prompt in its token log, x = embedding(prompt[0]), q0 = 0
     DecodeModel.decode(steps)     run steps (execute.decode wraps it in the reference's report)
 
@@ -25,9 +33,9 @@ import os
 import numpy as np
 
 from agxforge_b200 import _native as N
-from agxforge_b200.inference import models
-from agxforge_b200.inference import tp as TP
-from agxforge_b200.kernels import qmv as Q
+from agxforge.inference import models
+from agxforge.inference import tp as TP
+from agxforge.kernels import qmv as Q
 
 ROLE = {"qkv": N.ROLE_QKV, "wo": N.ROLE_WO, "gate": N.ROLE_GATE, "up": N.ROLE_UP, "down": N.ROLE_DOWN,
         "head": N.ROLE_HEAD}
@@ -37,8 +45,19 @@ DEFAULTS = dict(model="internlm2.5-1.8b", bits=4, scale_dtype="fp16", cap=2048, 
                 init_std=0.02, embed_std=0.02, bias_std=0.02)
 
 
-def configure(config):
-    """Normalise a config (dict or path of a JSON file)."""
+_current = None
+
+
+def configure(*args):
+    """Normalise a config (dict or path of a JSON file): configure(config), or the reference's configure(deliver,
+    config) with the deliver index ignored. The result is also the module's current config (for build(bits))."""
+    global _current
+    if len(args) == 1:
+        config = args[0]
+    elif len(args) == 2:
+        config = args[1]
+    else:
+        raise TypeError("configure(config) or configure(deliver, config)")
     if isinstance(config, (str, os.PathLike)):
         with open(config) as f:
             config = json.load(f)
@@ -48,6 +67,7 @@ def configure(config):
     if isinstance(shape, str):
         shape = models.get(shape)
     elif isinstance(shape, dict):
+        shape = dict(shape)
         base = models.get(shape.pop("base")) if "base" in shape else None
         shape = base.replace(**shape) if base else models.Model(**shape)
     cfg["shape"] = shape
@@ -63,7 +83,15 @@ def configure(config):
     TP.check(shape, cfg["tp"], B)
     if not 0 <= cfg["tp_rank"] < cfg["tp"]:
         raise ValueError("configure: 0 <= tp_rank < tp")
+    _current = cfg
     return cfg
+
+
+def simulate(bits, tokens):
+    """The reference's CPU replay (assemble.py:934-955). This package runs only on the device; the CPU restatement
+    of the decode step used as the parity oracle is test infrastructure outside it."""
+    raise NotImplementedError("simulate: the CPU replay of the decode step is not part of the agxforge package on "
+                              "the B200 (no CPU path); the repository's oracle package restates it for the tests")
 
 
 def _gen(torch, seed, *key):
@@ -88,7 +116,7 @@ class DecodeModel:
     def __init__(self, cfg, device=0, tp_id=None):
         import torch
         if not torch.cuda.is_available():
-            raise RuntimeError("agxforge_b200 needs a CUDA device (B200); none is visible")
+            raise RuntimeError("agxforge needs a CUDA device (B200); none is visible")
         self.cfg = cfg
         self.shape = S = cfg["shape"]
         self.device = device
@@ -268,7 +296,7 @@ class DecodeModel:
 def synthetic_pack(torch, N_, K, bits, scale_dtype, gen, std, device):
     """N(0, std) fp32 weights generated on the device, quantised on the device: reference-format (packed, s, b)."""
     W = torch.randn((N_, K), generator=gen, device="cuda:%d" % device, dtype=torch.float32) * std
-    out = Q.quantize(W, bits=bits, scale_dtype=scale_dtype, device=device)
+    out = Q.quantize(W, bits=bits, scale_dtype=scale_dtype, device=device)[:3]
     del W
     return out
 
@@ -280,6 +308,12 @@ def build(config, device=0, weights=None, keep_packs=False):
     keep_packs=True keeps a host copy of every pack and vector in model.packs (for the CPU oracle); an integer n keeps
     the packs of the first n layers only (and the head)."""
     import torch
+    if isinstance(config, int) and not isinstance(config, bool):
+        if _current is None:
+            raise ValueError("build(bits): configure a model first")
+        config = dict(_current, bits=config)
+        config.pop("shape", None)
+        config["model"] = _current["shape"]
     cfg = configure(config)
     S = cfg["shape"]
     world, rank = cfg["tp"], cfg["tp_rank"]
@@ -332,7 +366,7 @@ def build(config, device=0, weights=None, keep_packs=False):
     if p is None:
         if S.TIED:
             e32 = emb.to(torch.float32) if hasattr(emb, "to") else torch.from_numpy(np.asarray(emb, np.float32)).cuda()
-            p = Q.quantize(e32, bits=bits, scale_dtype=sdt, device=device)
+            p = Q.quantize(e32, bits=bits, scale_dtype=sdt, device=device)[:3]
         else:
             p = synthetic_pack(torch, S.VOCAB, S.D_MODEL, bits, sdt, _gen(torch, seed, "head"), cfg["init_std"], device)
     m.set_pack(0, "head", *TP.shard_pack("head", p, S, bits, world, rank))

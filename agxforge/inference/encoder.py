@@ -78,7 +78,7 @@ class Encoder:
     def __init__(self, config, max_batch=32, max_seq=128, device=0):
         import torch
         if not torch.cuda.is_available():
-            raise RuntimeError("agxforge_b200 needs a CUDA device (B200); none is visible")
+            raise RuntimeError("agxforge needs a CUDA device (B200); none is visible")
         self.config = dict(config)
         W, L, H, F, V, P, T, eps = check_config(self.config)
         self.hidden, self.layers, self.heads, self.ffn, self.vocab = W, L, H, F, V

@@ -12,7 +12,7 @@ from __future__ import annotations
 import ctypes as C
 
 from agxforge_b200 import _native as N
-from agxforge_b200.kernels import qmv as _qmv
+from agxforge.kernels import qmv as _qmv
 
 
 def qmm(pack, x, ksplit=0, out=None):

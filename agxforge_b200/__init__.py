@@ -1,13 +1,4 @@
-"""agxforge_b200 — AGXForge's quantized LLM decode path, rebuilt for NVIDIA B200 (sm_100a).
-
-The package keeps the reference's Python module layout for this path:
-
-    agxforge_b200.kernels      qmv (affine group-64 packs, the GEMV family), attention, norm, argmax, numerics
-    agxforge_b200.inference    models (shapes), catalog (which kernel form each role runs), assemble (the layer
-                               builder: a model's weights, KV cache and decode graph on the device), execute (the
-                               decode loop and its report)
-
-Every computation runs in libagxcuda.so (hand-written CUDA for sm_100a, built in-tree by
-``python -m agxforge_b200.build``) through the C ABI in include/agxc.h. There is no CPU fallback.
-"""
-__version__ = "0.1.0"
+"""agxforge_b200 — the native half of the B200 decode path: the CUDA sources (csrc/), the built library
+(lib/libagxcuda.so, ``python -m agxforge_b200.build``) and its ctypes binding (_native). The Python API that mirrors
+the reference's modules lives in the ``agxforge`` package beside this one."""
+__version__ = "0.2.0"

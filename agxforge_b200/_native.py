@@ -81,6 +81,8 @@ SIGNATURES = {
     "agxc_qmm": (_I, [_P, _P, _P, _I, _P, _I, _I, _P]),
     "agxc_rmsnorm_dev": (_I, [_P, _P, _I, _I, _I, _P, C.c_float, _P, _P]),
     "agxc_attention_dev": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
+    "agxc_rope_append_dev": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, C.c_float, _P, _P, _P, _P]),
+    "agxc_argmax_dev": (_I, [_P, _P, _I, _P, _P]),
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "agxc_tp_unique_id": (_I, [_P]),
     "agxc_model_prefill": (_I, [_P, _I, _P, _I, C.POINTER(Timing)]),

@@ -196,13 +196,17 @@ def dist_setup(gpus):
     return rank, world, local, dist
 
 
-def cpu_baseline_sample(m, sample_layers, pos):
-    """Time the numpy FP32 port of the reference's CPU decode step on `sample_layers` layers + the head."""
+def cpu_baseline_sample(m, tokens, pos):
+    """Time the numpy FP32 port of the reference's CPU decode step (oracle/cpu_decode.py) on `tokens` whole tokens
+    (every layer, the head, the first argmax) at positions pos .., over this model's packs copied to the host."""
     from oracle.cpu_decode import CpuDecoder
-    cpu = CpuDecoder(m.shape, m.packs, m.bits, m.cfg["scale_dtype"], pos + 2)
-    t_layer, t_head = cpu.timed_sample(sample_layers, pos)
-    per_token = t_layer * m.shape.LAYERS + t_head
-    return per_token, t_layer, t_head, cpu.threads
+    cpu = CpuDecoder(m.shape, m.packs, m.bits, m.cfg["scale_dtype"], pos + tokens + 2)
+    cpu.fill_history(pos, seed=1792)
+    tok = 1
+    t0 = time.perf_counter()
+    for i in range(tokens):
+        tok = cpu.decode_token(tok, pos + i)
+    return (time.perf_counter() - t0) / tokens, cpu.threads
 
 
 def trace_step(args):
@@ -211,7 +215,7 @@ def trace_step(args):
     stage = activations staged - wait; first = first weight chunk landed - staged; loop = last chunk consumed - first
     chunk; total = its last exit - phase i-1's last exit (all taken at the slowest CTA)."""
     import numpy as np
-    from agxforge_b200.inference import assemble
+    from agxforge.inference import assemble
     model, bits, batch, hist = CONFIGS[args.config]
     if batch != 1:
         raise SystemExit("--trace-step: batch-1 configs only")
@@ -242,31 +246,74 @@ def trace_step(args):
                           head_us=round((head["exit"][1] - tr[-2]["exit"][1]) / 1e3, 2), phases=phases)), flush=True)
 
 
-def run_reference(args, rank):
-    """--impl reference: the reference's CPU implementation of the path (the port; the reference's Python package
-    cannot travel with this repository) on this host's cores, same config/metric."""
-    import torch
-    from agxforge_b200.inference import assemble
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def workload_config(args, world, model, bits, batch, hist, tp):
+    """The config object of a decode workload's line: identical in both arms (--impl ours / reference)."""
+    K = args.steps
+    step_bytes = None
+    try:
+        from agxforge.inference import models
+        S = models.get(model)
+        step_bytes = S.weight_bytes(bits) + batch * S.kv_bytes_per_position() * (hist + (K - 1) / 2.0 + 1)
+    except Exception:  # noqa: BLE001
+        pass
+    return dict(workload=args.config, model=model, bits=bits, group=64, scale_dtype="fp16", batch=batch,
+                history=hist, positions=[hist, hist + K - 1],
+                parallelism=("tp%d" % tp) if tp > 1 else ("replicas" if world > 1 else "1gpu"),
+                l2="inputs larger than L2 (%.2f GB per step vs 126 MB L2)" % (step_bytes / 1e9) if step_bytes
+                else "inputs larger than L2")
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation of the path on this host's cores, with the same config,
+    metric and unit as our arm. The reference's own CPU references (its Python package) do not travel with this
+    repository, so the timed code is their restatement, oracle/cpu_decode.py (the QSim chain as numpy FP32, row
+    blocks on a thread pool over every core). Nothing here loads the CUDA library: the packs are made on the host from
+    the config's seed (N(0, 0.02) weights quantised by oracle.pack, the reference's quantize). Each step is one whole
+    token (every layer, the head, the first argmax) at the positions our arm times: W warm-up tokens at hist - W ..
+    hist - 1 over a seeded history, then K timed tokens at hist .. hist + K - 1."""
+    from agxforge.inference import models       # shapes only (plain Python)
+    from oracle import cpu_decode as CD
     model, bits, batch, hist = CONFIGS[args.config]
-    cfg = dict(model=model, bits=bits, batch=1, cap=hist + 8, seed=2)
-    # the packs come from the same device quantiser as our arm (same seeded weights), copied to the host
-    m = assemble.build(cfg, keep_packs=args.ref_layers)
-    torch.cuda.synchronize()
-    samples = []
-    for i in range(max(1, args.ref_steps)):
-        per_token, t_layer, t_head, cores = cpu_baseline_sample(m, args.ref_layers, hist)
-        samples.append(per_token)
-    per_token = statistics.median(samples)
-    v = batch / per_token if batch == 1 else 1.0 / per_token
-    line = dict(metric=METRIC, impl="reference", value=round(1.0 / per_token, 5), unit="tok/s", n_gpus=args.gpus,
-                steps=args.steps, warmup=args.warmup, ms_per_step=round(per_token * 1e3, 1), higher_is_better=True,
-                scaling="weak", vs_baseline=None, dtype="f32", data="synthetic",
-                config=dict(workload=args.config, model=model, bits=bits, batch=1, history=hist),
-                cpu_baseline=dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores, kind="port",
-                                  sample="%d of %d layers + head of one token at position %d, median of %d, scaled "
-                                         "to the full depth" % (args.ref_layers, m.shape.LAYERS, hist,
-                                                                 len(samples))),
+    tp = world if args.config in TP_CONFIGS else 1
+    S = models.get(model)
+    K, W = args.steps, args.warmup
+    t0 = time.perf_counter()
+    packs = CD.host_packs(S, bits, "fp16", 2)
+    pack_s = time.perf_counter() - t0
+    cpu = CD.CpuDecoder(S, packs, bits, "fp16", hist + K + 2)
+    cpu.fill_history(hist - W, seed=1792)
+    tok = 1
+    for i in range(W):
+        tok = cpu.decode_token(tok, hist - W + i)
+    t0 = time.perf_counter()
+    for i in range(K):
+        tok = cpu.decode_token(tok, hist + i)
+    dt = time.perf_counter() - t0
+    per_token = dt / K
+    v = batch / per_token if batch > 1 else 1.0 / per_token
+    cores = cpu.threads
+    sample = ("%d whole tokens (all %d layers, head, argmax) at positions %d..%d over a seeded %d-position history, "
+              "batch %d of %d sequences (the CPU step is per sequence)" % (K, S.LAYERS, hist, hist + K - 1, hist - W,
+                                                                             1, batch))
+    line = dict(metric=METRIC, impl="reference", value=round(1.0 / per_token, 5), unit="tok/s", n_gpus=world,
+                steps=K, warmup=W, ms_per_step=round(per_token * 1e3, 1), higher_is_better=True,
+                scaling="strong" if tp > 1 else "weak", vs_baseline=None, dtype="f32", data="synthetic",
+                config=workload_config(args, world, model, bits, batch, hist, tp),
+                cpu_baseline=dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores, cpu=cpu_model(),
+                                  kind="port", sample=sample, packs_made_on_host_s=round(pack_s, 1)),
                 e2e=dict(value=round(1.0 / per_token, 5), unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    del v
     print(json.dumps(line), flush=True)
 
 
@@ -308,7 +355,7 @@ def run_encoder_reference(args):
 def run_encoder(args, rank, world, local, dist):
     """Config 2 on each GPU (replicas only: the encoder's batches are independent)."""
     import torch
-    from agxforge_b200.inference.encoder import MINILM_L6, Encoder
+    from agxforge.inference.encoder import MINILM_L6, Encoder
     B, S = ENCODER_CONFIGS[args.config]
     K, W = args.steps, args.warmup
     enc = Encoder.synthetic(MINILM_L6, seed=1 + rank, max_batch=B, max_seq=S, device=local)
@@ -382,9 +429,9 @@ def kernel_case(args, rank):
     kernel's name, `-s 3 -c 1`). GEMV kernels run through agxc_qmv on packs of the workload's shape (same planner and
     kernels as the model); attention through agxc_attention_dev on a cache of the workload's shape at position 1,792."""
     import torch
-    from agxforge_b200.kernels import attention as A
-    from agxforge_b200.kernels import qmv as Q
-    from agxforge_b200.inference import models
+    from agxforge.kernels import attention as A
+    from agxforge.kernels import qmv as Q
+    from agxforge.inference import models
     model, bits, batch, hist = CONFIGS[args.config]
     S = models.get(model)
     torch.manual_seed(5)
@@ -397,13 +444,13 @@ def kernel_case(args, rank):
             A.attention(q, K, V, [hist] * batch)
     elif (args.case_batch or batch) >= 32:
         # the batched tensor-core GEMM (agxc_qmm) on the kernel's shape (gate/up as one plain 2F-row pack)
-        from agxforge_b200.kernels.qmm import qmm
+        from agxforge.kernels.qmm import qmm
         B = args.case_batch or batch
         shapes = {r: (n, k) for r, n, k in S.matrices()}
         n, k = {"qkv": shapes["qkv"], "wo": shapes["wo"], "ffn": (2 * shapes["gate"][0], shapes["gate"][1]),
                 "down": shapes["down"], "head": (S.VOCAB, S.D_MODEL)}[args.kernel_case]
         W = torch.randn(n, k, device="cuda") * 0.02
-        pk = Q.Pack(*Q.quantize(W, bits=bits), n, k, bits=bits)
+        pk = Q.Pack(*Q.quantize(W, bits=bits, scale_dtype="fp16")[:3], n, k, bits=bits)
         del W
         x = torch.randn(B, k, device="cuda").half()
         for _ in range(4):
@@ -414,12 +461,12 @@ def kernel_case(args, rank):
                 "head": (S.VOCAB, S.D_MODEL)}[args.kernel_case]
         W = torch.randn(n, k, device="cuda") * 0.02
         if args.kernel_case == "ffn":
-            g = Q.quantize(W, bits=bits)
-            u = Q.quantize(torch.randn(n, k, device="cuda") * 0.02, bits=bits)
+            g = Q.quantize(W, bits=bits, scale_dtype="fp16")[:3]
+            u = Q.quantize(torch.randn(n, k, device="cuda") * 0.02, bits=bits, scale_dtype="fp16")[:3]
             pk = Q.Pack.gateup(g, u, n, k, bits=bits)
             epi = "swiglu"
         else:
-            pk = Q.Pack(*Q.quantize(W, bits=bits), n, k, bits=bits)
+            pk = Q.Pack(*Q.quantize(W, bits=bits, scale_dtype="fp16")[:3], n, k, bits=bits)
             epi = "f32"
         del W
         x = torch.randn(args.case_batch or batch, k, device="cuda").half()
@@ -438,7 +485,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="internlm-q4-1792", choices=sorted(CONFIGS) + sorted(ENCODER_CONFIGS))
-    ap.add_argument("--ref-layers", type=int, default=2)
+    ap.add_argument("--cpu-tokens", type=int, default=2, help="whole tokens the cpu_baseline leg times")
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--profile-steps", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
@@ -464,13 +511,13 @@ def main():
         return
     if args.impl == "reference":
         if rank == 0:
-            run_reference(args, rank)
+            run_reference(args, rank, world)
         if dist is not None:
             dist.destroy_process_group()
         return
 
     import torch
-    from agxforge_b200.inference import assemble
+    from agxforge.inference import assemble
     if args.kernel_case:
         kernel_case(args, rank)
         if dist is not None:
@@ -488,7 +535,7 @@ def main():
     cap = hist + 4 * K + args.profile_steps + 8   # timed, e2e (sizing + two runs), profiled steps: no position clamps
     tp = world if args.config in TP_CONFIGS else 1
     rseed = 0 if tp > 1 else rank        # tensor parallel ranks hold shards of ONE model and the same sequences
-    keep = args.ref_layers if (rank == 0 and not args.no_cpu) else False
+    keep = bool(rank == 0 and world == 1 and not args.no_cpu)
     m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=2 + rseed, tp=tp,
                             tp_rank=rank if tp > 1 else 0), device=local, keep_packs=keep)
     S = m.shape
@@ -605,11 +652,15 @@ def main():
                        tok_s=round((hist - 1) / (pt["gpu_ms"] / 1e3), 1), launches=pt["launches"])
 
     cpu = None
-    if rank == 0 and not args.no_cpu:
-        per_token, t_layer, t_head, cores = cpu_baseline_sample(m, args.ref_layers, hist)
-        cpu = dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores, kind="port",
-                   sample="%d of %d layers + head of one token at position %d (%.2f s/layer, %.2f s head), scaled "
-                          "to the full depth" % (args.ref_layers, S.LAYERS, hist, t_layer, t_head))
+    if keep:
+        per_token, cores = cpu_baseline_sample(m, args.cpu_tokens, hist)
+        cpu = dict(value=round(1.0 / per_token, 5), unit="tok/s", cores=cores,
+                   cpu=cpu_model(), kind="port",
+                   sample="%d whole tokens (all %d layers, head, argmax) of one sequence at position %d over a seeded "
+                          "history, this run's packs copied to the host (%.2f s a token)%s" % (
+                              args.cpu_tokens, S.LAYERS, hist, per_token,
+                              "; the CPU step is per sequence, so a batch of %d takes %d such tokens" % (batch, batch)
+                              if batch > 1 else ""))
 
     if rank == 0:
         line = dict(
@@ -617,10 +668,7 @@ def main():
             ms_per_step=round(gpu_ms / K, 4), higher_is_better=True, scaling="strong" if tp > 1 else "weak",
             vs_baseline=None, dtype="u4" if
             bits == 4 else "u8", data="synthetic (seeded random-init weights and uniform-random token ids)",
-            config=dict(workload=args.config, model=model, bits=bits, group=64, scale_dtype="fp16", batch=batch,
-                        history=hist, positions=[hist, hist + K - 1],
-                        parallelism=("tp%d" % tp) if tp > 1 else ("replicas" if world > 1 else "1gpu"),
-                        l2="inputs larger than L2 (%.2f GB per step vs 126 MB L2)" % (step_bytes / 1e9)),
+            config=workload_config(args, world, model, bits, batch, hist, tp),
             e2e=dict(value=round(e2e_tok_s, 2), unit="tok/s", h2d_bytes_per_step=4 * batch,
                      d2h_bytes_per_step=4 * batch, loop="one step queued ahead (sync_each 2)",
                      lockstep=round(lock_tok_s, 2)),

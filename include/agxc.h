@@ -147,6 +147,19 @@ AGXC_API int agxc_attention_dev(agxc_ctx* ctx, int nb, int heads, int kv_heads, 
                        const uint16_t* q16_dev, const uint16_t* k_dev, const uint16_t* v_dev, uint16_t* out_dev,
                        int splits, void* stream);
 
+/* RoPE + q scale + KV append on one token's fp32 qkv row in the reference's logical order [heads | kv_heads |
+ * kv_heads] x head_dim (attention.py:1309-1323 attn_rope_reference; numerics.py:340-346 rope_rotate): q16 fp16
+ * [heads][head_dim] = fp16(rope(q) * qscale); K and V rows fp16 written at row `pos` (clamped to cap-1) of the caches
+ * [kv_heads][cap][head_dim]. cos/sin fp32 [head_dim/2] for that position. Each rotated value is two rounded products
+ * and one rounded sum, as rope_rotate. (In the decode step this is the qkv GEMV's epilogue.) */
+AGXC_API int agxc_rope_append_dev(agxc_ctx* ctx, const float* qkv_dev, int heads, int kv_heads, int head_dim, int cap,
+                                  int pos, const float* cos_dev, const float* sin_dev, float qscale,
+                                  uint16_t* q16_dev, uint16_t* kcache_dev, uint16_t* vcache_dev, void* stream);
+
+/* The first maximum of an fp32 row of n values (argmax.py:287-288 argmax_reference; NaN-free input): *out_dev =
+ * the smallest index holding the largest value. (In the decode step this is the vocabulary GEMV's epilogue.) */
+AGXC_API int agxc_argmax_dev(agxc_ctx* ctx, const float* x_dev, int n, int32_t* out_dev, void* stream);
+
 /* ---- the model (agxforge/inference/assemble.py configure 71-92, build 596-828; models.py 26-54) -------------- */
 typedef struct {
   int32_t d_model, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab;

@@ -9,6 +9,11 @@ FP32: each projection dequantises its pack row-block by row-block (w = q*s + b, 
 and forms the fp32 dot products, with the reference's storage rounding points (fp16 x, normed rows, q/k/v, attention
 output, SwiGLU product). Row blocks run on a thread pool over the host's cores, as the reference's references do
 (qmv.py:1641-1648, G17_REF_THREADS).
+
+    host_packs(shape, bits, scale_dtype, seed)   the model's packs made on the host: seeded N(0, 0.02) fp32 weights
+                                                 quantised by oracle.pack (the reference's quantize), fp16 embedding,
+                                                 unit gains; no device and no native library involved
+    CpuDecoder.decode_token(x16, pos)            one whole decode step (every layer, the head, the first argmax)
 """
 from __future__ import annotations
 
@@ -22,6 +27,37 @@ import numpy as np
 from oracle import pack as P
 
 F32 = np.float32
+
+
+ROLE_SEED = {"qkv": 0, "wo": 1, "gate": 2, "up": 3, "down": 4, "head": 5}
+
+
+def host_packs(shape, bits, scale_dtype, seed, threads=None, std=0.02):
+    """Every pack, gain and the embedding of a synthetic model, generated and quantised on the host (matrices in
+    parallel over the cores; numpy's generators and array kernels release the GIL). Keys as DecodeModel.packs."""
+    S = shape
+    jobs = [((l, role), n, k) for l in range(S.LAYERS) for role, n, k in S.matrices()]
+    jobs.append(((None, "head"), S.VOCAB, S.D_MODEL))
+    out = {}
+
+    def make(job):
+        (l, role), n, k = job
+        rng = np.random.default_rng([seed, 1000 if l is None else l, ROLE_SEED[role]])
+        W = rng.standard_normal((n, k), dtype=F32) * F32(std)
+        a, sc, b, _ = P.quantize(W, bits, scale_dtype=scale_dtype)
+        return job[0], (a, sc, b)
+    with ThreadPoolExecutor(threads or os.cpu_count() or 1) as pool:
+        for key, val in pool.map(make, jobs):
+            out[key] = val
+    rng = np.random.default_rng([seed, 99])
+    out["embed"] = (rng.standard_normal((S.VOCAB, S.D_MODEL), dtype=F32) * F32(std)).astype(np.float16)
+    for l in range(S.LAYERS):
+        out[(l, "attn_gain")] = np.ones(S.D_MODEL, np.float16)
+        out[(l, "ffn_gain")] = np.ones(S.D_MODEL, np.float16)
+        if S.QKV_BIAS:
+            out[(l, "qkv_bias")] = (rng.standard_normal(S.QKV, dtype=F32) * F32(std)).astype(np.float16)
+    out["final_gain"] = np.ones(S.D_MODEL, np.float16)
+    return out
 
 
 class CpuDecoder:
@@ -100,6 +136,20 @@ class CpuDecoder:
     def head(self, x16):
         xf = self.rmsnorm(x16, self.k["final_gain"], self.S.EPS)
         return self.matvec((None, "head"), self.S.VOCAB, self.S.D_MODEL, xf)
+
+    def fill_history(self, n, seed=0):
+        """KV rows 0 .. n-1 of every layer hold seeded N(0, 1) fp16 values (the bench's device-filled history)."""
+        rng = np.random.default_rng(seed)
+        self.K[:, :, :n] = rng.standard_normal(self.K[:, :, :n].shape, dtype=F32).astype(np.float16)
+        self.V[:, :, :n] = rng.standard_normal(self.V[:, :, :n].shape, dtype=F32).astype(np.float16)
+
+    def decode_token(self, token, pos):
+        """One whole decode step of the token at position `pos`: x = embedding(token), every layer (appending its K/V
+        row at pos), the final norm, the head and the first argmax. Returns the next token."""
+        x = self.k["embed"][int(token)].astype(F32)
+        for l in range(self.S.LAYERS):
+            x = self.layer(l, x, pos)
+        return int(np.argmax(self.head(x)))
 
     def timed_sample(self, layers, pos, seed=0):
         """Time `layers` layers and the head of one decode step at position `pos` (the KV rows before pos hold

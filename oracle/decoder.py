@@ -225,6 +225,54 @@ class Model:
         logits = xf @ self.head.w64().T
         return (logits, kept) if keep else logits
 
+    def forward_both(self, tokens, logit_positions):
+        """Both policies in one pass over the layers (each pack dequantised once): returns (logits FP64, logits
+        half-transport, the half-transport final normed rows xf [positions, d] and the head's FP64 weights), for the
+        argmax's rounding bound (argmax_rounding_bound)."""
+        S = self.shape
+        tokens = np.asarray(tokens, np.int64)
+        T = tokens.size
+        H, KVH, hd = S.n_heads, S.n_kv_heads, S.head_dim
+        pos = np.arange(T)
+        cos_h, sin_h = (a.astype(F64) for a in rope_tables(T, hd, S.rope_theta))
+        inv = S.rope_theta ** (-np.arange(0, hd, 2, dtype=F64) / hd)
+        ang = pos[:, None].astype(F64) * inv[None, :]
+        cos_f, sin_f = np.cos(ang), np.sin(ang)
+        qscale = LOG2E / math.sqrt(hd)
+        x = {False: self.embed[tokens].astype(F64), True: self.embed[tokens].astype(F64)}
+        for L in self.layers:
+            w = {r: L[r].w64() for r in ("qkv", "wo", "gate", "up", "down")}
+            for half in (False, True):
+                cos, sin = (cos_h, sin_h) if half else (cos_f, sin_f)
+                xx = x[half]
+                h1 = rmsnorm(xx, L["g1"].astype(F64), S.eps, half)
+                qkv = h1 @ w["qkv"].T
+                if L.get("bias") is not None:
+                    qkv = qkv + np.asarray(L["bias"], np.float16).astype(F64)
+                q = qkv[:, :H * hd].reshape(T, H, hd)
+                k = qkv[:, H * hd:(H + KVH) * hd].reshape(T, KVH, hd)
+                v = qkv[:, (H + KVH) * hd:].reshape(T, KVH, hd)
+                qr = rope(q, cos[:, None, :], sin[:, None, :]) * qscale
+                kr = rope(k, cos[:, None, :], sin[:, None, :])
+                if half:
+                    qr, kr, v = f16(qr), f16(kr), f16(v)
+                a = attention_causal(qr, kr, v, KVH).reshape(T, H * hd)
+                if half:
+                    a = f16(a)
+                h = xx + a @ w["wo"].T
+                h2 = rmsnorm(h, L["g2"].astype(F64), S.eps, half)
+                act = silu(h2 @ w["gate"].T) * (h2 @ w["up"].T)
+                if half:
+                    act = f16(act)
+                xn = h + act @ w["down"].T
+                x[half] = f16(xn) if half else xn
+            del w
+        sel = np.asarray(logit_positions, np.int64)
+        W = self.head.w64()
+        xf64 = rmsnorm(x[False][sel], self.final_gain.astype(F64), S.eps, False)
+        xfh = rmsnorm(x[True][sel], self.final_gain.astype(F64), S.eps, True)
+        return xf64 @ W.T, xfh @ W.T, xfh, W
+
 
 def first_argmax(v):
     """The first index of the maximum (np.argmax's rule; agxforge/kernels/argmax.py:287-288)."""
@@ -237,6 +285,26 @@ def top2_margin(v):
     i = int(np.argmax(v))
     w = np.delete(v, i)
     return float(v[i] - w.max())
+
+
+def argmax_rounding_bound(W, xfh, i, j, K=None):
+    """How far apart two logits i and j of one step may be and still swap order between the GPU and the
+    half-transport oracle through rounding alone. The two sides store the same fp16 points; after the last layer the
+    final normed row xf is fp16 on both, and a pre-rounding value that lands on the other side of an fp16 rounding
+    boundary moves an element by one fp16 ulp. Assuming at most that (one ulp16 per element of xf) plus the fp32
+    accumulation of the K-term dot products (K eps32 relative, the textbook gamma_K bound), each logit moves by at
+    most
+        d_r = sum_k |W_rk| ulp16(xf_k) + K eps32 sum_k |W_rk xf_k|,
+    and the order of i and j can only flip if their margin is at most d_i + d_j."""
+    xfh = np.asarray(xfh, F64)
+    ulp = np.spacing(np.abs(xfh).astype(np.float16)).astype(F64)
+    K = xfh.size if K is None else K
+    eps32 = float(np.finfo(np.float32).eps)
+
+    def d(r):
+        wr = np.abs(np.asarray(W[r], F64))
+        return float(wr @ ulp + K * eps32 * (wr @ np.abs(xfh)))
+    return d(i) + d(j)
 
 
 def logit_bound(ref):

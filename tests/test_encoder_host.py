@@ -2,7 +2,7 @@
 (agxforge/g17/inferencegraph.py:116-157) plus this encoder's shape limits, and the MiniLM-L6 config is admitted."""
 import pytest
 
-from agxforge_b200.inference import encoder as ENC
+from agxforge.inference import encoder as ENC
 
 
 def test_minilm_config_admitted():

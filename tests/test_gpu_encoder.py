@@ -29,7 +29,7 @@ def torch():
 
 @pytest.fixture(scope="module")
 def enc(torch):
-    from agxforge_b200.inference.encoder import Encoder
+    from agxforge.inference.encoder import Encoder
     e = Encoder(E.MINILM_L6, max_batch=32, max_seq=128).load(E.make_params(1))
     yield e
     e.close()
@@ -42,7 +42,7 @@ def enc(torch):
 def test_hgemm_against_torch(torch, M, N, K, epi):
     import ctypes as C
     from agxforge_b200 import _native as N_
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
     A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).half()
     W = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
@@ -150,7 +150,7 @@ def test_refusals(enc):
 def test_long_sequences_fp32_attention_path(torch):
     """Sequences longer than 128 tokens take the fp32 CUDA-core attention (the tensor-core kernel holds a whole
     score row of at most 128 keys in registers); both paths meet the same bound."""
-    from agxforge_b200.inference.encoder import Encoder
+    from agxforge.inference.encoder import Encoder
     cfg = dict(E.MINILM_L6, num_hidden_layers=2)
     e = Encoder(cfg, max_batch=4, max_seq=200).load(E.make_params(7, cfg))
     ids, mask = _workload(seed=8, B=4, S=200)
@@ -164,7 +164,7 @@ def test_long_sequences_fp32_attention_path(torch):
 def test_large_batch_fused_layernorm_epilogue(torch):
     """Enough token rows for one full wave of 128-row tiles: o_proj and FFN down carry the LayerNorm in their
     epilogue (5 launches a layer instead of 7), within the same bound."""
-    from agxforge_b200.inference.encoder import Encoder
+    from agxforge.inference.encoder import Encoder
     cfg = dict(E.MINILM_L6, num_hidden_layers=2)
     B, S = 152, 128                                   # 19,456 rows = 152 tiles >= 148 SMs
     e = Encoder(cfg, max_batch=B, max_seq=S).load(E.make_params(9, cfg))

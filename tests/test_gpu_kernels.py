@@ -38,22 +38,24 @@ def ulp16(v):
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("sdt", ["fp16", "bf16"])
 def test_quantize_bit_exact(torch, bits, sdt):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(100 + bits)
     W = _w(rng, 96, 512)
     W[1, :64] = 0.25                                   # constant group
     W[2, 64:128] *= 40                                 # wide group
-    packed, s16, b16 = Q.quantize(W, bits=bits, scale_dtype=sdt)
+    packed, s16, b16, q = Q.quantize(W, bits=bits, scale_dtype=sdt)
     rp, rs, rb, rq = P.quantize(W, bits=bits, scale_dtype=sdt)
     assert np.array_equal(s16, rs)
     assert np.array_equal(b16, rb)
     assert np.array_equal(packed, rp)
+    assert q.dtype == np.uint32 and np.array_equal(q, rq.astype(np.uint32))
 
 
 @pytest.mark.parametrize("bits", [4, 8])
 def test_quantize_matches_reference_golden(torch, golden, bits):
-    from agxforge_b200.kernels import qmv as Q
-    packed, s16, b16 = Q.quantize(golden["quant%d_W" % bits], bits=bits, scale_dtype="bf16")
+    from agxforge.kernels import qmv as Q
+    packed, s16, b16, q = Q.quantize(golden["quant%d_W" % bits], bits=bits)   # bf16, the reference's default
+    assert np.array_equal(q, golden["quant%d_q" % bits].astype(np.uint32))
     assert np.array_equal(packed, golden["quant%d_packed" % bits])
     assert np.array_equal(s16, golden["quant%d_s16" % bits])
     assert np.array_equal(b16, golden["quant%d_b16" % bits])
@@ -62,7 +64,7 @@ def test_quantize_matches_reference_golden(torch, golden, bits):
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("sdt", ["fp16", "bf16"])
 def test_unpack_dequant_bit_exact(torch, bits, sdt):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(7)
     W = _w(rng, 48, 320)
     rp, rs, rb, rq = P.quantize(W, bits=bits, scale_dtype=sdt)
@@ -73,7 +75,7 @@ def test_unpack_dequant_bit_exact(torch, bits, sdt):
 
 
 def test_gateup_pack_layout_bit_exact(torch):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(8)
     Wg, Wu = _w(rng, 64, 256), _w(rng, 64, 256)
     g = P.quantize(Wg, 4, scale_dtype="fp16")
@@ -84,7 +86,7 @@ def test_gateup_pack_layout_bit_exact(torch):
 
 
 def _gemv_case(torch, bits, N_, K, nb, sdt="fp16", seed=0):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(seed)
     W = _w(rng, N_, K)
     rp, rs, rb, rq = P.quantize(W, bits=bits, scale_dtype=sdt)
@@ -98,7 +100,7 @@ def _gemv_case(torch, bits, N_, K, nb, sdt="fp16", seed=0):
 @pytest.mark.parametrize("shape", [(16, 64), (64, 1024), (4096, 2048), (2048, 8192), (1152, 896), (896, 4864)])
 @pytest.mark.parametrize("nb", [1, 3, 8])
 def test_gemv_f32(torch, bits, shape, nb):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     N_, K = shape
     pk, x16, W64 = _gemv_case(torch, bits, N_, K, nb, seed=N_ + K + nb)
     y = Q.qmv(pk, torch.from_numpy(x16).cuda()).cpu().numpy().astype(np.float64)
@@ -111,7 +113,7 @@ def test_gemv_f32(torch, bits, shape, nb):
 
 @pytest.mark.parametrize("splits", [1, 2, 4, 8, 32])
 def test_gemv_splits_agree(torch, splits):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     pk, x16, W64 = _gemv_case(torch, 4, 256, 2048, 2, seed=3)
     y = Q.qmv(pk, torch.from_numpy(x16).cuda(), splits=splits).cpu().numpy().astype(np.float64)
     ref = x16.astype(np.float64) @ W64.T
@@ -120,7 +122,7 @@ def test_gemv_splits_agree(torch, splits):
 
 
 def test_gemv_bf16_scales(torch):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     pk, x16, W64 = _gemv_case(torch, 4, 512, 1024, 1, sdt="bf16", seed=5)
     y = Q.qmv(pk, torch.from_numpy(x16).cuda()).cpu().numpy().astype(np.float64)
     ref = x16.astype(np.float64) @ W64.T
@@ -129,7 +131,7 @@ def test_gemv_bf16_scales(torch):
 
 def test_gemv_matches_reference_kernel_golden(torch, golden):
     """The reference's own qmv2_ksplit_reference values (bf16 packs, fp16-valued x) within fp32 rounding."""
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     for bits in (4, 8):
         rp, rs, rb = golden["qmv%d_packed" % bits], golden["qmv%d_s16" % bits], golden["qmv%d_b16" % bits]
         N_, K = rp.shape[0], rp.shape[1] * 32 // bits
@@ -143,7 +145,7 @@ def test_gemv_matches_reference_kernel_golden(torch, golden):
 
 @pytest.mark.parametrize("x_f32", [False, True])
 def test_gemv_norm_prologue(torch, x_f32):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(11)
     N_, K, nb = 1024, 2048, 2
     pk, _, W64 = _gemv_case(torch, 4, N_, K, nb, seed=11)
@@ -160,7 +162,7 @@ def test_gemv_norm_prologue(torch, x_f32):
 
 
 def test_residual_epilogues(torch):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(12)
     pk, x16, W64 = _gemv_case(torch, 4, 512, 1024, 2, seed=12)
     ref = x16.astype(np.float64) @ W64.T
@@ -177,7 +179,7 @@ def test_residual_epilogues(torch):
 
 
 def test_swiglu_epilogue(torch):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(13)
     F, K, nb = 512, 1024, 3
     Wg, Wu = _w(rng, F, K), _w(rng, F, K)
@@ -198,7 +200,7 @@ def test_swiglu_epilogue(torch):
 
 
 def test_rmsnorm_standalone(torch):
-    from agxforge_b200.kernels import norm
+    from agxforge.kernels import norm
     rng = np.random.default_rng(14)
     v = (rng.standard_normal((3, 2048)) * 2).astype(np.float32)
     g = (1 + 0.1 * rng.standard_normal(2048)).astype(np.float16)
@@ -210,7 +212,7 @@ def test_rmsnorm_standalone(torch):
 @pytest.mark.parametrize("H,KVH,hd", [(16, 8, 128), (14, 2, 64), (32, 8, 128), (4, 4, 64)])
 @pytest.mark.parametrize("q0", [0, 5, 196, 1791])
 def test_attention(torch, H, KVH, hd, q0):
-    from agxforge_b200.kernels import attention as A
+    from agxforge.kernels import attention as A
     rng = np.random.default_rng(300 + q0)
     cap = 2048
     nb = 2
@@ -226,11 +228,13 @@ def test_attention(torch, H, KVH, hd, q0):
     assert np.all(np.isfinite(out))
     for b in range(nb):
         ref = D.attention_step(q16[b].astype(np.float64), K[b], V[b], int(q0s[b]) + 1, KVH)
-        assert np.all(np.abs(out[b] - ref) <= 2 * ulp16(ref) + 2e-3 * np.abs(ref).max())
+        # the reference's row-scaled enclosure of the true base-2 softmax (tools/g17deliver.py:793)
+        rowmax = np.abs(ref).max(axis=1, keepdims=True)
+        assert (np.abs(out[b] - ref) / rowmax).max() <= 8.7e-4
 
 
 def test_attention_splits_agree(torch):
-    from agxforge_b200.kernels import attention as A
+    from agxforge.kernels import attention as A
     rng = np.random.default_rng(9)
     H, KVH, hd, cap, q0 = 16, 8, 128, 1024, 900
     q16 = (rng.standard_normal((1, H, hd)) * 0.25).astype(np.float16)
@@ -240,11 +244,12 @@ def test_attention_splits_agree(torch):
     for S in (1, 2, 4, 8, 16):
         out = A.attention(torch.from_numpy(q16).cuda(), torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(),
                           [q0], splits=S).cpu().numpy().astype(np.float64).reshape(H, hd)
-        assert np.all(np.abs(out - ref) <= 2 * ulp16(ref) + 2e-3 * np.abs(ref).max())
+        rowmax = np.abs(ref).max(axis=1, keepdims=True)
+        assert (np.abs(out - ref) / rowmax).max() <= 8.7e-4
 
 
 def test_bad_shapes_raise(torch):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     with pytest.raises(ValueError):
         Q.Pack(np.zeros((10, 8), np.uint32), np.zeros((10, 1), np.uint16), np.zeros((10, 1), np.uint16), 10, 64)
     rng = np.random.default_rng(1)
@@ -259,7 +264,7 @@ def test_bad_shapes_raise(torch):
 @pytest.mark.parametrize("nb", [1, 3])
 def test_gemv_plan_overrides_agree(torch, rw, cg, st, nb):
     """Every unit shape (row tiles x K lanes), chunk size and ring depth computes the same GEMV."""
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     pk, x16, W64 = _gemv_case(torch, 4, 512, 2048, nb, seed=21)
     y = Q.qmv(pk, torch.from_numpy(x16).cuda(), row_tiles=rw, chunk_groups=cg, stages=st).cpu().numpy()
     ref = x16.astype(np.float64) @ W64.T
@@ -269,7 +274,7 @@ def test_gemv_plan_overrides_agree(torch, rw, cg, st, nb):
 
 @pytest.mark.parametrize("rw", [2, 4, 8])
 def test_swiglu_unit_shapes(torch, rw):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(31)
     F, K = 256, 1024
     g = P.quantize(_w(rng, F, K), 4, scale_dtype="fp16")

@@ -20,10 +20,10 @@ def torch():
 
 
 def _case(torch, bits, N_, K, B, sdt="fp16", seed=0):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(seed)
     W = (rng.standard_normal((N_, K)) * 0.02).astype(np.float32)
-    packed, s16, b16 = Q.quantize(W, bits=bits, scale_dtype=sdt)
+    packed, s16, b16, _ = Q.quantize(W, bits=bits, scale_dtype=sdt)
     pk = Q.Pack(packed, s16, b16, N_, K, bits=bits, scale_dtype=sdt)
     W64 = P.dequant64(P.unpack(packed, bits, N_, K), s16, b16, sdt)
     x16 = rng.standard_normal((B, K)).astype(np.float16)
@@ -41,7 +41,7 @@ def _check(y, x16, W64):
 @pytest.mark.parametrize("bits", [4, 8])
 @pytest.mark.parametrize("B", [32, 64, 128, 256])
 def test_qmm_against_fp64(torch, bits, B):
-    from agxforge_b200.kernels.qmm import qmm
+    from agxforge.kernels.qmm import qmm
     pk, x16, W64 = _case(torch, bits, 256, 1024, B, seed=B + bits)
     y = qmm(pk, torch.from_numpy(x16).cuda(), ksplit=1).cpu().numpy()
     _check(y, x16, W64)
@@ -49,14 +49,14 @@ def test_qmm_against_fp64(torch, bits, B):
 
 @pytest.mark.parametrize("ksplit", [1, 2, 4, 0])
 def test_qmm_k_split(torch, ksplit):
-    from agxforge_b200.kernels.qmm import qmm
+    from agxforge.kernels.qmm import qmm
     pk, x16, W64 = _case(torch, 4, 384, 2048, 48, seed=7)
     y = qmm(pk, torch.from_numpy(x16).cuda(), ksplit=ksplit).cpu().numpy()
     _check(y, x16, W64)
 
 
 def test_qmm_bf16_scales_and_wide_n(torch):
-    from agxforge_b200.kernels.qmm import qmm
+    from agxforge.kernels.qmm import qmm
     pk, x16, W64 = _case(torch, 4, 2048, 512, 32, sdt="bf16", seed=9)
     y = qmm(pk, torch.from_numpy(x16).cuda()).cpu().numpy()
     _check(y, x16, W64)
@@ -65,8 +65,8 @@ def test_qmm_bf16_scales_and_wide_n(torch):
 def test_qmm_agrees_with_gemv_rows(torch):
     """The first 8 activation rows through the CUDA-core GEMV (exact factorised form) and through the tensor-core
     GEMM (fp16 weights) agree within the fp16 weight rounding."""
-    from agxforge_b200.kernels import qmv as Q
-    from agxforge_b200.kernels.qmm import qmm
+    from agxforge.kernels import qmv as Q
+    from agxforge.kernels.qmm import qmm
     pk, x16, W64 = _case(torch, 8, 512, 1024, 32, seed=13)
     x = torch.from_numpy(x16).cuda()
     y_mm = qmm(pk, x).cpu().numpy()[:8].astype(np.float64)
@@ -76,7 +76,7 @@ def test_qmm_agrees_with_gemv_rows(torch):
 
 
 def test_qmm_rejects_bad_shapes(torch):
-    from agxforge_b200.kernels.qmm import qmm
+    from agxforge.kernels.qmm import qmm
     pk, x16, _ = _case(torch, 4, 256, 512, 32, seed=1)
     with pytest.raises(ValueError):
         qmm(pk, torch.zeros((24, 512), dtype=torch.float16, device="cuda"))

@@ -66,8 +66,9 @@ def test_product_fails_loudly_without_library(monkeypatch, tmp_path):
         N.lib()
 
 
-def test_package_never_imports_oracle():
-    pkg = os.path.join(ROOT, "agxforge_b200")
+@pytest.mark.parametrize("package", ["agxforge", "agxforge_b200"])
+def test_package_never_imports_oracle(package):
+    pkg = os.path.join(ROOT, package)
     for dirpath, _, files in os.walk(pkg):
         for f in files:
             if f.endswith((".py", ".cu", ".cuh", ".h")):

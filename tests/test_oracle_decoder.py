@@ -58,7 +58,7 @@ def test_half_policy_close_to_fp64():
 
 def test_cpu_port_matches_oracle():
     from oracle.cpu_decode import CpuDecoder
-    from agxforge_b200.inference.models import Model as MShape
+    from agxforge.inference.models import Model as MShape
     m = tiny_model(2)
     S = m.shape
     shape = MShape("tiny", S.d_model, S.n_layers, S.n_heads, S.n_kv_heads, S.head_dim, S.ffn, S.vocab, S.rope_theta,

@@ -9,8 +9,8 @@ import socket
 import numpy as np
 import pytest
 
-from agxforge_b200.inference import models
-from agxforge_b200.inference import tp as TP
+from agxforge.inference import models
+from agxforge.inference import tp as TP
 from oracle import pack as OP
 
 

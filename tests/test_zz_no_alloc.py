@@ -27,10 +27,10 @@ def torch():
 
 
 def _case(torch, bits, N_, K, nb, seed):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     rng = np.random.default_rng(seed)
     W = (rng.standard_normal((N_, K)) * 0.02).astype(np.float32)
-    packed, s16, b16 = Q.quantize(W, bits=bits)
+    packed, s16, b16, _ = Q.quantize(W, bits=bits, scale_dtype="fp16")
     pk = Q.Pack(packed, s16, b16, N_, K, bits=bits)
     W64 = P.dequant64(P.unpack(packed, bits, N_, K), s16, b16, "fp16")
     x16 = rng.standard_normal((nb, K)).astype(np.float16)
@@ -40,7 +40,7 @@ def _case(torch, bits, N_, K, nb, seed):
 def _noalloc(torch, pk, x, epi="f32", res=None, splits=0):
     """agxc_qmv_noalloc through the C-ABI with the argument block agxc_qmv takes."""
     from agxforge_b200 import _native as N
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     nb, K = x.shape
     nout = pk.N
     dt = torch.float32 if epi in ("f32", "add16") else torch.float16
@@ -58,12 +58,12 @@ def _bound(x16, W64):
 
 @pytest.mark.parametrize("bits,N_,K,nb,splits", [
     (4, 2048, 4096, 4, 4),     # split K asked for
-    (4, 1024, 8192, 8, 0),     # split K chosen by the planner (8 rows of 8,192 fp16 do not fit one CTA's stage)
+    (4, 1024, 8192, 8, 2),     # 8 rows of 8,192 columns, K split in two (an explicit plan, independent of the planner)
     (8, 512, 2048, 2, 8),
     (4, 768, 1024, 1, 1),      # no split: the static block is not touched
 ])
 def test_noalloc_matches_qmv_twice(torch, bits, N_, K, nb, splits):
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     pk, x16, W64 = _case(torch, bits, N_, K, nb, seed=N_ + K + nb + bits)
     x = torch.from_numpy(x16).cuda()
     y_ref = Q.qmv(pk, x, splits=splits)
@@ -78,7 +78,7 @@ def test_noalloc_matches_qmv_twice(torch, bits, N_, K, nb, splits):
 
 def test_noalloc_residual_epilogue_and_interleaving(torch):
     """add32_to16 with split K, interleaved with agxc_qmv calls of another shape on the same stream."""
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     pk, x16, W64 = _case(torch, 4, 1536, 4096, 3, seed=11)
     pk2, x16b, _ = _case(torch, 4, 256, 2048, 2, seed=12)
     x = torch.from_numpy(x16).cuda()
@@ -104,6 +104,6 @@ def test_noalloc_rejects_oversize_plan(torch):
     with pytest.raises(ValueError, match="static scratch"):
         _noalloc(torch, pk, x, splits=16)
     # the same pack with a plan that fits still runs and agrees with agxc_qmv
-    from agxforge_b200.kernels import qmv as Q
+    from agxforge.kernels import qmv as Q
     y = _noalloc(torch, pk, x, splits=4)
     assert torch.equal(y, Q.qmv(pk, x, splits=4))

@@ -32,7 +32,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-    from agxforge_b200.inference import assemble, models
+    from agxforge.inference import assemble, models
     from tests import modelcheck as MC
 
     if args.case == "internlm7b":
