@@ -173,21 +173,41 @@ class DecodeModel:
             N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, C.c_void_p(t.data_ptr()),
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
+    OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused")
+
     def set_option(self, option, value):
-        """Model options: "pdl" (programmatic dependent launch between the step's kernels: 0 off, 1 (default)
-        successor let in after the dependency wait, 2 after the inputs are staged, 3 after the last weight chunk);
-        "trace"
-        (each launch records its CTAs' entry / wait / exit times on the device's global timer; read with trace());
-        "persistent" (batch 1: the whole step as one persistent cooperative kernel; default off); "bulk" (GEMV weights
-        by plain bulk copies instead of TMA tensor boxes); "wait_ms" (tensor parallel: the host's bound on a decode
-        call, past which the communicator is aborted and TimeoutError raised; default 60000); "tp_fused" (tensor
-        parallel: 1 = the o_proj/down GEMMs push their tiles to every rank over NVLink and the sum is fused with the
-        residual, the default where available; 0 = NCCL all-reduce; every rank must set the same value)."""
-        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "persistent": N.OPT_PERSISTENT, "bulk": N.OPT_BULK,
+        """Model options: "fused" (batch 1 on one device: the whole step as one persistent kernel whose layer phases
+        wait only on the counters of the data they read; 1 by default where it fits, 0 = one kernel per projection
+        and attention); "pdl" (the per-kernel path: programmatic dependent launch between the step's kernels: 0 off,
+        1 (default) successor let in after the dependency wait, 2 after the inputs are staged, 3 after the last weight
+        chunk); "trace" (the per-kernel path records each launch's CTA entry / wait / exit times, read with trace();
+        the fused step records per-CTA phase times, read with trace_fused()); "bulk" (per-kernel GEMV weights by
+        plain bulk copies instead of TMA tensor boxes); "wait_ms" (tensor parallel: the host's bound on a decode call,
+        past which the communicator is aborted and TimeoutError raised; default 60000); "tp_fused" (tensor parallel:
+        1 = the o_proj/down GEMMs push their tiles to every rank over NVLink and the sum is fused with the residual,
+        the default where available; 0 = NCCL all-reduce; every rank must set the same value)."""
+        opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "fused": N.OPT_FUSED, "bulk": N.OPT_BULK,
                 "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")
+
+    @property
+    def fused(self):
+        """True when decode steps run as the fused persistent kernel."""
+        return bool(self.plan_info()["fused"]["on"])
+
+    def trace_fused(self):
+        """The fused step's per-CTA marks of the last traced step (ns of the global timer, 0 = not reached): an array
+        [marks, CTAs]; per layer eight marks (qkv dependency met, qkv done, attention dependency met, attention done,
+        o_proj dependency met, o_proj done, FFN dependency met, FFN done), then the head's two."""
+        marks = 8 * self.shape.LAYERS + 2
+        ctas = 256
+        buf = (C.c_uint64 * (marks * ctas))()
+        ph, ct = C.c_int32(), C.c_int32()
+        N.check(N.lib().agxc_model_trace_cta_read(self._h, buf, marks * ctas, C.byref(ph), C.byref(ct)),
+                "trace_cta_read")
+        return np.frombuffer(buf, np.uint64)[: ph.value * ct.value].reshape(ph.value, ct.value).copy()
 
     def trace(self):
         """The launch trace since tracing started or the last call, then reset: one dict per launch of the step (in
@@ -378,4 +398,6 @@ def build(config, device=0, weights=None, keep_packs=False):
         kept["final_gain"] = np.asarray(host(fg), np.float16) if fg is not None else np.ones(S.D_MODEL, np.float16)
     torch.cuda.synchronize()
     m.packs = kept
+    if os.environ.get("AGXC_FUSED") == "0" and m.batch == 1 and m.tp == 1:
+        m.set_option("fused", 0)      # the per-kernel path, for comparison runs
     return m

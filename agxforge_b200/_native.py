@@ -21,7 +21,7 @@ ROLE_QKV, ROLE_WO, ROLE_GATE, ROLE_UP, ROLE_DOWN, ROLE_HEAD = range(6)
 VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
 OPT_PDL = 0
 OPT_TRACE = 1
-OPT_PERSISTENT = 2
+OPT_FUSED = 2
 OPT_BULK = 3
 OPT_WAIT_MS = 4
 OPT_TP_FUSED = 5

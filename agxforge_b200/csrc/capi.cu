@@ -132,6 +132,10 @@ int agxc_init(int device, agxc_ctx** out) {
     agxc_ctx_free(c);
     return rc;
   }
+  if (int rc = fstep_configure(c)) {
+    agxc_ctx_free(c);
+    return rc;
+  }
   *out = c;
   return 0;
 }

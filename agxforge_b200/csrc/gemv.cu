@@ -92,10 +92,18 @@ int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows
 }
 
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z) {
+  return encode_kv_map_box(m, base, hd, cap, Z, kAttnKeys);
+}
+
+int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW) {
+  return make_map(m, base, inner_words, G, RT, CG, RW);
+}
+
+int encode_kv_map_box(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z, int box_keys) {
   if (int rc = encode_fn()) return rc;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(Z)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(hd) * 2 * cap};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kAttnKeys), 1};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_keys), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -124,33 +124,47 @@ struct AttnParams {
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
 
-// ---- the persistent step kernel (step.cu): a batch-1 decode step as one cooperative launch running a program of
-// phases (GEMV with an epilogue, or attention) separated by grid barriers
-enum { kPhaseGemv = 0, kPhaseAttn = 1 };
-struct alignas(16) StepPhase {
-  int kind = kPhaseGemv;
-  int q_epi = 0;                  // GEMV epilogue
-  int RW = 1, CG = 0, nchunks = 0, units = 0;  // GEMV plan: row tiles a unit, groups a chunk, chunks a unit, units
-  int S = 1;                      // attention: key chunks per KV head (one CTA each)
-  QmvParams q;
-  AttnParams a;
-  unsigned long long* cta_trace = nullptr;  // tracing: [CTA][6] stamps (barrier arrival, start, end, 3 inner points)
-};
-struct StepParams {
-  const StepPhase* phases = nullptr;
-  int nphases = 0;
-  unsigned* bar = nullptr;        // [0] barrier arrivals, [1] CTAs that left (zero between launches)
+// ---- the fused step (fstep.cu): a batch-1 decode step as one persistent cooperative kernel, four phases a layer
+// with fine-grained counters between them
+struct FstepArgs {
+  int L = 0, d = 0, H = 0, KVH = 0, hd = 0, F = 0, V = 0, cap = 0, bits = 4, sdt = 0, stages = 0, smax = 1, grid = 0;
+  float eps = 1e-6f;
+  const CUtensorMap* maps = nullptr;  // device: per layer fstep_maps_per_layer(), then the head's 2, then K and V
+  const __half* gains = nullptr;
+  const __half* bias = nullptr;
+  const __half* final_gain = nullptr;
+  const __half* embed = nullptr;
+  __half* kc = nullptr;
+  __half* vc = nullptr;
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+  uint32_t* q0 = nullptr;
+  uint32_t* log = nullptr;
+  int32_t* tok_out = nullptr;
+  uint32_t* force_next = nullptr;
+  __half* x16 = nullptr;
+  float* logits = nullptr;
+  __half* q16 = nullptr;
+  float* apart = nullptr;
+  float* acc = nullptr;
+  unsigned* sync = nullptr;
+  int nctr = 0;
+  float* pairs = nullptr;
   unsigned* err = nullptr;
-  const uint32_t* q0 = nullptr;   // the step's position (batch 1)
-  int cap = 0;
-  int kmax = 0;                   // the widest GEMV input (sizes the activation staging)
-  int ring = 2;                   // shared-memory ring stages
+  unsigned long long* trace = nullptr;
 };
-int step_plan_gemv(StepPhase* P, int N, int K, int bits, int epi, int grid);
-// *ok = 1 when one CTA of the step kernel fits every SM (called once per model, outside stream capture)
-int step_configure(const agxc_ctx* ctx, int bits, int hd, int kmax, int* ok, int* stages);
-int step_launch(const StepParams& sp, int bits, int hd, int grid, cudaStream_t s);
-size_t step_smem(int kmax, int stages);
+int fstep_configure(const agxc_ctx* ctx);
+int fstep_stages(const agxc_ctx* ctx, int d, int G, int hd);
+size_t fstep_smem(int d, int G, int hd, int stages);
+int fstep_launch(const FstepArgs& a, cudaStream_t s);
+int fstep_counters(int L, int KVH);
+int fstep_trace_marks(int L);
+int fstep_maps_per_layer();
+int fstep_tiles_per_stage(int bits);
+// A 3-D TMA map over a pack's tiles [RT row tiles][G groups][inner 32-bit words] with a box of (inner, CG, RW).
+int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW);
+// A TMA map over fp16 KV rows [Z][cap][hd] with boxes of 64 dims x box_keys keys x 1, 128-byte swizzle.
+int encode_kv_map_box(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z, int box_keys);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
 constexpr int kAttnKeys = 128;
 int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);

@@ -61,17 +61,19 @@ struct agxc_model {
   agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
   int attn_S = 1;
   int pdl = 1;
-  // the persistent step kernel (batch 1): its program, grid barrier words, and whether the device runs it
-  int persistent = 0;
   int bulk = 0;                 // GEMV weights by plain bulk copies (AGXC_OPT_BULK)
-  int step_ok = 0;
-  int step_kmax = 0;
-  int step_ring = 0;
-  agxc::StepPhase* step_phases = nullptr;
-  int step_nphases = 0;
-  unsigned* step_bar = nullptr;
+  // the fused step (batch 1, fstep.cu): one persistent kernel a step, when the device and the shape allow it
+  int fused = 1;                // AGXC_OPT_FUSED
+  int fs_ok = 0;                // the shapes and the device fit it
+  int fs_stages = 0;            // ring stages
+  int fs_smax = 1;              // attention splits per KV group at most
+  int fs_nctr = 0;              // counter words of one parity set
+  CUtensorMap* fs_maps = nullptr;  // device: the step's TMA maps
+  unsigned* fs_sync = nullptr;  // [64 + 2 nctr]: [0] the step counter, then both parities' counters
+  float* fs_acc = nullptr;      // [2 parities][2][L][d] the o_proj and down accumulators
+  float* fs_apart = nullptr;    // [KVH][smax][G][hd + 2] attention partials
   unsigned long long* trace = nullptr;  // [launches][12] when tracing (AGXC_OPT_TRACE)
-  unsigned long long* cta_trace = nullptr;  // persistent step, tracing: [phase][CTA][6]
+  unsigned long long* cta_trace = nullptr;  // fused step, tracing: [mark][CTA]
   int trace_n = 0;
   // graph
   cudaGraph_t graph = nullptr;
@@ -174,7 +176,7 @@ __global__ void trace_reset_kernel(unsigned long long* t, int n) {
 }
 
 // The parameters of layer l's five launches (qkv, attention, o_proj, gate/up, down) and of the head: one place for
-// the per-kernel graph and the persistent step kernel.
+// the per-kernel graph.
 void layer_params(agxc_model* m, int l, QmvParams& p, AttnParams& a, QmvParams& q, QmvParams& g, QmvParams& w) {
   const agxc_model_desc& D = m->d;
   const int B = D.batch, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim, d = D.d_model, F = D.ffn;
@@ -218,59 +220,62 @@ void head_params(agxc_model* m, QmvParams& hp) {
   hp.counters = m->counters + 20480; hp.err = m->ctx->err_dev;
 }
 
-// The persistent step's program (batch 1): 5 phases a layer + the head, uploaded to the device once.
-int build_step_program(agxc_model* m) {
+bool fused_active(const agxc_model* m) { return m->d.batch == 1 && m->fused && m->fs_ok; }
+
+int enqueue_step_fused(agxc_model* m, cudaStream_t s) {
   const agxc_model_desc& D = m->d;
-  std::vector<StepPhase> ph;
-  const int grid = m->ctx->num_sms;
-  const int S = std::max(1, grid / D.n_kv_heads);
-  for (int l = 0; l < D.n_layers; ++l) {
-    StepPhase P1, P2, P3, P4, P5;
-    layer_params(m, l, P1.q, P2.a, P3.q, P4.q, P5.q);
+  FstepArgs a;
+  a.L = D.n_layers; a.d = D.d_model; a.H = D.n_heads; a.KVH = D.n_kv_heads; a.hd = D.head_dim; a.F = D.ffn;
+  a.V = D.vocab; a.cap = D.cap; a.bits = D.bits; a.sdt = D.scale_dtype; a.stages = m->fs_stages; a.smax = m->fs_smax;
+  a.grid = m->ctx->num_sms; a.eps = D.eps;
+  a.maps = m->fs_maps; a.gains = m->gains; a.bias = D.qkv_bias ? m->bias : nullptr; a.final_gain = m->final_gain;
+  a.embed = m->embed; a.kc = m->kcache; a.vc = m->vcache; a.cos_t = m->cos_t; a.sin_t = m->sin_t; a.q0 = m->q0;
+  a.log = m->log; a.tok_out = m->tok; a.force_next = m->force_next; a.x16 = m->x16;
+  a.logits = D.keep_logits ? m->logits : nullptr; a.q16 = m->q16; a.apart = m->fs_apart; a.acc = m->fs_acc;
+  a.sync = m->fs_sync; a.nctr = m->fs_nctr; a.pairs = m->pairs; a.err = m->ctx->err_dev; a.trace = m->cta_trace;
+  m->launches = 1;
+  return fstep_launch(a, s);
+}
+
+// The fused step's TMA maps: per layer the qkv, o_proj, gate/up and down packs (weights and scale/bias), then the
+// head, then the K and V caches. Box shapes: row tiles x gchunk groups (qkv, gate/up, head); one row tile x the
+// group's K range (o_proj); dn_rows row tiles x one group (down); 64 dims x the stage's keys (caches).
+int build_fused_maps(agxc_model* m) {
+  const agxc_model_desc& D = m->d;
+  const int L = D.n_layers, d = D.d_model, hd = D.head_dim, G = D.n_heads / D.n_kv_heads;
+  const int TW = tile_bytes(D.bits) / 4, TPS = fstep_tiles_per_stage(D.bits);
+  const int gd = d / 64, gchunk = std::min(gd, TPS), gk = G * hd / 64, dn_rows = std::min(d / 16, TPS);
+  const int MPL = fstep_maps_per_layer();
+  std::vector<CUtensorMap> maps(static_cast<size_t>(L) * MPL + 4);
+  auto pair = [&](CUtensorMap* mp, const agxc_pack& pk, int cg, int rw) -> int {
+    const int G_ = pk.k / 64, RT = pk.n / 16;
+    if (int rc = encode_pack_map(mp, pk.tiles, TW, G_, RT, cg, rw)) return rc;
+    return encode_pack_map(mp + 1, pk.sb, 16, G_, RT, cg, rw);
+  };
+  for (int l = 0; l < L; ++l) {
+    CUtensorMap* mp = maps.data() + static_cast<size_t>(l) * MPL;
     int rc;
-    if ((rc = step_plan_gemv(&P1, m->qkv_rows, D.d_model, D.bits, EPI_QKV, grid)) ||
-        (rc = step_plan_gemv(&P3, D.d_model, m->attn_dim, D.bits, EPI_RES1, grid)) ||
-        (rc = step_plan_gemv(&P4, 2 * D.ffn, D.d_model, D.bits, EPI_SWIGLU, grid)) ||
-        (rc = step_plan_gemv(&P5, D.d_model, D.ffn, D.bits, EPI_RES2, grid)))
+    if ((rc = pair(mp + 0, m->qkv[l], gchunk, 1)) || (rc = pair(mp + 2, m->wo[l], gk, 1)) ||
+        (rc = pair(mp + 4, m->gu[l], gchunk, 1)) || (rc = pair(mp + 6, m->down[l], 1, dn_rows)))
       return rc;
-    P2.kind = kPhaseAttn;
-    P2.S = S;
-    if (m->cta_trace) {  // per phase, per CTA stamps, in step order
-      const size_t base = ph.size(), w = static_cast<size_t>(grid) * kTraceSlots;
-      P1.cta_trace = m->cta_trace + w * base;
-      P2.cta_trace = m->cta_trace + w * (base + 1);
-      P3.cta_trace = m->cta_trace + w * (base + 2);
-      P4.cta_trace = m->cta_trace + w * (base + 3);
-      P5.cta_trace = m->cta_trace + w * (base + 4);
-    }
-    ph.push_back(P1);
-    ph.push_back(P2);
-    ph.push_back(P3);
-    ph.push_back(P4);
-    ph.push_back(P5);
   }
-  StepPhase Ph;
-  head_params(m, Ph.q);
-  if (int rc = step_plan_gemv(&Ph, D.vocab, D.d_model, D.bits, EPI_ARGMAX, grid)) return rc;
-  if (m->cta_trace) Ph.cta_trace = m->cta_trace + static_cast<size_t>(grid) * kTraceSlots * ph.size();
-  ph.push_back(Ph);
-  AGXC_CUDA(cudaMemcpy(m->step_phases, ph.data(), ph.size() * sizeof(StepPhase), cudaMemcpyHostToDevice));
-  m->step_nphases = static_cast<int>(ph.size());
+  CUtensorMap* mh = maps.data() + static_cast<size_t>(L) * MPL;
+  if (int rc = pair(mh, m->head, gchunk, 1)) return rc;
+  const int kc_keys = 16384 / (4 * hd);
+  const int64_t Z = static_cast<int64_t>(L) * D.n_kv_heads;
+  if (int rc = encode_kv_map_box(mh + 2, m->kcache, hd, D.cap, Z, kc_keys)) return rc;
+  if (int rc = encode_kv_map_box(mh + 3, m->vcache, hd, D.cap, Z, kc_keys)) return rc;
+  AGXC_CUDA(cudaMemcpy(m->fs_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
   return 0;
 }
 
-int enqueue_step_persistent(agxc_model* m, cudaStream_t s) {
-  StepParams sp;
-  sp.phases = m->step_phases;
-  sp.nphases = m->step_nphases;
-  sp.bar = m->step_bar;
-  sp.err = m->ctx->err_dev;
-  sp.q0 = m->q0;
-  sp.cap = m->d.cap;
-  sp.kmax = m->step_kmax;
-  sp.ring = m->step_ring;
-  m->launches = 1;
-  return step_launch(sp, m->d.bits, m->d.head_dim, m->ctx->num_sms, s);
+// Both parities' counters and accumulators and the step counter to zero (at creation, and after a step that gave up).
+int fused_reset(agxc_model* m) {
+  if (!m->fs_ok) return 0;
+  const agxc_model_desc& D = m->d;
+  AGXC_CUDA(cudaMemset(m->fs_sync, 0, (64 + 2 * static_cast<size_t>(m->fs_nctr)) * 4));
+  AGXC_CUDA(cudaMemset(m->fs_acc, 0, static_cast<size_t>(4) * D.n_layers * D.d_model * 4));
+  return 0;
 }
 
 // The batched step (batch >= 32): RMSNorm -> tensor-core GEMM -> per-row kernel for each projection, attention
@@ -402,7 +407,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
 // layer, then head): ev holds 2 * launches events.
 int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
   if (m->d.batch >= 32) return enqueue_step_batched(m, s, ev);
-  if (!ev && m->persistent && m->step_ok) return enqueue_step_persistent(m, s);
+  if (!ev && fused_active(m)) return enqueue_step_fused(m, s);
   const agxc_model_desc& D = m->d;
   int rc;
   m->launches = 0;
@@ -446,10 +451,6 @@ int wait_done(agxc_model* m, cudaEvent_t e) {
 int ensure_graph(agxc_model* m) {
   if (m->exec) return 0;
   cudaStream_t s = m->ctx->stream;
-  if (m->persistent && m->step_ok && !m->step_nphases) {
-    AGXC_CUDA(cudaStreamSynchronize(s));
-    if (int rc = build_step_program(m)) return rc;
-  }
   AGXC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = enqueue_step(m, s);
   cudaGraph_t g = nullptr;
@@ -702,20 +703,27 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
   if ((rc = dalloc_t(m, &m->part, std::max<size_t>(part, 64)))) return bail(rc);
   if ((rc = dalloc_t(m, &m->pairs, static_cast<size_t>(std::max(m->p_head.grid, ctx->num_sms)) * 16)))
     return bail(rc);
-  // the persistent step kernel: batch 1, when its shared memory fits one CTA per SM
-  m->step_kmax = std::max({d, m->attn_dim, F});
-  if (B == 1) {
-    if ((rc = step_configure(ctx, D.bits, hd, m->step_kmax, &m->step_ok, &m->step_ring))) return bail(rc);
-    if (D.n_heads / D.n_kv_heads > 8) m->step_ok = 0;
-  }
-  if (m->step_ok) {
-    if ((rc = dalloc_t(m, &m->apart, static_cast<size_t>(ctx->num_sms) * 8 * (hd + 2)))) return bail(rc);
-    if ((rc = dalloc_t(m, &m->step_bar, 64))) return bail(rc);
-    void* ph = nullptr;
-    if (cudaMalloc(&ph, static_cast<size_t>(5 * L + 1) * sizeof(StepPhase)) != cudaSuccess)
-      return bail(fail(AGXC_ENOMEM, "model: step program"));
-    m->allocs.push_back(ph);
-    m->step_phases = static_cast<StepPhase*>(ph);
+  // the fused step: batch 1 on one device, when a ring of stages fits the shared memory; its maps, counters,
+  // accumulators and attention partials
+  {
+    const int G = D.n_heads / D.n_kv_heads;
+    const int nrc = (d / 64 + fstep_tiles_per_stage(D.bits) - 1) / fstep_tiles_per_stage(D.bits);
+    m->fs_stages = fstep_stages(ctx, d, G, hd);
+    m->fs_ok = B == 1 && T == 1 && d % 64 == 0 && F % 64 == 0 && (G * hd) % 64 == 0 && V % 16 == 0 &&
+               m->fs_stages >= 4 * nrc && (d / 16) % 1 == 0 && G <= 8;
+    if (m->fs_ok) {
+      m->fs_smax = std::max(1, ctx->num_sms / D.n_kv_heads);
+      m->fs_nctr = fstep_counters(L, D.n_kv_heads);
+      void* mp = nullptr;
+      if ((rc = dalloc(m, &mp, (static_cast<size_t>(L) * fstep_maps_per_layer() + 4) * sizeof(CUtensorMap))))
+        return bail(rc);
+      m->fs_maps = static_cast<CUtensorMap*>(mp);
+      if ((rc = dalloc_t(m, &m->fs_sync, 64 + 2 * static_cast<size_t>(m->fs_nctr)))) return bail(rc);
+      if ((rc = dalloc_t(m, &m->fs_acc, static_cast<size_t>(4) * L * d))) return bail(rc);
+      if ((rc = dalloc_t(m, &m->fs_apart, static_cast<size_t>(D.n_kv_heads) * m->fs_smax * G * (hd + 2))))
+        return bail(rc);
+      if ((rc = build_fused_maps(m)) || (rc = fused_reset(m))) return bail(rc);
+    }
   }
   m->counters_n = 24576;
   if (static_cast<size_t>(m->qkv_rows / hd) > 4096 || static_cast<size_t>(B * D.n_kv_heads) > 4096 ||
@@ -723,8 +731,7 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
     return bail(fail(AGXC_EINVAL, "model: too many epilogue blocks for the counter regions"));
   if ((rc = dalloc_t(m, &m->counters, m->counters_n))) return bail(rc);
   cudaStream_t s = ctx->stream;
-  if ((m->step_bar && cudaMemsetAsync(m->step_bar, 0, 64 * sizeof(unsigned), s) != cudaSuccess) ||
-      cudaMemsetAsync(m->counters, 0, m->counters_n * sizeof(unsigned), s) != cudaSuccess ||
+  if (cudaMemsetAsync(m->counters, 0, m->counters_n * sizeof(unsigned), s) != cudaSuccess ||
       cudaMemsetAsync(m->kcache, 0, kv * 2, s) != cudaSuccess || cudaMemsetAsync(m->vcache, 0, kv * 2, s) != cudaSuccess ||
       cudaMemsetAsync(m->q0, 0, B * 4, s) != cudaSuccess ||
       cudaMemsetAsync(m->force_next, 0xFF, B * 4, s) != cudaSuccess ||
@@ -1019,6 +1026,7 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
   if (err) {
     const uint32_t zero = 0;
     cudaMemcpy(m->ctx->err_dev, &zero, 4, cudaMemcpyHostToDevice);
+    if (fused_active(m)) fused_reset(m);  // a step that gave up leaves its counters part-way
     return fail(err & kErrMbarTimeout ? AGXC_ETIMEOUT : AGXC_ECORRUPT, "prefill: device error word " + std::to_string(err));
   }
   return 0;
@@ -1146,6 +1154,7 @@ int model_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* to
   if (err) {
     const uint32_t zero = 0;
     cudaMemcpy(m->ctx->err_dev, &zero, 4, cudaMemcpyHostToDevice);
+    if (fused_active(m)) fused_reset(m);  // a step that gave up leaves its counters part-way
     if (err & kErrMbarTimeout) return fail(AGXC_ETIMEOUT, "decode: a bounded device wait gave up");
     return fail(AGXC_ECORRUPT, "decode: device error word " + std::to_string(err));
   }
@@ -1313,9 +1322,10 @@ int agxc_model_plan_info(agxc_model* m, char* buf, size_t len) {
   std::string j = "{" + one("qkv", m->p_qkv) + ", " + one("wo", m->p_wo) + ", " + one("ffn", m->p_gu) + ", " +
                   one("down", m->p_down) + ", " + one("head", m->p_head) + ", \"attn\": {\"chunks\": " +
                   std::to_string(m->attn_S) + ", \"max_cluster\": " + std::to_string(m->ctx->max_cluster) +
-                  "}, \"pdl\": " + std::to_string(m->pdl) + ", \"persistent\": {\"on\": " +
-                  std::to_string(m->persistent && m->step_ok) + ", \"fits\": " + std::to_string(m->step_ok) +
-                  ", \"ring_stages\": " + std::to_string(m->step_ring) + ", \"grid\": " +
+                  "}, \"pdl\": " + std::to_string(m->pdl) + ", \"fused\": {\"on\": " +
+                  std::to_string(agxc::fused_active(m)) + ", \"fits\": " + std::to_string(m->fs_ok) +
+                  ", \"ring_stages\": " + std::to_string(m->fs_stages) + ", \"max_splits\": " +
+                  std::to_string(m->fs_smax) + ", \"grid\": " +
                   std::to_string(m->ctx->num_sms) + "}, \"tp\": {\"world\": " + std::to_string(m->tp) +
                   ", \"rank\": " + std::to_string(m->tp_rank) + ", \"heads\": " + std::to_string(m->d.n_heads) +
                   ", \"kv_heads\": " + std::to_string(m->d.n_kv_heads) + ", \"ffn\": " +
@@ -1343,11 +1353,12 @@ int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n
 
 int agxc_model_trace_cta_read(agxc_model* m, uint64_t* out, size_t capacity, int32_t* phases, int32_t* ctas) {
   if (!m || !out || !phases || !ctas) return agxc::fail(AGXC_EINVAL, "trace_cta_read: null argument");
-  if (!m->cta_trace) return agxc::fail(AGXC_EINVAL, "trace_cta_read: no persistent-step trace (AGXC_OPT_TRACE)");
-  const size_t w = static_cast<size_t>(m->trace_n) * m->ctx->num_sms * agxc::kTraceSlots;
+  if (!m->cta_trace) return agxc::fail(AGXC_EINVAL, "trace_cta_read: no fused-step trace (AGXC_OPT_TRACE)");
+  const int marks = agxc::fstep_trace_marks(m->d.n_layers);
+  const size_t w = static_cast<size_t>(marks) * m->ctx->num_sms;
   AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
   AGXC_CUDA(cudaMemcpy(out, m->cta_trace, std::min(capacity, w) * 8, cudaMemcpyDeviceToHost));
-  *phases = m->trace_n;
+  *phases = marks;
   *ctas = m->ctx->num_sms;
   return 0;
 }
@@ -1373,8 +1384,11 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
     if (value < 1) return agxc::fail(AGXC_EINVAL, "set_option: wait_ms must be positive");
     m->wait_ms = value;
     return 0;  // no graph change
-  } else if (option == AGXC_OPT_PERSISTENT) {
-    m->persistent = value ? 1 : 0;
+  } else if (option == AGXC_OPT_FUSED) {
+    if (value && !m->fs_ok)
+      return agxc::fail(AGXC_EUNSUPPORTED, "set_option: this model has no fused step (batch 1 on one device, and the "
+                                           "ring must fit the shared memory)");
+    m->fused = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {
     if (value && !m->trace) {
       const int n = 2 * agxc::kTraceSlots * (5 * m->d.n_layers + 1);
@@ -1385,8 +1399,8 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
       }
       m->trace = static_cast<unsigned long long*>(t);
       m->trace_n = n / (2 * agxc::kTraceSlots);
-      if (m->step_ok) {
-        const size_t cw = static_cast<size_t>(m->trace_n) * m->ctx->num_sms * agxc::kTraceSlots;
+      if (m->fs_ok) {
+        const size_t cw = static_cast<size_t>(agxc::fstep_trace_marks(m->d.n_layers)) * m->ctx->num_sms;
         if (cudaMalloc(&t, cw * 8) != cudaSuccess) {
           cudaGetLastError();
           return agxc::fail(AGXC_ENOMEM, "set_option: trace buffer");
@@ -1415,7 +1429,6 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
     cudaGraphDestroy(m->graph);
     m->graph = nullptr;
   }
-  m->step_nphases = 0;  // the step program is rebuilt with the new options
   return 0;
 }
 

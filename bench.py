@@ -220,7 +220,7 @@ def trace_step(args):
     if batch != 1:
         raise SystemExit("--trace-step: batch-1 configs only")
     m = assemble.build(dict(model=model, bits=bits, batch=1, cap=hist + 16, seed=2))
-    m.set_option("persistent", 0)
+    m.set_option("fused", 0)
     m.start(0, [1])
     m.fill_history(0, hist - args.warmup, seed=1792)
     m.decode(args.warmup, want_tokens=False)
@@ -651,6 +651,27 @@ def main():
         prefill = dict(tokens=hist - 1, gpu_ms=round(pt["gpu_ms"], 3),
                        tok_s=round((hist - 1) / (pt["gpu_ms"] / 1e3), 1), launches=pt["launches"])
 
+    # the dominant kernel: the fused step when it runs (the step's only launch; its device time is the timed
+    # replays'), else the per-kernel path's largest share
+    fused = batch == 1 and tp == 1 and m.fused
+    if fused:
+        us = gpu_ms / K * 1e3
+        ftraffic = None
+        for ln in (open(tpath) if os.path.exists(tpath) else []):
+            if ln.startswith("traffic %s fused " % args.config):
+                try:
+                    ftraffic = int(ln.split()[3])
+                except (IndexError, ValueError):
+                    ftraffic = None
+        roofline = dict(bound="hbm", kernel="fused_step", achieved=round(step_gbs, 1), peak=peak, unit="GB/s",
+                        frac=round(step_gbs / peak, 4), traffic=ftraffic, peak_source=peak_kind,
+                        bytes_per_launch=int(step_bytes), us_per_launch=round(us, 3),
+                        timing="CUDA events on the library's stream around the K timed steps (one launch a step)")
+    else:
+        roofline = dict(bound="hbm", kernel=dname, achieved=round(achieved, 1), peak=peak, unit="GB/s",
+                        frac=round(achieved / peak, 4), traffic=traffic, peak_source=peak_kind,
+                        bytes_per_launch=kind_bytes[dname], us_per_launch=round(per_launch_ms * 1e3, 3))
+
     cpu = None
     if keep:
         per_token, cores = cpu_baseline_sample(m, args.cpu_tokens, hist)
@@ -672,13 +693,12 @@ def main():
             e2e=dict(value=round(e2e_tok_s, 2), unit="tok/s", h2d_bytes_per_step=4 * batch,
                      d2h_bytes_per_step=4 * batch, loop="one step queued ahead (sync_each 2)",
                      lockstep=round(lock_tok_s, 2)),
-            roofline=dict(bound="hbm", kernel=dname, achieved=round(achieved, 1), peak=peak, unit="GB/s",
-                          frac=round(achieved / peak, 4), traffic=traffic, peak_source=peak_kind,
-                          bytes_per_launch=kind_bytes[dname], us_per_launch=round(per_launch_ms * 1e3, 3)),
+            roofline=roofline,
             step_roofline=dict(bound="hbm", achieved=round(step_gbs, 1), peak=peak, unit="GB/s",
                                frac=round(step_gbs / peak, 4), bytes_per_token=int(step_bytes / batch),
                                weight_bytes=w_bytes, peak_source=peak_kind),
-            kernels=kinds,
+            kernels=kinds if not fused else None,
+            graph_path_kernels=kinds if fused else None,
             prefill=prefill,
             plans=m.plan_info(),
             cpu_baseline=cpu,

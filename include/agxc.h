@@ -272,11 +272,12 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_TRACE 1      /* 1: every launch of the step records, over its CTAs, the first and last %globaltimer
                                  (ns) at CTA entry, after the dependency wait, and at CTA exit (read with
                                  agxc_model_trace_read); 0 (default): off */
-#define AGXC_OPT_PERSISTENT 2 /* 1: a batch-1 model runs each step as ONE persistent cooperative kernel (one CTA per
-                                 SM streams every weight of the step through its shared-memory ring while the phases
-                                 run between grid barriers) when the device fits it; 0 (default): one kernel per
-                                 projection and attention, chained by programmatic dependent launch (always the case
-                                 for batch > 1) */
+#define AGXC_OPT_FUSED 2      /* 1 (default where it fits): a batch-1 model on one device runs each step as ONE
+                                 persistent cooperative kernel: one CTA per SM, a producer warp streams every weight
+                                 chunk and KV row the CTA reads through a shared-memory ring while the layer's four
+                                 phases (qkv; attention; merge + o_proj; gate/up + down) wait only on the counters of
+                                 the data they read. 0: one kernel per projection and attention, chained by
+                                 programmatic dependent launch (always the case for batch > 1) */
 #define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
                                  a chunk); 0 (default): by 3-D TMA tensor boxes */
 #define AGXC_OPT_TP_FUSED 5    /* tensor parallel: 1 (default when every rank could map the others' buffers) = the
@@ -297,10 +298,10 @@ AGXC_API int agxc_model_set_option(agxc_model* m, int option, int value);
  * unit's epilogue, and when the first weight chunk had landed. Launches in step order (per layer qkv, attn, wo, ffn,
  * down; then head); *n = launches. */
 AGXC_API int agxc_model_trace_read(agxc_model* m, uint64_t* out, int capacity, int32_t* n);
-/* The persistent step's per-CTA trace of the last traced step: out[phase][CTA][6] global-timer stamps (ns) at the
- * phase's barrier arrival, after the barrier, at the phase's end, and three inner points (GEMV: inputs staged, units
- * done, first chunk landed; attention: queries loaded, units done, keys done), 0 = not reached. *phases, *ctas = the
- * dimensions; at most `capacity` words are written. */
+/* The fused step's per-CTA trace of the last traced step: out[mark][CTA] global-timer stamps (ns); per layer eight
+ * marks (qkv: dependency met, done; attention: dependency met, done; o_proj: dependency met, done; FFN: dependency
+ * met, done), then the head's two (dependency met, done); 0 = not reached (a CTA with no work in that phase).
+ * *phases = marks, *ctas = CTAs; at most `capacity` words are written. */
 AGXC_API int agxc_model_trace_cta_read(agxc_model* m, uint64_t* out, size_t capacity, int32_t* phases, int32_t* ctas);
 
 /* The model's launch plans as a JSON object (per kernel: row tiles per unit, K splits, groups per unit and chunk,
