@@ -275,6 +275,23 @@ class DecodeModel:
         N.check(N.lib().agxc_model_state(self._h, b, q0.ctypes.data_as(C.c_void_p), log.ctypes.data_as(C.c_void_p)))
         return int(q0[0]), log
 
+    def save_state(self, b=0):
+        """Sequence b's decode state as bytes: q0, the token log, a pending forced token, the next input row and every
+        layer's K/V rows 0 .. q0-1 (agxc_model_state_save's image)."""
+        n = int(N.lib().agxc_model_state_bytes(self._h, b))
+        if n < 0:
+            N.check(n, "state_bytes")
+        buf = C.create_string_buffer(n)
+        w = C.c_size_t()
+        N.check(N.lib().agxc_model_state_save(self._h, b, buf, n, C.byref(w)), "state_save")
+        return buf.raw[: w.value]
+
+    def restore_state(self, image, b=0):
+        """Replace sequence b's decode state with a save_state() image (same shapes; the cap must hold it)."""
+        data = bytes(image)
+        buf = C.create_string_buffer(data, len(data))
+        N.check(N.lib().agxc_model_state_restore(self._h, b, buf, len(data)), "state_restore")
+
     def read_kv(self, layer, b, n):
         S = self.shape
         k = np.zeros((S.KV_HEADS, n, S.HEAD_DIM), np.uint16)

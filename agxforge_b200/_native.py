@@ -104,6 +104,9 @@ SIGNATURES = {
     "agxc_decode": (_I, [_P, _I, _P, _P, _P, _I, C.POINTER(Timing)]),
     "agxc_model_state": (_I, [_P, _I, _P, _P]),
     "agxc_model_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
+    "agxc_model_state_bytes": (C.c_int64, [_P, _I]),
+    "agxc_model_state_save": (_I, [_P, _I, _P, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "agxc_model_state_restore": (_I, [_P, _I, _P, C.c_size_t]),
     "agxc_model_logits_dev": (_I, [_P, C.POINTER(_P)]),
     "agxc_model_profile": (_I, [_P, _I, _P, _P]),
     "agxc_model_set_option": (_I, [_P, _I, _I]),

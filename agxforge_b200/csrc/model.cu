@@ -862,7 +862,7 @@ int model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
     AGXC_CUDA(cudaMemsetAsync(m->kcache + off, 0, seq_kv * 2, s));
     AGXC_CUDA(cudaMemsetAsync(m->vcache + off, 0, seq_kv * 2, s));
   }
-  std::vector<uint32_t> log(D.cap, kTokenUnset);
+  std::vector<uint32_t> log(D.cap, agxc::kTokenUnset);
   for (int i = 0; i < n; ++i) log[i] = static_cast<uint32_t>(prompt[i]);
   AGXC_CUDA(cudaMemcpyAsync(m->log + static_cast<size_t>(b) * D.cap, log.data(), D.cap * 4, cudaMemcpyHostToDevice, s));
   const uint32_t zero = 0;
@@ -1073,7 +1073,7 @@ int model_fill_history(agxc_model* m, int b, int n, uint64_t seed) {
     }
   AGXC_CUDA(cudaGetLastError());
   std::mt19937_64 rng(seed);
-  std::vector<uint32_t> log(D.cap, kTokenUnset);
+  std::vector<uint32_t> log(D.cap, agxc::kTokenUnset);
   for (int i = 0; i <= n; ++i) log[i] = static_cast<uint32_t>(rng() % static_cast<uint64_t>(m->vt));
   AGXC_CUDA(cudaMemcpyAsync(m->log + static_cast<size_t>(b) * D.cap, log.data(), D.cap * 4, cudaMemcpyHostToDevice, s));
   const uint32_t q0 = static_cast<uint32_t>(n);
@@ -1275,6 +1275,124 @@ int agxc_model_state(agxc_model* m, int b, uint32_t* q0, uint32_t* log) {
   if (!m || b < 0 || b >= m->d.batch) return agxc::fail(AGXC_EINVAL, "state: bad argument");
   if (q0) AGXC_CUDA(cudaMemcpy(q0, m->q0 + b, 4, cudaMemcpyDeviceToHost));
   if (log) AGXC_CUDA(cudaMemcpy(log, m->log + static_cast<size_t>(b) * m->d.cap, m->d.cap * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+namespace {
+
+struct StateHeader {            // 64 bytes, little-endian
+  char magic[4];                // "AGXS"
+  uint32_t version;             // 1
+  uint32_t layers, kv_heads, head_dim, d_model, vocab, cap;
+  uint32_t q0;                  // the next step's position; K/V rows 0 .. q0-1 follow
+  uint32_t force_next;          // a pending forced token (0xFFFFFFFF = none)
+  uint32_t reserved[6];
+};
+static_assert(sizeof(StateHeader) == 64, "the state header is 64 bytes");
+
+size_t state_bytes(const agxc_model* m, uint32_t q0) {
+  const agxc_model_desc& D = m->d;
+  return sizeof(StateHeader) + static_cast<size_t>(D.cap) * 4 + static_cast<size_t>(D.d_model) * 2 +
+         2 * static_cast<size_t>(D.n_layers) * D.n_kv_heads * q0 * D.head_dim * 2;
+}
+
+// (layer, KV head) row block of sequence b in the cache [L][B][KVH][cap][hd]
+size_t kv_off(const agxc_model* m, int l, int b, int kv) {
+  const agxc_model_desc& D = m->d;
+  return ((static_cast<size_t>(l) * D.batch + b) * D.n_kv_heads + kv) * D.cap * D.head_dim;
+}
+
+}  // namespace
+
+int64_t agxc_model_state_bytes(agxc_model* m, int b) {
+  if (!m || b < 0 || b >= m->d.batch) return agxc::fail(AGXC_EINVAL, "state_bytes: bad argument");
+  uint32_t q0 = 0;
+  AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  AGXC_CUDA(cudaMemcpy(&q0, m->q0 + b, 4, cudaMemcpyDeviceToHost));
+  return static_cast<int64_t>(state_bytes(m, q0));
+}
+
+int agxc_model_state_save(agxc_model* m, int b, void* out, size_t capacity, size_t* written) {
+  if (!m || !out || b < 0 || b >= m->d.batch) return agxc::fail(AGXC_EINVAL, "state_save: bad argument");
+  if (m->tp > 1) return agxc::fail(AGXC_EUNSUPPORTED, "state_save: a single-device model");
+  const agxc_model_desc& D = m->d;
+  AGXC_CUDA(cudaStreamSynchronize(m->ctx->stream));
+  StateHeader h{};
+  std::memcpy(h.magic, "AGXS", 4);
+  h.version = 1;
+  h.layers = D.n_layers; h.kv_heads = D.n_kv_heads; h.head_dim = D.head_dim; h.d_model = D.d_model;
+  h.vocab = m->vt; h.cap = D.cap;
+  AGXC_CUDA(cudaMemcpy(&h.q0, m->q0 + b, 4, cudaMemcpyDeviceToHost));
+  AGXC_CUDA(cudaMemcpy(&h.force_next, m->force_next + b, 4, cudaMemcpyDeviceToHost));
+  const size_t need = state_bytes(m, h.q0);
+  if (capacity < need) return agxc::fail(AGXC_EINVAL, "state_save: the buffer holds " + std::to_string(capacity) +
+                                                          " bytes, the state needs " + std::to_string(need));
+  uint8_t* o = static_cast<uint8_t*>(out);
+  std::memcpy(o, &h, sizeof h);
+  o += sizeof h;
+  AGXC_CUDA(cudaMemcpy(o, m->log + static_cast<size_t>(b) * D.cap, static_cast<size_t>(D.cap) * 4,
+                       cudaMemcpyDeviceToHost));
+  o += static_cast<size_t>(D.cap) * 4;
+  AGXC_CUDA(cudaMemcpy(o, m->x16 + static_cast<size_t>(b) * D.d_model, static_cast<size_t>(D.d_model) * 2,
+                       cudaMemcpyDeviceToHost));
+  o += static_cast<size_t>(D.d_model) * 2;
+  const size_t rows = static_cast<size_t>(h.q0) * D.head_dim * 2;
+  for (int which = 0; which < 2; ++which)
+    for (int l = 0; l < D.n_layers; ++l)
+      for (int kv = 0; kv < D.n_kv_heads; ++kv) {
+        const __half* src = (which ? m->vcache : m->kcache) + kv_off(m, l, b, kv);
+        if (rows) AGXC_CUDA(cudaMemcpy(o, src, rows, cudaMemcpyDeviceToHost));
+        o += rows;
+      }
+  if (written) *written = need;
+  return 0;
+}
+
+int agxc_model_state_restore(agxc_model* m, int b, const void* in, size_t bytes) {
+  if (!m || !in || b < 0 || b >= m->d.batch) return agxc::fail(AGXC_EINVAL, "state_restore: bad argument");
+  if (m->tp > 1) return agxc::fail(AGXC_EUNSUPPORTED, "state_restore: a single-device model");
+  const agxc_model_desc& D = m->d;
+  if (bytes < sizeof(StateHeader)) return agxc::fail(AGXC_EINVAL, "state_restore: shorter than its header");
+  StateHeader h;
+  std::memcpy(&h, in, sizeof h);
+  if (std::memcmp(h.magic, "AGXS", 4) || h.version != 1) return agxc::fail(AGXC_EINVAL, "state_restore: not a state image");
+  if (h.layers != static_cast<uint32_t>(D.n_layers) || h.kv_heads != static_cast<uint32_t>(D.n_kv_heads) ||
+      h.head_dim != static_cast<uint32_t>(D.head_dim) || h.d_model != static_cast<uint32_t>(D.d_model) ||
+      h.vocab != static_cast<uint32_t>(m->vt))
+    return agxc::fail(AGXC_EINVAL, "state_restore: the image's shapes differ from the model's");
+  if (h.q0 + 1 > static_cast<uint32_t>(D.cap)) return agxc::fail(AGXC_EINVAL, "state_restore: q0 beyond the cap");
+  if (h.force_next != agxc::kTokenUnset && h.force_next >= h.vocab)
+    return agxc::fail(AGXC_EINVAL, "state_restore: forced token out of range");
+  const size_t saved_cap = h.cap;
+  const size_t need = sizeof h + saved_cap * 4 + static_cast<size_t>(D.d_model) * 2 +
+                      2 * static_cast<size_t>(D.n_layers) * D.n_kv_heads * h.q0 * D.head_dim * 2;
+  if (bytes != need) return agxc::fail(AGXC_EINVAL, "state_restore: the image's size disagrees with its header");
+  const uint8_t* p = static_cast<const uint8_t*>(in) + sizeof h;
+  std::vector<uint32_t> log(D.cap, agxc::kTokenUnset);
+  const uint32_t* slog = reinterpret_cast<const uint32_t*>(p);
+  for (size_t i = 0; i < saved_cap; ++i) {
+    const uint32_t t = slog[i];
+    if (t != agxc::kTokenUnset && t >= h.vocab) return agxc::fail(AGXC_EINVAL, "state_restore: a logged token is out of range");
+    if (i < static_cast<size_t>(D.cap)) log[i] = t;
+    else if (t != agxc::kTokenUnset) return agxc::fail(AGXC_EINVAL, "state_restore: the log does not fit the cap");
+  }
+  p += saved_cap * 4;
+  cudaStream_t s = m->ctx->stream;
+  AGXC_CUDA(cudaStreamSynchronize(s));
+  AGXC_CUDA(cudaMemcpy(m->log + static_cast<size_t>(b) * D.cap, log.data(), log.size() * 4, cudaMemcpyHostToDevice));
+  AGXC_CUDA(cudaMemcpy(m->x16 + static_cast<size_t>(b) * D.d_model, p, static_cast<size_t>(D.d_model) * 2,
+                       cudaMemcpyHostToDevice));
+  p += static_cast<size_t>(D.d_model) * 2;
+  const size_t rows = static_cast<size_t>(h.q0) * D.head_dim * 2;
+  for (int which = 0; which < 2; ++which)
+    for (int l = 0; l < D.n_layers; ++l)
+      for (int kv = 0; kv < D.n_kv_heads; ++kv) {
+        __half* dst = (which ? m->vcache : m->kcache) + kv_off(m, l, b, kv);
+        if (rows) AGXC_CUDA(cudaMemcpy(dst, p, rows, cudaMemcpyHostToDevice));
+        p += rows;
+      }
+  AGXC_CUDA(cudaMemcpy(m->q0 + b, &h.q0, 4, cudaMemcpyHostToDevice));
+  AGXC_CUDA(cudaMemcpy(m->force_next + b, &h.force_next, 4, cudaMemcpyHostToDevice));
   return 0;
 }
 

@@ -248,6 +248,18 @@ AGXC_API int agxc_decode(agxc_model* m, int steps, const int32_t* forced_in, int
 
 /* Copy the state of sequence b to the host: q0 and the token log (cap entries). */
 AGXC_API int agxc_model_state(agxc_model* m, int b, uint32_t* q0, uint32_t* log);
+
+/* Decode-state save and restore of sequence b (the reference keeps a decode's state in its region R and token log and
+ * forces a shared history by rewriting that log, tools/g17forcehistory.py:32-80; here the whole state moves): everything
+ * the next step reads — q0, the token log, a pending forced token, the next input row x16 [d_model] fp16, and every
+ * layer's K and V rows 0 .. q0-1 (fp16) — as one host byte image: a 64-byte header ("AGXS", version 1, the shapes)
+ * then those arrays. agxc_model_state_bytes gives the image's size now. A restore checks the header against the model
+ * (layers, KV heads, head_dim, d_model, vocab; the cap must hold q0 + 1 positions) and refuses a mismatch with
+ * AGXC_EINVAL; it replaces the sequence's state, so the next decode continues exactly where the saved one would
+ * have. Single device only (AGXC_EUNSUPPORTED under tensor parallelism). */
+AGXC_API int64_t agxc_model_state_bytes(agxc_model* m, int b);
+AGXC_API int agxc_model_state_save(agxc_model* m, int b, void* out, size_t capacity, size_t* written);
+AGXC_API int agxc_model_state_restore(agxc_model* m, int b, const void* in, size_t bytes);
 /* Read back layer `layer`'s K and V cache rows [0, n) of sequence b (fp16 patterns, [kv_heads][n][head_dim] each). */
 AGXC_API int agxc_model_read_kv(agxc_model* m, int layer, int b, int n, uint16_t* k_out, uint16_t* v_out);
 /* Device pointer of the last step's logits [batch][vocab] fp32 (keep_logits) for in-place checks. */
