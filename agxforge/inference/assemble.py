@@ -159,9 +159,11 @@ class DecodeModel:
         N.check(N.lib().agxc_model_set_pack(self._h, layer, ROLE[role], *args, int(on_dev)), "set_pack %s" % role)
 
     def set_vector(self, layer, which, data):
-        """fp16 vector: which in {"attn_gain", "ffn_gain", "qkv_bias", "final_gain", "embed"}."""
+        """fp16 vector: which in {"attn_gain", "ffn_gain", "qkv_bias", "final_gain", "embed", "q_norm", "k_norm"}
+        (the last two: the layer's QK-norm gains [head_dim])."""
         idx = {"attn_gain": N.VEC_ATTN_GAIN, "ffn_gain": N.VEC_FFN_GAIN, "qkv_bias": N.VEC_QKV_BIAS,
-               "final_gain": N.VEC_FINAL_GAIN, "embed": N.VEC_EMBED}[which]
+               "final_gain": N.VEC_FINAL_GAIN, "embed": N.VEC_EMBED, "q_norm": N.VEC_Q_NORM,
+               "k_norm": N.VEC_K_NORM}[which]
         if isinstance(data, np.ndarray):
             a = np.ascontiguousarray(data.astype(np.float16, copy=False))
             N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, a.ctypes.data_as(C.c_void_p), a.nbytes, 0),
@@ -173,7 +175,7 @@ class DecodeModel:
             N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, C.c_void_p(t.data_ptr()),
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
-    OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused")
+    OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused", "qk_norm")
 
     def set_option(self, option, value):
         """Model options: "fused" (batch 1 on one device: the whole step as one persistent kernel whose layer phases
@@ -185,9 +187,11 @@ class DecodeModel:
         plain bulk copies instead of TMA tensor boxes); "wait_ms" (tensor parallel: the host's bound on a decode call,
         past which the communicator is aborted and TimeoutError raised; default 60000); "tp_fused" (tensor parallel:
         1 = the o_proj/down GEMMs push their tiles to every rank over NVLink and the sum is fused with the residual,
-        the default where available; 0 = NCCL all-reduce; every rank must set the same value)."""
+        the default where available; 0 = NCCL all-reduce; every rank must set the same value); "qk_norm" (Qwen3:
+        the per-head RMSNorm of q and k before RoPE, with the "q_norm" / "k_norm" gains; build() sets it for a
+        QK_NORM shape)."""
         opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "fused": N.OPT_FUSED, "bulk": N.OPT_BULK,
-                "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED}
+                "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED, "qk_norm": N.OPT_QK_NORM}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")
@@ -356,6 +360,8 @@ def build(config, device=0, weights=None, keep_packs=False):
     world, rank = cfg["tp"], cfg["tp_rank"]
     tp_id = TP.exchange_id(world, rank) if world > 1 else None
     m = DecodeModel(cfg, device, tp_id=tp_id)
+    if S.QK_NORM:
+        m.set_option("qk_norm", 1)
     bits, sdt, seed = m.bits, cfg["scale_dtype"], cfg["seed"]
     weights = weights or {}
     kept = {} if keep_packs else None
@@ -391,6 +397,15 @@ def build(config, device=0, weights=None, keep_packs=False):
                 m.set_vector(l, vec, v)
             if kept is not None:
                 kept[(l, vec)] = np.asarray(host(v), np.float16) if v is not None else np.ones(S.D_MODEL, np.float16)
+        if S.QK_NORM:
+            for vec in ("q_norm", "k_norm"):
+                v = weights.get((l, vec))
+                if v is None:   # synthetic: 1 + N(0, 0.1^2), so the gains matter
+                    v = (1.0 + 0.1 * torch.randn((S.HEAD_DIM,), generator=_gen(torch, seed, l, vec),
+                                                 device="cuda:%d" % device)).to(torch.float16)
+                m.set_vector(l, vec, v)
+                if kept is not None:
+                    kept[(l, vec)] = np.asarray(host(v), np.float16)
         if S.QKV_BIAS:
             v = weights.get((l, "qkv_bias"))
             if v is None:

@@ -18,13 +18,14 @@ SCALE_FP16, SCALE_BF16 = 0, 1
 TOKEN_UNSET = 0xFFFFFFFF
 EPI_F32, EPI_RES1, EPI_RES2, EPI_SWIGLU = 0, 1, 2, 3
 ROLE_QKV, ROLE_WO, ROLE_GATE, ROLE_UP, ROLE_DOWN, ROLE_HEAD = range(6)
-VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED = range(5)
+VEC_ATTN_GAIN, VEC_FFN_GAIN, VEC_QKV_BIAS, VEC_FINAL_GAIN, VEC_EMBED, VEC_Q_NORM, VEC_K_NORM = range(7)
 OPT_PDL = 0
 OPT_TRACE = 1
 OPT_FUSED = 2
 OPT_BULK = 3
 OPT_WAIT_MS = 4
 OPT_TP_FUSED = 5
+OPT_QK_NORM = 6
 
 
 class PackDesc(C.Structure):

@@ -72,6 +72,57 @@ __global__ void rope_append_kernel(const YRows y, int rows, const __half* __rest
   }
 }
 
+// The same with QK-norm (Qwen3, agxforge/kernels/attention.py:256-265): one CTA per (row, head) and one thread per
+// RoPE pair; q and k heads are RMS-normed over head_dim with the layer's shared gains (qkg[0..hd) for q,
+// qkg[hd..2hd) for k) in fp32, (x r) g, before the rotation; v heads are stored as they are.
+__global__ void rope_append_qknorm_kernel(const YRows y, const __half* __restrict__ bias,
+                                          const __half* __restrict__ qkg, float eps, const float* __restrict__ cos_t,
+                                          const float* __restrict__ sin_t, const uint32_t* __restrict__ q0, int H,
+                                          int KVH, int hd, int cap, float qscale, __half* __restrict__ q16,
+                                          __half* __restrict__ kc, __half* __restrict__ vc, int seq) {
+  const int head = blockIdx.x, b = blockIdx.y, pr = threadIdx.x;  // pr < hd / 2
+  const int half = hd / 2;
+  const int tt = pr / 8, r = pr % 8;
+  const int prow0 = head * hd + tt * 16;
+  const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
+  float y1 = yval(y, b, prow0 + r), y2 = yval(y, b, prow0 + r + 8);
+  if (bias) {
+    y1 += __half2float(bias[head * hd + i1]);
+    y2 += __half2float(bias[head * hd + i2]);
+  }
+  int pos = static_cast<int>(q0[b]);
+  if (pos > cap - 1) pos = cap - 1;
+  const int sq = seq >= 0 ? seq : b;
+  if (head >= H + KVH) {
+    __half* v = vc + ((static_cast<size_t>(sq) * KVH + (head - H - KVH)) * cap + pos) * hd;
+    v[i1] = __float2half_rn(y1);
+    v[i2] = __float2half_rn(y2);
+    return;  // the whole CTA (one head) leaves together
+  }
+  __shared__ float red[4];
+  float ss = warp_sum(fmaf(y1, y1, y2 * y2));
+  if ((pr & 31) == 0) red[pr >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < half / 32; ++w) tot += red[w];
+  const float rn = rsqrtf(tot / static_cast<float>(hd) + eps);
+  const __half* g = qkg + (head < H ? 0 : hd);
+  y1 = (y1 * rn) * __half2float(g[i1]);
+  y2 = (y2 * rn) * __half2float(g[i2]);
+  const float c = cos_t[static_cast<size_t>(pos) * half + i1];
+  const float s = sin_t[static_cast<size_t>(pos) * half + i1];
+  const float o1 = y1 * c - y2 * s, o2 = y2 * c + y1 * s;
+  if (head < H) {
+    __half* q = q16 + (static_cast<size_t>(b) * H + head) * hd;
+    q[i1] = __float2half_rn(o1 * qscale);
+    q[i2] = __float2half_rn(o2 * qscale);
+  } else {
+    __half* k = kc + ((static_cast<size_t>(sq) * KVH + (head - H)) * cap + pos) * hd;
+    k[i1] = __float2half_rn(o1);
+    k[i2] = __float2half_rn(o2);
+  }
+}
+
 __global__ void residual16_kernel(const YRows y, const __half* __restrict__ x16, float* h, int d, int B) {
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
@@ -271,9 +322,14 @@ inline unsigned blocks_for(long long n, int threads) { return static_cast<unsign
 
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
-                       __half* vc, int B, cudaStream_t s, int seq) {
-  rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
-      y, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
+                       __half* vc, int B, cudaStream_t s, int seq, const __half* qkg, float qk_eps) {
+  if (qkg) {
+    rope_append_qknorm_kernel<<<dim3(H + 2 * KVH, B), hd / 2, 0, s>>>(y, bias, qkg, qk_eps, cos_t, sin_t, q0, H, KVH,
+                                                                      hd, cap, qscale, q16, kc, vc, seq);
+  } else {
+    rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
+        y, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
+  }
   AGXC_CUDA(cudaGetLastError());
   return 0;
 }

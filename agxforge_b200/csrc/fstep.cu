@@ -66,7 +66,7 @@ __host__ __device__ inline int tile_b(int bits) { return bits == 4 ? 512 : 1024;
 __host__ __device__ inline int ctr_per_layer(int KVH) { return 2 * KVH + 2; }
 
 struct Layout {
-  int ring, x16k, hk, xs, xsum, xo, xsumo, act, xsuma, red, ov, om, misc, total;
+  int ring, x16k, hk, xs, xsum, xo, xsumo, act, xsuma, red, ov, om, kn, misc, total;
 };
 
 // Shared memory, 1,024-byte aligned base: the ring first (the KV boxes' 128-byte swizzle wants 1,024-byte alignment).
@@ -85,6 +85,7 @@ __host__ __device__ inline Layout smem_layout(int d, int kattn, int stages) {
   L.red = o; o += kConsumerWarps * 16 * 4 * 2;            // per-warp partial rows
   L.ov = o; o += (kattn * 4 + 127) / 128 * 128;           // attention: the CTA's o accumulator [G][hd]
   L.om = o; o += kConsumerWarps * 8 * 2 * 4;              // attention: per-warp (m, l) per head
+  L.kn = o; o += 256;                                     // QK-norm: the group's new k row (fp16, head_dim <= 128)
   L.misc = o; o += 1024;
   L.total = o;
   return L;
@@ -97,6 +98,8 @@ struct Params {
   const CUtensorMap* maps;
   const __half* gains;     // [L][2][d]
   const __half* bias;      // [L][qkv rows] or null
+  const __half* qkg;       // [L][2][hd] QK-norm gains (q, k), or null: no QK-norm
+  float* qkraw;            // [(H + KVH) hd] QK-norm: the qkv phase's q and k rows before the norm and RoPE
   const __half* final_gain;
   const __half* embed;     // [V][d]
   __half* kc;              // [L][KVH][cap][hd]
@@ -522,15 +525,58 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
   const size_t kvbase = (static_cast<size_t>(l) * P.KVH + j) * P.cap * HD;
   float* ov = reinterpret_cast<float*>(C.smem + C.Lo.ov);     // [G][HD] fp32 (the CTA's rescaled o sum)
   float* om = reinterpret_cast<float*>(C.smem + C.Lo.om);     // [warp][8 heads][m, l]
+  __half* qn = reinterpret_cast<__half*>(C.smem + C.Lo.xo);   // QK-norm: the group's q rows [G][HD] (fp16, scaled)
+  __half* kn = reinterpret_cast<__half*>(C.smem + C.Lo.kn);   // and its new k row [HD]
+  if (P.qkg) {
+    // warp g < G: q head j G + g; warp G: k head j. RMS over HD in fp32, (x r) g, rotate-half RoPE at pos, fp16
+    // (q scaled for the base-2 softmax) — the qkv epilogue's rounding points, after the per-head norm
+    if (warp <= G) {
+      const bool isq = warp < G;
+      const int head = isq ? j * G + warp : P.H + j;
+      const float* src = P.qkraw + static_cast<size_t>(head) * HD;
+      const __half* gg = P.qkg + (static_cast<size_t>(l) * 2 + (isq ? 0 : 1)) * HD;
+      constexpr int PER = HD / 64;   // RoPE pairs a lane: (i, i + HD/2) for i = lane, lane + 32 (HD 128)
+      float a[PER], b[PER];
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        a[e] = __ldcg(src + lane + 32 * e);
+        b[e] = __ldcg(src + HD / 2 + lane + 32 * e);
+        ss = fmaf(a[e], a[e], fmaf(b[e], b[e], ss));
+      }
+      ss = warp_sum(ss);
+      const float rn = rsqrtf(ss / static_cast<float>(HD) + P.eps);
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        const int i = lane + 32 * e;
+        const float y1 = (a[e] * rn) * __half2float(gg[i]), y2 = (b[e] * rn) * __half2float(gg[HD / 2 + i]);
+        const float cs = P.cos_t[static_cast<size_t>(pos) * (HD / 2) + i];
+        const float sn = P.sin_t[static_cast<size_t>(pos) * (HD / 2) + i];
+        const float o1 = y1 * cs - y2 * sn, o2 = y2 * cs + y1 * sn;
+        if (isq) {
+          qn[warp * HD + i] = __float2half_rn(o1 * P.qscale);
+          qn[warp * HD + HD / 2 + i] = __float2half_rn(o2 * P.qscale);
+        } else {
+          kn[i] = __float2half_rn(o1);
+          kn[HD / 2 + i] = __float2half_rn(o2);
+        }
+      }
+    }
+    consumer_sync();
+    // the CTA whose keys hold the new row writes it to the cache (later steps read it from there)
+    if (pos >= k0 && pos < k1 && tid < HD / 8)
+      reinterpret_cast<uint4*>(P.kc + kvbase + static_cast<size_t>(pos) * HD)[tid] = reinterpret_cast<const uint4*>(kn)[tid];
+  }
   // Q^T fragments: lane (g8, t4) holds q[head g8][16 ks + 2 t4 + {0, 1, 8, 9}] (pre-scaled fp16)
   uint32_t qb[KS][2];
   {
     const bool live = g8 < G;
     const uint32_t* qrow = reinterpret_cast<const uint32_t*>(P.q16 + static_cast<size_t>(j * G + (live ? g8 : 0)) * HD);
+    const uint32_t* qsm = reinterpret_cast<const uint32_t*>(qn + (live ? g8 : 0) * HD);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
-      qb[ks][0] = live ? __ldcg(qrow + ks * 8 + t4) : 0u;
-      qb[ks][1] = live ? __ldcg(qrow + ks * 8 + 4 + t4) : 0u;
+      qb[ks][0] = !live ? 0u : P.qkg ? qsm[ks * 8 + t4] : __ldcg(qrow + ks * 8 + t4);
+      qb[ks][1] = !live ? 0u : P.qkg ? qsm[ks * 8 + 4 + t4] : __ldcg(qrow + ks * 8 + 4 + t4);
     }
   }
   for (int t = tid; t < G * HD; t += kConsumers) ov[t] = 0.f;
@@ -558,7 +604,9 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
       if (pos >= a && pos < a + n) {
         for (int e = lane; e < 2 * HD / 8; e += 32) {
           const int kv = e / (HD / 8), cc = e % (HD / 8);
-          const uint4 v = __ldcg(reinterpret_cast<const uint4*>((kv ? P.vc : P.kc) + kvbase + static_cast<size_t>(pos) * HD) + cc);
+          const uint4 v = !kv && P.qkg ? reinterpret_cast<const uint4*>(kn)[cc]
+                                       : __ldcg(reinterpret_cast<const uint4*>((kv ? P.vc : P.kc) + kvbase +
+                                                                               static_cast<size_t>(pos) * HD) + cc);
           *reinterpret_cast<uint4*>((kv ? Vs : Ks) + (cc >> 3) * KC * 128 + swz(row0 + pos - a, cc)) = v;
         }
       }
@@ -779,7 +827,11 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           y1 += __half2float(b[head * HD + i1]);
           y2 += __half2float(b[head * HD + i2]);
         }
-        if (head < P.H + P.KVH) {
+        if (head < P.H + P.KVH && P.qkg) {
+          // QK-norm: the head's norm needs all its rows; the attention phase finishes q and k from these
+          P.qkraw[head * HD + i1] = y1;
+          P.qkraw[head * HD + i2] = y2;
+        } else if (head < P.H + P.KVH) {
           const float cs = P.cos_t[static_cast<size_t>(Sc.pos) * half + i1];
           const float sn = P.sin_t[static_cast<size_t>(Sc.pos) * half + i1];
           const float o1 = y1 * cs - y2 * sn, o2 = y2 * cs + y1 * sn;
@@ -1081,6 +1133,7 @@ int fstep_launch(const FstepArgs& a, cudaStream_t s) {
   p.dn_rows = std::min(p.rt_d, fstep::tps(a.bits));
   p.smax = a.smax;
   p.maps = a.maps; p.gains = a.gains; p.bias = a.bias; p.final_gain = a.final_gain; p.embed = a.embed;
+  p.qkg = a.qkg; p.qkraw = a.qkraw;
   p.kc = a.kc; p.vc = a.vc; p.cos_t = a.cos_t; p.sin_t = a.sin_t; p.q0 = a.q0; p.log = a.log; p.tok_out = a.tok_out;
   p.force_next = a.force_next; p.x16 = a.x16; p.logits = a.logits; p.q16 = a.q16; p.apart = a.apart; p.acc = a.acc;
   p.sync = a.sync; p.nctr = a.nctr; p.pairs = a.pairs; p.err = a.err; p.trace = a.trace;

@@ -132,6 +132,8 @@ struct FstepArgs {
   const CUtensorMap* maps = nullptr;  // device: per layer fstep_maps_per_layer(), then the head's 2, then K and V
   const __half* gains = nullptr;
   const __half* bias = nullptr;
+  const __half* qkg = nullptr;        // [L][2][hd] QK-norm gains, or NULL (no QK-norm)
+  float* qkraw = nullptr;             // [(H + KVH) hd] QK-norm scratch
   const __half* final_gain = nullptr;
   const __half* embed = nullptr;
   __half* kc = nullptr;
@@ -184,9 +186,11 @@ struct YRows {
 
 // ---- the per-row steps of the batched decode step (batched.cu)
 // q0: each row's position; seq < 0: row b is sequence b's (batched decode), else every row is sequence seq's (prefill)
+// qkg: the layer's QK-norm gains [q hd | k hd] (NULL = no QK-norm), normed with qk_eps before the rotation
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
-                       __half* vc, int B, cudaStream_t s, int seq = -1);
+                       __half* vc, int B, cudaStream_t s, int seq = -1, const __half* qkg = nullptr,
+                       float qk_eps = 1e-6f);
 // causal attention of M prompt rows at positions p0 .. p0 + M - 1 of cache sequence `seq` (prefill.cu)
 int launch_prefill_attention(const __half* q16, const __half* kc, const __half* vc, int M, int p0, int H, int KVH,
                              int hd, int cap, int seq, __half* out, cudaStream_t s);

@@ -33,6 +33,9 @@ struct agxc_model {
   __half* gains = nullptr;      // [L][2][d]
   __half* bias = nullptr;       // [L][qkv_rows]
   __half* final_gain = nullptr; // [d]
+  __half* qk_gains = nullptr;   // [L][2][hd] QK-norm gains (q, k), 1.0 until set
+  int qk_norm = 0;              // AGXC_OPT_QK_NORM: q and k heads RMS-normed before RoPE (Qwen3)
+  float* qkv_raw = nullptr;     // [B][qkv rows] the per-kernel path's qkv GEMV output under QK-norm
   __half* embed = nullptr;      // [V][d]
   // cache and activations
   __half* kcache = nullptr;     // [L][B][KVH][cap][hd]
@@ -58,7 +61,7 @@ struct agxc_model {
   unsigned* counters = nullptr;
   size_t counters_n = 0;
   // plans
-  agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head;
+  agxc::QmvPlan p_qkv, p_wo, p_gu, p_down, p_head, p_qkv_raw;
   int attn_S = 1;
   int pdl = 1;
   int bulk = 0;                 // GEMV weights by plain bulk copies (AGXC_OPT_BULK)
@@ -222,6 +225,10 @@ void head_params(agxc_model* m, QmvParams& hp) {
 
 bool fused_active(const agxc_model* m) { return m->d.batch == 1 && m->fused && m->fs_ok; }
 
+const __half* qk_gains_of(const agxc_model* m, int l) {
+  return m->qk_norm ? m->qk_gains + static_cast<size_t>(l) * 2 * m->d.head_dim : nullptr;
+}
+
 int enqueue_step_fused(agxc_model* m, cudaStream_t s) {
   const agxc_model_desc& D = m->d;
   FstepArgs a;
@@ -229,6 +236,7 @@ int enqueue_step_fused(agxc_model* m, cudaStream_t s) {
   a.V = D.vocab; a.cap = D.cap; a.bits = D.bits; a.sdt = D.scale_dtype; a.stages = m->fs_stages; a.smax = m->fs_smax;
   a.grid = m->ctx->num_sms; a.eps = D.eps;
   a.maps = m->fs_maps; a.gains = m->gains; a.bias = D.qkv_bias ? m->bias : nullptr; a.final_gain = m->final_gain;
+  a.qkg = m->qk_norm ? m->qk_gains : nullptr; a.qkraw = m->qkv_raw;
   a.embed = m->embed; a.kc = m->kcache; a.vc = m->vcache; a.cos_t = m->cos_t; a.sin_t = m->sin_t; a.q0 = m->q0;
   a.log = m->log; a.tok_out = m->tok; a.force_next = m->force_next; a.x16 = m->x16;
   a.logits = D.keep_logits ? m->logits : nullptr; a.q16 = m->q16; a.apart = m->fs_apart; a.acc = m->fs_acc;
@@ -337,7 +345,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, p.norm_gain, D.eps, m->xn16, s)) ||
         (rc = gemm_r(m->qkv[l], m->xn16, m->qkv_rows)) ||
         (rc = launch_rope_append(yr, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, H, KVH, hd, D.cap, qscale, m->q16,
-                                 p.kcache, p.vcache, B, s)) ||
+                                 p.kcache, p.vcache, B, s, -1, qk_gains_of(m, l), D.eps)) ||
         (rc = close()))
       return rc;
     a.pdl = 0;
@@ -425,7 +433,29 @@ int enqueue_step(agxc_model* m, cudaStream_t s, cudaEvent_t* ev = nullptr) {
     QmvParams p, q, g, w;
     AttnParams a;
     layer_params(m, l, p, a, q, g, w);
-    if ((rc = launch_gemv(p, m->p_qkv, EPI_QKV))) return rc;
+    if (m->qk_norm) {
+      // QK-norm: the qkv GEMV's fp32 rows (physical order), then the per-head norm + RoPE + append kernel; one
+      // "qkv" entry of the launch accounting
+      QmvParams r = p;
+      r.out_f32 = m->qkv_raw;
+      r.out_ld = m->qkv_rows;
+      r.pdl = 0;
+      r.bulk = m->bulk;
+      r.trace = nullptr;
+      YRows yr;
+      yr.y = m->qkv_raw;
+      yr.ld = m->qkv_rows;
+      if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
+      if ((rc = launch_qmv_epi(m->ctx, r, m->p_qkv_raw, EPI_F32, s)) ||
+          (rc = launch_rope_append(yr, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, D.n_heads, D.n_kv_heads,
+                                   D.head_dim, D.cap, p.qscale, m->q16, p.kcache, p.vcache, D.batch, s, -1,
+                                   qk_gains_of(m, l), D.eps)))
+        return rc;
+      if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches + 1], s));
+      ++m->launches;
+    } else if ((rc = launch_gemv(p, m->p_qkv, EPI_QKV))) {
+      return rc;
+    }
     a.pdl = m->pdl;
     a.trace = trace_slot(m);
     if (ev) AGXC_CUDA(cudaEventRecord(ev[2 * m->launches], s));
@@ -663,6 +693,8 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
   if ((rc = dalloc_t(m, &m->gains, static_cast<size_t>(L) * 2 * d))) return bail(rc);
   if ((rc = dalloc_t(m, &m->bias, static_cast<size_t>(L) * m->qkv_rows))) return bail(rc);
   if ((rc = dalloc_t(m, &m->final_gain, d))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->qk_gains, static_cast<size_t>(L) * 2 * hd))) return bail(rc);
+  if ((rc = dalloc_t(m, &m->qkv_raw, static_cast<size_t>(B) * m->qkv_rows))) return bail(rc);
   if ((rc = dalloc_t(m, &m->embed, static_cast<size_t>(m->vt) * d))) return bail(rc);
   const size_t kv = static_cast<size_t>(L) * B * D.n_kv_heads * D.cap * hd;
   if ((rc = dalloc_t(m, &m->kcache, kv))) return bail(rc);
@@ -690,6 +722,7 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
   // plans and scratch
   const int nbg = std::min(B, 8);  // the GEMV plans (batch >= 32 runs the tensor-core GEMM instead)
   m->p_qkv = plan_qmv(ctx, m->qkv_rows, d, D.bits, nbg, EPI_QKV, hd, 0);
+  m->p_qkv_raw = plan_qmv(ctx, m->qkv_rows, d, D.bits, nbg, EPI_F32, hd, 0);
   m->p_wo = plan_qmv(ctx, d, m->attn_dim, D.bits, nbg, EPI_RES1, hd, 0);
   m->p_gu = plan_qmv(ctx, 2 * F, d, D.bits, nbg, EPI_SWIGLU, hd, 0);
   m->p_down = plan_qmv(ctx, d, F, D.bits, nbg, EPI_RES2, hd, 0);
@@ -697,6 +730,7 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
   m->attn_S = attn_splits(ctx, B, D.n_kv_heads, D.cap);
   size_t part = 0;
   part = std::max(part, qmv_part_floats(m->p_qkv, m->qkv_rows, nbg, EPI_QKV));
+  part = std::max(part, qmv_part_floats(m->p_qkv_raw, m->qkv_rows, nbg, EPI_F32));
   part = std::max(part, qmv_part_floats(m->p_wo, d, nbg, EPI_RES1));
   part = std::max(part, qmv_part_floats(m->p_gu, 2 * F, nbg, EPI_SWIGLU));
   part = std::max(part, qmv_part_floats(m->p_down, d, nbg, EPI_RES2));
@@ -741,9 +775,11 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
     return bail(fail(AGXC_ECUDA, "model: initial memset failed"));
   // gains default to 1.0 (fp16 0x3C00)
   {
-    std::vector<uint16_t> ones(std::max<size_t>(static_cast<size_t>(L) * 2 * d, d), 0x3C00);
+    std::vector<uint16_t> ones(std::max({static_cast<size_t>(L) * 2 * d, static_cast<size_t>(d),
+                                         static_cast<size_t>(L) * 2 * hd}), 0x3C00);
     if (cudaMemcpy(m->gains, ones.data(), static_cast<size_t>(L) * 2 * d * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(m->final_gain, ones.data(), static_cast<size_t>(d) * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+        cudaMemcpy(m->final_gain, ones.data(), static_cast<size_t>(d) * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->qk_gains, ones.data(), static_cast<size_t>(L) * 2 * hd * 2, cudaMemcpyHostToDevice) != cudaSuccess)
       return bail(fail(AGXC_ECUDA, "model: gain upload failed"));
   }
   // RoPE tables: angle p * theta^(-2i/hd) in double, cos/sin rounded once to fp32 (assemble.py:665-668)
@@ -834,9 +870,15 @@ int model_set_vector(agxc_model* m, int layer, int which, const void* data, size
     case AGXC_VEC_QKV_BIAS: dst = m->bias + static_cast<size_t>(layer) * m->qkv_rows; want = m->qkv_rows * 2; break;
     case AGXC_VEC_FINAL_GAIN: dst = m->final_gain; want = D.d_model * 2; break;
     case AGXC_VEC_EMBED: dst = m->embed; want = static_cast<size_t>(m->vt) * D.d_model * 2; break;
+    case AGXC_VEC_Q_NORM:
+      dst = m->qk_gains + static_cast<size_t>(layer) * 2 * D.head_dim; want = D.head_dim * 2; break;
+    case AGXC_VEC_K_NORM:
+      dst = m->qk_gains + static_cast<size_t>(layer) * 2 * D.head_dim + D.head_dim; want = D.head_dim * 2; break;
     default: return fail(AGXC_EINVAL, "set_vector: unknown vector");
   }
-  if (which <= AGXC_VEC_QKV_BIAS && (layer < 0 || layer >= D.n_layers)) return fail(AGXC_EINVAL, "set_vector: layer");
+  if ((which <= AGXC_VEC_QKV_BIAS || which == AGXC_VEC_Q_NORM || which == AGXC_VEC_K_NORM) &&
+      (layer < 0 || layer >= D.n_layers))
+    return fail(AGXC_EINVAL, "set_vector: layer");
   if (bytes != want) return fail(AGXC_EINVAL, "set_vector: expected " + std::to_string(want) + " bytes");
   AGXC_CUDA(cudaMemcpy(dst, data, bytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
   return 0;
@@ -993,7 +1035,7 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
       if ((rc = launch_rmsnorm(m->pf_x16, 0, Mp, d, g1, D.eps, m->pf_xn16, s)) ||
           (rc = gemm_rows(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, m->pf_part, s, &yr)) ||
           (rc = launch_rope_append(yr, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd, D.cap, qscale,
-                                   m->pf_q16, kc, vc, Mc, s, b)) ||
+                                   m->pf_q16, kc, vc, Mc, s, b, qk_gains_of(m, l), D.eps)) ||
           (rc = launch_prefill_attention(m->pf_q16, kc, vc, Mc, p0, H, KVH, hd, D.cap, b, m->pf_attn, s)) ||
           (rc = gemm_rows(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
           (rc = launch_residual16(yr, m->pf_x16, m->pf_h, d, Mp, s)) ||
@@ -1507,6 +1549,8 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
       return agxc::fail(AGXC_EUNSUPPORTED, "set_option: this model has no fused step (batch 1 on one device, and the "
                                            "ring must fit the shared memory)");
     m->fused = value ? 1 : 0;
+  } else if (option == AGXC_OPT_QK_NORM) {
+    m->qk_norm = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {
     if (value && !m->trace) {
       const int n = 2 * agxc::kTraceSlots * (5 * m->d.n_layers + 1);

@@ -478,6 +478,66 @@ def kernel_case(args, rank):
                               launches=4)), flush=True)
 
 
+def tp_block(args, rank, world, local, dist):
+    """BASELINE config 5 in the same process as the replica line: the InternLM2.5-7B shape (4-bit), 64 sequences at
+    8,192-token histories, tensor parallel over all `world` ranks (strong scaling: the same work at every N).
+    Device time of K steps (max over ranks), the per-GPU step roofline, the per-layer time of the o_proj and down
+    groups (GEMM + all-reduce, from a per-kind CUDA-event profile) and the all-reduce path that ran."""
+    import ctypes as C
+
+    import torch
+    from agxforge.inference import assemble
+    from agxforge_b200 import _native as N
+    model, bits, batch, hist = CONFIGS["internlm7b-q4-8192-b64-tp"]
+    K = min(args.steps, args.tp_steps)
+    W = 3
+    cap = hist + W + K + 2 * args.profile_steps + 4
+    m = assemble.build(dict(model=model, bits=bits, batch=batch, cap=cap, seed=4, tp=world,
+                            tp_rank=rank if world > 1 else 0), device=local)
+    S = m.shape
+    rng = np.random.default_rng(8192)
+    for b in range(batch):
+        m.start(b, [int(rng.integers(0, S.VOCAB))])
+        m.fill_history(b, hist - W, seed=8192 + b)
+    m.decode(W, want_tokens=False)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    _, _, t = m.decode(K, want_tokens=False)
+    gpu_ms = t["gpu_ms"]
+    if dist is not None:
+        tt = torch.tensor([gpu_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        gpu_ms = float(tt.item())
+    kind_ms = (C.c_float * 6)()
+    kind_n = (C.c_int32 * 6)()
+    N.check(N.lib().agxc_model_profile(m.handle, args.profile_steps, kind_ms, kind_n), "profile")
+    prof = [kind_ms[i] for i in range(6)]
+    if dist is not None:
+        tt = torch.tensor(prof, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        prof = [float(x) for x in tt.tolist()]
+    per_layer_us = {KIND_NAMES[i]: round(1e3 * prof[i] / max(1, kind_n[i]), 2) for i in range(6)}
+    kv = batch * S.LAYERS * (S.KV_HEADS // world) * S.HEAD_DIM * 2 * 2 * (hist + (K - 1) / 2.0 + 1)
+    step_bytes_gpu = m.weight_bytes + kv
+    step_s = gpu_ms / 1e3 / K
+    plans = m.plan_info()["tp"]
+    out = dict(config="internlm7b-q4-8192-b64-tp", model=model, batch=batch, history=hist, tp=world, steps=K,
+               value=round(batch * K / (gpu_ms / 1e3), 1), unit="tok/s", ms_per_step=round(gpu_ms / K, 3),
+               scaling="strong", per_gpu_step_roofline=dict(achieved=round(step_bytes_gpu / step_s / 1e9, 1),
+                                                          bytes_per_step=int(step_bytes_gpu)),
+               per_layer_us=per_layer_us,
+               o_proj_group_us=per_layer_us["wo"], down_group_us=per_layer_us["down"],
+               allreduce=("none (one device)" if world == 1 else
+                          ("fused peer stores, two-shot" if plans["two_shot"] else "fused peer stores, one-shot")
+                          if plans["fused"] else "NCCL all-reduce"))
+    m.close()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -488,6 +548,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=2, help="whole tokens the cpu_baseline leg times")
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--tp-steps", type=int, default=16, help="timed steps of the tensor-parallel block")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel block (config 5)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--tp-allreduce", default="fused", choices=["fused", "nccl"],
                     help="tensor-parallel configs: GEMM + peer-memory all-reduce (fused) or NCCL all-reduce")
@@ -705,8 +767,14 @@ def main():
             clocks=clk.summary(),
             gpu_launches=int(launches * K),
         )
-        print(json.dumps(line), flush=True)
     m.close()
+    torch.cuda.synchronize()
+    if args.config == "internlm-q4-1792" and not args.no_tp:
+        tpb = tp_block(args, rank, world, local, dist)
+        if rank == 0:
+            line["tp"] = tpb
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

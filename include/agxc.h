@@ -200,6 +200,8 @@ AGXC_API int agxc_model_vocab_slice(const agxc_model* m, int32_t* offset, int32_
 #define AGXC_VEC_QKV_BIAS 2   /* fp16 [qkv rows] */
 #define AGXC_VEC_FINAL_GAIN 3 /* fp16 [d], layer ignored */
 #define AGXC_VEC_EMBED 4      /* fp16 [vocab][d], layer ignored */
+#define AGXC_VEC_Q_NORM 5     /* fp16 [head_dim]: the layer's QK-norm gain of q heads (AGXC_OPT_QK_NORM) */
+#define AGXC_VEC_K_NORM 6     /* fp16 [head_dim]: the layer's QK-norm gain of k heads */
 
 AGXC_API int agxc_model_create(agxc_ctx* ctx, const agxc_model_desc* desc, agxc_model** out);
 AGXC_API void agxc_model_free(agxc_model* m);
@@ -299,6 +301,9 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
                                  its rows and a cooperative kernel reduces them and stores them into every rank's
                                  residual stream (two-shot). 2 / 3 force two-shot / one-shot (before the first fused
                                  step only); 0 = NCCL all-reduce. Every rank must set the same value. */
+#define AGXC_OPT_QK_NORM 6     /* 1: QK-norm (Qwen3; attention.py:256-265 with_qknorm): every q and k head of the qkv
+                                 projection is RMS-normed over head_dim with the layer's AGXC_VEC_Q_NORM / _K_NORM gain
+                                 (fp32, (x r) g, the model's eps) before RoPE, on every path; 0 (default): off */
 #define AGXC_OPT_WAIT_MS 4     /* tensor parallel: host bound (ms, default 60000) on a decode call's completion; past it
                                  the communicator is aborted (its kernels end) and the call returns AGXC_ETIMEOUT, so a
                                  rank that died between steps cannot hold the others' GPUs */

@@ -55,6 +55,7 @@ class Shape:
     rope_theta: float = 1e6
     qkv_bias: bool = False
     tied: bool = False
+    qk_norm: bool = False
 
     @property
     def qkv_rows(self):
@@ -100,6 +101,14 @@ def rope(t, cos, sin):
     h = t.shape[-1] // 2
     x1, x2 = t[..., :h], t[..., h:]
     return np.concatenate([x1 * cos - x2 * sin, x2 * cos + x1 * sin], axis=-1)
+
+
+def head_norm(t, g, eps):
+    """QK-norm (Qwen3): RMSNorm of every head's row over head_dim with a gain shared by the heads, before RoPE and
+    without a storage rounding (agxforge/kernels/attention.py:256-265 with_qknorm; tools/g17qwen3.py:216-231)."""
+    t = np.asarray(t, F64)
+    r = 1.0 / np.sqrt(np.mean(t * t, axis=-1, keepdims=True) + eps)
+    return t * r * np.asarray(g, np.float16).astype(F64)
 
 
 def silu(x):
@@ -201,6 +210,8 @@ class Model:
             q = qkv[:, :H * hd].reshape(T, H, hd)
             k = qkv[:, H * hd:(H + KVH) * hd].reshape(T, KVH, hd)
             v = qkv[:, (H + KVH) * hd:].reshape(T, KVH, hd)
+            if S.qk_norm:
+                q, k = head_norm(q, L["qn"], S.eps), head_norm(k, L["kn"], S.eps)
             qr = rope(q, cos[:, None, :], sin[:, None, :]) * qscale
             kr = rope(k, cos[:, None, :], sin[:, None, :])
             if half:
@@ -252,6 +263,8 @@ class Model:
                 q = qkv[:, :H * hd].reshape(T, H, hd)
                 k = qkv[:, H * hd:(H + KVH) * hd].reshape(T, KVH, hd)
                 v = qkv[:, (H + KVH) * hd:].reshape(T, KVH, hd)
+                if S.qk_norm:
+                    q, k = head_norm(q, L["qn"], S.eps), head_norm(k, L["kn"], S.eps)
                 qr = rope(q, cos[:, None, :], sin[:, None, :]) * qscale
                 kr = rope(k, cos[:, None, :], sin[:, None, :])
                 if half:

@@ -24,7 +24,7 @@ def oracle_model(m):
     """The CPU oracle's copy of a DecodeModel built with keep_packs=True."""
     S = m.shape
     shape = D.Shape(S.D_MODEL, S.LAYERS, S.HEADS, S.KV_HEADS, S.HEAD_DIM, S.FFN, S.VOCAB, S.EPS, S.ROPE_THETA,
-                    S.QKV_BIAS, S.TIED)
+                    S.QKV_BIAS, S.TIED, S.QK_NORM)
     k = m.packs
     bits, sdt = m.bits, m.cfg["scale_dtype"]
 
@@ -40,6 +40,8 @@ def oracle_model(m):
         L["g1"] = k[(l, "attn_gain")]
         L["g2"] = k[(l, "ffn_gain")]
         L["bias"] = k.get((l, "qkv_bias"))
+        L["qn"] = k.get((l, "q_norm"))
+        L["kn"] = k.get((l, "k_norm"))
         layers.append(L)
     head = pack((None, "head"), S.VOCAB, S.D_MODEL)
     return D.Model(shape, layers, head, k["embed"], k["final_gain"])
