@@ -266,6 +266,21 @@ class DecodeModel:
         N.check(N.lib().agxc_model_prefill(self._h, b, p.ctypes.data_as(C.c_void_p), p.size, C.byref(t)), "prefill")
         return dict(gpu_ms=t.gpu_ms, host_ms=t.host_ms, launches=t.launches_per_step)
 
+    def verify(self, draft, b=0, want_logits=False):
+        """The speculative verify step (agxc_model_verify): the current token and the drafted tokens as rows at
+        q0 .. q0 + len(draft); returns (emitted tokens — the accepted drafts and the model's choice after them, all
+        committed to the sequence —, the rows' logits [len(draft) + 1, V] or None)."""
+        d = np.ascontiguousarray(np.asarray(draft, np.int32))
+        if d.size > 15:
+            raise ValueError("verify: at most 15 drafted tokens")
+        out = np.zeros(16, np.int32)
+        n = C.c_int32()
+        lg = np.zeros((d.size + 1, self.vocab_count), np.float32) if want_logits else None
+        N.check(N.lib().agxc_model_verify(self._h, b, d.ctypes.data_as(C.c_void_p) if d.size else None, d.size,
+                                          out.ctypes.data_as(C.c_void_p), C.byref(n),
+                                          None if lg is None else lg.ctypes.data_as(C.c_void_p)), "verify")
+        return [int(t) for t in out[: n.value]], lg
+
     def force(self, b, pos, tokens):
         t = np.ascontiguousarray(np.asarray(tokens, np.int32))
         N.check(N.lib().agxc_model_force(self._h, b, pos, t.ctypes.data_as(C.c_void_p), t.size), "force")

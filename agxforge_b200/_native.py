@@ -87,6 +87,7 @@ SIGNATURES = {
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "agxc_tp_unique_id": (_I, [_P]),
     "agxc_model_prefill": (_I, [_P, _I, _P, _I, C.POINTER(Timing)]),
+    "agxc_model_verify": (_I, [_P, _I, _P, _I, _P, C.POINTER(C.c_int32), _P]),
     "agxc_hgemm_dev": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, C.c_float, _P]),
     "agxc_encoder_create": (_I, [_P, C.POINTER(EncoderDesc), C.POINTER(_P)]),
     "agxc_encoder_free": (None, [_P]),

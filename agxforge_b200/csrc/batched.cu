@@ -123,6 +123,39 @@ __global__ void rope_append_qknorm_kernel(const YRows y, const __half* __restric
   }
 }
 
+// Per row of a GEMM output (its K ranges added in order): the first maximum over V columns, and the row itself to
+// `logits` when given (the speculative verify step's rows).
+__global__ void __launch_bounds__(1024) rows_argmax_kernel(const YRows y, int V, float* logits, int32_t* amax) {
+  const int b = blockIdx.x;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int n = threadIdx.x; n < V; n += blockDim.x) {
+    const float v = yval(y, b, n);
+    if (logits) logits[static_cast<size_t>(b) * V + n] = v;
+    if (v > bv || (bi == 0x7fffffff)) { bv = v; bi = n; }
+  }
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    bv = lane < static_cast<int>(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    bi = lane < static_cast<int>(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+    for (int m = 16; m >= 1; m >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) amax[b] = bi;
+  }
+}
+
 __global__ void residual16_kernel(const YRows y, const __half* __restrict__ x16, float* h, int d, int B) {
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
@@ -319,6 +352,12 @@ __global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, int 
 inline unsigned blocks_for(long long n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
 
 }  // namespace
+
+int launch_rows_argmax(const YRows& y, int V, int rows, float* logits, int32_t* amax, cudaStream_t s) {
+  rows_argmax_kernel<<<rows, 1024, 0, s>>>(y, V, logits, amax);
+  AGXC_CUDA(cudaGetLastError());
+  return 0;
+}
 
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,

@@ -186,6 +186,8 @@ struct YRows {
 
 // ---- the per-row steps of the batched decode step (batched.cu)
 // q0: each row's position; seq < 0: row b is sequence b's (batched decode), else every row is sequence seq's (prefill)
+// per row: the first maximum of V columns (and the row to `logits` when given)
+int launch_rows_argmax(const YRows& y, int V, int rows, float* logits, int32_t* amax, cudaStream_t s);
 // qkg: the layer's QK-norm gains [q hd | k hd] (NULL = no QK-norm), normed with qk_eps before the rotation
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,

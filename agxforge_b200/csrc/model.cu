@@ -126,6 +126,8 @@ struct agxc_model {
   uint32_t* pf_pos = nullptr;   // [rows]
   uint32_t* pf_tok = nullptr;   // [cap] the prompt
   float* pf_part = nullptr;     // the split-K partial sums of the prefill GEMMs
+  float* sp_y = nullptr;        // the verify step's head rows [32][V]
+  int32_t* sp_amax = nullptr;   // and their first maxima
 };
 
 namespace agxc {
@@ -917,6 +919,7 @@ int model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
 }
 
 constexpr int kPrefillRows = 256;  // rows per prefill chunk (the tensor-core GEMM's largest row count)
+constexpr int kVerifyRows = 16;    // rows of the speculative verify step: the current token and up to 15 drafts
 
 __global__ void positions_kernel(uint32_t* pos, int p0, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -995,6 +998,45 @@ int prefill_buffers(agxc_model* m) {
   return 0;
 }
 
+// Mc rows of sequence b at positions p0 .. p0 + Mc - 1 (tokens at m->pf_tok[p0 ..]) through every layer on the
+// tensor-core GEMMs: RMSNorm rows -> qkv GEMM -> RoPE + append (the rows' K/V into b's cache) -> causal attention
+// over the cache rows 0 .. p0 - 1 and the rows before each row -> o_proj GEMM -> add16 -> RMSNorm rows -> gate/up GEMM
+// -> SwiGLU -> down GEMM -> add32_to16. The rows' last-layer x16 stays in m->pf_x16.
+int rows_pass(agxc_model* m, int b, int p0, int Mc, cudaStream_t s, int* launches) {
+  const agxc_model_desc& D = m->d;
+  const int d = D.d_model, F = D.ffn, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim;
+  const size_t layer_kv = static_cast<size_t>(D.batch) * KVH * D.cap * hd;
+  const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  const int Mp = std::max(32, (Mc + 15) / 16 * 16);
+  YRows yr;
+  int rc = 0;
+  embed_rows_kernel<<<Mc, 256, 0, s>>>(m->embed, d, m->pf_tok + p0, Mc, m->pf_x16);
+  positions_kernel<<<(Mc + 255) / 256, 256, 0, s>>>(m->pf_pos, p0, Mc);
+  AGXC_CUDA(cudaGetLastError());
+  *launches += 2;
+  for (int l = 0; l < D.n_layers && !rc; ++l) {
+    const __half* g1 = m->gains + static_cast<size_t>(l) * 2 * d;
+    const __half* bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
+    __half* kc = m->kcache + l * layer_kv;
+    __half* vc = m->vcache + l * layer_kv;
+    if ((rc = launch_rmsnorm(m->pf_x16, 0, Mp, d, g1, D.eps, m->pf_xn16, s)) ||
+        (rc = gemm_rows(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, m->pf_part, s, &yr)) ||
+        (rc = launch_rope_append(yr, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd, D.cap, qscale,
+                                 m->pf_q16, kc, vc, Mc, s, b, qk_gains_of(m, l), D.eps)) ||
+        (rc = launch_prefill_attention(m->pf_q16, kc, vc, Mc, p0, H, KVH, hd, D.cap, b, m->pf_attn, s)) ||
+        (rc = gemm_rows(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
+        (rc = launch_residual16(yr, m->pf_x16, m->pf_h, d, Mp, s)) ||
+        (rc = launch_rmsnorm(m->pf_h, 1, Mp, d, g1 + d, D.eps, m->pf_xn16, s)) ||
+        (rc = gemm_rows(m, m->gu[l], m->pf_xn16, Mp, m->pf_y, 2 * F, m->pf_part, s, &yr)) ||
+        (rc = launch_swiglu(yr, m->pf_act, F, Mp, s)) ||
+        (rc = gemm_rows(m, m->down[l], m->pf_act, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
+        (rc = launch_residual32(yr, m->pf_h, m->pf_x16, d, Mp, s)))
+      break;
+    *launches += 11;
+  }
+  return rc;
+}
+
 // Start sequence b with its prompt and run positions 0 .. n-2 as the prefill section: chunks of up to 256 rows, each
 // layer as RMSNorm rows -> qkv GEMM -> RoPE + append (the chunk's K/V rows into b's cache) -> causal attention of the
 // chunk -> o_proj GEMM -> add16 -> RMSNorm rows -> gate/up GEMM -> SwiGLU -> down GEMM -> add32_to16 (the reference's
@@ -1011,43 +1053,13 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
   const auto h0 = std::chrono::steady_clock::now();
   AGXC_CUDA(cudaEventRecord(m->ev0, s));
   const int total = n - 1;
-  const int d = D.d_model, F = D.ffn, H = D.n_heads, KVH = D.n_kv_heads, hd = D.head_dim;
-  const size_t layer_kv = static_cast<size_t>(D.batch) * KVH * D.cap * hd;
-  const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  const int d = D.d_model;
   int rc = 0, launches = 0;
-  YRows yr;
   if (total > 0) {
     std::vector<uint32_t> tok(prompt, prompt + n);
     AGXC_CUDA(cudaMemcpyAsync(m->pf_tok, tok.data(), static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, s));
   }
-  for (int p0 = 0; p0 < total && !rc; p0 += kPrefillRows) {
-    const int Mc = std::min(kPrefillRows, total - p0);
-    const int Mp = std::max(32, (Mc + 15) / 16 * 16);
-    embed_rows_kernel<<<Mc, 256, 0, s>>>(m->embed, d, m->pf_tok + p0, Mc, m->pf_x16);
-    positions_kernel<<<(Mc + 255) / 256, 256, 0, s>>>(m->pf_pos, p0, Mc);
-    AGXC_CUDA(cudaGetLastError());
-    launches += 2;
-    for (int l = 0; l < D.n_layers && !rc; ++l) {
-      const __half* g1 = m->gains + static_cast<size_t>(l) * 2 * d;
-      const __half* bias = D.qkv_bias ? m->bias + static_cast<size_t>(l) * m->qkv_rows : nullptr;
-      __half* kc = m->kcache + l * layer_kv;
-      __half* vc = m->vcache + l * layer_kv;
-      if ((rc = launch_rmsnorm(m->pf_x16, 0, Mp, d, g1, D.eps, m->pf_xn16, s)) ||
-          (rc = gemm_rows(m, m->qkv[l], m->pf_xn16, Mp, m->pf_y, m->qkv_rows, m->pf_part, s, &yr)) ||
-          (rc = launch_rope_append(yr, m->qkv_rows, bias, m->cos_t, m->sin_t, m->pf_pos, H, KVH, hd, D.cap, qscale,
-                                   m->pf_q16, kc, vc, Mc, s, b, qk_gains_of(m, l), D.eps)) ||
-          (rc = launch_prefill_attention(m->pf_q16, kc, vc, Mc, p0, H, KVH, hd, D.cap, b, m->pf_attn, s)) ||
-          (rc = gemm_rows(m, m->wo[l], m->pf_attn, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
-          (rc = launch_residual16(yr, m->pf_x16, m->pf_h, d, Mp, s)) ||
-          (rc = launch_rmsnorm(m->pf_h, 1, Mp, d, g1 + d, D.eps, m->pf_xn16, s)) ||
-          (rc = gemm_rows(m, m->gu[l], m->pf_xn16, Mp, m->pf_y, 2 * F, m->pf_part, s, &yr)) ||
-          (rc = launch_swiglu(yr, m->pf_act, F, Mp, s)) ||
-          (rc = gemm_rows(m, m->down[l], m->pf_act, Mp, m->pf_y, d, m->pf_part, s, &yr)) ||
-          (rc = launch_residual32(yr, m->pf_h, m->pf_x16, d, Mp, s)))
-        break;
-      launches += 11;
-    }
-  }
+  for (int p0 = 0; p0 < total && !rc; p0 += kPrefillRows) rc = rows_pass(m, b, p0, std::min(kPrefillRows, total - p0), s, &launches);
   if (rc) return rc;
   // the last prompt token is the next decode step's input, at position n-1
   const uint32_t q0 = static_cast<uint32_t>(n - 1);
@@ -1071,6 +1083,93 @@ int model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timin
     if (fused_active(m)) fused_reset(m);  // a step that gave up leaves its counters part-way
     return fail(err & kErrMbarTimeout ? AGXC_ETIMEOUT : AGXC_ECORRUPT, "prefill: device error word " + std::to_string(err));
   }
+  return 0;
+}
+
+// The speculative verify step (the reference's verify section, agxforge/inference/assemble.py:244-253,747-803, driven
+// by tools/g17specgen.m): the current token (log[q0], whose embedding is the next decode input) and n_draft drafted
+// tokens as rows at positions q0 .. q0 + n_draft through the row pass (their K/V rows into the cache), the final
+// norm, the head and each row's first maximum. Row i's choice is the token at position q0 + i + 1 — the logged one
+// where the log fixes it (the generation step's rule), else the maximum. The drafts are accepted while they equal the
+// choices; the accepted drafts and the choice after them are emitted and committed: logged, q0 advanced past them,
+// x16 = the last one's embedding. Rows past the accepted ones leave K/V rows the next steps overwrite.
+int model_verify(agxc_model* m, int b, const int32_t* draft, int n_draft, int32_t* emitted, int32_t* n_emitted,
+                 float* logits_out) {
+  const agxc_model_desc& D = m->d;
+  if (m->comm) return fail(AGXC_EUNSUPPORTED, "verify: a single-device model");
+  if (m->qkv_rows % 128 || D.d_model % 128 || (2 * D.ffn) % 128 || D.vocab % 128)
+    return fail(AGXC_EUNSUPPORTED, "verify: needs qkv rows, d_model, 2 x ffn and vocab multiples of 128");
+  if (b < 0 || b >= D.batch) return fail(AGXC_EINVAL, "verify: sequence index");
+  if (n_draft < 0 || n_draft > kVerifyRows - 1) return fail(AGXC_EINVAL, "verify: 0 to 15 drafted tokens");
+  for (int i = 0; i < n_draft; ++i)
+    if (draft[i] < 0 || draft[i] >= m->vt) return fail(AGXC_EINVAL, "verify: draft token out of range");
+  if (int rc = prefill_buffers(m)) return rc;
+  cudaStream_t s = m->ctx->stream;
+  AGXC_CUDA(cudaStreamSynchronize(s));
+  uint32_t q0 = 0;
+  AGXC_CUDA(cudaMemcpy(&q0, m->q0 + b, 4, cudaMemcpyDeviceToHost));
+  const int R = n_draft + 1;
+  if (static_cast<int>(q0) + R >= D.cap) return fail(AGXC_EINVAL, "verify: the rows would pass the cap");
+  std::vector<uint32_t> log(R + 1);
+  AGXC_CUDA(cudaMemcpy(log.data(), m->log + static_cast<size_t>(b) * D.cap + q0, (R + 1) * 4, cudaMemcpyDeviceToHost));
+  if (log[0] == kTokenUnset || log[0] >= static_cast<uint32_t>(m->vt))
+    return fail(AGXC_EINVAL, "verify: no current token at q0 (start the sequence first)");
+  std::vector<uint32_t> rows(R);
+  rows[0] = log[0];
+  for (int i = 0; i < n_draft; ++i) rows[i + 1] = static_cast<uint32_t>(draft[i]);
+  if (!m->sp_y) {
+    int rc;
+    if ((rc = dalloc_t(m, &m->sp_y, static_cast<size_t>(32) * D.vocab)) || (rc = dalloc_t(m, &m->sp_amax, 32)))
+      return rc;
+  }
+  AGXC_CUDA(cudaMemcpyAsync(m->pf_tok + q0, rows.data(), R * 4, cudaMemcpyHostToDevice, s));
+  int launches = 0;
+  int rc = rows_pass(m, b, static_cast<int>(q0), R, s, &launches);
+  YRows yr;
+  if (!rc) rc = launch_rmsnorm(m->pf_x16, 0, 32, D.d_model, m->final_gain, D.eps, m->pf_xn16, s);
+  if (!rc) rc = gemm_rows(m, m->head, m->pf_xn16, 32, m->sp_y, D.vocab, m->pf_part, s, &yr);
+  if (!rc) rc = launch_rows_argmax(yr, D.vocab, R, nullptr, m->sp_amax, s);
+  if (rc) return rc;
+  std::vector<int32_t> amax(R);
+  AGXC_CUDA(cudaMemcpyAsync(amax.data(), m->sp_amax, R * 4, cudaMemcpyDeviceToHost, s));
+  if (logits_out) {
+    if (yr.ks > 1) {   // the head's split-K slices summed into the output rows
+      float* dev = m->sp_y;
+      if ((rc = launch_rows_argmax(yr, D.vocab, R, dev, m->sp_amax, s))) return rc;
+      AGXC_CUDA(cudaMemcpyAsync(logits_out, dev, static_cast<size_t>(R) * D.vocab * 4, cudaMemcpyDeviceToHost, s));
+    } else {
+      AGXC_CUDA(cudaMemcpyAsync(logits_out, m->sp_y, static_cast<size_t>(R) * D.vocab * 4, cudaMemcpyDeviceToHost, s));
+    }
+  }
+  AGXC_CUDA(cudaStreamSynchronize(s));
+  uint32_t err = 0;
+  AGXC_CUDA(cudaMemcpy(&err, m->ctx->err_dev, 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    const uint32_t zero = 0;
+    cudaMemcpy(m->ctx->err_dev, &zero, 4, cudaMemcpyHostToDevice);
+    return fail(err & kErrMbarTimeout ? AGXC_ETIMEOUT : AGXC_ECORRUPT, "verify: device error word " + std::to_string(err));
+  }
+  // accept: choice i = the logged token at q0 + i + 1 where set, else row i's maximum
+  int k = 0;
+  std::vector<uint32_t> out;
+  for (int i = 0; i < R; ++i) {
+    const uint32_t choice = log[i + 1] != kTokenUnset ? log[i + 1] : static_cast<uint32_t>(amax[i]);
+    out.push_back(choice);
+    if (i < n_draft && static_cast<uint32_t>(draft[i]) == choice) {
+      ++k;
+      continue;
+    }
+    break;
+  }
+  // commit: log the emitted tokens, q0 past them, x16 = the last one's embedding
+  const uint32_t nq0 = q0 + static_cast<uint32_t>(out.size());
+  AGXC_CUDA(cudaMemcpy(m->log + static_cast<size_t>(b) * D.cap + q0 + 1, out.data(), out.size() * 4,
+                       cudaMemcpyHostToDevice));
+  AGXC_CUDA(cudaMemcpy(m->q0 + b, &nq0, 4, cudaMemcpyHostToDevice));
+  AGXC_CUDA(cudaMemcpy(m->x16 + static_cast<size_t>(b) * D.d_model, m->embed + static_cast<size_t>(out.back()) * D.d_model,
+                       static_cast<size_t>(D.d_model) * 2, cudaMemcpyDeviceToDevice));
+  for (size_t i = 0; i < out.size(); ++i) emitted[i] = static_cast<int32_t>(out[i]);
+  *n_emitted = static_cast<int32_t>(out.size());
   return 0;
 }
 
@@ -1295,6 +1394,12 @@ int agxc_model_start(agxc_model* m, int b, const int32_t* prompt, int n) {
 int agxc_model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timing* t) {
   if (!m || !prompt) return agxc::fail(AGXC_EINVAL, "prefill: null argument");
   return agxc::model_prefill(m, b, prompt, n, t);
+}
+
+int agxc_model_verify(agxc_model* m, int b, const int32_t* draft, int n_draft, int32_t* emitted, int32_t* n_emitted,
+                      float* logits_out) {
+  if (!m || (!draft && n_draft) || !emitted || !n_emitted) return agxc::fail(AGXC_EINVAL, "verify: null argument");
+  return agxc::model_verify(m, b, draft, n_draft, emitted, n_emitted, logits_out);
 }
 
 int agxc_model_force(agxc_model* m, int b, int pos, const int32_t* tokens, int n) {

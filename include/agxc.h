@@ -245,6 +245,17 @@ typedef struct {
  * generated token: the state n-1 teacher-forced decode steps would leave (within rounding). Needs qkv rows, d_model
  * and 2 x ffn multiples of 128 and one device; `t` (nullable) gets the device time. */
 AGXC_API int agxc_model_prefill(agxc_model* m, int b, const int32_t* prompt, int n, agxc_timing* t);
+
+/* The speculative verify step (the reference's verify section, agxforge/inference/assemble.py:244-253,747-803 and its
+ * driver tools/g17specgen.m): sequence b's current token and n_draft (0..15) drafted tokens run as rows at positions
+ * q0 .. q0 + n_draft through the tensor-core GEMMs (their K/V rows written into the cache), then the final norm, the
+ * head and each row's first maximum. Row i chooses the token at position q0 + i + 1 (a logged token where the log
+ * fixes it, else the maximum); drafts are accepted while they equal the choices. The accepted drafts and the choice
+ * after them (1 .. n_draft + 1 tokens) go to emitted[] / *n_emitted and are committed: logged, q0 advanced past them,
+ * the next input row = the last one's embedding. logits_out (nullable): [n_draft + 1][vocab] fp32 of the rows.
+ * Single device; needs qkv rows, d_model, 2 x ffn and vocab multiples of 128. */
+AGXC_API int agxc_model_verify(agxc_model* m, int b, const int32_t* draft, int n_draft, int32_t* emitted,
+                               int32_t* n_emitted, float* logits_out);
 AGXC_API int agxc_decode(agxc_model* m, int steps, const int32_t* forced_in, int32_t* tokens_out, float* logits_out,
                 int sync_each, agxc_timing* t);
 
