@@ -175,7 +175,7 @@ class DecodeModel:
             N.check(N.lib().agxc_model_set_vector(self._h, layer, idx, C.c_void_p(t.data_ptr()),
                                                   t.numel() * 2, 1), "set_vector %s" % which)
 
-    OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused", "qk_norm")
+    OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused", "qk_norm", "device_wait_us")
 
     def set_option(self, option, value):
         """Model options: "fused" (batch 1 on one device: the whole step as one persistent kernel whose layer phases
@@ -189,9 +189,11 @@ class DecodeModel:
         1 = the o_proj/down GEMMs push their tiles to every rank over NVLink and the sum is fused with the residual,
         the default where available; 0 = NCCL all-reduce; every rank must set the same value); "qk_norm" (Qwen3:
         the per-head RMSNorm of q and k before RoPE, with the "q_norm" / "k_norm" gains; build() sets it for a
-        QK_NORM shape)."""
+        QK_NORM shape); "device_wait_us" (the bound on every wait of the fused step and the tensor-parallel reduce,
+        default 2,000,000 us: a wait past it leaves the step undone and the call raises TimeoutError)."""
         opts = {"pdl": N.OPT_PDL, "trace": N.OPT_TRACE, "fused": N.OPT_FUSED, "bulk": N.OPT_BULK,
-                "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED, "qk_norm": N.OPT_QK_NORM}
+                "wait_ms": N.OPT_WAIT_MS, "tp_fused": N.OPT_TP_FUSED, "qk_norm": N.OPT_QK_NORM,
+                "device_wait_us": N.OPT_DEVICE_WAIT_US}
         if option not in opts:
             raise ValueError("unknown option %r (known: %s)" % (option, sorted(opts)))
         N.check(N.lib().agxc_model_set_option(self._h, opts[option], int(value)), "set_option")

@@ -26,6 +26,7 @@ OPT_BULK = 3
 OPT_WAIT_MS = 4
 OPT_TP_FUSED = 5
 OPT_QK_NORM = 6
+OPT_DEVICE_WAIT_US = 7
 
 
 class PackDesc(C.Structure):
@@ -84,6 +85,7 @@ SIGNATURES = {
     "agxc_attention_dev": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "agxc_rope_append_dev": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, C.c_float, _P, _P, _P, _P]),
     "agxc_argmax_dev": (_I, [_P, _P, _I, _P, _P]),
+    "agxc_tp_reduce_dev": (_I, [_P, _P, _I, _I, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P]),
     "agxc_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "agxc_tp_unique_id": (_I, [_P]),
     "agxc_model_prefill": (_I, [_P, _I, _P, _I, C.POINTER(Timing)]),

@@ -1,10 +1,11 @@
-// api.cu — two small device entry points behind the reference's per-kernel Python functions that the decode step
-// itself fuses elsewhere:
+// api.cu — small device entry points: two behind the reference's per-kernel Python functions that the decode step
+// itself fuses elsewhere, and the tensor-parallel reduce on its own (for its bounded-wait check):
 //   agxc_rope_append_dev   RoPE + q scale + KV append on one token's fp32 qkv row in the reference's logical order
 //                          [q heads | k heads | v heads] x head_dim (attention.py:1309-1323 attn_rope_reference); in
 //                          the decode step this is the qkv GEMV's epilogue
 //   agxc_argmax_dev        the first maximum of an fp32 row (argmax.py:287-288 argmax_reference); in the decode step
 //                          this is the vocabulary GEMV's epilogue
+//   agxc_tp_reduce_dev     the tensor-parallel all-reduce's local reduction with its bounded flag wait
 #include <cfloat>
 
 #include "common.cuh"
@@ -100,6 +101,25 @@ AGXC_API int agxc_rope_append_dev(agxc_ctx* ctx, const float* qkv_dev, int heads
                                                        reinterpret_cast<__half*>(vcache_dev));
   AGXC_CUDA(cudaGetLastError());
   return 0;
+}
+
+AGXC_API int agxc_tp_reduce_dev(agxc_ctx* ctx, const float* recv_dev, int ranks, int rank, const unsigned* flag_dev,
+                                const unsigned* epoch_dev, int uses_per_step, int use_in_step, int tiles_per_rank,
+                                const uint16_t* res16_dev, const float* res32_dev, float* out32_dev,
+                                uint16_t* out16_dev, int d, int batch, int wait_us, void* stream) {
+  if (!ctx || !recv_dev || !flag_dev || !epoch_dev) return fail(AGXC_EINVAL, "tp_reduce: null argument");
+  if (ranks < 1 || ranks > 8 || rank < 0 || rank >= ranks || d <= 0 || batch <= 0 || wait_us < 0)
+    return fail(AGXC_EINVAL, "tp_reduce: 1..8 ranks, 0 <= rank < ranks, positive d and batch, wait_us >= 0");
+  if ((res16_dev == nullptr) == (res32_dev == nullptr))
+    return fail(AGXC_EINVAL, "tp_reduce: exactly one residual (fp16 for o_proj, fp32 for down)");
+  if ((res16_dev && !out32_dev) || (res32_dev && !out16_dev)) return fail(AGXC_EINVAL, "tp_reduce: null output");
+  TpGather g;
+  g.out32[rank] = out32_dev;
+  g.out16[rank] = reinterpret_cast<__half*>(out16_dev);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+  return launch_tp_reduce(recv_dev, ranks, rank, flag_dev, epoch_dev, uses_per_step, use_in_step, tiles_per_rank,
+                          reinterpret_cast<const __half*>(res16_dev), res32_dev, g, d, batch, ctx->err_dev, s, false,
+                          static_cast<uint64_t>(wait_us) * 1000ull);
 }
 
 AGXC_API int agxc_argmax_dev(agxc_ctx* ctx, const float* x_dev, int n, int32_t* out_dev, void* stream) {

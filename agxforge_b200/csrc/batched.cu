@@ -281,14 +281,15 @@ __global__ void gen_from_pairs_kernel(const uint32_t* __restrict__ pairs, int ra
   gen_step(b, bi, V, embed, d, q0, log, cap, tok_out, force_next, x16, err, &s_tok);
 }
 
-// A bounded spin until *flag reaches target (the signed difference handles wrap-around); false after 2 s.
-__device__ bool wait_flag_sys(const unsigned* flag, unsigned target, unsigned* err) {
+// A bounded spin until *flag reaches target (the signed difference handles wrap-around); false after limit_ns of
+// the global timer (2 s unless the model's device wait limit says otherwise).
+__device__ bool wait_flag_sys(const unsigned* flag, unsigned target, unsigned* err, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (unsigned it = 0;; ++it) {
     unsigned v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (static_cast<int>(v - target) >= 0) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) {
       atomicOr(err, kErrMbarTimeout);
       return false;
     }
@@ -302,17 +303,19 @@ __device__ bool wait_flag_sys(const unsigned* flag, unsigned target, unsigned* e
 __global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, int rank, const unsigned* flag,
                                  const unsigned* epoch, int uses_per_step, int use_in_step, int tiles_per_rank,
                                  const __half* __restrict__ res16, const float* __restrict__ res32, TpGather gather,
-                                 int d, int B, unsigned* err, int two_shot) {
+                                 int d, int B, unsigned* err, int two_shot, uint64_t wait_ns) {
   __shared__ int s_ok;
   const unsigned use = *epoch * static_cast<unsigned>(uses_per_step) + static_cast<unsigned>(use_in_step);
   const unsigned arrivals = static_cast<unsigned>(ranks * tiles_per_rank * (two_shot ? 1 : ranks));
-  if (threadIdx.x == 0) s_ok = wait_flag_sys(flag, (use + 1u) * arrivals, err);
+  if (threadIdx.x == 0) s_ok = wait_flag_sys(flag, (use + 1u) * arrivals, err, wait_ns);
   __syncthreads();
   const int w = two_shot ? d / ranks : d, n0 = two_shot ? rank * w : 0;  // the rows reduced here
   const int rlo = two_shot ? 0 : rank, rhi = two_shot ? ranks : rank + 1;  // the ranks whose streams are written
   const size_t slot = static_cast<size_t>(B) * d;
   const int per_row = w / 4;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B * per_row; i += gridDim.x * blockDim.x) {
+  // a wait that gave up leaves every residual stream as it was (no partial sum reaches a peer); the gather signal
+  // below still goes out so the other ranks' bounded waits end
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; s_ok && i < B * per_row; i += gridDim.x * blockDim.x) {
     const int b = i / per_row;
     const size_t at = static_cast<size_t>(b) * d + n0 + (i % per_row) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -344,7 +347,7 @@ __global__ void tp_reduce_kernel(const float* __restrict__ recv, int ranks, int 
     for (int r = 0; r < ranks; ++r)
       asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(gather.gflag[r]) : "memory");
     // every rank's rows are here once every block of every rank has signalled this use
-    wait_flag_sys(gather.gflag[rank], (use + 1u) * static_cast<unsigned>(ranks) * gridDim.x, err);
+    wait_flag_sys(gather.gflag[rank], (use + 1u) * static_cast<unsigned>(ranks) * gridDim.x, err, wait_ns);
   }
   __syncthreads();
 }
@@ -400,7 +403,8 @@ int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, ui
 
 int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* flag, const unsigned* epoch,
                      int uses_per_step, int use_in_step, int tiles_per_rank, const __half* res16, const float* res32,
-                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot) {
+                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot,
+                     uint64_t wait_ns) {
   if (d % (4 * ranks)) return fail(AGXC_EINVAL, "tp_reduce: d a multiple of 4 x ranks");
   const long long elems4 = static_cast<long long>(B) * d / (two_shot ? ranks : 1) / 4;
   // two-shot: a fixed grid, the same on every rank (the gather target counts every rank's blocks), all resident
@@ -415,7 +419,7 @@ int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* fla
   cfg.attrs = attr;
   cfg.numAttrs = two_shot ? 1 : 0;
   AGXC_CUDA(cudaLaunchKernelEx(&cfg, tp_reduce_kernel, recv, ranks, rank, flag, epoch, uses_per_step, use_in_step,
-                               tiles_per_rank, res16, res32, gather, d, B, err, two_shot ? 1 : 0));
+                               tiles_per_rank, res16, res32, gather, d, B, err, two_shot ? 1 : 0, wait_ns));
   return 0;
 }
 

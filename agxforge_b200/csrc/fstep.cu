@@ -55,7 +55,6 @@ constexpr int kSbOff = 16384;         // the scale/bias part of a stage
 constexpr int kMaxRing = 12;
 constexpr int kKeyTile = 16;          // keys per MMA tile (M)
 constexpr int kMinKeys = 32;          // the fewest keys an attention split takes
-constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kTraceMarks = 8;        // per layer: Q wait, Q done, A wait, A done, O wait, O done, F wait, F done
 
 // The maps of a model: per layer kMapsPerLayer, then the head's two and the caches' two.
@@ -94,6 +93,7 @@ __host__ __device__ inline Layout smem_layout(int d, int kattn, int stages) {
 struct Params {
   int L, d, H, KVH, hd, G, F, V, cap, bits, sdt, stages;
   float eps, qscale;
+  uint64_t wait_ns;        // the bound on every wait (global timer)
   int rt_qkv, rt_d, nf, rt_v, gd, gk, gchunk, dn_rows, smax;
   const CUtensorMap* maps;
   const __half* gains;     // [L][2][d]
@@ -181,7 +181,7 @@ __device__ bool mbar_wait_abortable(uint64_t* bar, unsigned parity, const Params
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 63u) {
       if (aborted(P)) return false;
-      if (globaltimer_ns() - t0 > kWaitNs) {
+      if (globaltimer_ns() - t0 > P.wait_ns) {
         raise_abort(P, kErrMbarTimeout);
         return false;
       }
@@ -200,8 +200,8 @@ __device__ bool wait_counter(const unsigned* c, unsigned target, const Params& P
         if (ld_acq(c) >= target) break;
         if ((it & 15u) == 15u) {
           if (aborted(P)) { ok = 0; break; }
-          if (globaltimer_ns() - t0 > kWaitNs) {
-            raise_abort(P, kErrGridTimeout);
+          if (globaltimer_ns() - t0 > P.wait_ns) {
+            raise_abort(P, kErrGridTimeout | kErrMbarTimeout);
             ok = 0;
             break;
           }
@@ -1121,7 +1121,7 @@ int fstep_configure(const agxc_ctx* ctx) {
 int fstep_launch(const FstepArgs& a, cudaStream_t s) {
   Params p;
   p.L = a.L; p.d = a.d; p.H = a.H; p.KVH = a.KVH; p.hd = a.hd; p.G = a.H / a.KVH; p.F = a.F; p.V = a.V;
-  p.cap = a.cap; p.bits = a.bits; p.sdt = a.sdt; p.stages = a.stages; p.eps = a.eps;
+  p.cap = a.cap; p.bits = a.bits; p.sdt = a.sdt; p.stages = a.stages; p.eps = a.eps; p.wait_ns = a.wait_ns;
   p.qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(a.hd)));
   p.rt_qkv = (a.H + 2 * a.KVH) * a.hd / 16;
   p.rt_d = a.d / 16;

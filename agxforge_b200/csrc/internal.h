@@ -129,6 +129,7 @@ int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
 struct FstepArgs {
   int L = 0, d = 0, H = 0, KVH = 0, hd = 0, F = 0, V = 0, cap = 0, bits = 4, sdt = 0, stages = 0, smax = 1, grid = 0;
   float eps = 1e-6f;
+  uint64_t wait_ns = 2000000000ull;   // the bound on every wait of the step (global timer)
   const CUtensorMap* maps = nullptr;  // device: per layer fstep_maps_per_layer(), then the head's 2, then K and V
   const __half* gains = nullptr;
   const __half* bias = nullptr;
@@ -255,9 +256,11 @@ struct TpGather {
   __half* out16[8] = {};
   unsigned* gflag[8] = {};  // rank r's gather counter of this buffer
 };
+// wait_ns: the bound on each of its spins (the global timer; 2 s by default)
 int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* flag, const unsigned* epoch,
                      int uses_per_step, int use_in_step, int tiles_per_rank, const __half* res16, const float* res32,
-                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot);
+                     const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot,
+                     uint64_t wait_ns = 2000000000ull);
 size_t attn_part_floats(int nb, int H, int S, int hd);
 // tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,

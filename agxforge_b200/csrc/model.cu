@@ -98,6 +98,7 @@ struct agxc_model {
   uint32_t* amax = nullptr;     // [B][2] this rank's (value bits, global index) per sequence
   uint32_t* amax_all = nullptr; // [tp][B][2] every rank's, after the all-gather
   int wait_ms = 60000;
+  uint64_t dev_wait_ns = 2000000000ull;  // AGXC_OPT_DEVICE_WAIT_US: the bound on the fused step's and the TP reduce's waits
   // the fused GEMM + all-reduce (peer memory): recv = [2 buffers (o_proj, down)][tp ranks][B][d] fp32 then 2 arrival
   // counters, one allocation exported to the other ranks by CUDA IPC; peer[r] = rank r's allocation, mapped here
   int tp_fused = 0;             // 1: o_proj and down push their tiles to every rank and reduce locally (no NCCL)
@@ -236,7 +237,7 @@ int enqueue_step_fused(agxc_model* m, cudaStream_t s) {
   FstepArgs a;
   a.L = D.n_layers; a.d = D.d_model; a.H = D.n_heads; a.KVH = D.n_kv_heads; a.hd = D.head_dim; a.F = D.ffn;
   a.V = D.vocab; a.cap = D.cap; a.bits = D.bits; a.sdt = D.scale_dtype; a.stages = m->fs_stages; a.smax = m->fs_smax;
-  a.grid = m->ctx->num_sms; a.eps = D.eps;
+  a.grid = m->ctx->num_sms; a.eps = D.eps; a.wait_ns = m->dev_wait_ns;
   a.maps = m->fs_maps; a.gains = m->gains; a.bias = D.qkv_bias ? m->bias : nullptr; a.final_gain = m->final_gain;
   a.qkg = m->qk_norm ? m->qk_gains : nullptr; a.qkraw = m->qkv_raw;
   a.embed = m->embed; a.kc = m->kcache; a.vc = m->vcache; a.cos_t = m->cos_t; a.sin_t = m->sin_t; a.q0 = m->q0;
@@ -357,7 +358,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
       if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, &ps)) ||
           (rc = launch_tp_reduce(m->recv, m->tp, m->tp_rank, m->recv_flags, m->epoch, D.n_layers, l,
                                  ps.tiles_per_rank, m->x16, nullptr, gather_of(0), d, B, m->ctx->err_dev, s,
-                                 m->tp_two_shot)) ||
+                                 m->tp_two_shot, m->dev_wait_ns)) ||
           (rc = close()))
         return rc;
     } else if (m->comm) {  // NCCL: the finished rows all-reduced, then the residual
@@ -378,7 +379,7 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
       if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, &ps)) ||
           (rc = launch_tp_reduce(m->recv + static_cast<size_t>(m->tp) * B * d, m->tp, m->tp_rank, m->recv_flags + 1,
                                  m->epoch, D.n_layers, l, ps.tiles_per_rank, nullptr, m->h, gather_of(1), d, B,
-                                 m->ctx->err_dev, s, m->tp_two_shot)) ||
+                                 m->ctx->err_dev, s, m->tp_two_shot, m->dev_wait_ns)) ||
           (rc = close()))
         return rc;
     } else if (m->comm) {
@@ -1654,6 +1655,9 @@ int agxc_model_set_option(agxc_model* m, int option, int value) {
       return agxc::fail(AGXC_EUNSUPPORTED, "set_option: this model has no fused step (batch 1 on one device, and the "
                                            "ring must fit the shared memory)");
     m->fused = value ? 1 : 0;
+  } else if (option == AGXC_OPT_DEVICE_WAIT_US) {
+    if (value < 0) return agxc::fail(AGXC_EINVAL, "set_option: device_wait_us must be >= 0");
+    m->dev_wait_ns = static_cast<uint64_t>(value) * 1000ull;
   } else if (option == AGXC_OPT_QK_NORM) {
     m->qk_norm = value ? 1 : 0;
   } else if (option == AGXC_OPT_TRACE) {

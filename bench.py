@@ -209,6 +209,37 @@ def cpu_baseline_sample(m, tokens, pos):
     return (time.perf_counter() - t0) / tokens, cpu.threads
 
 
+def trace_fused_step(args, m, hist):
+    """--trace-step on the fused step: one traced step's per-CTA marks reduced to per-phase times (µs), means over
+    layers 2 .. L-2. Per layer: qkv = its slowest CTA's qkv work after x was complete; attn_wait = from the last qkv
+    tile to the last attention CTA passing its group's dependency; attn = attention work (slowest CTA); o_wait / o_proj
+    = the same for the merge + o_proj; h_wait = to the last CTA passing the h dependency; ffn = the FFN work (slowest
+    CTA); x_wait = from the last FFN unit to the last CTA passing the next layer's x dependency; layer = x-complete to
+    x-complete."""
+    m.start(0, [1])
+    m.fill_history(0, hist - args.warmup, seed=1792)
+    m.decode(args.warmup, want_tokens=False)
+    m.set_option("trace", 1)
+    m.decode(1, want_tokens=False)
+    tr = m.trace_fused().astype(np.float64)
+    m.close()
+    L = (tr.shape[0] - 2) // 8
+    rec = []
+    for l in range(2, L - 2):
+        b = 8 * l
+        mx = lambda k: tr[b + k][tr[b + k] > 0].max()   # noqa: E731
+        mn = lambda k: tr[b + k][tr[b + k] > 0].min()   # noqa: E731
+        nxt = tr[b + 8][tr[b + 8] > 0].max()
+        rec.append(dict(qkv=mx(1) - mx(0), attn_wait=mx(2) - mx(1), attn=mx(3) - mx(2), o_wait=mx(4) - mx(3),
+                        o_proj=mx(5) - mx(4), h_wait=mx(6) - mx(5), ffn=mx(7) - mx(6), x_wait=nxt - mx(7),
+                        layer=nxt - mx(0), x_skew=mx(0) - mn(0)))
+    phases = {k: round(float(np.mean([r[k] for r in rec])) / 1e3, 2) for k in rec[0]}
+    head = tr[8 * L + 1][tr[8 * L + 1] > 0].max() - tr[8 * L][tr[8 * L] > 0].max()
+    step = tr[8 * L + 1][tr[8 * L + 1] > 0].max() - tr[0][tr[0] > 0].min()
+    print(json.dumps(dict(trace_step=args.config, fused=True, layers=L, step_us=round(step / 1e3, 1),
+                          head_us=round(head / 1e3, 2), phases=phases)), flush=True)
+
+
 def trace_step(args):
     """--trace-step: one traced step of a batch-1 config after the bench's warm-up, reduced to per-phase means (µs)
     over layers 2 .. L-2. For phase i: handoff = its last CTA past the dependency wait - phase i-1's last exit;
@@ -220,7 +251,9 @@ def trace_step(args):
     if batch != 1:
         raise SystemExit("--trace-step: batch-1 configs only")
     m = assemble.build(dict(model=model, bits=bits, batch=1, cap=hist + 16, seed=2))
-    m.set_option("fused", 0)
+    if m.fused:
+        trace_fused_step(args, m, hist)
+        return
     m.start(0, [1])
     m.fill_history(0, hist - args.warmup, seed=1792)
     m.decode(args.warmup, want_tokens=False)

@@ -156,6 +156,16 @@ AGXC_API int agxc_rope_append_dev(agxc_ctx* ctx, const float* qkv_dev, int heads
                                   int pos, const float* cos_dev, const float* sin_dev, float qscale,
                                   uint16_t* q16_dev, uint16_t* kcache_dev, uint16_t* vcache_dev, void* stream);
 
+/* The tensor-parallel all-reduce's local reduction (one-shot): waits (bounded by wait_us of the global timer) until
+ * *flag_dev reaches the arrivals of this use (every rank's o_proj or down tiles pushed into recv [ranks][batch][d]),
+ * then writes this rank's residual stream: out32 = sum over ranks + res16 (o_proj, add16) or out16 = fp16(sum +
+ * res32) (down, add32_to16). A wait that gives up sets the error word's timeout bit and writes nothing; the context
+ * stays usable. (In the decode step this runs inside the step's graph; this entry point exposes it to tests.) */
+AGXC_API int agxc_tp_reduce_dev(agxc_ctx* ctx, const float* recv_dev, int ranks, int rank, const unsigned* flag_dev,
+                                const unsigned* epoch_dev, int uses_per_step, int use_in_step, int tiles_per_rank,
+                                const uint16_t* res16_dev, const float* res32_dev, float* out32_dev,
+                                uint16_t* out16_dev, int d, int batch, int wait_us, void* stream);
+
 /* The first maximum of an fp32 row of n values (argmax.py:287-288 argmax_reference; NaN-free input): *out_dev =
  * the smallest index holding the largest value. (In the decode step this is the vocabulary GEMV's epilogue.) */
 AGXC_API int agxc_argmax_dev(agxc_ctx* ctx, const float* x_dev, int n, int32_t* out_dev, void* stream);
@@ -315,6 +325,9 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_QK_NORM 6     /* 1: QK-norm (Qwen3; attention.py:256-265 with_qknorm): every q and k head of the qkv
                                  projection is RMS-normed over head_dim with the layer's AGXC_VEC_Q_NORM / _K_NORM gain
                                  (fp32, (x r) g, the model's eps) before RoPE, on every path; 0 (default): off */
+#define AGXC_OPT_DEVICE_WAIT_US 7 /* the bound (us of the global timer) on every wait of the fused step and of the
+                                 tensor-parallel reduce (default 2,000,000): a wait past it sets the error word, the
+                                 launch leaves, and the decode call returns AGXC_ETIMEOUT with the step undone */
 #define AGXC_OPT_WAIT_MS 4     /* tensor parallel: host bound (ms, default 60000) on a decode call's completion; past it
                                  the communicator is aborted (its kernels end) and the call returns AGXC_ETIMEOUT, so a
                                  rank that died between steps cannot hold the others' GPUs */
