@@ -115,19 +115,34 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
+def swiglu64(g, u):
+    """silu(g) * u over row blocks on the thread pool (float64 throughout)."""
+    out = np.empty_like(g)
+
+    def block(r0, r1):
+        gg = g[r0:r1]
+        out[r0:r1] = gg / (1.0 + np.exp(-gg)) * u[r0:r1]
+    P.parallel_rows(g.shape[0], block)
+    return out
+
+
 def attention_causal(q16, k16, v16, n_kv_heads):
     """Base-2 softmax attention of every position over keys 0..p. q16 [T, H, hd] (already scaled by log2e/sqrt(hd)),
     k16/v16 [T, KVH, hd]. Returns [T, H, hd] float64 (attention.py:1659-1668 on every position)."""
     T, H, hd = q16.shape
     G = H // n_kv_heads
     out = np.empty((T, H, hd), F64)
-    mask = np.tril(np.ones((T, T), bool))
     for h in range(H):
         kv = h // G
         s = q16[:, h, :] @ k16[:, kv, :].T                         # [T, T]
-        s = np.where(mask, s, -np.inf)
-        p = np.exp2(s - s.max(axis=1, keepdims=True))
-        out[:, h, :] = (p @ v16[:, kv, :]) / p.sum(axis=1, keepdims=True)
+        pr = np.empty_like(s)
+
+        def block(r0, r1):   # rows r0 .. r1-1 see keys 0 .. r (causal)
+            sb = s[r0:r1]
+            sb[np.arange(r1 - r0)[:, None] + r0 < np.arange(T)[None, :]] = -np.inf
+            pr[r0:r1] = np.exp2(sb - sb.max(axis=1, keepdims=True))
+        P.parallel_rows(T, block)
+        out[:, h, :] = (pr @ v16[:, kv, :]) / pr.sum(axis=1, keepdims=True)
     return out
 
 
@@ -223,9 +238,7 @@ class Model:
                 a = f16(a)
             h = x + a @ L["wo"].w64().T
             h2 = rmsnorm(h, L["g2"].astype(F64), S.eps, half)
-            g = h2 @ L["gate"].w64().T
-            u = h2 @ L["up"].w64().T
-            act = silu(g) * u
+            act = swiglu64(h2 @ L["gate"].w64().T, h2 @ L["up"].w64().T)
             if half:
                 act = f16(act)
             x = h + act @ L["down"].w64().T
@@ -274,7 +287,7 @@ class Model:
                     a = f16(a)
                 h = xx + a @ w["wo"].T
                 h2 = rmsnorm(h, L["g2"].astype(F64), S.eps, half)
-                act = silu(h2 @ w["gate"].T) * (h2 @ w["up"].T)
+                act = swiglu64(h2 @ w["gate"].T, h2 @ w["up"].T)
                 if half:
                     act = f16(act)
                 xn = h + act @ w["down"].T

@@ -99,7 +99,12 @@ def unpack(packed, bits, N, K):
     per = 32 // bits
     w = np.asarray(packed).reshape(N, K // per).astype(np.uint32, copy=False)
     sh = (bits * np.arange(per)).astype(np.uint32)
-    return ((w[:, :, None] >> sh) & np.uint32((1 << bits) - 1)).astype(np.uint8).reshape(N, K)
+    out = np.empty((N, K), np.uint8)
+
+    def block(r0, r1):
+        out[r0:r1] = ((w[r0:r1, :, None] >> sh) & np.uint32((1 << bits) - 1)).astype(np.uint8).reshape(r1 - r0, K)
+    parallel_rows(N, block)
+    return out
 
 
 def fma32(a, b, c):
@@ -129,11 +134,36 @@ def dequant(q, s16, b16, scale_dtype, group=64):
 
 
 def dequant64(q, s16, b16, scale_dtype, group=64):
-    """The exact (FP64) value of every weight: q*s + b with no rounding beyond float64 (the FP64 oracle's weights)."""
+    """The exact (FP64) value of every weight: q*s + b with no rounding beyond float64 (the FP64 oracle's weights).
+    Row blocks run on a thread pool (numpy's array kernels release the GIL)."""
     q = np.asarray(q)
-    s = np.repeat(from_16(s16, scale_dtype).astype(np.float64), group, axis=1)
-    b = np.repeat(from_16(b16, scale_dtype).astype(np.float64), group, axis=1)
-    return q.astype(np.float64) * s + b
+    N, K = q.shape
+    s = from_16(s16, scale_dtype).astype(np.float64)
+    b = from_16(b16, scale_dtype).astype(np.float64)
+    out = np.empty((N, K), np.float64)
+
+    def block(r0, r1):
+        w = q[r0:r1].reshape(r1 - r0, K // group, group).astype(np.float64)
+        w *= s[r0:r1, :, None]
+        w += b[r0:r1, :, None]
+        out[r0:r1] = w.reshape(r1 - r0, K)
+    parallel_rows(N, block)
+    return out
+
+
+_POOL = None
+
+
+def parallel_rows(n, fn, min_rows=64):
+    """fn(r0, r1) over row blocks of [0, n) on a thread pool of the host's cores (the oracle's elementwise work)."""
+    global _POOL
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    cores = os.cpu_count() or 1
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(cores)
+    step = max(min_rows, -(-n // (2 * cores)))
+    list(_POOL.map(lambda r0: fn(r0, min(n, r0 + step)), range(0, n, step)))
 
 
 def pack_bytes(N, K, bits, group=64):
