@@ -95,6 +95,8 @@ struct Params {
   float eps, qscale;
   uint64_t wait_ns;        // the bound on every wait (global timer)
   int rt_qkv, rt_d, nf, rt_v, gd, gk, gchunk, dn_rows, smax;
+  int o_per, o_sb;         // o_proj: row tiles a stage, and the byte stride of their scale/bias boxes (a TMA
+                           // destination starts on a 128-byte boundary)
   const CUtensorMap* maps;
   const __half* gains;     // [L][2][d]
   const __half* bias;      // [L][qkv rows] or null
@@ -316,16 +318,15 @@ __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
       // O: W_o columns of group j for the split's row tiles, one row tile a box, TPS / gk row tiles a stage
       int r0, r1;
       S.orows(P, s, &r0, &r1);
-      const int per = max(1, TPS / P.gk);
-      for (int r = r0; r < r1; r += per) {
+      for (int r = r0; r < r1; r += P.o_per) {
         uint8_t* st = pr.acquire(P);
         if (!st) return;
-        const int nr = min(per, r1 - r);
+        const int nr = min(P.o_per, r1 - r);
         const int TB = tile_b(BITS);
         mbar_arrive_expect_tx(&pr.full[pr.slot], static_cast<unsigned>(nr * P.gk * (TB + 64)));
         for (int q = 0; q < nr; ++q) {
           tma3(st + q * P.gk * TB, P.maps + mb + M_WO_W, 0, j * P.gk, r + q, &pr.full[pr.slot]);
-          tma3(st + kSbOff + q * P.gk * 64, P.maps + mb + M_WO_SB, 0, j * P.gk, r + q, &pr.full[pr.slot]);
+          tma3(st + kSbOff + q * P.o_sb, P.maps + mb + M_WO_SB, 0, j * P.gk, r + q, &pr.full[pr.slot]);
         }
         pr.advance();
       }
@@ -473,11 +474,12 @@ __device__ bool rows_batch(const Params& P, Cons& C, int n, const int* rt, const
   return !fail;
 }
 
-// A chunk of nr row tiles x gb groups (tile (q, g) at (q gb + g) TB, scale/bias at kSbOff + (q gb + g) 64): warp w
-// owns row tiles w, w + 16, ... entirely; `emit(q, row, value)` gets the value of row `row` (0..15) of row tile q from
-// the lanes that hold it (c4 == 0).
+// A chunk of nr row tiles x gb groups (tile (q, g) at (q gb + g) TB, scale/bias at kSbOff + q sb_stride + 64 g):
+// warp w owns row tiles w, w + 16, ... entirely; `emit(q, row, value)` gets the value of row `row` (0..15) of row tile
+// q from the lanes that hold it (c4 == 0).
 template <int BITS, typename Emit>
-__device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, uint32_t xs_addr, uint32_t xsum_addr, Emit emit) {
+__device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_stride, uint32_t xs_addr,
+                            uint32_t xsum_addr, Emit emit) {
   constexpr int TB = BITS == 4 ? 512 : 1024;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r8 = lane >> 2, c4 = lane & 3;
@@ -488,7 +490,7 @@ __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, uint32_t x
     for (int q = warp; q < nr; q += kConsumerWarps) {
       float ys[4] = {0.f, 0.f, 0.f, 0.f}, yb[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t aw = st + q * gb * TB + lane * 16;
-      uint32_t asb = st + kSbOff + q * gb * 64 + r8 * 8;
+      uint32_t asb = st + kSbOff + q * sb_stride + r8 * 8;
       uint32_t ax = xs_addr + c4 * 32;
       uint32_t axs = xsum_addr + c4 * 8;
       for (int g = 0; g < gb; ++g) {
@@ -906,10 +908,9 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           if (lane == 0) xsumo[g * 8] = sm;
         }
         consumer_sync();
-        const int per = max(1, TPS / P.gk);
-        for (int r = r0; r < r1 && ok; r += per) {
-          const int nr = min(per, r1 - r);
-          ok = owned_chunk<BITS>(P, C, nr, P.gk, smem_u32(xo), smem_u32(xsumo),
+        for (int r = r0; r < r1 && ok; r += P.o_per) {
+          const int nr = min(P.o_per, r1 - r);
+          ok = owned_chunk<BITS>(P, C, nr, P.gk, P.o_sb, smem_u32(xo), smem_u32(xsumo),
                                  [&](int q, int row, float v) { red_f32(acc_h + (r + q) * 16 + row, v); });
         }
         if (consumer_sync_or(!ok)) { ok = false; break; }
@@ -953,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
       // down: K slice f (one group) of every row tile, dn_rows row tiles a chunk
       for (int r = 0; r < P.rt_d && ok; r += P.dn_rows) {
         const int nr = min(P.dn_rows, P.rt_d - r);
-        ok = owned_chunk<BITS>(P, C, nr, 1, smem_u32(act), smem_u32(xsuma),
+        ok = owned_chunk<BITS>(P, C, nr, 1, 64, smem_u32(act), smem_u32(xsuma),
                                [&](int q, int row, float v) { red_f32(acc_x + (r + q) * 16 + row, v); });
       }
       if (consumer_sync_or(!ok)) { ok = false; break; }
@@ -1131,6 +1132,8 @@ int fstep_launch(const FstepArgs& a, cudaStream_t s) {
   p.gk = p.G * a.hd / 64;
   p.gchunk = std::min(p.gd, fstep::tps(a.bits));
   p.dn_rows = std::min(p.rt_d, fstep::tps(a.bits));
+  p.o_sb = (p.gk * 64 + 127) / 128 * 128;
+  p.o_per = std::max(1, std::min(fstep::tps(a.bits) / p.gk, (fstep::kStage - fstep::kSbOff) / p.o_sb));
   p.smax = a.smax;
   p.maps = a.maps; p.gains = a.gains; p.bias = a.bias; p.final_gain = a.final_gain; p.embed = a.embed;
   p.qkg = a.qkg; p.qkraw = a.qkraw;

@@ -147,7 +147,7 @@ def test_execute_report_keys(torch, fused):
     m = _build(dict(SMALL), bits=4)
     m.set_option("fused", fused)
     m.start(0, [1, 2, 3])
-    rep = execute.decode(m, 5)
+    rep = execute.decode(m, 5, env={})  # no AGXC_* options from the environment
     for key in ("out_ids", "tokens_per_s", "per_token_ms", "gpu_ms_per_token", "host_ms_per_token",
                 "dispatches_per_token", "batch"):
         assert key in rep
