@@ -20,9 +20,11 @@ agxforge/inference/assemble.py: configure 71-92, build 596-828; its region R and
     DecodeModel.start(b, prompt)  the sequence's prompt in its token log, x = embedding(prompt[0]), q0 = 0
     DecodeModel.decode(steps)     run steps (execute.decode wraps it in the reference's report)
 
-The layer is five kernels (RMSNorm+qkv+bias+RoPE+append, split-KV attention + merge, o_proj + residual,
-RMSNorm+gate/up+SiLU*mul, down + residual) and the head one (final norm + vocabulary GEMV + argmax + generation
-step); a whole step is one CUDA graph.
+At batch 1 on one device a whole step is one persistent kernel (the "fused" option): per layer RMSNorm + qkv + bias
++ RoPE + append, split-KV attention, the merge + o_proj + residual, RMSNorm + gate/up + SiLU*mul + down + residual,
+each CTA waiting only on the counters of the data it reads; then the final norm, the vocabulary GEMV, the argmax and
+the generation step. Otherwise (batch 2..8, or "fused" 0) the layer is five kernels (the same five stages) and the
+head one, and at 32..256 sequences the projections are tensor-core GEMMs; a whole step is one CUDA graph.
 """
 from __future__ import annotations
 
@@ -108,6 +110,9 @@ def hash_key(*key):
             h = ((h ^ ch) * 1099511628211) % (2 ** 64)
         h = ((h ^ 0xFF) * 1099511628211) % (2 ** 64)
     return h
+
+
+FUSED_TRACE_MARKS = 20   # the fused step's trace marks a layer (trace_fused)
 
 
 class DecodeModel:
@@ -205,9 +210,12 @@ class DecodeModel:
 
     def trace_fused(self):
         """The fused step's per-CTA marks of the last traced step (ns of the global timer, 0 = not reached): an array
-        [marks, CTAs]; per layer eight marks (qkv dependency met, qkv done, attention dependency met, attention done,
-        o_proj dependency met, o_proj done, FFN dependency met, FFN done), then the head's two."""
-        marks = 8 * self.shape.LAYERS + 2
+        [marks, CTAs]; per layer twenty marks (0 qkv dependency met, 1 qkv done, 2 attention dependency met,
+        3 attention done, 4 o_proj dependency met, 5 o_proj done, 6 FFN dependency met, 7 FFN done; 8 qkv input
+        normed, 9 first qkv row tile done, 10 attention keys done, 11 attention partials merged, 12 FFN input normed,
+        13 first gate/up batch done, 14 gate/up done, 15 first down chunk done; the producer's issue of 16 the first
+        qkv chunk, 17 the first attention chunk, 18 the first FFN chunk, 19 the last FFN chunk), then the head's two."""
+        marks = FUSED_TRACE_MARKS * self.shape.LAYERS + 2
         ctas = 256
         buf = (C.c_uint64 * (marks * ctas))()
         ph, ct = C.c_int32(), C.c_int32()

@@ -55,7 +55,11 @@ constexpr int kSbOff = 16384;         // the scale/bias part of a stage
 constexpr int kMaxRing = 12;
 constexpr int kKeyTile = 16;          // keys per MMA tile (M)
 constexpr int kMinKeys = 32;          // the fewest keys an attention split takes
-constexpr int kTraceMarks = 8;        // per layer: Q wait, Q done, A wait, A done, O wait, O done, F wait, F done
+// per layer: 0 Q dependency met, 1 Q done, 2 A dependency met, 3 A done, 4 O dependency met, 5 O done, 6 F dependency
+// met, 7 F done; within phases: 8 Q input normed, 9 Q first row tile done, 10 A keys done (before the CTA's merge),
+// 11 O partials merged, 12 F input normed, 13 F first gate/up batch done, 14 F gate/up done, 15 F first down chunk
+// done; the producer's issue times: 16 first Q chunk, 17 first A chunk, 18 first F chunk, 19 last F chunk
+constexpr int kTraceMarks = 20;
 
 // The maps of a model: per layer kMapsPerLayer, then the head's two and the caches' two.
 enum : int { M_QKV_W = 0, M_QKV_SB, M_WO_W, M_WO_SB, M_GU_W, M_GU_SB, M_DN_W, M_DN_SB, kMapsPerLayer };
@@ -219,6 +223,10 @@ __device__ bool wait_counter(const unsigned* c, unsigned target, const Params& P
 __device__ __forceinline__ void mark(const Params& P, int slot) {
   if (P.trace && threadIdx.x == 0) P.trace[static_cast<size_t>(slot) * gridDim.x + blockIdx.x] = globaltimer_ns();
 }
+// the producer's marks (its one issuing thread)
+__device__ __forceinline__ void pmark(const Params& P, int slot) {
+  if (P.trace) P.trace[static_cast<size_t>(slot) * gridDim.x + blockIdx.x] = globaltimer_ns();
+}
 
 // ------------------------------------------------------------------------------------------------ the schedule
 // Which work a CTA owns; the producer and the consumers enumerate it identically.
@@ -296,6 +304,7 @@ __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
   const CUtensorMap* vmap = kmap + 1;
   for (int l = 0; l < P.L && !*pr.dead; ++l) {
     const int mb = l * kMapsPerLayer;
+    pmark(P, l * kTraceMarks + 16);
     // Q: the CTA's qkv row tiles, each in row_chunks chunks of gchunk groups
     for (int t = c; t < P.rt_qkv; t += grid)
       for (int k = 0; k < nrc; ++k)
@@ -304,6 +313,7 @@ __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
     if (S.attn(P, c, &j, &s, &k0, &k1)) {
       // A: the key range in KC-key chunks (K and V rows of the group's KV head, 64-dim swizzled boxes)
       const int z = l * P.KVH + j;
+      pmark(P, l * kTraceMarks + 17);
       for (int a = k0; a < k1; a += KC) {
         uint8_t* st = pr.acquire(P);
         if (!st) return;
@@ -333,11 +343,13 @@ __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
     }
     // F: gate/up row tiles 8f .. 8f + 7 (four gate/up tile pairs), then down's K slice f for every row tile
     for (int f = c; f < P.nf; f += grid) {
+      pmark(P, l * kTraceMarks + 18);
       for (int t = 8 * f; t < 8 * f + 8; ++t)
         for (int k = 0; k < nrc; ++k)
           if (!pr.pack_chunk(P, mb + M_GU_W, k * P.gchunk, t, P.gchunk, 1)) return;
       for (int r = 0; r < P.rt_d; r += P.dn_rows)
         if (!pr.pack_chunk(P, mb + M_DN_W, f, r, 1, P.dn_rows)) return;
+      pmark(P, l * kTraceMarks + 19);
     }
   }
   // the head: a contiguous range of vocabulary row tiles
@@ -661,6 +673,7 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
     if (lane == 0) gemv::mbar_arrive(&C.empty[C.slot_of(i)]);
   }
   C.ci += nch;
+  mark(P, l * kTraceMarks + 10);
   // l over the warp's key rows (lanes with the same t4), then the CTA's combination: M = max over warps, each warp
   // adds its o scaled by 2^(m_w - M) into ov (shared-memory atomics)
 #pragma unroll
@@ -815,9 +828,11 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     }
     mark(P, l * kTraceMarks + 0);
     stage_norm(P, C, [&](int k) { return __half2float(x16k[k]); }, g1);
+    mark(P, l * kTraceMarks + 8);
     for (int t = c; t < P.rt_qkv && ok; t += grid) {
       for (int k = 0; k < nrc; ++k) { rts[k] = t; g0s[k] = k * P.gchunk; gbs[k] = min(P.gchunk, P.gd - k * P.gchunk); }
       if (!rows_batch<BITS>(P, C, nrc, rts, g0s, gbs, xs_a, xsum_a, uv)) { ok = false; break; }
+      if (t == c) mark(P, l * kTraceMarks + 9);
       // epilogue: 8 RoPE pairs (tile rows r, r + 8 = logical rows 8 tt + r, hd/2 + 8 tt + r of the head)
       if (tid < 8) {
         const int r = tid;
@@ -908,6 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           if (lane == 0) xsumo[g * 8] = sm;
         }
         consumer_sync();
+        mark(P, l * kTraceMarks + 11);
         for (int r = r0; r < r1 && ok; r += P.o_per) {
           const int nr = min(P.o_per, r1 - r);
           ok = owned_chunk<BITS>(P, C, nr, P.gk, P.o_sb, smem_u32(xo), smem_u32(xsumo),
@@ -927,6 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     for (int k = tid; k < P.d; k += kConsumers) hk[k] = __half2float(x16k[k]) + __ldcg(acc_h + k);
     consumer_sync();
     stage_norm(P, C, [&](int k) { return hk[k]; }, g2);
+    mark(P, l * kTraceMarks + 12);
     for (int f = c; f < P.nf && ok; f += grid) {
       // gate/up: row tiles 8f .. 8f + 7 (pairs: gate tile 2p, up tile 2p + 1), one batch per two pairs
       __half* act = reinterpret_cast<__half*>(smem + Lo.act);
@@ -942,6 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           act[(pb + pp) * 16 + r] = __float2half_rn(gemv::silu_f(g) * u);
         }
         consumer_sync();
+        if (f == c) mark(P, l * kTraceMarks + 13 + pb / 2);
       }
       if (!ok) break;
       float* xsuma = reinterpret_cast<float*>(smem + Lo.xsuma);
@@ -956,6 +974,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
         const int nr = min(P.dn_rows, P.rt_d - r);
         ok = owned_chunk<BITS>(P, C, nr, 1, 64, smem_u32(act), smem_u32(xsuma),
                                [&](int q, int row, float v) { red_f32(acc_x + (r + q) * 16 + row, v); });
+        if (r == 0 && f == c) mark(P, l * kTraceMarks + 15);
       }
       if (consumer_sync_or(!ok)) { ok = false; break; }
       if (tid == 0) {

@@ -6,8 +6,9 @@ Default workload (BASELINE config 3 at its headline point): InternLM2.5-1.8B-sha
 N(0, 0.02) weights, 4-bit affine group 64 with fp16 scale/bias), batch 1, a history of 1,792 - W positions (the KV
 cache rows filled on the device with seeded N(0, 1) fp16 values: throughput does not depend on their content), W
 warm-up steps, then K greedy decode steps at positions 1,792 .. 1,792+K-1. A step is one token: one CUDA-graph replay
-of the 121 kernels. Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB of KV per token against a 126 MB L2),
-so no flush is needed between steps.
+of the fused persistent step kernel (AGXC_FUSED=0 in the environment: the per-kernel path's 121 kernels). Inputs are
+far larger than L2 (0.96 GB of packs + 0.18 GB of KV per token against a 126 MB L2), so no flush is needed between
+steps.
 
     python bench.py --kernel-case ffn|qkv|wo|down|head|attn [--case-batch B]
         one launch of that kernel of the workload (after 3 warm-ups) through the C-ABI: the ncu capture case
@@ -27,7 +28,8 @@ One JSON line on rank 0:
                  algorithmic bytes per launch / its mean launch time, against the measured HBM copy bandwidth
   step_roofline  the whole step: (pack bytes + KV bytes read) per token x tokens/s, against the same peak
   cpu_baseline   the reference's CPU decode step (its QSim chain) as the numpy FP32 port in oracle/cpu_decode.py,
-                 timed on this host's cores on a bounded sample (a few layers + the head of one token, scaled)
+                 timed on this host's cores on a bounded sample (--cpu-tokens whole tokens: every layer, the head and
+                 the argmax)
   prefill        the same model's prefill section on a prompt of `history` tokens (device time, prompt tok/s)
 Multi-GPU (torchrun, --gpus N): configs 1-4 do not shard (replicas only): every rank decodes its own sequence on its
 own GPU, timing is the max over ranks, `value` sums the tokens of all ranks ("scaling": "weak").
@@ -215,7 +217,11 @@ def trace_fused_step(args, m, hist):
     tile to the last attention CTA passing its group's dependency; attn = attention work (slowest CTA); o_wait / o_proj
     = the same for the merge + o_proj; h_wait = to the last CTA passing the h dependency; ffn = the FFN work (slowest
     CTA); x_wait = from the last FFN unit to the last CTA passing the next layer's x dependency; layer = x-complete to
-    x-complete."""
+    x-complete. `timeline`: every mark of the layer (assemble.DecodeModel.trace_fused) as [median, max] over the CTAs
+    that reach it, µs after the layer's x-complete (the producer's marks may precede it: negative)."""
+    from agxforge.inference.assemble import FUSED_TRACE_MARKS as NM
+    names = ["q_dep", "q_done", "a_dep", "a_done", "o_dep", "o_done", "f_dep", "f_done", "q_normed", "q_tile1",
+             "a_keys", "o_merged", "f_normed", "f_gu1", "f_gu", "f_down1", "p_q", "p_a", "p_f", "p_f_last"]
     m.start(0, [1])
     m.fill_history(0, hist - args.warmup, seed=1792)
     m.decode(args.warmup, want_tokens=False)
@@ -223,21 +229,29 @@ def trace_fused_step(args, m, hist):
     m.decode(1, want_tokens=False)
     tr = m.trace_fused().astype(np.float64)
     m.close()
-    L = (tr.shape[0] - 2) // 8
-    rec = []
+    L = (tr.shape[0] - 2) // NM
+    rec, tl = [], []
     for l in range(2, L - 2):
-        b = 8 * l
+        b = NM * l
         mx = lambda k: tr[b + k][tr[b + k] > 0].max()   # noqa: E731
         mn = lambda k: tr[b + k][tr[b + k] > 0].min()   # noqa: E731
-        nxt = tr[b + 8][tr[b + 8] > 0].max()
+        nxt = tr[b + NM][tr[b + NM] > 0].max()
         rec.append(dict(qkv=mx(1) - mx(0), attn_wait=mx(2) - mx(1), attn=mx(3) - mx(2), o_wait=mx(4) - mx(3),
                         o_proj=mx(5) - mx(4), h_wait=mx(6) - mx(5), ffn=mx(7) - mx(6), x_wait=nxt - mx(7),
                         layer=nxt - mx(0), x_skew=mx(0) - mn(0)))
+        t0 = mx(0)
+        row = {}
+        for k, nm in enumerate(names):
+            v = tr[b + k][tr[b + k] > 0] - t0
+            row[nm] = (float(np.median(v)), float(v.max())) if v.size else (np.nan, np.nan)
+        tl.append(row)
     phases = {k: round(float(np.mean([r[k] for r in rec])) / 1e3, 2) for k in rec[0]}
-    head = tr[8 * L + 1][tr[8 * L + 1] > 0].max() - tr[8 * L][tr[8 * L] > 0].max()
-    step = tr[8 * L + 1][tr[8 * L + 1] > 0].max() - tr[0][tr[0] > 0].min()
+    timeline = {nm: [round(float(np.nanmean([r[nm][0] for r in tl])) / 1e3, 2),
+                     round(float(np.nanmean([r[nm][1] for r in tl])) / 1e3, 2)] for nm in names}
+    head = tr[NM * L + 1][tr[NM * L + 1] > 0].max() - tr[NM * L][tr[NM * L] > 0].max()
+    step = tr[NM * L + 1][tr[NM * L + 1] > 0].max() - tr[0][tr[0] > 0].min()
     print(json.dumps(dict(trace_step=args.config, fused=True, layers=L, step_us=round(step / 1e3, 1),
-                          head_us=round(head / 1e3, 2), phases=phases)), flush=True)
+                          head_us=round(head / 1e3, 2), phases=phases, timeline=timeline)), flush=True)
 
 
 def trace_step(args):
