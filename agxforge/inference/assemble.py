@@ -112,7 +112,11 @@ def hash_key(*key):
     return h
 
 
-FUSED_TRACE_MARKS = 20   # the fused step's trace marks a layer (trace_fused)
+FUSED_TRACE_MARKS = 26   # the fused step's trace marks a layer (trace_fused)
+# the fused step's cycle-profile regions, in the library's order (profile_fused); "" = unused
+FUSED_PROFILE_REGIONS = ["top", "preload", "wait", "act_load", "norm", "rows", "rows_reduce", "qkv_epilogue",
+                         "signal", "attn_q", "attn_keys", "attn_merge", "attn_out", "o_merge", "owned", "silu",
+                         "head_argmax", "tail", "owned_wait", "rows_wait", "attn_wait", "", "", ""]
 
 
 class DecodeModel:
@@ -208,20 +212,31 @@ class DecodeModel:
         """True when decode steps run as the fused persistent kernel."""
         return bool(self.plan_info()["fused"]["on"])
 
-    def trace_fused(self):
-        """The fused step's per-CTA marks of the last traced step (ns of the global timer, 0 = not reached): an array
-        [marks, CTAs]; per layer twenty marks (0 qkv dependency met, 1 qkv done, 2 attention dependency met,
-        3 attention done, 4 o_proj dependency met, 5 o_proj done, 6 FFN dependency met, 7 FFN done; 8 qkv input
-        normed, 9 first qkv row tile done, 10 attention keys done, 11 attention partials merged, 12 FFN input normed,
-        13 first gate/up batch done, 14 gate/up done, 15 first down chunk done; the producer's issue of 16 the first
-        qkv chunk, 17 the first attention chunk, 18 the first FFN chunk, 19 the last FFN chunk), then the head's two."""
-        marks = FUSED_TRACE_MARKS * self.shape.LAYERS + 2
+    def _trace_fused_rows(self):
+        rows = FUSED_TRACE_MARKS * self.shape.LAYERS + 2 + len(FUSED_PROFILE_REGIONS)
         ctas = 256
-        buf = (C.c_uint64 * (marks * ctas))()
+        buf = (C.c_uint64 * (rows * ctas))()
         ph, ct = C.c_int32(), C.c_int32()
-        N.check(N.lib().agxc_model_trace_cta_read(self._h, buf, marks * ctas, C.byref(ph), C.byref(ct)),
+        N.check(N.lib().agxc_model_trace_cta_read(self._h, buf, rows * ctas, C.byref(ph), C.byref(ct)),
                 "trace_cta_read")
         return np.frombuffer(buf, np.uint64)[: ph.value * ct.value].reshape(ph.value, ct.value).copy()
+
+    def trace_fused(self):
+        """The fused step's per-CTA marks of the last traced step (ns of the global timer, 0 = not reached): an array
+        [marks, CTAs]; per layer twenty-six marks (0 qkv dependency met, 1 qkv done, 2 attention dependency met,
+        3 attention done, 4 o_proj dependency met, 5 o_proj done, 6 FFN dependency met, 7 FFN done; 8 qkv input
+        normed, 9 qkv tiles done, 10 attention keys done, 11 attention partials merged, 12 FFN input normed,
+        13 first gate/up batch done, 14 gate/up done, 15 first down chunk done; the producer: 16 first qkv chunk
+        issued, 17 attention chunks begin, 18 first FFN chunk issued, 19 last FFN chunk issued; 20 / 21 the qkv
+        batch's first chunk landed / consumer thread 0's share done, 22 / 23 the same for the first gate/up batch, 24
+        the second gate/up batch's first chunk landed, 25 the first down chunk issued), then the head's two."""
+        return self._trace_fused_rows()[: FUSED_TRACE_MARKS * self.shape.LAYERS + 2]
+
+    def profile_fused(self):
+        """The fused step's cycle profile of the last traced step: {region: per-CTA SM cycles of consumer thread 0}
+        (FUSED_PROFILE_REGIONS; thread 0 passes every consumer barrier, so the regions partition the CTA's time)."""
+        tr = self._trace_fused_rows()[FUSED_TRACE_MARKS * self.shape.LAYERS + 2:]
+        return {name: tr[k].astype(np.float64) for k, name in enumerate(FUSED_PROFILE_REGIONS) if name}
 
     def trace(self):
         """The launch trace since tracing started or the last call, then reset: one dict per launch of the step (in

@@ -48,7 +48,11 @@ using gemv::consumer_sync_or;
 using gemv::group_step;
 using gemv::kConsumers;
 using gemv::kConsumerWarps;
-using gemv::kThreads;
+// 16 consumer warps, the producer warp, and the signal warp: it performs the consumers' release counts (a gpu-scope
+// release waits for the CTA's earlier writes to reach L2, ~1 us), so the consumers go on at once
+constexpr int kThreads = gemv::kConsumers + 64;
+constexpr int kSignalWarp = kConsumerWarps + 1;
+constexpr int kSigSlots = 16;
 
 constexpr int kStage = 18432;         // one ring stage: 16 KB of weight tiles (or K/V rows) + 2 KB of scale/bias
 constexpr int kSbOff = 16384;         // the scale/bias part of a stage
@@ -58,11 +62,16 @@ constexpr int kMinKeys = 32;          // the fewest keys an attention split take
 // per layer: 0 Q dependency met, 1 Q done, 2 A dependency met, 3 A done, 4 O dependency met, 5 O done, 6 F dependency
 // met, 7 F done; within phases: 8 Q input normed, 9 Q first row tile done, 10 A keys done (before the CTA's merge),
 // 11 O partials merged, 12 F input normed, 13 F first gate/up batch done, 14 F gate/up done, 15 F first down chunk
-// done; the producer's issue times: 16 first Q chunk, 17 first A chunk, 18 first F chunk, 19 last F chunk
-constexpr int kTraceMarks = 20;
+// done; the producer: 16 first Q chunk issued, 17 A chunks begin, 18 first F chunk issued, 19 last F chunk issued;
+// 20 / 21 the first qkv tile's chunk landed / thread 0's share done, 22 / 23 the same for the first gate/up batch,
+// 24 the second gate/up batch's first chunk landed, 25 the producer's first down chunk issued
+constexpr int kTraceMarks = 26;
 
-// The maps of a model: per layer kMapsPerLayer, then the head's two and the caches' two.
-enum : int { M_QKV_W = 0, M_QKV_SB, M_WO_W, M_WO_SB, M_GU_W, M_GU_SB, M_DN_W, M_DN_SB, kMapsPerLayer };
+// The maps of a model: one 4-D map (the pack's 3-D tile grid x the layer) per role of the layer, then the head's two
+// and the caches' two. Few descriptors: the TMA unit keeps them cached instead of fetching one from memory for every
+// copy (per-layer maps, 8 a layer, cost a descriptor fetch nearly every copy).
+enum : int { M_QKV_W = 0, M_QKV_SB, M_WO_W, M_WO_SB, M_GU_W, M_GU_SB, M_DN_W, M_DN_SB, M_HEAD_W, M_HEAD_SB, M_K, M_V,
+             kMaps };
 
 __host__ __device__ inline int tps(int bits) { return bits == 4 ? 32 : 16; }          // tiles per stage
 __host__ __device__ inline int tile_b(int bits) { return bits == 4 ? 512 : 1024; }
@@ -87,7 +96,7 @@ __host__ __device__ inline Layout smem_layout(int d, int kattn, int stages) {
   L.xsuma = o; o += 128;
   L.red = o; o += kConsumerWarps * 16 * 4 * 2;            // per-warp partial rows
   L.ov = o; o += (kattn * 4 + 127) / 128 * 128;           // attention: the CTA's o accumulator [G][hd]
-  L.om = o; o += kConsumerWarps * 8 * 2 * 4;              // attention: per-warp (m, l) per head
+  L.om = o; o += kConsumerWarps * 8 * 2 * 4 + 64;         // attention: per-warp (m, l) per head, then M, L per head
   L.kn = o; o += 256;                                     // QK-norm: the group's new k row (fp16, head_dim <= 128)
   L.misc = o; o += 1024;
   L.total = o;
@@ -137,11 +146,39 @@ __device__ __forceinline__ unsigned ld_acq(const unsigned* p) {
 __device__ __forceinline__ void red_rel(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+
+// The consumers' release counts, handed to the signal warp: thread 0 posts (counter, value) after a consumer barrier
+// (the mbarrier arrive is a CTA-scope release, the signal warp's wait a CTA-scope acquire, and its gpu-scope release
+// count is cumulative over the consumers' writes). A null counter ends the queue.
+struct SigQueue {
+  unsigned* addr[kSigSlots];
+  unsigned val[kSigSlots];
+  uint64_t full[kSigSlots], empty[kSigSlots];
+};
 __device__ __forceinline__ void red_f32(float* p, float v) {
   asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, unsigned cnt) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(cnt) : "memory");
+}
+__device__ __forceinline__ void tma4(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+// L2 prefetches of a box (no shared memory, no barrier): the weights and history a CTA will load later are brought
+// from HBM into L2 ahead of time, so HBM keeps streaming while the CTAs wait on each other.
+__device__ __forceinline__ void pf4(const CUtensorMap* map, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void pf3(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z)
+               : "memory");
 }
 __device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
@@ -163,6 +200,12 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t a) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
   return d;
 }
+// 2^x by the SFU (ex2.approx.ftz: relative error about 2^-22; -inf -> 0), as the reference's hardware exp2
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   uint32_t u;
@@ -180,8 +223,8 @@ __device__ __forceinline__ bool aborted(const Params& P) {
 __device__ __forceinline__ void raise_abort(const Params& P, unsigned bits) { atomicOr(P.err, bits | kErrAbort); }
 
 // A bounded mbarrier wait that also leaves when the launch aborted.
-__device__ bool mbar_wait_abortable(uint64_t* bar, unsigned parity, const Params& P) {
-  if (mbar_try_wait(bar, parity)) return true;
+// The slow path of a wait, out of line (one copy, off the hot path's instruction footprint).
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, unsigned parity, const Params& P) {
   const uint64_t t0 = globaltimer_ns();
   for (unsigned it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -193,6 +236,9 @@ __device__ bool mbar_wait_abortable(uint64_t* bar, unsigned parity, const Params
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, unsigned parity, const Params& P) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, P);
 }
 
 // Thread 0 of the consumers polls a counter until it reaches `target` (bounded, abortable); then every consumer
@@ -226,6 +272,41 @@ __device__ __forceinline__ void mark(const Params& P, int slot) {
 // the producer's marks (its one issuing thread)
 __device__ __forceinline__ void pmark(const Params& P, int slot) {
   if (P.trace) P.trace[static_cast<size_t>(slot) * gridDim.x + blockIdx.x] = globaltimer_ns();
+}
+
+// The cycle profile (when tracing): consumer thread 0's SM cycles, accumulated per region over the step and written
+// after the marks as kProfRegions rows [region][CTA]. prof(P, k) closes the current interval into region k. Thread 0
+// passes every consumer barrier, so its time line is the CTA's.
+enum : int {
+  R_TOP = 0, R_PRELOAD, R_WAIT, R_ACTLOAD, R_NORM, R_ROWS, R_REDUCE, R_QKV_EPI, R_SIGNAL, R_ATTN_Q, R_ATTN_KEYS,
+  R_ATTN_MERGE, R_ATTN_OUT, R_O_MERGE, R_OWNED, R_SILU, R_HEAD, R_TAIL, R_OWNED_WAIT, R_ROWS_WAIT, R_ATTN_WAIT,
+  kProfRegions = 24
+};
+__device__ __forceinline__ long long* prof_acc() {
+  __shared__ long long a[kProfRegions + 1];  // [regions], then the interval's start
+  return a;
+}
+__device__ __forceinline__ void prof(const Params& P, int k) {
+  if (P.trace && threadIdx.x == 0) {
+    long long* a = prof_acc();
+    const long long t = clock64();
+    a[k] += t - a[kProfRegions];
+    a[kProfRegions] = t;
+  }
+}
+__device__ __forceinline__ void prof_begin(const Params& P) {
+  if (P.trace && threadIdx.x == 0) {
+    long long* a = prof_acc();
+    for (int k = 0; k < kProfRegions; ++k) a[k] = 0;
+    a[kProfRegions] = clock64();
+  }
+}
+__device__ __forceinline__ void prof_end(const Params& P) {
+  if (P.trace && threadIdx.x == 0) {
+    const long long* a = prof_acc();
+    for (int k = 0; k < kProfRegions; ++k)
+      P.trace[static_cast<size_t>(P.L * kTraceMarks + 2 + k) * gridDim.x + blockIdx.x] = static_cast<unsigned long long>(a[k]);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ the schedule
@@ -280,40 +361,121 @@ struct Prod {
     ++issued;
     if (++slot == stages) { slot = 0; phase ^= 1; }
   }
-  // one box of (gb groups x rb row tiles) of a pack (weights and scale/bias maps), into one stage; gb and rb are the
-  // maps' box dimensions (a box reaching past the pack's groups or row tiles still lands whole, zero-filled)
-  __device__ bool pack_chunk(const Params& P, int mw, int g0, int rt, int gb, int rb) {
+  // one box of (gb groups x rb row tiles) of layer l's pack (weights and scale/bias maps; l < 0: the head's 3-D
+  // maps), into one stage; gb and rb are the maps' box dimensions (a box reaching past the pack's groups or row tiles
+  // still lands whole, zero-filled)
+  __device__ bool pack_chunk(const Params& P, int mw, int l, int g0, int rt, int gb, int rb) {
     uint8_t* st = acquire(P);
     if (!st) return false;
     const int TB = tile_b(P.bits);
     mbar_arrive_expect_tx(&full[slot], static_cast<unsigned>(gb * rb * (TB + 64)));
-    tma3(st, P.maps + mw, 0, g0, rt, &full[slot]);
-    tma3(st + kSbOff, P.maps + mw + 1, 0, g0, rt, &full[slot]);
+    if (l >= 0) {
+      tma4(st, P.maps + mw, 0, g0, rt, l, &full[slot]);
+      tma4(st + kSbOff, P.maps + mw + 1, 0, g0, rt, l, &full[slot]);
+    } else {
+      tma3(st, P.maps + mw, 0, g0, rt, &full[slot]);
+      tma3(st + kSbOff, P.maps + mw + 1, 0, g0, rt, &full[slot]);
+    }
     advance();
     return true;
+  }
+};
+
+// The producer's L2 prefetches mirror its loads one layer ahead: layer l + 1's boxes of a phase are prefetched when
+// the same phase of layer l is issued, the head's first rows during the last FFN phase and then kHeadAhead row tiles
+// ahead, and layer 0's boxes (of the next step) after the head.
+constexpr int kHeadAhead = 12;
+struct Prefetch {
+  const Params& P;
+  int c, grid, nrc, KC, HD;
+  __device__ void q(int l) const {
+    #pragma unroll 1
+    for (int t = c; t < P.rt_qkv; t += grid)
+      #pragma unroll 1
+      for (int k = 0; k < nrc; ++k) {
+        pf4(P.maps + M_QKV_W, 0, k * P.gchunk, t, l);
+        pf4(P.maps + M_QKV_SB, 0, k * P.gchunk, t, l);
+      }
+  }
+  __device__ void a(int l, int j, int k0, int k1) const {
+    const int z = l * P.KVH + j;
+    #pragma unroll 1
+    for (int a = k0; a < k1; a += KC)
+      #pragma unroll 1
+      for (int h = 0; h < HD / 64; ++h) {
+        pf3(P.maps + M_K, h * 64, a, z);
+        pf3(P.maps + M_V, h * 64, a, z);
+      }
+  }
+  __device__ void o(int l, int j, int r0, int r1) const {
+    #pragma unroll 1
+    for (int r = r0; r < r1; ++r) {
+      pf4(P.maps + M_WO_W, 0, j * P.gk, r, l);
+      pf4(P.maps + M_WO_SB, 0, j * P.gk, r, l);
+    }
+  }
+  __device__ void f(int l) const {
+    #pragma unroll 1
+    for (int f = c; f < P.nf; f += grid) {
+      #pragma unroll 1
+      for (int t = 8 * f; t < 8 * f + 8; ++t)
+        #pragma unroll 1
+        for (int k = 0; k < nrc; ++k) {
+          pf4(P.maps + M_GU_W, 0, k * P.gchunk, t, l);
+          pf4(P.maps + M_GU_SB, 0, k * P.gchunk, t, l);
+        }
+      #pragma unroll 1
+      for (int r = 0; r < P.rt_d; r += P.dn_rows) {
+        pf4(P.maps + M_DN_W, 0, f, r, l);
+        pf4(P.maps + M_DN_SB, 0, f, r, l);
+      }
+    }
+  }
+  __device__ void head(int t0, int t1) const {
+    #pragma unroll 1
+    for (int t = t0; t < t1; ++t)
+      #pragma unroll 1
+      for (int k = 0; k < nrc; ++k) {
+        pf3(P.maps + M_HEAD_W, 0, k * P.gchunk, t);
+        pf3(P.maps + M_HEAD_SB, 0, k * P.gchunk, t);
+      }
   }
 };
 
 template <int BITS, int HD>
 __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
   const int c = blockIdx.x, grid = gridDim.x;
-  const int TPS = tps(BITS);
   const int nrc = row_chunks(P);
   const int KC = kv_keys(P);
-  const CUtensorMap* kmap = P.maps + P.L * kMapsPerLayer + 2;
-  const CUtensorMap* vmap = kmap + 1;
+  const CUtensorMap* kmap = P.maps + M_K;
+  const CUtensorMap* vmap = P.maps + M_V;
+  #pragma unroll 1
+  for (int i = 0; i < kMaps; ++i)  // every descriptor of the step into the TMA unit's cache up front
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(P.maps + i)) : "memory");
+  const Prefetch pf{P, c, grid, nrc, KC, HD};
+  int j, s, k0, k1, r0 = 0, r1 = 0;
+  const bool has_attn = S.attn(P, c, &j, &s, &k0, &k1);
+  if (has_attn) S.orows(P, s, &r0, &r1);
+  const int h0 = static_cast<int>(static_cast<long long>(c) * P.rt_v / grid);
+  const int h1 = static_cast<int>(static_cast<long long>(c + 1) * P.rt_v / grid);
+  #pragma unroll 1
   for (int l = 0; l < P.L && !*pr.dead; ++l) {
-    const int mb = l * kMapsPerLayer;
-    pmark(P, l * kTraceMarks + 16);
+    const bool next = l + 1 < P.L;
     // Q: the CTA's qkv row tiles, each in row_chunks chunks of gchunk groups
+    if (next) pf.q(l + 1);
+    #pragma unroll 1
     for (int t = c; t < P.rt_qkv; t += grid)
-      for (int k = 0; k < nrc; ++k)
-        if (!pr.pack_chunk(P, mb + M_QKV_W, k * P.gchunk, t, P.gchunk, 1)) return;
-    int j, s, k0, k1;
-    if (S.attn(P, c, &j, &s, &k0, &k1)) {
+      #pragma unroll 1
+      for (int k = 0; k < nrc; ++k) {
+        if (!pr.pack_chunk(P, M_QKV_W, l, k * P.gchunk, t, P.gchunk, 1)) return;
+        if (t == c && k == 0) pmark(P, l * kTraceMarks + 16);
+      }
+    if (has_attn) {
       // A: the key range in KC-key chunks (K and V rows of the group's KV head, 64-dim swizzled boxes)
       const int z = l * P.KVH + j;
+      if (next) pf.a(l + 1, j, k0, k1);
       pmark(P, l * kTraceMarks + 17);
+      #pragma unroll 1
       for (int a = k0; a < k1; a += KC) {
         uint8_t* st = pr.acquire(P);
         if (!st) return;
@@ -326,39 +488,57 @@ __device__ void produce(const Params& P, const Sched& S, Prod& pr) {
         pr.advance();
       }
       // O: W_o columns of group j for the split's row tiles, one row tile a box, TPS / gk row tiles a stage
-      int r0, r1;
-      S.orows(P, s, &r0, &r1);
+      if (next) pf.o(l + 1, j, r0, r1);
+      #pragma unroll 1
       for (int r = r0; r < r1; r += P.o_per) {
         uint8_t* st = pr.acquire(P);
         if (!st) return;
         const int nr = min(P.o_per, r1 - r);
         const int TB = tile_b(BITS);
         mbar_arrive_expect_tx(&pr.full[pr.slot], static_cast<unsigned>(nr * P.gk * (TB + 64)));
+        #pragma unroll 1
         for (int q = 0; q < nr; ++q) {
-          tma3(st + q * P.gk * TB, P.maps + mb + M_WO_W, 0, j * P.gk, r + q, &pr.full[pr.slot]);
-          tma3(st + kSbOff + q * P.o_sb, P.maps + mb + M_WO_SB, 0, j * P.gk, r + q, &pr.full[pr.slot]);
+          tma4(st + q * P.gk * TB, P.maps + M_WO_W, 0, j * P.gk, r + q, l, &pr.full[pr.slot]);
+          tma4(st + kSbOff + q * P.o_sb, P.maps + M_WO_SB, 0, j * P.gk, r + q, l, &pr.full[pr.slot]);
         }
         pr.advance();
       }
     }
     // F: gate/up row tiles 8f .. 8f + 7 (four gate/up tile pairs), then down's K slice f for every row tile
+    if (next) pf.f(l + 1);
+    else pf.head(h0, min(h1, h0 + kHeadAhead));
+    #pragma unroll 1
     for (int f = c; f < P.nf; f += grid) {
-      pmark(P, l * kTraceMarks + 18);
+      #pragma unroll 1
       for (int t = 8 * f; t < 8 * f + 8; ++t)
-        for (int k = 0; k < nrc; ++k)
-          if (!pr.pack_chunk(P, mb + M_GU_W, k * P.gchunk, t, P.gchunk, 1)) return;
-      for (int r = 0; r < P.rt_d; r += P.dn_rows)
-        if (!pr.pack_chunk(P, mb + M_DN_W, f, r, 1, P.dn_rows)) return;
-      pmark(P, l * kTraceMarks + 19);
+        #pragma unroll 1
+        for (int k = 0; k < nrc; ++k) {
+          if (!pr.pack_chunk(P, M_GU_W, l, k * P.gchunk, t, P.gchunk, 1)) return;
+          if (f == c && t == 8 * f && k == 0) pmark(P, l * kTraceMarks + 18);
+        }
+      #pragma unroll 1
+      for (int r = 0; r < P.rt_d; r += P.dn_rows) {
+        if (!pr.pack_chunk(P, M_DN_W, l, f, r, 1, P.dn_rows)) return;
+        if (f == c && r == 0) pmark(P, l * kTraceMarks + 25);
+      }
+      if (f == c) pmark(P, l * kTraceMarks + 19);
     }
   }
   // the head: a contiguous range of vocabulary row tiles
-  const int hm = P.L * kMapsPerLayer;
-  const int h0 = static_cast<int>(static_cast<long long>(c) * P.rt_v / grid);
-  const int h1 = static_cast<int>(static_cast<long long>(c + 1) * P.rt_v / grid);
-  for (int t = h0; t < h1; ++t)
+  #pragma unroll 1
+  for (int t = h0; t < h1; ++t) {
+    if (t + kHeadAhead < h1) pf.head(t + kHeadAhead, t + kHeadAhead + 1);
+    #pragma unroll 1
     for (int k = 0; k < nrc; ++k)
-      if (!pr.pack_chunk(P, hm, k * P.gchunk, t, P.gchunk, 1)) return;
+      if (!pr.pack_chunk(P, M_HEAD_W, -1, k * P.gchunk, t, P.gchunk, 1)) return;
+  }
+  // the next step's first layer (the same schedule: its keys reach one position further)
+  pf.q(0);
+  if (has_attn) {
+    pf.a(0, j, k0, k1);
+    pf.o(0, j, r0, r1);
+  }
+  pf.f(0);
 }
 
 // ------------------------------------------------------------------------------------------------ consumers
@@ -370,16 +550,35 @@ struct Cons {
   volatile int* flag;     // wait_counter's broadcast
   volatile int* dead;     // a wait gave up (CTA-wide, read after a consumer barrier)
   int stages;
-  long ci = 0;            // chunks consumed (the same in every consumer warp)
-  __device__ int slot_of(long i) const { return static_cast<int>(i % stages); }
-  __device__ unsigned par_of(long i) const { return static_cast<unsigned>((i / stages) & 1); }
-  __device__ uint32_t stage_addr(long i) const { return smem_u32(smem + Lo.ring + slot_of(i) * kStage); }
+  // the next chunk's stage and its full-barrier parity (the same in every consumer warp), advanced by increments:
+  // no division per chunk
+  int slot = 0;
+  unsigned phase = 0;
+  __device__ uint32_t stage_addr(int sl) const { return smem_u32(smem + Lo.ring + sl * kStage); }
+  __device__ void step(int& sl, unsigned& ph) const {
+    if (++sl == stages) {
+      sl = 0;
+      ph ^= 1u;
+    }
+  }
 };
 
-// Stage one row v[0..d) (fp32 values in shared memory or given by `get`) normed with gain g into xs (fp16) and its
-// per-group sums (xsum[g * 8]): y = fp16(v * r * g), r = rsqrt(mean(v^2) + eps) (norm.py:185-203's rounding point).
-template <typename Get>
-__device__ void stage_norm(const Params& P, Cons& C, Get get, const __half* g) {
+// A norm gain's 8-element slices k = tid, tid + 512, ... of this consumer thread (kNormSlices at most: d <= 8192),
+// loaded ahead of the dependency wait that precedes the norm.
+constexpr int kNormSlices = 2;
+__device__ __forceinline__ void norm_gains(const Params& P, const __half* g, uint4* out) {
+#pragma unroll
+  for (int i = 0; i < kNormSlices; ++i) {
+    const int k = threadIdx.x + i * kConsumers;
+    out[i] = k < P.d / 8 ? __ldg(reinterpret_cast<const uint4*>(g) + k) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Stage one row v[0..d) (fp32 values in shared memory or given by `get`) normed with gain g (this thread's slices,
+// norm_gains) into xs (fp16) and its per-group sums (xsum[g * 8]): y = fp16(v * r * g), r = rsqrt(mean(v^2) + eps)
+// (norm.py:185-203's rounding point).
+__device__ void stage_norm(const Params& P, Cons& C, const __half* xh, const float* xf, const uint4* gpre) {
+  auto get = [&](int k) { return xh ? __half2float(xh[k]) : xf[k]; };
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __half* xs = reinterpret_cast<__half*>(C.smem + C.Lo.xs);
   float* xsum = reinterpret_cast<float*>(C.smem + C.Lo.xsum);
@@ -399,12 +598,14 @@ __device__ void stage_norm(const Params& P, Cons& C, Get get, const __half* g) {
 #pragma unroll
   for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
   const float r = rsqrtf(tot / static_cast<float>(P.d) + P.eps);
-  for (int base = 0; base < n8; base += kConsumers) {  // the same trip count in every thread (shuffles below)
-    const int k = base + tid;
+#pragma unroll
+  for (int i = 0; i < kNormSlices; ++i) {  // the same trip count in every thread (shuffles below)
+    const int k = i * kConsumers + tid;
+    if (i * kConsumers >= n8) break;
     const bool live = k < n8;
     float sum = 0.f;
     if (live) {
-      const uint4 gu = __ldg(reinterpret_cast<const uint4*>(g) + k);
+      const uint4 gu = gpre[i];
       __half2 gh[4];
       memcpy(gh, &gu, 16);
       __half2 oh[4];
@@ -427,15 +628,19 @@ __device__ void stage_norm(const Params& P, Cons& C, Get get, const __half* g) {
   consumer_sync();
 }
 
-// A batch of n chunks (n <= stages), chunk k = one row tile rows[k] over `gb` groups starting at group g0s[k] of the
-// staged input (xs, xsum). Warp w works on chunk w % n (groups w / n, w / n + warps_k, ...); every warp waits for
-// every chunk of the batch in order and releases it (the ring's rule: no release before the chunk landed). The
-// per-row-tile sums over the warps land in uv[k][16] (shared), all consumer threads synchronised. Returns false if a
-// wait gave up.
+// A batch of n chunks (n <= stages): chunk k is row tile rt0 + (k / nrc) * rts over groups g0 = (k % nrc) gchunk ..
+// g0 + min(gchunk, gd - g0) of the staged input (xs, xsum) — the layout of the producer's pack_chunk sequence; the
+// batch is described arithmetically, not by per-thread arrays (which would live in local memory, behind L1 misses
+// to L2). Warp w works on chunk w % n (groups w / n, w / n + warps_k, ...); every warp waits for every chunk of the
+// batch in order and releases it (the ring's rule: no release before the chunk landed). The per-row-tile sums over
+// the warps land in uv[first chunk of the tile][16] (shared; 0 for a tile's other chunks), all consumer threads
+// synchronised. Returns false if a wait gave up.
 template <int BITS>
-__device__ bool rows_batch(const Params& P, Cons& C, int n, const int* rt, const int* g0s, const int* gbs,
-                           uint32_t xs_addr, uint32_t xsum_addr, float* uv) {
+__device__ bool rows_batch(const Params& P, Cons& C, int n, int nrc, int rt0, int rts, uint32_t xs_addr,
+                           uint32_t xsum_addr, float* uv, int mk = -1) {
   constexpr int TB = BITS == 4 ? 512 : 1024;
+  (void)rt0;
+  (void)rts;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r8 = lane >> 2, c4 = lane & 3;
   const int k = warp % n, sub = warp / n;
@@ -443,17 +648,23 @@ __device__ bool rows_batch(const Params& P, Cons& C, int n, const int* rt, const
   float* red = reinterpret_cast<float*>(C.smem + C.Lo.red);
   float ys[4] = {0.f, 0.f, 0.f, 0.f}, yb[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
-  for (int q = 0; q < n; ++q) {
-    const long i = C.ci + q;
-    if (ok && !mbar_wait_abortable(&C.full[C.slot_of(i)], C.par_of(i), P)) ok = false;
+  const int g0k = (k % nrc) * P.gchunk;
+  const int gbk = min(P.gchunk, P.gd - g0k);
+  int sl = C.slot;
+  unsigned ph = C.phase;
+  for (int q = 0; q < n; ++q, C.step(sl, ph)) {
+    prof(P, R_ROWS);
+    if (ok && !mbar_wait_abortable(&C.full[sl], ph, P)) ok = false;
+    prof(P, R_ROWS_WAIT);
+    if (q == 0 && mk >= 0) mark(P, mk);
     if (ok && q == k) {
-      const uint32_t st = C.stage_addr(i);
-      const int gb = gbs[k];
+      const uint32_t st = C.stage_addr(sl);
       uint32_t aw = st + sub * TB + lane * 16;
       uint32_t asb = st + kSbOff + sub * 64 + r8 * 8;
-      uint32_t ax = xs_addr + (g0s[k] + sub) * 128 + c4 * 32;
-      uint32_t axs = xsum_addr + (g0s[k] + sub) * 32 + c4 * 8;
-      for (int g = sub; g < gb; g += wk) {
+      uint32_t ax = xs_addr + (g0k + sub) * 128 + c4 * 32;
+      uint32_t axs = xsum_addr + (g0k + sub) * 32 + c4 * 8;
+#pragma unroll 1
+      for (int g = sub; g < gbk; g += wk) {
         group_step<BITS, 1>(aw, asb, ax, axs, P.sdt, ys, yb);
         aw += wk * TB;
         asb += wk * 64;
@@ -462,49 +673,53 @@ __device__ bool rows_batch(const Params& P, Cons& C, int n, const int* rt, const
       }
     }
     __syncwarp();
-    if (lane == 0) gemv::mbar_arrive(&C.empty[C.slot_of(i)]);
+    if (lane == 0) gemv::mbar_arrive(&C.empty[sl]);
   }
-  C.ci += n;
+  C.slot = sl;
+  C.phase = ph;
+  prof(P, R_ROWS);
+  if (mk >= 0 && mk != 24) mark(P, mk + 1);
   if (c4 == 0) {
     red[warp * 16 + r8] = fmaf(ys[0], gemv::k2p24, yb[0]);
     red[warp * 16 + r8 + 8] = fmaf(ys[2], gemv::k2p24, yb[2]);
   }
   const bool fail = consumer_sync_or(!ok);
-  // the sum over the warps of each row tile (chunks of one row tile may be several: same rt)
+  // the sum over the warps of each row tile (the warps of all nrc chunks of the tile)
   for (int t = tid; t < n * 16; t += kConsumers) {
     const int kk = t / 16, r = t % 16;
     float s = 0.f;
-    if (kk == 0 || rt[kk] != rt[kk - 1]) {
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const int kw = w % n;
-        if (rt[kw] == rt[kk]) s += red[w * 16 + r];
-      }
-    }
+    if (kk % nrc == 0)
+      for (int w = 0; w < kConsumerWarps; ++w)
+        if ((w % n) / nrc == kk / nrc) s += red[w * 16 + r];
     uv[t] = s;
   }
   consumer_sync();
+  prof(P, R_REDUCE);
   return !fail;
 }
 
 // A chunk of nr row tiles x gb groups (tile (q, g) at (q gb + g) TB, scale/bias at kSbOff + q sb_stride + 64 g):
-// warp w owns row tiles w, w + 16, ... entirely; `emit(q, row, value)` gets the value of row `row` (0..15) of row tile
-// q from the lanes that hold it (c4 == 0).
-template <int BITS, typename Emit>
+// warp w owns row tiles w, w + 16, ... entirely; row `row` (0..15) of row tile q is added into acc[16 q + row] (fp32
+// reduction in L2) by the lanes that hold it (c4 == 0).
+template <int BITS>
 __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_stride, uint32_t xs_addr,
-                            uint32_t xsum_addr, Emit emit) {
+                            uint32_t xsum_addr, float* acc) {
   constexpr int TB = BITS == 4 ? 512 : 1024;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r8 = lane >> 2, c4 = lane & 3;
-  const long i = C.ci;
-  bool ok = mbar_wait_abortable(&C.full[C.slot_of(i)], C.par_of(i), P);
+  const int sl = C.slot;
+  prof(P, R_OWNED);
+  bool ok = mbar_wait_abortable(&C.full[sl], C.phase, P);
+  prof(P, R_OWNED_WAIT);
   if (ok) {
-    const uint32_t st = C.stage_addr(i);
+    const uint32_t st = C.stage_addr(sl);
     for (int q = warp; q < nr; q += kConsumerWarps) {
       float ys[4] = {0.f, 0.f, 0.f, 0.f}, yb[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t aw = st + q * gb * TB + lane * 16;
       uint32_t asb = st + kSbOff + q * sb_stride + r8 * 8;
       uint32_t ax = xs_addr + c4 * 32;
       uint32_t axs = xsum_addr + c4 * 8;
+#pragma unroll 1
       for (int g = 0; g < gb; ++g) {
         group_step<BITS, 1>(aw, asb, ax, axs, P.sdt, ys, yb);
         aw += TB;
@@ -513,14 +728,14 @@ __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_str
         axs += 32;
       }
       if (c4 == 0) {
-        emit(q, r8, fmaf(ys[0], gemv::k2p24, yb[0]));
-        emit(q, r8 + 8, fmaf(ys[2], gemv::k2p24, yb[2]));
+        red_f32(acc + q * 16 + r8, fmaf(ys[0], gemv::k2p24, yb[0]));
+        red_f32(acc + q * 16 + r8 + 8, fmaf(ys[2], gemv::k2p24, yb[2]));
       }
     }
   }
   __syncwarp();
-  if (lane == 0) gemv::mbar_arrive(&C.empty[C.slot_of(i)]);
-  ++C.ci;
+  if (lane == 0) gemv::mbar_arrive(&C.empty[sl]);
+  C.step(C.slot, C.phase);
   return ok;
 }
 
@@ -581,19 +796,24 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
     if (pos >= k0 && pos < k1 && tid < HD / 8)
       reinterpret_cast<uint4*>(P.kc + kvbase + static_cast<size_t>(pos) * HD)[tid] = reinterpret_cast<const uint4*>(kn)[tid];
   }
+  if (!P.qkg) {  // the group's q rows into shared memory: one round trip to L2 for the whole CTA
+    const uint4* qsrc = reinterpret_cast<const uint4*>(P.q16 + static_cast<size_t>(j * G) * HD);
+    for (int t = tid; t < G * HD / 8; t += kConsumers) reinterpret_cast<uint4*>(qn)[t] = __ldcg(qsrc + t);
+    consumer_sync();
+  }
   // Q^T fragments: lane (g8, t4) holds q[head g8][16 ks + 2 t4 + {0, 1, 8, 9}] (pre-scaled fp16)
   uint32_t qb[KS][2];
   {
     const bool live = g8 < G;
-    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(P.q16 + static_cast<size_t>(j * G + (live ? g8 : 0)) * HD);
     const uint32_t* qsm = reinterpret_cast<const uint32_t*>(qn + (live ? g8 : 0) * HD);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
-      qb[ks][0] = !live ? 0u : P.qkg ? qsm[ks * 8 + t4] : __ldcg(qrow + ks * 8 + t4);
-      qb[ks][1] = !live ? 0u : P.qkg ? qsm[ks * 8 + 4 + t4] : __ldcg(qrow + ks * 8 + 4 + t4);
+      qb[ks][0] = live ? qsm[ks * 8 + t4] : 0u;
+      qb[ks][1] = live ? qsm[ks * 8 + 4 + t4] : 0u;
     }
   }
   for (int t = tid; t < G * HD; t += kConsumers) ov[t] = 0.f;
+  prof(P, R_ATTN_Q);
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float oacc[KS][4];
 #pragma unroll
@@ -602,10 +822,13 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
   const int nch = (k1 - k0 + KC - 1) / KC;
   const int tpc = KC / kKeyTile;  // tiles per chunk
   bool ok = true;
-  for (int q = 0; q < nch; ++q) {
-    const long i = C.ci + q;
-    if (ok && !mbar_wait_abortable(&C.full[C.slot_of(i)], C.par_of(i), P)) ok = false;
-    uint8_t* Ks = C.smem + C.Lo.ring + C.slot_of(i) * kStage;
+  int sl = C.slot;
+  unsigned ph = C.phase;
+  for (int q = 0; q < nch; ++q, C.step(sl, ph)) {
+    prof(P, R_ATTN_KEYS);
+    if (ok && !mbar_wait_abortable(&C.full[sl], ph, P)) ok = false;
+    prof(P, R_ATTN_WAIT);
+    uint8_t* Ks = C.smem + C.Lo.ring + sl * kStage;
     uint8_t* Vs = Ks + NB * KC * 128;
     for (int tt = 0; tt < tpc && ok; ++tt) {
       const int t = q * tpc + tt;
@@ -649,8 +872,8 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
         x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
       }
       const float mn0 = fmaxf(m0, x0), mn1 = fmaxf(m1, x1);  // finite: key a is live
-      const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
-      const float p0 = exp2f(s0 - mn0), p1 = exp2f(s1 - mn1), p2 = exp2f(s2 - mn0), p3 = exp2f(s3 - mn1);
+      const float al0 = ex2(m0 - mn0), al1 = ex2(m1 - mn1);
+      const float p0 = ex2(s0 - mn0), p1 = ex2(s1 - mn1), p2 = ex2(s2 - mn0), p3 = ex2(s3 - mn1);
       l0 = fmaf(l0, al0, p0 + p2);
       l1 = fmaf(l1, al1, p1 + p3);
       m0 = mn0;
@@ -670,9 +893,11 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
       }
     }
     __syncwarp();
-    if (lane == 0) gemv::mbar_arrive(&C.empty[C.slot_of(i)]);
+    if (lane == 0) gemv::mbar_arrive(&C.empty[sl]);
   }
-  C.ci += nch;
+  C.slot = sl;
+  C.phase = ph;
+  prof(P, R_ATTN_KEYS);
   mark(P, l * kTraceMarks + 10);
   // l over the warp's key rows (lanes with the same t4), then the CTA's combination: M = max over warps, each warp
   // adds its o scaled by 2^(m_w - M) into ov (shared-memory atomics)
@@ -689,13 +914,24 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
   }
   const bool fail = consumer_sync_or(!ok);
   if (fail) return false;
-  float M0 = -INFINITY, M1 = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) {
-    M0 = fmaxf(M0, om[(w * 8 + 2 * t4) * 2]);
-    M1 = fmaxf(M1, om[(w * 8 + 2 * t4 + 1) * 2]);
+  // per head h (thread h): M = the max over the warps, L = sum_w l_w 2^(m_w - M)
+  float* mh = om + kConsumerWarps * 16;  // [8] M, then [8] L
+  if (tid < G) {
+    float M = -INFINITY;
+#pragma unroll 4
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, om[(w * 8 + tid) * 2]);
+    float Ls = 0.f;
+#pragma unroll 4
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float mw = om[(w * 8 + tid) * 2];
+      if (mw != -INFINITY) Ls = fmaf(om[(w * 8 + tid) * 2 + 1], ex2(mw - M), Ls);
+    }
+    mh[tid] = M;
+    mh[8 + tid] = Ls;
   }
-  const float f0 = m0 == -INFINITY ? 0.f : exp2f(m0 - M0), f1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M1);
+  consumer_sync();
+  const float M0 = mh[2 * t4 < G ? 2 * t4 : 0], M1 = mh[2 * t4 + 1 < G ? 2 * t4 + 1 : 0];
+  const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - M0), f1 = m1 == -INFINITY ? 0.f : ex2(m1 - M1);
   if (m0 != -INFINITY || m1 != -INFINITY) {
 #pragma unroll
     for (int dt = 0; dt < KS; ++dt) {
@@ -710,28 +946,13 @@ __device__ bool attention_split(const Params& P, Cons& C, const Sched& Sc, int l
     }
   }
   consumer_sync();
+  prof(P, R_ATTN_MERGE);
   // the CTA's partial: per head (M, L, o[HD])
   float* dst = P.apart + (static_cast<size_t>(j) * P.smax + s) * G * (HD + 2);
+#pragma unroll 1
   for (int t = tid; t < G * (HD + 2); t += kConsumers) {
     const int g = t / (HD + 2), e = t % (HD + 2);
-    float v;
-    if (e == 0) {
-      float M = -INFINITY;
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, om[(w * 8 + g) * 2]);
-      v = M;
-    } else if (e == 1) {
-      float M = -INFINITY;
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, om[(w * 8 + g) * 2]);
-      float Ls = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float mw = om[(w * 8 + g) * 2];
-        if (mw != -INFINITY) Ls = fmaf(om[(w * 8 + g) * 2 + 1], exp2f(mw - M), Ls);
-      }
-      v = Ls;
-    } else {
-      v = ov[g * HD + e - 2];
-    }
-    dst[t] = v;
+    dst[t] = e == 0 ? mh[g] : e == 1 ? mh[8 + g] : ov[g * HD + e - 2];
   }
   return true;
 }
@@ -746,6 +967,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
   const Layout Lo = smem_layout(P.d, P.G * HD, P.stages);
   __shared__ __align__(8) uint64_t bars[2 * kMaxRing];
   __shared__ int sh_flag, sh_dead;
+  __shared__ __align__(8) SigQueue sq;
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxRing;
   const unsigned epoch = P.sync[0];
@@ -761,6 +983,10 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    for (int s = 0; s < kSigSlots; ++s) {
+      mbar_init(&sq.full[s], 1);
+      mbar_init(&sq.empty[s], 1);
+    }
     sh_dead = 0;
     fence_mbar_init();
   }
@@ -774,6 +1000,20 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
   }
   __syncthreads();
 
+  if (warp == kSignalWarp) {
+    if (lane == 0) {
+      for (long n = 0;; ++n) {
+        const int sl = static_cast<int>(n % kSigSlots);
+        if (!mbar_wait_abortable(&sq.full[sl], static_cast<unsigned>((n / kSigSlots) & 1), P)) break;
+        unsigned* a = sq.addr[sl];
+        const unsigned v = sq.val[sl];
+        gemv::mbar_arrive(&sq.empty[sl]);
+        if (!a) break;
+        red_rel(a, v);
+      }
+    }
+    return;
+  }
   if (warp == kConsumerWarps) {
     if (lane == 0) {
       Prod pr;
@@ -792,6 +1032,16 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     return;
   }
 
+  long nsig = 0;  // thread 0: signals posted
+  auto post = [&](unsigned* a, unsigned v) {  // thread 0, after a consumer barrier
+    const int sl = static_cast<int>(nsig % kSigSlots);
+    if (nsig >= kSigSlots && !mbar_wait_abortable(&sq.empty[sl], static_cast<unsigned>(((nsig / kSigSlots) - 1) & 1), P))
+      return;
+    sq.addr[sl] = a;
+    sq.val[sl] = v;
+    gemv::mbar_arrive(&sq.full[sl]);
+    ++nsig;
+  };
   Cons C;
   C.smem = smem;
   C.Lo = Lo;
@@ -808,13 +1058,39 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
   const int TPS = tps(BITS);
   const int nrc = row_chunks(P);
   bool ok = true;
-  int rts[16], g0s[16], gbs[16];
 
+  // the CTA's qkv row tiles c, c + grid, ... (kMaxQkvTiles at most, checked on the host)
+  const int nq = c < P.rt_qkv ? (P.rt_qkv - 1 - c) / grid + 1 : 0;
+  prof_begin(P);
   for (int l = 0; l < P.L && ok; ++l) {
+    prof(P, R_TOP);
     const __half* g1 = P.gains + static_cast<size_t>(l) * 2 * P.d;
     const __half* g2 = g1 + P.d;
     float* acc_h = acc + static_cast<size_t>(l) * P.d;
     float* acc_x = acc + static_cast<size_t>(P.L + l) * P.d;
+    // operands that do not depend on the step's activations, loaded before the dependency waits: the norm gains
+    // (a thread's 8-element slices) and, for thread 8 ti + r (r < 8), row pair r of its qkv tile ti: bias and the
+    // RoPE (cos, sin) at this position
+    uint4 gpre1[kNormSlices], gpre2[kNormSlices];
+    norm_gains(P, g1, gpre1);
+    norm_gains(P, g2, gpre2);
+    float eb1 = 0.f, eb2 = 0.f, ecs = 1.f, esn = 0.f;
+    const int eti = tid >> 3, er = tid & 7;
+    const int et = c + eti * grid;
+    const int ehead = et * 16 / HD, ett = (et * 16 % HD) / 16;
+    const int ei1 = 8 * ett + er, ei2 = HD / 2 + 8 * ett + er;
+    if (tid < 8 * nq) {
+      if (P.bias) {
+        const __half* b = P.bias + static_cast<size_t>(l) * P.rt_qkv * 16;
+        eb1 = __half2float(b[ehead * HD + ei1]);
+        eb2 = __half2float(b[ehead * HD + ei2]);
+      }
+      if (ehead < P.H + P.KVH && !P.qkg) {
+        ecs = P.cos_t[static_cast<size_t>(Sc.pos) * (HD / 2) + ei1];
+        esn = P.sin_t[static_cast<size_t>(Sc.pos) * (HD / 2) + ei1];
+      }
+    }
+    prof(P, R_PRELOAD);
     // ---------------- Q
     if (l == 0) {
       for (int k = tid; k < P.d / 8; k += kConsumers)
@@ -822,57 +1098,52 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
       consumer_sync();
     } else {
       if (!wait_counter(ctr + (l - 1) * CL + 2 * P.KVH + 1, static_cast<unsigned>(P.nf), P, C.flag)) { ok = false; break; }
+      prof(P, R_WAIT);
       const float* ax = acc + static_cast<size_t>(P.L + l - 1) * P.d;
       for (int k = tid; k < P.d; k += kConsumers) x16k[k] = __float2half_rn(hk[k] + __ldcg(ax + k));
       consumer_sync();
     }
+    prof(P, R_ACTLOAD);
     mark(P, l * kTraceMarks + 0);
-    stage_norm(P, C, [&](int k) { return __half2float(x16k[k]); }, g1);
+    stage_norm(P, C, x16k, nullptr, gpre1);
+    prof(P, R_NORM);
     mark(P, l * kTraceMarks + 8);
-    for (int t = c; t < P.rt_qkv && ok; t += grid) {
-      for (int k = 0; k < nrc; ++k) { rts[k] = t; g0s[k] = k * P.gchunk; gbs[k] = min(P.gchunk, P.gd - k * P.gchunk); }
-      if (!rows_batch<BITS>(P, C, nrc, rts, g0s, gbs, xs_a, xsum_a, uv)) { ok = false; break; }
-      if (t == c) mark(P, l * kTraceMarks + 9);
-      // epilogue: 8 RoPE pairs (tile rows r, r + 8 = logical rows 8 tt + r, hd/2 + 8 tt + r of the head)
-      if (tid < 8) {
-        const int r = tid;
-        const int prow0 = t * 16, head = prow0 / HD, tt = (prow0 % HD) / 16, half = HD / 2;
-        const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
-        float y1 = uv[r], y2 = uv[r + 8];
-        if (P.bias) {
-          const __half* b = P.bias + static_cast<size_t>(l) * P.rt_qkv * 16;
-          y1 += __half2float(b[head * HD + i1]);
-          y2 += __half2float(b[head * HD + i2]);
-        }
-        if (head < P.H + P.KVH && P.qkg) {
+    if (nq > 0) {
+      // every qkv tile of the CTA in one batch
+      if (!rows_batch<BITS>(P, C, nq * nrc, nrc, c, grid, xs_a, xsum_a, uv, l * kTraceMarks + 20)) { ok = false; break; }
+      mark(P, l * kTraceMarks + 9);
+      // epilogue: per tile 8 RoPE pairs (tile rows r, r + 8 = logical rows 8 tt + r, hd/2 + 8 tt + r of the head)
+      if (tid < 8 * nq) {
+        const float y1 = uv[(eti * nrc) * 16 + er] + eb1, y2 = uv[(eti * nrc) * 16 + er + 8] + eb2;
+        if (ehead < P.H + P.KVH && P.qkg) {
           // QK-norm: the head's norm needs all its rows; the attention phase finishes q and k from these
-          P.qkraw[head * HD + i1] = y1;
-          P.qkraw[head * HD + i2] = y2;
-        } else if (head < P.H + P.KVH) {
-          const float cs = P.cos_t[static_cast<size_t>(Sc.pos) * half + i1];
-          const float sn = P.sin_t[static_cast<size_t>(Sc.pos) * half + i1];
-          const float o1 = y1 * cs - y2 * sn, o2 = y2 * cs + y1 * sn;
-          if (head < P.H) {
-            P.q16[head * HD + i1] = __float2half_rn(o1 * P.qscale);
-            P.q16[head * HD + i2] = __float2half_rn(o2 * P.qscale);
+          P.qkraw[ehead * HD + ei1] = y1;
+          P.qkraw[ehead * HD + ei2] = y2;
+        } else if (ehead < P.H + P.KVH) {
+          const float o1 = y1 * ecs - y2 * esn, o2 = y2 * ecs + y1 * esn;
+          if (ehead < P.H) {
+            P.q16[ehead * HD + ei1] = __float2half_rn(o1 * P.qscale);
+            P.q16[ehead * HD + ei2] = __float2half_rn(o2 * P.qscale);
           } else {
-            __half* kr = P.kc + ((static_cast<size_t>(l) * P.KVH + head - P.H) * P.cap + Sc.pos) * HD;
-            kr[i1] = __float2half_rn(o1);
-            kr[i2] = __float2half_rn(o2);
+            __half* kr = P.kc + ((static_cast<size_t>(l) * P.KVH + ehead - P.H) * P.cap + Sc.pos) * HD;
+            kr[ei1] = __float2half_rn(o1);
+            kr[ei2] = __float2half_rn(o2);
           }
         } else {
-          __half* vr = P.vc + ((static_cast<size_t>(l) * P.KVH + head - P.H - P.KVH) * P.cap + Sc.pos) * HD;
-          vr[i1] = __float2half_rn(y1);
-          vr[i2] = __float2half_rn(y2);
+          __half* vr = P.vc + ((static_cast<size_t>(l) * P.KVH + ehead - P.H - P.KVH) * P.cap + Sc.pos) * HD;
+          vr[ei1] = __float2half_rn(y1);
+          vr[ei2] = __float2half_rn(y2);
         }
       }
       consumer_sync();
-      if (tid == 0) {
-        const int head = t * 16 / HD;
-        const int grp = head < P.H ? head / P.G : head < P.H + P.KVH ? head - P.H : head - P.H - P.KVH;
-        __threadfence();
-        red_rel(ctr + l * CL + grp, 1u);
-      }
+      prof(P, R_QKV_EPI);
+      if (tid == 0)  // release: the CTA's stores above are ordered before each count (barrier + cumulativity)
+        for (int ti = 0; ti < nq; ++ti) {
+          const int head = (c + ti * grid) * 16 / HD;
+          const int grp = head < P.H ? head / P.G : head < P.H + P.KVH ? head - P.H : head - P.H - P.KVH;
+          post(ctr + l * CL + grp, 1u);
+        }
+      prof(P, R_SIGNAL);
     }
     if (!ok) break;
     mark(P, l * kTraceMarks + 1);
@@ -882,39 +1153,53 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     if (has_attn) {
       const unsigned qkv_tiles = static_cast<unsigned>((P.G + 2) * HD / 16);
       if (!wait_counter(ctr + l * CL + j, qkv_tiles, P, C.flag)) { ok = false; break; }
+      prof(P, R_WAIT);
       mark(P, l * kTraceMarks + 2);
       if (!attention_split<HD>(P, C, Sc, l, j, s, k0, k1)) { ok = false; break; }
       consumer_sync();
-      if (tid == 0) {
-        __threadfence();
-        red_rel(ctr + l * CL + P.KVH + j, 1u);
-      }
+      prof(P, R_ATTN_OUT);
+      if (tid == 0) post(ctr + l * CL + P.KVH + j, 1u);
+      prof(P, R_SIGNAL);
       mark(P, l * kTraceMarks + 3);
       // ---------------- O
       int r0, r1;
       Sc.orows(P, s, &r0, &r1);
       if (r1 > r0) {
         if (!wait_counter(ctr + l * CL + P.KVH + j, static_cast<unsigned>(Sc.S), P, C.flag)) { ok = false; break; }
+        prof(P, R_WAIT);
         mark(P, l * kTraceMarks + 4);
-        // merge the group's S partials: attn = fp16(sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M))
+        // merge the group's S partials: attn = fp16(sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M)). Warp g: head g's
+        // S (m, l) pairs at once, its weights 2^(m_s - M) and sum L to shared memory (hk: h is rebuilt in F); then
+        // every element's S o values at once
         __half* xo = reinterpret_cast<__half*>(smem + Lo.xo);
         float* xsumo = reinterpret_cast<float*>(smem + Lo.xsumo);
+        float* wq = hk;                                   // [G][S] weights, then [G] sums at wq + G S
         const float* src = P.apart + static_cast<size_t>(j) * P.smax * P.G * (HD + 2);
-        const int KA = P.G * HD;
-        for (int t = tid; t < KA; t += kConsumers) {
-          const int g = t / HD, e = t % HD;
+        const int KA = P.G * HD, S_ = Sc.S;
+        for (int g = warp; g < P.G; g += kConsumerWarps) {
           float M = -INFINITY;
-          for (int q = 0; q < Sc.S; ++q) M = fmaxf(M, __ldcg(src + (static_cast<size_t>(q) * P.G + g) * (HD + 2)));
-          float Ls = 0.f, Os = 0.f;
-          for (int q = 0; q < Sc.S; ++q) {
+          for (int q = lane; q < S_; q += 32) M = fmaxf(M, __ldcg(src + (static_cast<size_t>(q) * P.G + g) * (HD + 2)));
+          M = warp_max(M);
+          float Ls = 0.f;
+          for (int q = lane; q < S_; q += 32) {
             const float* pq = src + (static_cast<size_t>(q) * P.G + g) * (HD + 2);
             const float mq = __ldcg(pq);
-            if (mq == -INFINITY) continue;
-            const float w = exp2f(mq - M);
+            const float w = mq == -INFINITY ? 0.f : ex2(mq - M);
+            wq[g * S_ + q] = w;
             Ls = fmaf(__ldcg(pq + 1), w, Ls);
-            Os = fmaf(__ldcg(pq + 2 + e), w, Os);
           }
-          xo[t] = __float2half_rn(Os / Ls);
+          Ls = warp_sum(Ls);
+          if (lane == 0) wq[P.G * S_ + g] = Ls;
+        }
+        consumer_sync();
+        for (int t = tid; t < KA; t += kConsumers) {
+          const int g = t / HD, e = t % HD;
+          const float* pe = src + static_cast<size_t>(g) * (HD + 2) + 2 + e;
+          const float* wg = wq + g * S_;
+          float Os = 0.f;
+#pragma unroll 8
+          for (int q = 0; q < S_; ++q) Os = fmaf(__ldcg(pe + static_cast<size_t>(q) * P.G * (HD + 2)), wg[q], Os);
+          xo[t] = __float2half_rn(Os / wq[P.G * S_ + g]);
         }
         consumer_sync();
         for (int g = warp; g < KA / 64; g += kConsumerWarps) {
@@ -923,35 +1208,35 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           if (lane == 0) xsumo[g * 8] = sm;
         }
         consumer_sync();
+        prof(P, R_O_MERGE);
         mark(P, l * kTraceMarks + 11);
         for (int r = r0; r < r1 && ok; r += P.o_per) {
           const int nr = min(P.o_per, r1 - r);
-          ok = owned_chunk<BITS>(P, C, nr, P.gk, P.o_sb, smem_u32(xo), smem_u32(xsumo),
-                                 [&](int q, int row, float v) { red_f32(acc_h + (r + q) * 16 + row, v); });
+          ok = owned_chunk<BITS>(P, C, nr, P.gk, P.o_sb, smem_u32(xo), smem_u32(xsumo), acc_h + r * 16);
         }
         if (consumer_sync_or(!ok)) { ok = false; break; }
-        if (tid == 0) {
-          __threadfence();
-          red_rel(ctr + l * CL + 2 * P.KVH, static_cast<unsigned>(r1 - r0));
-        }
+        prof(P, R_OWNED);
+        if (tid == 0) post(ctr + l * CL + 2 * P.KVH, static_cast<unsigned>(r1 - r0));
+        prof(P, R_SIGNAL);
         mark(P, l * kTraceMarks + 5);
       }
     }
     // ---------------- F
     if (!wait_counter(ctr + l * CL + 2 * P.KVH, static_cast<unsigned>(P.KVH * P.rt_d), P, C.flag)) { ok = false; break; }
+    prof(P, R_WAIT);
     mark(P, l * kTraceMarks + 6);
     for (int k = tid; k < P.d; k += kConsumers) hk[k] = __half2float(x16k[k]) + __ldcg(acc_h + k);
     consumer_sync();
-    stage_norm(P, C, [&](int k) { return hk[k]; }, g2);
+    prof(P, R_ACTLOAD);
+    stage_norm(P, C, nullptr, hk, gpre2);
+    prof(P, R_NORM);
     mark(P, l * kTraceMarks + 12);
     for (int f = c; f < P.nf && ok; f += grid) {
       // gate/up: row tiles 8f .. 8f + 7 (pairs: gate tile 2p, up tile 2p + 1), one batch per two pairs
       __half* act = reinterpret_cast<__half*>(smem + Lo.act);
       for (int pb = 0; pb < 4 && ok; pb += 2) {
-        int n = 0;
-        for (int t = 8 * f + 2 * pb; t < 8 * f + 2 * pb + 4; ++t)
-          for (int k = 0; k < nrc; ++k, ++n) { rts[n] = t; g0s[n] = k * P.gchunk; gbs[n] = min(P.gchunk, P.gd - k * P.gchunk); }
-        if (!rows_batch<BITS>(P, C, n, rts, g0s, gbs, xs_a, xsum_a, uv)) { ok = false; break; }
+        if (!rows_batch<BITS>(P, C, 4 * nrc, nrc, 8 * f + 2 * pb, 1, xs_a, xsum_a, uv,
+                              f == c ? l * kTraceMarks + (pb ? 24 : 22) : -1)) { ok = false; break; }
         // uv: [chunk][16]; the first chunk of row tile q of this batch is q * nrc
         if (tid < 32) {
           const int pp = tid / 16, r = tid % 16;  // pair pb + pp of the unit
@@ -959,6 +1244,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
           act[(pb + pp) * 16 + r] = __float2half_rn(gemv::silu_f(g) * u);
         }
         consumer_sync();
+        prof(P, R_SILU);
         if (f == c) mark(P, l * kTraceMarks + 13 + pb / 2);
       }
       if (!ok) break;
@@ -969,42 +1255,45 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
         if (lane == 0) xsuma[0] = sm;
       }
       consumer_sync();
+      prof(P, R_SILU);
       // down: K slice f (one group) of every row tile, dn_rows row tiles a chunk
       for (int r = 0; r < P.rt_d && ok; r += P.dn_rows) {
         const int nr = min(P.dn_rows, P.rt_d - r);
-        ok = owned_chunk<BITS>(P, C, nr, 1, 64, smem_u32(act), smem_u32(xsuma),
-                               [&](int q, int row, float v) { red_f32(acc_x + (r + q) * 16 + row, v); });
+        ok = owned_chunk<BITS>(P, C, nr, 1, 64, smem_u32(act), smem_u32(xsuma), acc_x + r * 16);
         if (r == 0 && f == c) mark(P, l * kTraceMarks + 15);
       }
       if (consumer_sync_or(!ok)) { ok = false; break; }
-      if (tid == 0) {
-        __threadfence();
-        red_rel(ctr + l * CL + 2 * P.KVH + 1, 1u);
-      }
+      prof(P, R_OWNED);
+      if (tid == 0) post(ctr + l * CL + 2 * P.KVH + 1, 1u);
+      prof(P, R_SIGNAL);
     }
     if (!ok) break;
     mark(P, l * kTraceMarks + 7);
   }
 
   // ---------------- head
+  prof(P, R_TOP);
+  uint4 gfin[kNormSlices];
+  norm_gains(P, P.final_gain, gfin);
+  prof(P, R_PRELOAD);
   if (ok && !wait_counter(ctr + (P.L - 1) * CL + 2 * P.KVH + 1, static_cast<unsigned>(P.nf), P, C.flag)) ok = false;
+  prof(P, R_WAIT);
   if (ok) {
     mark(P, P.L * kTraceMarks + 0);
     const float* ax = acc + static_cast<size_t>(2 * P.L - 1) * P.d;
     for (int k = tid; k < P.d; k += kConsumers) x16k[k] = __float2half_rn(hk[k] + __ldcg(ax + k));
     consumer_sync();
-    stage_norm(P, C, [&](int k) { return __half2float(x16k[k]); }, P.final_gain);
+    prof(P, R_ACTLOAD);
+    stage_norm(P, C, x16k, nullptr, gfin);
+    prof(P, R_NORM);
     float bv = -INFINITY;  // thread 0's running first maximum of the CTA's rows
     int bi = 0x7fffffff;
     const int h0 = static_cast<int>(static_cast<long long>(c) * P.rt_v / grid);
     const int h1 = static_cast<int>(static_cast<long long>(c + 1) * P.rt_v / grid);
-    const int nmax = max(1, min(8, P.stages / nrc));  // row tiles a batch
+    const int nmax = max(1, min(8, (P.stages / 2) / nrc));  // row tiles a batch: the next batch streams meanwhile
     for (int t0 = h0; t0 < h1 && ok; t0 += nmax) {
       const int nt = min(nmax, h1 - t0);
-      int n = 0;
-      for (int t = t0; t < t0 + nt; ++t)
-        for (int k = 0; k < nrc; ++k, ++n) { rts[n] = t; g0s[n] = k * P.gchunk; gbs[n] = min(P.gchunk, P.gd - k * P.gchunk); }
-      if (!rows_batch<BITS>(P, C, n, rts, g0s, gbs, xs_a, xsum_a, uv)) { ok = false; break; }
+      if (!rows_batch<BITS>(P, C, nt * nrc, nrc, t0, 1, xs_a, xsum_a, uv)) { ok = false; break; }
       if (warp == 0) {
         float v = -INFINITY;
         int vi = 0x7fffffff;
@@ -1024,16 +1313,20 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
         if (v > bv || (v == bv && vi < bi)) { bv = v; bi = vi; }
       }
       consumer_sync();
+      prof(P, R_HEAD);
     }
     if (tid == 0) {
       P.pairs[2 * c] = bv;
       P.pairs[2 * c + 1] = __int_as_float(bi);
     }
   }
+  if (tid == 0) post(nullptr, 0u);  // the signal warp's last entry
   if (consumer_sync_or(!ok)) {
     *C.dead = 1;  // the producer stops at its next stage
     return;
   }
+  prof(P, R_TAIL);
+  prof_end(P);
   mark(P, P.L * kTraceMarks + 1);
   if (tid == 0) {
     __threadfence();
@@ -1124,8 +1417,19 @@ size_t fstep_smem(int d, int G, int hd, int stages) {
 
 // The deepest ring (up to kMaxRing stages) that fits the device's opt-in shared memory; 0 if fewer than 4 fit.
 int fstep_stages(const agxc_ctx* ctx, int d, int G, int hd) {
+  // the kernel's static shared memory (barriers, the signal queue, the profile), the largest of the instantiations
+  size_t fixed = 0;
+  for (auto kern : {fstep::fstep_kernel<4, 64>, fstep::fstep_kernel<4, 128>, fstep::fstep_kernel<8, 64>,
+                    fstep::fstep_kernel<8, 128>}) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    fixed = std::max(fixed, static_cast<size_t>(fa.sharedSizeBytes));
+  }
   for (int st = fstep::kMaxRing; st >= 4; --st)
-    if (fstep_smem(d, G, hd, st) + 2 * fstep::kMaxRing * 8 + 64 <= static_cast<size_t>(ctx->max_smem_optin)) return st;
+    if (fstep_smem(d, G, hd, st) + fixed <= static_cast<size_t>(ctx->max_smem_optin)) return st;
   return 0;
 }
 
@@ -1169,8 +1473,8 @@ int fstep_launch(const FstepArgs& a, cudaStream_t s) {
 
 // Counter words of one parity set (rounded to 32).
 int fstep_counters(int L, int KVH) { return (L * fstep::ctr_per_layer(KVH) + 1 + 31) / 32 * 32; }
-int fstep_trace_marks(int L) { return L * fstep::kTraceMarks + 2; }
-int fstep_maps_per_layer() { return fstep::kMapsPerLayer; }
+int fstep_trace_marks(int L) { return L * fstep::kTraceMarks + 2 + fstep::kProfRegions; }
+int fstep_map_count() { return fstep::kMaps; }
 int fstep_tiles_per_stage(int bits) { return fstep::tps(bits); }
 
 }  // namespace agxc

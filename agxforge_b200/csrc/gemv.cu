@@ -99,6 +99,26 @@ int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, in
   return make_map(m, base, inner_words, G, RT, CG, RW);
 }
 
+// The same boxes over L layers' packs of one role at a constant byte stride (a 4-D map: words, groups, row tiles,
+// layers).
+int encode_pack_map_layers(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int L,
+                           uint64_t layer_stride, int CG, int RW) {
+  if (int rc = encode_fn()) return rc;
+  if (layer_stride % 16) return fail(AGXC_EINVAL, "tensor map: a layer stride that is a multiple of 16 bytes");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(inner_words), static_cast<cuuint64_t>(G),
+                        static_cast<cuuint64_t>(RT), static_cast<cuuint64_t>(L)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(inner_words) * 4,
+                           static_cast<cuuint64_t>(inner_words) * 4 * G, static_cast<cuuint64_t>(layer_stride)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(inner_words), static_cast<cuuint32_t>(CG),
+                       static_cast<cuuint32_t>(RW), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AGXC_ECUDA, "cuTensorMapEncodeTiled (layers) failed (" + std::to_string(r) + ")");
+  return 0;
+}
+
 int encode_kv_map_box(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z, int box_keys) {
   if (int rc = encode_fn()) return rc;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(cap), static_cast<cuuint64_t>(Z)};

@@ -130,7 +130,7 @@ struct FstepArgs {
   int L = 0, d = 0, H = 0, KVH = 0, hd = 0, F = 0, V = 0, cap = 0, bits = 4, sdt = 0, stages = 0, smax = 1, grid = 0;
   float eps = 1e-6f;
   uint64_t wait_ns = 2000000000ull;   // the bound on every wait of the step (global timer)
-  const CUtensorMap* maps = nullptr;  // device: per layer fstep_maps_per_layer(), then the head's 2, then K and V
+  const CUtensorMap* maps = nullptr;  // device: fstep_map_count() maps (per role over all layers, head, K, V)
   const __half* gains = nullptr;
   const __half* bias = nullptr;
   const __half* qkg = nullptr;        // [L][2][hd] QK-norm gains, or NULL (no QK-norm)
@@ -162,11 +162,13 @@ size_t fstep_smem(int d, int G, int hd, int stages);
 int fstep_launch(const FstepArgs& a, cudaStream_t s);
 int fstep_counters(int L, int KVH);
 int fstep_trace_marks(int L);
-int fstep_maps_per_layer();
+int fstep_map_count();
 int fstep_tiles_per_stage(int bits);
 // A 3-D TMA map over a pack's tiles [RT row tiles][G groups][inner 32-bit words] with a box of (inner, CG, RW).
 int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW);
 // A TMA map over fp16 KV rows [Z][cap][hd] with boxes of 64 dims x box_keys keys x 1, 128-byte swizzle.
+int encode_pack_map_layers(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int L,
+                           uint64_t layer_stride, int CG, int RW);
 int encode_kv_map_box(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z, int box_keys);
 // A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
 constexpr int kAttnKeys = 128;

@@ -248,34 +248,39 @@ int enqueue_step_fused(agxc_model* m, cudaStream_t s) {
   return fstep_launch(a, s);
 }
 
-// The fused step's TMA maps: per layer the qkv, o_proj, gate/up and down packs (weights and scale/bias), then the
-// head, then the K and V caches. Box shapes: row tiles x gchunk groups (qkv, gate/up, head); one row tile x the
-// group's K range (o_proj); dn_rows row tiles x one group (down); 64 dims x the stage's keys (caches).
+// The fused step's TMA maps: one per role over all layers (the layers' packs of a role sit at a constant stride in
+// the weight arena): the qkv, o_proj, gate/up and down packs (weights and scale/bias), then the head, then the K and
+// V caches. Box shapes: row tiles x gchunk groups (qkv, gate/up, head); one row tile x the group's K range (o_proj);
+// dn_rows row tiles x one group (down); 64 dims x the stage's keys (caches).
 int build_fused_maps(agxc_model* m) {
   const agxc_model_desc& D = m->d;
   const int L = D.n_layers, d = D.d_model, hd = D.head_dim, G = D.n_heads / D.n_kv_heads;
   const int TW = tile_bytes(D.bits) / 4, TPS = fstep_tiles_per_stage(D.bits);
   const int gd = d / 64, gchunk = std::min(gd, TPS), gk = G * hd / 64, dn_rows = std::min(d / 16, TPS);
-  const int MPL = fstep_maps_per_layer();
-  std::vector<CUtensorMap> maps(static_cast<size_t>(L) * MPL + 4);
-  auto pair = [&](CUtensorMap* mp, const agxc_pack& pk, int cg, int rw) -> int {
-    const int G_ = pk.k / 64, RT = pk.n / 16;
-    if (int rc = encode_pack_map(mp, pk.tiles, TW, G_, RT, cg, rw)) return rc;
-    return encode_pack_map(mp + 1, pk.sb, 16, G_, RT, cg, rw);
+  std::vector<CUtensorMap> maps(fstep_map_count());
+  const uint64_t LS = L > 1 ? static_cast<uint64_t>(m->qkv[1].tiles - m->qkv[0].tiles) : 256;
+  auto role = [&](CUtensorMap* mp, const std::vector<agxc_pack>& v, int cg, int rw) -> int {
+    for (int l = 0; l < L; ++l)
+      if (v[l].tiles != v[0].tiles + l * LS || v[l].sb != v[0].sb + l * LS)
+        return fail(AGXC_EINVAL, "fused step: the layers' packs are not at a constant stride");
+    const int G_ = v[0].k / 64, RT = v[0].n / 16;
+    if (int rc = encode_pack_map_layers(mp, v[0].tiles, TW, G_, RT, L, LS, cg, rw)) return rc;
+    return encode_pack_map_layers(mp + 1, v[0].sb, 16, G_, RT, L, LS, cg, rw);
   };
-  for (int l = 0; l < L; ++l) {
-    CUtensorMap* mp = maps.data() + static_cast<size_t>(l) * MPL;
-    int rc;
-    if ((rc = pair(mp + 0, m->qkv[l], gchunk, 1)) || (rc = pair(mp + 2, m->wo[l], gk, 1)) ||
-        (rc = pair(mp + 4, m->gu[l], gchunk, 1)) || (rc = pair(mp + 6, m->down[l], 1, dn_rows)))
+  int rc;
+  if ((rc = role(&maps[0], m->qkv, gchunk, 1)) || (rc = role(&maps[2], m->wo, gk, 1)) ||
+      (rc = role(&maps[4], m->gu, gchunk, 1)) || (rc = role(&maps[6], m->down, 1, dn_rows)))
+    return rc;
+  {
+    const int G_ = m->head.k / 64, RT = m->head.n / 16;
+    if ((rc = encode_pack_map(&maps[8], m->head.tiles, TW, G_, RT, gchunk, 1)) ||
+        (rc = encode_pack_map(&maps[9], m->head.sb, 16, G_, RT, gchunk, 1)))
       return rc;
   }
-  CUtensorMap* mh = maps.data() + static_cast<size_t>(L) * MPL;
-  if (int rc = pair(mh, m->head, gchunk, 1)) return rc;
   const int kc_keys = 16384 / (4 * hd);
   const int64_t Z = static_cast<int64_t>(L) * D.n_kv_heads;
-  if (int rc = encode_kv_map_box(mh + 2, m->kcache, hd, D.cap, Z, kc_keys)) return rc;
-  if (int rc = encode_kv_map_box(mh + 3, m->vcache, hd, D.cap, Z, kc_keys)) return rc;
+  if ((rc = encode_kv_map_box(&maps[10], m->kcache, hd, D.cap, Z, kc_keys))) return rc;
+  if ((rc = encode_kv_map_box(&maps[11], m->vcache, hd, D.cap, Z, kc_keys))) return rc;
   AGXC_CUDA(cudaMemcpy(m->fs_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
   return 0;
 }
@@ -746,13 +751,19 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
     const int G = D.n_heads / D.n_kv_heads;
     const int nrc = (d / 64 + fstep_tiles_per_stage(D.bits) - 1) / fstep_tiles_per_stage(D.bits);
     m->fs_stages = fstep_stages(ctx, d, G, hd);
+    // the qkv tiles of a CTA are consumed as one batch (at most 16 chunks, within the ring); the norm keeps d / 8
+    // slices of 8 in two per thread (d <= 8192)
+    const int qkv_tiles = (D.n_heads + 2 * D.n_kv_heads) * hd / 16;
+    const int nq_max = (qkv_tiles + ctx->num_sms - 1) / ctx->num_sms;
     m->fs_ok = B == 1 && T == 1 && d % 64 == 0 && F % 64 == 0 && (G * hd) % 64 == 0 && V % 16 == 0 &&
-               m->fs_stages >= 4 * nrc && (d / 16) % 1 == 0 && G <= 8;
+               m->fs_stages >= 4 * nrc && G <= 8 && d <= 8192 && nq_max * nrc <= 16 && nq_max * nrc <= m->fs_stages;
     if (m->fs_ok) {
-      m->fs_smax = std::max(1, ctx->num_sms / D.n_kv_heads);
+      // attention splits per KV group: the SMs over the groups, and the merge's weights (G per split + G sums) must
+      // fit the d floats of the h buffer it borrows
+      m->fs_smax = std::max(1, std::min(ctx->num_sms / D.n_kv_heads, d / G - 1));
       m->fs_nctr = fstep_counters(L, D.n_kv_heads);
       void* mp = nullptr;
-      if ((rc = dalloc(m, &mp, (static_cast<size_t>(L) * fstep_maps_per_layer() + 4) * sizeof(CUtensorMap))))
+      if ((rc = dalloc(m, &mp, static_cast<size_t>(fstep_map_count()) * sizeof(CUtensorMap))))
         return bail(rc);
       m->fs_maps = static_cast<CUtensorMap*>(mp);
       if ((rc = dalloc_t(m, &m->fs_sync, 64 + 2 * static_cast<size_t>(m->fs_nctr)))) return bail(rc);

@@ -211,6 +211,19 @@ def cpu_baseline_sample(m, tokens, pos):
     return (time.perf_counter() - t0) / tokens, cpu.threads
 
 
+def sm_max_mhz():
+    """The device's maximum SM clock (NVML), to turn the cycle profile into time; 1965 (B200) without NVML."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        u = str(torch.cuda.get_device_properties(0).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
+        return float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+    except Exception:  # noqa: BLE001
+        return 1965.0
+
+
 def trace_fused_step(args, m, hist):
     """--trace-step on the fused step: one traced step's per-CTA marks reduced to per-phase times (µs), means over
     layers 2 .. L-2. Per layer: qkv = its slowest CTA's qkv work after x was complete; attn_wait = from the last qkv
@@ -218,16 +231,19 @@ def trace_fused_step(args, m, hist):
     = the same for the merge + o_proj; h_wait = to the last CTA passing the h dependency; ffn = the FFN work (slowest
     CTA); x_wait = from the last FFN unit to the last CTA passing the next layer's x dependency; layer = x-complete to
     x-complete. `timeline`: every mark of the layer (assemble.DecodeModel.trace_fused) as [median, max] over the CTAs
-    that reach it, µs after the layer's x-complete (the producer's marks may precede it: negative)."""
+    that reach it, µs after the layer's x-complete (the producer's marks may precede it: negative). `profile_us`:
+    the cycle profile (assemble.DecodeModel.profile_fused), µs of the whole step per region for the median CTA."""
     from agxforge.inference.assemble import FUSED_TRACE_MARKS as NM
     names = ["q_dep", "q_done", "a_dep", "a_done", "o_dep", "o_done", "f_dep", "f_done", "q_normed", "q_tile1",
-             "a_keys", "o_merged", "f_normed", "f_gu1", "f_gu", "f_down1", "p_q", "p_a", "p_f", "p_f_last"]
+             "a_keys", "o_merged", "f_normed", "f_gu1", "f_gu", "f_down1", "p_q", "p_a", "p_f", "p_f_last",
+             "q_landed", "q_t0done", "f_gu1_landed", "f_gu1_t0done", "f_gu2_landed", "p_down"]
     m.start(0, [1])
     m.fill_history(0, hist - args.warmup, seed=1792)
     m.decode(args.warmup, want_tokens=False)
     m.set_option("trace", 1)
     m.decode(1, want_tokens=False)
     tr = m.trace_fused().astype(np.float64)
+    prof = m.profile_fused()
     m.close()
     L = (tr.shape[0] - 2) // NM
     rec, tl = [], []
@@ -250,8 +266,11 @@ def trace_fused_step(args, m, hist):
                      round(float(np.nanmean([r[nm][1] for r in tl])) / 1e3, 2)] for nm in names}
     head = tr[NM * L + 1][tr[NM * L + 1] > 0].max() - tr[NM * L][tr[NM * L] > 0].max()
     step = tr[NM * L + 1][tr[NM * L + 1] > 0].max() - tr[0][tr[0] > 0].min()
+    mhz = sm_max_mhz()
+    profile = {k: round(float(np.median(v)) / mhz, 1) for k, v in prof.items()}   # µs over the step, median CTA
     print(json.dumps(dict(trace_step=args.config, fused=True, layers=L, step_us=round(step / 1e3, 1),
-                          head_us=round(head / 1e3, 2), phases=phases, timeline=timeline)), flush=True)
+                          head_us=round(head / 1e3, 2), phases=phases, timeline=timeline,
+                          profile_us=profile, profile_mhz=mhz)), flush=True)
 
 
 def trace_step(args):

@@ -242,24 +242,27 @@ def test_fused_step_steps_back_to_back_and_free_run(torch):
 
 def test_fused_step_trace(torch):
     """The fused step's per-CTA trace: every CTA passes the qkv and FFN phases of every layer and the head, each CTA's
-    marks (0 = a phase it had no work in) run forward in time, and no CTA met layer l + 1's qkv dependency before
+    phase marks (0 = a phase it had no work in) run forward in time, and no CTA met layer l + 1's qkv dependency before
     the first CTA met layer l's FFN dependency (the counters order the layers)."""
+    from agxforge.inference.assemble import FUSED_TRACE_MARKS as NM
     m = _build(dict(SMALL), bits=4, cap=64)
     m.start(0, [5, 6, 7])
     m.set_option("trace", 1)
     m.decode(2, want_tokens=False)
     tr = m.trace_fused().astype(np.int64)
     L = m.shape.LAYERS
-    assert tr.shape[0] == 8 * L + 2
+    assert tr.shape[0] == NM * L + 2
     for l in range(L):
-        b = 8 * l
+        b = NM * l
         for k in (0, 1, 6, 7):
             assert np.all(tr[b + k] > 0)
         if l + 1 < L:
-            assert tr[b + 8].min() >= tr[b + 6].min()
-    assert np.all(tr[8 * L] > 0) and np.all(tr[8 * L + 1] > 0)
+            assert tr[b + NM].min() >= tr[b + 6].min()
+    assert np.all(tr[NM * L] > 0) and np.all(tr[NM * L + 1] > 0)
+    phase_rows = [NM * l + k for l in range(L) for k in range(8)] + [NM * L, NM * L + 1]
     for c in range(tr.shape[1]):
-        seq = tr[:, c][tr[:, c] > 0]
+        col = tr[phase_rows, c]
+        seq = col[col > 0]
         assert np.all(np.diff(seq) >= 0)
     m.set_option("trace", 0)
     m.close()
