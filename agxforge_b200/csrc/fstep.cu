@@ -43,14 +43,23 @@
 namespace agxc {
 namespace fstep {
 
-using gemv::consumer_sync;
-using gemv::consumer_sync_or;
 using gemv::group_step;
-using gemv::kConsumers;
-using gemv::kConsumerWarps;
+// 16 consumer warps (with the producer and the signal warp, 18: 96 registers a thread)
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = kConsumerWarps * 32;
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+__device__ __forceinline__ bool consumer_sync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(kConsumers)
+      : "memory");
+  return r != 0;
+}
 // 16 consumer warps, the producer warp, and the signal warp: it performs the consumers' release counts (a gpu-scope
 // release waits for the CTA's earlier writes to reach L2, ~1 us), so the consumers go on at once
-constexpr int kThreads = gemv::kConsumers + 64;
+constexpr int kThreads = kConsumers + 64;
 constexpr int kSignalWarp = kConsumerWarps + 1;
 constexpr int kSigSlots = 16;
 
@@ -563,7 +572,7 @@ struct Cons {
   }
 };
 
-// A norm gain's 8-element slices k = tid, tid + 512, ... of this consumer thread (kNormSlices at most: d <= 8192),
+// A norm gain's 8-element slices k = tid, tid + kConsumers, ... of this consumer thread (kNormSlices at most),
 // loaded ahead of the dependency wait that precedes the norm.
 constexpr int kNormSlices = 2;
 __device__ __forceinline__ void norm_gains(const Params& P, const __half* g, uint4* out) {
@@ -574,23 +583,72 @@ __device__ __forceinline__ void norm_gains(const Params& P, const __half* g, uin
   }
 }
 
-// Stage one row v[0..d) (fp32 values in shared memory or given by `get`) normed with gain g (this thread's slices,
-// norm_gains) into xs (fp16) and its per-group sums (xsum[g * 8]): y = fp16(v * r * g), r = rsqrt(mean(v^2) + eps)
-// (norm.py:185-203's rounding point).
-__device__ void stage_norm(const Params& P, Cons& C, const __half* xh, const float* xf, const uint4* gpre) {
-  auto get = [&](int k) { return xh ? __half2float(xh[k]) : xf[k]; };
+// The input of a phase, built and normed in one pass: thread t takes the 8-element slices k = t, t + 512, ... of the
+// row, forms the value v (mode X_ACC: x16 = fp16(h + a) from the fp32 h in shared memory and the fp32 accumulator a
+// in L2, v = x16; X_LOAD: x16 from L2; H_ACC: h = x16 + a, v = h), keeps it in registers, and after one reduction of
+// the sum of squares stages y = fp16(v * r * g) (r = rsqrt(mean(v^2) + eps), norm.py:185-203's rounding point) into
+// xs with the per-group sums of y (xsum[g * 8]). Two consumer barriers.
+enum : int { X_ACC = 0, X_LOAD, H_ACC };
+__device__ void stage_input(const Params& P, Cons& C, int mode, const float* a, const uint4* gpre) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __half* x16k = reinterpret_cast<__half*>(C.smem + C.Lo.x16k);
+  float* hk = reinterpret_cast<float*>(C.smem + C.Lo.hk);
   __half* xs = reinterpret_cast<__half*>(C.smem + C.Lo.xs);
   float* xsum = reinterpret_cast<float*>(C.smem + C.Lo.xsum);
   float* red = reinterpret_cast<float*>(C.smem + C.Lo.red);
   const int n8 = P.d / 8;
   float ss = 0.f;
-  for (int k = tid; k < n8; k += kConsumers)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float v = get(8 * k + e);
-      ss = fmaf(v, v, ss);
+  for (int i = 0; i < kNormSlices; ++i) {
+    const int k = i * kConsumers + tid;
+    if (k >= n8) break;
+    float v[8];
+    if (mode == X_LOAD) {
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(P.x16) + k);
+      reinterpret_cast<uint4*>(x16k)[k] = u;
+      __half2 hh[4];
+      memcpy(hh, &u, 16);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(hh[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    } else {
+      const float4 a0 = __ldcg(reinterpret_cast<const float4*>(a) + 2 * k);
+      const float4 a1 = __ldcg(reinterpret_cast<const float4*>(a) + 2 * k + 1);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      if (mode == X_ACC) {
+        const float4 h0 = reinterpret_cast<const float4*>(hk)[2 * k], h1 = reinterpret_cast<const float4*>(hk)[2 * k + 1];
+        const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        __half2 oh[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          oh[e] = __floats2half2_rn(hv[2 * e] + av[2 * e], hv[2 * e + 1] + av[2 * e + 1]);
+          const float2 f = __half22float2(oh[e]);
+          v[2 * e] = f.x;
+          v[2 * e + 1] = f.y;
+        }
+        uint4 o;
+        memcpy(&o, oh, 16);
+        reinterpret_cast<uint4*>(x16k)[k] = o;
+      } else {
+        const uint4 u = reinterpret_cast<const uint4*>(x16k)[k];
+        __half2 hh[4];
+        memcpy(hh, &u, 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(hh[e]);
+          v[2 * e] = f.x + av[2 * e];
+          v[2 * e + 1] = f.y + av[2 * e + 1];
+        }
+        reinterpret_cast<float4*>(hk)[2 * k] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(hk)[2 * k + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      }
     }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+  }
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
   consumer_sync();
@@ -605,14 +663,28 @@ __device__ void stage_norm(const Params& P, Cons& C, const __half* xh, const flo
     const bool live = k < n8;
     float sum = 0.f;
     if (live) {
-      const uint4 gu = gpre[i];
+      float v[8];  // the slice again, from shared memory (x16 or h)
+      if (mode == H_ACC) {
+        const float4 h0 = reinterpret_cast<const float4*>(hk)[2 * k], h1 = reinterpret_cast<const float4*>(hk)[2 * k + 1];
+        v[0] = h0.x; v[1] = h0.y; v[2] = h0.z; v[3] = h0.w; v[4] = h1.x; v[5] = h1.y; v[6] = h1.z; v[7] = h1.w;
+      } else {
+        const uint4 u = reinterpret_cast<const uint4*>(x16k)[k];
+        __half2 hh[4];
+        memcpy(hh, &u, 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(hh[e]);
+          v[2 * e] = f.x;
+          v[2 * e + 1] = f.y;
+        }
+      }
       __half2 gh[4];
-      memcpy(gh, &gu, 16);
+      memcpy(gh, &gpre[i], 16);
       __half2 oh[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 gg = __half22float2(gh[e]);
-        oh[e] = __floats2half2_rn((get(8 * k + 2 * e) * r) * gg.x, (get(8 * k + 2 * e + 1) * r) * gg.y);
+        oh[e] = __floats2half2_rn((v[2 * e] * r) * gg.x, (v[2 * e + 1] * r) * gg.y);
         const float2 f = __half22float2(oh[e]);
         sum += f.x + f.y;
       }
@@ -699,8 +771,9 @@ __device__ bool rows_batch(const Params& P, Cons& C, int n, int nrc, int rt0, in
 }
 
 // A chunk of nr row tiles x gb groups (tile (q, g) at (q gb + g) TB, scale/bias at kSbOff + q sb_stride + 64 g):
-// warp w owns row tiles w, w + 16, ... entirely; row `row` (0..15) of row tile q is added into acc[16 q + row] (fp32
-// reduction in L2) by the lanes that hold it (c4 == 0).
+// with ks = min(gb, 16 / nr) K parts a row tile (1 when nr >= 16), work item w = (row tile w % nr, K part w / nr)
+// goes to warp w mod 16, and each item's rows are added into acc[16 q + row] (fp32 reduction in L2) by the lanes that
+// hold them (c4 == 0): the K parts meet in L2, no barrier.
 template <int BITS>
 __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_stride, uint32_t xs_addr,
                             uint32_t xsum_addr, float* acc) {
@@ -713,19 +786,21 @@ __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_str
   prof(P, R_OWNED_WAIT);
   if (ok) {
     const uint32_t st = C.stage_addr(sl);
-    for (int q = warp; q < nr; q += kConsumerWarps) {
+    const int ks = 1;  // (splitting o_proj's K over more warps measured no faster)
+    for (int wi = warp; wi < nr * ks; wi += kConsumerWarps) {
+      const int q = wi % nr, kp = wi / nr;
       float ys[4] = {0.f, 0.f, 0.f, 0.f}, yb[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t aw = st + q * gb * TB + lane * 16;
-      uint32_t asb = st + kSbOff + q * sb_stride + r8 * 8;
-      uint32_t ax = xs_addr + c4 * 32;
-      uint32_t axs = xsum_addr + c4 * 8;
+      uint32_t aw = st + (q * gb + kp) * TB + lane * 16;
+      uint32_t asb = st + kSbOff + q * sb_stride + kp * 64 + r8 * 8;
+      uint32_t ax = xs_addr + kp * 128 + c4 * 32;
+      uint32_t axs = xsum_addr + kp * 32 + c4 * 8;
 #pragma unroll 1
-      for (int g = 0; g < gb; ++g) {
+      for (int g = kp; g < gb; g += ks) {
         group_step<BITS, 1>(aw, asb, ax, axs, P.sdt, ys, yb);
-        aw += TB;
-        asb += 64;
-        ax += 128;
-        axs += 32;
+        aw += ks * TB;
+        asb += ks * 64;
+        ax += ks * 128;
+        axs += ks * 32;
       }
       if (c4 == 0) {
         red_f32(acc + q * 16 + r8, fmaf(ys[0], gemv::k2p24, yb[0]));
@@ -1071,9 +1146,8 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     // operands that do not depend on the step's activations, loaded before the dependency waits: the norm gains
     // (a thread's 8-element slices) and, for thread 8 ti + r (r < 8), row pair r of its qkv tile ti: bias and the
     // RoPE (cos, sin) at this position
-    uint4 gpre1[kNormSlices], gpre2[kNormSlices];
+    uint4 gpre1[kNormSlices];
     norm_gains(P, g1, gpre1);
-    norm_gains(P, g2, gpre2);
     float eb1 = 0.f, eb2 = 0.f, ecs = 1.f, esn = 0.f;
     const int eti = tid >> 3, er = tid & 7;
     const int et = c + eti * grid;
@@ -1092,20 +1166,12 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
     }
     prof(P, R_PRELOAD);
     // ---------------- Q
-    if (l == 0) {
-      for (int k = tid; k < P.d / 8; k += kConsumers)
-        reinterpret_cast<uint4*>(x16k)[k] = __ldcg(reinterpret_cast<const uint4*>(P.x16) + k);
-      consumer_sync();
-    } else {
+    if (l > 0) {
       if (!wait_counter(ctr + (l - 1) * CL + 2 * P.KVH + 1, static_cast<unsigned>(P.nf), P, C.flag)) { ok = false; break; }
       prof(P, R_WAIT);
-      const float* ax = acc + static_cast<size_t>(P.L + l - 1) * P.d;
-      for (int k = tid; k < P.d; k += kConsumers) x16k[k] = __float2half_rn(hk[k] + __ldcg(ax + k));
-      consumer_sync();
     }
-    prof(P, R_ACTLOAD);
     mark(P, l * kTraceMarks + 0);
-    stage_norm(P, C, x16k, nullptr, gpre1);
+    stage_input(P, C, l == 0 ? X_LOAD : X_ACC, acc + static_cast<size_t>(P.L + l - 1) * P.d, gpre1);
     prof(P, R_NORM);
     mark(P, l * kTraceMarks + 8);
     if (nq > 0) {
@@ -1222,40 +1288,44 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
       }
     }
     // ---------------- F
+    uint4 gpre2[kNormSlices];  // loaded here, not at the layer's start: no registers held through the attention
+    norm_gains(P, g2, gpre2);
     if (!wait_counter(ctr + l * CL + 2 * P.KVH, static_cast<unsigned>(P.KVH * P.rt_d), P, C.flag)) { ok = false; break; }
     prof(P, R_WAIT);
     mark(P, l * kTraceMarks + 6);
-    for (int k = tid; k < P.d; k += kConsumers) hk[k] = __half2float(x16k[k]) + __ldcg(acc_h + k);
-    consumer_sync();
-    prof(P, R_ACTLOAD);
-    stage_norm(P, C, nullptr, hk, gpre2);
+    stage_input(P, C, H_ACC, acc_h, gpre2);
     prof(P, R_NORM);
     mark(P, l * kTraceMarks + 12);
     for (int f = c; f < P.nf && ok; f += grid) {
-      // gate/up: row tiles 8f .. 8f + 7 (pairs: gate tile 2p, up tile 2p + 1), one batch per two pairs
+      // gate/up: row tiles 8f .. 8f + 7 (pairs: gate tile 2p, up tile 2p + 1), ppb pairs a batch (all four when
+      // their chunks fit the ring); warp 0 forms act = fp16(SiLU(gate) up) of each batch and, after the last, the
+      // group sum of act for down
       __half* act = reinterpret_cast<__half*>(smem + Lo.act);
-      for (int pb = 0; pb < 4 && ok; pb += 2) {
-        if (!rows_batch<BITS>(P, C, 4 * nrc, nrc, 8 * f + 2 * pb, 1, xs_a, xsum_a, uv,
-                              f == c ? l * kTraceMarks + (pb ? 24 : 22) : -1)) { ok = false; break; }
+      float* xsuma = reinterpret_cast<float*>(smem + Lo.xsuma);
+      const int cap_chunks = min(16, P.stages);
+      const int ppb = 8 * nrc <= cap_chunks ? 4 : 4 * nrc <= cap_chunks ? 2 : 1;
+      for (int pb = 0; pb < 4 && ok; pb += ppb) {
+        if (!rows_batch<BITS>(P, C, 2 * ppb * nrc, nrc, 8 * f + 2 * pb, 1, xs_a, xsum_a, uv,
+                              f == c && pb == 0 ? l * kTraceMarks + 22 : -1)) { ok = false; break; }
         // uv: [chunk][16]; the first chunk of row tile q of this batch is q * nrc
-        if (tid < 32) {
-          const int pp = tid / 16, r = tid % 16;  // pair pb + pp of the unit
-          const float g = uv[(2 * pp) * nrc * 16 + r], u = uv[(2 * pp + 1) * nrc * 16 + r];
-          act[(pb + pp) * 16 + r] = __float2half_rn(gemv::silu_f(g) * u);
+        if (warp == 0) {
+          for (int e = lane; e < ppb * 16; e += 32) {
+            const int pp = e / 16, r = e % 16;  // pair pb + pp of the unit
+            const float g = uv[(2 * pp) * nrc * 16 + r], u = uv[(2 * pp + 1) * nrc * 16 + r];
+            act[(pb + pp) * 16 + r] = __float2half_rn(gemv::silu_f(g) * u);
+          }
+          if (pb + ppb == 4) {
+            __syncwarp();
+            const float2 fv = __half22float2(reinterpret_cast<const __half2*>(act)[lane]);
+            const float sm = warp_sum(fv.x + fv.y);
+            if (lane == 0) xsuma[0] = sm;
+          }
         }
-        consumer_sync();
-        prof(P, R_SILU);
-        if (f == c) mark(P, l * kTraceMarks + 13 + pb / 2);
       }
       if (!ok) break;
-      float* xsuma = reinterpret_cast<float*>(smem + Lo.xsuma);
-      if (warp == 0) {
-        const float2 fv = __half22float2(reinterpret_cast<const __half2*>(act)[lane]);
-        const float sm = warp_sum(fv.x + fv.y);
-        if (lane == 0) xsuma[0] = sm;
-      }
-      consumer_sync();
+      consumer_sync();  // act and its sum for every warp
       prof(P, R_SILU);
+      if (f == c) mark(P, l * kTraceMarks + 14);
       // down: K slice f (one group) of every row tile, dn_rows row tiles a chunk
       for (int r = 0; r < P.rt_d && ok; r += P.dn_rows) {
         const int nr = min(P.dn_rows, P.rt_d - r);
@@ -1280,11 +1350,7 @@ __global__ void __launch_bounds__(kThreads, 1) fstep_kernel(const __grid_constan
   prof(P, R_WAIT);
   if (ok) {
     mark(P, P.L * kTraceMarks + 0);
-    const float* ax = acc + static_cast<size_t>(2 * P.L - 1) * P.d;
-    for (int k = tid; k < P.d; k += kConsumers) x16k[k] = __float2half_rn(hk[k] + __ldcg(ax + k));
-    consumer_sync();
-    prof(P, R_ACTLOAD);
-    stage_norm(P, C, x16k, nullptr, gfin);
+    stage_input(P, C, X_ACC, acc + static_cast<size_t>(2 * P.L - 1) * P.d, gfin);
     prof(P, R_NORM);
     float bv = -INFINITY;  // thread 0's running first maximum of the CTA's rows
     int bi = 0x7fffffff;
@@ -1476,5 +1542,6 @@ int fstep_counters(int L, int KVH) { return (L * fstep::ctr_per_layer(KVH) + 1 +
 int fstep_trace_marks(int L) { return L * fstep::kTraceMarks + 2 + fstep::kProfRegions; }
 int fstep_map_count() { return fstep::kMaps; }
 int fstep_tiles_per_stage(int bits) { return fstep::tps(bits); }
+int fstep_max_d() { return fstep::kNormSlices * fstep::kConsumers * 8; }
 
 }  // namespace agxc

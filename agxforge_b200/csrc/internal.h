@@ -163,6 +163,7 @@ int fstep_launch(const FstepArgs& a, cudaStream_t s);
 int fstep_counters(int L, int KVH);
 int fstep_trace_marks(int L);
 int fstep_map_count();
+int fstep_max_d();                   // the largest d_model the fused step stages
 int fstep_tiles_per_stage(int bits);
 // A 3-D TMA map over a pack's tiles [RT row tiles][G groups][inner 32-bit words] with a box of (inner, CG, RW).
 int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW);

@@ -751,12 +751,12 @@ int model_create_local(agxc_ctx* ctx, const agxc_model_desc& G, int T, agxc_mode
     const int G = D.n_heads / D.n_kv_heads;
     const int nrc = (d / 64 + fstep_tiles_per_stage(D.bits) - 1) / fstep_tiles_per_stage(D.bits);
     m->fs_stages = fstep_stages(ctx, d, G, hd);
-    // the qkv tiles of a CTA are consumed as one batch (at most 16 chunks, within the ring); the norm keeps d / 8
-    // slices of 8 in two per thread (d <= 8192)
+    // the qkv tiles of a CTA are consumed as one batch (at most 16 chunks, within the ring); the norm keeps the
+    // row's 8-element slices in registers, two per consumer thread at most (fstep_max_d)
     const int qkv_tiles = (D.n_heads + 2 * D.n_kv_heads) * hd / 16;
     const int nq_max = (qkv_tiles + ctx->num_sms - 1) / ctx->num_sms;
     m->fs_ok = B == 1 && T == 1 && d % 64 == 0 && F % 64 == 0 && (G * hd) % 64 == 0 && V % 16 == 0 &&
-               m->fs_stages >= 4 * nrc && G <= 8 && d <= 8192 && nq_max * nrc <= 16 && nq_max * nrc <= m->fs_stages;
+               m->fs_stages >= 4 * nrc && G <= 8 && d <= fstep_max_d() && nq_max * nrc <= 16 && nq_max * nrc <= m->fs_stages;
     if (m->fs_ok) {
       // attention splits per KV group: the SMs over the groups, and the merge's weights (G per split + G sums) must
       // fit the d floats of the h buffer it borrows
