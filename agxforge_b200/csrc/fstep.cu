@@ -167,6 +167,12 @@ struct SigQueue {
 __device__ __forceinline__ void red_f32(float* p, float v) {
   asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
+// four consecutive floats (16-byte aligned) added in one reduction operation
+__device__ __forceinline__ void red_f32x4(float* p, float4 v) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, unsigned cnt) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(cnt) : "memory");
 }
@@ -802,10 +808,16 @@ __device__ bool owned_chunk(const Params& P, Cons& C, int nr, int gb, int sb_str
         ax += ks * 128;
         axs += ks * 32;
       }
+      // the tile's 16 rows through the warp's shared-memory slot to four lanes, one 4-float reduction each: every
+      // unit of the phase adds into the same rows, and L2 serialises reductions per line, so 4x fewer operations
+      float* wsl = reinterpret_cast<float*>(C.smem + C.Lo.red) + warp * 16;
       if (c4 == 0) {
-        red_f32(acc + q * 16 + r8, fmaf(ys[0], gemv::k2p24, yb[0]));
-        red_f32(acc + q * 16 + r8 + 8, fmaf(ys[2], gemv::k2p24, yb[2]));
+        wsl[r8] = fmaf(ys[0], gemv::k2p24, yb[0]);
+        wsl[r8 + 8] = fmaf(ys[2], gemv::k2p24, yb[2]);
       }
+      __syncwarp();
+      if (lane < 4) red_f32x4(acc + q * 16 + 4 * lane, reinterpret_cast<const float4*>(wsl)[lane]);
+      __syncwarp();
     }
   }
   __syncwarp();
