@@ -20,11 +20,11 @@ agxforge/inference/assemble.py: configure 71-92, build 596-828; its region R and
     DecodeModel.start(b, prompt)  the sequence's prompt in its token log, x = embedding(prompt[0]), q0 = 0
     DecodeModel.decode(steps)     run steps (execute.decode wraps it in the reference's report)
 
-At batch 1 on one device a whole step is one persistent kernel (the "fused" option): per layer RMSNorm + qkv + bias
-+ RoPE + append, split-KV attention, the merge + o_proj + residual, RMSNorm + gate/up + SiLU*mul + down + residual,
-each CTA waiting only on the counters of the data it reads; then the final norm, the vocabulary GEMV, the argmax and
-the generation step. Otherwise (batch 2..8, or "fused" 0) the layer is five kernels (the same five stages) and the
-head one, and at 32..256 sequences the projections are tensor-core GEMMs; a whole step is one CUDA graph.
+At batch 1..8 the layer is five kernels (RMSNorm + qkv + bias + RoPE + append, split-KV attention + merge, o_proj +
+residual, RMSNorm + gate/up + SiLU*mul, down + residual) and the head one (final norm + vocabulary GEMV + argmax +
+generation step), chained by programmatic dependent launch in one CUDA graph a step; at 32..256 sequences the
+projections are tensor-core GEMMs. At batch 1 on one device the "fused" option runs the whole step as one persistent
+kernel instead (each CTA waiting only on the counters of the data it reads).
 """
 from __future__ import annotations
 
@@ -187,9 +187,9 @@ class DecodeModel:
     OPTIONS = ("pdl", "trace", "fused", "bulk", "wait_ms", "tp_fused", "qk_norm", "device_wait_us")
 
     def set_option(self, option, value):
-        """Model options: "fused" (batch 1 on one device: the whole step as one persistent kernel whose layer phases
-        wait only on the counters of the data they read; 1 by default where it fits, 0 = one kernel per projection
-        and attention); "pdl" (the per-kernel path: programmatic dependent launch between the step's kernels: 0 off,
+        """Model options: "fused" (batch 1 on one device: 1 = the whole step as one persistent kernel whose layer
+        phases wait only on the counters of the data they read, where it fits; 0 (default) = one kernel per
+        projection and attention in one CUDA graph, which measures faster at the 1.8B shape); "pdl" (the per-kernel path: programmatic dependent launch between the step's kernels: 0 off,
         1 (default) successor let in after the dependency wait, 2 after the inputs are staged, 3 after the last weight
         chunk); "trace" (the per-kernel path records each launch's CTA entry / wait / exit times, read with trace();
         the fused step records per-CTA phase times, read with trace_fused()); "bulk" (per-kernel GEMV weights by
@@ -470,6 +470,6 @@ def build(config, device=0, weights=None, keep_packs=False):
         kept["final_gain"] = np.asarray(host(fg), np.float16) if fg is not None else np.ones(S.D_MODEL, np.float16)
     torch.cuda.synchronize()
     m.packs = kept
-    if os.environ.get("AGXC_FUSED") == "0" and m.batch == 1 and m.tp == 1:
-        m.set_option("fused", 0)      # the per-kernel path, for comparison runs
+    if os.environ.get("AGXC_FUSED") == "1" and m.batch == 1 and m.tp == 1 and m.plan_info()["fused"]["fits"]:
+        m.set_option("fused", 1)      # the fused persistent step, for comparison runs
     return m

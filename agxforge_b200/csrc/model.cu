@@ -66,7 +66,7 @@ struct agxc_model {
   int pdl = 1;
   int bulk = 0;                 // GEMV weights by plain bulk copies (AGXC_OPT_BULK)
   // the fused step (batch 1, fstep.cu): one persistent kernel a step, when the device and the shape allow it
-  int fused = 1;                // AGXC_OPT_FUSED
+  int fused = 0;                // AGXC_OPT_FUSED (opt-in: at the 1.8B shape the per-kernel graph measures faster)
   int fs_ok = 0;                // the shapes and the device fit it
   int fs_stages = 0;            // ring stages
   int fs_smax = 1;              // attention splits per KV group at most

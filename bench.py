@@ -6,9 +6,9 @@ Default workload (BASELINE config 3 at its headline point): InternLM2.5-1.8B-sha
 N(0, 0.02) weights, 4-bit affine group 64 with fp16 scale/bias), batch 1, a history of 1,792 - W positions (the KV
 cache rows filled on the device with seeded N(0, 1) fp16 values: throughput does not depend on their content), W
 warm-up steps, then K greedy decode steps at positions 1,792 .. 1,792+K-1. A step is one token: one CUDA-graph replay
-of the fused persistent step kernel (AGXC_FUSED=0 in the environment: the per-kernel path's 121 kernels). Inputs are
-far larger than L2 (0.96 GB of packs + 0.18 GB of KV per token against a 126 MB L2), so no flush is needed between
-steps.
+of the step's 121 kernels (AGXC_FUSED=1 in the environment: the fused persistent step kernel instead; the line's
+"fused_step" block times it beside the default either way). Inputs are far larger than L2 (0.96 GB of packs + 0.18 GB
+of KV per token against a 126 MB L2), so no flush is needed between steps.
 
     python bench.py --kernel-case ffn|qkv|wo|down|head|attn [--case-batch B]
         one launch of that kernel of the workload (after 3 warm-ups) through the C-ABI: the ncu capture case
@@ -660,7 +660,8 @@ def main():
 
     model, bits, batch, hist = CONFIGS[args.config]
     K, W = args.steps, args.warmup
-    cap = hist + 4 * K + args.profile_steps + 8   # timed, e2e (sizing + two runs), profiled steps: no position clamps
+    # timed, e2e (sizing + two runs), profiled and the other batch-1 path's steps: no position clamps
+    cap = hist + 5 * K + W + args.profile_steps + 8
     tp = world if args.config in TP_CONFIGS else 1
     rseed = 0 if tp > 1 else rank        # tensor parallel ranks hold shards of ONE model and the same sequences
     keep = bool(rank == 0 and world == 1 and not args.no_cpu)
@@ -762,6 +763,20 @@ def main():
                 except (IndexError, ValueError):
                     traffic = None
 
+    # the other batch-1 path on the same model (the fused persistent step when the graph is the default, or the
+    # reverse): W warm-up and K timed steps after the profiled ones, device time; reported beside, not in, the value
+    other = None
+    if batch == 1 and tp == 1 and m.plan_info()["fused"]["fits"]:
+        was = m.fused
+        m.set_option("fused", 0 if was else 1)
+        m.decode(W, want_tokens=False)
+        _, _, to = m.decode(K, want_tokens=False)
+        m.set_option("fused", 1 if was else 0)
+        other = dict(path="graph (one kernel per projection)" if was else "fused persistent step",
+                     tok_s=round(K / (to["gpu_ms"] / 1e3), 2), ms_per_step=round(to["gpu_ms"] / K, 4),
+                     launches_per_step=to["launches_per_step"],
+                     positions=[hist + 4 * K + args.profile_steps + W, hist + 5 * K + args.profile_steps + W - 1])
+
     # whole-step algorithmic bytes: every pack once + every sequence's KV over the timed positions (mean)
     w_bytes = m.weight_bytes
     kv_bytes = batch * S.LAYERS * kvrow * (hist + (K - 1) / 2.0 + 1)
@@ -827,6 +842,7 @@ def main():
                                weight_bytes=w_bytes, peak_source=peak_kind),
             kernels=kinds if not fused else None,
             graph_path_kernels=kinds if fused else None,
+            other_path=other,
             prefill=prefill,
             plans=m.plan_info(),
             cpu_baseline=cpu,

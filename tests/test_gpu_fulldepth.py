@@ -58,6 +58,19 @@ def test_config3_full_depth(internlm_q4, history, path):
         assert int(free[i, 0]) == int(np.argmax(flg[i, 0]))
 
 
+def test_config3_full_depth_fused_step(internlm_q4):
+    """Config 3 at history 1,792 on the fused persistent step (the same forced sequence as the graph path's case)."""
+    m = internlm_q4
+    m.set_option("fused", 1)
+    try:
+        rng = np.random.default_rng(1000 + 1792)
+        prompt = rng.integers(0, m.shape.VOCAB, 1792).tolist()
+        seqs, lg, toks = MC.run_forced(m, [prompt], 64, seed=2000 + 1792, prefill=False)
+        MC.compare(m, seqs, lg, 64, name="config3 q4 history 1792 fused step")
+    finally:
+        m.set_option("fused", 0)
+
+
 def test_config1_full_depth(torch):
     m = _build("qwen2.5-0.5b", 4, seed=0, cap=256)
     rng = np.random.default_rng(0)

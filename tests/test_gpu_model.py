@@ -229,6 +229,7 @@ def test_fused_step_steps_back_to_back_and_free_run(torch):
     """Many fused steps in one call (the counters and accumulators alternate between two sets by the step's parity):
     free generation picks the first maximum of the device logits every step, and the token log and q0 follow."""
     m = _build(dict(SMALL), bits=4, cap=128)
+    m.set_option("fused", 1)
     assert m.fused
     m.start(0, [3, 1, 4, 1, 5])
     m.decode(4, want_tokens=False)
@@ -246,6 +247,7 @@ def test_fused_step_trace(torch):
     the first CTA met layer l's FFN dependency (the counters order the layers)."""
     from agxforge.inference.assemble import FUSED_TRACE_MARKS as NM
     m = _build(dict(SMALL), bits=4, cap=64)
+    m.set_option("fused", 1)
     m.start(0, [5, 6, 7])
     m.set_option("trace", 1)
     m.decode(2, want_tokens=False)

@@ -66,6 +66,8 @@ def test_fused_step_wait_limit_zero_leaves_cleanly(torch):
     from agxforge.inference import assemble
     mk = lambda: assemble.build(dict(model=dict(SMALL), bits=4, cap=64, seed=3, keep_logits=True))  # noqa: E731
     m, twin = mk(), mk()
+    for x in (m, twin):
+        x.set_option("fused", 1)
     assert m.fused and twin.fused
     for x in (m, twin):
         x.start(0, [4, 5, 6])
