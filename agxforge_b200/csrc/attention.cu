@@ -9,7 +9,7 @@
 //     O^T[hd][8 heads]      += V^T[hd][16 keys] . P^T[16 keys][8 heads]  (V by ldmatrix.trans, P^T by movmatrix.trans)
 // q is pre-scaled by log2(e)/sqrt(hd), so the softmax is base 2; P is rounded to fp16 for the second product, the
 // running sums stay fp32. K and V move into shared memory by TMA tensor copies (boxes of 64 dims x 128 keys, 128-byte
-// swizzle, so ldmatrix reads without bank conflicts) in 128-key sub-chunks, two stages; each warp takes a 16-key tile
+// swizzle, so ldmatrix reads without bank conflicts) in 64-key sub-chunks, two stages; each warp takes a 16-key tile
 // of every sub-chunk. The history rows are requested before the upstream kernel finishes; the new row q0 is read after
 // it and replaces its stale copy in shared memory. Each CTA's partial (m, l, o[hd]) stays in its shared memory;
 // after a cluster barrier every CTA merges a slice of the outputs by reading the others' partials through
@@ -23,17 +23,19 @@ namespace agxc {
 
 namespace {
 
-constexpr int kAttnThreads = 256;
-constexpr int kAttnWarps = 8;
-constexpr int kSub = kAttnKeys;  // keys per shared-memory sub-chunk: one 16-key tile per warp
+// Two shapes of CTA: NW = 8 warps and 128-key sub-chunks (132 KB of shared memory at head_dim 128) for one to a few
+// sequences, where each KV head's keys split over a cluster; NW = 4 warps and 64-key sub-chunks (66 KB, three CTAs an
+// SM) for batched steps, whose sequences x KV heads already fill the SMs and want to be resident at once.
+template <int NW> constexpr int kThr = NW * 32;
+template <int NW> constexpr int kSubK = NW * 16;  // keys per shared-memory sub-chunk: one 16-key tile per warp
 constexpr int kMinChunk = 32;    // the fewest keys a chunk takes before more chunks are used
 constexpr int kHeadsN = 8;       // the MMA's N: query heads of one KV head
 
-// A stage holds K then V of one sub-chunk, each as HD / 64 boxes of [kSub rows][128 B] in the TMA's 128-byte swizzle
+// A stage holds K then V of one sub-chunk, each as HD / 64 boxes of [kSubK rows][128 B] in the TMA's 128-byte swizzle
 // (the 16-byte chunk c of row r sits at chunk c ^ (r % 8)), so ldmatrix reads 8 rows of one chunk without conflicts.
-__host__ __device__ constexpr int box_bytes() { return kSub * 128; }
-__host__ __device__ constexpr int stage_bytes(int hd) { return 2 * (hd / 64) * box_bytes(); }
-__host__ __device__ inline int attn_smem_bytes(int hd) { return 1024 + 2 * stage_bytes(hd); }
+template <int NW> __host__ __device__ constexpr int box_bytes() { return kSubK<NW> * 128; }
+template <int NW> __host__ __device__ constexpr int stage_bytes(int hd) { return 2 * (hd / 64) * box_bytes<NW>(); }
+template <int NW> __host__ __device__ inline int attn_smem_bytes(int hd) { return 1024 + 2 * stage_bytes<NW>(hd); }
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset of (row, 16-byte chunk) in a box
   return static_cast<uint32_t>(row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
@@ -81,8 +83,8 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 // One CLUSTER per (KV head, sequence): its gridDim.x CTAs take consecutive key chunks [s L, min(nk, (s+1) L)),
 // L = ceil(nk / gridDim.x), and meet in distributed shared memory for the merge. Every CTA passes both cluster
 // barriers on every path (an empty chunk contributes m = -inf), so no CTA waits on one that left.
-template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const __grid_constant__ CUtensorMap tk,
+template <int HD, int NW>
+__global__ void __launch_bounds__(kThr<NW>) attn_kernel(AttnParams p, const __grid_constant__ CUtensorMap tk,
                                                             const __grid_constant__ CUtensorMap tv) {
   constexpr int KS = HD / 16;  // k-steps of the score product, dim tiles of the value product
   constexpr int NB = HD / 64;  // boxes per K (or V) sub-chunk
@@ -94,7 +96,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   const int g8 = lane >> 2, t4 = lane & 3;  // MMA fragment coordinates
   const int G = p.H / p.KVH;
   __shared__ __align__(8) uint64_t bars[2];
-  __shared__ float sm_m[kAttnWarps][kHeadsN], sm_l[kAttnWarps][kHeadsN];
+  __shared__ float sm_m[NW][kHeadsN], sm_l[NW][kHeadsN];
   __shared__ float part_m[kHeadsN], part_l[kHeadsN];
   __shared__ float part_o[kHeadsN][HD];
 
@@ -104,20 +106,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   const int L = (nk + CL - 1) / CL;
   const int j0 = s * L;
   const int j1 = min(nk, j0 + L);
-  const int nsub = j1 > j0 ? (j1 - j0 + kSub - 1) / kSub : 0;
+  const int nsub = j1 > j0 ? (j1 - j0 + kSubK<NW> - 1) / kSubK<NW> : 0;
   const size_t kvbase = (static_cast<size_t>(b) * p.KVH + kvh) * p.cap * HD;
-  const int zrow = p.z0 + b * p.KVH + kvh;
+  const int zrow = b * p.KVH + kvh;
 
-  // sub-chunk i -> stage i % 2: whole boxes of kSub rows from key j0 + i kSub (rows past the cache end read as zero;
+  // sub-chunk i -> stage i % 2: whole boxes of kSubK rows from key j0 + i kSubK (rows past the cache end read as zero;
   // rows from pos on are replaced or masked: row pos is written by the upstream kernel, read after the wait)
   auto issue = [&](int i) {
     uint64_t* bar = &bars[i & 1];
-    uint8_t* st = smem + (i & 1) * stage_bytes(HD);
-    mbar_arrive_expect_tx(bar, static_cast<unsigned>(stage_bytes(HD)));
+    uint8_t* st = smem + (i & 1) * stage_bytes<NW>(HD);
+    mbar_arrive_expect_tx(bar, static_cast<unsigned>(stage_bytes<NW>(HD)));
 #pragma unroll
     for (int h = 0; h < NB; ++h) {
-      tma_load_3d(st + h * box_bytes(), &tk, h * 64, j0 + i * kSub, zrow, bar);
-      tma_load_3d(st + (NB + h) * box_bytes(), &tv, h * 64, j0 + i * kSub, zrow, bar);
+      tma_load_3d(st + h * box_bytes<NW>(), &tk, h * 64, j0 + i * kSubK<NW>, zrow, bar);
+      tma_load_3d(st + (NB + h) * box_bytes<NW>(), &tv, h * 64, j0 + i * kSubK<NW>, zrow, bar);
     }
   };
   if (tid == 0) {
@@ -162,10 +164,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   bool ok = true;
   int i = 0;
   for (; i < nsub; ++i) {
-    const int a = j0 + i * kSub;
-    const int n = min(kSub, j1 - a);
-    uint8_t* Ks = smem + (i & 1) * stage_bytes(HD);
-    uint8_t* Vs = Ks + NB * box_bytes();
+    const int a = j0 + i * kSubK<NW>;
+    const int n = min(kSubK<NW>, j1 - a);
+    uint8_t* Ks = smem + (i & 1) * stage_bytes<NW>(HD);
+    uint8_t* Vs = Ks + NB * box_bytes<NW>();
     const bool landed = mbar_wait_bounded(&bars[i & 1], (i >> 1) & 1, p.err);
     if (__syncthreads_or(!landed)) {  // leave together: the error word is set
       ok = false;
@@ -178,11 +180,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
       if (pos >= a && pos < a + n && tid < 2 * HD / 8) {
         const int kv = tid / (HD / 8), c = tid % (HD / 8);
         const uint4 v = reinterpret_cast<const uint4*>((kv ? p.vc : p.kc) + kvbase + static_cast<size_t>(pos) * HD)[c];
-        *reinterpret_cast<uint4*>((kv ? Vs : Ks) + (c >> 3) * box_bytes() + swz(pos - a, c)) = v;
+        *reinterpret_cast<uint4*>((kv ? Vs : Ks) + (c >> 3) * box_bytes<NW>() + swz(pos - a, c)) = v;
       }
-      for (int t = tid; t < (n16 - n) * (HD / 8); t += kAttnThreads) {
+      for (int t = tid; t < (n16 - n) * (HD / 8); t += kThr<NW>) {
         const int r = n + t / (HD / 8), c = t % (HD / 8);
-        *reinterpret_cast<uint4*>(Vs + (c >> 3) * box_bytes() + swz(r, c)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(Vs + (c >> 3) * box_bytes<NW>() + swz(r, c)) = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async();  // generic writes into a buffer that later bulk copies overwrite
       __syncthreads();
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
       for (int ks = 0; ks < KS; ++ks) {
         uint32_t a0, a1, a2, a3;
         const int c = ks * 2 + (lane >> 4);
-        ldsm_x4(smem_u32(Ks + (c >> 3) * box_bytes() + swz(krow, c)), a0, a1, a2, a3);
+        ldsm_x4(smem_u32(Ks + (c >> 3) * box_bytes<NW>() + swz(krow, c)), a0, a1, a2, a3);
         mma_16816(c0, c1, c2, c3, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
       }
       const bool va = kt + g8 < n, vb = kt + g8 + 8 < n;
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
         oacc[dt][3] *= al1;
         uint32_t a0, a1, a2, a3;
         const int c = dt * 2 + ((lane >> 3) & 1);
-        ldsm_x4_t(smem_u32(Vs + (c >> 3) * box_bytes() + swz(vrow, c)), a0, a1, a2, a3);
+        ldsm_x4_t(smem_u32(Vs + (c >> 3) * box_bytes<NW>() + swz(vrow, c)), a0, a1, a2, a3);
         mma_16816(oacc[dt][0], oacc[dt][1], oacc[dt][2], oacc[dt][3], a0, a1, a2, a3, pb0, pb1);
       }
     }
@@ -268,14 +270,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   }
   __syncthreads();
   // combine the warps into this CTA's chunk partial
-  for (int t = tid; t < G * HD; t += kAttnThreads) {
+  for (int t = tid; t < G * HD; t += kThr<NW>) {
     const int g = t / HD, d = t % HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][g]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][g]);
     float Ls = 0.f, Os = 0.f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float f = sm_m[w][g] == -INFINITY ? 0.f : exp2f(sm_m[w][g] - M);
       Ls = fmaf(sm_l[w][g], f, Ls);
       Os = fmaf(sm_o[w][g][d], f, Os);
@@ -287,7 +289,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   // lanes take one output, lane r reading chunk r's partial, so every remote load of a pass is in flight at once
   cluster_sync_all();
   const int total = G * HD, per = (total + CL - 1) / CL;
-  const int ro = kAttnThreads / CL;
+  const int ro = kThr<NW> / CL;
   const int r = tid % CL;
   for (int base = 0; base < per; base += ro) {  // the same trip count in every thread
     const int oi = base + tid / CL, t = s * per + oi;
@@ -311,12 +313,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p, const 
   if (tid == 0) trace_mark(p.trace, 2);
 }
 
-template <int HD>
+template <int HD, int NW>
 cudaLaunchConfig_t attn_config(const AttnParams& p, cudaStream_t s, cudaLaunchAttribute* attr, int cluster) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster, p.KVH, p.nb);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = attn_smem_bytes(HD);
+  cfg.blockDim = dim3(kThr<NW>);
+  cfg.dynamicSmemBytes = attn_smem_bytes<NW>(HD);
   cfg.stream = s;
   int na = 0;
   attr[na].id = cudaLaunchAttributeClusterDimension;
@@ -334,11 +336,16 @@ cudaLaunchConfig_t attn_config(const AttnParams& p, cudaStream_t s, cudaLaunchAt
   return cfg;
 }
 
-template <int HD>
-int launch_attn_t(const AttnParams& p, cudaStream_t s, const CUtensorMap& tk, const CUtensorMap& tv) {
+template <int HD, int NW>
+int launch_attn_t(const AttnParams& p, cudaStream_t s) {
+  // the KV maps: boxes of 64 dims x the variant's sub-chunk keys
+  CUtensorMap tk, tv;
+  const int64_t Z = static_cast<int64_t>(p.nb) * p.KVH;
+  if (int rc = encode_kv_map_box(&tk, p.kc, HD, p.cap, Z, kSubK<NW>)) return rc;
+  if (int rc = encode_kv_map_box(&tv, p.vc, HD, p.cap, Z, kSubK<NW>)) return rc;
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = attn_config<HD>(p, s, attr, p.S);
-  AGXC_CUDA(cudaLaunchKernelEx(&cfg, attn_kernel<HD>, p, tk, tv));
+  cudaLaunchConfig_t cfg = attn_config<HD, NW>(p, s, attr, p.S);
+  AGXC_CUDA(cudaLaunchKernelEx(&cfg, attn_kernel<HD, NW>, p, tk, tv));
   return 0;
 }
 
@@ -353,16 +360,16 @@ int attn_allow(K kern, int optin) {
 }
 
 // How many clusters of each power-of-two size (1 .. 16) the device keeps resident at once.
-template <int HD>
+template <int HD, int NW>
 void cluster_residency(int* active) {
   AttnParams p;
   p.KVH = 1;
   for (int i = 0; i < 5; ++i) {
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = attn_config<HD>(p, nullptr, attr, 1 << i);
+    cudaLaunchConfig_t cfg = attn_config<HD, NW>(p, nullptr, attr, 1 << i);
     cfg.gridDim = dim3(1 << i, 1, 1);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_kernel<HD>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, attn_kernel<HD, NW>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -416,8 +423,10 @@ int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap) {
 int attn_configure(agxc_ctx* ctx) {
   const int o = ctx->max_smem_optin;
   int rc;
-  if ((rc = attn_allow(attn_kernel<128>, o)) || (rc = attn_allow(attn_kernel<64>, o))) return rc;
-  cluster_residency<128>(ctx->cluster_active);  // the larger variant bounds the smaller
+  if ((rc = attn_allow(attn_kernel<128, 8>, o)) || (rc = attn_allow(attn_kernel<64, 8>, o)) ||
+      (rc = attn_allow(attn_kernel<128, 4>, o)) || (rc = attn_allow(attn_kernel<64, 4>, o)))
+    return rc;
+  cluster_residency<128, 8>(ctx->cluster_active);  // the largest variant bounds the others
   ctx->max_cluster = 1;
   for (int i = 0; i < 5; ++i)
     if (ctx->cluster_active[i] > 0) ctx->max_cluster = 1 << i;
@@ -426,8 +435,7 @@ int attn_configure(agxc_ctx* ctx) {
 
 size_t attn_part_floats(int nb, int H, int S, int hd) { return static_cast<size_t>(nb) * H * S * (hd + 2); }
 
-int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk,
-                     const CUtensorMap* tv) {
+int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s) {
   if (p.H % p.KVH) return fail(AGXC_EINVAL, "attention: heads must be a multiple of kv_heads");
   const int G = p.H / p.KVH;
   if (p.hd != 64 && p.hd != 128) return fail(AGXC_EINVAL, "attention: head_dim 64 or 128");
@@ -435,16 +443,11 @@ int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, c
   if (p.S < 1 || p.S > 16 || (p.S & (p.S - 1)) || p.nb < 1)
     return fail(AGXC_EINVAL, "attention: splits a power of two up to 16, and a positive batch");
   if (ctx && p.S > ctx->max_cluster) return fail(AGXC_EINVAL, "attention: splits exceed the device's cluster size");
-  CUtensorMap mk, mv;
-  if (!tk || !tv) {
-    const int64_t Z = static_cast<int64_t>(p.nb) * p.KVH;
-    if (int rc = encode_kv_map(&mk, p.kc, p.hd, p.cap, Z)) return rc;
-    if (int rc = encode_kv_map(&mv, p.vc, p.hd, p.cap, Z)) return rc;
-    tk = &mk;
-    tv = &mv;
-  }
-  if (p.hd == 128) return launch_attn_t<128>(p, s, *tk, *tv);
-  return launch_attn_t<64>(p, s, *tk, *tv);
+  // 16 or more sequences: the 4-warp CTAs (three an SM; their sequences x KV heads fill the SMs); fewer: 8 warps
+  // (measured faster there: one sequence's key chunks split over a cluster)
+  const bool small_cta = p.nb >= 16;
+  if (p.hd == 128) return small_cta ? launch_attn_t<128, 4>(p, s) : launch_attn_t<128, 8>(p, s);
+  return small_cta ? launch_attn_t<64, 4>(p, s) : launch_attn_t<64, 8>(p, s);
 }
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out,

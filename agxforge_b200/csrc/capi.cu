@@ -108,6 +108,16 @@ int agxc_init(int device, agxc_ctx** out) {
   e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&c->err_dev, 256);
   if (e == cudaSuccess) e = cudaMemset(c->err_dev, 0, 256);
+  if (e == cudaSuccess) {
+    // the stream-ordered scratch of agxc_qmv / agxc_qmm (split-K partial sums) comes from the device's default pool:
+    // keep freed blocks in the pool (this process only) so each call reuses them instead of mapping new memory
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+      uint64_t keep = ~0ull;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     agxc_ctx_free(c);
     return cuda_fail(e, "init");

@@ -91,10 +91,6 @@ int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows
   return 0;
 }
 
-int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z) {
-  return encode_kv_map_box(m, base, hd, cap, Z, kAttnKeys);
-}
-
 int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int CG, int RW) {
   return make_map(m, base, inner_words, G, RT, CG, RW);
 }

@@ -119,7 +119,6 @@ struct AttnParams {
   unsigned* counters = nullptr;   // unused
   unsigned* err = nullptr;
   int pdl = 0;
-  int z0 = 0;                     // the first (sequence, KV head) row of kc/vc in the tensor maps' third dimension
   unsigned long long* trace = nullptr;  // this launch's six trace words, or NULL
 };
 int attn_splits(const agxc_ctx* ctx, int nb, int KVH, int cap);
@@ -171,9 +170,6 @@ int encode_pack_map(CUtensorMap* m, const void* base, int inner_words, int G, in
 int encode_pack_map_layers(CUtensorMap* m, const void* base, int inner_words, int G, int RT, int L,
                            uint64_t layer_stride, int CG, int RW);
 int encode_kv_map_box(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z, int box_keys);
-// A TMA map over fp16 KV rows [Z][cap][hd]: boxes of 64 dims x kAttnKeys keys x 1, 128-byte swizzle.
-constexpr int kAttnKeys = 128;
-int encode_kv_map(CUtensorMap* m, const void* base, int hd, int cap, int64_t Z);
 // fp16 rows [rows][K] (K % 64 == 0) as boxes of 64 columns x box_rows rows, 128-byte swizzle (the UMMA K-major tile)
 int encode_rows_map(CUtensorMap* m, const void* x, int rows, int K, int box_rows);
 // A TMA map over fp16 activation rows X [B][K]: boxes of 64 columns x B rows, 128-byte swizzle.
@@ -265,9 +261,8 @@ int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* fla
                      const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot,
                      uint64_t wait_ns = 2000000000ull);
 size_t attn_part_floats(int nb, int H, int S, int hd);
-// tk/tv: maps over the caches from encode_kv_map (NULL: made here over kc/vc with Z = nb x KVH, z0 = 0)
-int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s, const CUtensorMap* tk = nullptr,
-                     const CUtensorMap* tv = nullptr);
+// (the KV maps are made here over kc/vc with Z = nb x KVH, boxes of the chosen variant's sub-chunk keys)
+int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
 int attn_configure(agxc_ctx* ctx);
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);

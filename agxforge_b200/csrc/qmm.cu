@@ -3,13 +3,16 @@
 // Y^T = W^T X^T with W dequantised once to fp16), on Blackwell's 5th-generation tensor cores.
 //
 // One CTA per 128 weight rows (x a K range when K is split): the MMA's M is the weight rows, its N the activation
-// rows (B = 32 .. 256), K advances by one 64-group per chunk. Per chunk:
-//   * the PRODUCER warp brings the chunk's 8 packed row tiles and their scale/bias (two 3-D TMA boxes of the pack)
-//     and the activations' 64 columns (a 2-D TMA box of X [B][K] fp16, 128-byte swizzle) into a ring stage;
+// rows (B = 32 .. 256), K advances by cg 64-groups per chunk (cg = 1, 2 or 4, the host's choice). Per chunk:
+//   * the PRODUCER warp brings the chunk's 8 packed row tiles x cg groups and their scale/bias (two 3-D TMA boxes of
+//     the pack) and the activations' cg x 64 columns (2-D TMA boxes of X [B][K] fp16, 128-byte swizzle) into a ring
+//     stage;
 //   * eight DEQUANT warps turn the tiles into fp16 weights in the MMA's canonical K-major 128-byte-swizzled layout
 //     (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes 1024 away
-//     exactly, HFMA2 applies the row's scale and bias with one rounding);
-//   * the MMA warp issues four tcgen05.mma.kind::f16 (M 128, N B, K 16) accumulating in TMEM, and commits: the
+//     exactly, HFMA2 applies the row's scale and bias with one rounding); each warp a row tile, cg groups a chunk:
+//     the barrier waits and the proxy fence of a chunk (about as long as one group's arithmetic) are paid once for cg
+//     groups;
+//   * the MMA warp issues 4 cg tcgen05.mma.kind::f16 (M 128, N B, K 16) accumulating in TMEM, and commits: the
 //     commit releases the stage and the dequant buffer when the tensor core has read them.
 // After the last chunk the dequant warps read the 128 x B fp32 accumulator back with tcgen05.ld (warp w reads TMEM
 // lanes 32 (w % 4) ..; the two warps of a lane quarter split the columns) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
@@ -29,7 +32,7 @@ namespace {
 constexpr int kM = 128;          // weight rows per CTA (the MMA's M)
 constexpr int kThreads = 320;    // warp 0 producer, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
 constexpr int kDeqWarps = 8;
-constexpr int kDeqBufs = 8;      // fp16 weight tiles in flight between the dequant warps and the tensor core
+constexpr int kMaxDeqBufs = 8;   // fp16 weight buffers in flight between the dequant warps and the tensor core
 
 struct QmmParams {
   const uint8_t* w = nullptr;
@@ -38,6 +41,8 @@ struct QmmParams {
   int B = 0;                      // activation rows (MMA N), a multiple of 16 in [32, 256]
   int ksplit = 1;                 // K ranges (CTAs) per 128-row tile
   int stages = 4;
+  int cg = 1;                     // 64-groups a chunk
+  int nbuf = 8;                   // dequant buffers
   float* y = nullptr;             // fp32 [B][ldy]
   int ldy = 0;
   float* part = nullptr;          // ksplit > 1: [ksplit][B][N] fp32, each K range's partial sums
@@ -50,17 +55,17 @@ struct QmmSmem {
   int bars, tmem_slot, deq, stage0, stage_bytes, x_off, w_off, sb_off, total;
 };
 
-__host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages) {
+__host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages, int cg, int nbuf) {
   QmmSmem L;
   const int TB = bits == 4 ? 512 : 1024;
   L.bars = 0;                                   // raw_full[S], raw_empty[S], deq_full[D], deq_empty[D], acc_full
-  L.tmem_slot = 512;                            // (S <= 16: the barriers fit below)
-  L.deq = 1024;                                 // kDeqBufs fp16 weight tiles of 128 x 64 (16 KB each)
-  L.stage0 = L.deq + kDeqBufs * kM * 128;
-  L.x_off = 0;                                  // X tile: B rows x 128 B (1,024-aligned for the swizzle)
-  L.w_off = (B * 128 + 1023) / 1024 * 1024;
-  L.sb_off = L.w_off + 8 * TB;
-  L.stage_bytes = (L.sb_off + 8 * 64 + 1023) / 1024 * 1024;
+  L.tmem_slot = 512;                            // (S <= 16, D <= 8: the barriers fit below)
+  L.deq = 1024;                                 // nbuf buffers of cg atoms 128 x 64 fp16 (16 KB each)
+  L.stage0 = L.deq + nbuf * cg * kM * 128;
+  L.x_off = 0;                                  // X: cg atoms of B rows x 128 B (1,024-aligned for the swizzle)
+  L.w_off = (cg * B * 128 + 1023) / 1024 * 1024;
+  L.sb_off = L.w_off + 8 * cg * TB;             // the boxes land row tile-major: (row tile, group) at (r cg + c)
+  L.stage_bytes = (L.sb_off + 8 * cg * 64 + 1023) / 1024 * 1024;
   L.total = L.stage0 + stages * L.stage_bytes;
   return L;
 }
@@ -133,11 +138,12 @@ __device__ __forceinline__ uint16_t to_f16_bits(uint16_t v, int sdt) {
 
 // One lane-task of the dequantisation: lane (r, c) of row tile t of the chunk -> rows 16t + r and 16t + r + 8,
 // k = 16c .. 16c + 15 (16-byte chunks 2c and 2c + 1 of each 128-byte row), fp16, swizzled.
+// wraw / sbraw: the group's tiles and scale/bias, row tile t at t * wstride / t * sbstride bytes.
 template <int BITS>
 __device__ __forceinline__ void dequant_task(const uint8_t* wraw, const uint8_t* sbraw, uint8_t* deq, int t, int l,
-                                             int sdt) {
+                                             int sdt, int wstride, int sbstride) {
   const int r = l >> 2, c = l & 3;
-  const uint2 e = *reinterpret_cast<const uint2*>(sbraw + t * 64 + r * 8);  // {s[r], s[r+8], b[r], b[r+8]}
+  const uint2 e = *reinterpret_cast<const uint2*>(sbraw + t * sbstride + r * 8);  // {s[r], s[r+8], b[r], b[r+8]}
   const uint32_t s0 = to_f16_bits(static_cast<uint16_t>(e.x & 0xFFFFu), sdt);
   const uint32_t s1 = to_f16_bits(static_cast<uint16_t>(e.x >> 16), sdt);
   const uint32_t b0 = to_f16_bits(static_cast<uint16_t>(e.y & 0xFFFFu), sdt);
@@ -146,7 +152,7 @@ __device__ __forceinline__ void dequant_task(const uint8_t* wraw, const uint8_t*
   const uint32_t b2[2] = {b0 | (b0 << 16), b1 | (b1 << 16)};
   uint32_t o[2][2][4];  // [row half][chunk][word]
   if (BITS == 4) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(wraw + t * 512 + l * 16);
+    const uint4 wv = *reinterpret_cast<const uint4*>(wraw + t * wstride + l * 16);
     const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};  // i: row r + 8 (i & 1), hi = i >> 1
 #pragma unroll
     for (int h = 0; h < 2; ++h) {      // row r (h 0) or r + 8 (h 1)
@@ -160,8 +166,8 @@ __device__ __forceinline__ void dequant_task(const uint8_t* wraw, const uint8_t*
       }
     }
   } else {
-    const uint4 lo = *reinterpret_cast<const uint4*>(wraw + t * 1024 + l * 16);
-    const uint4 hi4 = *reinterpret_cast<const uint4*>(wraw + t * 1024 + 512 + l * 16);
+    const uint4 lo = *reinterpret_cast<const uint4*>(wraw + t * wstride + l * 16);
+    const uint4 hi4 = *reinterpret_cast<const uint4*>(wraw + t * wstride + 512 + l * 16);
     const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi4.x, hi4.y, hi4.z, hi4.w};  // wi: k0 = 16c + 4 (wi >> 1) + 2 (wi & 1)
 #pragma unroll
     for (int wi = 0; wi < 8; ++wi) {
@@ -191,19 +197,21 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr int TB = BITS == 4 ? 512 : 1024;
-  const QmmSmem L = qmm_layout(BITS, p.B, p.stages);
+  const int cg = p.cg, D = p.nbuf;
+  const QmmSmem L = qmm_layout(BITS, p.B, p.stages, cg, D);
   const int S = p.stages;
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* raw_empty = raw_full + S;
   uint64_t* deq_full = raw_empty + S;
-  uint64_t* deq_empty = deq_full + kDeqBufs;
-  uint64_t* acc_full = deq_empty + kDeqBufs;
+  uint64_t* deq_empty = deq_full + D;
+  uint64_t* acc_full = deq_empty + D;
   volatile int* dead = reinterpret_cast<volatile int*>(acc_full + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L.tmem_slot);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tile = blockIdx.x / p.ksplit, ks = blockIdx.x % p.ksplit;
-  const int gper = p.G / p.ksplit;              // groups (chunks) of this CTA's K range
-  const int g0 = ks * gper;
+  const int gk = p.G / p.ksplit;                // groups of this CTA's K range
+  const int g0 = ks * gk;
+  const int gper = gk / cg;                     // its chunks
   const int ncols = p.B <= 32 ? 32 : p.B <= 64 ? 64 : p.B <= 128 ? 128 : 256;
 
   if (tid == 0) {
@@ -211,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], 1);
     }
-    for (int d = 0; d < kDeqBufs; ++d) {
+    for (int d = 0; d < D; ++d) {
       mbar_init(&deq_full[d], kDeqWarps);
       mbar_init(&deq_empty[d], 1);
     }
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ts)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
-      const unsigned bytes = static_cast<unsigned>(p.B * 128 + 8 * TB + 8 * 64);
+      const unsigned bytes = static_cast<unsigned>(cg * (p.B * 128 + 8 * TB + 8 * 64));
       int issued = 0;
       for (int i = 0; i < gper && !*dead; ++i, ++issued) {
         const int s = i % S;
@@ -246,9 +254,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
         }
         uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
         mbar_arrive_expect_tx(&raw_full[s], bytes);
-        tma_3d(st + L.w_off, &tw, 0, g0 + i, tile * 8, &raw_full[s]);
-        tma_3d(st + L.sb_off, &ts, 0, g0 + i, tile * 8, &raw_full[s]);
-        tma_2d(st + L.x_off, &tx, (g0 + i) * 64, 0, &raw_full[s]);
+        tma_3d(st + L.w_off, &tw, 0, g0 + i * cg, tile * 8, &raw_full[s]);
+        tma_3d(st + L.sb_off, &ts, 0, g0 + i * cg, tile * 8, &raw_full[s]);
+        for (int c = 0; c < cg; ++c)  // one 128-byte-swizzled atom of B rows x 64 columns each
+          tma_2d(st + L.x_off + c * p.B * 128, &tx, (g0 + i * cg + c) * 64, 0, &raw_full[s]);
       }
       if (*dead) {  // a wait gave up: no copy of this CTA may land after it leaves (bounded)
         for (int i = issued > S ? issued - S : 0; i < issued; ++i)
@@ -259,48 +268,52 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(p.B);
-      for (int i = 0; i < gper; ++i) {
-        const int s = i % S, d = i % kDeqBufs;
-        if (*dead || !mbar_wait_bounded(&deq_full[d], (i / kDeqBufs) & 1, p.err)) {
+      for (int i = 0, d = 0, dph = 0, s = 0; i < gper; ++i) {
+        if (*dead || !mbar_wait_bounded(&deq_full[d], static_cast<unsigned>(dph), p.err)) {
           *dead = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + L.deq + d * kM * 128);
-        const uint32_t b0 = smem_u32(smem + L.stage0 + s * L.stage_bytes + L.x_off);
+        for (int c = 0; c < cg; ++c) {
+          const uint32_t a0 = smem_u32(smem + L.deq + (d * cg + c) * kM * 128);
+          const uint32_t b0 = smem_u32(smem + L.stage0 + s * L.stage_bytes + L.x_off + c * p.B * 128);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {  // four K = 16 steps: +32 bytes within the swizzled 128-byte rows
-          const uint64_t ad = desc_sw128(a0 + 32 * k), bd = desc_sw128(b0 + 32 * k);
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-              "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-              : "memory");
+          for (int k = 0; k < 4; ++k) {  // four K = 16 steps: +32 bytes within the swizzled 128-byte rows
+            const uint64_t ad = desc_sw128(a0 + 32 * k), bd = desc_sw128(b0 + 32 * k);
+            const uint32_t acc = (i > 0 || c > 0 || k > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+                : "memory");
+          }
         }
         tc_commit(&raw_empty[s]);  // the stage (weights read, X read) is free once these MMAs are done
         tc_commit(&deq_empty[d]);
+        if (++s == S) s = 0;
+        if (++d == D) { d = 0; dph ^= 1; }
       }
       tc_commit(acc_full);  // every MMA of the CTA done: the accumulator is final
     }
   } else {
     // ---- dequant warps, then the epilogue
     const int dw = warp - 2;  // 0..7
-    for (int i = 0; i < gper; ++i) {
-      const int s = i % S, d = i % kDeqBufs;
-      const bool ok1 = !*dead && mbar_wait_bounded(&raw_full[s], (i / S) & 1, p.err);
-      const bool ok2 =
-          ok1 && (i < kDeqBufs || mbar_wait_bounded(&deq_empty[d], ((i / kDeqBufs) - 1) & 1, p.err));
+    for (int i = 0, s = 0, sph = 0, d = 0, dph = 0; i < gper; ++i) {
+      const bool ok1 = !*dead && mbar_wait_bounded(&raw_full[s], static_cast<unsigned>(sph), p.err);
+      const bool ok2 = ok1 && (i < D || mbar_wait_bounded(&deq_empty[d], static_cast<unsigned>(dph ^ 1), p.err));
       if (!__all_sync(0xffffffffu, ok2)) {  // the warp leaves together
         *dead = 1;
         break;
       }
       const uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
-      uint8_t* deq = smem + L.deq + d * kM * 128;
-      dequant_task<BITS>(st + L.w_off, st + L.sb_off, deq, dw, lane, p.sdt);  // warp dw: row tile dw
+      for (int c = 0; c < cg; ++c)  // warp dw: row tile dw of each of the chunk's groups
+        dequant_task<BITS>(st + L.w_off + c * TB, st + L.sb_off + c * 64, smem + L.deq + (d * cg + c) * kM * 128, dw,
+                           lane, p.sdt, cg * TB, cg * 64);
       fence_proxy_async();  // the tensor core reads what these generic stores wrote
       __syncwarp();
       if (lane == 0) mbar_arrive1(&deq_full[d]);
+      if (++s == S) { s = 0; sph ^= 1; }
+      if (++d == D) { d = 0; dph ^= 1; }
     }
     // epilogue: TMEM lanes 32 (warp % 4) .. + 31 = weight rows; columns = activation rows
     const bool ok = __all_sync(0xffffffffu, !*dead && mbar_wait_bounded(acc_full, 0, p.err));  // warp-uniform:
@@ -426,14 +439,34 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
       return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks owning equal numbers of 128-row tiles");
     p.push = *push;
   }
-  // as many stages as fit beside the dequant tiles (at most 16: a stage cycles through the copy, the dequant and the
-  // MMA's completion before it is refilled, so small stages want many)
-  p.stages = 16;
-  while (p.stages > 2 && qmm_layout(pk->bits, B, p.stages).total + 1024 > ctx->max_smem_optin - 2048) --p.stages;
-  const int smem = qmm_layout(pk->bits, B, p.stages).total + 1024;
-  // maps: the pack's tiles and scale/bias as boxes of 1 group x 8 row tiles; X [B][K] fp16 as 64 x B boxes
+  // the chunk: 2 groups where the K range divides and at least three stages fit beside the dequant buffers (the
+  // dequant warps' per-chunk waits and fence then cover two groups), else 1; as many stages as fit (at most 16: a stage
+  // cycles through the copy, the dequant and the MMA's completion before it is refilled, so small stages want many)
+  const int gk = G / ksplit;
+  auto stages_for = [&](int cg, int nbuf) {
+    int st = 16;
+    while (st > 2 && qmm_layout(pk->bits, B, st, cg, nbuf).total + 1024 > ctx->max_smem_optin - 2048) --st;
+    return qmm_layout(pk->bits, B, st, cg, nbuf).total + 1024 > ctx->max_smem_optin - 2048 ? 0 : st;
+  };
+  p.cg = 1;
+  p.nbuf = kMaxDeqBufs;
+  p.stages = 0;
+  const int opts[][3] = {{2, 4, 3}, {2, 3, 3}, {1, 8, 2}, {1, 4, 2}, {1, 2, 2}};  // cg, buffers, fewest stages
+  for (const auto& o : opts) {
+    if (gk % o[0]) continue;
+    const int st = stages_for(o[0], o[1]);
+    if (st >= o[2]) {
+      p.cg = o[0];
+      p.nbuf = o[1];
+      p.stages = st;
+      break;
+    }
+  }
+  if (!p.stages) return fail(AGXC_EINVAL, "qmm: the batch does not fit the shared memory");
+  const int smem = qmm_layout(pk->bits, B, p.stages, p.cg, p.nbuf).total + 1024;
+  // maps: the pack's tiles and scale/bias as boxes of cg groups x 8 row tiles; X [B][K] fp16 as 64 x B boxes
   QmvPlan plan;
-  plan.CG = 1;
+  plan.CG = p.cg;
   plan.RW = 8;
   CUtensorMap tw, ts, tx;
   if (int rc = qmv_maps(plan, pk->tiles, pk->sb, pk->n, pk->k, pk->bits, &tw, &ts)) return rc;
