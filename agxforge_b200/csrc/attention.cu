@@ -377,7 +377,8 @@ void cluster_residency(int* active) {
   }
 }
 
-__global__ void rmsnorm_kernel(const void* x, int x_f32, int d, const __half* g, float eps, __half* out) {
+__global__ void rmsnorm_kernel(const void* x, int x_f32, int d, const __half* g, float eps, __half* out, int pdl) {
+  pdl_enter(pdl);
   const int b = blockIdx.x, tid = threadIdx.x;
   __shared__ float red[32];
   float ss = 0.f;
@@ -451,10 +452,8 @@ int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s) {
 }
 
 int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out,
-                   cudaStream_t s) {
-  rmsnorm_kernel<<<nb, 256, 0, s>>>(x, x_f32, d, g, eps, out);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+                   cudaStream_t s, int pdl) {
+  return launch_ex(rmsnorm_kernel, dim3(nb), dim3(256), 0, s, pdl, x, x_f32, d, g, eps, out, pdl);
 }
 
 }  // namespace agxc

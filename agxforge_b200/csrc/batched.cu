@@ -34,7 +34,8 @@ __global__ void rope_append_kernel(const YRows y, int rows, const __half* __rest
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                    const uint32_t* __restrict__ q0, int H, int KVH, int hd, int cap, float qscale,
                                    __half* __restrict__ q16, __half* __restrict__ kc, __half* __restrict__ vc, int B,
-                                   int seq) {
+                                   int seq, int pdl) {
+  pdl_enter(pdl);
   const int pairs = rows / 2;
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * pairs) return;
@@ -156,21 +157,24 @@ __global__ void __launch_bounds__(1024) rows_argmax_kernel(const YRows y, int V,
   }
 }
 
-__global__ void residual16_kernel(const YRows y, const __half* __restrict__ x16, float* h, int d, int B) {
+__global__ void residual16_kernel(const YRows y, const __half* __restrict__ x16, float* h, int d, int B, int pdl) {
+  pdl_enter(pdl);
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
   const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
   h[t] = yval(y, b, i) + __half2float(x16[t]);
 }
 
-__global__ void residual32_kernel(const YRows y, const float* __restrict__ h, __half* x16, int d, int B) {
+__global__ void residual32_kernel(const YRows y, const float* __restrict__ h, __half* x16, int d, int B, int pdl) {
+  pdl_enter(pdl);
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * d) return;
   const int b = static_cast<int>(t / d), i = static_cast<int>(t % d);
   x16[t] = __float2half_rn(yval(y, b, i) + h[t]);
 }
 
-__global__ void swiglu_kernel(const YRows y, __half* __restrict__ act, int F, int B) {
+__global__ void swiglu_kernel(const YRows y, __half* __restrict__ act, int F, int B, int pdl) {
+  pdl_enter(pdl);
   const long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (t >= static_cast<long long>(B) * F) return;
   const int b = static_cast<int>(t / F), j = static_cast<int>(t % F);
@@ -234,7 +238,8 @@ __device__ void gen_step(int b, int best, int V, const __half* __restrict__ embe
 
 __global__ void __launch_bounds__(kArgThreads) argmax_gen_kernel(
     const float* __restrict__ logits, int V, const __half* __restrict__ embed, int d, uint32_t* q0, uint32_t* log,
-    int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err) {
+    int cap, int32_t* tok_out, uint32_t* force_next, __half* x16, unsigned* err, int pdl) {
+  pdl_enter(pdl);
   __shared__ float sv[kArgThreads / 32];
   __shared__ int si[kArgThreads / 32];
   __shared__ int s_tok;
@@ -364,41 +369,36 @@ int launch_rows_argmax(const YRows& y, int V, int rows, float* logits, int32_t* 
 
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
-                       __half* vc, int B, cudaStream_t s, int seq, const __half* qkg, float qk_eps) {
+                       __half* vc, int B, cudaStream_t s, int seq, const __half* qkg, float qk_eps, int pdl) {
   if (qkg) {
     rope_append_qknorm_kernel<<<dim3(H + 2 * KVH, B), hd / 2, 0, s>>>(y, bias, qkg, qk_eps, cos_t, sin_t, q0, H, KVH,
                                                                       hd, cap, qscale, q16, kc, vc, seq);
-  } else {
-    rope_append_kernel<<<blocks_for(static_cast<long long>(B) * rows / 2, 256), 256, 0, s>>>(
-        y, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq);
+    AGXC_CUDA(cudaGetLastError());
+    return 0;
   }
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+  return launch_ex(rope_append_kernel, dim3(blocks_for(static_cast<long long>(B) * rows / 2, 256)), dim3(256), 0, s, pdl,
+                   y, rows, bias, cos_t, sin_t, q0, H, KVH, hd, cap, qscale, q16, kc, vc, B, seq, pdl);
 }
 
-int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s) {
-  residual16_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, x16, h, d, B);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s, int pdl) {
+  return launch_ex(residual16_kernel, dim3(blocks_for(static_cast<long long>(B) * d, 256)), dim3(256), 0, s, pdl, y, x16,
+                   h, d, B, pdl);
 }
 
-int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s) {
-  residual32_kernel<<<blocks_for(static_cast<long long>(B) * d, 256), 256, 0, s>>>(y, h, x16, d, B);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s, int pdl) {
+  return launch_ex(residual32_kernel, dim3(blocks_for(static_cast<long long>(B) * d, 256)), dim3(256), 0, s, pdl, y, h,
+                   x16, d, B, pdl);
 }
 
-int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s) {
-  swiglu_kernel<<<blocks_for(static_cast<long long>(B) * F, 256), 256, 0, s>>>(y, act, F, B);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s, int pdl) {
+  return launch_ex(swiglu_kernel, dim3(blocks_for(static_cast<long long>(B) * F, 256)), dim3(256), 0, s, pdl, y, act,
+                   F, B, pdl);
 }
 
 int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
-                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s) {
-  argmax_gen_kernel<<<B, kArgThreads, 0, s>>>(logits, V, embed, d, q0, log, cap, tok, force_next, x16, err);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s, int pdl) {
+  return launch_ex(argmax_gen_kernel, dim3(B), dim3(kArgThreads), 0, s, pdl, logits, V, embed, d, q0, log, cap, tok,
+                   force_next, x16, err, pdl);
 }
 
 int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* flag, const unsigned* epoch,

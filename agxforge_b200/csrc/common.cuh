@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 namespace agxc {
 
@@ -116,6 +117,33 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// A kernel that may start before its predecessor in the stream has finished (pdl != 0): it waits for it before any
+// global memory access, and lets its own successor start.
+__device__ __forceinline__ void pdl_enter(int pdl) {
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+}
+
+// Launch with programmatic dependent launch allowed when pdl != 0 (the kernel calls pdl_enter / pdl_wait first).
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  AGXC_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+  return 0;
 }
 
 // D = A B + C, m16n8k16, fp16 operands, fp32 accumulate.

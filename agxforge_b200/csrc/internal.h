@@ -192,16 +192,16 @@ int launch_rows_argmax(const YRows& y, int V, int rows, float* logits, int32_t* 
 int launch_rope_append(const YRows& y, int rows, const __half* bias, const float* cos_t, const float* sin_t,
                        const uint32_t* q0, int H, int KVH, int hd, int cap, float qscale, __half* q16, __half* kc,
                        __half* vc, int B, cudaStream_t s, int seq = -1, const __half* qkg = nullptr,
-                       float qk_eps = 1e-6f);
+                       float qk_eps = 1e-6f, int pdl = 0);
 // causal attention of M prompt rows at positions p0 .. p0 + M - 1 of cache sequence `seq` (prefill.cu)
 int launch_prefill_attention(const __half* q16, const __half* kc, const __half* vc, int M, int p0, int H, int KVH,
                              int hd, int cap, int seq, __half* out, cudaStream_t s);
 int prefill_configure(const agxc_ctx* ctx);
-int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s);
-int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s);
-int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s);
+int launch_residual16(const YRows& y, const __half* x16, float* h, int d, int B, cudaStream_t s, int pdl = 0);
+int launch_residual32(const YRows& y, const float* h, __half* x16, int d, int B, cudaStream_t s, int pdl = 0);
+int launch_swiglu(const YRows& y, __half* act, int F, int B, cudaStream_t s, int pdl = 0);
 int launch_argmax_gen(const float* logits, int V, const __half* embed, int d, uint32_t* q0, uint32_t* log, int cap,
-                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s);
+                      int32_t* tok, uint32_t* force_next, __half* x16, unsigned* err, int B, cudaStream_t s, int pdl = 0);
 
 int launch_argmax_part(const float* logits, int V, int v0, uint32_t* pairs, int B, cudaStream_t s);
 int launch_gen_from_pairs(const uint32_t* pairs, int ranks, int V, const __half* embed, int d, uint32_t* q0,
@@ -242,8 +242,11 @@ struct QmmPush {
 // ksplit > 1: `part` [ksplit][B][N] fp32 scratch and `tile_ctr` [N / 128] zeroed counters (also needed by `push`);
 // the last K-range CTA of each tile sums the ranges in order into y (deterministic, y need not be cleared). y NULL
 // (ksplit > 1, no push): only the partial sums are written, for consumers that add them (YRows).
+// pdl: the GEMM may start before its predecessor in the stream finishes (its weight copies start at once; X, the
+// outputs and the counters wait for the predecessor)
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s, const QmmPush* push = nullptr, float* part = nullptr, unsigned* tile_ctr = nullptr);
+               cudaStream_t s, const QmmPush* push = nullptr, float* part = nullptr, unsigned* tile_ctr = nullptr,
+               int pdl = 0);
 // After the GEMM's pushes (use = *epoch x uses_per_step + use_in_step; every wait bounded). One-shot: wait until every
 // rank's tiles are here (*flag >= (use + 1) x ranks x ranks x tiles_per_rank), reduce every row in rank order plus the
 // residual into this rank's own output. Two-shot (one cooperative grid): wait for this rank's rows only (*flag >=
@@ -265,7 +268,7 @@ size_t attn_part_floats(int nb, int H, int S, int hd);
 int launch_attention(const agxc_ctx* ctx, const AttnParams& p, cudaStream_t s);
 int attn_configure(agxc_ctx* ctx);
 
-int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s);
+int launch_rmsnorm(const void* x, int x_f32, int nb, int d, const __half* g, float eps, __half* out, cudaStream_t s, int pdl = 0);
 
 // pack kernels
 int launch_quantize(const float* w, int N, int K, int bits, int sdt, uint32_t* packed, uint16_t* s16, uint16_t* b16,

@@ -345,18 +345,19 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     return g;
   };
   const float qscale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(hd)));
+  const int pdl = m->pdl ? 1 : 0;  // every kernel of the chain may start before its predecessor ends
   m->launches = 0;
   for (int l = 0; l < D.n_layers; ++l) {
     QmvParams p, q, g, w;
     AttnParams a;
     layer_params(m, l, p, a, q, g, w);
-    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, p.norm_gain, D.eps, m->xn16, s)) ||
+    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, p.norm_gain, D.eps, m->xn16, s, pdl)) ||
         (rc = gemm_r(m->qkv[l], m->xn16, m->qkv_rows)) ||
         (rc = launch_rope_append(yr, m->qkv_rows, p.bias, m->cos_t, m->sin_t, m->q0, H, KVH, hd, D.cap, qscale, m->q16,
-                                 p.kcache, p.vcache, B, s, -1, qk_gains_of(m, l), D.eps)) ||
+                                 p.kcache, p.vcache, B, s, -1, qk_gains_of(m, l), D.eps, pdl)) ||
         (rc = close()))
       return rc;
-    a.pdl = 0;
+    a.pdl = pdl;
     if ((rc = open()) || (rc = launch_attention(m->ctx, a, s)) || (rc = close())) return rc;
     if (fused) {  // o_proj tiles pushed to their owner ranks by the GEMM; each owner's sum + residual to every rank
       QmmPush ps = push_of(0);
@@ -369,14 +370,14 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     } else if (m->comm) {  // NCCL: the finished rows all-reduced, then the residual
       if ((rc = open()) || (rc = gemm(m->wo[l], m->attn, m->ybuf, d, nullptr)) ||
           (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s)) ||
-          (rc = launch_residual16(ydone, m->x16, m->h, d, B, s)) || (rc = close()))
+          (rc = launch_residual16(ydone, m->x16, m->h, d, B, s, pdl)) || (rc = close()))
         return rc;
     } else if ((rc = open()) || (rc = gemm_r(m->wo[l], m->attn, d)) ||
-               (rc = launch_residual16(yr, m->x16, m->h, d, B, s)) || (rc = close())) {
+               (rc = launch_residual16(yr, m->x16, m->h, d, B, s, pdl)) || (rc = close())) {
       return rc;
     }
-    if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s)) ||
-        (rc = gemm_r(m->gu[l], m->xn16, 2 * F)) || (rc = launch_swiglu(yr, m->act, F, B, s)) ||
+    if ((rc = open()) || (rc = launch_rmsnorm(m->h, 1, B, d, g.norm_gain, D.eps, m->xn16, s, pdl)) ||
+        (rc = gemm_r(m->gu[l], m->xn16, 2 * F)) || (rc = launch_swiglu(yr, m->act, F, B, s, pdl)) ||
         (rc = close()))
       return rc;
     if (fused) {
@@ -390,15 +391,15 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     } else if (m->comm) {
       if ((rc = open()) || (rc = gemm(m->down[l], m->act, m->ybuf, d, nullptr)) ||
           (rc = tp_allreduce_f32(m->comm, m->ybuf, static_cast<size_t>(B) * d, s)) ||
-          (rc = launch_residual32(ydone, m->h, m->x16, d, B, s)) || (rc = close()))
+          (rc = launch_residual32(ydone, m->h, m->x16, d, B, s, pdl)) || (rc = close()))
         return rc;
     } else if ((rc = open()) || (rc = gemm_r(m->down[l], m->act, d)) ||
-               (rc = launch_residual32(yr, m->h, m->x16, d, B, s)) || (rc = close())) {
+               (rc = launch_residual32(yr, m->h, m->x16, d, B, s, pdl)) || (rc = close())) {
       return rc;
     }
   }
   if (m->comm) {  // vocabulary sliced over ranks: local first maxima, all-gathered, then the same choice everywhere
-    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
+    if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s, pdl)) ||
         (rc = gemm(m->head, m->xn16, m->logits, D.vocab)) ||
         (rc = launch_argmax_part(m->logits, D.vocab, m->v0, m->amax, B, s)) ||
         (rc = tp_allgather_u32(m->comm, m->amax, m->amax_all, static_cast<size_t>(2) * B, s)) ||
@@ -409,10 +410,10 @@ int enqueue_step_batched(agxc_model* m, cudaStream_t s, cudaEvent_t* ev) {
     m->launches = 11 * D.n_layers + 4;  // this library's kernels (the collectives are the communicator's)
     return 0;
   }
-  if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s)) ||
+  if ((rc = open()) || (rc = launch_rmsnorm(m->x16, 0, B, d, m->final_gain, D.eps, m->xn16, s, pdl)) ||
       (rc = gemm(m->head, m->xn16, m->logits, D.vocab)) ||
       (rc = launch_argmax_gen(m->logits, D.vocab, m->embed, d, m->q0, m->log, D.cap, m->tok, m->force_next, m->x16,
-                              m->ctx->err_dev, B, s)) ||
+                              m->ctx->err_dev, B, s, pdl)) ||
       (rc = close()))
     return rc;
   m->launches = 11 * D.n_layers + 3;
@@ -950,7 +951,7 @@ int qmm_ksplit(const agxc_ctx* ctx, const agxc_pack& pk) {
 // ([ks][rows][N]) and the last range of each tile adds them up in order.
 int run_qmm(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, float* y, int ld, cudaStream_t s,
             float* part, const QmmPush* push) {
-  return launch_qmm(m->ctx, &pk, x, rows, y, ld, qmm_ksplit(m->ctx, pk), s, push, part, m->tile_ctr);
+  return launch_qmm(m->ctx, &pk, x, rows, y, ld, qmm_ksplit(m->ctx, pk), s, push, part, m->tile_ctr, m->pdl ? 1 : 0);
 }
 
 // The GEMM for consumers that add the K ranges themselves: split K writes the ranges' partial sums to `part` and
@@ -960,10 +961,10 @@ int gemm_rows(agxc_model* m, const agxc_pack& pk, const __half* x, int rows, flo
   const int ks = qmm_ksplit(m->ctx, pk);
   if (ks > 1) {
     *out = YRows{part, pk.n, ks, static_cast<size_t>(rows) * pk.n};
-    return launch_qmm(m->ctx, &pk, x, rows, nullptr, pk.n, ks, s, nullptr, part, nullptr);
+    return launch_qmm(m->ctx, &pk, x, rows, nullptr, pk.n, ks, s, nullptr, part, nullptr, m->pdl ? 1 : 0);
   }
   *out = YRows{ybuf, ld, 1, 0};
-  return launch_qmm(m->ctx, &pk, x, rows, ybuf, ld, 1, s);
+  return launch_qmm(m->ctx, &pk, x, rows, ybuf, ld, 1, s, nullptr, nullptr, nullptr, m->pdl ? 1 : 0);
 }
 
 // The tile counters (the widest pack's tiles) and a partial-sum scratch for `rows` activation rows of any of the

@@ -43,6 +43,7 @@ struct QmmParams {
   int stages = 4;
   int cg = 1;                     // 64-groups a chunk
   int nbuf = 8;                   // dequant buffers
+  int pdl = 0;                    // started before the predecessor finished: wait for it before X and any output
   float* y = nullptr;             // fp32 [B][ldy]
   int ldy = 0;
   float* part = nullptr;          // ksplit > 1: [ksplit][B][N] fp32, each K range's partial sums
@@ -237,6 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (p.pdl && warp != 0) {  // (the producer starts the weights first, then waits)
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 
   if (warp == 0) {
     // ---- producer
@@ -245,8 +250,28 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ts)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
       const unsigned bytes = static_cast<unsigned>(cg * (p.B * 128 + 8 * TB + 8 * 64));
-      int issued = 0;
-      for (int i = 0; i < gper && !*dead; ++i, ++issued) {
+      auto weights = [&](int i, uint8_t* st, uint64_t* bar) {
+        tma_3d(st + L.w_off, &tw, 0, g0 + i * cg, tile * 8, bar);
+        tma_3d(st + L.sb_off, &ts, 0, g0 + i * cg, tile * 8, bar);
+      };
+      auto acts = [&](int i, uint8_t* st, uint64_t* bar) {
+        for (int c = 0; c < cg; ++c)  // one 128-byte-swizzled atom of B rows x 64 columns each
+          tma_2d(st + L.x_off + c * p.B * 128, &tx, (g0 + i * cg + c) * 64, 0, bar);
+      };
+      // under programmatic dependent launch: the first stages' weights (independent of the predecessor) at once,
+      // then the wait, then their activations
+      const int pre = p.pdl ? min(S, gper) : 0;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&raw_full[i], bytes);
+        weights(i, smem + L.stage0 + i * L.stage_bytes, &raw_full[i]);
+      }
+      if (p.pdl) {
+        pdl_wait();
+        pdl_launch_dependents();
+      }
+      for (int i = 0; i < pre; ++i) acts(i, smem + L.stage0 + i * L.stage_bytes, &raw_full[i]);
+      int issued = pre;
+      for (int i = pre; i < gper && !*dead; ++i, ++issued) {
         const int s = i % S;
         if (i >= S && !mbar_wait_bounded(&raw_empty[s], ((i / S) - 1) & 1, p.err)) {
           *dead = 1;
@@ -254,10 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
         }
         uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
         mbar_arrive_expect_tx(&raw_full[s], bytes);
-        tma_3d(st + L.w_off, &tw, 0, g0 + i * cg, tile * 8, &raw_full[s]);
-        tma_3d(st + L.sb_off, &ts, 0, g0 + i * cg, tile * 8, &raw_full[s]);
-        for (int c = 0; c < cg; ++c)  // one 128-byte-swizzled atom of B rows x 64 columns each
-          tma_2d(st + L.x_off + c * p.B * 128, &tx, (g0 + i * cg + c) * 64, 0, &raw_full[s]);
+        weights(i, st, &raw_full[s]);
+        acts(i, st, &raw_full[s]);
       }
       if (*dead) {  // a wait gave up: no copy of this CTA may land after it leaves (bounded)
         for (int i = issued > S ? issued - S : 0; i < issued; ++i)
@@ -420,7 +443,7 @@ int qmm_configure(const agxc_ctx* ctx) {
 // Y [B][ldy] fp32 = X [B][K] fp16 x W^T for a pack W [N][K]: 128-row tiles, the K range split over ksplit CTAs when
 // the tiles alone would leave SMs idle (then Y must hold zeros: the CTAs add into it).
 int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, float* y, int ldy, int ksplit,
-               cudaStream_t s, const QmmPush* push, float* part, unsigned* tile_ctr) {
+               cudaStream_t s, const QmmPush* push, float* part, unsigned* tile_ctr, int pdl) {
   if (B < 32 || B > 256 || B % 16) return fail(AGXC_EINVAL, "qmm: 32 to 256 activation rows, a multiple of 16");
   if (pk->n % kM) return fail(AGXC_EINVAL, "qmm: N must be a multiple of 128");
   if (ldy < pk->n) return fail(AGXC_EINVAL, "qmm: ldy < N");
@@ -472,10 +495,9 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
   if (int rc = qmv_maps(plan, pk->tiles, pk->sb, pk->n, pk->k, pk->bits, &tw, &ts)) return rc;
   if (int rc = encode_act_map(&tx, x, B, pk->k)) return rc;
   const int grid = (pk->n / kM) * ksplit;
-  if (pk->bits == 4) qmm_kernel<4><<<grid, kThreads, smem, s>>>(p, tw, ts, tx);
-  else qmm_kernel<8><<<grid, kThreads, smem, s>>>(p, tw, ts, tx);
-  AGXC_CUDA(cudaGetLastError());
-  return 0;
+  p.pdl = pdl;
+  if (pk->bits == 4) return launch_ex(qmm_kernel<4>, dim3(grid), dim3(kThreads), smem, s, pdl, p, tw, ts, tx);
+  return launch_ex(qmm_kernel<8>, dim3(grid), dim3(kThreads), smem, s, pdl, p, tw, ts, tx);
 }
 
 }  // namespace agxc
