@@ -22,11 +22,20 @@ namespace {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
-// row b, column n of a GEMM's output (its K ranges added in order)
+// row b, column n of a GEMM's output (its K ranges added in order; with several ranges their loads are issued 8 at a
+// time and then added one after the other)
 __device__ __forceinline__ float yval(const YRows& y, int b, int n) {
-  const size_t at = static_cast<size_t>(b) * y.ld + n;
-  float v = y.y[at];
-  for (int q = 1; q < y.ks; ++q) v += y.y[q * y.slice + at];
+  const float* src = y.y + static_cast<size_t>(b) * y.ld + n;
+  float v = src[0];
+  if (y.ks == 1) return v;
+  for (int q0 = 1; q0 < y.ks; q0 += 8) {
+    float t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = q0 + j < y.ks ? src[(q0 + j) * y.slice] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (q0 + j < y.ks) v += t[j];
+  }
   return v;
 }
 
@@ -301,6 +310,8 @@ __device__ bool wait_flag_sys(const unsigned* flag, unsigned target, unsigned* e
   }
 }
 
+constexpr int kMaxRanks = 8;
+
 // Tensor parallel, after the GEMM's pushes. Two-shot (one cooperative grid: its blocks wait on one another's gather
 // signals, so all are resident): this rank's rows [rank d / ranks, ...) = the sum over ranks in rank order plus the
 // residual, stored into every rank's residual stream. One-shot: every row, reduced here and stored here only. Either
@@ -405,6 +416,7 @@ int launch_tp_reduce(const float* recv, int ranks, int rank, const unsigned* fla
                      int uses_per_step, int use_in_step, int tiles_per_rank, const __half* res16, const float* res32,
                      const TpGather& gather, int d, int B, unsigned* err, cudaStream_t s, bool two_shot,
                      uint64_t wait_ns) {
+  if (ranks < 1 || ranks > kMaxRanks) return fail(AGXC_EINVAL, "tp_reduce: 1 to 8 ranks");
   if (d % (4 * ranks)) return fail(AGXC_EINVAL, "tp_reduce: d a multiple of 4 x ranks");
   const long long elems4 = static_cast<long long>(B) * d / (two_shot ? ranks : 1) / 4;
   // two-shot: a fixed grid, the same on every rank (the gather target counts every rank's blocks), all resident

@@ -65,6 +65,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0;
 }
 
+// The same with a suspend-time hint: a thread whose phase is not complete sleeps (issuing nothing) until the phase
+// completes or about hint_ns pass.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, unsigned parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -92,6 +104,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
   for (unsigned it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) {
+      if (err) atomicOr(err, kErrMbarTimeout);
+      return false;
+    }
+  }
+}
+
+// The bounded wait for warps that share a scheduler with busy ones: between polls the thread sleeps until the phase
+// completes (or 0.2 ms pass), so a waiting warp takes no issue slots from the warps still working.
+__device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, unsigned parity, unsigned* err,
+                                                uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 200000u)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) {
       if (err) atomicOr(err, kErrMbarTimeout);
       return false;
     }

@@ -7,15 +7,19 @@
 //   * the PRODUCER warp brings the chunk's 8 packed row tiles x cg groups and their scale/bias (two 3-D TMA boxes of
 //     the pack) and the activations' cg x 64 columns (2-D TMA boxes of X [B][K] fp16, 128-byte swizzle) into a ring
 //     stage;
-//   * eight DEQUANT warps turn the tiles into fp16 weights in the MMA's canonical K-major 128-byte-swizzled layout
-//     (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes 1024 away
-//     exactly, HFMA2 applies the row's scale and bias with one rounding); each warp a row tile, cg groups a chunk:
-//     the barrier waits and the proxy fence of a chunk (about as long as one group's arithmetic) are paid once for cg
-//     groups;
-//   * the MMA warp issues 4 cg tcgen05.mma.kind::f16 (M 128, N B, K 16) accumulating in TMEM, and commits: the
-//     commit releases the stage and the dequant buffer when the tensor core has read them.
-// After the last chunk the dequant warps read the 128 x B fp32 accumulator back with tcgen05.ld (warp w reads TMEM
-// lanes 32 (w % 4) ..; the two warps of a lane quarter split the columns) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
+//   * sixteen DEQUANT warps turn the tiles into fp16 weights and store them straight into TENSOR MEMORY, the MMA's A
+//     operand (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes
+//     1024 away exactly, HFMA2 applies the row's scale and bias with one rounding). One thread is one weight row =
+//     one TMEM lane (a warp's 32 lanes are its quarter of the 128 rows); a group is 64 fp16 = 32 columns, written
+//     with tcgen05.st. The four warps of a lane quarter split a chunk's cg x 64 k in 16 k (cg 1) or 32 k (cg 2)
+//     slices: each warp's share is short, and four of them a scheduler hide one another's latencies (the conversion
+//     is latency-bound: the MMA waits for the slowest warp of a chunk). The fp16 weights never pass through shared
+//     memory;
+//   * the MMA warp issues 4 cg tcgen05.mma.kind::f16 (M 128, N B, K 16; A from TMEM, B = X from shared memory)
+//     accumulating in TMEM, and commits: the commit releases the stage and the TMEM A buffer when the tensor core has
+//     read them.
+// After the last chunk the first eight dequant warps read the 128 x B fp32 accumulator back with tcgen05.ld (warp w
+// reads TMEM lanes 32 (w % 4) ..; the two warps of a lane quarter split the columns) and store Y (fp32 [B][N]; atomically added when K is split over CTAs). Every wait is bounded.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -30,9 +34,12 @@ namespace agxc {
 namespace {
 
 constexpr int kM = 128;          // weight rows per CTA (the MMA's M)
-constexpr int kThreads = 320;    // warp 0 producer, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
-constexpr int kDeqWarps = 8;
-constexpr int kMaxDeqBufs = 8;   // fp16 weight buffers in flight between the dequant warps and the tensor core
+constexpr int kDeqWarps = 16;    // four a TMEM lane quarter
+constexpr int kEpiWarps = 8;     // the first eight dequant warps also run the epilogue
+constexpr int kThreads = 64 + 32 * kDeqWarps;  // warp 0 producer, warp 1 MMA + TMEM, then the dequant warps
+constexpr int kTmemCols = 512;   // the whole tensor memory of the SM (one CTA per SM: the ring takes the shared memory)
+constexpr int kAcol = 256;       // A buffers from this column (the accumulator takes columns 0 .. B - 1 <= 255)
+constexpr int kABufCols = 256;   // nbuf x cg groups x 32 columns
 
 struct QmmParams {
   const uint8_t* w = nullptr;
@@ -42,7 +49,7 @@ struct QmmParams {
   int ksplit = 1;                 // K ranges (CTAs) per 128-row tile
   int stages = 4;
   int cg = 1;                     // 64-groups a chunk
-  int nbuf = 8;                   // dequant buffers
+  int nbuf = 4;                   // TMEM A buffers (of cg groups each; nbuf x cg <= 8)
   int pdl = 0;                    // started before the predecessor finished: wait for it before X and any output
   float* y = nullptr;             // fp32 [B][ldy]
   int ldy = 0;
@@ -53,16 +60,15 @@ struct QmmParams {
 };
 
 struct QmmSmem {
-  int bars, tmem_slot, deq, stage0, stage_bytes, x_off, w_off, sb_off, total;
+  int bars, tmem_slot, stage0, stage_bytes, x_off, w_off, sb_off, total;
 };
 
-__host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages, int cg, int nbuf) {
+__host__ __device__ inline QmmSmem qmm_layout(int bits, int B, int stages, int cg) {
   QmmSmem L;
   const int TB = bits == 4 ? 512 : 1024;
   L.bars = 0;                                   // raw_full[S], raw_empty[S], deq_full[D], deq_empty[D], acc_full
   L.tmem_slot = 512;                            // (S <= 16, D <= 8: the barriers fit below)
-  L.deq = 1024;                                 // nbuf buffers of cg atoms 128 x 64 fp16 (16 KB each)
-  L.stage0 = L.deq + nbuf * cg * kM * 128;
+  L.stage0 = 1024;
   L.x_off = 0;                                  // X: cg atoms of B rows x 128 B (1,024-aligned for the swizzle)
   L.w_off = (cg * B * 128 + 1023) / 1024 * 1024;
   L.sb_off = L.w_off + 8 * cg * TB;             // the boxes land row tile-major: (row tile, group) at (r cg + c)
@@ -107,6 +113,21 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+// One lane of the (converged) warp: true there, false elsewhere.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile("{\n .reg .pred P;\n elect.sync _|P, 0xffffffff;\n selp.b32 %0, 1, 0, P;\n}\n" : "=r"(pred));
+  return pred != 0;
+}
+// D (TMEM) += A (TMEM) x B (shared-memory descriptor), or D = A x B when accumulate is false.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(static_cast<uint32_t>(accumulate))
+      : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -137,57 +158,60 @@ __device__ __forceinline__ uint16_t to_f16_bits(uint16_t v, int sdt) {
   return __half_as_ushort(__float2half_rn(__uint_as_float(static_cast<uint32_t>(v) << 16)));
 }
 
-// One lane-task of the dequantisation: lane (r, c) of row tile t of the chunk -> rows 16t + r and 16t + r + 8,
-// k = 16c .. 16c + 15 (16-byte chunks 2c and 2c + 1 of each 128-byte row), fp16, swizzled.
-// wraw / sbraw: the group's tiles and scale/bias, row tile t at t * wstride / t * sbstride bytes.
-template <int BITS>
-__device__ __forceinline__ void dequant_task(const uint8_t* wraw, const uint8_t* sbraw, uint8_t* deq, int t, int l,
-                                             int sdt, int wstride, int sbstride) {
-  const int r = l >> 2, c = l & 3;
-  const uint2 e = *reinterpret_cast<const uint2*>(sbraw + t * sbstride + r * 8);  // {s[r], s[r+8], b[r], b[r+8]}
-  const uint32_t s0 = to_f16_bits(static_cast<uint16_t>(e.x & 0xFFFFu), sdt);
-  const uint32_t s1 = to_f16_bits(static_cast<uint16_t>(e.x >> 16), sdt);
-  const uint32_t b0 = to_f16_bits(static_cast<uint16_t>(e.y & 0xFFFFu), sdt);
-  const uint32_t b1 = to_f16_bits(static_cast<uint16_t>(e.y >> 16), sdt);
-  const uint32_t s2[2] = {s0 | (s0 << 16), s1 | (s1 << 16)};
-  const uint32_t b2[2] = {b0 | (b0 << 16), b1 | (b1 << 16)};
-  uint32_t o[2][2][4];  // [row half][chunk][word]
-  if (BITS == 4) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(wraw + t * wstride + l * 16);
-    const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};  // i: row r + 8 (i & 1), hi = i >> 1
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// One weight row of one group, lane slots c0 .. c0 + NC - 1 (16 k each): the row's fp16 weights, k in order, into
+// NC x 8 TMEM columns of this thread's lane from column taddr. wt / sbt: the row's tile (16 rows x 64 k in the GEMV
+// fragment layout: lane slot (r, c) holds rows r and r + 8 at k = 16c ..) and its scale/bias in the stage; r16: the
+// row within the tile.
+template <int BITS, int NC>
+__device__ __forceinline__ void dequant_row(const uint8_t* wt, const uint8_t* sbt, int r16, int c0, int sdt,
+                                            uint32_t taddr) {
+  const int r = r16 & 7, h = r16 >> 3;
+  const uint2 e = *reinterpret_cast<const uint2*>(sbt + r * 8);  // {s[r], s[r+8]}, {b[r], b[r+8]}
+  const uint32_t sv = to_f16_bits(static_cast<uint16_t>(h ? e.x >> 16 : e.x & 0xFFFFu), sdt);
+  const uint32_t bv = to_f16_bits(static_cast<uint16_t>(h ? e.y >> 16 : e.y & 0xFFFFu), sdt);
+  const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
+  constexpr int U = NC < 2 ? NC : 2;  // lane slots a store
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {      // row r (h 0) or r + 8 (h 1)
+  for (int cc = 0; cc < NC; cc += U) {
+    uint32_t o[8 * U];  // columns 8 (c0 + cc) .. : the pair (k0, k0 + 1) at column k0 / 2
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {    // pair (k0, k0 + 1), k0 = 16c + 4j + 2hi
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + cc + u;
+      if (BITS == 4) {
+        // word i of the slot: row r + 8 (i & 1), k0 = 16c + 4j + 2 (i >> 1) for the field pair at bits 4j, 16 + 4j
+        const uint4 wv = *reinterpret_cast<const uint4*>(wt + (r * 4 + c) * 16);
+        const uint32_t w0 = h ? wv.y : wv.x, w1 = h ? wv.w : wv.z;
 #pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-          const uint32_t q = ((w[h + 2 * hi] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-          o[h][j >> 1][2 * (j & 1) + hi] = hfma2(hsub_1024(q), s2[h], b2[h]);
+        for (int j = 0; j < 4; ++j) {
+          o[8 * u + 2 * j] = hfma2(hsub_1024(((w0 >> (4 * j)) & 0x000F000Fu) | 0x64006400u), s2, b2);
+          o[8 * u + 2 * j + 1] = hfma2(hsub_1024(((w1 >> (4 * j)) & 0x000F000Fu) | 0x64006400u), s2, b2);
         }
+      } else {
+        // word wi: k0 = 16c + 2 wi; bytes 0, 1 row r, bytes 2, 3 row r + 8
+        const uint4 lo = *reinterpret_cast<const uint4*>(wt + (r * 4 + c) * 16);
+        const uint4 hi4 = *reinterpret_cast<const uint4*>(wt + 512 + (r * 4 + c) * 16);
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi4.x, hi4.y, hi4.z, hi4.w};
+        const uint32_t sel = h ? 0x4342u : 0x4140u;
+#pragma unroll
+        for (int wi = 0; wi < 8; ++wi) o[8 * u + wi] = hfma2(hsub_1024(prmt(w[wi], 0x64646464u, sel)), s2, b2);
       }
     }
-  } else {
-    const uint4 lo = *reinterpret_cast<const uint4*>(wraw + t * wstride + l * 16);
-    const uint4 hi4 = *reinterpret_cast<const uint4*>(wraw + t * wstride + 512 + l * 16);
-    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi4.x, hi4.y, hi4.z, hi4.w};  // wi: k0 = 16c + 4 (wi >> 1) + 2 (wi & 1)
-#pragma unroll
-    for (int wi = 0; wi < 8; ++wi) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t q = prmt(w[wi], 0x64646464u, h ? 0x4342u : 0x4140u);  // (1024 + q[k0], 1024 + q[k0 + 1])
-        o[h][wi >> 2][wi & 3] = hfma2(hsub_1024(q), s2[h], b2[h]);
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int row = 16 * t + r + 8 * h;
-#pragma unroll
-    for (int ch = 0; ch < 2; ++ch) {
-      const int chunk = 2 * c + ch;
-      *reinterpret_cast<uint4*>(deq + row * 128 + (((chunk ^ (row & 7)) & 7) << 4)) =
-          make_uint4(o[h][ch][0], o[h][ch][1], o[h][ch][2], o[h][ch][3]);
-    }
+    if (U == 2) tmem_st16(taddr + 8 * cc, o);
+    else tmem_st8(taddr + 8 * cc, o);
   }
 }
 
@@ -199,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr int TB = BITS == 4 ? 512 : 1024;
   const int cg = p.cg, D = p.nbuf;
-  const QmmSmem L = qmm_layout(BITS, p.B, p.stages, cg, D);
+  const QmmSmem L = qmm_layout(BITS, p.B, p.stages, cg);
   const int S = p.stages;
   uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* raw_empty = raw_full + S;
@@ -213,7 +237,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   const int gk = p.G / p.ksplit;                // groups of this CTA's K range
   const int g0 = ks * gk;
   const int gper = gk / cg;                     // its chunks
-  const int ncols = p.B <= 32 ? 32 : p.B <= 64 ? 64 : p.B <= 128 ? 128 : 256;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -228,9 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
     *dead = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {  // TMEM: ncols fp32 columns x 128 lanes for the accumulator
+  if (warp == 1) {  // TMEM: the accumulator (B fp32 columns x 128 lanes) and the A buffers
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(ncols)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     tc_fence_before();
@@ -244,171 +267,196 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   }
 
   if (warp == 0) {
-    // ---- producer
-    if (lane == 0) {
+    // ---- producer: the whole warp walks the chunks (its coordinates stay warp-uniform), one elected lane issues
+    const bool leader = elect_one();
+    if (leader) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&ts)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tx)) : "memory");
-      const unsigned bytes = static_cast<unsigned>(cg * (p.B * 128 + 8 * TB + 8 * 64));
-      auto weights = [&](int i, uint8_t* st, uint64_t* bar) {
-        tma_3d(st + L.w_off, &tw, 0, g0 + i * cg, tile * 8, bar);
-        tma_3d(st + L.sb_off, &ts, 0, g0 + i * cg, tile * 8, bar);
-      };
-      auto acts = [&](int i, uint8_t* st, uint64_t* bar) {
-        for (int c = 0; c < cg; ++c)  // one 128-byte-swizzled atom of B rows x 64 columns each
-          tma_2d(st + L.x_off + c * p.B * 128, &tx, (g0 + i * cg + c) * 64, 0, bar);
-      };
-      // under programmatic dependent launch: the first stages' weights (independent of the predecessor) at once,
-      // then the wait, then their activations
-      const int pre = p.pdl ? min(S, gper) : 0;
+    }
+    const unsigned bytes = static_cast<unsigned>(cg * (p.B * 128 + 8 * TB + 8 * 64));
+    auto weights = [&](int i, uint8_t* st, uint64_t* bar) {
+      tma_3d(st + L.w_off, &tw, 0, g0 + i * cg, tile * 8, bar);
+      tma_3d(st + L.sb_off, &ts, 0, g0 + i * cg, tile * 8, bar);
+    };
+    auto acts = [&](int i, uint8_t* st, uint64_t* bar) {
+      for (int c = 0; c < cg; ++c)  // one 128-byte-swizzled atom of B rows x 64 columns each
+        tma_2d(st + L.x_off + c * p.B * 128, &tx, (g0 + i * cg + c) * 64, 0, bar);
+    };
+    // under programmatic dependent launch: the first stages' weights (independent of the predecessor) at once, then
+    // the wait, then their activations
+    const int pre = p.pdl ? min(S, gper) : 0;
+    if (leader)
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&raw_full[i], bytes);
         weights(i, smem + L.stage0 + i * L.stage_bytes, &raw_full[i]);
       }
-      if (p.pdl) {
-        pdl_wait();
-        pdl_launch_dependents();
-      }
+    if (p.pdl) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    if (leader)
       for (int i = 0; i < pre; ++i) acts(i, smem + L.stage0 + i * L.stage_bytes, &raw_full[i]);
-      int issued = pre;
-      for (int i = pre; i < gper && !*dead; ++i, ++issued) {
-        const int s = i % S;
-        if (i >= S && !mbar_wait_bounded(&raw_empty[s], ((i / S) - 1) & 1, p.err)) {
-          *dead = 1;
-          break;
-        }
-        uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+    int issued = pre;
+    bool gave_up = false;
+    for (int i = pre, s = pre % S, eph = (pre / S + 1) & 1; i < gper; ++i, ++issued) {
+      // stage s was last filled for chunk i - S: wait for the commit of its MMAs (phase eph of raw_empty)
+      const bool ok = !*dead && (i < S || mbar_wait_quiet(&raw_empty[s], static_cast<unsigned>(eph), p.err));
+      if (!__all_sync(0xffffffffu, ok)) {
+        gave_up = true;
+        break;
+      }
+      uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
+      if (leader) {
         mbar_arrive_expect_tx(&raw_full[s], bytes);
         weights(i, st, &raw_full[s]);
         acts(i, st, &raw_full[s]);
       }
-      if (*dead) {  // a wait gave up: no copy of this CTA may land after it leaves (bounded)
+      __syncwarp();
+      if (++s == S) { s = 0; eph ^= 1; }
+    }
+    if (gave_up || *dead) {
+      *dead = 1;
+      if (leader)  // a wait gave up: no copy of this CTA may land after it leaves (bounded)
         for (int i = issued > S ? issued - S : 0; i < issued; ++i)
           mbar_wait_bounded(&raw_full[i % S], (i / S) & 1, nullptr, 100000000ull);
-      }
     }
+    __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16(p.B);
-      for (int i = 0, d = 0, dph = 0, s = 0; i < gper; ++i) {
-        if (*dead || !mbar_wait_bounded(&deq_full[d], static_cast<unsigned>(dph), p.err)) {
-          *dead = 1;
-          break;
-        }
-        tc_fence_after();
+    // ---- MMA issuer: the whole warp walks the chunks (its TMEM addresses and descriptors stay warp-uniform), one
+    // elected lane issues each chunk's MMAs and commits. The B descriptor of (stage s, group c, k step) is stage 0's
+    // plus the byte offset / 16 (the start-address field; smem addresses stay below 2^18, so no carry leaves it).
+    const uint32_t idesc = idesc_f16(p.B);
+    const uint64_t bd0 = desc_sw128(smem_u32(smem + L.stage0 + L.x_off));
+    const uint64_t bd_stage = static_cast<uint64_t>(L.stage_bytes >> 4), bd_atom = static_cast<uint64_t>(p.B * 8);
+    const bool leader = elect_one();
+    for (int i = 0, d = 0, dph = 0, s = 0; i < gper; ++i) {
+      const bool ok = !*dead && mbar_wait_quiet(&deq_full[d], static_cast<unsigned>(dph), p.err);
+      if (!__all_sync(0xffffffffu, ok)) {
+        *dead = 1;
+        break;
+      }
+      tc_fence_after();
+      if (leader) {
+        const uint64_t bs = bd0 + static_cast<uint64_t>(s) * bd_stage;
+        const uint32_t as = tmem + kAcol + d * cg * 32;  // the chunk's groups: 32 columns of fp16 pairs each
         for (int c = 0; c < cg; ++c) {
-          const uint32_t a0 = smem_u32(smem + L.deq + (d * cg + c) * kM * 128);
-          const uint32_t b0 = smem_u32(smem + L.stage0 + s * L.stage_bytes + L.x_off + c * p.B * 128);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {  // four K = 16 steps: +32 bytes within the swizzled 128-byte rows
-            const uint64_t ad = desc_sw128(a0 + 32 * k), bd = desc_sw128(b0 + 32 * k);
-            const uint32_t acc = (i > 0 || c > 0 || k > 0) ? 1u : 0u;
-            asm volatile(
-                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
-                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-                : "memory");
-          }
+          for (int k = 0; k < 4; ++k)  // four K = 16 steps: A +8 columns, B +32 bytes in the swizzled 128-byte rows
+            tc_mma(tmem, as + c * 32 + 8 * k, bs + c * bd_atom + 2 * k, idesc, (i | c | k) != 0);
         }
         tc_commit(&raw_empty[s]);  // the stage (weights read, X read) is free once these MMAs are done
         tc_commit(&deq_empty[d]);
-        if (++s == S) s = 0;
-        if (++d == D) { d = 0; dph ^= 1; }
       }
-      tc_commit(acc_full);  // every MMA of the CTA done: the accumulator is final
+      __syncwarp();
+      if (++s == S) s = 0;
+      if (++d == D) { d = 0; dph ^= 1; }
     }
+    if (leader) tc_commit(acc_full);  // every MMA of the CTA done: the accumulator is final
+    __syncwarp();
   } else {
     // ---- dequant warps, then the epilogue
-    const int dw = warp - 2;  // 0..7
+    const int dw = warp - 2;  // 0 .. kDeqWarps - 1
+    const int q4 = warp & 3;  // this warp's TMEM lane quarter: CTA rows 32 q4 .. + 31, one a thread
+    const int rt = (32 * q4 + lane) >> 4, r16 = lane & 15;
+    // the warp's slice of the chunk (si = 0..3 within its quarter): cg 2: group si / 2, k 32 (si % 2) ..; cg 1: k 16 si
+    const int si = dw >> 2;
+    const int gc = cg == 2 ? si >> 1 : 0, cslot = cg == 2 ? 2 * (si & 1) : si;
+    const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     for (int i = 0, s = 0, sph = 0, d = 0, dph = 0; i < gper; ++i) {
-      const bool ok1 = !*dead && mbar_wait_bounded(&raw_full[s], static_cast<unsigned>(sph), p.err);
-      const bool ok2 = ok1 && (i < D || mbar_wait_bounded(&deq_empty[d], static_cast<unsigned>(dph ^ 1), p.err));
+      const bool ok1 = !*dead && mbar_wait_quiet(&raw_full[s], static_cast<unsigned>(sph), p.err);
+      const bool ok2 = ok1 && (i < D || mbar_wait_quiet(&deq_empty[d], static_cast<unsigned>(dph ^ 1), p.err));
       if (!__all_sync(0xffffffffu, ok2)) {  // the warp leaves together
         *dead = 1;
         break;
       }
       const uint8_t* st = smem + L.stage0 + s * L.stage_bytes;
-      for (int c = 0; c < cg; ++c)  // warp dw: row tile dw of each of the chunk's groups
-        dequant_task<BITS>(st + L.w_off + c * TB, st + L.sb_off + c * 64, smem + L.deq + (d * cg + c) * kM * 128, dw,
-                           lane, p.sdt, cg * TB, cg * 64);
-      fence_proxy_async();  // the tensor core reads what these generic stores wrote
+      // (row tile rt, group gc) of the chunk sits at (rt cg + gc) in the stage's boxes
+      const uint8_t* wt = st + L.w_off + (rt * cg + gc) * TB;
+      const uint8_t* sbt = st + L.sb_off + (rt * cg + gc) * 64;
+      const uint32_t ta = tlane + kAcol + (d * cg + gc) * 32 + 8 * cslot;
+      if (cg == 2) dequant_row<BITS, 2>(wt, sbt, r16, cslot, p.sdt, ta);
+      else dequant_row<BITS, 1>(wt, sbt, r16, cslot, p.sdt, ta);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();    // the MMA warp reads these columns after its barrier wait
       __syncwarp();
       if (lane == 0) mbar_arrive1(&deq_full[d]);
       if (++s == S) { s = 0; sph ^= 1; }
       if (++d == D) { d = 0; dph ^= 1; }
     }
-    // epilogue: TMEM lanes 32 (warp % 4) .. + 31 = weight rows; columns = activation rows
-    const bool ok = __all_sync(0xffffffffu, !*dead && mbar_wait_bounded(acc_full, 0, p.err));  // warp-uniform:
-    tc_fence_after();                                                                        // tcgen05.ld is aligned
-    if (ok) {
-      const int q4 = warp & 3;
-      const int row = tile * kM + 32 * q4 + lane;
-      const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
-      const int half = (p.B / 16 + 1) / 2 * 16;  // columns of the first warp of the quarter
-      const int cb = dw < 4 ? 0 : half, ce = dw < 4 ? half : p.B;
-      for (int c0 = cb; c0 < ce; c0 += 16) {
-        uint32_t v[16];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-            "%14, %15}, [%16];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(base + static_cast<uint32_t>(c0)));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < p.N) {
-          // one K range: straight into Y; several: this range's partial sums into its own slice
-          float* dst = p.ksplit > 1 ? p.part + static_cast<size_t>(ks) * p.B * p.N : p.y;
-          const int ld = p.ksplit > 1 ? p.N : p.ldy;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(c0 + j) * ld + row] = __uint_as_float(v[j]);
-        }
-      }
-    }
-    const bool push = p.push.ranks > 0;
-    if ((p.ksplit > 1 && p.y) || push) {  // (y NULL: the consumers add the K ranges themselves)
-      // the tile's last K-range CTA sums the ranges in order (the same result every run: no atomics on the data)
-      // and, under tensor parallelism, sends the finished B x 128 block of Y to the ranks
-      __threadfence();                               // this CTA's partial sums are visible at L2
-      const bool all_ok = epi_all(ok);
-      volatile int* s_last = dead + 1;
-      if (all_ok && dw == 0 && lane == 0) {
-        const unsigned prev = atomicAdd(p.tile_ctr + tile, 1u);
-        *s_last = prev == static_cast<unsigned>(p.ksplit - 1);
-        if (*s_last) p.tile_ctr[tile] = 0;           // every K-range CTA of the tile has arrived
-      }
-      epi_sync();
-      if (all_ok && *s_last) {
-        __threadfence();                             // the other CTAs' partials, read below from L2
-        // to_owner: the tile's rows go to the one rank owning them (reduce-scatter; d / ranks consecutive rows a
-        // rank); else to every rank (each then reduces all rows itself)
-        const int r0 = push && p.push.to_owner ? tile / p.push.tiles_per_rank : 0;
-        const int r1 = !push ? 0 : p.push.to_owner ? r0 + 1 : p.push.ranks;
-        const int et = dw * 32 + lane;               // 0 .. 255
-        const size_t slice = static_cast<size_t>(p.B) * p.N;
-        for (int i = et; i < p.B * (kM / 4); i += 256) {
-          const int b = i / (kM / 4), n = tile * kM + (i % (kM / 4)) * 4;
-          float4 v4;
-          if (p.ksplit > 1) {
-            const float* src = p.part + static_cast<size_t>(b) * p.N + n;
-            v4 = __ldcg(reinterpret_cast<const float4*>(src));
-            for (int q = 1; q < p.ksplit; ++q) {
-              const float4 t4 = __ldcg(reinterpret_cast<const float4*>(src + q * slice));
-              v4.x += t4.x; v4.y += t4.y; v4.z += t4.z; v4.w += t4.w;
-            }
-            *reinterpret_cast<float4*>(p.y + static_cast<size_t>(b) * p.ldy + n) = v4;
-          } else {
-            v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
+    // epilogue (the first eight dequant warps): TMEM lanes 32 (warp % 4) .. + 31 = weight rows; columns =
+    // activation rows
+    if (dw < kEpiWarps) {
+      const bool ok = __all_sync(0xffffffffu, !*dead && mbar_wait_quiet(acc_full, 0, p.err));  // warp-uniform:
+      tc_fence_after();                                                                        // tcgen05.ld is aligned
+      if (ok) {
+        const int row = tile * kM + 32 * q4 + lane;
+        const uint32_t base = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+        const int half = (p.B / 16 + 1) / 2 * 16;  // columns of the first warp of the quarter
+        const int cb = dw < 4 ? 0 : half, ce = dw < 4 ? half : p.B;
+        for (int c0 = cb; c0 < ce; c0 += 16) {
+          uint32_t v[16];
+          asm volatile(
+              "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+              "%14, %15}, [%16];"
+              : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+              : "r"(base + static_cast<uint32_t>(c0)));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (row < p.N) {
+            // one K range: straight into Y; several: this range's partial sums into its own slice
+            float* dst = p.ksplit > 1 ? p.part + static_cast<size_t>(ks) * p.B * p.N : p.y;
+            const int ld = p.ksplit > 1 ? p.N : p.ldy;
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(c0 + j) * ld + row] = __uint_as_float(v[j]);
           }
-          for (int r = r0; r < r1; ++r)
-            *reinterpret_cast<float4*>(p.push.slot[r] + static_cast<size_t>(b) * p.N + n) = v4;
         }
-        if (push) {
-          __threadfence_system();                    // the stores reach their ranks before the counters move
-          epi_sync();
-          if (et == 0)
+      }
+      const bool push = p.push.ranks > 0;
+      if ((p.ksplit > 1 && p.y) || push) {  // (y NULL: the consumers add the K ranges themselves)
+        // the tile's last K-range CTA sums the ranges in order (the same result every run: no atomics on the data)
+        // and, under tensor parallelism, sends the finished B x 128 block of Y to the ranks
+        __threadfence();                               // this CTA's partial sums are visible at L2
+        const bool all_ok = epi_all(ok);
+        volatile int* s_last = dead + 1;
+        if (all_ok && dw == 0 && lane == 0) {
+          const unsigned prev = atomicAdd(p.tile_ctr + tile, 1u);
+          *s_last = prev == static_cast<unsigned>(p.ksplit - 1);
+          if (*s_last) p.tile_ctr[tile] = 0;           // every K-range CTA of the tile has arrived
+        }
+        epi_sync();
+        if (all_ok && *s_last) {
+          __threadfence();                             // the other CTAs' partials, read below from L2
+          // to_owner: the tile's rows go to the one rank owning them (reduce-scatter; d / ranks consecutive rows a
+          // rank); else to every rank (each then reduces all rows itself)
+          const int r0 = push && p.push.to_owner ? tile / p.push.tiles_per_rank : 0;
+          const int r1 = !push ? 0 : p.push.to_owner ? r0 + 1 : p.push.ranks;
+          const int et = dw * 32 + lane;               // 0 .. 255
+          const size_t slice = static_cast<size_t>(p.B) * p.N;
+          for (int i = et; i < p.B * (kM / 4); i += 256) {
+            const int b = i / (kM / 4), n = tile * kM + (i % (kM / 4)) * 4;
+            float4 v4;
+            if (p.ksplit > 1) {
+              const float* src = p.part + static_cast<size_t>(b) * p.N + n;
+              v4 = __ldcg(reinterpret_cast<const float4*>(src));
+              for (int q = 1; q < p.ksplit; ++q) {
+                const float4 t4 = __ldcg(reinterpret_cast<const float4*>(src + q * slice));
+                v4.x += t4.x; v4.y += t4.y; v4.z += t4.z; v4.w += t4.w;
+              }
+              *reinterpret_cast<float4*>(p.y + static_cast<size_t>(b) * p.ldy + n) = v4;
+            } else {
+              v4 = __ldcg(reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.ldy + n));
+            }
             for (int r = r0; r < r1; ++r)
-              asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
+              *reinterpret_cast<float4*>(p.push.slot[r] + static_cast<size_t>(b) * p.N + n) = v4;
+          }
+          if (push) {
+            __threadfence_system();                    // the stores reach their ranks before the counters move
+            epi_sync();
+            if (et == 0)
+              for (int r = r0; r < r1; ++r)
+                asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.push.flag[r]) : "memory");
+          }
         }
       }
     }
@@ -419,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -462,31 +510,17 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
       return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks owning equal numbers of 128-row tiles");
     p.push = *push;
   }
-  // the chunk: 2 groups where the K range divides and at least three stages fit beside the dequant buffers (the
-  // dequant warps' per-chunk waits and fence then cover two groups), else 1; as many stages as fit (at most 16: a stage
-  // cycles through the copy, the dequant and the MMA's completion before it is refilled, so small stages want many)
+  // the chunk: 2 groups where the K range divides (the dequant warps' per-chunk waits then cover two groups), else
+  // 1; the TMEM A buffers hold 8 groups either way; as many stages as fit (at most 16: a stage cycles through the
+  // copy, the dequant and the MMA's completion before it is refilled, so small stages want many)
   const int gk = G / ksplit;
-  auto stages_for = [&](int cg, int nbuf) {
-    int st = 16;
-    while (st > 2 && qmm_layout(pk->bits, B, st, cg, nbuf).total + 1024 > ctx->max_smem_optin - 2048) --st;
-    return qmm_layout(pk->bits, B, st, cg, nbuf).total + 1024 > ctx->max_smem_optin - 2048 ? 0 : st;
-  };
-  p.cg = 1;
-  p.nbuf = kMaxDeqBufs;
-  p.stages = 0;
-  const int opts[][3] = {{2, 4, 3}, {2, 3, 3}, {1, 8, 2}, {1, 4, 2}, {1, 2, 2}};  // cg, buffers, fewest stages
-  for (const auto& o : opts) {
-    if (gk % o[0]) continue;
-    const int st = stages_for(o[0], o[1]);
-    if (st >= o[2]) {
-      p.cg = o[0];
-      p.nbuf = o[1];
-      p.stages = st;
-      break;
-    }
-  }
-  if (!p.stages) return fail(AGXC_EINVAL, "qmm: the batch does not fit the shared memory");
-  const int smem = qmm_layout(pk->bits, B, p.stages, p.cg, p.nbuf).total + 1024;
+  p.cg = gk % 2 == 0 ? 2 : 1;
+  p.nbuf = kABufCols / 32 / p.cg;
+  p.stages = 16;
+  while (p.stages > 2 && qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024 > ctx->max_smem_optin - 2048) --p.stages;
+  if (qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024 > ctx->max_smem_optin - 2048)
+    return fail(AGXC_EINVAL, "qmm: the batch does not fit the shared memory");
+  const int smem = qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024;
   // maps: the pack's tiles and scale/bias as boxes of cg groups x 8 row tiles; X [B][K] fp16 as 64 x B boxes
   QmvPlan plan;
   plan.CG = p.cg;

@@ -307,12 +307,12 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_TRACE 1      /* 1: every launch of the step records, over its CTAs, the first and last %globaltimer
                                  (ns) at CTA entry, after the dependency wait, and at CTA exit (read with
                                  agxc_model_trace_read); 0 (default): off */
-#define AGXC_OPT_FUSED 2      /* 1 (default where it fits): a batch-1 model on one device runs each step as ONE
-                                 persistent cooperative kernel: one CTA per SM, a producer warp streams every weight
-                                 chunk and KV row the CTA reads through a shared-memory ring while the layer's four
-                                 phases (qkv; attention; merge + o_proj; gate/up + down) wait only on the counters of
-                                 the data they read. 0: one kernel per projection and attention, chained by
-                                 programmatic dependent launch (always the case for batch > 1) */
+#define AGXC_OPT_FUSED 2      /* 1 (where it fits): a batch-1 model on one device runs each step as ONE persistent
+                                 cooperative kernel: one CTA per SM, a producer warp streams every weight chunk and KV
+                                 row the CTA reads through a shared-memory ring while the layer's four phases (qkv;
+                                 attention; merge + o_proj; gate/up + down) wait only on the counters of the data they
+                                 read. 0 (default): one kernel per projection and attention, chained by programmatic
+                                 dependent launch (always the case for batch > 1) */
 #define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
                                  a chunk); 0 (default): by 3-D TMA tensor boxes */
 #define AGXC_OPT_TP_FUSED 5    /* tensor parallel: 1 (default when every rank could map the others' buffers) = the

@@ -54,3 +54,15 @@ def test_tp_internlm7b_shape_two_layers():
         pytest.skip("needs 2 GPUs")
     rep = _run("internlm7b", 8 if n >= 8 else 2)
     assert rep["max_diff_vs_tp1"] < 0.02
+
+
+@pytest.mark.parametrize("mode", ["fused", "nccl"])
+def test_tp4_internlm7b_shape(mode):
+    """Four ranks: the fused path is the two-shot all-reduce there (reduce-scatter by the GEMMs' peer stores, a
+    cooperative reduce + all-gather kernel); NCCL alongside."""
+    if _gpus() < 4:
+        pytest.skip("needs 4 GPUs")
+    rep = _run("internlm7b", 4, mode)
+    assert rep["max_diff_vs_tp1"] < 0.02
+    if mode == "fused":
+        assert rep["two_shot"] == 1

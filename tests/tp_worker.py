@@ -56,7 +56,7 @@ def main():
     parts = [None] * world
     dist.all_gather_object(parts, (m.vocab_offset, lg, free_t, free_lg))
     ok, report = True, dict(case=args.case, world=world, rank=rank, mode=args.mode,
-                            fused=m.plan_info()["tp"]["fused"])
+                            fused=m.plan_info()["tp"]["fused"], two_shot=m.plan_info()["tp"]["two_shot"])
     if rank == 0:
         parts.sort(key=lambda p: p[0])
         full = np.concatenate([p[1] for p in parts], axis=2)
