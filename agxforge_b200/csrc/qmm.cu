@@ -11,10 +11,10 @@
 //     operand (two fields at a time: (word >> 4j) & 0x000F000F | 0x64006400 is the fp16 pair 1024 + q, HSUB2 takes
 //     1024 away exactly, HFMA2 applies the row's scale and bias with one rounding). One thread is one weight row =
 //     one TMEM lane (a warp's 32 lanes are its quarter of the 128 rows); a group is 64 fp16 = 32 columns, written
-//     with tcgen05.st. The four warps of a lane quarter split a chunk's cg x 64 k in 16 k (cg 1) or 32 k (cg 2)
-//     slices: each warp's share is short, and four of them a scheduler hide one another's latencies (the conversion
-//     is latency-bound: the MMA waits for the slowest warp of a chunk). The fp16 weights never pass through shared
-//     memory;
+//     with tcgen05.st. The four warps of a lane quarter split a chunk's cg x 64 k: a group each (cg 4), 32 k
+//     (cg 2) or 16 k (cg 1); four of them a scheduler hide one another's latencies (the conversion is latency-bound:
+//     the MMA waits for the slowest warp of a chunk, and each warp pays two barrier polls and a TMEM store wait a
+//     chunk). The fp16 weights never pass through shared memory;
 //   * the MMA warp issues 4 cg tcgen05.mma.kind::f16 (M 128, N B, K 16; A from TMEM, B = X from shared memory)
 //     accumulating in TMEM, and commits: the commit releases the stage and the TMEM A buffer when the tensor core has
 //     read them.
@@ -113,6 +113,18 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+// Two barrier phases polled together (one round trip): true when both are complete.
+__device__ __forceinline__ bool mbar_try_wait2(uint64_t* a, unsigned pa, uint64_t* b, unsigned pb) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p, q;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 q, [%3], %4;\n and.pred p, p, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb)
+      : "memory");
+  return ok != 0;
+}
+
 // One lane of the (converged) warp: true there, false elsewhere.
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
@@ -361,11 +373,17 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
     const int rt = (32 * q4 + lane) >> 4, r16 = lane & 15;
     // the warp's slice of the chunk (si = 0..3 within its quarter): cg 2: group si / 2, k 32 (si % 2) ..; cg 1: k 16 si
     const int si = dw >> 2;
-    const int gc = cg == 2 ? si >> 1 : 0, cslot = cg == 2 ? 2 * (si & 1) : si;
+    const int gc = cg == 4 ? si : cg == 2 ? si >> 1 : 0, cslot = cg == 4 ? 0 : cg == 2 ? 2 * (si & 1) : si;
     const uint32_t tlane = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     for (int i = 0, s = 0, sph = 0, d = 0, dph = 0; i < gper; ++i) {
-      const bool ok1 = !*dead && mbar_wait_quiet(&raw_full[s], static_cast<unsigned>(sph), p.err);
-      const bool ok2 = ok1 && (i < D || mbar_wait_quiet(&deq_empty[d], static_cast<unsigned>(dph ^ 1), p.err));
+      // the stage's copies landed and the A buffer's previous MMAs done: both polled in one round trip first
+      bool ok2 = !*dead && (i < D ? mbar_try_wait(&raw_full[s], static_cast<unsigned>(sph))
+                                  : mbar_try_wait2(&raw_full[s], static_cast<unsigned>(sph), &deq_empty[d],
+                                                   static_cast<unsigned>(dph ^ 1)));
+      if (!ok2) {
+        const bool ok1 = !*dead && mbar_wait_quiet(&raw_full[s], static_cast<unsigned>(sph), p.err);
+        ok2 = ok1 && (i < D || mbar_wait_quiet(&deq_empty[d], static_cast<unsigned>(dph ^ 1), p.err));
+      }
       if (!__all_sync(0xffffffffu, ok2)) {  // the warp leaves together
         *dead = 1;
         break;
@@ -375,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_kernel(const QmmParams p, con
       const uint8_t* wt = st + L.w_off + (rt * cg + gc) * TB;
       const uint8_t* sbt = st + L.sb_off + (rt * cg + gc) * 64;
       const uint32_t ta = tlane + kAcol + (d * cg + gc) * 32 + 8 * cslot;
-      if (cg == 2) dequant_row<BITS, 2>(wt, sbt, r16, cslot, p.sdt, ta);
+      if (cg == 4) dequant_row<BITS, 4>(wt, sbt, r16, 0, p.sdt, ta);
+      else if (cg == 2) dequant_row<BITS, 2>(wt, sbt, r16, cslot, p.sdt, ta);
       else dequant_row<BITS, 1>(wt, sbt, r16, cslot, p.sdt, ta);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();    // the MMA warp reads these columns after its barrier wait
@@ -510,16 +529,20 @@ int launch_qmm(const agxc_ctx* ctx, const agxc_pack* pk, const void* x, int B, f
       return fail(AGXC_EINVAL, "qmm: push to 1..8 ranks owning equal numbers of 128-row tiles");
     p.push = *push;
   }
-  // the chunk: 2 groups where the K range divides (the dequant warps' per-chunk waits then cover two groups), else
-  // 1; the TMEM A buffers hold 8 groups either way; as many stages as fit (at most 16: a stage cycles through the
-  // copy, the dequant and the MMA's completion before it is refilled, so small stages want many)
+  // the chunk: 4 groups where the K range divides and four stages of them fit (one whole group a dequant warp: its two
+  // barrier polls, about 200 cycles each, and its TMEM store latency are paid once for four groups), else 2, else 1;
+  // the TMEM A buffers hold 8 groups either way; as many stages as fit (at most 16: a stage cycles through the copy,
+  // the dequant and the MMA's completion before it is refilled, so small stages want many)
   const int gk = G / ksplit;
-  p.cg = gk % 2 == 0 ? 2 : 1;
+  auto stages_for = [&](int cg) {
+    int st = 16;
+    while (st > 2 && qmm_layout(pk->bits, B, st, cg).total + 1024 > ctx->max_smem_optin - 2048) --st;
+    return qmm_layout(pk->bits, B, st, cg).total + 1024 > ctx->max_smem_optin - 2048 ? 0 : st;
+  };
+  p.cg = gk % 4 == 0 && stages_for(4) >= 4 ? 4 : gk % 2 == 0 ? 2 : 1;
   p.nbuf = kABufCols / 32 / p.cg;
-  p.stages = 16;
-  while (p.stages > 2 && qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024 > ctx->max_smem_optin - 2048) --p.stages;
-  if (qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024 > ctx->max_smem_optin - 2048)
-    return fail(AGXC_EINVAL, "qmm: the batch does not fit the shared memory");
+  p.stages = stages_for(p.cg);
+  if (!p.stages) return fail(AGXC_EINVAL, "qmm: the batch does not fit the shared memory");
   const int smem = qmm_layout(pk->bits, B, p.stages, p.cg).total + 1024;
   // maps: the pack's tiles and scale/bias as boxes of cg groups x 8 row tiles; X [B][K] fp16 as 64 x B boxes
   QmvPlan plan;
