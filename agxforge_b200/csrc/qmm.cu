@@ -196,6 +196,66 @@ __device__ __forceinline__ void dequant_row(const uint8_t* wt, const uint8_t* sb
   const uint32_t sv = to_f16_bits(static_cast<uint16_t>(h ? e.x >> 16 : e.x & 0xFFFFu), sdt);
   const uint32_t bv = to_f16_bits(static_cast<uint16_t>(h ? e.y >> 16 : e.y & 0xFFFFu), sdt);
   const uint32_t s2 = sv | (sv << 16), b2 = bv | (bv << 16);
+  if (NC == 4) {
+    // All four lane slots: loaded in an order rotated by r / 2, so the eight rows of a tile (64 bytes apart, i.e.
+    // two 16-byte bank groups) read eight different bank groups per step instead of four-way conflicting; two
+    // select levels put the words back in slot order.
+    const int rr = r >> 1;
+    const bool rot1 = rr & 1, rot2 = rr & 2;
+    auto unrotate = [&](uint32_t* x) {  // x[c] holds slot (c + rr) & 3 -> x[j] = slot j
+      uint32_t y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = rot1 ? x[(j + 3) & 3] : x[j];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] = rot2 ? y[(j + 2) & 3] : y[j];
+    };
+    if (BITS == 4) {
+      uint32_t w0[4], w1[4];  // words h and h + 2 of each slot (hi = 0, 1)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wt + (r * 4 + ((c + rr) & 3)) * 16);
+        w0[c] = h ? wv.y : wv.x;
+        w1[c] = h ? wv.w : wv.z;
+      }
+      unrotate(w0);
+      unrotate(w1);
+#pragma unroll
+      for (int cc = 0; cc < 4; cc += 2) {
+        uint32_t o[16];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            o[8 * u + 2 * j] = hfma2(hsub_1024(((w0[cc + u] >> (4 * j)) & 0x000F000Fu) | 0x64006400u), s2, b2);
+            o[8 * u + 2 * j + 1] = hfma2(hsub_1024(((w1[cc + u] >> (4 * j)) & 0x000F000Fu) | 0x64006400u), s2, b2);
+          }
+        tmem_st16(taddr + 8 * cc, o);
+      }
+    } else {
+      const uint32_t sel = h ? 0x4342u : 0x4140u;
+      uint32_t w[8][4];  // [word of the slot][slot]
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int sl = (c + rr) & 3;
+        const uint4 lo = *reinterpret_cast<const uint4*>(wt + (r * 4 + sl) * 16);
+        const uint4 hi4 = *reinterpret_cast<const uint4*>(wt + 512 + (r * 4 + sl) * 16);
+        w[0][c] = lo.x; w[1][c] = lo.y; w[2][c] = lo.z; w[3][c] = lo.w;
+        w[4][c] = hi4.x; w[5][c] = hi4.y; w[6][c] = hi4.z; w[7][c] = hi4.w;
+      }
+#pragma unroll
+      for (int wi = 0; wi < 8; ++wi) unrotate(w[wi]);
+#pragma unroll
+      for (int cc = 0; cc < 4; cc += 2) {
+        uint32_t o[16];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int wi = 0; wi < 8; ++wi) o[8 * u + wi] = hfma2(hsub_1024(prmt(w[wi][cc + u], 0x64646464u, sel)), s2, b2);
+        tmem_st16(taddr + 8 * cc, o);
+      }
+    }
+    return;
+  }
   constexpr int U = NC < 2 ? NC : 2;  // lane slots a store
 #pragma unroll
   for (int cc = 0; cc < NC; cc += U) {
