@@ -104,7 +104,7 @@ struct agxc_model {
   int tp_fused = 0;             // 1: o_proj and down push their tiles to every rank and reduce locally (no NCCL)
   int tp_fused_ok = 0;          // the peer mappings exist on every rank
   int tp_fused_ran = 0;         // a fused step has run (the variant is fixed from then on)
-  int tp_two_shot = 0;          // 1 (4 or more ranks): reduce-scatter by the GEMM + all-gather; 0: every rank's tiles
+  int tp_two_shot = 0;          // 1 (8 ranks): reduce-scatter by the GEMM + all-gather; 0: every rank's tiles
                                 // to every rank (2 ranks: one synchronisation instead of two)
   float* recv = nullptr;
   unsigned* recv_flags = nullptr;
@@ -577,7 +577,9 @@ int tp_peer_setup(agxc_model* m) {
   float sum = 0.f;
   AGXC_CUDA(cudaMemcpy(&sum, m->ybuf, 4, cudaMemcpyDeviceToHost));
   m->tp_fused_ok = sum == static_cast<float>(T);
-  m->tp_two_shot = T >= 4;
+  // two-shot from 8 ranks: at 4 the one-shot push (4 MB out a rank per all-reduce at 64 sequences) measured faster
+  // than the two-shot's extra synchronisation round (o_proj group 44.7 against 63.5 us a layer, 7B TP4)
+  m->tp_two_shot = T >= 8;
   if (!m->tp_fused_ok && m->tp_fused_why.empty()) m->tp_fused_why = "a peer rank could not map the buffers";
   m->tp_fused = m->tp_fused_ok;
   if (m->tp_fused_ok) {  // the residual stream lives in the exported allocation: owners write every rank's rows

@@ -316,11 +316,11 @@ AGXC_API int agxc_model_profile(agxc_model* m, int steps, float* kind_ms /*[6]*/
 #define AGXC_OPT_BULK 3       /* 1: the per-projection GEMVs move weight chunks by plain bulk copies (one per row tile of
                                  a chunk); 0 (default): by 3-D TMA tensor boxes */
 #define AGXC_OPT_TP_FUSED 5    /* tensor parallel: 1 (default when every rank could map the others' buffers) = the
-                                 o_proj and down GEMMs carry the all-reduce over NVLink peer memory: with 2 ranks each
-                                 finished tile goes to every rank and a bounded-wait kernel sums the ranks' slots
-                                 fused with the residual (one-shot); with 4 or more, each tile goes to the rank owning
-                                 its rows and a cooperative kernel reduces them and stores them into every rank's
-                                 residual stream (two-shot). 2 / 3 force two-shot / one-shot (before the first fused
+                                 o_proj and down GEMMs carry the all-reduce over NVLink peer memory: with 2 or 4 ranks
+                                 each finished tile goes to every rank and a bounded-wait kernel sums the ranks' slots
+                                 fused with the residual (one-shot); with 8, each tile goes to the rank owning its
+                                 rows and a cooperative kernel reduces them and stores them into every rank's residual
+                                 stream (two-shot). 2 / 3 force two-shot / one-shot (before the first fused
                                  step only); 0 = NCCL all-reduce. Every rank must set the same value. */
 #define AGXC_OPT_QK_NORM 6     /* 1: QK-norm (Qwen3; attention.py:256-265 with_qknorm): every q and k head of the qkv
                                  projection is RMS-normed over head_dim with the layer's AGXC_VEC_Q_NORM / _K_NORM gain

@@ -56,13 +56,12 @@ def test_tp_internlm7b_shape_two_layers():
     assert rep["max_diff_vs_tp1"] < 0.02
 
 
-@pytest.mark.parametrize("mode", ["fused", "nccl"])
+@pytest.mark.parametrize("mode", ["fused", "two_shot", "nccl"])
 def test_tp4_internlm7b_shape(mode):
-    """Four ranks: the fused path is the two-shot all-reduce there (reduce-scatter by the GEMMs' peer stores, a
-    cooperative reduce + all-gather kernel); NCCL alongside."""
+    """Four ranks: the fused one-shot all-reduce (the default there), the two-shot forced (reduce-scatter by the
+    GEMMs' peer stores, a cooperative reduce + all-gather kernel; the default from 8 ranks) and NCCL."""
     if _gpus() < 4:
         pytest.skip("needs 4 GPUs")
     rep = _run("internlm7b", 4, mode)
     assert rep["max_diff_vs_tp1"] < 0.02
-    if mode == "fused":
-        assert rep["two_shot"] == 1
+    assert rep["two_shot"] == (1 if mode == "two_shot" else 0)
