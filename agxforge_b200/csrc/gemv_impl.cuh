@@ -166,13 +166,14 @@ __device__ __forceinline__ void group_step(uint32_t aw, uint32_t asb, uint32_t a
 }
 
 // ------------------------------------------------------------------------------------------------ epilogues
-// vals: [rows][NBT] fp32 (column = activation row b) for the block of `rows` physical rows starting at `row0`.
-template <int EPI, int NBT>
+// vals(i): the value of element i = r NBT + b of the block ([rows][NBT] fp32, column = activation row b) of `rows`
+// physical rows starting at `row0`: an array read, or the warps' partial sums added on demand.
+template <int EPI, int NBT, typename Vals>
 // resv: prefetched operands of these rows, or NULL to read them here: the residual ([rows][NBT] fp32) of RES1/RES2,
 // the RoPE (cos, sin) per pair ([rows/2][NBT][2]) of QKV
 // t0 / tstride: the calling threads' index and count (default: all consumer threads); the argmax keeps its running
 // maximum in misc[0], misc[1] of the calling group (one warp, t0 = lane, when a warp finalises a unit alone).
-__device__ void epilogue(const QmvParams& p, int row0, int rows, const float* vals, float* misc,
+__device__ void epilogue(const QmvParams& p, int row0, int rows, Vals vals, float* misc,
                          const float* resv = nullptr, int t0 = -1, int tstride = kConsumers) {
   const int tid = t0 >= 0 ? t0 : static_cast<int>(threadIdx.x);
   const int nb = p.nb;
@@ -180,7 +181,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
     for (int t = tid; t < rows * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
-      p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * NBT + b];
+      p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals(r * NBT + b);
     }
   } else if (EPI == EPI_RES1) {
     for (int t = tid; t < rows * NBT; t += tstride) {
@@ -189,14 +190,14 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       const float x = resv ? resv[r * NBT + b]
                            : __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p.res16) +
                                                                   static_cast<size_t>(b) * p.res_ld + row0 + r)));
-      p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals[r * NBT + b] + x;
+      p.out_f32[static_cast<size_t>(b) * p.out_ld + row0 + r] = vals(r * NBT + b) + x;
     }
   } else if (EPI == EPI_RES2) {
     for (int t = tid; t < rows * NBT; t += tstride) {
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
       const float h = resv ? resv[r * NBT + b] : __ldcg(p.res32 + static_cast<size_t>(b) * p.res_ld + row0 + r);
-      p.out_f16[static_cast<size_t>(b) * p.out_ld + row0 + r] = __float2half_rn(vals[r * NBT + b] + h);
+      p.out_f16[static_cast<size_t>(b) * p.out_ld + row0 + r] = __float2half_rn(vals(r * NBT + b) + h);
     }
   } else if (EPI == EPI_SWIGLU) {
     // pairs of row tiles: a gate tile (rows 0..15 of the pair) and its up tile (rows 16..31); output (row0/32)*16 + r
@@ -204,7 +205,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       const int r = t / NBT, b = t % NBT;
       if (b >= nb) continue;
       const int pr = r / 16, rr = r % 16;
-      const float g = vals[(pr * 32 + rr) * NBT + b], u = vals[(pr * 32 + 16 + rr) * NBT + b];
+      const float g = vals((pr * 32 + rr) * NBT + b), u = vals((pr * 32 + 16 + rr) * NBT + b);
       p.out_f16[static_cast<size_t>(b) * p.out_ld + (row0 / 32 + pr) * 16 + rr] = __float2half_rn(silu_f(g) * u);
     }
   } else if (EPI == EPI_QKV) {
@@ -220,7 +221,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       const int head = prow0 / hd;
       const int tt = (prow0 % hd) / 16;            // tile index within the head
       const int i1 = 8 * tt + r, i2 = half + 8 * tt + r;
-      float y1 = vals[(tile * 16 + r) * NBT + b], y2 = vals[(tile * 16 + r + 8) * NBT + b];
+      float y1 = vals((tile * 16 + r) * NBT + b), y2 = vals((tile * 16 + r + 8) * NBT + b);
       if (p.bias) {
         y1 += __half2float(p.bias[head * hd + i1]);
         y2 += __half2float(p.bias[head * hd + i2]);
@@ -251,7 +252,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       for (int t = tid; t < rows * NBT; t += tstride) {
         const int r = t / NBT, b = t % NBT;
         if (b >= nb) continue;
-        p.out_f32[static_cast<size_t>(b) * p.V + row0 + r] = vals[r * NBT + b];
+        p.out_f32[static_cast<size_t>(b) * p.V + row0 + r] = vals(r * NBT + b);
       }
     }
     // warp b keeps the running first-maximum of column b: misc[2b] value, misc[2b+1] index (int bits)
@@ -260,7 +261,7 @@ __device__ void epilogue(const QmvParams& p, int row0, int rows, const float* va
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       for (int r = lane; r < rows; r += 32) {
-        const float v = vals[r * NBT + w];
+        const float v = vals(r * NBT + w);
         if (v > bv) { bv = v; bi = row0 + r; }  // rows ascend per lane: the first of equal values stays
       }
 #pragma unroll
@@ -713,18 +714,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       rw[(r8 + 8) * NBT + 2 * c4 + 1] = fmaf(ys[3], k2p24, yb[3]);
     }
     consumer_sync();
-    for (int t = tid; t < RW * 16 * NBT; t += kConsumers) {
+    // element t = row NBT + b of the unit: the KW K-lane warps' partial sums of its row, added in warp order
+    auto reduced = [red](int t) {
       const int row = t / NBT, b = t % NBT;
       const int rt = row / 16, rw16 = row % 16;
       float s = 0.f;
 #pragma unroll
       for (int q = 0; q < KW; ++q) s += red[(rt + q * RW) * 16 * NBT + rw16 * NBT + b];
-      uv[t] = s;
-    }
-    consumer_sync();
+      return s;
+    };
     const int row0 = rb * RW * 16;
+    if (SC == 1 && EPI != EPI_ARGMAX) {
+      // each epilogue thread adds up the rows it needs itself (the same sums in the same order): no barrier between
+      // the reduction and the epilogue; one before the next unit's partial sums overwrite `red`
+      epilogue<EPI, NBT>(p, row0, RW * 16, reduced, misc,
+                         (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
+      if (i + 1 < my_units) consumer_sync();
+      continue;
+    }
+    for (int t = tid; t < RW * 16 * NBT; t += kConsumers) uv[t] = reduced(t);
+    consumer_sync();
+    auto uv_at = [uv](int t) { return uv[t]; };
     if (SC == 1) {
-      epilogue<EPI, NBT>(p, row0, RW * 16, uv, misc, (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
+      epilogue<EPI, NBT>(p, row0, RW * 16, uv_at, misc, (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
     } else {
       // split K: this unit's partial rows to scratch; the last of the SC units of these rows sums them in order
       for (int t = tid; t < RW * 16 * NBT; t += kConsumers) {
@@ -749,7 +761,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           ev[t] = s;
         }
         consumer_sync();
-        epilogue<EPI, NBT>(p, row0, RW * 16, ev, misc,
+        auto ev_at = [ev](int t) { return ev[t]; };
+        epilogue<EPI, NBT>(p, row0, RW * 16, ev_at, misc,
                            (kRes || (kRope && p.pos_ready)) && i == 0 ? resv : nullptr);
       }
       consumer_sync();
