@@ -47,6 +47,17 @@ def test_qmm_against_fp64(torch, bits, B):
     _check(y, x16, W64)
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("groups,B", [(7, 32), (7, 128), (6, 64), (14, 256), (3, 48)])
+def test_qmm_chunk_shapes(torch, bits, groups, B):
+    """K ranges of an odd number of 64-groups (one-group chunks: four dequant warps share a group's k) and of 2 mod 4
+    groups (two-group chunks), as the tensor-parallel shards produce (the 7B down projection at 8 ranks: 7 groups)."""
+    from agxforge.kernels.qmm import qmm
+    pk, x16, W64 = _case(torch, bits, 256, 64 * groups, B, seed=groups * 10 + bits)
+    y = qmm(pk, torch.from_numpy(x16).cuda(), ksplit=1).cpu().numpy()
+    _check(y, x16, W64)
+
+
 @pytest.mark.parametrize("ksplit", [1, 2, 4, 0])
 def test_qmm_k_split(torch, ksplit):
     from agxforge.kernels.qmm import qmm
