@@ -851,15 +851,24 @@ def main():
         )
     m.close()
     torch.cuda.synchronize()
+    tp_failed = False
     if args.config == "internlm-q4-1792" and not args.no_tp:
-        tpb = tp_block(args, rank, world, local, dist)
+        try:
+            tpb = tp_block(args, rank, world, local, dist)
+        except Exception as e:  # the replica line stands; the tensor-parallel block reports what went wrong
+            tpb = dict(error="%s: %s" % (type(e).__name__, str(e)[:300]))
+            tp_failed = True
         if rank == 0:
             line["tp"] = tpb
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+        try:
+            dist.barrier()
+            dist.destroy_process_group()
+        except Exception:
+            if not tp_failed:  # a communicator broken by the failed block may not close cleanly
+                raise
 
 
 if __name__ == "__main__":
